@@ -1,0 +1,490 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 SAR rasterizer.
+
+Workload (the multi-view inference sweep): N = 1,000,000 Gaussians in a
+40 x 40 x 10 m box, 1,024 radar views per step (track angle stepped by
+0.35 deg, incidence uniform 15-45 deg), 256 x 256 images at 0.2 m, forward
+only. Seeded synthetic data (no dataset). With --gpus N (torchrun), every
+rank renders its own 1,024-view sweep (offset track angles): per-GPU work is
+fixed, views are independent, no collective on the data path.
+
+value     forward views/s over all ranks, inputs resident in HBM, L2 flushed
+          (512 MiB write) before every timed step, device time from CUDA events,
+          max over ranks.
+e2e       the same sweep through the public C ABI with host buffers: pinned
+          host -> device copy of the scene, the render, and device -> host copy
+          of all images every step.
+fwd_bwd   forward + backward steps/s of one view at 1M Gaussians, 256 x 256
+          (the autograd path: forward state reused by the backward, dense
+          gradients for all N Gaussians).
+
+--impl reference runs the CPU restatement of the reference algorithm (the
+reference ships no CPU implementation) on the host cores, and times the
+reference's own CUDA kernels on a few views as `gpu_reference`.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+import torch
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+for p in (os.path.join(REPO, "sar-3dgs_b200"), REPO):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+from cuda_rasterizer import _native  # noqa: E402
+from cuda_rasterizer import synthetic as S  # noqa: E402
+
+METRIC = "fwd views/s & fwd+bwd steps/s, 1M Gaussians 256², 1/8 B200; % HBM roofline"
+HBM_FALLBACK_GBS = 6650.0
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--n", type=int, default=1_000_000)
+    ap.add_argument("--views", type=int, default=1024)
+    ap.add_argument("--samples", type=int, default=256)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-fwdbwd", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    return ap.parse_args()
+
+
+def peaks():
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as fh:
+            return float(json.load(fh)["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return HBM_FALLBACK_GBS, "fallback"
+
+
+class Dist:
+    def __init__(self):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.pg = None
+        if self.world > 1:
+            import datetime
+            import torch.distributed as dist
+            torch.cuda.set_device(self.local)
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                    device_id=torch.device("cuda", self.local))
+            self.pg = dist
+        self.device = torch.device("cuda", self.local)
+
+    def barrier(self):
+        if self.pg:
+            self.pg.barrier()
+
+    def max(self, x):
+        if not self.pg:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=self.device)
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum(self, x):
+        if not self.pg:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=self.device)
+        self.pg.all_reduce(t)
+        return float(t.item())
+
+    def close(self):
+        if self.pg:
+            self.pg.barrier()
+            self.pg.destroy_process_group()
+
+
+class Clocks:
+    """nvidia-smi sampling of SM clock and throttle reasons during a region."""
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.proc = None
+        try:
+            self.uuid = str(torch.cuda.get_device_properties(device).uuid)
+            if not self.uuid.startswith("GPU-"):
+                self.uuid = "GPU-" + self.uuid
+        except Exception:
+            self.uuid = None
+
+    def start(self):
+        self.out = tempfile.TemporaryFile(mode="w+")
+        try:
+            cmd = ["nvidia-smi", "--query-gpu=" + self.FIELDS, "--format=csv,noheader,nounits",
+                   "-lms", "50"]
+            if self.uuid:
+                cmd[1:1] = ["-i", self.uuid]
+            self.proc = subprocess.Popen(cmd, stdout=self.out, stderr=subprocess.DEVNULL)
+            time.sleep(0.2)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.1)
+        self.proc.terminate()
+        self.proc.wait(timeout=10)
+        self.out.seek(0)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.out:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 7:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx.append(float(parts[1]))
+            except ValueError:
+                continue
+            for nm, val in zip(names, parts[3:7]):
+                if val.lower().startswith("active"):
+                    reasons.add(nm)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def flush_l2(buf, k):
+    buf.fill_(float(k % 7))
+
+
+def scene_name(n):
+    return "sweep_1m" if n == 1_000_000 else None
+
+
+def make_scene(args, device):
+    if scene_name(args.n):
+        return S.named_scene("sweep_1m", seed=0, device=device)
+    return S.make_scene(args.n, (40.0, 40.0, 10.0), (0.05, 0.5), seed=0, device=device)
+
+
+def rank_views(args, d):
+    return S.sweep_views(args.views, samples=args.samples, offset_deg=0.35 * d.rank / max(d.world, 1))
+
+
+def bin_bytes_per_launch(n, nviews, T, C):
+    """Algorithmic bytes of one bin_kernel launch over `nviews` views: every
+    view reads the 40 B of means/cov6/transmittance per Gaussian, writes its
+    4 B tile rectangle per Gaussian and the C x T chunk counts."""
+    return nviews * (40 * n + 4 * n + C * T)
+
+
+def bench_ours(args, d):
+    dev = d.device
+    torch.cuda.set_device(dev)
+    sc = make_scene(args, dev)
+    means, cov, layout, sigma, sh, sh_stride, sh_k = _native.prepare_inputs(
+        sc["means"], sc["cov6"], sc["sigma"], sc["sh"])
+    n, s = args.n, args.samples
+    views = [_native.make_view(*t) for t in rank_views(args, d)]
+    V = len(views)
+    images = torch.empty((V, s, s), dtype=torch.float32, device=dev)
+    ws = torch.empty(_native.workspace_bytes(n, s, s, V), dtype=torch.uint8, device=dev)
+    flush = torch.empty((512 << 20) // 4, dtype=torch.float32, device=dev)
+
+    def step():
+        _native.forward(views, means, cov, layout, sigma, sh, sh_stride, sh_k, images, ws=ws)
+
+    for k in range(args.warmup):
+        flush_l2(flush, k)
+        step()
+    torch.cuda.synchronize()
+    d.barrier()
+
+    clocks = Clocks(dev)
+    clocks.start()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    torch.cuda.synchronize()
+    d.barrier()
+    l0 = _native.launch_count()
+    for k in range(args.steps):
+        flush_l2(flush, k)
+        ev[k][0].record()
+        step()
+        ev[k][1].record()
+    torch.cuda.synchronize()
+    launches = _native.launch_count() - l0
+    d.barrier()
+    clk = clocks.stop()
+    t_ms = sum(a.elapsed_time(b) for a, b in ev)
+    t_ms_max = d.max(t_ms)
+    total_views = d.sum(float(V * args.steps))
+    value = total_views / (t_ms_max / 1e3)
+
+    # checksum of the last step's images (guards against a step doing no work)
+    checksum = float(images.double().sum().item())
+
+    # roofline: per-kernel device time from the library's event hooks
+    _native.profile_enable(True)
+    rsteps = min(args.steps, 5)
+    for k in range(rsteps):
+        flush_l2(flush, k)
+        step()
+    torch.cuda.synchronize()
+    prof = _native.profile_read()
+    _native.profile_enable(False)
+    T = ((s + 15) // 16) ** 2
+    C = (n + 511) // 512
+    kname, (kms, klaunch) = max(prof.items(), key=lambda kv: kv[1][0])
+    peak, peak_kind = peaks()
+    roof = None
+    if kname == "bin_kernel" and klaunch:
+        per_launch_views = V / (klaunch / rsteps)
+        bytes_per_launch = bin_bytes_per_launch(n, per_launch_views, T, C)
+        achieved = bytes_per_launch / (kms / klaunch / 1e3) / 1e9
+        roof = {"kernel": kname, "bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                "peak_source": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                "traffic": None, "bytes_per_launch": int(bytes_per_launch),
+                "avg_launch_us": round(kms / klaunch * 1e3, 2)}
+    kernels = {k: {"ms_per_step": round(v[0] / rsteps, 4), "launches_per_step": v[1] / rsteps}
+               for k, v in prof.items() if v[1]}
+
+    out = {"value": value, "ms_per_step": t_ms_max / args.steps, "launches": launches,
+           "clocks": clk, "roofline": roof, "kernels": kernels, "checksum": checksum,
+           "views_per_rank": V}
+    if not args.no_e2e:
+        out["e2e"] = bench_e2e(args, d, sc, views)
+    if not args.no_fwdbwd:
+        out["fwd_bwd"] = bench_fwd_bwd(args, d, means, cov, layout, sigma, sh, sh_stride, sh_k,
+                                       views, flush)
+    return out
+
+
+def bench_e2e(args, d, sc, views):
+    """Host buffers in, host images out, through the C ABI; the device->host
+    copy of each group of images overlaps the render of the next group."""
+    dev = d.device
+    n, s, V = args.n, args.samples, len(views)
+    h = {k: sc[k].cpu().pin_memory() for k in ("means", "cov6", "sigma", "sh")}
+    dm = {k: torch.empty_like(v, device=dev) for k, v in h.items()}
+    h_img = torch.empty((V, s, s), dtype=torch.float32).pin_memory()
+    d_img = torch.empty((V, s, s), dtype=torch.float32, device=dev)
+    group = 128
+    ws = torch.empty(_native.workspace_bytes(n, s, s, 32), dtype=torch.uint8, device=dev)
+    comp = torch.cuda.current_stream(dev)
+    copy = torch.cuda.Stream(dev)
+    flush = torch.empty((512 << 20) // 4, dtype=torch.float32, device=dev)
+    h2d = sum(v.numel() * 4 for v in h.values())
+    d2h = V * s * s * 4
+
+    def step():
+        for k in ("means", "cov6", "sigma", "sh"):
+            dm[k].copy_(h[k], non_blocking=True)
+        means, cov, layout, sigma, sh, st, kk = _native.prepare_inputs(dm["means"], dm["cov6"],
+                                                                      dm["sigma"], dm["sh"])
+        for g0 in range(0, V, group):
+            g1 = min(V, g0 + group)
+            _native.forward(views[g0:g1], means, cov, layout, sigma, sh, st, kk, d_img[g0:g1], ws=ws)
+            ev = torch.cuda.Event()
+            ev.record(comp)
+            copy.wait_event(ev)
+            with torch.cuda.stream(copy):
+                h_img[g0:g1].copy_(d_img[g0:g1], non_blocking=True)
+        comp.wait_stream(copy)
+
+    steps = max(3, min(args.steps, 10))
+    for k in range(2):
+        flush_l2(flush, k)
+        step()
+    torch.cuda.synchronize()
+    d.barrier()
+    t = 0.0
+    for k in range(steps):
+        flush_l2(flush, k)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(comp)
+        step()
+        b.record(comp)
+        b.synchronize()
+        t += a.elapsed_time(b)
+    torch.cuda.synchronize()
+    ok = bool(torch.equal(h_img[V - 1].to(dev), d_img[V - 1]))
+    d.barrier()
+    t_max = d.max(t)
+    value = d.sum(float(V * steps)) / (t_max / 1e3)
+    return {"value": value, "unit": "views/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "ms_per_step": t_max / steps, "steps": steps, "host_copy_verified": ok}
+
+
+def bench_fwd_bwd(args, d, means, cov, layout, sigma, sh, sh_stride, sh_k, views, flush):
+    """One view per step: forward keeping its state, backward reusing it,
+    dense gradients for all N Gaussians (the SARRasterizer training path)."""
+    dev = d.device
+    n, s = args.n, args.samples
+    img = torch.empty((s, s), dtype=torch.float32, device=dev)
+    g = torch.randn((s, s), generator=torch.Generator().manual_seed(1)).to(dev)
+    state = torch.empty(_native.state_bytes(n, s, s), dtype=torch.uint8, device=dev)
+    ws = torch.empty(_native.workspace_bytes(n, s, s, 1), dtype=torch.uint8, device=dev)
+    gm = torch.empty((n, 3), device=dev)
+    gc = torch.empty((n, 6), device=dev)
+    gs = torch.empty((n,), device=dev)
+    gsh = torch.empty((n, 16), device=dev)
+    gn = torch.empty((n,), device=dev)
+    per_block = 64
+
+    def block(k0):
+        for j in range(per_block):
+            v = [views[(k0 + j) % len(views)]]
+            _native.forward(v, means, cov, layout, sigma, sh, sh_stride, sh_k, img, states=state, ws=ws)
+            _native.backward(v, means, cov, layout, sigma, sh, sh_stride, sh_k, g, gm, gc,
+                             _native.SARR_COV6, gs, gsh, grad_norm=gn, states=state, ws=ws)
+
+    block(0)
+    torch.cuda.synchronize()
+    d.barrier()
+    blocks = 5
+    t = 0.0
+    for b in range(blocks):
+        flush_l2(flush, b)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        block(b * per_block)
+        e1.record()
+        e1.synchronize()
+        t += e0.elapsed_time(e1)
+    t_max = d.max(t)
+    steps = blocks * per_block
+    value = d.sum(float(steps)) / (t_max / 1e3)
+    return {"value": value, "unit": "steps/s", "ms_per_step": t_max / steps,
+            "step": "1 view fwd+bwd, dense grads for 1M Gaussians, 256x256",
+            "l2": "flushed every 64 steps"}
+
+
+def cpu_baseline(args):
+    """CPU restatement of the reference algorithm on a bounded sample of the
+    same workload (image-only forward), all host threads."""
+    from oracle import oracle as O
+    sc = make_scene(args, "cpu")
+    s = {k: v.numpy() for k, v in sc.items()}
+    views = S.sweep_views(args.views, samples=args.samples)
+    done, t0 = 0, time.perf_counter()
+    while done < 64:
+        O.forward(O.make_view(*views[done]), s["means"], s["cov6"], s["sigma"], s["sh"],
+                  want_omega=False)
+        done += 1
+        if time.perf_counter() - t0 > 12.0:
+            break
+    dt = time.perf_counter() - t0
+    return {"value": done / dt, "unit": "views/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"{done} views of the sweep (N={args.n}, {args.samples}x{args.samples}), "
+                      "image-only forward, C restatement with OpenMP"}
+
+
+def bench_reference(args, d):
+    """Reference arm: the CPU restatement on the host cores (rank 0 only), K
+    steps of a bounded 2-view sample; plus the reference's own CUDA kernels on
+    two views when its harness and a GPU are available."""
+    if d.rank != 0:
+        return None
+    from oracle import oracle as O
+    sc = make_scene(args, "cpu")
+    s = {k: v.numpy() for k, v in sc.items()}
+    views = S.sweep_views(args.views, samples=args.samples)
+    per_step = 2
+    for k in range(args.warmup):
+        O.forward(O.make_view(*views[k % len(views)]), s["means"], s["cov6"], s["sigma"], s["sh"],
+                  want_omega=False)
+    t0 = time.perf_counter()
+    for k in range(args.steps):
+        for j in range(per_step):
+            O.forward(O.make_view(*views[(k * per_step + j) % len(views)]), s["means"], s["cov6"],
+                      s["sigma"], s["sh"], want_omega=False)
+    dt = time.perf_counter() - t0
+    value = args.steps * per_step / dt
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "views/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": dt * 1e3 / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": config(args),
+            "cpu_baseline": {"value": value, "unit": "views/s", "cores": os.cpu_count(),
+                             "kind": "port",
+                             "sample": f"{per_step} views per step of the sweep, image-only forward"},
+            "e2e": {"value": value, "unit": "views/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    try:
+        line["gpu_reference"] = gpu_reference(args, sc, views)
+    except Exception as e:  # reported, not fatal: the CPU arm above is the reference arm
+        line["gpu_reference"] = {"unavailable": f"{type(e).__name__}: {e}"}
+    return line
+
+
+def gpu_reference(args, sc, views):
+    from oracle.ref import build_ref
+    R = build_ref.load_module()
+    dev = torch.device("cuda", 0)
+    t = {k: sc[k].to(dev).contiguous() for k in ("means", "cov6", "sigma", "sh")}
+    R.render_sar(t["means"], t["cov6"], t["sigma"], t["sh"], *views[0], False, False)
+    torch.cuda.synchronize()
+    nv = 2
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for j in range(nv):
+        R.render_sar(t["means"], t["cov6"], t["sigma"], t["sh"], *views[1 + j], False, False)
+    b.record()
+    b.synchronize()
+    ms = a.elapsed_time(b)
+    return {"value": nv / (ms / 1e3), "unit": "views/s", "kind": "reference",
+            "sample": f"{nv} views, reference rasterizer_impl_v2.cu kernels (slot-indexing fix), "
+                      "render_sar incl. its per-call allocations and Omega host round trip"}
+
+
+def config(args):
+    return {"workload": f"sar_sweep_n{args.n}_{args.samples}px_{args.views}views",
+            "n_gaussians": args.n, "image": [args.samples, args.samples], "rho_m": 0.2,
+            "views_per_step_per_gpu": args.views, "scene_box_m": [40, 40, 10],
+            "l2": "flushed before every timed step (512 MiB device write)",
+            "parallelism": f"view-sharded x{args.gpus}, no data-path collective",
+            "outputs": "images only (the SARRasterizer forward contract)"}
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        d = Dist() if int(os.environ.get("WORLD_SIZE", "1")) > 1 else None
+        rank = d.rank if d else 0
+        line = bench_reference(args, d or type("D", (), {"rank": 0})())
+        if rank == 0 and line:
+            print(json.dumps(line))
+        if d:
+            d.close()
+        return
+    d = Dist()
+    r = bench_ours(args, d)
+    line = {"metric": METRIC, "value": r["value"], "unit": "views/s", "n_gpus": d.world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": r["ms_per_step"],
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded; BASELINE sweep distributions)", "config": config(args),
+            "roofline": r["roofline"], "gpu_launches": r["launches"], "clocks": r["clocks"],
+            "kernels": r["kernels"], "image_checksum": r["checksum"]}
+    if "e2e" in r:
+        line["e2e"] = r["e2e"]
+    if "fwd_bwd" in r:
+        line["fwd_bwd"] = r["fwd_bwd"]
+    if d.rank == 0 and d.world == 1 and not args.no_cpu:
+        line["cpu_baseline"] = cpu_baseline(args)
+    if d.rank == 0:
+        print(json.dumps(line))
+    d.close()
+
+
+if __name__ == "__main__":
+    main()

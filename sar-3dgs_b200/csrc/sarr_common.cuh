@@ -1,0 +1,354 @@
+// Shared device code of the B200 SAR rasterizer: constants, per-view constants,
+// the per-Gaussian radar projection, the tile records and the TMA helpers.
+//
+// Floating-point expressions that decide tile membership, validity and the
+// pixel value are written term by term in the same order as the reference
+// (cuda_rasterizer/rasterizer_impl_v2.cu), zero terms included: nvcc contracts
+// a*b+c into fma, and the rounding of the result depends on which product is
+// fused, so the expression trees must be the same for the tile lists to be
+// bit-exact. Everything else (data movement, tile selection, sorting,
+// reductions) is this library's own design.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace sarr {
+
+// Constants fixed by the reference (rasterizer_impl_v2.cu:10-13, :472-474).
+constexpr float kEps = 1e-6f;                   // EPSILON
+constexpr float kPi = 3.14159265358979323846f;  // PI
+constexpr int kTile = 16;                       // BLOCK_X == BLOCK_Y
+constexpr int kCap = 64;                        // MAX_GAUSSIANS_PER_TILE
+constexpr int kSh = 16;                         // SH_COEFFS_SIZE
+
+// Design constants of this implementation.
+constexpr int kBinThreads = 256;                 // threads of a binning CTA
+constexpr int kBinPerThread = 2;                 // Gaussians per binning thread
+constexpr int kChunk = kBinThreads * kBinPerThread;  // Gaussians per count row
+constexpr int kSelectThreads = 256;
+constexpr int kWarpsPerTile = 8;                 // 8 warps x 32 pixels = one 16x16 tile
+constexpr int kMaxTilesAxis = 128;               // images up to 2048 x 2048
+constexpr int kMaxViewsPerLaunch = 32;
+constexpr uint32_t kEmptyRect = 0x000000FFu;     // tc0 = 255 > tc1 = 0
+
+// Device error bits (workspace error word).
+constexpr int kDevErrTmaTimeout = 1;
+constexpr int kDevErrListSlot = 2;
+
+// Per-view values computed on the host exactly as CUDASARRenderer::render
+// does (rasterizer_impl_v2.cu:1100-1120).
+struct ViewHost {
+  float radar_x, radar_y, radar_z;
+  float alpha;  // track angle [rad]
+  float beta;   // asin(sin(incidence) cos(azimuth)) [rad]
+  float Rc;     // scene-centre slant range
+  float rho_r, rho_a;
+  int Nr, Na;
+  float sh_basis[kSh];
+};
+
+// ViewHost plus the rotation trig, evaluated on the device with CUDA's
+// cosf/sinf like the reference kernels do (:103-106, :128-131).
+struct ViewConst {
+  ViewHost h;
+  float cos_a, sin_a, cos_b, sin_b;
+  int tiles_x, tiles_y;
+  int pad0, pad1;
+};
+
+struct ViewHostPack {
+  int n;
+  ViewHost v[kMaxViewsPerLaunch];
+};
+
+// One Gaussian of a tile list, as the compositing kernels read it.
+// For the image-plane list (mx, my) = (ipp_c, ipp_r) and (cxx, cxy, cyy) =
+// (cov_cc, cov_rc, cov_rr): the argument order of compute_gaussian_density_2d
+// in render_kernel (:815-819). For the shadow list (mx, my) = (X_r, Y_r) and
+// (cxx, cxy, cyy) = (cov_XrXr, cov_XrYr, cov_YrYr) (:701-705).
+struct __align__(16) Rec {
+  float mx, my;
+  float cxx, cxy, cyy;
+  float inv_det;  // 1 / (cxx*cyy - cxy*cxy)
+  float norm;     // 2*PI*sqrt(det); -1 marks |det| < EPSILON (density is 0)
+  float sigma;    // transmittance
+  float s_pos;    // max(0, S), S the leaky-ReLU SH scattering (image list only)
+  float z;        // Z_r, the depth sort key
+  float yr;       // Y_r (backward chain)
+  int pos;        // slot of this Gaussian in the index-ordered tile list
+};
+static_assert(sizeof(Rec) == 48, "Rec must stay 48 bytes (TMA bulk granularity)");
+
+// Radar-frame projection of one Gaussian.
+struct Proj {
+  float xr, yr, zr;
+  float r, c;                    // ipp_r, ipp_c
+  float cov_rr, cov_cc, cov_rc;  // image-plane covariance [pixel^2]
+  float XX, YY, XY;              // radar-frame covariance block used for the shadow plane
+};
+
+__device__ __forceinline__ void load_cov6(const float* __restrict__ p, int layout, float cw[6]) {
+  if (layout == 6) {
+    cw[0] = p[0]; cw[1] = p[1]; cw[2] = p[2]; cw[3] = p[3]; cw[4] = p[4]; cw[5] = p[5];
+  } else {  // [3,3] row major: xx yy zz xy xz yz = [0] [4] [8] [1] [2] [5]
+    cw[0] = p[0]; cw[1] = p[4]; cw[2] = p[8]; cw[3] = p[1]; cw[4] = p[2]; cw[5] = p[5];
+  }
+}
+
+// IEEE single-precision operations that the compiler may neither contract
+// nor reassociate. The reference is compiled with nvcc's default FMA
+// contraction, so its results depend on which products got fused; the
+// expressions below spell out that fusion explicitly (established bit for bit
+// against the reference's own kernels on a B200), which makes the results
+// independent of how this file's surrounding code is compiled.
+__device__ __forceinline__ float mul_(float a, float b) { return __fmul_rn(a, b); }
+__device__ __forceinline__ float add_(float a, float b) { return __fadd_rn(a, b); }
+__device__ __forceinline__ float sub_(float a, float b) { return __fsub_rn(a, b); }
+__device__ __forceinline__ float fma_(float a, float b, float c) { return __fmaf_rn(a, b, c); }
+__device__ __forceinline__ float div_(float a, float b) { return __fdiv_rn(a, b); }
+__device__ __forceinline__ float sqrt_(float a) { return __fsqrt_rn(a); }
+
+// k0 x0 + k1 x1 + ... + k5 x5 left to right: the first product fused into the
+// first addition, every later product fused into the running sum.
+__device__ __forceinline__ float chain6(const float k[6], const float x[6]) {
+  float s = fma_(k[0], x[0], mul_(k[1], x[1]));
+#pragma unroll
+  for (int i = 2; i < 6; ++i) s = fma_(k[i], x[i], s);
+  return s;
+}
+
+// world_to_radar + project_to_ipp + transform_covariance_3x3 +
+// compute_jacobian_ipp + project_covariance_ipp + project_covariance_shadow
+// (rasterizer_impl_v2.cu:98-213), as evaluated by preprocess_kernel (:356-403).
+// Zero entries of R and J (R02, J00, J11, J12) are kept as terms: they leave
+// finite results unchanged and propagate non-finite inputs as the reference does.
+__device__ __forceinline__ void project_gaussian(const ViewConst& v, float px, float py, float pz,
+                                                 const float cw[6], Proj& o) {
+  const float ca = v.cos_a, sa = v.sin_a, cb = v.cos_b, sb = v.sin_b;
+  const float rho_r = v.h.rho_r, rho_a = v.h.rho_a;
+
+  const float dx = sub_(px, v.h.radar_x);
+  const float dy = sub_(py, v.h.radar_y);
+  const float dz = sub_(pz, v.h.radar_z);
+  const float xr = fma_(ca, dx, mul_(sa, dy));
+  const float yr = fma_(-sb, dz, fma_(mul_(cb, sa), dx, -mul_(mul_(cb, ca), dy)));
+  const float zr = fma_(-cb, dz, fma_(mul_(sb, ca), dy, -mul_(mul_(sb, sa), dx)));
+  o.xr = xr;
+  o.yr = yr;
+  o.zr = zr;
+
+  const float Rmin = sqrt_(add_(fma_(yr, yr, mul_(zr, zr)), kEps * kEps));
+  o.r = sub_(add_(div_(Rmin, rho_r), mul_((float)v.h.Nr, 0.5f)), div_(v.h.Rc, rho_r));
+  o.c = add_(div_(xr, rho_a), mul_((float)v.h.Na, 0.5f));
+
+  const float x6[6] = {cw[0], cw[1], cw[2], cw[3], cw[4], cw[5]};  // xx yy zz xy xz yz
+  const float R00 = ca, R01 = sa, R02 = 0.0f;
+  const float R10 = mul_(cb, sa), R11 = -mul_(cb, ca), R12 = -sb;
+  const float R20 = -mul_(sb, sa), R21 = mul_(sb, ca), R22 = -cb;
+  const float kXX[6] = {mul_(R00, R00), mul_(R01, R01), mul_(R02, R02), mul_(mul_(2.0f, R00), R01),
+                        mul_(mul_(2.0f, R00), R02), mul_(mul_(2.0f, R01), R02)};
+  const float kYY[6] = {mul_(R10, R10), mul_(R11, R11), mul_(R12, R12), mul_(mul_(2.0f, R10), R11),
+                        mul_(mul_(2.0f, R10), R12), mul_(mul_(2.0f, R11), R12)};
+  const float kZZ[6] = {mul_(R20, R20), mul_(R21, R21), mul_(R22, R22), mul_(mul_(2.0f, R20), R21),
+                        mul_(mul_(2.0f, R20), R22), mul_(mul_(2.0f, R21), R22)};
+  const float kXY[6] = {mul_(R00, R10), mul_(R01, R11), mul_(R02, R12), fma_(R00, R11, mul_(R01, R10)),
+                        fma_(R00, R12, mul_(R02, R10)), fma_(R01, R12, mul_(R02, R11))};
+  const float kXZ[6] = {mul_(R00, R20), mul_(R01, R21), mul_(R02, R22), fma_(R00, R21, mul_(R01, R20)),
+                        fma_(R00, R22, mul_(R02, R20)), fma_(R01, R22, mul_(R02, R21))};
+  const float kYZ[6] = {mul_(R10, R20), mul_(R11, R21), mul_(R12, R22), fma_(R10, R21, mul_(R11, R20)),
+                        fma_(R12, R20, mul_(R10, R22)), fma_(R12, R21, mul_(R11, R22))};
+  const float XX = chain6(kXX, x6), YY = chain6(kYY, x6), ZZ = chain6(kZZ, x6);
+  const float XY = chain6(kXY, x6), XZ = chain6(kXZ, x6), YZ = chain6(kYZ, x6);
+  const float X6[6] = {XX, YY, ZZ, XY, XZ, YZ};
+
+  const float J00 = 0.0f, J11 = 0.0f, J12 = 0.0f;
+  const float J01 = div_(yr, mul_(rho_r, Rmin));
+  const float J02 = div_(zr, mul_(rho_r, Rmin));
+  const float J10 = div_(1.0f, rho_a);
+  const float krr[6] = {mul_(J00, J00), mul_(J01, J01), mul_(J02, J02), mul_(mul_(2.0f, J00), J01),
+                        mul_(mul_(2.0f, J00), J02), mul_(mul_(2.0f, J01), J02)};
+  const float kcc[6] = {mul_(J10, J10), mul_(J11, J11), mul_(J12, J12), mul_(mul_(2.0f, J10), J11),
+                        mul_(mul_(2.0f, J10), J12), mul_(mul_(2.0f, J11), J12)};
+  const float krc[6] = {mul_(J00, J10), mul_(J01, J11), mul_(J02, J12), fma_(J01, J10, mul_(J00, J11)),
+                        fma_(J02, J10, mul_(J00, J12)), fma_(J01, J12, mul_(J02, J11))};
+  o.cov_rr = chain6(krr, X6);
+  o.cov_cc = chain6(kcc, X6);
+  o.cov_rc = chain6(krc, X6);
+
+  o.XX = XX;
+  o.YY = YY;
+  o.XY = XY;
+}
+
+// preprocess_kernel's validity test (:405-406); the sigma < 0.01 test
+// (:351) is applied by the callers before projecting.
+__device__ __forceinline__ bool proj_valid(const Proj& o, int Nr, int Na) {
+  return (o.r >= 0 && o.r < (float)Nr && o.c >= 0 && o.c < (float)Na);
+}
+
+// compute_ranges_kernel for a valid Gaussian (:446-464).
+__device__ __forceinline__ void ipp_ranges(const Proj& o, int Nr, int Na, int& r_min, int& r_max,
+                                           int& c_min, int& c_max) {
+  const float cov_rr = o.cov_rr, cov_cc = o.cov_cc, cov_rc = o.cov_rc;
+  float det = fma_(cov_rr, cov_cc, -mul_(cov_rc, cov_rc));
+  if (det < kEps) det = kEps;
+  const float inv_det = div_(1.0f, det);
+  const float std_r = sqrt_(fmaxf(mul_(mul_(cov_rr, cov_cc), inv_det), kEps));
+  const float std_c = sqrt_(fmaxf(mul_(mul_(cov_cc, cov_rr), inv_det), kEps));
+  r_min = (int)floorf(fma_(-3.0f, std_r, o.r));
+  r_max = (int)ceilf(fma_(3.0f, std_r, o.r));
+  c_min = (int)floorf(fma_(-3.0f, std_c, o.c));
+  c_max = (int)ceilf(fma_(3.0f, std_c, o.c));
+  r_min = max(0, r_min);
+  r_max = min(Nr - 1, r_max);
+  c_min = max(0, c_min);
+  c_max = min(Na - 1, c_max);
+}
+
+// build_shadow_tile_list_kernel's footprint of a valid Gaussian (:572-597).
+// Returns false when |det| < EPSILON (the reference skips the Gaussian).
+__device__ __forceinline__ bool shadow_ranges(const Proj& o, int Nr, int Na, int& r_min, int& r_max,
+                                              int& c_min, int& c_max) {
+  const float mux = o.xr, muy = o.yr;
+  const float cov_xx = o.XX, cov_yy = o.YY, cov_xy = o.XY;
+  const float det = fma_(cov_xx, cov_yy, -mul_(cov_xy, cov_xy));
+  if (fabsf(det) < kEps) return false;
+  const float inv_det = div_(1.0f, det);
+  const float std_xy = sqrt_(fmaxf(mul_(mul_(cov_xx, cov_yy), inv_det), kEps));  // std_x == std_y
+  c_min = (int)floorf(fma_(-3.0f, std_xy, mux));
+  c_max = (int)ceilf(fma_(3.0f, std_xy, mux));
+  r_min = (int)floorf(fma_(-3.0f, std_xy, muy));
+  r_max = (int)ceilf(fma_(3.0f, std_xy, muy));
+  c_min = max(0, c_min);
+  c_max = min(Na - 1, c_max);
+  r_min = max(0, r_min);
+  r_max = min(Nr - 1, r_max);
+  return true;
+}
+
+// Tiles hit by a pixel bbox, packed as 4 bytes (tc0, tc1, tr0, tr1).
+// The reference hit test for tile (tr, tc) (:511-529) is
+//   !(r_max < 16 tr || r_min > min(16 tr + 16, Nr) || c_max < 16 tc || c_min > min(16 tc + 16, Na))
+// (an inclusive upper pixel bound, so neighbouring tiles overlap by one
+// pixel). Solved for the tile index: tr in [ceil((r_min-16)/16), floor(r_max/16)]
+// when 0 <= r_max and r_min <= Nr, otherwise no tile.
+__host__ __device__ __forceinline__ uint32_t make_rect(int r_min, int r_max, int c_min, int c_max,
+                                                       int Nr, int Na) {
+  if (r_max < 0 || c_max < 0 || r_min > Nr || c_min > Na) return kEmptyRect;
+  const int tr0 = (r_min > 0 ? r_min - 1 : 0) / kTile;
+  const int tr1 = r_max / kTile;
+  const int tc0 = (c_min > 0 ? c_min - 1 : 0) / kTile;
+  const int tc1 = c_max / kTile;
+  if (tr0 > tr1 || tc0 > tc1) return kEmptyRect;
+  return (uint32_t)tc0 | ((uint32_t)tc1 << 8) | ((uint32_t)tr0 << 16) | ((uint32_t)tr1 << 24);
+}
+
+__host__ __device__ __forceinline__ bool rect_has(uint32_t rc, int tx, int ty) {
+  const int tc0 = rc & 0xFF, tc1 = (rc >> 8) & 0xFF, tr0 = (rc >> 16) & 0xFF, tr1 = rc >> 24;
+  return tx >= tc0 && tx <= tc1 && ty >= tr0 && ty <= tr1;
+}
+
+// compute_sh_scattering_with_basis (:236-244).
+__device__ __forceinline__ float sh_scattering(const ViewConst& v, const float* __restrict__ row,
+                                               int sh_k) {
+  float scattering = mul_(sh_k > 0 ? row[0] : 0.0f, v.h.sh_basis[0]);
+#pragma unroll
+  for (int i = 1; i < kSh; i++) {
+    const float ci = i < sh_k ? row[i] : 0.0f;
+    scattering = fma_(ci, v.h.sh_basis[i], scattering);
+  }
+  const float LEAKY_ALPHA = 0.1f;
+  return scattering > 0.0f ? scattering : mul_(LEAKY_ALPHA, scattering);
+}
+
+constexpr float kTwoPi = 2.0f * kPi;
+
+// The per-Gaussian constants of compute_gaussian_density_2d (:223-226, :231).
+__device__ __forceinline__ void rec_density_consts(Rec& g) {
+  const float det = fma_(g.cxx, g.cyy, -mul_(g.cxy, g.cxy));
+  if (fabsf(det) < kEps) {
+    g.inv_det = 0.0f;
+    g.norm = -1.0f;
+  } else {
+    g.inv_det = div_(1.0f, det);
+    g.norm = mul_(kTwoPi, sqrt_(det));
+  }
+}
+
+// compute_gaussian_density_2d (:215-234) at pixel (px, py) = (pix_c, pix_r).
+__device__ __forceinline__ float rec_density(const Rec& g, float px, float py) {
+  if (g.norm < 0.0f) return 0.0f;
+  const float dx = sub_(px, g.mx);
+  const float dy = sub_(py, g.my);
+  const float q = fma_(mul_(g.cxx, dy), dy,
+                       fma_(mul_(g.cyy, dx), dx, -mul_(mul_(mul_(2.0f, g.cxy), dx), dy)));
+  const float exponent = mul_(mul_(-0.5f, q), g.inv_det);
+  if (exponent < -20.0f) return 0.0f;
+  const float result = div_(expf(exponent), g.norm);
+  return fmaxf(result, 0.0f);
+}
+
+// ---------------------------------------------------------------------------
+// TMA bulk copy (cp.async.bulk, no multicast) and mbarrier helpers.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+
+// Global -> shared bulk copy; dst, src 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void tma_load_1d(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// Waits for phase `parity` of the barrier for at most ~2 s of SM clock. On
+// expiry it records kDevErrTmaTimeout, waits once more (bounded) so that no
+// copy into this CTA's shared memory is left in flight when the caller
+// returns, and reports failure.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* err) {
+  const long long limit = 4000000000LL;
+  long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (clock64() - t0 > limit) {
+      if (err) atomicOr(err, kDevErrTmaTimeout);
+      t0 = clock64();
+      while (!mbar_try_wait(bar, parity)) {
+        if (clock64() - t0 > limit) break;
+      }
+      return false;
+    }
+  }
+  return true;
+}
+
+__device__ __forceinline__ float warp_sum(float x) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+  return x;
+}
+
+}  // namespace sarr

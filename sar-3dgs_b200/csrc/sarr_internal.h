@@ -1,0 +1,200 @@
+// Internal interface between the C ABI layer (sarr_abi.cu) and the kernels
+// (sarr_kernels.cu): memory layouts of the per-view state and the workspace,
+// kernel argument blocks and launch wrappers.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "sarr_common.cuh"
+
+namespace sarr {
+
+__host__ __device__ inline size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+// Image / tiling geometry of one call (all views of a call share it).
+struct Dims {
+  int64_t n;
+  int Nr, Na;
+  int tiles_x, tiles_y, T;
+  int C;  // count rows: ceil(n / kChunk)
+};
+
+// Per-view forward state. The image-plane list is what the backward reuses;
+// the shadow list (same layout, yz unused) only lives in the workspace.
+//   rects  [n] u32   tile rectangle of each Gaussian (kEmptyRect when invalid)
+//   count  [T] i32   list length (<= 64)
+//   list   [T][64]   Gaussian ids in index order (the reference's tile list)
+//   yz     [T][64]   (Y_r, Z_r) of list slot s (backward chain)
+//   recs   [T][64]   Rec in compositing (Z_r, index) order
+struct StateLayout {
+  size_t rects, count, list, yz, recs, bytes;
+};
+
+__host__ __device__ inline StateLayout state_layout(int64_t n, int T) {
+  StateLayout L;
+  size_t o = 0;
+  L.rects = o;
+  o += align256((size_t)n * 4);
+  L.count = o;
+  o += align256((size_t)T * 4);
+  L.list = o;
+  o += align256((size_t)T * kCap * 4);
+  L.yz = o;
+  o += align256((size_t)T * kCap * 8);
+  L.recs = o;
+  o += align256((size_t)T * kCap * sizeof(Rec));
+  L.bytes = o;
+  return L;
+}
+
+// Workspace: [ViewConst x 32][error word][per-view areas x group]
+//   per view: counts_ipp [C][T] u8, counts_sh [C][T] u8, state_ipp (used when
+//   the caller gives no state), state_sh, partial_om [T][64] float2,
+//   partial_bwd [T][64][8] float.
+struct WsLayout {
+  size_t viewconst, err, head;
+  size_t counts_ipp, counts_sh, state_ipp, state_sh, partial_om, partial_bwd, per_view;
+  StateLayout st;
+};
+
+__host__ inline WsLayout ws_layout(const Dims& d) {
+  WsLayout L;
+  L.viewconst = 0;
+  L.err = align256(sizeof(ViewConst) * kMaxViewsPerLaunch);
+  L.head = L.err + 256;
+  L.st = state_layout(d.n, d.T);
+  size_t o = 0;
+  L.counts_ipp = o;
+  o += align256((size_t)d.C * d.T);
+  L.counts_sh = o;
+  o += align256((size_t)d.C * d.T);
+  L.state_ipp = o;
+  o += L.st.bytes;
+  L.state_sh = o;
+  o += L.st.bytes;
+  L.partial_om = o;
+  o += align256((size_t)d.T * kCap * 8);
+  L.partial_bwd = o;
+  o += align256((size_t)d.T * kCap * 8 * 4);
+  L.per_view = o;
+  return L;
+}
+
+// A strided family of per-view state buffers.
+struct StateRef {
+  unsigned char* base;
+  size_t vstride;
+  StateLayout L;
+};
+
+struct BinArgs {
+  const ViewConst* views;
+  int64_t n;
+  int C;
+  const float* means;
+  const float* cov;
+  int cov_layout;
+  const float* sigma;
+  StateRef ipp;  // rects written into ipp.base + v * vstride + L.rects
+  StateRef sh;   // used when the shadow list is built
+  uint8_t* counts_ipp;
+  uint8_t* counts_sh;
+  size_t counts_vstride;
+  int use_tma;
+  int* err;
+};
+
+struct SelectArgs {
+  const ViewConst* views;
+  int64_t n;
+  int C;
+  const float* means;
+  const float* cov;
+  int cov_layout;
+  const float* sigma;
+  const float* sh;
+  int sh_stride;
+  int sh_k;
+  StateRef st;
+  const uint8_t* counts;
+  size_t counts_vstride;
+  int* err;
+};
+
+struct TileArgs {
+  const ViewConst* views;
+  StateRef st;
+  float* images;  // render: output; backward: (const) grad images
+  size_t img_vstride;
+  float* partial;  // omega: float2 [T][64]; backward: float [T][64][8]
+  size_t partial_vstride;
+  int* err;
+};
+
+struct OmegaScatterArgs {
+  const ViewConst* views;
+  int64_t n;
+  StateRef sh;
+  const float* partial;
+  size_t partial_vstride;
+  float* omega;
+  size_t omega_vstride;
+};
+
+struct BwdScatterArgs {
+  const ViewConst* views;
+  int nviews;
+  int64_t n;
+  StateRef ipp;
+  const float* partial;
+  size_t partial_vstride;
+  float* grad_means;
+  float* grad_cov;
+  int grad_cov_layout;
+  float* grad_sigma;
+  float* grad_sh;
+  int grad_sh_cols;
+  float* grad_norm;
+  int accumulate;
+};
+
+struct DebugPreArgs {
+  ViewHost vh;
+  int64_t n;
+  const float* means;
+  const float* cov;
+  int cov_layout;
+  const float* sigma;
+  const float* sh;
+  int sh_stride;
+  int sh_k;
+  float* f32;
+  int32_t* i32;
+};
+
+struct DebugListArgs {
+  int T;
+  StateRef st;
+  int32_t* counts;
+  int32_t* lists;
+  int32_t* sorted;
+};
+
+// Launch wrappers; each returns the cudaError_t of the launch.
+cudaError_t launch_view_setup(const ViewHostPack& pack, ViewConst* out, cudaStream_t s);
+cudaError_t launch_bin(const BinArgs& a, const Dims& d, int nviews, bool shadow, cudaStream_t s);
+cudaError_t launch_select(const SelectArgs& a, const Dims& d, int nviews, bool shadow_list,
+                          cudaStream_t s);
+cudaError_t launch_render(const TileArgs& a, const Dims& d, int nviews, cudaStream_t s);
+cudaError_t launch_omega_tile(const TileArgs& a, const Dims& d, int nviews, cudaStream_t s);
+cudaError_t launch_omega_scatter(const OmegaScatterArgs& a, const Dims& d, int nviews,
+                                 cudaStream_t s);
+cudaError_t launch_bwd_tile(const TileArgs& a, const Dims& d, int nviews, cudaStream_t s);
+cudaError_t launch_bwd_scatter(const BwdScatterArgs& a, const Dims& d, cudaStream_t s);
+cudaError_t launch_debug_preprocess(const DebugPreArgs& a, cudaStream_t s);
+cudaError_t launch_debug_lists(const DebugListArgs& a, cudaStream_t s);
+cudaError_t launch_debug_view(const ViewHost& vh, float* out, cudaStream_t s);
+
+}  // namespace sarr

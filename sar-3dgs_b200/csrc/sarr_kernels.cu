@@ -1,0 +1,844 @@
+// Kernels of the B200 SAR rasterizer.
+//
+// Forward pipeline per view (replaces preprocess_kernel, compute_ranges_kernel,
+// build_tile_gaussian_list_kernel, build_shadow_tile_list_kernel,
+// compute_omega_kernel, the host Omega average and render_kernel of
+// cuda_rasterizer/rasterizer_impl_v2.cu:322-839, :1239-1252):
+//
+//   bin_kernel       one CTA per chunk of 512 Gaussians: TMA bulk copy of the
+//                    chunk's means/cov/sigma into shared memory, projection,
+//                    validity, pixel bbox -> tile rectangle (4 bytes per list),
+//                    and a per-chunk per-tile hit count built with a 2-D
+//                    difference array (4 shared atomics per Gaussian however
+//                    many tiles it covers).
+//   select_kernel    one CTA per tile: scan of the chunk counts, then each
+//                    needed chunk is re-scanned with warp ballots so that the
+//                    first 64 hits in index order land in their slots; the
+//                    selected Gaussians are projected again (SH only for them),
+//                    ranked by (Z_r, index) and stored as 48-byte records.
+//   render_kernel    one warp per 2 tile columns: TMA bulk copy of the tile's
+//                    sorted records, front-to-back compositing.
+//   omega_tile_kernel / omega_scatter_kernel
+//                    per-pixel Omega walk with per-slot warp reductions, then
+//                    a per-Gaussian gather of those partial sums.
+//
+// Backward (replaces backward_kernel :841-1020): bwd_tile_kernel replays each
+// pixel front to back and reduces the 7 per-(pixel, Gaussian) terms over the
+// tile with warp shuffles; bwd_scatter_kernel gathers them per Gaussian and
+// writes the dense gradient rows, applying the per-Gaussian chain rule once.
+// No float atomics: results are deterministic.
+#include "sarr_internal.h"
+
+namespace sarr {
+
+// ---------------------------------------------------------------------------
+// view setup
+// ---------------------------------------------------------------------------
+__global__ void view_setup_kernel(const ViewHostPack pack, ViewConst* __restrict__ out) {
+  const int v = threadIdx.x;
+  if (v >= pack.n) return;
+  ViewConst c;
+  c.h = pack.v[v];
+  c.cos_a = cosf(c.h.alpha);
+  c.sin_a = sinf(c.h.alpha);
+  c.cos_b = cosf(c.h.beta);
+  c.sin_b = sinf(c.h.beta);
+  c.tiles_x = (c.h.Na + kTile - 1) / kTile;
+  c.tiles_y = (c.h.Nr + kTile - 1) / kTile;
+  c.pad0 = 0;
+  c.pad1 = 0;
+  out[v] = c;
+}
+
+// ---------------------------------------------------------------------------
+// binning
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void diff_add(int* d, int pitch, uint32_t rc) {
+  const int tc0 = rc & 0xFF, tc1 = (rc >> 8) & 0xFF, tr0 = (rc >> 16) & 0xFF, tr1 = rc >> 24;
+  if (tc0 > tc1) return;
+  atomicAdd(&d[tr0 * pitch + tc0], 1);
+  atomicAdd(&d[tr0 * pitch + tc1 + 1], -1);
+  atomicAdd(&d[(tr1 + 1) * pitch + tc0], -1);
+  atomicAdd(&d[(tr1 + 1) * pitch + tc1 + 1], 1);
+}
+
+template <bool kShadow>
+__global__ void __launch_bounds__(kBinThreads) bin_kernel(const BinArgs a) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  __shared__ uint64_t bar;
+
+  const int tid = threadIdx.x;
+  const int v = blockIdx.y;
+  const int chunk = blockIdx.x;
+  const ViewConst vc = a.views[v];
+  const int Nr = vc.h.Nr, Na = vc.h.Na;
+  const int tiles_x = vc.tiles_x, tiles_y = vc.tiles_y, T = tiles_x * tiles_y;
+  const int cs = a.cov_layout;
+
+  float* s_means = reinterpret_cast<float*>(smem_raw);
+  float* s_cov = s_means + 3 * kChunk;
+  float* s_sigma = s_cov + cs * kChunk;
+  int* s_diff_ipp = reinterpret_cast<int*>(s_sigma + kChunk);
+  const int pitch = tiles_x + 1;
+  const int T1 = (tiles_y + 1) * pitch;
+  int* s_diff_sh = s_diff_ipp + T1;
+
+  const int64_t base = (int64_t)chunk * kChunk;
+  const int gcount = (int)min((int64_t)kChunk, a.n - base);
+  const bool tma = a.use_tma && gcount == kChunk;
+
+  if (tid == 0 && tma) mbar_init(&bar, 1);
+  for (int i = tid; i < T1 * (kShadow ? 2 : 1); i += kBinThreads) s_diff_ipp[i] = 0;
+  __syncthreads();
+
+  bool ok = true;
+  if (tma) {
+    if (tid == 0) {
+      const uint32_t bm = 3u * kChunk * 4u, bc = (uint32_t)cs * kChunk * 4u, bs = kChunk * 4u;
+      mbar_arrive_expect_tx(&bar, bm + bc + bs);
+      tma_load_1d(s_means, a.means + base * 3, bm, &bar);
+      tma_load_1d(s_cov, a.cov + base * cs, bc, &bar);
+      tma_load_1d(s_sigma, a.sigma + base, bs, &bar);
+    }
+    ok = mbar_wait_bounded(&bar, 0, a.err);
+  } else {
+    for (int i = tid; i < 3 * gcount; i += kBinThreads) s_means[i] = a.means[base * 3 + i];
+    for (int i = tid; i < cs * gcount; i += kBinThreads) s_cov[i] = a.cov[base * cs + i];
+    for (int i = tid; i < gcount; i += kBinThreads) s_sigma[i] = a.sigma[base + i];
+  }
+  if (!__syncthreads_and(ok)) return;
+
+  uint32_t* rects_ipp = reinterpret_cast<uint32_t*>(a.ipp.base + v * a.ipp.vstride + a.ipp.L.rects);
+  uint32_t* rects_sh =
+      kShadow ? reinterpret_cast<uint32_t*>(a.sh.base + v * a.sh.vstride + a.sh.L.rects) : nullptr;
+
+#pragma unroll
+  for (int k = 0; k < kBinPerThread; ++k) {
+    const int j = tid + k * kBinThreads;
+    if (j < gcount) {
+      uint32_t rc_ipp = kEmptyRect, rc_sh = kEmptyRect;
+      const float sigma = s_sigma[j];
+      if (!(sigma < 0.01f)) {  // preprocess_kernel: transmittance < 0.01 -> invalid (:351)
+        float cw[6];
+        load_cov6(s_cov + j * cs, cs, cw);
+        Proj o;
+        project_gaussian(vc, s_means[3 * j], s_means[3 * j + 1], s_means[3 * j + 2], cw, o);
+        if (proj_valid(o, Nr, Na)) {
+          int r0, r1, c0, c1;
+          ipp_ranges(o, Nr, Na, r0, r1, c0, c1);
+          rc_ipp = make_rect(r0, r1, c0, c1, Nr, Na);
+          if (kShadow) {
+            if (shadow_ranges(o, Nr, Na, r0, r1, c0, c1)) rc_sh = make_rect(r0, r1, c0, c1, Nr, Na);
+          }
+        }
+      }
+      rects_ipp[base + j] = rc_ipp;
+      diff_add(s_diff_ipp, pitch, rc_ipp);
+      if (kShadow) {
+        rects_sh[base + j] = rc_sh;
+        diff_add(s_diff_sh, pitch, rc_sh);
+      }
+    }
+  }
+  __syncthreads();
+
+  // 2-D inclusive prefix of the difference arrays: rows, then columns.
+  // Threads [0,128) handle the image-plane list, [128,256) the shadow list.
+  {
+    const int half = tid >> 7, i = tid & 127;
+    if (half == 0 || kShadow) {
+      int* d = half ? s_diff_sh : s_diff_ipp;
+      if (i < tiles_y) {
+        int run = 0;
+        for (int x = 0; x < tiles_x; ++x) {
+          run += d[i * pitch + x];
+          d[i * pitch + x] = run;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  {
+    const int half = tid >> 7, i = tid & 127;
+    if (half == 0 || kShadow) {
+      int* d = half ? s_diff_sh : s_diff_ipp;
+      if (i < tiles_x) {
+        int run = 0;
+        for (int y = 0; y < tiles_y; ++y) {
+          run += d[y * pitch + i];
+          d[y * pitch + i] = run;
+        }
+      }
+    }
+  }
+  __syncthreads();
+
+  uint8_t* cnt_ipp = a.counts_ipp + v * a.counts_vstride + (size_t)chunk * T;
+  uint8_t* cnt_sh = kShadow ? a.counts_sh + v * a.counts_vstride + (size_t)chunk * T : nullptr;
+  for (int t = tid; t < T; t += kBinThreads) {
+    const int y = t / tiles_x, x = t - y * tiles_x;
+    cnt_ipp[t] = (uint8_t)min(s_diff_ipp[y * pitch + x], 255);
+    if (kShadow) cnt_sh[t] = (uint8_t)min(s_diff_sh[y * pitch + x], 255);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// capped tile selection + tile records
+// ---------------------------------------------------------------------------
+template <bool kShadowList>
+__global__ void __launch_bounds__(kSelectThreads) select_kernel(const SelectArgs a) {
+  __shared__ int s_warp[kSelectThreads / 32];
+  __shared__ int s_nneed;
+  __shared__ int4 s_need[kCap];
+  __shared__ int s_list[kCap];
+  __shared__ __align__(16) Rec s_rec[kCap];
+  __shared__ float s_z[kCap];
+  __shared__ int s_rank[kCap];
+
+  const int t = blockIdx.x, v = blockIdx.y;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const ViewConst& vc = a.views[v];
+  const int tiles_x = vc.tiles_x, T = tiles_x * vc.tiles_y;
+  const int tx = t % tiles_x, ty = t / tiles_x;
+  const uint8_t* counts = a.counts + v * a.counts_vstride;
+  unsigned char* st = a.st.base + v * a.st.vstride;
+  int* st_count = reinterpret_cast<int*>(st + a.st.L.count);
+
+  // 1. per-tile totals over the chunk rows, block exclusive scan.
+  const int C = a.C;
+  const int cpt = (C + kSelectThreads - 1) / kSelectThreads;
+  const int c0 = min(tid * cpt, C), c1 = min(c0 + cpt, C);
+  int local = 0;
+  for (int c = c0; c < c1; ++c) local += counts[(size_t)c * T + t];
+  int incl = local;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  if (lane == 31) s_warp[warp] = incl;
+  if (tid == 0) s_nneed = 0;
+  if (tid < kCap) s_list[tid] = -1;
+  __syncthreads();
+  int wpre = 0, total = 0;
+#pragma unroll
+  for (int w = 0; w < kSelectThreads / 32; ++w) {
+    const int x = s_warp[w];
+    wpre += (w < warp) ? x : 0;
+    total += x;
+  }
+  const int count = min(total, kCap);
+  if (count == 0) {
+    if (tid == 0) st_count[t] = 0;
+    return;
+  }
+  // chunks holding slots < 64
+  int pre = wpre + incl - local;
+  for (int c = c0; c < c1 && pre < kCap; ++c) {
+    const int cnt = counts[(size_t)c * T + t];
+    if (cnt > 0) {
+      const int q = atomicAdd(&s_nneed, 1);
+      s_need[q] = make_int4(c, pre, cnt, 0);
+    }
+    pre += cnt;
+  }
+  __syncthreads();
+
+  // 2. emit: the hits of each needed chunk in index order.
+  const uint32_t* rects = reinterpret_cast<const uint32_t*>(st + a.st.L.rects);
+  const int nneed = s_nneed;
+  for (int q = warp; q < nneed; q += kSelectThreads / 32) {
+    const int4 nd = s_need[q];
+    const int need = min(nd.z, kCap - nd.y);
+    const int64_t b0 = (int64_t)nd.x * kChunk;
+    const int64_t b1 = min(b0 + kChunk, a.n);
+    int found = 0;
+    for (int64_t j0 = b0; j0 < b1 && found < need; j0 += 32) {
+      const int64_t j = j0 + lane;
+      const bool hit = (j < b1) && rect_has(rects[j], tx, ty);
+      const unsigned m = __ballot_sync(0xffffffffu, hit);
+      if (hit) {
+        const int rk = found + __popc(m & ((1u << lane) - 1u));
+        if (rk < need) s_list[nd.y + rk] = (int)j;
+      }
+      found += __popc(m);
+    }
+  }
+  __syncthreads();
+
+  // 3. records of the selected Gaussians.
+  bool nan_z = false;
+  if (tid < count && (s_list[tid] < 0 || (int64_t)s_list[tid] >= a.n)) {
+    // The chunk counts and the rectangles come from the same bin pass, so every
+    // slot below `count` is filled; this guard only keeps a corrupted
+    // workspace from turning into an out-of-range gather.
+    atomicOr(a.err, kDevErrListSlot);
+    s_list[tid] = 0;
+  }
+  if (tid < count) {
+    const int id = s_list[tid];
+    float cw[6];
+    load_cov6(a.cov + (size_t)id * a.cov_layout, a.cov_layout, cw);
+    const float* m = a.means + (size_t)id * 3;
+    Proj o;
+    project_gaussian(vc, m[0], m[1], m[2], cw, o);
+    Rec g;
+    if (!kShadowList) {
+      g.mx = o.c;
+      g.my = o.r;
+      g.cxx = o.cov_cc;
+      g.cxy = o.cov_rc;
+      g.cyy = o.cov_rr;
+      const float S = sh_scattering(vc, a.sh + (size_t)id * a.sh_stride, a.sh_k);
+      g.s_pos = fmaxf(0.0f, S);
+    } else {
+      g.mx = o.xr;
+      g.my = o.yr;
+      g.cxx = o.XX;
+      g.cxy = o.XY;
+      g.cyy = o.YY;
+      g.s_pos = 0.0f;
+    }
+    rec_density_consts(g);
+    g.sigma = a.sigma[id];
+    g.z = o.zr;
+    g.yr = o.yr;
+    g.pos = tid;
+    s_rec[tid] = g;
+    s_z[tid] = o.zr;
+    nan_z = (o.zr != o.zr);
+    if (!kShadowList) {
+      float2* yz = reinterpret_cast<float2*>(st + a.st.L.yz);
+      yz[(size_t)t * kCap + tid] = make_float2(o.yr, o.zr);
+    }
+  }
+
+  // 4. rank by (Z_r, slot): equal to the reference's stable insertion sort on
+  // Z_r with strict '>' (:795-807) whenever no Z_r is NaN; with a NaN the
+  // insertion sort itself is replayed.
+  if (__syncthreads_or(nan_z)) {
+    if (tid == 0) {
+      int idx[kCap];
+      float zv[kCap];
+      for (int i = 0; i < count; ++i) {
+        idx[i] = i;
+        zv[i] = s_z[i];
+      }
+      for (int i = 1; i < count; ++i) {
+        const int ti = idx[i];
+        const float tz = zv[i];
+        int j = i - 1;
+        while (j >= 0 && zv[j] > tz) {
+          idx[j + 1] = idx[j];
+          zv[j + 1] = zv[j];
+          j--;
+        }
+        idx[j + 1] = ti;
+        zv[j + 1] = tz;
+      }
+      for (int k = 0; k < count; ++k) s_rank[idx[k]] = k;
+    }
+  } else if (tid < count) {
+    const float z = s_z[tid];
+    int rk = 0;
+    for (int j = 0; j < count; ++j) {
+      const float zj = s_z[j];
+      rk += (zj < z) || (zj == z && j < tid);
+    }
+    s_rank[tid] = rk;
+  }
+  __syncthreads();
+
+  // 5. state
+  if (tid == 0) st_count[t] = count;
+  if (tid < count) {
+    int* st_list = reinterpret_cast<int*>(st + a.st.L.list);
+    Rec* st_recs = reinterpret_cast<Rec*>(st + a.st.L.recs);
+    st_list[(size_t)t * kCap + tid] = s_list[tid];
+    st_recs[(size_t)t * kCap + s_rank[tid]] = s_rec[tid];
+  }
+}
+
+// ---------------------------------------------------------------------------
+// compositing
+// ---------------------------------------------------------------------------
+// Loads the `count` sorted records of tile t into shared memory with one TMA
+// bulk copy. Every thread of the CTA must call it.
+__device__ __forceinline__ bool load_tile_recs(Rec* s_rec, uint64_t* bar, const unsigned char* st,
+                                               const StateLayout& L, int t, int count, int* err,
+                                               bool whole_block) {
+  if (threadIdx.x == 0) mbar_init(bar, 1);
+  if (whole_block) __syncthreads(); else __syncwarp();
+  if (threadIdx.x == 0) {
+    const uint32_t bytes = (uint32_t)count * (uint32_t)sizeof(Rec);
+    mbar_arrive_expect_tx(bar, bytes);
+    tma_load_1d(s_rec, st + L.recs + (size_t)t * kCap * sizeof(Rec), bytes, bar);
+  }
+  return mbar_wait_bounded(bar, 0, err);
+}
+
+__global__ void __launch_bounds__(32) render_kernel(const TileArgs a) {
+  __shared__ __align__(16) Rec s_rec[kCap];
+  __shared__ uint64_t bar;
+  const int v = blockIdx.y;
+  const int t = blockIdx.x / kWarpsPerTile, slab = blockIdx.x % kWarpsPerTile;
+  const int lane = threadIdx.x;
+  const ViewConst& vc = a.views[v];
+  const int Nr = vc.h.Nr, Na = vc.h.Na, tiles_x = vc.tiles_x;
+  const int tx = t % tiles_x, ty = t / tiles_x;
+  const int pc = tx * kTile + slab * 2 + (lane >> 4);
+  const int pr = ty * kTile + (lane & 15);
+  const bool in = pc < Na && pr < Nr;
+  const unsigned char* st = a.st.base + v * a.st.vstride;
+  const int count = reinterpret_cast<const int*>(st + a.st.L.count)[t];
+
+  float pixel_value = 0.0f;
+  if (count > 0) {
+    const bool ok = load_tile_recs(s_rec, &bar, st, a.st.L, t, count, a.err, false);
+    if (__all_sync(0xffffffffu, ok)) {
+      float transmittance_acc = 1.0f;
+      const float fx = (float)pc, fy = (float)pr;
+      for (int k = 0; k < count; ++k) {
+        const Rec& g = s_rec[k];
+        const float gamma_ipp = rec_density(g, fx, fy);
+        if (gamma_ipp < 1e-8f) continue;
+        const float alpha_i = mul_(g.sigma, gamma_ipp);
+        pixel_value = fma_(mul_(transmittance_acc, alpha_i), g.s_pos, pixel_value);
+        transmittance_acc = mul_(transmittance_acc, fma_(-g.sigma, gamma_ipp, 1.0f));
+        if (transmittance_acc < 1e-8f) {
+          transmittance_acc = 0.0f;
+          break;
+        }
+      }
+    }
+  }
+  if (in) a.images[v * a.img_vstride + (size_t)pc * Nr + pr] = pixel_value;
+}
+
+// Omega per pixel (compute_omega_kernel :696-718): Omega_before of every
+// listed Gaussian reached by the pixel is summed over the tile's pixels with
+// warp reductions; partial[t][slot] = (sum, pixel count).
+__global__ void __launch_bounds__(kWarpsPerTile * 32) omega_tile_kernel(const TileArgs a) {
+  __shared__ __align__(16) Rec s_rec[kCap];
+  __shared__ float2 s_red[kWarpsPerTile][kCap];
+  __shared__ uint64_t bar;
+  const int v = blockIdx.y, t = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const ViewConst& vc = a.views[v];
+  const int Nr = vc.h.Nr, Na = vc.h.Na, tiles_x = vc.tiles_x;
+  const int tx = t % tiles_x, ty = t / tiles_x;
+  const unsigned char* st = a.st.base + v * a.st.vstride;
+  const int count = reinterpret_cast<const int*>(st + a.st.L.count)[t];
+  if (count == 0) return;
+  const bool ok = load_tile_recs(s_rec, &bar, st, a.st.L, t, count, a.err, true);
+  if (!__syncthreads_and(ok)) return;
+
+  const int pc = tx * kTile + warp * 2 + (lane >> 4);
+  const int pr = ty * kTile + (lane & 15);
+  bool alive = pc < Na && pr < Nr;
+  const float fx = (float)pc, fy = (float)pr;
+  float omega = 1.0f;
+  for (int k = 0; k < count; ++k) {
+    const unsigned counted = __ballot_sync(0xffffffffu, alive);
+    if (counted == 0) {
+      if (lane == 0)
+        for (int kk = k; kk < count; ++kk) s_red[warp][kk] = make_float2(0.0f, 0.0f);
+      break;
+    }
+    const float before = alive ? omega : 0.0f;
+    if (alive) {
+      const Rec& g = s_rec[k];
+      const float gamma_shadow = rec_density(g, fx, fy);
+      const float sigma_i = g.sigma;
+      omega = mul_(omega, fma_(-gamma_shadow, sigma_i, 1.0f));
+      if (omega < 1e-8f) {
+        omega = 0.0f;
+        alive = false;
+      }
+    }
+    const float sum = warp_sum(before);
+    if (lane == 0) s_red[warp][k] = make_float2(sum, (float)__popc(counted));
+  }
+  __syncthreads();
+  if (tid < count) {
+    float2 acc = make_float2(0.0f, 0.0f);
+#pragma unroll
+    for (int w = 0; w < kWarpsPerTile; ++w) {
+      acc.x += s_red[w][tid].x;
+      acc.y += s_red[w][tid].y;
+    }
+    float2* partial = reinterpret_cast<float2*>(a.partial + v * a.partial_vstride);
+    partial[(size_t)t * kCap + s_rec[tid].pos] = acc;
+  }
+}
+
+// Position of Gaussian i in the index-ordered list of tile t, or -1.
+__device__ __forceinline__ int list_find(const int* __restrict__ list, int cnt, int i) {
+  if (cnt <= 0 || i < list[0] || i > list[cnt - 1]) return -1;
+  int lo = 0, hi = cnt - 1;
+  while (lo <= hi) {
+    const int mid = (lo + hi) >> 1;
+    const int x = list[mid];
+    if (x == i) return mid;
+    if (x < i) lo = mid + 1; else hi = mid - 1;
+  }
+  return -1;
+}
+
+// Host-side Omega average (:1239-1252) as a gather over the tiles whose shadow
+// list contains the Gaussian.
+__global__ void __launch_bounds__(256) omega_scatter_kernel(const OmegaScatterArgs a) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int v = blockIdx.y;
+  if (i >= a.n) return;
+  const ViewConst& vc = a.views[v];
+  const int tiles_x = vc.tiles_x;
+  const unsigned char* st = a.sh.base + v * a.sh.vstride;
+  const uint32_t rc = reinterpret_cast<const uint32_t*>(st + a.sh.L.rects)[i];
+  float s = 0.0f, c = 0.0f;
+  const int tc0 = rc & 0xFF, tc1 = (rc >> 8) & 0xFF, tr0 = (rc >> 16) & 0xFF, tr1 = rc >> 24;
+  if (tc0 <= tc1) {
+    const int* cnts = reinterpret_cast<const int*>(st + a.sh.L.count);
+    const int* lists = reinterpret_cast<const int*>(st + a.sh.L.list);
+    const float2* partial = reinterpret_cast<const float2*>(a.partial + v * a.partial_vstride);
+    for (int ty = tr0; ty <= tr1; ++ty)
+      for (int tx = tc0; tx <= tc1; ++tx) {
+        const int t = ty * tiles_x + tx;
+        const int p = list_find(lists + (size_t)t * kCap, cnts[t], (int)i);
+        if (p >= 0) {
+          const float2 q = partial[(size_t)t * kCap + p];
+          s += q.x;
+          c += q.y;
+        }
+      }
+  }
+  a.omega[v * a.omega_vstride + i] = c > 0.0f ? s / c : 1.0f;
+}
+
+// ---------------------------------------------------------------------------
+// backward
+// ---------------------------------------------------------------------------
+// Per (pixel, Gaussian) terms of backward_kernel (:910-1018), summed over the
+// tile: 0 grad_sigma, 1 dL/dpixel * dpixel/dS (times the SH basis later),
+// 2..4 grad_cov rr, cc, rc, 5..6 grad_ipp_r, grad_ipp_c.
+__global__ void __launch_bounds__(kWarpsPerTile * 32) bwd_tile_kernel(const TileArgs a) {
+  __shared__ __align__(16) Rec s_rec[kCap];
+  __shared__ float s_red[kWarpsPerTile][kCap][8];
+  __shared__ uint64_t bar;
+  const int v = blockIdx.y, t = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const ViewConst& vc = a.views[v];
+  const int Nr = vc.h.Nr, Na = vc.h.Na, tiles_x = vc.tiles_x;
+  const int tx = t % tiles_x, ty = t / tiles_x;
+  const unsigned char* st = a.st.base + v * a.st.vstride;
+  const int count = reinterpret_cast<const int*>(st + a.st.L.count)[t];
+  if (count == 0) return;
+  const bool ok = load_tile_recs(s_rec, &bar, st, a.st.L, t, count, a.err, true);
+  if (!__syncthreads_and(ok)) return;
+
+  const int pc = tx * kTile + warp * 2 + (lane >> 4);
+  const int pr = ty * kTile + (lane & 15);
+  const bool in = pc < Na && pr < Nr;
+  const float dL_d_pixel = in ? a.images[v * a.img_vstride + (size_t)pc * Nr + pr] : 0.0f;
+  const float fx = (float)pc, fy = (float)pr;
+  float prev_transmittance = 1.0f;
+
+  for (int k = 0; k < count; ++k) {
+    const Rec& g = s_rec[k];
+    float A[7] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    bool contrib = false;
+    if (in) {
+      const float gamma_ipp = rec_density(g, fx, fy);
+      if (gamma_ipp >= 1e-8f) {
+        contrib = true;
+        const float sigma_i = g.sigma;
+        const float S_i = g.s_pos;
+        const float alpha_i = mul_(sigma_i, gamma_ipp);
+        const float d_pixel_d_alpha = mul_(prev_transmittance, S_i);
+        const float d_pixel_d_S = mul_(prev_transmittance, alpha_i);
+        const float g_a = mul_(dL_d_pixel, d_pixel_d_alpha);  // dL/dpixel * dpixel/dalpha
+        const float g_as = mul_(g_a, sigma_i);
+        A[0] = mul_(g_a, gamma_ipp);
+        A[1] = mul_(dL_d_pixel, d_pixel_d_S);
+        const float dx = sub_(fx, g.mx);
+        const float dy = sub_(fy, g.my);
+        const float cov_rr = g.cyy, cov_cc = g.cxx, cov_rc = g.cxy;
+        const float det = fma_(cov_rr, cov_cc, -mul_(cov_rc, cov_rc));
+        if (det > kEps) {
+          const float inv_det = div_(1.0f, det);
+          // the backward's own exponent pairs cov_cc with dx^2 and cov_rr with dy^2 (:950)
+          const float q = fma_(mul_(cov_rr, dy), dy,
+                               fma_(mul_(cov_cc, dx), dx, -mul_(mul_(mul_(2.0f, cov_rc), dx), dy)));
+          const float exponent = mul_(mul_(-0.5f, q), inv_det);
+          if (exponent > -20.0f) {
+            const float exp_val = expf(exponent);
+            const float base_val = div_(exp_val, mul_(kTwoPi, sqrt_(det)));
+            const float h = mul_(mul_(0.5f, base_val), inv_det);
+            const float d_gamma_d_cov_rr = mul_(h, fma_(dy, dy, -mul_(mul_(cov_cc, inv_det), 0.5f)));
+            const float d_gamma_d_cov_cc = mul_(h, fma_(dx, dx, -mul_(mul_(cov_rr, inv_det), 0.5f)));
+            const float d_gamma_d_cov_rc = mul_(mul_(mul_(-base_val, inv_det), dx), dy);
+            A[2] = mul_(g_as, d_gamma_d_cov_rr);
+            A[3] = mul_(g_as, d_gamma_d_cov_cc);
+            A[4] = mul_(g_as, d_gamma_d_cov_rc);
+          }
+        }
+        const float det_eps = add_(det, kEps);
+        const float d_center_dr = div_(-fma_(cov_rc, dx, -mul_(cov_rr, dy)), det_eps);
+        const float d_center_dc = div_(-fma_(cov_cc, dx, -mul_(cov_rc, dy)), det_eps);
+        A[5] = mul_(g_as, d_center_dr);
+        A[6] = mul_(g_as, d_center_dc);
+        prev_transmittance = mul_(prev_transmittance, fma_(-sigma_i, gamma_ipp, 1.0f));
+        if (prev_transmittance < 1e-8f) prev_transmittance = 0.0f;
+      }
+    }
+    if (__any_sync(0xffffffffu, contrib)) {
+#pragma unroll
+      for (int c = 0; c < 7; ++c) A[c] = warp_sum(A[c]);
+    }
+    if (lane == 0) {
+#pragma unroll
+      for (int c = 0; c < 7; ++c) s_red[warp][k][c] = A[c];
+    }
+  }
+  __syncthreads();
+  float* partial = a.partial + v * a.partial_vstride;
+  for (int e = tid; e < count * 7; e += kWarpsPerTile * 32) {
+    const int k = e / 7, c = e - k * 7;
+    float acc = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kWarpsPerTile; ++w) acc += s_red[w][k][c];
+    partial[((size_t)t * kCap + s_rec[k].pos) * 8 + c] = acc;
+  }
+}
+
+// Dense gradient rows. The per-Gaussian chain of backward_kernel (:979-1013)
+// is linear in (grad_ipp_r, grad_ipp_c), so it is applied once to the tile sums.
+__global__ void __launch_bounds__(256) bwd_scatter_kernel(const BwdScatterArgs a) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= a.n) return;
+  float g_sigma = 0.f, g_rr = 0.f, g_cc = 0.f, g_rc = 0.f, gx = 0.f, gy = 0.f, gz = 0.f;
+  float g_sh[kSh];
+#pragma unroll
+  for (int k = 0; k < kSh; ++k) g_sh[k] = 0.f;
+
+  for (int v = 0; v < a.nviews; ++v) {
+    const ViewConst& vc = a.views[v];
+    const int tiles_x = vc.tiles_x;
+    const unsigned char* st = a.ipp.base + v * a.ipp.vstride;
+    const uint32_t rc = reinterpret_cast<const uint32_t*>(st + a.ipp.L.rects)[i];
+    const int tc0 = rc & 0xFF, tc1 = (rc >> 8) & 0xFF, tr0 = (rc >> 16) & 0xFF, tr1 = rc >> 24;
+    if (tc0 > tc1) continue;
+    const int* cnts = reinterpret_cast<const int*>(st + a.ipp.L.count);
+    const int* lists = reinterpret_cast<const int*>(st + a.ipp.L.list);
+    const float2* yz = reinterpret_cast<const float2*>(st + a.ipp.L.yz);
+    const float* partial = a.partial + v * a.partial_vstride;
+    float A[7] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    float2 yzr = make_float2(0.f, 0.f);
+    bool hit = false;
+    for (int ty = tr0; ty <= tr1; ++ty)
+      for (int tx = tc0; tx <= tc1; ++tx) {
+        const int t = ty * tiles_x + tx;
+        const int p = list_find(lists + (size_t)t * kCap, cnts[t], (int)i);
+        if (p >= 0) {
+          hit = true;
+          const float* q = partial + ((size_t)t * kCap + p) * 8;
+#pragma unroll
+          for (int c = 0; c < 7; ++c) A[c] += q[c];
+          yzr = yz[(size_t)t * kCap + p];
+        }
+      }
+    if (!hit) continue;
+    g_sigma += A[0];
+#pragma unroll
+    for (int k = 0; k < kSh; ++k) g_sh[k] += A[1] * vc.h.sh_basis[k];
+    g_rr += A[2];
+    g_cc += A[3];
+    g_rc += A[4];
+
+    const float rho_r = vc.h.rho_r, rho_a = vc.h.rho_a;
+    const float yr = yzr.x, zr = yzr.y;
+    const float grad_ipp_r = A[5], grad_ipp_c = A[6];
+    const float Rmin = sqrtf(yr * yr + zr * zr + kEps);
+    const float d_r_d_yr = yr / (rho_r * Rmin);
+    const float d_r_d_zr = zr / (rho_r * Rmin);
+    const float grad_xr = grad_ipp_c / rho_a;
+    const float grad_yr = grad_ipp_r * d_r_d_yr / rho_r;
+    const float grad_zr = grad_ipp_r * d_r_d_zr / rho_r;
+    const float cos_a = vc.cos_a, sin_a = vc.sin_a, cos_b = vc.cos_b, sin_b = vc.sin_b;
+    const float d_xr_d_xw = cos_a, d_xr_d_yw = sin_a, d_xr_d_zw = 0.0f;
+    const float d_yr_d_xw = cos_b * sin_a, d_yr_d_yw = -cos_b * cos_a, d_yr_d_zw = -sin_b;
+    const float d_zr_d_xw = -sin_b * sin_a, d_zr_d_yw = sin_b * cos_a, d_zr_d_zw = -cos_b;
+    gx += grad_xr * d_xr_d_xw + grad_yr * d_yr_d_xw + grad_zr * d_zr_d_xw;
+    gy += grad_xr * d_xr_d_yw + grad_yr * d_yr_d_yw + grad_zr * d_zr_d_yw;
+    gz += grad_xr * d_xr_d_zw + grad_yr * d_yr_d_zw + grad_zr * d_zr_d_zw;
+  }
+
+  float* gm = a.grad_means + i * 3;
+  if (a.accumulate) {
+    gx += gm[0];
+    gy += gm[1];
+    gz += gm[2];
+  }
+  gm[0] = gx;
+  gm[1] = gy;
+  gm[2] = gz;
+  if (a.grad_norm) a.grad_norm[i] = sqrtf(gx * gx + gy * gy + gz * gz);
+
+  if (a.grad_cov_layout == 6) {
+    float* gc = a.grad_cov + i * 6;
+    float c6[6] = {g_rr, g_cc, 0.f, g_rc, 0.f, 0.f};
+#pragma unroll
+    for (int c = 0; c < 6; ++c) gc[c] = a.accumulate ? gc[c] + c6[c] : c6[c];
+  } else {
+    float* gc = a.grad_cov + i * 9;
+    float c9[9] = {g_rr, g_rc, 0.f, g_rc, g_cc, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int c = 0; c < 9; ++c) gc[c] = a.accumulate ? gc[c] + c9[c] : c9[c];
+  }
+  a.grad_sigma[i] = a.accumulate ? a.grad_sigma[i] + g_sigma : g_sigma;
+  float* gs = a.grad_sh + i * a.grad_sh_cols;
+  if (a.grad_sh_cols == kSh && !a.accumulate && ((uintptr_t)gs & 15) == 0) {
+    float4* gs4 = reinterpret_cast<float4*>(gs);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) gs4[q] = make_float4(g_sh[4 * q], g_sh[4 * q + 1], g_sh[4 * q + 2], g_sh[4 * q + 3]);
+  } else {
+#pragma unroll
+    for (int k = 0; k < kSh; ++k)
+      if (k < a.grad_sh_cols) gs[k] = a.accumulate ? gs[k] + g_sh[k] : g_sh[k];
+  }
+}
+
+// ---------------------------------------------------------------------------
+// test hooks
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) debug_preprocess_kernel(const DebugPreArgs a) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= a.n) return;
+  ViewConst vc;
+  vc.h = a.vh;
+  vc.cos_a = cosf(a.vh.alpha);
+  vc.sin_a = sinf(a.vh.alpha);
+  vc.cos_b = cosf(a.vh.beta);
+  vc.sin_b = sinf(a.vh.beta);
+  const int Nr = a.vh.Nr, Na = a.vh.Na;
+  float cw[6];
+  load_cov6(a.cov + (size_t)i * a.cov_layout, a.cov_layout, cw);
+  const float* m = a.means + (size_t)i * 3;
+  Proj o;
+  project_gaussian(vc, m[0], m[1], m[2], cw, o);
+  const float S = sh_scattering(vc, a.sh + (size_t)i * a.sh_stride, a.sh_k);
+  const float f[13] = {o.r, o.c, o.cov_rr, o.cov_cc, o.cov_rc, o.xr, o.yr, o.XX, o.YY, o.XY, o.yr, o.zr, S};
+#pragma unroll
+  for (int k = 0; k < 13; ++k) a.f32[(size_t)k * a.n + i] = f[k];
+  const bool valid = !(a.sigma[i] < 0.01f) && proj_valid(o, Nr, Na);
+  int r0 = 0, r1 = 0, c0 = 0, c1 = 0, s_ok = 0, sc0 = 0, sc1 = 0, sr0 = 0, sr1 = 0;
+  if (valid) {
+    ipp_ranges(o, Nr, Na, r0, r1, c0, c1);
+    s_ok = shadow_ranges(o, Nr, Na, sr0, sr1, sc0, sc1) ? 1 : 0;
+  }
+  const int32_t q[10] = {valid ? 1 : 0, r0, r1, c0, c1, s_ok, sc0, sc1, sr0, sr1};
+#pragma unroll
+  for (int k = 0; k < 10; ++k) a.i32[(size_t)k * a.n + i] = q[k];
+}
+
+__global__ void __launch_bounds__(kCap) debug_lists_kernel(const DebugListArgs a) {
+  const int t = blockIdx.x, s = threadIdx.x;
+  const unsigned char* st = a.st.base;
+  const int cnt = reinterpret_cast<const int*>(st + a.st.L.count)[t];
+  const int* list = reinterpret_cast<const int*>(st + a.st.L.list) + (size_t)t * kCap;
+  const Rec* recs = reinterpret_cast<const Rec*>(st + a.st.L.recs) + (size_t)t * kCap;
+  if (s == 0) a.counts[t] = cnt;
+  a.lists[(size_t)t * kCap + s] = s < cnt ? list[s] : -1;
+  a.sorted[(size_t)t * kCap + s] = s < cnt ? list[recs[s].pos] : -1;
+}
+
+__global__ void debug_view_kernel(const ViewHost vh, float* __restrict__ out) {
+  const float f[14] = {vh.radar_x, vh.radar_y, vh.radar_z, vh.alpha, vh.beta, vh.Rc, vh.rho_r,
+                       vh.rho_a, (float)vh.Nr, (float)vh.Na, cosf(vh.alpha), sinf(vh.alpha),
+                       cosf(vh.beta), sinf(vh.beta)};
+  for (int k = 0; k < 14; ++k) out[k] = f[k];
+  for (int k = 0; k < kSh; ++k) out[14 + k] = vh.sh_basis[k];
+}
+
+// ---------------------------------------------------------------------------
+// launch wrappers
+// ---------------------------------------------------------------------------
+static size_t bin_smem_bytes(const Dims& d, int cov_layout, bool shadow) {
+  const size_t stage = (size_t)(3 + cov_layout + 1) * kChunk * sizeof(float);
+  const size_t T1 = (size_t)(d.tiles_y + 1) * (d.tiles_x + 1);
+  return stage + T1 * sizeof(int) * (shadow ? 2 : 1);
+}
+
+cudaError_t launch_view_setup(const ViewHostPack& pack, ViewConst* out, cudaStream_t s) {
+  view_setup_kernel<<<1, kMaxViewsPerLaunch, 0, s>>>(pack, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_bin(const BinArgs& a, const Dims& d, int nviews, bool shadow, cudaStream_t s) {
+  const size_t smem = bin_smem_bytes(d, a.cov_layout, shadow);
+  const dim3 grid(d.C, nviews);
+  if (shadow) {
+    cudaFuncSetAttribute(bin_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    bin_kernel<true><<<grid, kBinThreads, smem, s>>>(a);
+  } else {
+    cudaFuncSetAttribute(bin_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    bin_kernel<false><<<grid, kBinThreads, smem, s>>>(a);
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_select(const SelectArgs& a, const Dims& d, int nviews, bool shadow_list,
+                          cudaStream_t s) {
+  const dim3 grid(d.T, nviews);
+  if (shadow_list)
+    select_kernel<true><<<grid, kSelectThreads, 0, s>>>(a);
+  else
+    select_kernel<false><<<grid, kSelectThreads, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_render(const TileArgs& a, const Dims& d, int nviews, cudaStream_t s) {
+  render_kernel<<<dim3(d.T * kWarpsPerTile, nviews), 32, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_omega_tile(const TileArgs& a, const Dims& d, int nviews, cudaStream_t s) {
+  omega_tile_kernel<<<dim3(d.T, nviews), kWarpsPerTile * 32, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_omega_scatter(const OmegaScatterArgs& a, const Dims& d, int nviews,
+                                 cudaStream_t s) {
+  const unsigned blocks = (unsigned)((d.n + 255) / 256);
+  omega_scatter_kernel<<<dim3(blocks, nviews), 256, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_bwd_tile(const TileArgs& a, const Dims& d, int nviews, cudaStream_t s) {
+  bwd_tile_kernel<<<dim3(d.T, nviews), kWarpsPerTile * 32, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_bwd_scatter(const BwdScatterArgs& a, const Dims& d, cudaStream_t s) {
+  const unsigned blocks = (unsigned)((d.n + 255) / 256);
+  bwd_scatter_kernel<<<blocks, 256, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_debug_preprocess(const DebugPreArgs& a, cudaStream_t s) {
+  const unsigned blocks = (unsigned)((a.n + 255) / 256);
+  debug_preprocess_kernel<<<blocks, 256, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_debug_view(const ViewHost& vh, float* out, cudaStream_t s) {
+  debug_view_kernel<<<1, 1, 0, s>>>(vh, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_debug_lists(const DebugListArgs& a, cudaStream_t s) {
+  debug_lists_kernel<<<a.T, kCap, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
+}  // namespace sarr
