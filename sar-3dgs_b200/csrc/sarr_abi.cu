@@ -117,13 +117,14 @@ int cuda_status(cudaError_t e) { return e == cudaSuccess ? SARR_OK : SARR_ERR_CU
 // ---------------------------------------------------------------------------
 enum KernelKind {
   kKindSetup = 0, kKindBin, kKindSelect, kKindSelectShadow, kKindRender, kKindOmegaTile,
-  kKindOmegaScatter, kKindBwdTile, kKindBwdScatter, kKindAux, kKindCount
+  kKindOmegaScatter, kKindBwdTile, kKindBwdScatter, kKindAux, kKindScan, kKindCount
 };
 static_assert(kKindCount == SARR_KERNEL_KINDS, "kernel kinds");
 
 const char* const kKindNames[kKindCount] = {
     "view_setup", "bin_kernel", "select_kernel", "select_kernel_shadow", "render_kernel",
-    "omega_tile_kernel", "omega_scatter_kernel", "bwd_tile_kernel", "bwd_scatter_kernel", "aux"};
+    "omega_tile_kernel", "omega_scatter_kernel", "bwd_tile_kernel", "bwd_scatter_kernel", "aux",
+    "scan_kernel"};
 
 struct ProfRecord {
   int kind, device;
@@ -248,7 +249,65 @@ cudaError_t run_selection(const Dims& d, const Ws& w, int gv, const float* means
   ba.counts_vstride = w.L.per_view;
   ba.use_tma = aligned(means, 16) && aligned(cov, 16) && aligned(sigma, 16);
   ba.err = w.err;
-  cudaError_t e = run_kernel(kKindBin, s, [&] { return launch_bin(ba, d, gv, shr != nullptr, s); });
+  ba.nviews = gv;
+  ba.sat_ipp = reinterpret_cast<const uint32_t*>(w.view_area() + w.L.sat_ipp);
+  ba.sat_sh = reinterpret_cast<const uint32_t*>(w.view_area() + w.L.sat_sh);
+  ba.sat_vstride = w.L.per_view / sizeof(uint32_t);
+  // Enough CTAs to fill the GPU (~8 per SM on 148 SMs): a large launch gets
+  // one CTA per chunk covering all views (the chunk is read once); a small
+  // one splits the views across CTAs.
+  auto views_per_cta = [gv](int chunks) {
+    const int target = 148 * 8;
+    int split = (target + chunks - 1) / chunks;
+    if (split > gv) split = gv;
+    if (split < 1) split = 1;
+    return (gv + split - 1) / split;
+  };
+  // The first kPrefixChunks chunks are binned exactly; tiles that they fill
+  // with 64 hits are marked saturated, and the remaining chunks skip the
+  // covariance projection of Gaussians that can only reach saturated tiles.
+  const int prefix = d.C > kPrefixChunks ? kPrefixChunks : d.C;
+  ba.chunk_offset = 0;
+  ba.views_per_cta = views_per_cta(prefix);
+  cudaError_t e = run_kernel(kKindBin, s, [&] {
+    return launch_bin(ba, d, prefix, shr != nullptr, false, s);
+  });
+  if (e != cudaSuccess) return e;
+  if (prefix < d.C) {
+    SatArgs sg;
+    sg.T = d.T;
+    sg.prefix_chunks = prefix;
+    sg.counts = ba.counts_ipp;
+    sg.counts_vstride = w.L.per_view;
+    sg.sat = const_cast<uint32_t*>(ba.sat_ipp);
+    sg.sat_vstride = ba.sat_vstride;
+    e = run_kernel(kKindAux, s, [&] { return launch_sat(sg, gv, s); });
+    if (e != cudaSuccess) return e;
+    if (shr) {
+      sg.counts = ba.counts_sh;
+      sg.sat = const_cast<uint32_t*>(ba.sat_sh);
+      e = run_kernel(kKindAux, s, [&] { return launch_sat(sg, gv, s); });
+      if (e != cudaSuccess) return e;
+    }
+    ba.chunk_offset = prefix;
+    ba.views_per_cta = views_per_cta(d.C - prefix);
+    e = run_kernel(kKindBin, s, [&] {
+      return launch_bin(ba, d, d.C - prefix, shr != nullptr, true, s);
+    });
+    if (e != cudaSuccess) return e;
+  }
+
+  ScanArgs sc;
+  sc.T = d.T;
+  sc.C = d.C;
+  sc.counts = ba.counts_ipp;
+  sc.counts_vstride = w.L.per_view;
+  sc.st = ipp;
+  sc.need = w.view_area() + w.L.need_ipp;
+  sc.need_vstride = w.L.per_view;
+  sc.need_n = reinterpret_cast<int*>(w.view_area() + w.L.need_n_ipp);
+  sc.need_n_vstride = w.L.per_view / sizeof(int);
+  e = run_kernel(kKindScan, s, [&] { return launch_scan(sc, gv, s); });
   if (e != cudaSuccess) return e;
 
   SelectArgs sa;
@@ -264,13 +323,23 @@ cudaError_t run_selection(const Dims& d, const Ws& w, int gv, const float* means
   sa.sh_stride = sh_stride;
   sa.sh_k = sh_k;
   sa.st = ipp;
-  sa.counts = ba.counts_ipp;
-  sa.counts_vstride = w.L.per_view;
+  sa.need = sc.need;
+  sa.need_vstride = sc.need_vstride;
+  sa.need_n = sc.need_n;
+  sa.need_n_vstride = sc.need_n_vstride;
   sa.err = w.err;
   e = run_kernel(kKindSelect, s, [&] { return launch_select(sa, d, gv, false, s); });
   if (e != cudaSuccess || !shr) return e;
+
+  sc.counts = ba.counts_sh;
+  sc.st = *shr;
+  sc.need = w.view_area() + w.L.need_sh;
+  sc.need_n = reinterpret_cast<int*>(w.view_area() + w.L.need_n_sh);
+  e = run_kernel(kKindScan, s, [&] { return launch_scan(sc, gv, s); });
+  if (e != cudaSuccess) return e;
   sa.st = *shr;
-  sa.counts = ba.counts_sh;
+  sa.need = sc.need;
+  sa.need_n = sc.need_n;
   e = run_kernel(kKindSelectShadow, s, [&] { return launch_select(sa, d, gv, true, s); });
   return e;
 }

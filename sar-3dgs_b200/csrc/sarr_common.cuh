@@ -24,9 +24,11 @@ constexpr int kSh = 16;                         // SH_COEFFS_SIZE
 
 // Design constants of this implementation.
 constexpr int kBinThreads = 256;                 // threads of a binning CTA
-constexpr int kBinPerThread = 2;                 // Gaussians per binning thread
+constexpr int kBinPerThread = 4;                 // Gaussians per binning thread
 constexpr int kChunk = kBinThreads * kBinPerThread;  // Gaussians per count row
 constexpr int kSelectThreads = 256;
+constexpr int kScanThreads = 512;
+constexpr int kPrefixChunks = 32;                // chunks binned exactly before saturation skipping
 constexpr int kWarpsPerTile = 8;                 // 8 warps x 32 pixels = one 16x16 tile
 constexpr int kMaxTilesAxis = 128;               // images up to 2048 x 2048
 constexpr int kMaxViewsPerLaunch = 32;
@@ -49,12 +51,21 @@ struct ViewHost {
 };
 
 // ViewHost plus the rotation trig, evaluated on the device with CUDA's
-// cosf/sinf like the reference kernels do (:103-106, :128-131).
+// cosf/sinf like the reference kernels do (:103-106, :128-131), and the
+// per-view products of the projection, computed once per view with the same
+// operations (and so the same bits) the per-Gaussian code would use.
 struct ViewConst {
   ViewHost h;
   float cos_a, sin_a, cos_b, sin_b;
   int tiles_x, tiles_y;
-  int pad0, pad1;
+  float cb_sa, cb_ca, sb_ca, sb_sa;      // world_to_radar products
+  float half_Nr, half_Na, Rc_rho;        // Nr/2, Na/2, R_c / rho_r
+  float J10;                             // 1 / rho_a
+  float kXX[6], kYY[6], kZZ[6], kXY[6], kXZ[6], kYZ[6];  // Sigma_r = R Sigma R^T coefficients
+  float kcc[6];                          // cov_cc = J10^2 XX (+ zero terms)
+  float krc0;                            // J00 * J10
+  float inv_rho_r, inv_rho_a;            // fast approximate centre (saturation skipping)
+  float center_margin;                   // its error bound [px], with room to spare
 };
 
 struct ViewHostPack {
@@ -118,34 +129,22 @@ __device__ __forceinline__ float chain6(const float k[6], const float x[6]) {
   return s;
 }
 
-// world_to_radar + project_to_ipp + transform_covariance_3x3 +
-// compute_jacobian_ipp + project_covariance_ipp + project_covariance_shadow
-// (rasterizer_impl_v2.cu:98-213), as evaluated by preprocess_kernel (:356-403).
-// Zero entries of R and J (R02, J00, J11, J12) are kept as terms: they leave
-// finite results unchanged and propagate non-finite inputs as the reference does.
-__device__ __forceinline__ void project_gaussian(const ViewConst& v, float px, float py, float pz,
-                                                 const float cw[6], Proj& o) {
+// Per-view products of the projection (:98-203): R = the world-to-radar
+// rotation rows, the coefficients of Sigma_r = R Sigma R^T per output entry,
+// and the view-only Jacobian terms. Same operations as the per-Gaussian code
+// would perform, so the same bits.
+__device__ __forceinline__ void view_derive(ViewConst& v) {
   const float ca = v.cos_a, sa = v.sin_a, cb = v.cos_b, sb = v.sin_b;
-  const float rho_r = v.h.rho_r, rho_a = v.h.rho_a;
-
-  const float dx = sub_(px, v.h.radar_x);
-  const float dy = sub_(py, v.h.radar_y);
-  const float dz = sub_(pz, v.h.radar_z);
-  const float xr = fma_(ca, dx, mul_(sa, dy));
-  const float yr = fma_(-sb, dz, fma_(mul_(cb, sa), dx, -mul_(mul_(cb, ca), dy)));
-  const float zr = fma_(-cb, dz, fma_(mul_(sb, ca), dy, -mul_(mul_(sb, sa), dx)));
-  o.xr = xr;
-  o.yr = yr;
-  o.zr = zr;
-
-  const float Rmin = sqrt_(add_(fma_(yr, yr, mul_(zr, zr)), kEps * kEps));
-  o.r = sub_(add_(div_(Rmin, rho_r), mul_((float)v.h.Nr, 0.5f)), div_(v.h.Rc, rho_r));
-  o.c = add_(div_(xr, rho_a), mul_((float)v.h.Na, 0.5f));
-
-  const float x6[6] = {cw[0], cw[1], cw[2], cw[3], cw[4], cw[5]};  // xx yy zz xy xz yz
+  v.cb_sa = mul_(cb, sa);
+  v.cb_ca = mul_(cb, ca);
+  v.sb_ca = mul_(sb, ca);
+  v.sb_sa = mul_(sb, sa);
+  v.half_Nr = mul_((float)v.h.Nr, 0.5f);
+  v.half_Na = mul_((float)v.h.Na, 0.5f);
+  v.Rc_rho = div_(v.h.Rc, v.h.rho_r);
   const float R00 = ca, R01 = sa, R02 = 0.0f;
-  const float R10 = mul_(cb, sa), R11 = -mul_(cb, ca), R12 = -sb;
-  const float R20 = -mul_(sb, sa), R21 = mul_(sb, ca), R22 = -cb;
+  const float R10 = v.cb_sa, R11 = -v.cb_ca, R12 = -sb;
+  const float R20 = -v.sb_sa, R21 = v.sb_ca, R22 = -cb;
   const float kXX[6] = {mul_(R00, R00), mul_(R01, R01), mul_(R02, R02), mul_(mul_(2.0f, R00), R01),
                         mul_(mul_(2.0f, R00), R02), mul_(mul_(2.0f, R01), R02)};
   const float kYY[6] = {mul_(R10, R10), mul_(R11, R11), mul_(R12, R12), mul_(mul_(2.0f, R10), R11),
@@ -158,27 +157,150 @@ __device__ __forceinline__ void project_gaussian(const ViewConst& v, float px, f
                         fma_(R00, R22, mul_(R02, R20)), fma_(R01, R22, mul_(R02, R21))};
   const float kYZ[6] = {mul_(R10, R20), mul_(R11, R21), mul_(R12, R22), fma_(R10, R21, mul_(R11, R20)),
                         fma_(R12, R20, mul_(R10, R22)), fma_(R12, R21, mul_(R11, R22))};
-  const float XX = chain6(kXX, x6), YY = chain6(kYY, x6), ZZ = chain6(kZZ, x6);
-  const float XY = chain6(kXY, x6), XZ = chain6(kXZ, x6), YZ = chain6(kYZ, x6);
-  const float X6[6] = {XX, YY, ZZ, XY, XZ, YZ};
-
   const float J00 = 0.0f, J11 = 0.0f, J12 = 0.0f;
-  const float J01 = div_(yr, mul_(rho_r, Rmin));
-  const float J02 = div_(zr, mul_(rho_r, Rmin));
-  const float J10 = div_(1.0f, rho_a);
-  const float krr[6] = {mul_(J00, J00), mul_(J01, J01), mul_(J02, J02), mul_(mul_(2.0f, J00), J01),
-                        mul_(mul_(2.0f, J00), J02), mul_(mul_(2.0f, J01), J02)};
+  const float J10 = div_(1.0f, v.h.rho_a);
   const float kcc[6] = {mul_(J10, J10), mul_(J11, J11), mul_(J12, J12), mul_(mul_(2.0f, J10), J11),
                         mul_(mul_(2.0f, J10), J12), mul_(mul_(2.0f, J11), J12)};
-  const float krc[6] = {mul_(J00, J10), mul_(J01, J11), mul_(J02, J12), fma_(J01, J10, mul_(J00, J11)),
+#pragma unroll
+  for (int i = 0; i < 6; ++i) {
+    v.kXX[i] = kXX[i];
+    v.kYY[i] = kYY[i];
+    v.kZZ[i] = kZZ[i];
+    v.kXY[i] = kXY[i];
+    v.kXZ[i] = kXZ[i];
+    v.kYZ[i] = kYZ[i];
+    v.kcc[i] = kcc[i];
+  }
+  v.J10 = J10;
+  v.krc0 = mul_(J00, J10);
+  v.inv_rho_r = 1.0f / v.h.rho_r;
+  v.inv_rho_a = 1.0f / v.h.rho_a;
+  // the approximate centre's error grows with the magnitude of the cancelling
+  // slant-range terms R_min / rho_r and R_c / rho_r (a few ulps of them)
+  v.center_margin = 0.25f + 4e-6f * fabsf(v.Rc_rho);
+}
+
+// world_to_radar + project_to_ipp (:98-113, :160-174): radar-frame centre and
+// image-plane position. Returns R_min.
+__device__ __forceinline__ float project_center(const ViewConst& v, float px, float py, float pz,
+                                                Proj& o) {
+  const float dx = sub_(px, v.h.radar_x);
+  const float dy = sub_(py, v.h.radar_y);
+  const float dz = sub_(pz, v.h.radar_z);
+  o.xr = fma_(v.cos_a, dx, mul_(v.sin_a, dy));
+  o.yr = fma_(-v.sin_b, dz, fma_(v.cb_sa, dx, -mul_(v.cb_ca, dy)));
+  o.zr = fma_(-v.cos_b, dz, fma_(v.sb_ca, dy, -mul_(v.sb_sa, dx)));
+  const float Rmin = sqrt_(add_(fma_(o.yr, o.yr, mul_(o.zr, o.zr)), kEps * kEps));
+  o.r = sub_(add_(div_(Rmin, v.h.rho_r), v.half_Nr), v.Rc_rho);
+  o.c = add_(div_(o.xr, v.h.rho_a), v.half_Na);
+  return Rmin;
+}
+
+// transform_covariance_3x3 (:115-158): the six entries of Sigma_r = R Sigma R^T
+// in the order XX, YY, ZZ, XY, XZ, YZ. Zero entries of R (R02) are kept as
+// terms: they leave finite results unchanged and propagate non-finite inputs
+// as the reference does.
+__device__ __forceinline__ void radar_cov(const ViewConst& v, const float cw[6], float X6[6]) {
+  const float x6[6] = {cw[0], cw[1], cw[2], cw[3], cw[4], cw[5]};  // xx yy zz xy xz yz
+  X6[0] = chain6(v.kXX, x6);
+  X6[1] = chain6(v.kYY, x6);
+  X6[2] = chain6(v.kZZ, x6);
+  X6[3] = chain6(v.kXY, x6);
+  X6[4] = chain6(v.kXZ, x6);
+  X6[5] = chain6(v.kYZ, x6);
+}
+
+// compute_jacobian_ipp + project_covariance_ipp + project_covariance_shadow
+// (:176-213) from Sigma_r. Zero entries of J (J00, J11, J12) are kept as terms.
+__device__ __forceinline__ void image_cov(const ViewConst& v, const float X6[6], float Rmin,
+                                          Proj& o) {
+  const float J00 = 0.0f, J11 = 0.0f, J12 = 0.0f;
+  const float rR = mul_(v.h.rho_r, Rmin);
+  const float J01 = div_(o.yr, rR);
+  const float J02 = div_(o.zr, rR);
+  const float J10 = v.J10;
+  const float krr[6] = {mul_(J00, J00), mul_(J01, J01), mul_(J02, J02), mul_(mul_(2.0f, J00), J01),
+                        mul_(mul_(2.0f, J00), J02), mul_(mul_(2.0f, J01), J02)};
+  const float krc[6] = {v.krc0, mul_(J01, J11), mul_(J02, J12), fma_(J01, J10, mul_(J00, J11)),
                         fma_(J02, J10, mul_(J00, J12)), fma_(J01, J12, mul_(J02, J11))};
   o.cov_rr = chain6(krr, X6);
-  o.cov_cc = chain6(kcc, X6);
+  o.cov_cc = chain6(v.kcc, X6);
   o.cov_rc = chain6(krc, X6);
+  o.XX = X6[0];
+  o.YY = X6[1];
+  o.XY = X6[3];
+}
 
-  o.XX = XX;
-  o.YY = YY;
-  o.XY = XY;
+__device__ __forceinline__ void project_cov(const ViewConst& v, const float cw[6], float Rmin,
+                                            Proj& o) {
+  float X6[6];
+  radar_cov(v, cw, X6);
+  image_cov(v, X6, Rmin, o);
+}
+
+// A bound valid for every view on the half-widths of the reference's 3-sigma
+// bboxes (pixels for the image plane, metres for the shadow footprint).
+// Both use std = sqrt(max(a*b / max(det, EPS), EPS)) <= 1/sqrt(1 - rho^2) for
+// the correlation rho of two projections of the Gaussian on orthogonal
+// directions (image plane: the radar X axis and a Y/Z combination; shadow: X
+// and Y). By Wielandt's inequality rho^2 <= ((kappa-1)/(kappa+1))^2 for the
+// covariance's condition number kappa, so std^2 <= (kappa+1)^2 / (4 kappa); a
+// 1% relative and 1.5 px absolute margin cover the float rounding of the
+// reference's own evaluation, which stays far below 1% for kappa <= 2.5e4.
+// The eigenvalues come from the
+// closed-form trigonometric solution of the symmetric 3x3 eigenproblem; a slack
+// closed-form trigonometric solution of the symmetric 3x3 eigenproblem; a slack
+// of 1e-5 * lambda_max on both extreme eigenvalues covers its float error.
+// +inf for covariances that are not clearly positive definite or have
+// kappa > 2.5e4.
+__device__ __forceinline__ float view_free_half_bound(const float cw[6]) {
+  const float xx = cw[0], yy = cw[1], zz = cw[2], xy = cw[3], xz = cw[4], yz = cw[5];
+  const float q = (xx + yy + zz) * (1.0f / 3.0f);
+  const float axx = xx - q, ayy = yy - q, azz = zz - q;
+  const float p2 = axx * axx + ayy * ayy + azz * azz + 2.0f * (xy * xy + xz * xz + yz * yz);
+  float lmax = q, lmin = q;
+  if (p2 > 0.0f) {
+    const float p = sqrtf(p2 * (1.0f / 6.0f));
+    const float inv = 1.0f / p;
+    const float bxx = axx * inv, byy = ayy * inv, bzz = azz * inv;
+    const float bxy = xy * inv, bxz = xz * inv, byz = yz * inv;
+    const float detB = bxx * (byy * bzz - byz * byz) - bxy * (bxy * bzz - byz * bxz) +
+                       bxz * (bxy * byz - byy * bxz);
+    const float hr = fminf(fmaxf(0.5f * detB, -1.0f), 1.0f);
+    const float phi = acosf(hr) * (1.0f / 3.0f);
+    lmax = q + 2.0f * p * cosf(phi);
+    lmin = q + 2.0f * p * cosf(phi + 2.0943951f);
+  }
+  const float slack = 1e-5f * fabsf(lmax);
+  const float hi = lmax + slack, lo = lmin - slack;
+  if (!(lo > 0.0f) || !(hi > 0.0f)) return INFINITY;
+  const float kappa = hi / lo;
+  if (!(kappa < 2.5e4f)) return INFINITY;
+  return 3.0f * ((kappa + 1.0f) / (2.0f * sqrtf(kappa))) * 1.01f + 1.5f;
+}
+
+// Centre of a Gaussian in the image plane (pixels) and the shadow plane
+// (metres) with fast arithmetic. Its error against project_center is a few
+// ulps of the cancelling slant-range terms R_min / rho_r and R_c / rho_r
+// (about 0.01 px for a 5 km altitude at 0.2 m), which ViewConst::center_margin
+// bounds with room to spare.
+__device__ __forceinline__ void approx_center(const ViewConst& v, float px, float py, float pz,
+                                              float& r, float& c, float& xr, float& yr) {
+  const float dx = px - v.h.radar_x, dy = py - v.h.radar_y, dz = pz - v.h.radar_z;
+  xr = v.cos_a * dx + v.sin_a * dy;
+  yr = -v.sin_b * dz + (v.cb_sa * dx - v.cb_ca * dy);
+  const float zr = -v.cos_b * dz + (v.sb_ca * dy - v.sb_sa * dx);
+  const float R2 = yr * yr + zr * zr + kEps * kEps;
+  const float Rmin = R2 * rsqrtf(R2);
+  r = (Rmin - v.h.Rc) * v.inv_rho_r + v.half_Nr;
+  c = xr * v.inv_rho_a + v.half_Na;
+}
+
+// The whole per-Gaussian projection of preprocess_kernel (:356-403).
+__device__ __forceinline__ void project_gaussian(const ViewConst& v, float px, float py, float pz,
+                                                 const float cw[6], Proj& o) {
+  const float Rmin = project_center(v, px, py, pz, o);
+  project_cov(v, cw, Rmin, o);
 }
 
 // preprocess_kernel's validity test (:405-406); the sigma < 0.01 test
@@ -194,8 +316,10 @@ __device__ __forceinline__ void ipp_ranges(const Proj& o, int Nr, int Na, int& r
   float det = fma_(cov_rr, cov_cc, -mul_(cov_rc, cov_rc));
   if (det < kEps) det = kEps;
   const float inv_det = div_(1.0f, det);
+  // std_r and std_c of the reference are the same value: cov_rr*cov_cc and
+  // cov_cc*cov_rr are equal in IEEE arithmetic.
   const float std_r = sqrt_(fmaxf(mul_(mul_(cov_rr, cov_cc), inv_det), kEps));
-  const float std_c = sqrt_(fmaxf(mul_(mul_(cov_cc, cov_rr), inv_det), kEps));
+  const float std_c = std_r;
   r_min = (int)floorf(fma_(-3.0f, std_r, o.r));
   r_max = (int)ceilf(fma_(3.0f, std_r, o.r));
   c_min = (int)floorf(fma_(-3.0f, std_c, o.c));

@@ -50,12 +50,14 @@ __host__ __device__ inline StateLayout state_layout(int64_t n, int T) {
 }
 
 // Workspace: [ViewConst x 32][error word][per-view areas x group]
-//   per view: counts_ipp [C][T] u8, counts_sh [C][T] u8, state_ipp (used when
-//   the caller gives no state), state_sh, partial_om [T][64] float2,
-//   partial_bwd [T][64][8] float.
+//   per view: counts_ipp [C][T] u8, counts_sh [C][T] u8, need_ipp / need_sh
+//   [T][64] int4 and need_n_ipp / need_n_sh [T] i32 (the chunks holding each
+//   tile's list, from scan_kernel), state_ipp (used when the caller gives no
+//   state), state_sh, partial_om [T][64] float2, partial_bwd [T][64][8] float.
 struct WsLayout {
   size_t viewconst, err, head;
-  size_t counts_ipp, counts_sh, state_ipp, state_sh, partial_om, partial_bwd, per_view;
+  size_t counts_ipp, counts_sh, need_ipp, need_sh, need_n_ipp, need_n_sh, sat_ipp, sat_sh;
+  size_t state_ipp, state_sh, partial_om, partial_bwd, per_view;
   StateLayout st;
 };
 
@@ -70,6 +72,18 @@ __host__ inline WsLayout ws_layout(const Dims& d) {
   o += align256((size_t)d.C * d.T);
   L.counts_sh = o;
   o += align256((size_t)d.C * d.T);
+  L.need_ipp = o;
+  o += align256((size_t)d.T * kCap * 16);
+  L.need_sh = o;
+  o += align256((size_t)d.T * kCap * 16);
+  L.need_n_ipp = o;
+  o += align256((size_t)d.T * 4);
+  L.need_n_sh = o;
+  o += align256((size_t)d.T * 4);
+  L.sat_ipp = o;
+  o += align256((size_t)(d.T + 31) / 32 * 4);
+  L.sat_sh = o;
+  o += align256((size_t)(d.T + 31) / 32 * 4);
   L.state_ipp = o;
   o += L.st.bytes;
   L.state_sh = o;
@@ -91,6 +105,12 @@ struct StateRef {
 
 struct BinArgs {
   const ViewConst* views;
+  int nviews;
+  int views_per_cta;  // views handled by one CTA (grid.y = ceil(nviews / views_per_cta))
+  int chunk_offset;   // first chunk of this launch
+  const uint32_t* sat_ipp;  // saturated-tile bitmaps (skip variant), sat_vstride words per view
+  const uint32_t* sat_sh;
+  size_t sat_vstride;
   int64_t n;
   int C;
   const float* means;
@@ -118,9 +138,30 @@ struct SelectArgs {
   int sh_stride;
   int sh_k;
   StateRef st;
+  const unsigned char* need;  // int4 [T][64] per view: chunk, hits before, hits in chunk
+  size_t need_vstride;        // bytes
+  const int* need_n;          // [T] per view
+  size_t need_n_vstride;      // ints
+  int* err;
+};
+
+struct SatArgs {
+  int T, prefix_chunks;
   const uint8_t* counts;
   size_t counts_vstride;
-  int* err;
+  uint32_t* sat;
+  size_t sat_vstride;  // words
+};
+
+struct ScanArgs {
+  int T, C;
+  const uint8_t* counts;
+  size_t counts_vstride;
+  StateRef st;  // receives the list lengths
+  unsigned char* need;
+  size_t need_vstride;
+  int* need_n;
+  size_t need_n_vstride;
 };
 
 struct TileArgs {
@@ -184,7 +225,11 @@ struct DebugListArgs {
 
 // Launch wrappers; each returns the cudaError_t of the launch.
 cudaError_t launch_view_setup(const ViewHostPack& pack, ViewConst* out, cudaStream_t s);
-cudaError_t launch_bin(const BinArgs& a, const Dims& d, int nviews, bool shadow, cudaStream_t s);
+// bin_kernel over chunks [a.chunk_offset, a.chunk_offset + chunks)
+cudaError_t launch_bin(const BinArgs& a, const Dims& d, int chunks, bool shadow, bool skip,
+                       cudaStream_t s);
+cudaError_t launch_sat(const SatArgs& a, int nviews, cudaStream_t s);
+cudaError_t launch_scan(const ScanArgs& a, int nviews, cudaStream_t s);
 cudaError_t launch_select(const SelectArgs& a, const Dims& d, int nviews, bool shadow_list,
                           cudaStream_t s);
 cudaError_t launch_render(const TileArgs& a, const Dims& d, int nviews, cudaStream_t s);

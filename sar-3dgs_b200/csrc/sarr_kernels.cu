@@ -45,8 +45,7 @@ __global__ void view_setup_kernel(const ViewHostPack pack, ViewConst* __restrict
   c.sin_b = sinf(c.h.beta);
   c.tiles_x = (c.h.Na + kTile - 1) / kTile;
   c.tiles_y = (c.h.Nr + kTile - 1) / kTile;
-  c.pad0 = 0;
-  c.pad1 = 0;
+  view_derive(c);
   out[v] = c;
 }
 
@@ -62,17 +61,67 @@ __device__ __forceinline__ void diff_add(int* d, int pitch, uint32_t rc) {
   atomicAdd(&d[(tr1 + 1) * pitch + tc1 + 1], 1);
 }
 
+// True when every tile of the rectangle is marked in the bitmap (or the
+// rectangle is empty).
+__device__ __forceinline__ bool rect_all_set(uint32_t rc, const uint32_t* __restrict__ bits,
+                                             int tiles_x) {
+  const int tc0 = rc & 0xFF, tc1 = (rc >> 8) & 0xFF, tr0 = (rc >> 16) & 0xFF, tr1 = rc >> 24;
+  for (int ty = tr0; ty <= tr1; ++ty)
+    for (int tx = tc0; tx <= tc1; ++tx) {
+      const int t = ty * tiles_x + tx;
+      if (!((bits[t >> 5] >> (t & 31)) & 1u)) return false;
+    }
+  return true;
+}
+
+// Tile rectangle of the pixel box centred on (cr, cc) with half-width h,
+// clamped like the reference's bboxes.
+__device__ __forceinline__ uint32_t bound_rect(float cr, float cc, float h, int Nr, int Na) {
+  const int r0 = max(0, (int)floorf(cr - h)), r1 = min(Nr - 1, (int)ceilf(cr + h));
+  const int c0 = max(0, (int)floorf(cc - h)), c1 = min(Na - 1, (int)ceilf(cc + h));
+  return make_rect(r0, r1, c0, c1, Nr, Na);
+}
+
+// Exact per-Gaussian binning of one Gaussian for one view (preprocess_kernel
+// + compute_ranges_kernel + the shadow footprint, :322-470, :572-597).
 template <bool kShadow>
+__device__ __forceinline__ void bin_exact(const ViewConst& vc, const float* s_means, const float* s_cov,
+                                          int cs, int j, uint32_t& rc_ipp, uint32_t& rc_sh) {
+  const int Nr = vc.h.Nr, Na = vc.h.Na;
+  Proj o;
+  const float Rmin = project_center(vc, s_means[3 * j], s_means[3 * j + 1], s_means[3 * j + 2], o);
+  if (!proj_valid(o, Nr, Na)) return;
+  float cw[6], X6[6];
+  load_cov6(s_cov + j * cs, cs, cw);
+  radar_cov(vc, cw, X6);
+  image_cov(vc, X6, Rmin, o);
+  int r0, r1, c0, c1;
+  ipp_ranges(o, Nr, Na, r0, r1, c0, c1);
+  rc_ipp = make_rect(r0, r1, c0, c1, Nr, Na);
+  if (kShadow) {
+    if (shadow_ranges(o, Nr, Na, r0, r1, c0, c1)) rc_sh = make_rect(r0, r1, c0, c1, Nr, Na);
+  }
+}
+
+// One CTA per chunk of kChunk Gaussians, all views of the launch: the chunk is
+// staged in shared memory once and projected for every view in turn.
+//
+// kSkip (chunks after the saturation prefix): a tile's list is complete once
+// the prefix holds 64 of its hits, so a later Gaussian whose bbox can only
+// reach such tiles enters no list and gets an empty rectangle. Stage 1 decides
+// that for every Gaussian from a fast approximate centre and a view-independent
+// bbox bound (both with margins); only the rest are queued, compacted, and
+// binned exactly in stage 2, which keeps the warps of both stages coherent.
+template <bool kShadow, bool kSkip>
 __global__ void __launch_bounds__(kBinThreads) bin_kernel(const BinArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   __shared__ uint64_t bar;
+  __shared__ int s_qn;
+  __shared__ short s_queue[kChunk];
 
-  const int tid = threadIdx.x;
-  const int v = blockIdx.y;
-  const int chunk = blockIdx.x;
-  const ViewConst vc = a.views[v];
-  const int Nr = vc.h.Nr, Na = vc.h.Na;
-  const int tiles_x = vc.tiles_x, tiles_y = vc.tiles_y, T = tiles_x * tiles_y;
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int chunk = blockIdx.x + a.chunk_offset;
+  const int tiles_x = a.views[0].tiles_x, tiles_y = a.views[0].tiles_y, T = tiles_x * tiles_y;
   const int cs = a.cov_layout;
 
   float* s_means = reinterpret_cast<float*>(smem_raw);
@@ -88,7 +137,6 @@ __global__ void __launch_bounds__(kBinThreads) bin_kernel(const BinArgs a) {
   const bool tma = a.use_tma && gcount == kChunk;
 
   if (tid == 0 && tma) mbar_init(&bar, 1);
-  for (int i = tid; i < T1 * (kShadow ? 2 : 1); i += kBinThreads) s_diff_ipp[i] = 0;
   __syncthreads();
 
   bool ok = true;
@@ -108,77 +156,200 @@ __global__ void __launch_bounds__(kBinThreads) bin_kernel(const BinArgs a) {
   }
   if (!__syncthreads_and(ok)) return;
 
-  uint32_t* rects_ipp = reinterpret_cast<uint32_t*>(a.ipp.base + v * a.ipp.vstride + a.ipp.L.rects);
-  uint32_t* rects_sh =
-      kShadow ? reinterpret_cast<uint32_t*>(a.sh.base + v * a.sh.vstride + a.sh.L.rects) : nullptr;
-
+  float hb[kBinPerThread];  // view-independent bbox half-width bounds (kSkip)
 #pragma unroll
   for (int k = 0; k < kBinPerThread; ++k) {
     const int j = tid + k * kBinThreads;
-    if (j < gcount) {
-      uint32_t rc_ipp = kEmptyRect, rc_sh = kEmptyRect;
-      const float sigma = s_sigma[j];
-      if (!(sigma < 0.01f)) {  // preprocess_kernel: transmittance < 0.01 -> invalid (:351)
-        float cw[6];
-        load_cov6(s_cov + j * cs, cs, cw);
-        Proj o;
-        project_gaussian(vc, s_means[3 * j], s_means[3 * j + 1], s_means[3 * j + 2], cw, o);
-        if (proj_valid(o, Nr, Na)) {
-          int r0, r1, c0, c1;
-          ipp_ranges(o, Nr, Na, r0, r1, c0, c1);
-          rc_ipp = make_rect(r0, r1, c0, c1, Nr, Na);
+    hb[k] = INFINITY;
+    if (kSkip && j < gcount) {
+      float cw[6];
+      load_cov6(s_cov + j * cs, cs, cw);
+      hb[k] = view_free_half_bound(cw);
+    }
+  }
+
+  const int v_begin = blockIdx.y * a.views_per_cta;
+  const int v_end = min(a.nviews, v_begin + a.views_per_cta);
+  for (int v = v_begin; v < v_end; ++v) {
+    const ViewConst& vc = a.views[v];
+    const int Nr = vc.h.Nr, Na = vc.h.Na;
+    for (int i = tid; i < T1 * (kShadow ? 2 : 1); i += kBinThreads) s_diff_ipp[i] = 0;
+    if (kSkip && tid == 0) s_qn = 0;
+    __syncthreads();
+
+    uint32_t* rects_ipp = reinterpret_cast<uint32_t*>(a.ipp.base + v * a.ipp.vstride + a.ipp.L.rects);
+    uint32_t* rects_sh =
+        kShadow ? reinterpret_cast<uint32_t*>(a.sh.base + v * a.sh.vstride + a.sh.L.rects) : nullptr;
+
+    if (kSkip) {
+      // stage 1: cheap conservative test for every Gaussian
+      const uint32_t* sat_ipp = a.sat_ipp + v * a.sat_vstride;
+      const uint32_t* sat_sh = a.sat_sh + v * a.sat_vstride;
+      const float r_m = vc.center_margin;
+      const float Rc = vc.h.Rc;
+      (void)Rc;
+#pragma unroll
+      for (int k = 0; k < kBinPerThread; ++k) {
+        const int j = tid + k * kBinThreads;
+        bool exact = false;
+        if (j < gcount) {
+          bool skip = s_sigma[j] < 0.01f;  // invalid: empty rectangles either way
+          if (!skip && hb[k] <= 64.0f) {
+            float r, c, xr, yr;
+            approx_center(vc, s_means[3 * j], s_means[3 * j + 1], s_means[3 * j + 2], r, c, xr, yr);
+            const float h = hb[k] + r_m;
+            skip = rect_all_set(bound_rect(r, c, h, Nr, Na), sat_ipp, tiles_x);
+            if (kShadow && skip) skip = rect_all_set(bound_rect(yr, xr, h, Nr, Na), sat_sh, tiles_x);
+          }
+          if (skip) {
+            rects_ipp[base + j] = kEmptyRect;
+            if (kShadow) rects_sh[base + j] = kEmptyRect;
+          }
+          exact = !skip;
+        }
+        const unsigned m = __ballot_sync(0xffffffffu, exact);
+        if (m) {
+          int slot0 = 0;
+          if (lane == 0) slot0 = atomicAdd(&s_qn, __popc(m));
+          slot0 = __shfl_sync(0xffffffffu, slot0, 0);
+          if (exact) s_queue[slot0 + __popc(m & ((1u << lane) - 1u))] = (short)j;
+        }
+      }
+      __syncthreads();
+      // stage 2: the queued Gaussians, exactly
+      const int qn = s_qn;
+      for (int q = tid; q < qn; q += kBinThreads) {
+        const int j = s_queue[q];
+        uint32_t rc_ipp = kEmptyRect, rc_sh = kEmptyRect;
+        bin_exact<kShadow>(vc, s_means, s_cov, cs, j, rc_ipp, rc_sh);
+        rects_ipp[base + j] = rc_ipp;
+        diff_add(s_diff_ipp, pitch, rc_ipp);
+        if (kShadow) {
+          rects_sh[base + j] = rc_sh;
+          diff_add(s_diff_sh, pitch, rc_sh);
+        }
+      }
+    } else {
+      const ViewConst vcl = vc;  // local copy: loaded once for all of this thread's Gaussians
+#pragma unroll
+      for (int k = 0; k < kBinPerThread; ++k) {
+        const int j = tid + k * kBinThreads;
+        if (j < gcount) {
+          uint32_t rc_ipp = kEmptyRect, rc_sh = kEmptyRect;
+          if (!(s_sigma[j] < 0.01f))  // preprocess_kernel: transmittance < 0.01 -> invalid (:351)
+            bin_exact<kShadow>(vcl, s_means, s_cov, cs, j, rc_ipp, rc_sh);
+          rects_ipp[base + j] = rc_ipp;
+          diff_add(s_diff_ipp, pitch, rc_ipp);
           if (kShadow) {
-            if (shadow_ranges(o, Nr, Na, r0, r1, c0, c1)) rc_sh = make_rect(r0, r1, c0, c1, Nr, Na);
+            rects_sh[base + j] = rc_sh;
+            diff_add(s_diff_sh, pitch, rc_sh);
           }
         }
       }
-      rects_ipp[base + j] = rc_ipp;
-      diff_add(s_diff_ipp, pitch, rc_ipp);
-      if (kShadow) {
-        rects_sh[base + j] = rc_sh;
-        diff_add(s_diff_sh, pitch, rc_sh);
-      }
     }
-  }
-  __syncthreads();
+    __syncthreads();
 
-  // 2-D inclusive prefix of the difference arrays: rows, then columns.
-  // Threads [0,128) handle the image-plane list, [128,256) the shadow list.
-  {
-    const int half = tid >> 7, i = tid & 127;
-    if (half == 0 || kShadow) {
-      int* d = half ? s_diff_sh : s_diff_ipp;
-      if (i < tiles_y) {
-        int run = 0;
-        for (int x = 0; x < tiles_x; ++x) {
-          run += d[i * pitch + x];
-          d[i * pitch + x] = run;
+    // 2-D inclusive prefix of the difference arrays: rows, then columns.
+    // Threads [0,128) handle the image-plane list, [128,256) the shadow list.
+    {
+      const int half = tid >> 7, i = tid & 127;
+      if (half == 0 || kShadow) {
+        int* d = half ? s_diff_sh : s_diff_ipp;
+        if (i < tiles_y) {
+          int run = 0;
+          for (int x = 0; x < tiles_x; ++x) {
+            run += d[i * pitch + x];
+            d[i * pitch + x] = run;
+          }
         }
       }
     }
-  }
-  __syncthreads();
-  {
-    const int half = tid >> 7, i = tid & 127;
-    if (half == 0 || kShadow) {
-      int* d = half ? s_diff_sh : s_diff_ipp;
-      if (i < tiles_x) {
-        int run = 0;
-        for (int y = 0; y < tiles_y; ++y) {
-          run += d[y * pitch + i];
-          d[y * pitch + i] = run;
+    __syncthreads();
+    {
+      const int half = tid >> 7, i = tid & 127;
+      if (half == 0 || kShadow) {
+        int* d = half ? s_diff_sh : s_diff_ipp;
+        if (i < tiles_x) {
+          int run = 0;
+          for (int y = 0; y < tiles_y; ++y) {
+            run += d[y * pitch + i];
+            d[y * pitch + i] = run;
+          }
         }
       }
     }
+    __syncthreads();
+
+    uint8_t* cnt_ipp = a.counts_ipp + v * a.counts_vstride + (size_t)chunk * T;
+    uint8_t* cnt_sh = kShadow ? a.counts_sh + v * a.counts_vstride + (size_t)chunk * T : nullptr;
+    for (int t = tid; t < T; t += kBinThreads) {
+      const int y = t / tiles_x, x = t - y * tiles_x;
+      cnt_ipp[t] = (uint8_t)min(s_diff_ipp[y * pitch + x], 255);
+      if (kShadow) cnt_sh[t] = (uint8_t)min(s_diff_sh[y * pitch + x], 255);
+    }
+    __syncthreads();  // the difference arrays and the queue are reused by the next view
+  }
+}
+
+// Saturation bitmap of one list: bit t of view v is set when the first
+// `prefix_chunks` chunk rows already hold >= 64 hits of tile t.
+__global__ void __launch_bounds__(256) sat_kernel(const SatArgs a) {
+  const int t = blockIdx.x * 256 + threadIdx.x;
+  const int v = blockIdx.y;
+  const uint8_t* counts = a.counts + v * a.counts_vstride;
+  int sum = 0;
+  if (t < a.T)
+    for (int c = 0; c < a.prefix_chunks && sum < kCap; ++c) sum += counts[(size_t)c * a.T + t];
+  const unsigned m = __ballot_sync(0xffffffffu, t < a.T && sum >= kCap);
+  const int word = t >> 5;
+  if ((threadIdx.x & 31) == 0 && word < (a.T + 31) / 32) a.sat[v * a.sat_vstride + word] = m;
+}
+
+// Per-tile prefix of the chunk counts, coalesced: one CTA per 32 adjacent
+// tiles (lane = tile), each warp summing a contiguous range of chunk rows.
+// Emits, per tile, the chunks that hold its first 64 hits in index order as
+// (chunk, hits before the chunk, hits in the chunk) and the list length.
+__global__ void __launch_bounds__(kScanThreads) scan_kernel(const ScanArgs a) {
+  __shared__ int s_part[kScanThreads / 32][32];
+  __shared__ int s_nneed[32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int v = blockIdx.y;
+  const int T = a.T;
+  const int t = blockIdx.x * 32 + lane;
+  const bool live = t < T;
+  const uint8_t* counts = a.counts + v * a.counts_vstride;
+  const int C = a.C;
+  const int per = (C + kScanThreads / 32 - 1) / (kScanThreads / 32);
+  const int c0 = min(warp * per, C), c1 = min(c0 + per, C);
+  int sum = 0;
+  if (live)
+    for (int c = c0; c < c1; ++c) sum += counts[(size_t)c * T + t];
+  s_part[warp][lane] = sum;
+  if (warp == 0) s_nneed[lane] = 0;
+  __syncthreads();
+  int pre = 0, total = 0;
+#pragma unroll
+  for (int w = 0; w < kScanThreads / 32; ++w) {
+    const int x = s_part[w][lane];
+    pre += (w < warp) ? x : 0;
+    total += x;
+  }
+  unsigned char* st = a.st.base + v * a.st.vstride;
+  int4* need = reinterpret_cast<int4*>(a.need + v * a.need_vstride);
+  if (live && pre < kCap) {
+    for (int c = c0; c < c1 && pre < kCap; ++c) {
+      const int cnt = counts[(size_t)c * T + t];
+      if (cnt > 0) {
+        const int q = atomicAdd(&s_nneed[lane], 1);
+        need[(size_t)t * kCap + q] = make_int4(c, pre, cnt, 0);
+      }
+      pre += cnt;
+    }
   }
   __syncthreads();
-
-  uint8_t* cnt_ipp = a.counts_ipp + v * a.counts_vstride + (size_t)chunk * T;
-  uint8_t* cnt_sh = kShadow ? a.counts_sh + v * a.counts_vstride + (size_t)chunk * T : nullptr;
-  for (int t = tid; t < T; t += kBinThreads) {
-    const int y = t / tiles_x, x = t - y * tiles_x;
-    cnt_ipp[t] = (uint8_t)min(s_diff_ipp[y * pitch + x], 255);
-    if (kShadow) cnt_sh[t] = (uint8_t)min(s_diff_sh[y * pitch + x], 255);
+  if (warp == 0 && live) {
+    reinterpret_cast<int*>(st + a.st.L.count)[t] = min(total, kCap);
+    a.need_n[v * a.need_n_vstride + t] = s_nneed[lane];
   }
 }
 
@@ -187,9 +358,6 @@ __global__ void __launch_bounds__(kBinThreads) bin_kernel(const BinArgs a) {
 // ---------------------------------------------------------------------------
 template <bool kShadowList>
 __global__ void __launch_bounds__(kSelectThreads) select_kernel(const SelectArgs a) {
-  __shared__ int s_warp[kSelectThreads / 32];
-  __shared__ int s_nneed;
-  __shared__ int4 s_need[kCap];
   __shared__ int s_list[kCap];
   __shared__ __align__(16) Rec s_rec[kCap];
   __shared__ float s_z[kCap];
@@ -198,57 +366,21 @@ __global__ void __launch_bounds__(kSelectThreads) select_kernel(const SelectArgs
   const int t = blockIdx.x, v = blockIdx.y;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const ViewConst& vc = a.views[v];
-  const int tiles_x = vc.tiles_x, T = tiles_x * vc.tiles_y;
+  const int tiles_x = vc.tiles_x;
   const int tx = t % tiles_x, ty = t / tiles_x;
-  const uint8_t* counts = a.counts + v * a.counts_vstride;
   unsigned char* st = a.st.base + v * a.st.vstride;
-  int* st_count = reinterpret_cast<int*>(st + a.st.L.count);
-
-  // 1. per-tile totals over the chunk rows, block exclusive scan.
-  const int C = a.C;
-  const int cpt = (C + kSelectThreads - 1) / kSelectThreads;
-  const int c0 = min(tid * cpt, C), c1 = min(c0 + cpt, C);
-  int local = 0;
-  for (int c = c0; c < c1; ++c) local += counts[(size_t)c * T + t];
-  int incl = local;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const int y = __shfl_up_sync(0xffffffffu, incl, o);
-    if (lane >= o) incl += y;
-  }
-  if (lane == 31) s_warp[warp] = incl;
-  if (tid == 0) s_nneed = 0;
+  // 1. list length and the chunks holding its slots (scan_kernel)
+  const int count = reinterpret_cast<const int*>(st + a.st.L.count)[t];
+  if (count == 0) return;
+  const int nneed = a.need_n[v * a.need_n_vstride + t];
+  const int4* need = reinterpret_cast<const int4*>(a.need + v * a.need_vstride) + (size_t)t * kCap;
   if (tid < kCap) s_list[tid] = -1;
-  __syncthreads();
-  int wpre = 0, total = 0;
-#pragma unroll
-  for (int w = 0; w < kSelectThreads / 32; ++w) {
-    const int x = s_warp[w];
-    wpre += (w < warp) ? x : 0;
-    total += x;
-  }
-  const int count = min(total, kCap);
-  if (count == 0) {
-    if (tid == 0) st_count[t] = 0;
-    return;
-  }
-  // chunks holding slots < 64
-  int pre = wpre + incl - local;
-  for (int c = c0; c < c1 && pre < kCap; ++c) {
-    const int cnt = counts[(size_t)c * T + t];
-    if (cnt > 0) {
-      const int q = atomicAdd(&s_nneed, 1);
-      s_need[q] = make_int4(c, pre, cnt, 0);
-    }
-    pre += cnt;
-  }
   __syncthreads();
 
   // 2. emit: the hits of each needed chunk in index order.
   const uint32_t* rects = reinterpret_cast<const uint32_t*>(st + a.st.L.rects);
-  const int nneed = s_nneed;
   for (int q = warp; q < nneed; q += kSelectThreads / 32) {
-    const int4 nd = s_need[q];
+    const int4 nd = need[q];
     const int need = min(nd.z, kCap - nd.y);
     const int64_t b0 = (int64_t)nd.x * kChunk;
     const int64_t b1 = min(b0 + kChunk, a.n);
@@ -349,8 +481,7 @@ __global__ void __launch_bounds__(kSelectThreads) select_kernel(const SelectArgs
   }
   __syncthreads();
 
-  // 5. state
-  if (tid == 0) st_count[t] = count;
+  // 5. state (the list length was written by scan_kernel)
   if (tid < count) {
     int* st_list = reinterpret_cast<int*>(st + a.st.L.list);
     Rec* st_recs = reinterpret_cast<Rec*>(st + a.st.L.recs);
@@ -720,6 +851,7 @@ __global__ void __launch_bounds__(256) debug_preprocess_kernel(const DebugPreArg
   vc.sin_a = sinf(a.vh.alpha);
   vc.cos_b = cosf(a.vh.beta);
   vc.sin_b = sinf(a.vh.beta);
+  view_derive(vc);
   const int Nr = a.vh.Nr, Na = a.vh.Na;
   float cw[6];
   load_cov6(a.cov + (size_t)i * a.cov_layout, a.cov_layout, cw);
@@ -774,16 +906,35 @@ cudaError_t launch_view_setup(const ViewHostPack& pack, ViewConst* out, cudaStre
   return cudaGetLastError();
 }
 
-cudaError_t launch_bin(const BinArgs& a, const Dims& d, int nviews, bool shadow, cudaStream_t s) {
+template <bool kShadow, bool kSkip>
+static void launch_bin_t(const BinArgs& a, dim3 grid, size_t smem, cudaStream_t s) {
+  if (smem > 48 * 1024)
+    cudaFuncSetAttribute(bin_kernel<kShadow, kSkip>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)smem);
+  bin_kernel<kShadow, kSkip><<<grid, kBinThreads, smem, s>>>(a);
+}
+
+cudaError_t launch_bin(const BinArgs& a, const Dims& d, int chunks, bool shadow, bool skip,
+                       cudaStream_t s) {
   const size_t smem = bin_smem_bytes(d, a.cov_layout, shadow);
-  const dim3 grid(d.C, nviews);
+  const dim3 grid(chunks, (a.nviews + a.views_per_cta - 1) / a.views_per_cta);
   if (shadow) {
-    cudaFuncSetAttribute(bin_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    bin_kernel<true><<<grid, kBinThreads, smem, s>>>(a);
+    if (skip) launch_bin_t<true, true>(a, grid, smem, s);
+    else launch_bin_t<true, false>(a, grid, smem, s);
   } else {
-    cudaFuncSetAttribute(bin_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    bin_kernel<false><<<grid, kBinThreads, smem, s>>>(a);
+    if (skip) launch_bin_t<false, true>(a, grid, smem, s);
+    else launch_bin_t<false, false>(a, grid, smem, s);
   }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_sat(const SatArgs& a, int nviews, cudaStream_t s) {
+  sat_kernel<<<dim3((a.T + 255) / 256, nviews), 256, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_scan(const ScanArgs& a, int nviews, cudaStream_t s) {
+  scan_kernel<<<dim3((a.T + 31) / 32, nviews), kScanThreads, 0, s>>>(a);
   return cudaGetLastError();
 }
 

@@ -201,6 +201,37 @@ def test_edge_cases():
     assert rel_linf(image_flat(img), ref["image"]) <= IMAGE_RTOL
 
 
+def test_saturation_skip_is_exact():
+    """After the exactly binned prefix, Gaussians whose conservative bbox only
+    reaches tiles already holding 64 hits skip the covariance projection. A
+    dense central cluster (saturating its tiles inside the prefix) followed by
+    spread-out, strongly anisotropic and near-singular Gaussians around the
+    saturation boundary must still give the oracle's lists bit for bit."""
+    g = torch.Generator().manual_seed(21)
+    n1, n2 = 20000, 30000
+    core = S.make_scene(n1, (6.0, 6.0, 2.0), (0.05, 0.3), seed=22)
+    rest = S.make_scene(n2, (30.0, 30.0, 8.0), (0.05, 0.5), seed=23)
+    # anisotropic tail: per-axis scales from 1e-3 to 2 m (condition numbers up to 4e6)
+    k = n2 // 3
+    s = torch.exp(torch.empty(k, 3).uniform_(-6.9, 0.7, generator=g))
+    q = torch.randn(k, 4, generator=g)
+    q = q / q.norm(dim=1, keepdim=True)
+    R = S.quat_to_rot(q.double())
+    cov = (R @ torch.diag_embed((s * s).double()) @ R.transpose(1, 2)).float()
+    rest["cov33"][:k] = cov
+    rest["cov6"][:k] = S.cov33_to_cov6(cov)
+    sc = {key: torch.cat([core[key], rest[key]]).cuda() for key in core}
+    for view in (S.sweep_views(8, samples=128)[2], S.training_views(3)[1]):
+        f, q_, (cnt, lst, srt) = _check_lists(sc, view)
+        fw = oracle_forward(sc, view)
+        np.testing.assert_array_equal(cnt, fw["counts"])
+        np.testing.assert_array_equal(lst, fw["lists"])
+        np.testing.assert_array_equal(srt, fw["sorted"])
+        img, om = gpu_forward(sc, view)
+        assert rel_linf(image_flat(img), fw["image"]) <= IMAGE_RTOL
+        assert rel_linf(om.cpu().numpy(), fw["omega"]) <= IMAGE_RTOL
+
+
 @pytest.mark.parametrize("view_idx", [3, 700])
 def test_full_size_sweep_view(view_idx):
     """N = 1M Gaussians, 256 x 256 at 0.2 m (the sweep workload): lists
