@@ -180,11 +180,37 @@ def rank_views(args, d):
     return S.sweep_views(args.views, samples=args.samples, offset_deg=0.35 * d.rank / max(d.world, 1))
 
 
-def bin_bytes_per_launch(n, nviews, T, C):
-    """Algorithmic bytes of one bin_kernel launch over `nviews` views: every
-    view reads the 40 B of means/cov6/transmittance per Gaussian, writes its
-    4 B tile rectangle per Gaussian and the C x T chunk counts."""
-    return nviews * (40 * n + 4 * n + C * T)
+CHUNK = 1024          # Gaussians per count row of the binning kernels
+PREFIX_CHUNKS = 32    # chunks binned exactly before saturation skipping
+CAP = 64              # tile list capacity
+
+
+def kernel_bytes_per_launch(kind, n, views, T, cov_floats, sh_floats, npix):
+    """Algorithmic bytes of one launch of a forward kernel over `views` views:
+    its compulsory reads and writes, each once.
+      bin_kernel       the prefix chunks: means/cov/transmittance of their
+                       Gaussians once; per view a 4 B tile rectangle per
+                       Gaussian and the u8 per-chunk tile counts.
+      bin_skip_kernel  the same over the remaining chunks.
+      select_kernel    per view and tile, the 64 selected Gaussians'
+                       parameters (means, cov, transmittance, SH) gathered and
+                       their 48 B records, list ids and (Y_r, Z_r) written.
+      render_kernel    per view the 64 records of every tile read and the
+                       image written."""
+    g_bytes = 4 * (3 + cov_floats + 1)
+    C = -(-n // CHUNK)
+    P = min(C, PREFIX_CHUNKS)
+    n_p = min(n, P * CHUNK)
+    if kind == "bin_kernel":
+        return g_bytes * n_p + views * (4 * n_p + P * T)
+    if kind == "bin_skip_kernel":
+        n_s = n - n_p
+        return g_bytes * n_s + views * (4 * n_s + (C - P) * T)
+    if kind == "select_kernel":
+        return views * T * CAP * (g_bytes + 4 * sh_floats + 48 + 4 + 8)
+    if kind == "render_kernel":
+        return views * (T * CAP * 48 + 4 * npix)
+    return None
 
 
 def bench_ours(args, d):
@@ -207,6 +233,7 @@ def bench_ours(args, d):
         flush_l2(flush, k)
         step()
     torch.cuda.synchronize()
+    checksum0 = float(images.double().sum().item())
     d.barrier()
 
     clocks = Clocks(dev)
@@ -243,23 +270,29 @@ def bench_ours(args, d):
     prof = _native.profile_read()
     _native.profile_enable(False)
     T = ((s + 15) // 16) ** 2
-    C = (n + 511) // 512
-    kname, (kms, klaunch) = max(prof.items(), key=lambda kv: kv[1][0])
     peak, peak_kind = peaks()
-    roof = None
-    if kname == "bin_kernel" and klaunch:
+    cov_floats = 9 if layout == 9 else 6
+    rooflines = {}
+    for kname, (kms, klaunch) in prof.items():
+        if not klaunch:
+            continue
         per_launch_views = V / (klaunch / rsteps)
-        bytes_per_launch = bin_bytes_per_launch(n, per_launch_views, T, C)
-        achieved = bytes_per_launch / (kms / klaunch / 1e3) / 1e9
-        roof = {"kernel": kname, "bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
-                "peak_source": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
-                "traffic": None, "bytes_per_launch": int(bytes_per_launch),
-                "avg_launch_us": round(kms / klaunch * 1e3, 2)}
+        b = kernel_bytes_per_launch(kname, n, per_launch_views, T, cov_floats, sh_k, s * s)
+        if b is None:
+            continue
+        achieved = b / (kms / klaunch / 1e3) / 1e9
+        rooflines[kname] = {"kernel": kname, "bound": "hbm", "achieved": round(achieved, 1),
+                            "peak": peak, "peak_source": peak_kind, "unit": "GB/s",
+                            "frac": round(achieved / peak, 4), "traffic": None,
+                            "bytes_per_launch": int(b), "avg_launch_us": round(kms / klaunch * 1e3, 2)}
+    dominant = max(prof.items(), key=lambda kv: kv[1][0])[0]
+    roof = rooflines.get(dominant)
     kernels = {k: {"ms_per_step": round(v[0] / rsteps, 4), "launches_per_step": v[1] / rsteps}
                for k, v in prof.items() if v[1]}
 
     out = {"value": value, "ms_per_step": t_ms_max / args.steps, "launches": launches,
-           "clocks": clk, "roofline": roof, "kernels": kernels, "checksum": checksum,
+           "clocks": clk, "roofline": roof, "kernel_rooflines": rooflines, "kernels": kernels,
+           "checksum": checksum, "checksum_stable": checksum == checksum0,
            "views_per_rank": V}
     if not args.no_e2e:
         out["e2e"] = bench_e2e(args, d, sc, views)
@@ -456,6 +489,26 @@ def config(args):
             "outputs": "images only (the SARRasterizer forward contract)"}
 
 
+GROUP_VIEWS = 32  # views per internal launch group of sarr_forward
+
+
+def path_roofline(args, r, world):
+    """Whole-forward HBM rooflines per GPU. Per view: the 104 B of fp32
+    parameters per Gaussian (means 12, cov6 24, transmittance 4, SH 64) read
+    and the image written once per view. Batched: the parameters read once
+    per launch group of 32 views, the image once per view."""
+    peak, peak_kind = peaks()
+    n, npix = args.n, args.samples * args.samples
+    vps = r["value"] / world
+    per_view = 104 * n + 4 * npix
+    batched = 104 * n / GROUP_VIEWS + 4 * npix
+    return {"peak": peak, "peak_source": peak_kind, "unit": "GB/s",
+            "per_view": {"bytes_per_view": per_view, "achieved": round(per_view * vps / 1e9, 1),
+                         "frac": round(per_view * vps / 1e9 / peak, 4)},
+            "batched": {"bytes_per_view": round(batched), "achieved": round(batched * vps / 1e9, 1),
+                        "frac": round(batched * vps / 1e9 / peak, 4)}}
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -474,7 +527,9 @@ def main():
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded; BASELINE sweep distributions)", "config": config(args),
             "roofline": r["roofline"], "gpu_launches": r["launches"], "clocks": r["clocks"],
-            "kernels": r["kernels"], "image_checksum": r["checksum"]}
+            "kernel_rooflines": r["kernel_rooflines"], "path_roofline": path_roofline(args, r, d.world),
+            "kernels": r["kernels"], "image_checksum": r["checksum"],
+            "image_checksum_stable": r["checksum_stable"]}
     if "e2e" in r:
         line["e2e"] = r["e2e"]
     if "fwd_bwd" in r:

@@ -117,14 +117,14 @@ int cuda_status(cudaError_t e) { return e == cudaSuccess ? SARR_OK : SARR_ERR_CU
 // ---------------------------------------------------------------------------
 enum KernelKind {
   kKindSetup = 0, kKindBin, kKindSelect, kKindSelectShadow, kKindRender, kKindOmegaTile,
-  kKindOmegaScatter, kKindBwdTile, kKindBwdScatter, kKindAux, kKindScan, kKindCount
+  kKindOmegaScatter, kKindBwdTile, kKindBwdScatter, kKindAux, kKindScan, kKindBinSkip, kKindCount
 };
 static_assert(kKindCount == SARR_KERNEL_KINDS, "kernel kinds");
 
 const char* const kKindNames[kKindCount] = {
     "view_setup", "bin_kernel", "select_kernel", "select_kernel_shadow", "render_kernel",
     "omega_tile_kernel", "omega_scatter_kernel", "bwd_tile_kernel", "bwd_scatter_kernel", "aux",
-    "scan_kernel"};
+    "scan_kernel", "bin_skip_kernel"};
 
 struct ProfRecord {
   int kind, device;
@@ -250,9 +250,9 @@ cudaError_t run_selection(const Dims& d, const Ws& w, int gv, const float* means
   ba.use_tma = aligned(means, 16) && aligned(cov, 16) && aligned(sigma, 16);
   ba.err = w.err;
   ba.nviews = gv;
-  ba.sat_ipp = reinterpret_cast<const uint32_t*>(w.view_area() + w.L.sat_ipp);
-  ba.sat_sh = reinterpret_cast<const uint32_t*>(w.view_area() + w.L.sat_sh);
-  ba.sat_vstride = w.L.per_view / sizeof(uint32_t);
+  ba.open_ipp = reinterpret_cast<const int*>(w.view_area() + w.L.open_ipp);
+  ba.open_sh = reinterpret_cast<const int*>(w.view_area() + w.L.open_sh);
+  ba.open_vstride = w.L.per_view / sizeof(int);
   // Enough CTAs to fill the GPU (~8 per SM on 148 SMs): a large launch gets
   // one CTA per chunk covering all views (the chunk is read once); a small
   // one splits the views across CTAs.
@@ -274,24 +274,21 @@ cudaError_t run_selection(const Dims& d, const Ws& w, int gv, const float* means
   });
   if (e != cudaSuccess) return e;
   if (prefix < d.C) {
-    SatArgs sg;
-    sg.T = d.T;
-    sg.prefix_chunks = prefix;
-    sg.counts = ba.counts_ipp;
-    sg.counts_vstride = w.L.per_view;
-    sg.sat = const_cast<uint32_t*>(ba.sat_ipp);
-    sg.sat_vstride = ba.sat_vstride;
-    e = run_kernel(kKindAux, s, [&] { return launch_sat(sg, gv, s); });
+    OpenArgs og;
+    og.tiles_x = d.tiles_x;
+    og.tiles_y = d.tiles_y;
+    og.prefix_chunks = prefix;
+    og.counts[0] = ba.counts_ipp;
+    og.counts[1] = ba.counts_sh;
+    og.counts_vstride = w.L.per_view;
+    og.table[0] = const_cast<int*>(ba.open_ipp);
+    og.table[1] = const_cast<int*>(ba.open_sh);
+    og.table_vstride = ba.open_vstride;
+    e = run_kernel(kKindAux, s, [&] { return launch_open_table(og, gv, shr ? 2 : 1, s); });
     if (e != cudaSuccess) return e;
-    if (shr) {
-      sg.counts = ba.counts_sh;
-      sg.sat = const_cast<uint32_t*>(ba.sat_sh);
-      e = run_kernel(kKindAux, s, [&] { return launch_sat(sg, gv, s); });
-      if (e != cudaSuccess) return e;
-    }
     ba.chunk_offset = prefix;
     ba.views_per_cta = views_per_cta(d.C - prefix);
-    e = run_kernel(kKindBin, s, [&] {
+    e = run_kernel(kKindBinSkip, s, [&] {
       return launch_bin(ba, d, d.C - prefix, shr != nullptr, true, s);
     });
     if (e != cudaSuccess) return e;

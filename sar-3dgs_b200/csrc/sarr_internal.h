@@ -52,11 +52,13 @@ __host__ __device__ inline StateLayout state_layout(int64_t n, int T) {
 // Workspace: [ViewConst x 32][error word][per-view areas x group]
 //   per view: counts_ipp [C][T] u8, counts_sh [C][T] u8, need_ipp / need_sh
 //   [T][64] int4 and need_n_ipp / need_n_sh [T] i32 (the chunks holding each
-//   tile's list, from scan_kernel), state_ipp (used when the caller gives no
+//   tile's list, from scan_kernel), open_ipp / open_sh [tiles_y+1][tiles_x+1]
+//   i32 (summed-area tables of the tiles still open after the saturation
+//   prefix, from open_table_kernel), state_ipp (used when the caller gives no
 //   state), state_sh, partial_om [T][64] float2, partial_bwd [T][64][8] float.
 struct WsLayout {
   size_t viewconst, err, head;
-  size_t counts_ipp, counts_sh, need_ipp, need_sh, need_n_ipp, need_n_sh, sat_ipp, sat_sh;
+  size_t counts_ipp, counts_sh, need_ipp, need_sh, need_n_ipp, need_n_sh, open_ipp, open_sh;
   size_t state_ipp, state_sh, partial_om, partial_bwd, per_view;
   StateLayout st;
 };
@@ -80,10 +82,10 @@ __host__ inline WsLayout ws_layout(const Dims& d) {
   o += align256((size_t)d.T * 4);
   L.need_n_sh = o;
   o += align256((size_t)d.T * 4);
-  L.sat_ipp = o;
-  o += align256((size_t)(d.T + 31) / 32 * 4);
-  L.sat_sh = o;
-  o += align256((size_t)(d.T + 31) / 32 * 4);
+  L.open_ipp = o;
+  o += align256((size_t)(d.tiles_y + 1) * (d.tiles_x + 1) * 4);
+  L.open_sh = o;
+  o += align256((size_t)(d.tiles_y + 1) * (d.tiles_x + 1) * 4);
   L.state_ipp = o;
   o += L.st.bytes;
   L.state_sh = o;
@@ -108,9 +110,9 @@ struct BinArgs {
   int nviews;
   int views_per_cta;  // views handled by one CTA (grid.y = ceil(nviews / views_per_cta))
   int chunk_offset;   // first chunk of this launch
-  const uint32_t* sat_ipp;  // saturated-tile bitmaps (skip variant), sat_vstride words per view
-  const uint32_t* sat_sh;
-  size_t sat_vstride;
+  const int* open_ipp;  // open-tile summed-area tables (skip variant), open_vstride ints per view
+  const int* open_sh;
+  size_t open_vstride;
   int64_t n;
   int C;
   const float* means;
@@ -145,12 +147,13 @@ struct SelectArgs {
   int* err;
 };
 
-struct SatArgs {
-  int T, prefix_chunks;
-  const uint8_t* counts;
+// Open-tile tables of up to two lists (blockIdx.y selects the list).
+struct OpenArgs {
+  int tiles_x, tiles_y, prefix_chunks;
+  const uint8_t* counts[2];
   size_t counts_vstride;
-  uint32_t* sat;
-  size_t sat_vstride;  // words
+  int* table[2];
+  size_t table_vstride;  // ints
 };
 
 struct ScanArgs {
@@ -228,7 +231,7 @@ cudaError_t launch_view_setup(const ViewHostPack& pack, ViewConst* out, cudaStre
 // bin_kernel over chunks [a.chunk_offset, a.chunk_offset + chunks)
 cudaError_t launch_bin(const BinArgs& a, const Dims& d, int chunks, bool shadow, bool skip,
                        cudaStream_t s);
-cudaError_t launch_sat(const SatArgs& a, int nviews, cudaStream_t s);
+cudaError_t launch_open_table(const OpenArgs& a, int nviews, int nlists, cudaStream_t s);
 cudaError_t launch_scan(const ScanArgs& a, int nviews, cudaStream_t s);
 cudaError_t launch_select(const SelectArgs& a, const Dims& d, int nviews, bool shadow_list,
                           cudaStream_t s);

@@ -61,17 +61,14 @@ __device__ __forceinline__ void diff_add(int* d, int pitch, uint32_t rc) {
   atomicAdd(&d[(tr1 + 1) * pitch + tc1 + 1], 1);
 }
 
-// True when every tile of the rectangle is marked in the bitmap (or the
-// rectangle is empty).
-__device__ __forceinline__ bool rect_all_set(uint32_t rc, const uint32_t* __restrict__ bits,
-                                             int tiles_x) {
-  const int tc0 = rc & 0xFF, tc1 = (rc >> 8) & 0xFF, tr0 = (rc >> 16) & 0xFF, tr1 = rc >> 24;
-  for (int ty = tr0; ty <= tr1; ++ty)
-    for (int tx = tc0; tx <= tc1; ++tx) {
-      const int t = ty * tiles_x + tx;
-      if (!((bits[t >> 5] >> (t & 31)) & 1u)) return false;
-    }
-  return true;
+// Number of open tiles inside a tile rectangle, from the summed-area table
+// tab[(tiles_y+1)][pitch] (entry [y][x] counts the open tiles above and left
+// of (y, x)). An empty rectangle holds none.
+__device__ __forceinline__ int open_in_rect(uint32_t rc, const int* __restrict__ tab, int pitch) {
+  if (rc == kEmptyRect) return 0;
+  const int tc0 = rc & 0xFF, tc1 = ((rc >> 8) & 0xFF) + 1, tr0 = (rc >> 16) & 0xFF, tr1 = (rc >> 24) + 1;
+  return __ldg(tab + tr1 * pitch + tc1) - __ldg(tab + tr0 * pitch + tc1) -
+         __ldg(tab + tr1 * pitch + tc0) + __ldg(tab + tr0 * pitch + tc0);
 }
 
 // Tile rectangle of the pixel box centred on (cr, cc) with half-width h,
@@ -101,6 +98,34 @@ __device__ __forceinline__ void bin_exact(const ViewConst& vc, const float* s_me
   if (kShadow) {
     if (shadow_ranges(o, Nr, Na, r0, r1, c0, c1)) rc_sh = make_rect(r0, r1, c0, c1, Nr, Na);
   }
+}
+
+// Stages chunk `base` (gcount Gaussians) of means, covariances and
+// transmittances in shared memory: one TMA bulk copy per array when the chunk
+// is full and the arrays are 16-byte aligned, plain loads otherwise. Every
+// thread of the CTA calls it; false when the copy timed out (error recorded).
+__device__ __forceinline__ bool stage_chunk(const BinArgs& a, int64_t base, int gcount, float* s_means,
+                                            float* s_cov, float* s_sigma, uint64_t* bar) {
+  const int tid = threadIdx.x, cs = a.cov_layout;
+  const bool tma = a.use_tma && gcount == kChunk;
+  if (tid == 0 && tma) mbar_init(bar, 1);
+  __syncthreads();
+  bool ok = true;
+  if (tma) {
+    if (tid == 0) {
+      const uint32_t bm = 3u * kChunk * 4u, bc = (uint32_t)cs * kChunk * 4u, bs = kChunk * 4u;
+      mbar_arrive_expect_tx(bar, bm + bc + bs);
+      tma_load_1d(s_means, a.means + base * 3, bm, bar);
+      tma_load_1d(s_cov, a.cov + base * cs, bc, bar);
+      tma_load_1d(s_sigma, a.sigma + base, bs, bar);
+    }
+    ok = mbar_wait_bounded(bar, 0, a.err);  // every reader observes the barrier phase
+  } else {
+    for (int i = tid; i < 3 * gcount; i += blockDim.x) s_means[i] = a.means[base * 3 + i];
+    for (int i = tid; i < cs * gcount; i += blockDim.x) s_cov[i] = a.cov[base * cs + i];
+    for (int i = tid; i < gcount; i += blockDim.x) s_sigma[i] = a.sigma[base + i];
+  }
+  return __syncthreads_and(ok);
 }
 
 // One CTA per chunk of kChunk Gaussians, all views of the launch: the chunk is
@@ -134,27 +159,7 @@ __global__ void __launch_bounds__(kBinThreads) bin_kernel(const BinArgs a) {
 
   const int64_t base = (int64_t)chunk * kChunk;
   const int gcount = (int)min((int64_t)kChunk, a.n - base);
-  const bool tma = a.use_tma && gcount == kChunk;
-
-  if (tid == 0 && tma) mbar_init(&bar, 1);
-  __syncthreads();
-
-  bool ok = true;
-  if (tma) {
-    if (tid == 0) {
-      const uint32_t bm = 3u * kChunk * 4u, bc = (uint32_t)cs * kChunk * 4u, bs = kChunk * 4u;
-      mbar_arrive_expect_tx(&bar, bm + bc + bs);
-      tma_load_1d(s_means, a.means + base * 3, bm, &bar);
-      tma_load_1d(s_cov, a.cov + base * cs, bc, &bar);
-      tma_load_1d(s_sigma, a.sigma + base, bs, &bar);
-    }
-    ok = mbar_wait_bounded(&bar, 0, a.err);
-  } else {
-    for (int i = tid; i < 3 * gcount; i += kBinThreads) s_means[i] = a.means[base * 3 + i];
-    for (int i = tid; i < cs * gcount; i += kBinThreads) s_cov[i] = a.cov[base * cs + i];
-    for (int i = tid; i < gcount; i += kBinThreads) s_sigma[i] = a.sigma[base + i];
-  }
-  if (!__syncthreads_and(ok)) return;
+  if (!stage_chunk(a, base, gcount, s_means, s_cov, s_sigma, &bar)) return;
 
   float hb[kBinPerThread];  // view-independent bbox half-width bounds (kSkip)
 #pragma unroll
@@ -183,11 +188,9 @@ __global__ void __launch_bounds__(kBinThreads) bin_kernel(const BinArgs a) {
 
     if (kSkip) {
       // stage 1: cheap conservative test for every Gaussian
-      const uint32_t* sat_ipp = a.sat_ipp + v * a.sat_vstride;
-      const uint32_t* sat_sh = a.sat_sh + v * a.sat_vstride;
-      const float r_m = vc.center_margin;
-      const float Rc = vc.h.Rc;
-      (void)Rc;
+      const ViewConst vcl = vc;  // local copy: the rect stores below cannot alias it
+      const int* open_ipp = a.open_ipp + v * a.open_vstride;
+      const int* open_sh = a.open_sh + v * a.open_vstride;
 #pragma unroll
       for (int k = 0; k < kBinPerThread; ++k) {
         const int j = tid + k * kBinThreads;
@@ -196,10 +199,10 @@ __global__ void __launch_bounds__(kBinThreads) bin_kernel(const BinArgs a) {
           bool skip = s_sigma[j] < 0.01f;  // invalid: empty rectangles either way
           if (!skip && hb[k] <= 64.0f) {
             float r, c, xr, yr;
-            approx_center(vc, s_means[3 * j], s_means[3 * j + 1], s_means[3 * j + 2], r, c, xr, yr);
-            const float h = hb[k] + r_m;
-            skip = rect_all_set(bound_rect(r, c, h, Nr, Na), sat_ipp, tiles_x);
-            if (kShadow && skip) skip = rect_all_set(bound_rect(yr, xr, h, Nr, Na), sat_sh, tiles_x);
+            approx_center(vcl, s_means[3 * j], s_means[3 * j + 1], s_means[3 * j + 2], r, c, xr, yr);
+            const float h = hb[k] + vcl.center_margin;
+            skip = open_in_rect(bound_rect(r, c, h, Nr, Na), open_ipp, pitch) == 0;
+            if (kShadow && skip) skip = open_in_rect(bound_rect(yr, xr, h, Nr, Na), open_sh, pitch) == 0;
           }
           if (skip) {
             rects_ipp[base + j] = kEmptyRect;
@@ -221,7 +224,7 @@ __global__ void __launch_bounds__(kBinThreads) bin_kernel(const BinArgs a) {
       for (int q = tid; q < qn; q += kBinThreads) {
         const int j = s_queue[q];
         uint32_t rc_ipp = kEmptyRect, rc_sh = kEmptyRect;
-        bin_exact<kShadow>(vc, s_means, s_cov, cs, j, rc_ipp, rc_sh);
+        bin_exact<kShadow>(vcl, s_means, s_cov, cs, j, rc_ipp, rc_sh);
         rects_ipp[base + j] = rc_ipp;
         diff_add(s_diff_ipp, pitch, rc_ipp);
         if (kShadow) {
@@ -291,18 +294,173 @@ __global__ void __launch_bounds__(kBinThreads) bin_kernel(const BinArgs a) {
   }
 }
 
-// Saturation bitmap of one list: bit t of view v is set when the first
-// `prefix_chunks` chunk rows already hold >= 64 hits of tile t.
-__global__ void __launch_bounds__(256) sat_kernel(const SatArgs a) {
-  const int t = blockIdx.x * 256 + threadIdx.x;
-  const int v = blockIdx.y;
-  const uint8_t* counts = a.counts + v * a.counts_vstride;
-  int sum = 0;
-  if (t < a.T)
-    for (int c = 0; c < a.prefix_chunks && sum < kCap; ++c) sum += counts[(size_t)c * a.T + t];
-  const unsigned m = __ballot_sync(0xffffffffu, t < a.T && sum >= kCap);
-  const int word = t >> 5;
-  if ((threadIdx.x & 31) == 0 && word < (a.T + 31) / 32) a.sat[v * a.sat_vstride + word] = m;
+// Adds one hit to every tile of a rectangle in a warp's tile counters (two
+// 16-bit counters per word; a chunk holds at most kChunk hits per tile).
+__device__ __forceinline__ void count_rect(uint32_t* cnt, uint32_t rc, int tiles_x) {
+  if (rc == kEmptyRect) return;
+  const int tc0 = rc & 0xFF, tc1 = (rc >> 8) & 0xFF, tr0 = (rc >> 16) & 0xFF, tr1 = rc >> 24;
+  for (int ty = tr0; ty <= tr1; ++ty)
+    for (int tx = tc0; tx <= tc1; ++tx) {
+      const int t = ty * tiles_x + tx;
+      atomicAdd(cnt + (t >> 1), 1u << ((t & 1) << 4));
+    }
+}
+
+// Writes a warp's tile counters of one view and chunk as saturating u8 counts
+// and clears them for the next view.
+__device__ __forceinline__ void flush_counts(uint32_t* cnt, uint8_t* out, int T, int lane) {
+  if ((T & 3) == 0) {
+    for (int t4 = lane; t4 < (T >> 2); t4 += 32) {
+      const uint32_t w0 = cnt[2 * t4], w1 = cnt[2 * t4 + 1];
+      const uint32_t c0 = min(w0 & 0xFFFFu, 255u), c1 = min(w0 >> 16, 255u);
+      const uint32_t c2 = min(w1 & 0xFFFFu, 255u), c3 = min(w1 >> 16, 255u);
+      reinterpret_cast<uint32_t*>(out)[t4] = c0 | (c1 << 8) | (c2 << 16) | (c3 << 24);
+    }
+  } else {
+    for (int t = lane; t < T; t += 32)
+      out[t] = (uint8_t)min((cnt[t >> 1] >> ((t & 1) << 4)) & 0xFFFFu, 255u);
+  }
+  __syncwarp();
+  for (int i = lane; i < ((T + 1) >> 1); i += 32) cnt[i] = 0;
+  __syncwarp();
+}
+
+// Saturation-skipping binning of the chunks after the prefix, one view per
+// warp at a time. The chunk is staged once per CTA (with the view-independent
+// bbox bounds); each warp then bins its views alone, with no CTA barrier:
+// a conservative test of every Gaussian (approximate centre, bbox bound,
+// open-tile table) writes empty rectangles for those that can only reach
+// saturated tiles, the others go to a warp queue that is drained 32 at a time
+// by exact binning, and the hits land in per-warp tile counters.
+template <bool kShadow>
+__global__ void __launch_bounds__(kBinThreads, 3) bin_skip_kernel(const BinArgs a) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  __shared__ uint64_t bar;
+  __shared__ short s_queue[kBinThreads / 32][64];
+  constexpr int kWarps = kBinThreads / 32;
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int chunk = blockIdx.x + a.chunk_offset;
+  const int tiles_x = a.views[0].tiles_x, tiles_y = a.views[0].tiles_y, T = tiles_x * tiles_y;
+  const int cs = a.cov_layout;
+  const int TW = (T + 1) >> 1;
+
+  float* s_means = reinterpret_cast<float*>(smem_raw);
+  float* s_cov = s_means + 3 * kChunk;
+  float* s_sigma = s_cov + cs * kChunk;
+  float* s_hb = s_sigma + kChunk;
+  uint32_t* s_cnt = reinterpret_cast<uint32_t*>(s_hb + kChunk) + warp * TW * (kShadow ? 2 : 1);
+  uint32_t* s_cnt_sh = s_cnt + TW;
+
+  const int64_t base = (int64_t)chunk * kChunk;
+  const int gcount = (int)min((int64_t)kChunk, a.n - base);
+  if (!stage_chunk(a, base, gcount, s_means, s_cov, s_sigma, &bar)) return;
+
+  for (int i = lane; i < TW * (kShadow ? 2 : 1); i += 32) s_cnt[i] = 0;
+  for (int j = tid; j < gcount; j += kBinThreads) {
+    float cw[6];
+    load_cov6(s_cov + j * cs, cs, cw);
+    s_hb[j] = view_free_half_bound(cw);
+  }
+  __syncthreads();
+
+  const int pitch = tiles_x + 1;
+  const unsigned lt_mask = (1u << lane) - 1u;
+  short* queue = s_queue[warp];
+  const int v_end = min(a.nviews, (int)(blockIdx.y + 1) * a.views_per_cta);
+  for (int v = blockIdx.y * a.views_per_cta + warp; v < v_end; v += kWarps) {
+    const ViewConst& vg = a.views[v];  // exact binning reads its constants from here (L1)
+    const ViewConst vc = vg;            // the stage-1 constants, held in registers
+    const int Nr = vc.h.Nr, Na = vc.h.Na;
+    uint32_t* rects_ipp = reinterpret_cast<uint32_t*>(a.ipp.base + v * a.ipp.vstride + a.ipp.L.rects) + base;
+    uint32_t* rects_sh =
+        kShadow ? reinterpret_cast<uint32_t*>(a.sh.base + v * a.sh.vstride + a.sh.L.rects) + base : nullptr;
+    const int* open_ipp = a.open_ipp + v * a.open_vstride;
+    const int* open_sh = a.open_sh + v * a.open_vstride;
+
+    // exact binning of queue[lane] (every lane with a queued Gaussian)
+    auto bin_queued = [&](int j) {
+      uint32_t rc_ipp = kEmptyRect, rc_sh = kEmptyRect;
+      bin_exact<kShadow>(vg, s_means, s_cov, cs, j, rc_ipp, rc_sh);
+      rects_ipp[j] = rc_ipp;
+      count_rect(s_cnt, rc_ipp, tiles_x);
+      if (kShadow) {
+        rects_sh[j] = rc_sh;
+        count_rect(s_cnt_sh, rc_sh, tiles_x);
+      }
+    };
+
+    int qn = 0;
+    for (int j0 = 0; j0 < gcount; j0 += 32) {
+      const int j = j0 + lane;
+      bool exact = false;
+      if (j < gcount) {
+        bool skip = s_sigma[j] < 0.01f;  // invalid: empty rectangles either way
+        const float hb = s_hb[j];
+        if (!skip && hb <= 64.0f) {
+          float r, c, xr, yr;
+          approx_center(vc, s_means[3 * j], s_means[3 * j + 1], s_means[3 * j + 2], r, c, xr, yr);
+          const float h = hb + vc.center_margin;
+          skip = open_in_rect(bound_rect(r, c, h, Nr, Na), open_ipp, pitch) == 0;
+          if (kShadow && skip) skip = open_in_rect(bound_rect(yr, xr, h, Nr, Na), open_sh, pitch) == 0;
+        }
+        if (skip) {
+          rects_ipp[j] = kEmptyRect;
+          if (kShadow) rects_sh[j] = kEmptyRect;
+        }
+        exact = !skip;
+      }
+      const unsigned m = __ballot_sync(0xffffffffu, exact);
+      if (exact) queue[qn + __popc(m & lt_mask)] = (short)j;
+      qn += __popc(m);
+      __syncwarp();
+      if (qn >= 32) {
+        bin_queued(queue[lane]);
+        __syncwarp();
+        if (lane < qn - 32) queue[lane] = queue[lane + 32];
+        qn -= 32;
+        __syncwarp();
+      }
+    }
+    if (lane < qn) bin_queued(queue[lane]);
+    __syncwarp();
+
+    flush_counts(s_cnt, a.counts_ipp + v * a.counts_vstride + (size_t)chunk * T, T, lane);
+    if (kShadow) flush_counts(s_cnt_sh, a.counts_sh + v * a.counts_vstride + (size_t)chunk * T, T, lane);
+  }
+}
+
+// Open-tile summed-area table of one list of one view (grid: views x lists).
+// A tile is open while the first `prefix_chunks` chunk rows hold fewer than 64
+// of its hits; entry [y][x] of the table counts the open tiles (ty, tx) with
+// ty < y and tx < x.
+__global__ void __launch_bounds__(256) open_table_kernel(const OpenArgs a) {
+  const int v = blockIdx.x, list = blockIdx.y;
+  const int tiles_x = a.tiles_x, tiles_y = a.tiles_y, T = tiles_x * tiles_y, pitch = tiles_x + 1;
+  const uint8_t* counts = (list ? a.counts[1] : a.counts[0]) + v * a.counts_vstride;
+  int* tab = (list ? a.table[1] : a.table[0]) + v * a.table_vstride;
+  for (int x = threadIdx.x; x < pitch; x += 256) tab[x] = 0;
+  for (int y = threadIdx.x; y < tiles_y; y += 256) tab[(y + 1) * pitch] = 0;
+  for (int t = threadIdx.x; t < T; t += 256) {
+    int sum = 0;
+    for (int c = 0; c < a.prefix_chunks && sum < kCap; ++c) sum += counts[(size_t)c * T + t];
+    const int y = t / tiles_x, x = t - y * tiles_x;
+    tab[(y + 1) * pitch + x + 1] = sum < kCap ? 1 : 0;
+  }
+  __syncthreads();
+  for (int y = threadIdx.x; y < tiles_y; y += 256) {
+    int* row = tab + (y + 1) * pitch;
+    int run = 0;
+    for (int x = 1; x <= tiles_x; ++x) row[x] = (run += row[x]);
+  }
+  __syncthreads();
+  for (int x = threadIdx.x; x < tiles_x; x += 256) {
+    int run = 0;
+    for (int y = 1; y <= tiles_y; ++y) {
+      int* e = tab + y * pitch + x + 1;
+      *e = (run += *e);
+    }
+  }
 }
 
 // Per-tile prefix of the chunk counts, coalesced: one CTA per 32 adjacent
@@ -895,10 +1053,33 @@ __global__ void debug_view_kernel(const ViewHost vh, float* __restrict__ out) {
 // ---------------------------------------------------------------------------
 // launch wrappers
 // ---------------------------------------------------------------------------
+// Dynamic shared memory above the default opt-in limit needs the function
+// attribute; the kernels' static shared memory (< 4 KB) counts against the
+// same 48 KB.
+static bool needs_smem_attr(size_t dynamic_smem) { return dynamic_smem + 4096 > 48 * 1024; }
+
 static size_t bin_smem_bytes(const Dims& d, int cov_layout, bool shadow) {
   const size_t stage = (size_t)(3 + cov_layout + 1) * kChunk * sizeof(float);
   const size_t T1 = (size_t)(d.tiles_y + 1) * (d.tiles_x + 1);
   return stage + T1 * sizeof(int) * (shadow ? 2 : 1);
+}
+
+// Per-warp tile counters of bin_skip_kernel; grids whose counters would not
+// fit in kWarpCountBytes use the CTA-wide skipping variant of bin_kernel.
+constexpr size_t kWarpCountBytes = 32 * 1024;
+static size_t warp_count_bytes(const Dims& d, bool shadow) {
+  return (size_t)(kBinThreads / 32) * ((d.T + 1) / 2) * 4 * (shadow ? 2 : 1);
+}
+static size_t bin_skip_smem_bytes(const Dims& d, int cov_layout, bool shadow) {
+  return (size_t)(3 + cov_layout + 2) * kChunk * sizeof(float) + warp_count_bytes(d, shadow);
+}
+
+template <bool kShadow>
+static void launch_bin_skip_t(const BinArgs& a, dim3 grid, size_t smem, cudaStream_t s) {
+  if (needs_smem_attr(smem))
+    cudaFuncSetAttribute(bin_skip_kernel<kShadow>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)smem);
+  bin_skip_kernel<kShadow><<<grid, kBinThreads, smem, s>>>(a);
 }
 
 cudaError_t launch_view_setup(const ViewHostPack& pack, ViewConst* out, cudaStream_t s) {
@@ -908,7 +1089,7 @@ cudaError_t launch_view_setup(const ViewHostPack& pack, ViewConst* out, cudaStre
 
 template <bool kShadow, bool kSkip>
 static void launch_bin_t(const BinArgs& a, dim3 grid, size_t smem, cudaStream_t s) {
-  if (smem > 48 * 1024)
+  if (needs_smem_attr(smem))
     cudaFuncSetAttribute(bin_kernel<kShadow, kSkip>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)smem);
   bin_kernel<kShadow, kSkip><<<grid, kBinThreads, smem, s>>>(a);
@@ -916,8 +1097,14 @@ static void launch_bin_t(const BinArgs& a, dim3 grid, size_t smem, cudaStream_t 
 
 cudaError_t launch_bin(const BinArgs& a, const Dims& d, int chunks, bool shadow, bool skip,
                        cudaStream_t s) {
-  const size_t smem = bin_smem_bytes(d, a.cov_layout, shadow);
   const dim3 grid(chunks, (a.nviews + a.views_per_cta - 1) / a.views_per_cta);
+  if (skip && warp_count_bytes(d, shadow) <= kWarpCountBytes) {
+    const size_t smem = bin_skip_smem_bytes(d, a.cov_layout, shadow);
+    if (shadow) launch_bin_skip_t<true>(a, grid, smem, s);
+    else launch_bin_skip_t<false>(a, grid, smem, s);
+    return cudaGetLastError();
+  }
+  const size_t smem = bin_smem_bytes(d, a.cov_layout, shadow);
   if (shadow) {
     if (skip) launch_bin_t<true, true>(a, grid, smem, s);
     else launch_bin_t<true, false>(a, grid, smem, s);
@@ -928,8 +1115,8 @@ cudaError_t launch_bin(const BinArgs& a, const Dims& d, int chunks, bool shadow,
   return cudaGetLastError();
 }
 
-cudaError_t launch_sat(const SatArgs& a, int nviews, cudaStream_t s) {
-  sat_kernel<<<dim3((a.T + 255) / 256, nviews), 256, 0, s>>>(a);
+cudaError_t launch_open_table(const OpenArgs& a, int nviews, int nlists, cudaStream_t s) {
+  open_table_kernel<<<dim3(nviews, nlists), 256, 0, s>>>(a);
   return cudaGetLastError();
 }
 

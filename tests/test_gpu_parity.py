@@ -232,6 +232,25 @@ def test_saturation_skip_is_exact():
         assert rel_linf(om.cpu().numpy(), fw["omega"]) <= IMAGE_RTOL
 
 
+@pytest.mark.parametrize("npx,rho", [(640, 0.08), (1024, 0.05)])
+def test_saturation_skip_on_large_tile_grids(npx, rho):
+    """The skipping binner keeps per-warp tile counters up to 2048 tiles per
+    list and switches to CTA-wide counters beyond. 640 px (1600 tiles): the
+    image-only forward (one list) takes the per-warp path and the debug lists
+    (image and shadow list) the CTA-wide one; 1024 px (4096 tiles): CTA-wide
+    for both. Lists bit-exact, images within tolerance."""
+    sc = {k: v.cuda() for k, v in S.make_scene(60000, (40.0, 40.0, 6.0), (0.05, 0.4), seed=31).items()}
+    view = S.view_tuple(33.0, 21.0, rho, npx)
+    f, q, (cnt, lst, srt) = _check_lists(sc, view)
+    assert cnt.max() == 64
+    fw = oracle_forward(sc, view, want_omega=False)
+    np.testing.assert_array_equal(cnt, fw["counts"])
+    np.testing.assert_array_equal(lst, fw["lists"])
+    img = RA.SARRasterizer(*view)(sc["means"], sc["cov33"], sc["sigma"], sc["sh"])
+    torch.cuda.synchronize()
+    assert rel_linf(image_flat(img), fw["image"]) <= IMAGE_RTOL
+
+
 @pytest.mark.parametrize("view_idx", [3, 700])
 def test_full_size_sweep_view(view_idx):
     """N = 1M Gaussians, 256 x 256 at 0.2 m (the sweep workload): lists
