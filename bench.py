@@ -185,6 +185,17 @@ PREFIX_CHUNKS = 32    # chunks binned exactly before saturation skipping
 CAP = 64              # tile list capacity
 
 
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one launch of
+# 32 views, N = 1M, 256 x 256, from an ncu capture of that launch; they belong
+# to this workload and the current kernels only.
+NCU_DRAM_BYTES_PER_LAUNCH = {
+    "bin_skip_kernel": 132_873_472,
+    "select_kernel": 43_704_832,
+    "render_kernel": 15_006_464,
+    "bin_kernel": 1_356_544,
+}
+
+
 def kernel_bytes_per_launch(kind, n, views, T, cov_floats, sh_floats, npix):
     """Algorithmic bytes of one launch of a forward kernel over `views` views:
     its compulsory reads and writes, each once.
@@ -283,7 +294,10 @@ def bench_ours(args, d):
         achieved = b / (kms / klaunch / 1e3) / 1e9
         rooflines[kname] = {"kernel": kname, "bound": "hbm", "achieved": round(achieved, 1),
                             "peak": peak, "peak_source": peak_kind, "unit": "GB/s",
-                            "frac": round(achieved / peak, 4), "traffic": None,
+                            "frac": round(achieved / peak, 4),
+                            "traffic": (NCU_DRAM_BYTES_PER_LAUNCH.get(kname)
+                                        if n == 1_000_000 and s == 256 and per_launch_views == 32
+                                        else None),
                             "bytes_per_launch": int(b), "avg_launch_us": round(kms / klaunch * 1e3, 2)}
     dominant = max(prof.items(), key=lambda kv: kv[1][0])[0]
     roof = rooflines.get(dominant)
