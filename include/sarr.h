@@ -41,6 +41,7 @@ typedef struct CUstream_st *sarr_stream_t;
 #define SARR_ERR_UNSUPPORTED 3  /* image larger than 2048 x 2048 pixels (128 tiles per axis) */
 #define SARR_ERR_CUDA 4         /* a CUDA runtime call or kernel launch failed */
 #define SARR_ERR_DEVICE 5       /* a kernel reported an error (bounded wait expired) */
+#define SARR_ERR_CAPACITY 6     /* request larger than the static scratch of sarr_forward_static */
 
 /* Covariance input layouts. */
 #define SARR_COV6 6   /* [N,6] packed upper triangle xx,yy,zz,xy,xz,yz (cov_3x3_to_6 order) */
@@ -115,6 +116,30 @@ int sarr_forward(const sarr_view *views, int n_views, int64_t n, const float *me
                  const float *cov, int cov_layout, const float *sigma, const float *sh,
                  int sh_stride, int sh_k, float *images, float *omega, void *states,
                  void *ws, size_t ws_bytes, sarr_stream_t stream);
+
+/*
+ * sarr_forward for one view, image only, without a workspace argument: the
+ * scratch is a 4.5 MiB array inside this library, one per device. No
+ * counterpart in the reference. It is for callers that cannot allocate
+ * device memory: a host whose device memory is all owned by another
+ * allocator (a pool reserved at start-up) or a C/C++ caller with no device
+ * allocator of its own, for whom cudaMalloc mid-run is not an option (it
+ * synchronises the device and can fail under memory pressure).
+ *   Limits: n <= 131072 Gaussians, range_samples and azimuth_samples <= 256;
+ *           larger requests return SARR_ERR_CAPACITY.
+ *   Setup:  the first call on a device (that device current) looks up the
+ *           scratch's device address once (cudaGetSymbolAddress); make that
+ *           first call before any stream capture begins.
+ *   Zero:   nothing has to start at zero; each call writes every scratch byte
+ *           it reads.
+ *   Races:  all calls on a device share the scratch; calls on one device
+ *           must not overlap (one stream, or ordered by the caller).
+ * Arguments as sarr_forward with n_views = 1, omega = states = NULL. Never
+ * allocates device or pinned memory.
+ */
+int sarr_forward_static(const sarr_view *view, int64_t n, const float *means, const float *cov,
+                        int cov_layout, const float *sigma, const float *sh, int sh_stride,
+                        int sh_k, float *image, sarr_stream_t stream);
 
 /*
  * Backward of n_views views; the parameter gradients are the SUM over the

@@ -353,6 +353,8 @@ const char* sarr_status_string(int status) {
     case SARR_ERR_UNSUPPORTED: return "image larger than 2048 x 2048 pixels is not supported";
     case SARR_ERR_CUDA: return "CUDA launch or runtime error";
     case SARR_ERR_DEVICE: return "device-side error (bounded wait expired)";
+    case SARR_ERR_CAPACITY:
+      return "request exceeds the static scratch of sarr_forward_static (n <= 131072, image <= 256 x 256)";
     default: return "unknown status";
   }
 }
