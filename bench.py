@@ -420,6 +420,7 @@ def cpu_baseline(args):
     """CPU restatement of the reference algorithm on a bounded sample of the
     same workload (image-only forward), all host threads."""
     from oracle import oracle as O
+    cores = O.set_threads()
     sc = make_scene(args, "cpu")
     s = {k: v.numpy() for k, v in sc.items()}
     views = S.sweep_views(args.views, samples=args.samples)
@@ -431,7 +432,7 @@ def cpu_baseline(args):
         if time.perf_counter() - t0 > 12.0:
             break
     dt = time.perf_counter() - t0
-    return {"value": done / dt, "unit": "views/s", "cores": os.cpu_count(), "kind": "port",
+    return {"value": done / dt, "unit": "views/s", "cores": cores, "kind": "port",
             "sample": f"{done} views of the sweep (N={args.n}, {args.samples}x{args.samples}), "
                       "image-only forward, C restatement with OpenMP"}
 
@@ -443,6 +444,7 @@ def bench_reference(args, d):
     if d.rank != 0:
         return None
     from oracle import oracle as O
+    cores = O.set_threads()
     sc = make_scene(args, "cpu")
     s = {k: v.numpy() for k, v in sc.items()}
     views = S.sweep_views(args.views, samples=args.samples)
@@ -462,7 +464,7 @@ def bench_reference(args, d):
             "ms_per_step": dt * 1e3 / args.steps, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": config(args),
-            "cpu_baseline": {"value": value, "unit": "views/s", "cores": os.cpu_count(),
+            "cpu_baseline": {"value": value, "unit": "views/s", "cores": cores,
                              "kind": "port",
                              "sample": f"{per_step} views per step of the sweep, image-only forward"},
             "e2e": {"value": value, "unit": "views/s", "h2d_bytes_per_step": 0,

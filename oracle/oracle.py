@@ -45,6 +45,14 @@ class ViewC(ctypes.Structure):
 _lib = None
 
 
+def set_threads(n=None):
+    """Sets the oracle's OpenMP thread count (default: every core this
+    process may run on) and returns the count in effect."""
+    if n is None:
+        n = len(os.sched_getaffinity(0))
+    return lib().oracle_set_threads(int(n))
+
+
 def lib():
     global _lib
     if _lib is None:
@@ -54,6 +62,8 @@ def lib():
         L = ctypes.CDLL(LIB_PATH)
         P = ctypes.c_void_p
         I = ctypes.c_int
+        L.oracle_set_threads.argtypes = [I]
+        L.oracle_set_threads.restype = I
         L.oracle_view_setup.argtypes = [ctypes.POINTER(View), P, ctypes.POINTER(ViewC)]
         L.oracle_preprocess.argtypes = [ctypes.POINTER(ViewC), I, P, P, I, P, P, I, I, P, P]
         L.oracle_tile_lists.argtypes = [I, I, I, P, I, P, P]
