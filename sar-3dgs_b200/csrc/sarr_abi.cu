@@ -197,9 +197,17 @@ struct Ws {
   unsigned char* view_area() const { return base + L.head; }
 };
 
+// Cell culling is used when the call qualifies (cells_eligible), the tile
+// grid suits the cell binner, and the workspace holds the cell layout for at
+// least one view; otherwise the call bins without cells.
+static bool use_cells(const Dims& d, int n_views) {
+  return cells_eligible(d, n_views) && bin_cell_supported(d);
+}
+
 int carve_ws(const Dims& d, void* ws, size_t ws_bytes, int n_views, Ws& w) {
   if (!ws || !aligned(ws, 256)) return SARR_ERR_WORKSPACE;
-  w.L = ws_layout(d);
+  w.L = ws_layout(d, use_cells(d, n_views));
+  if (w.L.cells && ws_bytes < w.L.head + w.L.per_view) w.L = ws_layout(d, false);
   if (ws_bytes < w.L.head + w.L.per_view) return SARR_ERR_WORKSPACE;
   size_t fit = (ws_bytes - w.L.head) / w.L.per_view;
   int g = n_views < kMaxViewsPerLaunch ? n_views : kMaxViewsPerLaunch;
@@ -228,6 +236,23 @@ cudaError_t setup_views(const sarr_view* views, int g0, int gv, const Ws& w, boo
   return run_kernel(kKindSetup, s, [&] { return launch_view_setup(pack, w.views, s); });
 }
 
+// The view-independent cell grid of a call (cell culling), before its groups.
+cudaError_t run_cell_prep(const Dims& d, const Ws& w, const float* means, const float* cov,
+                          int cov_layout, const float* sigma, cudaStream_t s) {
+  if (!w.L.cells) return cudaSuccess;
+  CellPrepArgs cp;
+  cp.n = d.n;
+  cp.means = means;
+  cp.cov = cov;
+  cp.cov_layout = cov_layout;
+  cp.sigma = sigma;
+  cp.grid = reinterpret_cast<SceneGrid*>(w.base + w.L.scene);
+  cp.hb = reinterpret_cast<float*>(w.base + w.L.hb);
+  cp.cid = reinterpret_cast<uint32_t*>(w.base + w.L.cid);
+  cp.cell_hb = reinterpret_cast<int*>(w.base + w.L.cell_hb);
+  return run_kernel(kKindAux, s, [&] { return launch_cell_prep(cp, s); });
+}
+
 // bin + select of the image-plane list (and optionally the shadow list) for a
 // group of views.
 cudaError_t run_selection(const Dims& d, const Ws& w, int gv, const float* means, const float* cov,
@@ -250,6 +275,9 @@ cudaError_t run_selection(const Dims& d, const Ws& w, int gv, const float* means
   ba.use_tma = aligned(means, 16) && aligned(cov, 16) && aligned(sigma, 16);
   ba.err = w.err;
   ba.nviews = gv;
+  ba.xcount = reinterpret_cast<int*>(w.view_area() + w.L.xcount);
+  ba.xlist = reinterpret_cast<uint16_t*>(w.view_area() + w.L.xlist);
+  ba.x_vstride = w.L.per_view;
   ba.open_ipp = reinterpret_cast<const int*>(w.view_area() + w.L.open_ipp);
   ba.open_sh = reinterpret_cast<const int*>(w.view_area() + w.L.open_sh);
   ba.open_vstride = w.L.per_view / sizeof(int);
@@ -287,11 +315,39 @@ cudaError_t run_selection(const Dims& d, const Ws& w, int gv, const float* means
     e = run_kernel(kKindAux, s, [&] { return launch_open_table(og, gv, shr ? 2 : 1, s); });
     if (e != cudaSuccess) return e;
     ba.chunk_offset = prefix;
-    ba.views_per_cta = views_per_cta(d.C - prefix);
-    e = run_kernel(kKindBinSkip, s, [&] {
-      return launch_bin(ba, d, d.C - prefix, shr != nullptr, true, s);
-    });
-    if (e != cudaSuccess) return e;
+    if (w.L.cells) {
+      CellTestArgs ct;
+      ct.views = w.views;
+      ct.grid = reinterpret_cast<const SceneGrid*>(w.base + w.L.scene);
+      ct.cell_hb = reinterpret_cast<const int*>(w.base + w.L.cell_hb);
+      ct.open_ipp = ba.open_ipp;
+      ct.open_sh = ba.open_sh;
+      ct.open_vstride = ba.open_vstride;
+      ct.shadow = shr != nullptr;
+      ct.bits = reinterpret_cast<uint32_t*>(w.view_area() + w.L.bits);
+      ct.bits_vstride = w.L.per_view / sizeof(uint32_t);
+      e = run_kernel(kKindAux, s, [&] { return launch_cell_test(ct, gv, s); });
+      if (e != cudaSuccess) return e;
+      ba.chunks = d.C - prefix;
+      // ~4 waves of 3 CTAs per SM over (chunks x view groups of 8), at least
+      // 2 chunks per CTA so that the per-warp cell bitmap load is amortised
+      const int vgroups = (gv + 7) / 8;
+      const int64_t units = (int64_t)ba.chunks * vgroups;
+      int cpc = (int)((units + 148 * 3 * 4 - 1) / (148 * 3 * 4));
+      ba.chunks_per_cta = cpc < 2 ? 2 : cpc;
+      ba.hb = reinterpret_cast<const float*>(w.base + w.L.hb);
+      ba.cid = reinterpret_cast<const uint32_t*>(w.base + w.L.cid);
+      ba.bits = ct.bits;
+      ba.bits_vstride = ct.bits_vstride;
+      e = run_kernel(kKindBinSkip, s, [&] { return launch_bin_cell(ba, d, shr != nullptr, s); });
+      if (e != cudaSuccess) return e;
+    } else {
+      ba.views_per_cta = views_per_cta(d.C - prefix);
+      e = run_kernel(kKindBinSkip, s, [&] {
+        return launch_bin(ba, d, d.C - prefix, shr != nullptr, true, s);
+      });
+      if (e != cudaSuccess) return e;
+    }
   }
 
   ScanArgs sc;
@@ -324,6 +380,13 @@ cudaError_t run_selection(const Dims& d, const Ws& w, int gv, const float* means
   sa.need_vstride = sc.need_vstride;
   sa.need_n = sc.need_n;
   sa.need_n_vstride = sc.need_n_vstride;
+  // the skipping binners record each chunk's exactly binned Gaussians, except
+  // the CTA-wide variant for very large tile grids
+  const bool xlists = prefix < d.C && (w.L.cells || skip_bin_per_warp(d, shr != nullptr));
+  sa.xlist_from = xlists ? prefix : INT32_MAX;
+  sa.xcount = xlists ? ba.xcount : nullptr;
+  sa.xlist = xlists ? ba.xlist : nullptr;
+  sa.x_vstride = ba.x_vstride;
   sa.err = w.err;
   e = run_kernel(kKindSelect, s, [&] { return launch_select(sa, d, gv, false, s); });
   if (e != cudaSuccess || !shr) return e;
@@ -372,7 +435,7 @@ int sarr_workspace_size(int64_t n, int range_samples, int azimuth_samples, int n
   Dims d;
   const int st = make_dims(&v, 1, n, d);
   if (st) return st;
-  const WsLayout L = ws_layout(d);
+  const WsLayout L = ws_layout(d, use_cells(d, n_views));
   const int g = n_views < kMaxViewsPerLaunch ? n_views : kMaxViewsPerLaunch;
   *bytes = L.head + L.per_view * (size_t)g;
   return SARR_OK;
@@ -416,6 +479,7 @@ int sarr_forward(const sarr_view* views, int n_views, int64_t n, const float* me
   st = carve_ws(d, ws, ws_bytes, n_views, w);
   if (st) return st;
   const size_t state_bytes = w.L.st.bytes;
+  if (run_cell_prep(d, w, means, cov, cov_layout, sigma, s) != cudaSuccess) return SARR_ERR_CUDA;
 
   for (int g0 = 0; g0 < n_views; g0 += w.group) {
     const int gv = (n_views - g0) < w.group ? (n_views - g0) : w.group;
@@ -507,6 +571,8 @@ int sarr_backward(const sarr_view* views, int n_views, int64_t n, const float* m
   st = carve_ws(d, ws, ws_bytes, n_views, w);
   if (st) return st;
   const size_t state_bytes = w.L.st.bytes;
+  if (!states && run_cell_prep(d, w, means, cov, cov_layout, sigma, s) != cudaSuccess)
+    return SARR_ERR_CUDA;
 
   for (int g0 = 0; g0 < n_views; g0 += w.group) {
     const int gv = (n_views - g0) < w.group ? (n_views - g0) : w.group;

@@ -29,12 +29,42 @@ constexpr int kChunk = kBinThreads * kBinPerThread;  // Gaussians per count row
 constexpr int kSelectThreads = 256;
 constexpr int kScanThreads = 512;
 constexpr int kPrefixChunks = 32;                // chunks binned exactly before saturation skipping
+constexpr int kXCap = 256;                       // exactly binned Gaussians listed per skipped chunk
 constexpr int kWarpsPerTile = 8;                 // 8 warps x 32 pixels = one 16x16 tile
 constexpr int kMaxTilesAxis = 128;               // images up to 2048 x 2048
 constexpr int kMaxViewsPerLaunch = 32;
 constexpr uint32_t kEmptyRect = 0x000000FFu;     // tc0 = 255 > tc1 = 0
 
 // Device error bits (workspace error word).
+// Cell culling of multi-view launches: a view-independent grid of cells over
+// the Gaussian centres; per view, one bit per cell says whether any member
+// can reach a tile that is still open after the saturation prefix.
+constexpr int kMaxCells = 32768;
+constexpr int kCellWords = kMaxCells / 32;
+constexpr int kCellMinViews = 8;                 // calls with fewer views bin without cells
+constexpr uint32_t kCellAlways = 0xFFFFFFFFu;    // no cell: always tested individually
+constexpr uint32_t kCellNever = 0xFFFFFFFEu;     // transmittance < 0.01: never in a list
+constexpr float kCellMaxHalfBound = 64.0f;       // larger bbox bounds are never culled
+
+struct SceneGrid {
+  int lo_key[3], hi_key[3];  // ordered-int keys of the finite centres' bounding box
+  float lo[3];
+  float a, inv_a;            // cell edge [m] and its inverse
+  int dims[3];
+  int ncells;
+  float half_diag;           // bound on |member centre - cell centre| [m], with margins
+  int valid;                 // 0: no finite centre (no Gaussian is in a cell)
+};
+
+// Order-preserving map of floats to ints (for atomicMin / atomicMax).
+__device__ __forceinline__ int ordered_key(float f) {
+  const int i = __float_as_int(f);
+  return i >= 0 ? i : i ^ 0x7FFFFFFF;
+}
+__device__ __forceinline__ float key_float(int k) {
+  return __int_as_float(k >= 0 ? k : k ^ 0x7FFFFFFF);
+}
+
 constexpr int kDevErrTmaTimeout = 1;
 constexpr int kDevErrListSlot = 2;
 

@@ -56,18 +56,42 @@ __host__ __device__ inline StateLayout state_layout(int64_t n, int T) {
 //   i32 (summed-area tables of the tiles still open after the saturation
 //   prefix, from open_table_kernel), state_ipp (used when the caller gives no
 //   state), state_sh, partial_om [T][64] float2, partial_bwd [T][64][8] float.
+// With cells (multi-view calls, see kCellMinViews) the head also holds the
+// SceneGrid, per-Gaussian bbox bounds hb [n] f32 and cell ids cid [n] u32, the
+// per-cell largest bound cell_hb [kMaxCells] (ordered-int keys), and each view
+// area its cell bitmap bits [kCellWords] u32.
 struct WsLayout {
-  size_t viewconst, err, head;
+  size_t viewconst, err, scene, hb, cid, cell_hb, head;
   size_t counts_ipp, counts_sh, need_ipp, need_sh, need_n_ipp, need_n_sh, open_ipp, open_sh;
-  size_t state_ipp, state_sh, partial_om, partial_bwd, per_view;
+  size_t bits, xcount, xlist, state_ipp, state_sh, partial_om, partial_bwd, per_view;
+  bool cells;
   StateLayout st;
 };
 
-__host__ inline WsLayout ws_layout(const Dims& d) {
+// Cell culling applies to calls of at least kCellMinViews views whose
+// Gaussians extend past the exactly binned prefix.
+__host__ inline bool cells_eligible(const Dims& d, int n_views) {
+  return n_views >= kCellMinViews && d.C > kPrefixChunks;
+}
+
+__host__ inline WsLayout ws_layout(const Dims& d, bool cells) {
   WsLayout L;
+  L.cells = cells;
   L.viewconst = 0;
   L.err = align256(sizeof(ViewConst) * kMaxViewsPerLaunch);
-  L.head = L.err + 256;
+  size_t h = L.err + 256;
+  L.scene = L.hb = L.cid = L.cell_hb = 0;
+  if (cells) {
+    L.scene = h;
+    h += align256(sizeof(SceneGrid));
+    L.hb = h;
+    h += align256((size_t)d.n * 4);
+    L.cid = h;
+    h += align256((size_t)d.n * 4);
+    L.cell_hb = h;
+    h += align256((size_t)kMaxCells * 4);
+  }
+  L.head = h;
   L.st = state_layout(d.n, d.T);
   size_t o = 0;
   L.counts_ipp = o;
@@ -86,6 +110,18 @@ __host__ inline WsLayout ws_layout(const Dims& d) {
   o += align256((size_t)(d.tiles_y + 1) * (d.tiles_x + 1) * 4);
   L.open_sh = o;
   o += align256((size_t)(d.tiles_y + 1) * (d.tiles_x + 1) * 4);
+  // Per chunk after the prefix: how many of its Gaussians the skipping binner
+  // binned exactly (-1: more than kXCap, or not recorded) and their chunk
+  // offsets in index order; select_kernel scans only those.
+  L.xcount = o;
+  o += align256((size_t)d.C * 4);
+  L.xlist = o;
+  o += align256((size_t)d.C * kXCap * 2);
+  L.bits = 0;
+  if (cells) {
+    L.bits = o;
+    o += align256((size_t)kCellWords * 4);
+  }
   L.state_ipp = o;
   o += L.st.bytes;
   L.state_sh = o;
@@ -113,6 +149,16 @@ struct BinArgs {
   const int* open_ipp;  // open-tile summed-area tables (skip variant), open_vstride ints per view
   const int* open_sh;
   size_t open_vstride;
+  int* xcount;         // exactly binned Gaussians per chunk (skip variants)
+  uint16_t* xlist;     // [C][kXCap] their chunk offsets
+  size_t x_vstride;    // bytes per view of both
+  // cell variant
+  int chunks;          // chunks of the launch
+  int chunks_per_cta;
+  const float* hb;     // [n] view-independent bbox bounds
+  const uint32_t* cid; // [n] cell ids
+  const uint32_t* bits;  // cell bitmaps, bits_vstride words per view
+  size_t bits_vstride;
   int64_t n;
   int C;
   const float* means;
@@ -126,6 +172,30 @@ struct BinArgs {
   size_t counts_vstride;
   int use_tma;
   int* err;
+};
+
+struct CellPrepArgs {
+  int64_t n;
+  const float* means;
+  const float* cov;
+  int cov_layout;
+  const float* sigma;
+  SceneGrid* grid;
+  float* hb;
+  uint32_t* cid;
+  int* cell_hb;
+};
+
+struct CellTestArgs {
+  const ViewConst* views;
+  const SceneGrid* grid;
+  const int* cell_hb;
+  const int* open_ipp;
+  const int* open_sh;
+  size_t open_vstride;
+  int shadow;
+  uint32_t* bits;
+  size_t bits_vstride;
 };
 
 struct SelectArgs {
@@ -144,6 +214,10 @@ struct SelectArgs {
   size_t need_vstride;        // bytes
   const int* need_n;          // [T] per view
   size_t need_n_vstride;      // ints
+  int xlist_from;             // first chunk with an exact list (INT32_MAX: none)
+  const int* xcount;
+  const uint16_t* xlist;
+  size_t x_vstride;           // bytes
   int* err;
 };
 
@@ -232,6 +306,15 @@ cudaError_t launch_view_setup(const ViewHostPack& pack, ViewConst* out, cudaStre
 cudaError_t launch_bin(const BinArgs& a, const Dims& d, int chunks, bool shadow, bool skip,
                        cudaStream_t s);
 cudaError_t launch_open_table(const OpenArgs& a, int nviews, int nlists, cudaStream_t s);
+// view-independent cell grid of one call (four kernels)
+cudaError_t launch_cell_prep(const CellPrepArgs& a, cudaStream_t s);
+cudaError_t launch_cell_test(const CellTestArgs& a, int nviews, cudaStream_t s);
+// bin_cell_kernel over the a.chunks chunks from a.chunk_offset
+cudaError_t launch_bin_cell(const BinArgs& a, const Dims& d, bool shadow, cudaStream_t s);
+bool bin_cell_supported(const Dims& d);
+// true when the skipping binner keeps per-warp counters (and records the
+// exact lists); false selects its CTA-wide variant
+bool skip_bin_per_warp(const Dims& d, bool shadow);
 cudaError_t launch_scan(const ScanArgs& a, int nviews, cudaStream_t s);
 cudaError_t launch_select(const SelectArgs& a, const Dims& d, int nviews, bool shadow_list,
                           cudaStream_t s);

@@ -294,6 +294,17 @@ __global__ void __launch_bounds__(kBinThreads) bin_kernel(const BinArgs a) {
   }
 }
 
+// Exact list of view v and chunk c (null when the launch records none), and
+// the per-chunk lengths of view v.
+__device__ __forceinline__ uint16_t* x_list(const BinArgs& a, int v, int c) {
+  if (!a.xlist) return nullptr;
+  return reinterpret_cast<uint16_t*>(reinterpret_cast<unsigned char*>(a.xlist) + v * a.x_vstride) +
+         (size_t)c * kXCap;
+}
+__device__ __forceinline__ int* x_count(const BinArgs& a, int v) {
+  return reinterpret_cast<int*>(reinterpret_cast<unsigned char*>(a.xcount) + v * a.x_vstride);
+}
+
 // Adds one hit to every tile of a rectangle in a warp's tile counters (two
 // 16-bit counters per word; a chunk holds at most kChunk hits per tile).
 __device__ __forceinline__ void count_rect(uint32_t* cnt, uint32_t rc, int tiles_x) {
@@ -378,6 +389,8 @@ __global__ void __launch_bounds__(kBinThreads, 3) bin_skip_kernel(const BinArgs 
     const int* open_ipp = a.open_ipp + v * a.open_vstride;
     const int* open_sh = a.open_sh + v * a.open_vstride;
 
+    uint16_t* xl = x_list(a, v, chunk);
+    int xn = 0;  // Gaussians of this chunk binned exactly so far (index order)
     // exact binning of queue[lane] (every lane with a queued Gaussian)
     auto bin_queued = [&](int j) {
       uint32_t rc_ipp = kEmptyRect, rc_sh = kEmptyRect;
@@ -388,6 +401,7 @@ __global__ void __launch_bounds__(kBinThreads, 3) bin_skip_kernel(const BinArgs 
         rects_sh[j] = rc_sh;
         count_rect(s_cnt_sh, rc_sh, tiles_x);
       }
+      if (xl && xn + lane < kXCap) xl[xn + lane] = (uint16_t)j;
     };
 
     int qn = 0;
@@ -416,6 +430,7 @@ __global__ void __launch_bounds__(kBinThreads, 3) bin_skip_kernel(const BinArgs 
       __syncwarp();
       if (qn >= 32) {
         bin_queued(queue[lane]);
+        xn += 32;
         __syncwarp();
         if (lane < qn - 32) queue[lane] = queue[lane + 32];
         qn -= 32;
@@ -423,10 +438,318 @@ __global__ void __launch_bounds__(kBinThreads, 3) bin_skip_kernel(const BinArgs 
       }
     }
     if (lane < qn) bin_queued(queue[lane]);
+    xn += qn;
     __syncwarp();
+    if (xl && lane == 0) x_count(a, v)[chunk] = xn <= kXCap ? xn : -1;
 
     flush_counts(s_cnt, a.counts_ipp + v * a.counts_vstride + (size_t)chunk * T, T, lane);
     if (kShadow) flush_counts(s_cnt_sh, a.counts_sh + v * a.counts_vstride + (size_t)chunk * T, T, lane);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// cell culling (calls of kCellMinViews views or more)
+// ---------------------------------------------------------------------------
+// Tile rectangle of the box (cr +- hr) x (cc +- hc), clamped like bound_rect;
+// half-widths that are not finite and below 1e6 give the whole image.
+__device__ __forceinline__ uint32_t bound_rect2(float cr, float cc, float hr, float hc, int Nr,
+                                                int Na) {
+  if (!(hr < 1e6f && hc < 1e6f && fabsf(cr) < 1e9f && fabsf(cc) < 1e9f))
+    return make_rect(0, Nr - 1, 0, Na - 1, Nr, Na);
+  const int r0 = max(0, (int)floorf(cr - hr)), r1 = min(Nr - 1, (int)ceilf(cr + hr));
+  const int c0 = max(0, (int)floorf(cc - hc)), c1 = min(Na - 1, (int)ceilf(cc + hc));
+  return make_rect(r0, r1, c0, c1, Nr, Na);
+}
+
+__global__ void cell_init_kernel(SceneGrid* g, int* cell_hb) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < kMaxCells) cell_hb[i] = ordered_key(-1.0f);
+  if (i < 3) {
+    g->lo_key[i] = ordered_key(INFINITY);
+    g->hi_key[i] = ordered_key(-INFINITY);
+  }
+}
+
+// Bounding box of the finite Gaussian centres.
+__global__ void __launch_bounds__(256) scene_bounds_kernel(const float* __restrict__ means,
+                                                           int64_t n, SceneGrid* g) {
+  float lo[3] = {INFINITY, INFINITY, INFINITY}, hi[3] = {-INFINITY, -INFINITY, -INFINITY};
+  for (int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; j < n;
+       j += (int64_t)gridDim.x * blockDim.x) {
+    const float p[3] = {means[3 * j], means[3 * j + 1], means[3 * j + 2]};
+    if (isfinite(p[0]) && isfinite(p[1]) && isfinite(p[2])) {
+#pragma unroll
+      for (int k = 0; k < 3; ++k) {
+        lo[k] = fminf(lo[k], p[k]);
+        hi[k] = fmaxf(hi[k], p[k]);
+      }
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < 3; ++k) {
+    for (int o = 16; o > 0; o >>= 1) {
+      lo[k] = fminf(lo[k], __shfl_xor_sync(0xffffffffu, lo[k], o));
+      hi[k] = fmaxf(hi[k], __shfl_xor_sync(0xffffffffu, hi[k], o));
+    }
+  }
+  if ((threadIdx.x & 31) == 0) {
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+      atomicMin(&g->lo_key[k], ordered_key(lo[k]));
+      atomicMax(&g->hi_key[k], ordered_key(hi[k]));
+    }
+  }
+}
+
+// Cell grid over the bounding box: about n / 32 cells, at most kMaxCells.
+// Membership uses floor((p - lo) / a) in float; half_diag bounds the distance
+// of a member to its cell's centre including those roundings.
+__global__ void scene_grid_kernel(SceneGrid* g, int64_t n) {
+  if (threadIdx.x != 0) return;
+  float lo[3], hi[3], ext[3];
+  bool ok = true;
+  for (int k = 0; k < 3; ++k) {
+    lo[k] = key_float(g->lo_key[k]);
+    hi[k] = key_float(g->hi_key[k]);
+    ok = ok && (lo[k] <= hi[k]);
+    ext[k] = hi[k] - lo[k];
+  }
+  g->valid = 0;
+  g->ncells = 0;
+  if (!ok) return;
+  const float emax = fmaxf(ext[0], fmaxf(ext[1], ext[2]));
+  const float pad = 1e-3f * emax + 1e-6f;
+  const float vol = (ext[0] + pad) * (ext[1] + pad) * (ext[2] + pad);
+  const int64_t target = max((int64_t)1, min((int64_t)kMaxCells, n / 32));
+  float a = cbrtf(vol / (float)target);
+  if (!(a > 0.0f) || !isfinite(a)) a = fmaxf(emax, 1e-6f);
+  int dims[3];
+  for (int it = 0; it < 200; ++it) {
+    int64_t prod = 1;
+    for (int k = 0; k < 3; ++k) {
+      float t = ceilf(ext[k] / a);
+      dims[k] = t < 1.0f ? 1 : (t > 1e6f ? 1000000 : (int)t);
+      while ((float)dims[k] * a < ext[k]) ++dims[k];
+      prod *= dims[k];
+    }
+    if (prod <= kMaxCells) break;
+    a *= 1.05f;
+  }
+  int64_t prod = (int64_t)dims[0] * dims[1] * dims[2];
+  if (prod > kMaxCells) return;  // not reached for finite boxes; no cells then
+  float scale = emax + a;
+  for (int k = 0; k < 3; ++k) {
+    g->lo[k] = lo[k];
+    g->dims[k] = dims[k];
+    scale += fabsf(lo[k]);
+  }
+  g->a = a;
+  g->inv_a = 1.0f / a;
+  g->ncells = (int)prod;
+  g->half_diag = a * 0.8660254f * 1.0001f + 4e-6f * scale;
+  g->valid = 1;
+}
+
+// Per Gaussian: its view-independent bbox bound and cell id, and the largest
+// bound of every cell.
+__global__ void __launch_bounds__(256) cell_assign_kernel(const CellPrepArgs a) {
+  const int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= a.n) return;
+  const SceneGrid& g = *a.grid;
+  uint32_t id = kCellAlways;
+  float hb = INFINITY;
+  if (a.sigma[j] < 0.01f) {
+    id = kCellNever;  // preprocess_kernel: invalid (:351)
+  } else {
+    float cw[6];
+    load_cov6(a.cov + j * a.cov_layout, a.cov_layout, cw);
+    hb = view_free_half_bound(cw);
+    const float x = a.means[3 * j], y = a.means[3 * j + 1], z = a.means[3 * j + 2];
+    if (g.valid && hb <= kCellMaxHalfBound && isfinite(x) && isfinite(y) && isfinite(z)) {
+      const int ix = min(max((int)floorf((x - g.lo[0]) * g.inv_a), 0), g.dims[0] - 1);
+      const int iy = min(max((int)floorf((y - g.lo[1]) * g.inv_a), 0), g.dims[1] - 1);
+      const int iz = min(max((int)floorf((z - g.lo[2]) * g.inv_a), 0), g.dims[2] - 1);
+      id = (uint32_t)((iz * g.dims[1] + iy) * g.dims[0] + ix);
+      atomicMax(a.cell_hb + id, ordered_key(hb));
+    }
+  }
+  a.hb[j] = hb;
+  a.cid[j] = id;
+}
+
+// Cell bitmap of one view: bit c is set when a member of cell c may reach a
+// tile still open after the prefix (either list). A member p of cell c lies
+// within half_diag of the cell centre q; R_min and X_r are 1-Lipschitz in the
+// world position, so its exact image centre lies within half_diag / rho
+// (pixels) of q's, and approximate-centre errors add center_margin at p and q.
+__global__ void __launch_bounds__(256) cell_test_kernel(const CellTestArgs a) {
+  const int c = blockIdx.x * 256 + threadIdx.x;
+  const int v = blockIdx.y;
+  const SceneGrid& g = *a.grid;
+  bool open = false;
+  if (g.valid && c < g.ncells) {
+    const float hbm = key_float(a.cell_hb[c]);
+    if (hbm >= 0.0f) {
+      const ViewConst& vc = a.views[v];
+      const int Nr = vc.h.Nr, Na = vc.h.Na, pitch = vc.tiles_x + 1;
+      const int d0 = g.dims[0], d1 = g.dims[1];
+      const int ix = c % d0, iy = (c / d0) % d1, iz = c / (d0 * d1);
+      const float qx = g.lo[0] + ((float)ix + 0.5f) * g.a;
+      const float qy = g.lo[1] + ((float)iy + 0.5f) * g.a;
+      const float qz = g.lo[2] + ((float)iz + 0.5f) * g.a;
+      float r, cc, xr, yr;
+      approx_center(vc, qx, qy, qz, r, cc, xr, yr);
+      const float base = hbm + 2.0f * vc.center_margin + 0.02f;
+      const float hr = base + g.half_diag * fabsf(vc.inv_rho_r) * 1.0001f;
+      const float hc = base + g.half_diag * fabsf(vc.inv_rho_a) * 1.0001f;
+      open = open_in_rect(bound_rect2(r, cc, hr, hc, Nr, Na), a.open_ipp + v * a.open_vstride,
+                          pitch) > 0;
+      if (a.shadow && !open) {
+        const float hs = base + g.half_diag * 1.0001f;
+        open = open_in_rect(bound_rect2(yr, xr, hs, hs, Nr, Na), a.open_sh + v * a.open_vstride,
+                            pitch) > 0;
+      }
+    }
+  }
+  const unsigned m = __ballot_sync(0xffffffffu, open);
+  if ((threadIdx.x & 31) == 0) a.bits[v * a.bits_vstride + (c >> 5)] = m;
+}
+
+// Saturation-skipping binning with cell culling: one view per warp, a range
+// of chunks per CTA. A Gaussian whose cell is closed for the view gets an
+// empty rectangle after one bitmap lookup; the others go through the
+// per-Gaussian test of bin_skip_kernel (queue A) and, when that cannot skip
+// them, exact binning (queue B). Parameters of queued Gaussians are read from
+// global memory (L2); only the chunk's cell ids are staged.
+template <bool kShadow>
+__global__ void __launch_bounds__(kBinThreads, 3) bin_cell_kernel(const BinArgs a) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  __shared__ short s_qa[kBinThreads / 32][64];
+  __shared__ short s_qb[kBinThreads / 32][64];
+  constexpr int kWarps = kBinThreads / 32;
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int v = blockIdx.y * kWarps + warp;
+  const bool active = v < a.nviews;
+  const int tiles_x = a.views[0].tiles_x, tiles_y = a.views[0].tiles_y, T = tiles_x * tiles_y;
+  const int cs = a.cov_layout;
+  const int TW = (T + 1) >> 1;
+  const int pitch = tiles_x + 1;
+
+  uint32_t* s_bits = reinterpret_cast<uint32_t*>(smem_raw) + warp * kCellWords;
+  uint32_t* s_cid = reinterpret_cast<uint32_t*>(smem_raw) + kWarps * kCellWords;
+  uint32_t* s_cnt = s_cid + kChunk + warp * TW * (kShadow ? 2 : 1);
+  uint32_t* s_cnt_sh = s_cnt + TW;
+  short* qa = s_qa[warp];
+  short* qb = s_qb[warp];
+
+  const int vv = active ? v : 0;
+  const ViewConst& vg = a.views[vv];
+  const ViewConst vc = vg;
+  const int Nr = vc.h.Nr, Na = vc.h.Na;
+  uint32_t* rects_ipp = reinterpret_cast<uint32_t*>(a.ipp.base + vv * a.ipp.vstride + a.ipp.L.rects);
+  uint32_t* rects_sh =
+      kShadow ? reinterpret_cast<uint32_t*>(a.sh.base + vv * a.sh.vstride + a.sh.L.rects) : nullptr;
+  const int* open_ipp = a.open_ipp + vv * a.open_vstride;
+  const int* open_sh = a.open_sh + vv * a.open_vstride;
+  if (active) {
+    const uint32_t* bits = a.bits + vv * a.bits_vstride;
+    for (int i = lane; i < kCellWords; i += 32) s_bits[i] = __ldg(bits + i);
+    for (int i = lane; i < TW * (kShadow ? 2 : 1); i += 32) s_cnt[i] = 0;
+  }
+  const unsigned lt_mask = (1u << lane) - 1u;
+
+  const int c_first = a.chunk_offset + blockIdx.x * a.chunks_per_cta;
+  const int c_last = min(a.chunk_offset + a.chunks, c_first + a.chunks_per_cta);
+  for (int chunk = c_first; chunk < c_last; ++chunk) {
+    const int64_t base = (int64_t)chunk * kChunk;
+    const int gcount = (int)min((int64_t)kChunk, a.n - base);
+    __syncthreads();  // the previous chunk's ids are consumed
+    for (int i = tid; i < gcount; i += kBinThreads) s_cid[i] = __ldg(a.cid + base + i);
+    __syncthreads();
+    if (!active) continue;
+    const float* means = a.means + base * 3;
+    const float* cov = a.cov + base * cs;
+    const float* hbp = a.hb + base;
+    uint32_t* r_ipp = rects_ipp + base;
+    uint32_t* r_sh = kShadow ? rects_sh + base : nullptr;
+
+    uint16_t* xl = x_list(a, vv, chunk);
+    int xn = 0;  // Gaussians of this chunk binned exactly so far (index order)
+    // exact binning of Gaussian j (chunk-local) by this lane
+    auto bin_queued = [&](int j) {
+      uint32_t rc_ipp = kEmptyRect, rc_sh = kEmptyRect;
+      bin_exact<kShadow>(vg, means, cov, cs, j, rc_ipp, rc_sh);
+      if (xl && xn + lane < kXCap) xl[xn + lane] = (uint16_t)j;
+      r_ipp[j] = rc_ipp;
+      count_rect(s_cnt, rc_ipp, tiles_x);
+      if (kShadow) {
+        r_sh[j] = rc_sh;
+        count_rect(s_cnt_sh, rc_sh, tiles_x);
+      }
+    };
+    // per-Gaussian test (bin_skip_kernel's) of Gaussian j: true when it
+    // needs exact binning; otherwise its empty rectangles are written
+    auto needs_exact = [&](int j) {
+      if (s_cid[j] == kCellAlways) return true;
+      float r, c, xr, yr;
+      approx_center(vc, __ldg(means + 3 * j), __ldg(means + 3 * j + 1), __ldg(means + 3 * j + 2), r,
+                    c, xr, yr);
+      const float h = __ldg(hbp + j) + vc.center_margin;
+      bool skip = open_in_rect(bound_rect(r, c, h, Nr, Na), open_ipp, pitch) == 0;
+      if (kShadow && skip) skip = open_in_rect(bound_rect(yr, xr, h, Nr, Na), open_sh, pitch) == 0;
+      if (skip) {
+        r_ipp[j] = kEmptyRect;
+        if (kShadow) r_sh[j] = kEmptyRect;
+      }
+      return !skip;
+    };
+    // tests queue A slots [0, min(na, 32)) and moves the survivors to queue B;
+    // bins 32 of queue B once it holds that many
+    int na = 0, nb = 0;
+    auto drain_a = [&]() {
+      const bool take = lane < na;
+      const int j1 = take ? qa[lane] : 0;
+      const bool exact = take && needs_exact(j1);
+      const unsigned mb = __ballot_sync(0xffffffffu, exact);
+      if (exact) qb[nb + __popc(mb & lt_mask)] = (short)j1;
+      nb += __popc(mb);
+      __syncwarp();
+      if (lane < na - 32) qa[lane] = qa[lane + 32];
+      na = na > 32 ? na - 32 : 0;
+      if (nb >= 32) {
+        bin_queued(qb[lane]);
+        xn += 32;
+        __syncwarp();
+        if (lane < nb - 32) qb[lane] = qb[lane + 32];
+        nb -= 32;
+      }
+      __syncwarp();
+    };
+    for (int j0 = 0; j0 < gcount; j0 += 32) {
+      const int j = j0 + lane;
+      bool cand = false;
+      if (j < gcount) {
+        const uint32_t id = s_cid[j];
+        cand = id == kCellAlways || (id != kCellNever && ((s_bits[id >> 5] >> (id & 31)) & 1u));
+        if (!cand) {
+          r_ipp[j] = kEmptyRect;
+          if (kShadow) r_sh[j] = kEmptyRect;
+        }
+      }
+      const unsigned m = __ballot_sync(0xffffffffu, cand);
+      if (cand) qa[na + __popc(m & lt_mask)] = (short)j;
+      na += __popc(m);
+      __syncwarp();
+      if (na >= 32) drain_a();
+    }
+    if (na > 0) drain_a();
+    if (lane < nb) bin_queued(qb[lane]);
+    xn += nb;
+    __syncwarp();
+    if (xl && lane == 0) x_count(a, vv)[chunk] = xn <= kXCap ? xn : -1;
+    flush_counts(s_cnt, a.counts_ipp + vv * a.counts_vstride + (size_t)chunk * T, T, lane);
+    if (kShadow) flush_counts(s_cnt_sh, a.counts_sh + vv * a.counts_vstride + (size_t)chunk * T, T, lane);
   }
 }
 
@@ -514,105 +837,171 @@ __global__ void __launch_bounds__(kScanThreads) scan_kernel(const ScanArgs a) {
 // ---------------------------------------------------------------------------
 // capped tile selection + tile records
 // ---------------------------------------------------------------------------
+// One warp per tile (kSelectThreads / 32 tiles per CTA), no CTA barrier.
+//  1. emit: every needed chunk's 1024 rectangles are loaded at once (eight
+//     16-byte loads per lane) and its hits are ranked in index order with a
+//     warp scan, filling list slots [hits before, hits before + needed);
+//  2. the listed Gaussians (two slots per lane) are projected again in full
+//     (SH only for them) into 48-byte records;
+//  3. each slot's rank by (Z_r, slot) places its record.
 template <bool kShadowList>
 __global__ void __launch_bounds__(kSelectThreads) select_kernel(const SelectArgs a) {
-  __shared__ int s_list[kCap];
-  __shared__ __align__(16) Rec s_rec[kCap];
-  __shared__ float s_z[kCap];
-  __shared__ int s_rank[kCap];
+  constexpr int kWarps = kSelectThreads / 32;
+  __shared__ int s_list[kWarps][kCap];
+  __shared__ float s_z[kWarps][kCap];
+  __shared__ int s_rank[kWarps][kCap];
 
-  const int t = blockIdx.x, v = blockIdx.y;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int v = blockIdx.y;
   const ViewConst& vc = a.views[v];
-  const int tiles_x = vc.tiles_x;
+  const int tiles_x = vc.tiles_x, T = tiles_x * vc.tiles_y;
+  const int t = blockIdx.x * kWarps + warp;
+  if (t >= T) return;  // warp-uniform; nothing below synchronises the CTA
   const int tx = t % tiles_x, ty = t / tiles_x;
   unsigned char* st = a.st.base + v * a.st.vstride;
-  // 1. list length and the chunks holding its slots (scan_kernel)
   const int count = reinterpret_cast<const int*>(st + a.st.L.count)[t];
   if (count == 0) return;
   const int nneed = a.need_n[v * a.need_n_vstride + t];
   const int4* need = reinterpret_cast<const int4*>(a.need + v * a.need_vstride) + (size_t)t * kCap;
-  if (tid < kCap) s_list[tid] = -1;
-  __syncthreads();
+  int* list = s_list[warp];
+  list[lane] = -1;
+  list[lane + 32] = -1;
+  __syncwarp();
 
-  // 2. emit: the hits of each needed chunk in index order.
+  // 1. emit
   const uint32_t* rects = reinterpret_cast<const uint32_t*>(st + a.st.L.rects);
-  for (int q = warp; q < nneed; q += kSelectThreads / 32) {
+  const int* xcount = a.xcount ? reinterpret_cast<const int*>(
+                                     reinterpret_cast<const unsigned char*>(a.xcount) + v * a.x_vstride)
+                               : nullptr;
+  const unsigned lt_mask = (1u << lane) - 1u;
+  for (int q = 0; q < nneed; ++q) {
     const int4 nd = need[q];
-    const int need = min(nd.z, kCap - nd.y);
+    const int want = min(nd.z, kCap - nd.y);
     const int64_t b0 = (int64_t)nd.x * kChunk;
-    const int64_t b1 = min(b0 + kChunk, a.n);
-    int found = 0;
-    for (int64_t j0 = b0; j0 < b1 && found < need; j0 += 32) {
-      const int64_t j = j0 + lane;
-      const bool hit = (j < b1) && rect_has(rects[j], tx, ty);
-      const unsigned m = __ballot_sync(0xffffffffu, hit);
-      if (hit) {
-        const int rk = found + __popc(m & ((1u << lane) - 1u));
-        if (rk < need) s_list[nd.y + rk] = (int)j;
+    const int xc = (xcount && nd.x >= a.xlist_from) ? xcount[nd.x] : -1;
+    if (xc >= 0) {
+      // only the chunk's exactly binned Gaussians can hit the tile
+      const uint16_t* xl = reinterpret_cast<const uint16_t*>(
+                               reinterpret_cast<const unsigned char*>(a.xlist) + v * a.x_vstride) +
+                           (size_t)nd.x * kXCap;
+      int found = 0;
+      for (int i0 = 0; i0 < xc && found < want; i0 += 32) {
+        const int i = i0 + lane;
+        bool hit = false;
+        int j = 0;
+        if (i < xc) {
+          j = (int)b0 + xl[i];
+          hit = rect_has(rects[j], tx, ty);
+        }
+        const unsigned m = __ballot_sync(0xffffffffu, hit);
+        const int rk = found + __popc(m & lt_mask);
+        if (hit && rk < want) list[nd.y + rk] = j;
+        found += __popc(m);
       }
-      found += __popc(m);
+      continue;
+    }
+    const int valid = (int)min((int64_t)kChunk, a.n - b0);
+    uint4 r4[kChunk / 128];
+#pragma unroll
+    for (int k = 0; k < kChunk / 128; ++k) {
+      const int j = k * 128 + 4 * lane;
+      if (j + 3 < valid) {
+        r4[k] = __ldg(reinterpret_cast<const uint4*>(rects + b0 + j));
+      } else {
+        r4[k].x = j < valid ? rects[b0 + j] : kEmptyRect;
+        r4[k].y = j + 1 < valid ? rects[b0 + j + 1] : kEmptyRect;
+        r4[k].z = j + 2 < valid ? rects[b0 + j + 2] : kEmptyRect;
+        r4[k].w = kEmptyRect;
+      }
+    }
+    int found = 0;
+#pragma unroll
+    for (int k = 0; k < kChunk / 128; ++k) {
+      if (found >= want) break;
+      const bool h0 = rect_has(r4[k].x, tx, ty), h1 = rect_has(r4[k].y, tx, ty);
+      const bool h2 = rect_has(r4[k].z, tx, ty), h3 = rect_has(r4[k].w, tx, ty);
+      const int cnt = (int)h0 + (int)h1 + (int)h2 + (int)h3;
+      int incl = cnt;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+      }
+      int rk = found + incl - cnt;
+      const int j = (int)b0 + k * 128 + 4 * lane;
+      if (h0) { if (rk < want) list[nd.y + rk] = j; ++rk; }
+      if (h1) { if (rk < want) list[nd.y + rk] = j + 1; ++rk; }
+      if (h2) { if (rk < want) list[nd.y + rk] = j + 2; ++rk; }
+      if (h3) { if (rk < want) list[nd.y + rk] = j + 3; }
+      found += __shfl_sync(0xffffffffu, incl, 31);
     }
   }
-  __syncthreads();
+  __syncwarp();
 
-  // 3. records of the selected Gaussians.
+  // 2. records of the listed Gaussians (slots lane and lane + 32)
+  Rec rec[2];
   bool nan_z = false;
-  if (tid < count && (s_list[tid] < 0 || (int64_t)s_list[tid] >= a.n)) {
-    // The chunk counts and the rectangles come from the same bin pass, so every
-    // slot below `count` is filled; this guard only keeps a corrupted
-    // workspace from turning into an out-of-range gather.
-    atomicOr(a.err, kDevErrListSlot);
-    s_list[tid] = 0;
-  }
-  if (tid < count) {
-    const int id = s_list[tid];
-    float cw[6];
-    load_cov6(a.cov + (size_t)id * a.cov_layout, a.cov_layout, cw);
-    const float* m = a.means + (size_t)id * 3;
-    Proj o;
-    project_gaussian(vc, m[0], m[1], m[2], cw, o);
-    Rec g;
-    if (!kShadowList) {
-      g.mx = o.c;
-      g.my = o.r;
-      g.cxx = o.cov_cc;
-      g.cxy = o.cov_rc;
-      g.cyy = o.cov_rr;
-      const float S = sh_scattering(vc, a.sh + (size_t)id * a.sh_stride, a.sh_k);
-      g.s_pos = fmaxf(0.0f, S);
-    } else {
-      g.mx = o.xr;
-      g.my = o.yr;
-      g.cxx = o.XX;
-      g.cxy = o.XY;
-      g.cyy = o.YY;
-      g.s_pos = 0.0f;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int slot = lane + 32 * h;
+    if (slot < count) {
+      int id = list[slot];
+      if (id < 0 || (int64_t)id >= a.n) {
+        // Every slot below `count` is filled (counts and rectangles come from
+        // the same bin pass); this guard only keeps a corrupted workspace from
+        // turning into an out-of-range gather.
+        atomicOr(a.err, kDevErrListSlot);
+        id = 0;
+        list[slot] = 0;
+      }
+      float cw[6];
+      load_cov6(a.cov + (size_t)id * a.cov_layout, a.cov_layout, cw);
+      const float* m = a.means + (size_t)id * 3;
+      Proj o;
+      project_gaussian(vc, m[0], m[1], m[2], cw, o);
+      Rec& g = rec[h];
+      if (!kShadowList) {
+        g.mx = o.c;
+        g.my = o.r;
+        g.cxx = o.cov_cc;
+        g.cxy = o.cov_rc;
+        g.cyy = o.cov_rr;
+        g.s_pos = fmaxf(0.0f, sh_scattering(vc, a.sh + (size_t)id * a.sh_stride, a.sh_k));
+      } else {
+        g.mx = o.xr;
+        g.my = o.yr;
+        g.cxx = o.XX;
+        g.cxy = o.XY;
+        g.cyy = o.YY;
+        g.s_pos = 0.0f;
+      }
+      rec_density_consts(g);
+      g.sigma = a.sigma[id];
+      g.z = o.zr;
+      g.yr = o.yr;
+      g.pos = slot;
+      s_z[warp][slot] = o.zr;
+      nan_z = nan_z || (o.zr != o.zr);
+      if (!kShadowList) {
+        float2* yz = reinterpret_cast<float2*>(st + a.st.L.yz);
+        yz[(size_t)t * kCap + slot] = make_float2(o.yr, o.zr);
+      }
     }
-    rec_density_consts(g);
-    g.sigma = a.sigma[id];
-    g.z = o.zr;
-    g.yr = o.yr;
-    g.pos = tid;
-    s_rec[tid] = g;
-    s_z[tid] = o.zr;
-    nan_z = (o.zr != o.zr);
-    if (!kShadowList) {
-      float2* yz = reinterpret_cast<float2*>(st + a.st.L.yz);
-      yz[(size_t)t * kCap + tid] = make_float2(o.yr, o.zr);
-    }
   }
+  __syncwarp();
 
-  // 4. rank by (Z_r, slot): equal to the reference's stable insertion sort on
+  // 3. rank by (Z_r, slot): equal to the reference's stable insertion sort on
   // Z_r with strict '>' (:795-807) whenever no Z_r is NaN; with a NaN the
   // insertion sort itself is replayed.
-  if (__syncthreads_or(nan_z)) {
-    if (tid == 0) {
+  int rank[2] = {0, 0};
+  const float* z = s_z[warp];
+  if (__any_sync(0xffffffffu, nan_z)) {
+    if (lane == 0) {
       int idx[kCap];
       float zv[kCap];
       for (int i = 0; i < count; ++i) {
         idx[i] = i;
-        zv[i] = s_z[i];
+        zv[i] = z[i];
       }
       for (int i = 1; i < count; ++i) {
         const int ti = idx[i];
@@ -626,25 +1015,31 @@ __global__ void __launch_bounds__(kSelectThreads) select_kernel(const SelectArgs
         idx[j + 1] = ti;
         zv[j + 1] = tz;
       }
-      for (int k = 0; k < count; ++k) s_rank[idx[k]] = k;
+      for (int k = 0; k < count; ++k) s_rank[warp][idx[k]] = k;
     }
-  } else if (tid < count) {
-    const float z = s_z[tid];
-    int rk = 0;
+    __syncwarp();
+    rank[0] = s_rank[warp][lane];
+    rank[1] = s_rank[warp][lane + 32];
+  } else {
+    const float z0 = lane < count ? z[lane] : 0.0f;
+    const float z1 = lane + 32 < count ? z[lane + 32] : 0.0f;
     for (int j = 0; j < count; ++j) {
-      const float zj = s_z[j];
-      rk += (zj < z) || (zj == z && j < tid);
+      const float zj = z[j];
+      rank[0] += (zj < z0) || (zj == z0 && j < lane);
+      rank[1] += (zj < z1) || (zj == z1 && j < lane + 32);
     }
-    s_rank[tid] = rk;
   }
-  __syncthreads();
 
-  // 5. state (the list length was written by scan_kernel)
-  if (tid < count) {
-    int* st_list = reinterpret_cast<int*>(st + a.st.L.list);
-    Rec* st_recs = reinterpret_cast<Rec*>(st + a.st.L.recs);
-    st_list[(size_t)t * kCap + tid] = s_list[tid];
-    st_recs[(size_t)t * kCap + s_rank[tid]] = s_rec[tid];
+  // 4. state (the list length was written by scan_kernel)
+  int* st_list = reinterpret_cast<int*>(st + a.st.L.list) + (size_t)t * kCap;
+  Rec* st_recs = reinterpret_cast<Rec*>(st + a.st.L.recs) + (size_t)t * kCap;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int slot = lane + 32 * h;
+    if (slot < count) {
+      st_list[slot] = list[slot];
+      st_recs[rank[h]] = rec[h];
+    }
   }
 }
 
@@ -1074,6 +1469,10 @@ static size_t bin_skip_smem_bytes(const Dims& d, int cov_layout, bool shadow) {
   return (size_t)(3 + cov_layout + 2) * kChunk * sizeof(float) + warp_count_bytes(d, shadow);
 }
 
+bool skip_bin_per_warp(const Dims& d, bool shadow) {
+  return warp_count_bytes(d, shadow) <= kWarpCountBytes;
+}
+
 template <bool kShadow>
 static void launch_bin_skip_t(const BinArgs& a, dim3 grid, size_t smem, cudaStream_t s) {
   if (needs_smem_attr(smem))
@@ -1098,7 +1497,7 @@ static void launch_bin_t(const BinArgs& a, dim3 grid, size_t smem, cudaStream_t 
 cudaError_t launch_bin(const BinArgs& a, const Dims& d, int chunks, bool shadow, bool skip,
                        cudaStream_t s) {
   const dim3 grid(chunks, (a.nviews + a.views_per_cta - 1) / a.views_per_cta);
-  if (skip && warp_count_bytes(d, shadow) <= kWarpCountBytes) {
+  if (skip && skip_bin_per_warp(d, shadow)) {
     const size_t smem = bin_skip_smem_bytes(d, a.cov_layout, shadow);
     if (shadow) launch_bin_skip_t<true>(a, grid, smem, s);
     else launch_bin_skip_t<false>(a, grid, smem, s);
@@ -1115,6 +1514,52 @@ cudaError_t launch_bin(const BinArgs& a, const Dims& d, int chunks, bool shadow,
   return cudaGetLastError();
 }
 
+// bin_cell_kernel: per-warp cell bitmaps, the chunk's cell ids, per-warp
+// tile counters (both lists counted when the shadow list is built).
+static size_t bin_cell_smem_bytes(const Dims& d, bool shadow) {
+  return (size_t)(kBinThreads / 32) * kCellWords * 4 + (size_t)kChunk * 4 +
+         warp_count_bytes(d, shadow);
+}
+
+bool bin_cell_supported(const Dims& d) { return warp_count_bytes(d, true) <= kWarpCountBytes; }
+
+template <bool kShadow>
+static void launch_bin_cell_t(const BinArgs& a, dim3 grid, size_t smem, cudaStream_t s) {
+  if (needs_smem_attr(smem))
+    cudaFuncSetAttribute(bin_cell_kernel<kShadow>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)smem);
+  bin_cell_kernel<kShadow><<<grid, kBinThreads, smem, s>>>(a);
+}
+
+cudaError_t launch_bin_cell(const BinArgs& a, const Dims& d, bool shadow, cudaStream_t s) {
+  const int vgroups = (a.nviews + kBinThreads / 32 - 1) / (kBinThreads / 32);
+  const dim3 grid((a.chunks + a.chunks_per_cta - 1) / a.chunks_per_cta, vgroups);
+  const size_t smem = bin_cell_smem_bytes(d, shadow);
+  if (shadow) launch_bin_cell_t<true>(a, grid, smem, s);
+  else launch_bin_cell_t<false>(a, grid, smem, s);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_cell_prep(const CellPrepArgs& a, cudaStream_t s) {
+  cell_init_kernel<<<(kMaxCells + 255) / 256, 256, 0, s>>>(a.grid, a.cell_hb);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  const int64_t blocks = min((int64_t)148 * 8, (a.n + 255) / 256);
+  scene_bounds_kernel<<<(unsigned)max((int64_t)1, blocks), 256, 0, s>>>(a.means, a.n, a.grid);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  scene_grid_kernel<<<1, 32, 0, s>>>(a.grid, a.n);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  cell_assign_kernel<<<(unsigned)((a.n + 255) / 256), 256, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_cell_test(const CellTestArgs& a, int nviews, cudaStream_t s) {
+  cell_test_kernel<<<dim3(kMaxCells / 256, nviews), 256, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_open_table(const OpenArgs& a, int nviews, int nlists, cudaStream_t s) {
   open_table_kernel<<<dim3(nviews, nlists), 256, 0, s>>>(a);
   return cudaGetLastError();
@@ -1127,7 +1572,7 @@ cudaError_t launch_scan(const ScanArgs& a, int nviews, cudaStream_t s) {
 
 cudaError_t launch_select(const SelectArgs& a, const Dims& d, int nviews, bool shadow_list,
                           cudaStream_t s) {
-  const dim3 grid(d.T, nviews);
+  const dim3 grid((d.T + kSelectThreads / 32 - 1) / (kSelectThreads / 32), nviews);
   if (shadow_list)
     select_kernel<true><<<grid, kSelectThreads, 0, s>>>(a);
   else

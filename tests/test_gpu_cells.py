@@ -1,0 +1,104 @@
+"""Cell culling of multi-view calls (8 views or more, N past the exactly
+binned prefix): the tile lists, images, Omega and gradients must equal those of
+single-view calls, which bin without cells and match the oracle bit for bit
+(test_gpu_parity). Lists and images are compared bitwise."""
+import numpy as np
+import pytest
+import torch
+
+from cuda_rasterizer import _native
+from cuda_rasterizer import cuda_rasterizer_sar as M
+from cuda_rasterizer import synthetic as S
+
+from _helpers import rel_linf
+
+pytestmark = pytest.mark.gpu
+
+
+def _a256(x):
+    return (x + 255) // 256 * 256
+
+
+def _state_lists(states, k, n, T, sbytes):
+    """(count [T], list [T,64]) of view k from a batch of per-view states."""
+    base = k * sbytes
+    o_count = _a256(4 * n)
+    o_list = o_count + _a256(4 * T)
+    count = states[base + o_count: base + o_count + 4 * T].view(torch.int32)
+    lst = states[base + o_list: base + o_list + 4 * T * 64].view(torch.int32).view(T, 64)
+    return count.cpu().numpy(), lst.cpu().numpy()
+
+
+def _check_batch_vs_single(sc, views, want_omega):
+    inputs = _native.prepare_inputs(sc["means"], sc["cov6"], sc["sigma"], sc["sh"])
+    means = inputs[0]
+    n = means.shape[0]
+    vs = [_native.make_view(*v) for v in views]
+    nr, na = views[0][8], views[0][9]
+    T = ((nr + 15) // 16) * ((na + 15) // 16)
+    sbytes = _native.state_bytes(n, nr, na)
+    V = len(vs)
+    states = torch.empty(V * sbytes, dtype=torch.uint8, device="cuda")
+    images = torch.empty((V, nr, na), dtype=torch.float32, device="cuda")
+    omega = torch.empty((V, n), dtype=torch.float32, device="cuda") if want_omega else None
+    _native.forward(vs, *inputs, images, omega=omega, states=states, check_device=True)
+    one_state = torch.empty(sbytes, dtype=torch.uint8, device="cuda")
+    one_img = torch.empty((1, nr, na), dtype=torch.float32, device="cuda")
+    one_om = torch.empty((1, n), dtype=torch.float32, device="cuda") if want_omega else None
+    for k, v in enumerate(vs):
+        _native.forward([v], *inputs, one_img, omega=one_om, states=one_state, check_device=True)
+        c1, l1 = _state_lists(one_state, 0, n, T, sbytes)
+        cb, lb = _state_lists(states, k, n, T, sbytes)
+        np.testing.assert_array_equal(cb, c1)
+        used = np.arange(64)[None, :] < c1[:, None]  # slots past the count are unspecified
+        np.testing.assert_array_equal(lb[used], l1[used])
+        assert torch.equal(images[k], one_img[0])
+        if want_omega:
+            assert torch.equal(omega[k], one_om[0])
+    return images
+
+
+@pytest.mark.parametrize("want_omega", [False, True])
+def test_cell_culling_lists_images_omega(want_omega):
+    sc = {k: v.cuda() for k, v in S.make_scene(200000, (40.0, 40.0, 10.0), (0.05, 0.5), seed=51).items()}
+    views = S.sweep_views(96)[::8]  # 12 views, incidence 15-45 deg
+    _check_batch_vs_single(sc, views, want_omega)
+
+
+def test_cell_culling_edge_cases():
+    """Non-finite centres, near-singular and very elongated covariances (no
+    cell), transmittances below 0.01, and a flat scene (zero z extent)."""
+    g = torch.Generator().manual_seed(52)
+    sc = S.make_scene(120000, (30.0, 30.0, 0.0), (0.02, 0.6), seed=53)
+    n = sc["means"].shape[0]
+    idx = torch.randperm(n, generator=g)
+    sc["means"][idx[:50]] = float("nan")
+    sc["means"][idx[50:60], 0] = float("inf")
+    k = 3000
+    s = torch.exp(torch.empty(k, 3).uniform_(-7.0, 1.0, generator=g))
+    q = torch.randn(k, 4, generator=g)
+    q = q / q.norm(dim=1, keepdim=True)
+    R = S.quat_to_rot(q.double())
+    cov = (R @ torch.diag_embed((s * s).double()) @ R.transpose(1, 2)).float()
+    sc["cov33"][idx[100:100 + k]] = cov
+    sc["cov6"][idx[100:100 + k]] = S.cov33_to_cov6(cov)
+    sc["sigma"][idx[5000:9000]] = 0.005
+    sc = {key: v.cuda() for key, v in sc.items()}
+    views = S.sweep_views(64, rho=0.15)[::7]  # 10 views
+    _check_batch_vs_single(sc, views, want_omega=True)
+
+
+def test_cell_culling_backward_equals_sum_of_single_views():
+    sc = {k: v.cuda() for k, v in S.make_scene(100000, (40.0, 40.0, 10.0), (0.05, 0.5), seed=54).items()}
+    views = S.sweep_views(80)[::8]  # 10 views
+    batch = M.render_sar_batched(sc["means"], sc["cov6"], sc["sigma"], sc["sh"], views)
+    for k, v in enumerate(views):
+        img, _ = M.render_sar(sc["means"], sc["cov6"], sc["sigma"], sc["sh"], *v)
+        assert torch.equal(batch[k], img)
+    gimg = torch.randn_like(batch)
+    grads = M.render_sar_backward_batched(sc["means"], sc["cov6"], sc["sigma"], sc["sh"], gimg, views)
+    single = [M.render_sar_backward(sc["means"], sc["cov6"], sc["sigma"], sc["sh"], gimg[k], *v)
+              for k, v in enumerate(views)]
+    for i in range(4):
+        total = sum(s[i] for s in single)
+        assert rel_linf(grads[i].cpu().numpy(), total.cpu().numpy()) <= 1e-5
