@@ -275,6 +275,10 @@ cudaError_t run_selection(const Dims& d, const Ws& w, int gv, const float* means
   ba.use_tma = aligned(means, 16) && aligned(cov, 16) && aligned(sigma, 16);
   ba.err = w.err;
   ba.nviews = gv;
+  const bool masks = segmask_supported(d);
+  ba.segmask = masks ? reinterpret_cast<uint32_t*>(w.view_area() + w.L.segmask_ipp) : nullptr;
+  ba.segmask_sh = masks ? reinterpret_cast<uint32_t*>(w.view_area() + w.L.segmask_sh) : nullptr;
+  ba.segmask_vstride = w.L.per_view / sizeof(uint32_t);
   ba.xcount = reinterpret_cast<int*>(w.view_area() + w.L.xcount);
   ba.xlist = reinterpret_cast<uint16_t*>(w.view_area() + w.L.xlist);
   ba.x_vstride = w.L.per_view;
@@ -383,6 +387,9 @@ cudaError_t run_selection(const Dims& d, const Ws& w, int gv, const float* means
   // the skipping binners record each chunk's exactly binned Gaussians, except
   // the CTA-wide variant for very large tile grids
   const bool xlists = prefix < d.C && (w.L.cells || skip_bin_per_warp(d, shr != nullptr));
+  sa.segmask = ba.segmask;
+  sa.segmask_vstride = ba.segmask_vstride;
+  sa.segmask_to = prefix;
   sa.xlist_from = xlists ? prefix : INT32_MAX;
   sa.xcount = xlists ? ba.xcount : nullptr;
   sa.xlist = xlists ? ba.xlist : nullptr;
@@ -398,6 +405,7 @@ cudaError_t run_selection(const Dims& d, const Ws& w, int gv, const float* means
   e = run_kernel(kKindScan, s, [&] { return launch_scan(sc, gv, s); });
   if (e != cudaSuccess) return e;
   sa.st = *shr;
+  sa.segmask = ba.segmask_sh;
   sa.need = sc.need;
   sa.need_n = sc.need_n;
   e = run_kernel(kKindSelectShadow, s, [&] { return launch_select(sa, d, gv, true, s); });

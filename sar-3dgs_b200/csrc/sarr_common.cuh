@@ -30,6 +30,7 @@ constexpr int kSelectThreads = 256;
 constexpr int kScanThreads = 512;
 constexpr int kPrefixChunks = 32;                // chunks binned exactly before saturation skipping
 constexpr int kXCap = 256;                       // exactly binned Gaussians listed per skipped chunk
+constexpr int kSegMaskMaxTiles = 2048;           // prefix-chunk segment masks up to this many tiles
 constexpr int kWarpsPerTile = 8;                 // 8 warps x 32 pixels = one 16x16 tile
 constexpr int kMaxTilesAxis = 128;               // images up to 2048 x 2048
 constexpr int kMaxViewsPerLaunch = 32;

@@ -63,7 +63,8 @@ __host__ __device__ inline StateLayout state_layout(int64_t n, int T) {
 struct WsLayout {
   size_t viewconst, err, scene, hb, cid, cell_hb, head;
   size_t counts_ipp, counts_sh, need_ipp, need_sh, need_n_ipp, need_n_sh, open_ipp, open_sh;
-  size_t bits, xcount, xlist, state_ipp, state_sh, partial_om, partial_bwd, per_view;
+  size_t bits, xcount, xlist, segmask_ipp, segmask_sh, state_ipp, state_sh, partial_om, partial_bwd,
+      per_view;
   bool cells;
   StateLayout st;
 };
@@ -113,6 +114,12 @@ __host__ inline WsLayout ws_layout(const Dims& d, bool cells) {
   // Per chunk after the prefix: how many of its Gaussians the skipping binner
   // binned exactly (-1: more than kXCap, or not recorded) and their chunk
   // offsets in index order; select_kernel scans only those.
+  // Per prefix chunk and tile: which 32-Gaussian segments of the chunk hold
+  // hits of the tile (select_kernel reads only those).
+  L.segmask_ipp = o;
+  o += align256((size_t)kPrefixChunks * d.T * 4);
+  L.segmask_sh = o;
+  o += align256((size_t)kPrefixChunks * d.T * 4);
   L.xcount = o;
   o += align256((size_t)d.C * 4);
   L.xlist = o;
@@ -149,6 +156,9 @@ struct BinArgs {
   const int* open_ipp;  // open-tile summed-area tables (skip variant), open_vstride ints per view
   const int* open_sh;
   size_t open_vstride;
+  uint32_t* segmask;     // prefix variant: segment masks [chunk][T] (null: none)
+  uint32_t* segmask_sh;
+  size_t segmask_vstride;  // words per view
   int* xcount;         // exactly binned Gaussians per chunk (skip variants)
   uint16_t* xlist;     // [C][kXCap] their chunk offsets
   size_t x_vstride;    // bytes per view of both
@@ -214,6 +224,9 @@ struct SelectArgs {
   size_t need_vstride;        // bytes
   const int* need_n;          // [T] per view
   size_t need_n_vstride;      // ints
+  const uint32_t* segmask;    // segment masks of chunks < segmask_to (null: none)
+  size_t segmask_vstride;     // words
+  int segmask_to;
   int xlist_from;             // first chunk with an exact list (INT32_MAX: none)
   const int* xcount;
   const uint16_t* xlist;
@@ -315,6 +328,7 @@ bool bin_cell_supported(const Dims& d);
 // true when the skipping binner keeps per-warp counters (and records the
 // exact lists); false selects its CTA-wide variant
 bool skip_bin_per_warp(const Dims& d, bool shadow);
+bool segmask_supported(const Dims& d);
 cudaError_t launch_scan(const ScanArgs& a, int nviews, cudaStream_t s);
 cudaError_t launch_select(const SelectArgs& a, const Dims& d, int nviews, bool shadow_list,
                           cudaStream_t s);

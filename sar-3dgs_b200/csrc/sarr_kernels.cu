@@ -5,19 +5,27 @@
 // compute_omega_kernel, the host Omega average and render_kernel of
 // cuda_rasterizer/rasterizer_impl_v2.cu:322-839, :1239-1252):
 //
-//   bin_kernel       one CTA per chunk of 512 Gaussians: TMA bulk copy of the
-//                    chunk's means/cov/sigma into shared memory, projection,
-//                    validity, pixel bbox -> tile rectangle (4 bytes per list),
-//                    and a per-chunk per-tile hit count built with a 2-D
-//                    difference array (4 shared atomics per Gaussian however
-//                    many tiles it covers).
-//   select_kernel    one CTA per tile: scan of the chunk counts, then each
-//                    needed chunk is re-scanned with warp ballots so that the
-//                    first 64 hits in index order land in their slots; the
-//                    selected Gaussians are projected again (SH only for them),
-//                    ranked by (Z_r, index) and stored as 48-byte records.
-//   render_kernel    one warp per 2 tile columns: TMA bulk copy of the tile's
-//                    sorted records, front-to-back compositing.
+//   bin_kernel       the first kPrefixChunks chunks of 1024 Gaussians, exactly:
+//                    TMA bulk copy of a chunk's means/cov/sigma into shared
+//                    memory, projection, validity, pixel bbox -> tile rectangle
+//                    (4 bytes per list), and a per-chunk per-tile hit count
+//                    built with a 2-D difference array.
+//   open_table_kernel  summed-area table of the tiles that the prefix left with
+//                    fewer than 64 hits (still open).
+//   bin_skip_kernel / bin_cell_kernel
+//                    the remaining chunks: Gaussians that can only reach full
+//                    tiles get an empty rectangle after a conservative test
+//                    (bin_cell_kernel first rejects whole cells of a
+//                    view-independent grid); the rest are binned exactly, one
+//                    view per warp, and listed per chunk.
+//   scan_kernel      per tile, the chunks holding its first 64 hits.
+//   select_kernel    one warp per tile: the hits of those chunks in index
+//                    order (warp ballots), the selected Gaussians projected
+//                    again (SH only for them), ranked by (Z_r, index) and
+//                    stored as 48-byte records.
+//   render_kernel    one CTA per tile: TMA bulk copy of its sorted records,
+//                    front-to-back compositing by 8 x 4 pixel warp blocks that
+//                    skip records whose density is 0 on the whole block.
 //   omega_tile_kernel / omega_scatter_kernel
 //                    per-pixel Omega walk with per-slot warp reductions, then
 //                    a per-Gaussian gather of those partial sums.
@@ -69,6 +77,14 @@ __device__ __forceinline__ int open_in_rect(uint32_t rc, const int* __restrict__
   const int tc0 = rc & 0xFF, tc1 = ((rc >> 8) & 0xFF) + 1, tr0 = (rc >> 16) & 0xFF, tr1 = (rc >> 24) + 1;
   return __ldg(tab + tr1 * pitch + tc1) - __ldg(tab + tr0 * pitch + tc1) -
          __ldg(tab + tr1 * pitch + tc0) + __ldg(tab + tr0 * pitch + tc0);
+}
+
+// ORs `bit` into the mask of every tile of a rectangle.
+__device__ __forceinline__ void mark_rect(uint32_t* mask, uint32_t rc, int tiles_x, uint32_t bit) {
+  if (rc == kEmptyRect) return;
+  const int tc0 = rc & 0xFF, tc1 = (rc >> 8) & 0xFF, tr0 = (rc >> 16) & 0xFF, tr1 = rc >> 24;
+  for (int ty = tr0; ty <= tr1; ++ty)
+    for (int tx = tc0; tx <= tc1; ++tx) atomicOr(mask + ty * tiles_x + tx, bit);
 }
 
 // Tile rectangle of the pixel box centred on (cr, cc) with half-width h,
@@ -156,6 +172,11 @@ __global__ void __launch_bounds__(kBinThreads) bin_kernel(const BinArgs a) {
   const int pitch = tiles_x + 1;
   const int T1 = (tiles_y + 1) * pitch;
   int* s_diff_sh = s_diff_ipp + T1;
+  // segment masks (exact variant, when a.segmask is set): bit s of tile t is
+  // set when Gaussians [32 s, 32 s + 32) of the chunk hold a hit of t
+  const bool masks = !kSkip && a.segmask != nullptr;
+  uint32_t* s_mask_ipp = reinterpret_cast<uint32_t*>(s_diff_ipp + T1 * (kShadow ? 2 : 1));
+  uint32_t* s_mask_sh = s_mask_ipp + T;
 
   const int64_t base = (int64_t)chunk * kChunk;
   const int gcount = (int)min((int64_t)kChunk, a.n - base);
@@ -179,6 +200,8 @@ __global__ void __launch_bounds__(kBinThreads) bin_kernel(const BinArgs a) {
     const ViewConst& vc = a.views[v];
     const int Nr = vc.h.Nr, Na = vc.h.Na;
     for (int i = tid; i < T1 * (kShadow ? 2 : 1); i += kBinThreads) s_diff_ipp[i] = 0;
+    if (masks)
+      for (int i = tid; i < T * (kShadow ? 2 : 1); i += kBinThreads) s_mask_ipp[i] = 0;
     if (kSkip && tid == 0) s_qn = 0;
     __syncthreads();
 
@@ -243,9 +266,11 @@ __global__ void __launch_bounds__(kBinThreads) bin_kernel(const BinArgs a) {
             bin_exact<kShadow>(vcl, s_means, s_cov, cs, j, rc_ipp, rc_sh);
           rects_ipp[base + j] = rc_ipp;
           diff_add(s_diff_ipp, pitch, rc_ipp);
+          if (masks) mark_rect(s_mask_ipp, rc_ipp, tiles_x, 1u << (j >> 5));
           if (kShadow) {
             rects_sh[base + j] = rc_sh;
             diff_add(s_diff_sh, pitch, rc_sh);
+            if (masks) mark_rect(s_mask_sh, rc_sh, tiles_x, 1u << (j >> 5));
           }
         }
       }
@@ -289,6 +314,14 @@ __global__ void __launch_bounds__(kBinThreads) bin_kernel(const BinArgs a) {
       const int y = t / tiles_x, x = t - y * tiles_x;
       cnt_ipp[t] = (uint8_t)min(s_diff_ipp[y * pitch + x], 255);
       if (kShadow) cnt_sh[t] = (uint8_t)min(s_diff_sh[y * pitch + x], 255);
+    }
+    if (masks) {
+      uint32_t* m = a.segmask + v * a.segmask_vstride + (size_t)chunk * T;
+      for (int t = tid; t < T; t += kBinThreads) m[t] = s_mask_ipp[t];
+      if (kShadow) {
+        uint32_t* msh = a.segmask_sh + v * a.segmask_vstride + (size_t)chunk * T;
+        for (int t = tid; t < T; t += kBinThreads) msh[t] = s_mask_sh[t];
+      }
     }
     __syncthreads();  // the difference arrays and the queue are reused by the next view
   }
@@ -901,6 +934,34 @@ __global__ void __launch_bounds__(kSelectThreads) select_kernel(const SelectArgs
       continue;
     }
     const int valid = (int)min((int64_t)kChunk, a.n - b0);
+    if (a.segmask && nd.x < a.segmask_to) {
+      // only the 32-Gaussian segments that hold hits of the tile, four at a time
+      uint32_t segs = a.segmask[v * a.segmask_vstride + (size_t)nd.x * T + t];
+      int found = 0;
+      while (segs && found < want) {
+        int sj[4];
+        uint32_t rc[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          sj[u] = -1;
+          if (segs) {
+            sj[u] = (__ffs(segs) - 1) * 32 + lane;
+            segs &= segs - 1;
+          }
+          rc[u] = (sj[u] >= 0 && sj[u] < valid) ? rects[b0 + sj[u]] : kEmptyRect;
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          if (found >= want) break;
+          const bool hit = rect_has(rc[u], tx, ty);
+          const unsigned m = __ballot_sync(0xffffffffu, hit);
+          const int rk = found + __popc(m & lt_mask);
+          if (hit && rk < want) list[nd.y + rk] = (int)b0 + sj[u];
+          found += __popc(m);
+        }
+      }
+      continue;
+    }
     uint4 r4[kChunk / 128];
 #pragma unroll
     for (int k = 0; k < kChunk / 128; ++k) {
@@ -1061,29 +1122,58 @@ __device__ __forceinline__ bool load_tile_recs(Rec* s_rec, uint64_t* bar, const 
   return mbar_wait_bounded(bar, 0, err);
 }
 
-__global__ void __launch_bounds__(32) render_kernel(const TileArgs a) {
+// Half-widths (columns, rows) of the box outside which rec_density's exponent
+// is below -20 for this record, so that it returns 0 there. The exponent is
+// -q / (2 det) with q = cxx dy^2 + cyy dx^2 - 2 cxy dx dy, and q <= 40 det
+// implies |dx| <= sqrt(40 cxx), |dy| <= sqrt(40 cyy). The box is taken for
+// 40.8 det (2 % on q) plus 0.01 px: for correlations |cxy| / sqrt(cxx cyy)
+// <= 0.999 the float evaluation of q and det is within 0.04 % of exact, so
+// the computed exponent stays below -20.39 outside it. Other records: no box
+// (density 0 everywhere when |det| < EPSILON; unbounded otherwise).
+__device__ __forceinline__ float2 density_extent(const Rec& g) {
+  if (g.norm < 0.0f) return make_float2(-1.0f, -1.0f);
+  const float cxx = g.cxx, cyy = g.cyy, cxy = g.cxy;
+  const bool bounded = cxx > 0.0f && cyy > 0.0f && cxx < 1e30f && cyy < 1e30f && g.inv_det > 0.0f &&
+                       cxy * cxy <= 0.998f * (cxx * cyy);
+  if (!bounded) return make_float2(INFINITY, INFINITY);
+  return make_float2(sqrtf(40.8f * cxx) + 0.01f, sqrtf(40.8f * cyy) + 0.01f);
+}
+
+// One CTA per tile: the tile's sorted records arrive with one TMA bulk copy;
+// warp w composites an 8 (range) x 4 (azimuth) pixel block, lanes along range
+// (contiguous in the image). A record whose density box misses the whole
+// block is skipped by the warp: every pixel of the block would evaluate its
+// density to 0 (< 1e-8) and skip it too.
+__global__ void __launch_bounds__(kWarpsPerTile * 32) render_kernel(const TileArgs a) {
   __shared__ __align__(16) Rec s_rec[kCap];
+  __shared__ float2 s_ext[kCap];
   __shared__ uint64_t bar;
-  const int v = blockIdx.y;
-  const int t = blockIdx.x / kWarpsPerTile, slab = blockIdx.x % kWarpsPerTile;
-  const int lane = threadIdx.x;
+  const int v = blockIdx.y, t = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const ViewConst& vc = a.views[v];
   const int Nr = vc.h.Nr, Na = vc.h.Na, tiles_x = vc.tiles_x;
   const int tx = t % tiles_x, ty = t / tiles_x;
-  const int pc = tx * kTile + slab * 2 + (lane >> 4);
-  const int pr = ty * kTile + (lane & 15);
+  const int r0 = ty * kTile + (warp & 1) * 8, c0 = tx * kTile + (warp >> 1) * 4;
+  const int pr = r0 + (lane & 7), pc = c0 + (lane >> 3);
   const bool in = pc < Na && pr < Nr;
   const unsigned char* st = a.st.base + v * a.st.vstride;
   const int count = reinterpret_cast<const int*>(st + a.st.L.count)[t];
 
   float pixel_value = 0.0f;
   if (count > 0) {
-    const bool ok = load_tile_recs(s_rec, &bar, st, a.st.L, t, count, a.err, false);
-    if (__all_sync(0xffffffffu, ok)) {
+    const bool ok = load_tile_recs(s_rec, &bar, st, a.st.L, t, count, a.err, true);
+    if (ok)
+      for (int k = tid; k < count; k += kWarpsPerTile * 32) s_ext[k] = density_extent(s_rec[k]);
+    if (__syncthreads_and(ok)) {
       float transmittance_acc = 1.0f;
       const float fx = (float)pc, fy = (float)pr;
+      const float bx0 = (float)c0, bx1 = (float)(c0 + 3), by0 = (float)r0, by1 = (float)(r0 + 7);
       for (int k = 0; k < count; ++k) {
         const Rec& g = s_rec[k];
+        const float2 e = s_ext[k];
+        const float mdx = fmaxf(0.0f, fmaxf(bx0 - g.mx, g.mx - bx1));
+        const float mdy = fmaxf(0.0f, fmaxf(by0 - g.my, g.my - by1));
+        if (mdx > e.x || mdy > e.y) continue;  // the same for every lane
         const float gamma_ipp = rec_density(g, fx, fy);
         if (gamma_ipp < 1e-8f) continue;
         const float alpha_i = mul_(g.sigma, gamma_ipp);
@@ -1453,10 +1543,15 @@ __global__ void debug_view_kernel(const ViewHost vh, float* __restrict__ out) {
 // same 48 KB.
 static bool needs_smem_attr(size_t dynamic_smem) { return dynamic_smem + 4096 > 48 * 1024; }
 
-static size_t bin_smem_bytes(const Dims& d, int cov_layout, bool shadow) {
+// Segment masks of the prefix chunks are kept for tile grids up to
+// kSegMaskMaxTiles tiles.
+bool segmask_supported(const Dims& d) { return d.T <= kSegMaskMaxTiles; }
+
+static size_t bin_smem_bytes(const Dims& d, int cov_layout, bool shadow, bool masks) {
   const size_t stage = (size_t)(3 + cov_layout + 1) * kChunk * sizeof(float);
   const size_t T1 = (size_t)(d.tiles_y + 1) * (d.tiles_x + 1);
-  return stage + T1 * sizeof(int) * (shadow ? 2 : 1);
+  return stage + T1 * sizeof(int) * (shadow ? 2 : 1) +
+         (masks ? (size_t)d.T * 4 * (shadow ? 2 : 1) : 0);
 }
 
 // Per-warp tile counters of bin_skip_kernel; grids whose counters would not
@@ -1503,7 +1598,7 @@ cudaError_t launch_bin(const BinArgs& a, const Dims& d, int chunks, bool shadow,
     else launch_bin_skip_t<false>(a, grid, smem, s);
     return cudaGetLastError();
   }
-  const size_t smem = bin_smem_bytes(d, a.cov_layout, shadow);
+  const size_t smem = bin_smem_bytes(d, a.cov_layout, shadow, !skip && a.segmask != nullptr);
   if (shadow) {
     if (skip) launch_bin_t<true, true>(a, grid, smem, s);
     else launch_bin_t<true, false>(a, grid, smem, s);
@@ -1581,7 +1676,7 @@ cudaError_t launch_select(const SelectArgs& a, const Dims& d, int nviews, bool s
 }
 
 cudaError_t launch_render(const TileArgs& a, const Dims& d, int nviews, cudaStream_t s) {
-  render_kernel<<<dim3(d.T * kWarpsPerTile, nviews), 32, 0, s>>>(a);
+  render_kernel<<<dim3(d.T, nviews), kWarpsPerTile * 32, 0, s>>>(a);
   return cudaGetLastError();
 }
 
