@@ -46,7 +46,11 @@ __global__ void view_setup_kernel(const ViewHostPack pack, ViewConst* __restrict
   const int v = threadIdx.x;
   if (v >= pack.n) return;
   ViewConst c;
-  c.h = pack.v[v];
+  // static indices into the parameter block (a dynamic one would copy the
+  // whole block to local memory in every thread)
+#pragma unroll
+  for (int i = 0; i < kMaxViewsPerLaunch; ++i)
+    if (i == v) c.h = pack.v[i];
   c.cos_a = cosf(c.h.alpha);
   c.sin_a = sinf(c.h.alpha);
   c.cos_b = cosf(c.h.beta);
@@ -789,33 +793,65 @@ __global__ void __launch_bounds__(kBinThreads, 3) bin_cell_kernel(const BinArgs 
 // Open-tile summed-area table of one list of one view (grid: views x lists).
 // A tile is open while the first `prefix_chunks` chunk rows hold fewer than 64
 // of its hits; entry [y][x] of the table counts the open tiles (ty, tx) with
-// ty < y and tx < x.
+// ty < y and tx < x. Built in shared memory with warp scans when it fits
+// (kOpenSmemInts), in global memory otherwise.
+constexpr int kOpenSmemInts = 8192;
+
+__device__ __forceinline__ int warp_incl_scan(int x, int lane) {
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  return x;
+}
+
 __global__ void __launch_bounds__(256) open_table_kernel(const OpenArgs a) {
+  __shared__ int s_tab[kOpenSmemInts];
   const int v = blockIdx.x, list = blockIdx.y;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int tiles_x = a.tiles_x, tiles_y = a.tiles_y, T = tiles_x * tiles_y, pitch = tiles_x + 1;
+  const int size = (tiles_y + 1) * pitch;
   const uint8_t* counts = (list ? a.counts[1] : a.counts[0]) + v * a.counts_vstride;
-  int* tab = (list ? a.table[1] : a.table[0]) + v * a.table_vstride;
-  for (int x = threadIdx.x; x < pitch; x += 256) tab[x] = 0;
-  for (int y = threadIdx.x; y < tiles_y; y += 256) tab[(y + 1) * pitch] = 0;
-  for (int t = threadIdx.x; t < T; t += 256) {
+  int* out = (list ? a.table[1] : a.table[0]) + v * a.table_vstride;
+  int* tab = size <= kOpenSmemInts ? s_tab : out;
+  for (int x = tid; x < pitch; x += 256) tab[x] = 0;
+  for (int y = tid; y < tiles_y; y += 256) tab[(y + 1) * pitch] = 0;
+  for (int t = tid; t < T; t += 256) {
     int sum = 0;
     for (int c = 0; c < a.prefix_chunks && sum < kCap; ++c) sum += counts[(size_t)c * T + t];
     const int y = t / tiles_x, x = t - y * tiles_x;
     tab[(y + 1) * pitch + x + 1] = sum < kCap ? 1 : 0;
   }
   __syncthreads();
-  for (int y = threadIdx.x; y < tiles_y; y += 256) {
-    int* row = tab + (y + 1) * pitch;
-    int run = 0;
-    for (int x = 1; x <= tiles_x; ++x) row[x] = (run += row[x]);
+  // rows: one warp per row, 32 columns per step
+  for (int y = warp; y < tiles_y; y += 8) {
+    int* row = tab + (y + 1) * pitch + 1;
+    int carry = 0;
+    for (int x0 = 0; x0 < tiles_x; x0 += 32) {
+      const int x = x0 + lane;
+      const int val = x < tiles_x ? row[x] : 0;
+      const int incl = warp_incl_scan(val, lane) + carry;
+      if (x < tiles_x) row[x] = incl;
+      carry = __shfl_sync(0xffffffffu, incl, 31);
+    }
   }
   __syncthreads();
-  for (int x = threadIdx.x; x < tiles_x; x += 256) {
-    int run = 0;
-    for (int y = 1; y <= tiles_y; ++y) {
-      int* e = tab + y * pitch + x + 1;
-      *e = (run += *e);
+  // columns: one warp per column
+  for (int x = warp; x < tiles_x; x += 8) {
+    int carry = 0;
+    for (int y0 = 0; y0 < tiles_y; y0 += 32) {
+      const int y = y0 + lane;
+      int* e = tab + (y + 1) * pitch + x + 1;
+      const int val = y < tiles_y ? *e : 0;
+      const int incl = warp_incl_scan(val, lane) + carry;
+      if (y < tiles_y) *e = incl;
+      carry = __shfl_sync(0xffffffffu, incl, 31);
     }
+  }
+  if (tab == s_tab) {
+    __syncthreads();
+    for (int i = tid; i < size; i += 256) out[i] = s_tab[i];
   }
 }
 
