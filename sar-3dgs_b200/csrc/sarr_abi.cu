@@ -250,6 +250,12 @@ cudaError_t run_cell_prep(const Dims& d, const Ws& w, const float* means, const 
   cp.hb = reinterpret_cast<float*>(w.base + w.L.hb);
   cp.cid = reinterpret_cast<uint32_t*>(w.base + w.L.cid);
   cp.cell_hb = reinterpret_cast<int*>(w.base + w.L.cell_hb);
+  cp.pstart = (int64_t)kPrefixChunks * kChunk;
+  cp.cell_count = reinterpret_cast<int*>(w.base + w.L.cell_count);
+  cp.cell_start = reinterpret_cast<int*>(w.base + w.L.cell_start);
+  cp.mem_pos = reinterpret_cast<float4*>(w.base + w.L.mem_pos);
+  cp.mem_idx = reinterpret_cast<int*>(w.base + w.L.mem_idx);
+  cp.always = reinterpret_cast<int*>(w.base + w.L.always);
   return run_kernel(kKindAux, s, [&] { return launch_cell_prep(cp, s); });
 }
 
@@ -330,19 +336,21 @@ cudaError_t run_selection(const Dims& d, const Ws& w, int gv, const float* means
       ct.shadow = shr != nullptr;
       ct.bits = reinterpret_cast<uint32_t*>(w.view_area() + w.L.bits);
       ct.bits_vstride = w.L.per_view / sizeof(uint32_t);
+      ct.xbits = reinterpret_cast<uint32_t*>(w.view_area() + w.L.xbits);
+      ct.xbits_vstride = w.L.per_view / sizeof(uint32_t);
+      ct.xbits_words = d.C * 32;
       e = run_kernel(kKindAux, s, [&] { return launch_cell_test(ct, gv, s); });
       if (e != cudaSuccess) return e;
       ba.chunks = d.C - prefix;
-      // ~4 waves of 3 CTAs per SM over (chunks x view groups of 8), at least
-      // 2 chunks per CTA so that the per-warp cell bitmap load is amortised
-      const int vgroups = (gv + 7) / 8;
-      const int64_t units = (int64_t)ba.chunks * vgroups;
-      int cpc = (int)((units + 148 * 3 * 4 - 1) / (148 * 3 * 4));
-      ba.chunks_per_cta = cpc < 2 ? 2 : cpc;
-      ba.hb = reinterpret_cast<const float*>(w.base + w.L.hb);
-      ba.cid = reinterpret_cast<const uint32_t*>(w.base + w.L.cid);
+      ba.grid = ct.grid;
+      ba.cell_start = reinterpret_cast<const int*>(w.base + w.L.cell_start);
+      ba.mem_pos = reinterpret_cast<const float4*>(w.base + w.L.mem_pos);
+      ba.mem_idx = reinterpret_cast<const int*>(w.base + w.L.mem_idx);
+      ba.always = reinterpret_cast<const int*>(w.base + w.L.always);
       ba.bits = ct.bits;
       ba.bits_vstride = ct.bits_vstride;
+      ba.xbits = ct.xbits;
+      ba.xbits_vstride = ct.xbits_vstride;
       e = run_kernel(kKindBinSkip, s, [&] { return launch_bin_cell(ba, d, shr != nullptr, s); });
       if (e != cudaSuccess) return e;
     } else {

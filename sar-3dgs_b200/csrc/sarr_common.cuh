@@ -29,7 +29,7 @@ constexpr int kChunk = kBinThreads * kBinPerThread;  // Gaussians per count row
 constexpr int kSelectThreads = 256;
 constexpr int kScanThreads = 512;
 constexpr int kPrefixChunks = 32;                // chunks binned exactly before saturation skipping
-constexpr int kXCap = 256;                       // exactly binned Gaussians listed per skipped chunk
+constexpr int kXCap = kChunk;                    // exactly binned Gaussians listed per skipped chunk
 constexpr int kSegMaskMaxTiles = 2048;           // prefix-chunk segment masks up to this many tiles
 constexpr int kWarpsPerTile = 8;                 // 8 warps x 32 pixels = one 16x16 tile
 constexpr int kMaxTilesAxis = 128;               // images up to 2048 x 2048
@@ -55,6 +55,7 @@ struct SceneGrid {
   int ncells;
   float half_diag;           // bound on |member centre - cell centre| [m], with margins
   int valid;                 // 0: no finite centre (no Gaussian is in a cell)
+  int n_always;              // Gaussians after the prefix that are in no cell
 };
 
 // Order-preserving map of floats to ints (for atomicMin / atomicMax).
@@ -498,6 +499,16 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
     }
   }
   return true;
+}
+
+// Inclusive prefix sum over the lanes of a full warp.
+__device__ __forceinline__ int warp_incl_scan(int x, int lane) {
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  return x;
 }
 
 __device__ __forceinline__ float warp_sum(float x) {

@@ -58,13 +58,17 @@ __host__ __device__ inline StateLayout state_layout(int64_t n, int T) {
 //   state), state_sh, partial_om [T][64] float2, partial_bwd [T][64][8] float.
 // With cells (multi-view calls, see kCellMinViews) the head also holds the
 // SceneGrid, per-Gaussian bbox bounds hb [n] f32 and cell ids cid [n] u32, the
-// per-cell largest bound cell_hb [kMaxCells] (ordered-int keys), and each view
-// area its cell bitmap bits [kCellWords] u32.
+// per-cell largest bound cell_hb [kMaxCells] (ordered-int keys), the cells'
+// member lists (Gaussians after the prefix, cell by cell: cell_start
+// [kMaxCells + 1], mem_pos [n] float4 = centre and bound, mem_idx [n]), the
+// Gaussians after the prefix that are in no cell (always [n]), and each view
+// area its cell bitmap bits [kCellWords] u32 and its exactly-binned bitmap
+// xbits [C][32] u32.
 struct WsLayout {
-  size_t viewconst, err, scene, hb, cid, cell_hb, head;
+  size_t viewconst, err, scene, hb, cid, cell_hb, cell_count, cell_start, mem_pos, mem_idx, always, head;
   size_t counts_ipp, counts_sh, need_ipp, need_sh, need_n_ipp, need_n_sh, open_ipp, open_sh;
-  size_t bits, xcount, xlist, segmask_ipp, segmask_sh, state_ipp, state_sh, partial_om, partial_bwd,
-      per_view;
+  size_t bits, xbits, xcount, xlist, segmask_ipp, segmask_sh, state_ipp, state_sh, partial_om,
+      partial_bwd, per_view;
   bool cells;
   StateLayout st;
 };
@@ -81,7 +85,8 @@ __host__ inline WsLayout ws_layout(const Dims& d, bool cells) {
   L.viewconst = 0;
   L.err = align256(sizeof(ViewConst) * kMaxViewsPerLaunch);
   size_t h = L.err + 256;
-  L.scene = L.hb = L.cid = L.cell_hb = 0;
+  L.scene = L.hb = L.cid = L.cell_hb = L.cell_count = L.cell_start = 0;
+  L.mem_pos = L.mem_idx = L.always = 0;
   if (cells) {
     L.scene = h;
     h += align256(sizeof(SceneGrid));
@@ -91,6 +96,16 @@ __host__ inline WsLayout ws_layout(const Dims& d, bool cells) {
     h += align256((size_t)d.n * 4);
     L.cell_hb = h;
     h += align256((size_t)kMaxCells * 4);
+    L.cell_count = h;
+    h += align256((size_t)kMaxCells * 4);
+    L.cell_start = h;
+    h += align256((size_t)(kMaxCells + 1) * 4);
+    L.mem_pos = h;
+    h += align256((size_t)d.n * 16);
+    L.mem_idx = h;
+    h += align256((size_t)d.n * 4);
+    L.always = h;
+    h += align256((size_t)d.n * 4);
   }
   L.head = h;
   L.st = state_layout(d.n, d.T);
@@ -125,9 +140,12 @@ __host__ inline WsLayout ws_layout(const Dims& d, bool cells) {
   L.xlist = o;
   o += align256((size_t)d.C * kXCap * 2);
   L.bits = 0;
+  L.xbits = 0;
   if (cells) {
     L.bits = o;
     o += align256((size_t)kCellWords * 4);
+    L.xbits = o;
+    o += align256((size_t)d.C * 32 * 4);
   }
   L.state_ipp = o;
   o += L.st.bytes;
@@ -163,12 +181,16 @@ struct BinArgs {
   uint16_t* xlist;     // [C][kXCap] their chunk offsets
   size_t x_vstride;    // bytes per view of both
   // cell variant
-  int chunks;          // chunks of the launch
-  int chunks_per_cta;
-  const float* hb;     // [n] view-independent bbox bounds
-  const uint32_t* cid; // [n] cell ids
+  int chunks;          // chunks after the prefix
+  const SceneGrid* grid;
+  const int* cell_start;
+  const float4* mem_pos;
+  const int* mem_idx;
+  const int* always;
   const uint32_t* bits;  // cell bitmaps, bits_vstride words per view
   size_t bits_vstride;
+  uint32_t* xbits;       // exactly-binned bitmaps [C][32] per view
+  size_t xbits_vstride;  // words
   int64_t n;
   int C;
   const float* means;
@@ -186,6 +208,7 @@ struct BinArgs {
 
 struct CellPrepArgs {
   int64_t n;
+  int64_t pstart;  // first Gaussian after the exactly binned prefix
   const float* means;
   const float* cov;
   int cov_layout;
@@ -194,6 +217,11 @@ struct CellPrepArgs {
   float* hb;
   uint32_t* cid;
   int* cell_hb;
+  int* cell_count;
+  int* cell_start;
+  float4* mem_pos;
+  int* mem_idx;
+  int* always;
 };
 
 struct CellTestArgs {
@@ -206,6 +234,9 @@ struct CellTestArgs {
   int shadow;
   uint32_t* bits;
   size_t bits_vstride;
+  uint32_t* xbits;       // exactly-binned bitmaps to clear, xbits_words per view
+  size_t xbits_vstride;  // words
+  int xbits_words;
 };
 
 struct SelectArgs {
@@ -322,7 +353,8 @@ cudaError_t launch_open_table(const OpenArgs& a, int nviews, int nlists, cudaStr
 // view-independent cell grid of one call (four kernels)
 cudaError_t launch_cell_prep(const CellPrepArgs& a, cudaStream_t s);
 cudaError_t launch_cell_test(const CellTestArgs& a, int nviews, cudaStream_t s);
-// bin_cell_kernel over the a.chunks chunks from a.chunk_offset
+// cell binning of the a.chunks chunks from a.chunk_offset: bin_cand_kernel
+// (candidate cells' members) then bin_finalize_kernel (per chunk)
 cudaError_t launch_bin_cell(const BinArgs& a, const Dims& d, bool shadow, cudaStream_t s);
 bool bin_cell_supported(const Dims& d);
 // true when the skipping binner keeps per-warp counters (and records the

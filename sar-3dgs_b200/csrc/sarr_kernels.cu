@@ -498,13 +498,17 @@ __device__ __forceinline__ uint32_t bound_rect2(float cr, float cc, float hr, fl
   return make_rect(r0, r1, c0, c1, Nr, Na);
 }
 
-__global__ void cell_init_kernel(SceneGrid* g, int* cell_hb) {
+__global__ void cell_init_kernel(SceneGrid* g, int* cell_hb, int* cell_count) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i < kMaxCells) cell_hb[i] = ordered_key(-1.0f);
+  if (i < kMaxCells) {
+    cell_hb[i] = ordered_key(-1.0f);
+    cell_count[i] = 0;
+  }
   if (i < 3) {
     g->lo_key[i] = ordered_key(INFINITY);
     g->hi_key[i] = ordered_key(-INFINITY);
   }
+  if (i == 0) g->n_always = 0;
 }
 
 // Bounding box of the finite Gaussian centres.
@@ -608,10 +612,56 @@ __global__ void __launch_bounds__(256) cell_assign_kernel(const CellPrepArgs a) 
       const int iz = min(max((int)floorf((z - g.lo[2]) * g.inv_a), 0), g.dims[2] - 1);
       id = (uint32_t)((iz * g.dims[1] + iy) * g.dims[0] + ix);
       atomicMax(a.cell_hb + id, ordered_key(hb));
+      if (j >= a.pstart) atomicAdd(a.cell_count + id, 1);
     }
   }
   a.hb[j] = hb;
   a.cid[j] = id;
+  if (id == kCellAlways && j >= a.pstart) a.always[atomicAdd(&a.grid->n_always, 1)] = (int)j;
+}
+
+// Exclusive scan of the cells' member counts into cell_start (one CTA); the
+// counts become the fill cursors.
+__global__ void __launch_bounds__(1024) cell_scan_kernel(const CellPrepArgs a) {
+  __shared__ int s_warp[32];
+  constexpr int kPer = kMaxCells / 1024;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  int v[kPer];
+  int sum = 0;
+#pragma unroll
+  for (int k = 0; k < kPer; ++k) {
+    v[k] = a.cell_count[tid * kPer + k];
+    sum += v[k];
+  }
+  const int incl = warp_incl_scan(sum, lane);
+  if (lane == 31) s_warp[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    const int w = s_warp[lane];
+    s_warp[lane] = warp_incl_scan(w, lane) - w;
+  }
+  __syncthreads();
+  int run = s_warp[warp] + incl - sum;
+#pragma unroll
+  for (int k = 0; k < kPer; ++k) {
+    a.cell_start[tid * kPer + k] = run;
+    a.cell_count[tid * kPer + k] = run;
+    run += v[k];
+  }
+  if (tid == 1023) a.cell_start[kMaxCells] = run;
+}
+
+// Member lists: centre and bbox bound of every Gaussian after the prefix,
+// grouped by cell (order inside a cell is immaterial: the lists are only
+// read to find the Gaussians to bin exactly, which are then ordered per chunk).
+__global__ void __launch_bounds__(256) cell_fill_kernel(const CellPrepArgs a) {
+  const int64_t j = a.pstart + (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= a.n) return;
+  const uint32_t id = a.cid[j];
+  if (id >= (uint32_t)kMaxCells) return;
+  const int pos = atomicAdd(a.cell_count + id, 1);
+  a.mem_pos[pos] = make_float4(a.means[3 * j], a.means[3 * j + 1], a.means[3 * j + 2], a.hb[j]);
+  a.mem_idx[pos] = (int)j;
 }
 
 // Cell bitmap of one view: bit c is set when a member of cell c may reach a
@@ -650,144 +700,130 @@ __global__ void __launch_bounds__(256) cell_test_kernel(const CellTestArgs a) {
   }
   const unsigned m = __ballot_sync(0xffffffffu, open);
   if ((threadIdx.x & 31) == 0) a.bits[v * a.bits_vstride + (c >> 5)] = m;
+  for (int i = blockIdx.x * 256 + threadIdx.x; i < a.xbits_words; i += gridDim.x * 256)
+    a.xbits[v * a.xbits_vstride + i] = 0;
 }
 
-// Saturation-skipping binning with cell culling: one view per warp, a range
-// of chunks per CTA. A Gaussian whose cell is closed for the view gets an
-// empty rectangle after one bitmap lookup; the others go through the
-// per-Gaussian test of bin_skip_kernel (queue A) and, when that cannot skip
-// them, exact binning (queue B). Parameters of queued Gaussians are read from
-// global memory (L2); only the chunk's cell ids are staged.
+// Cell binning, part 1 (per view): the members of the view's candidate cells
+// (bit set by cell_test_kernel) go through bin_skip_kernel's per-Gaussian
+// test; those it cannot skip, and the Gaussians in no cell, get their bit set
+// in the view's exactly-binned bitmap. bin_finalize_kernel bins them.
+// Grid: (kMaxCells / 256 cell blocks + kAlwaysBlocks, views); a warp handles
+// the 32 cells of one bitmap word, or a stride of the no-cell list.
+constexpr int kAlwaysBlocks = 64;
+
 template <bool kShadow>
-__global__ void __launch_bounds__(kBinThreads, 3) bin_cell_kernel(const BinArgs a) {
-  extern __shared__ __align__(16) unsigned char smem_raw[];
-  __shared__ short s_qa[kBinThreads / 32][64];
-  __shared__ short s_qb[kBinThreads / 32][64];
+__global__ void __launch_bounds__(kBinThreads) bin_cand_kernel(const BinArgs a) {
   constexpr int kWarps = kBinThreads / 32;
-
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int v = blockIdx.y * kWarps + warp;
-  const bool active = v < a.nviews;
-  const int tiles_x = a.views[0].tiles_x, tiles_y = a.views[0].tiles_y, T = tiles_x * tiles_y;
-  const int cs = a.cov_layout;
-  const int TW = (T + 1) >> 1;
-  const int pitch = tiles_x + 1;
-
-  uint32_t* s_bits = reinterpret_cast<uint32_t*>(smem_raw) + warp * kCellWords;
-  uint32_t* s_cid = reinterpret_cast<uint32_t*>(smem_raw) + kWarps * kCellWords;
-  uint32_t* s_cnt = s_cid + kChunk + warp * TW * (kShadow ? 2 : 1);
-  uint32_t* s_cnt_sh = s_cnt + TW;
-  short* qa = s_qa[warp];
-  short* qb = s_qb[warp];
-
-  const int vv = active ? v : 0;
-  const ViewConst& vg = a.views[vv];
-  const ViewConst vc = vg;
-  const int Nr = vc.h.Nr, Na = vc.h.Na;
-  uint32_t* rects_ipp = reinterpret_cast<uint32_t*>(a.ipp.base + vv * a.ipp.vstride + a.ipp.L.rects);
-  uint32_t* rects_sh =
-      kShadow ? reinterpret_cast<uint32_t*>(a.sh.base + vv * a.sh.vstride + a.sh.L.rects) : nullptr;
-  const int* open_ipp = a.open_ipp + vv * a.open_vstride;
-  const int* open_sh = a.open_sh + vv * a.open_vstride;
-  if (active) {
-    const uint32_t* bits = a.bits + vv * a.bits_vstride;
-    for (int i = lane; i < kCellWords; i += 32) s_bits[i] = __ldg(bits + i);
-    for (int i = lane; i < TW * (kShadow ? 2 : 1); i += 32) s_cnt[i] = 0;
-  }
-  const unsigned lt_mask = (1u << lane) - 1u;
-
-  const int c_first = a.chunk_offset + blockIdx.x * a.chunks_per_cta;
-  const int c_last = min(a.chunk_offset + a.chunks, c_first + a.chunks_per_cta);
-  for (int chunk = c_first; chunk < c_last; ++chunk) {
-    const int64_t base = (int64_t)chunk * kChunk;
-    const int gcount = (int)min((int64_t)kChunk, a.n - base);
-    __syncthreads();  // the previous chunk's ids are consumed
-    for (int i = tid; i < gcount; i += kBinThreads) s_cid[i] = __ldg(a.cid + base + i);
-    __syncthreads();
-    if (!active) continue;
-    const float* means = a.means + base * 3;
-    const float* cov = a.cov + base * cs;
-    const float* hbp = a.hb + base;
-    uint32_t* r_ipp = rects_ipp + base;
-    uint32_t* r_sh = kShadow ? rects_sh + base : nullptr;
-
-    uint16_t* xl = x_list(a, vv, chunk);
-    int xn = 0;  // Gaussians of this chunk binned exactly so far (index order)
-    // exact binning of Gaussian j (chunk-local) by this lane
-    auto bin_queued = [&](int j) {
-      uint32_t rc_ipp = kEmptyRect, rc_sh = kEmptyRect;
-      bin_exact<kShadow>(vg, means, cov, cs, j, rc_ipp, rc_sh);
-      if (xl && xn + lane < kXCap) xl[xn + lane] = (uint16_t)j;
-      r_ipp[j] = rc_ipp;
-      count_rect(s_cnt, rc_ipp, tiles_x);
-      if (kShadow) {
-        r_sh[j] = rc_sh;
-        count_rect(s_cnt_sh, rc_sh, tiles_x);
-      }
-    };
-    // per-Gaussian test (bin_skip_kernel's) of Gaussian j: true when it
-    // needs exact binning; otherwise its empty rectangles are written
-    auto needs_exact = [&](int j) {
-      if (s_cid[j] == kCellAlways) return true;
-      float r, c, xr, yr;
-      approx_center(vc, __ldg(means + 3 * j), __ldg(means + 3 * j + 1), __ldg(means + 3 * j + 2), r,
-                    c, xr, yr);
-      const float h = __ldg(hbp + j) + vc.center_margin;
-      bool skip = open_in_rect(bound_rect(r, c, h, Nr, Na), open_ipp, pitch) == 0;
-      if (kShadow && skip) skip = open_in_rect(bound_rect(yr, xr, h, Nr, Na), open_sh, pitch) == 0;
-      if (skip) {
-        r_ipp[j] = kEmptyRect;
-        if (kShadow) r_sh[j] = kEmptyRect;
-      }
-      return !skip;
-    };
-    // tests queue A slots [0, min(na, 32)) and moves the survivors to queue B;
-    // bins 32 of queue B once it holds that many
-    int na = 0, nb = 0;
-    auto drain_a = [&]() {
-      const bool take = lane < na;
-      const int j1 = take ? qa[lane] : 0;
-      const bool exact = take && needs_exact(j1);
-      const unsigned mb = __ballot_sync(0xffffffffu, exact);
-      if (exact) qb[nb + __popc(mb & lt_mask)] = (short)j1;
-      nb += __popc(mb);
-      __syncwarp();
-      if (lane < na - 32) qa[lane] = qa[lane + 32];
-      na = na > 32 ? na - 32 : 0;
-      if (nb >= 32) {
-        bin_queued(qb[lane]);
-        xn += 32;
-        __syncwarp();
-        if (lane < nb - 32) qb[lane] = qb[lane + 32];
-        nb -= 32;
-      }
-      __syncwarp();
-    };
-    for (int j0 = 0; j0 < gcount; j0 += 32) {
-      const int j = j0 + lane;
-      bool cand = false;
-      if (j < gcount) {
-        const uint32_t id = s_cid[j];
-        cand = id == kCellAlways || (id != kCellNever && ((s_bits[id >> 5] >> (id & 31)) & 1u));
-        if (!cand) {
-          r_ipp[j] = kEmptyRect;
-          if (kShadow) r_sh[j] = kEmptyRect;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int v = blockIdx.y;
+  const SceneGrid& g = *a.grid;
+  uint32_t* xbits = a.xbits + v * a.xbits_vstride;
+  const int cell_blocks = kMaxCells / (kWarps * 32);
+  if ((int)blockIdx.x < cell_blocks) {
+    if (!g.valid) return;
+    const int word = blockIdx.x * kWarps + warp;
+    if (word * 32 >= g.ncells) return;
+    uint32_t cand = a.bits[v * a.bits_vstride + word];
+    if (!cand) return;
+    const ViewConst vc = a.views[v];
+    const int Nr = vc.h.Nr, Na = vc.h.Na, pitch = vc.tiles_x + 1;
+    const int* open_ipp = a.open_ipp + v * a.open_vstride;
+    const int* open_sh = a.open_sh + v * a.open_vstride;
+    while (cand) {
+      const int c = word * 32 + __ffs(cand) - 1;
+      cand &= cand - 1;
+      const int m_end = a.cell_start[c + 1];
+      for (int m = a.cell_start[c] + lane; m < m_end; m += 32) {
+        const float4 p = a.mem_pos[m];
+        float r, cc, xr, yr;
+        approx_center(vc, p.x, p.y, p.z, r, cc, xr, yr);
+        const float h = p.w + vc.center_margin;
+        bool exact = open_in_rect(bound_rect(r, cc, h, Nr, Na), open_ipp, pitch) != 0;
+        if (kShadow && !exact) exact = open_in_rect(bound_rect(yr, xr, h, Nr, Na), open_sh, pitch) != 0;
+        if (exact) {
+          const int j = a.mem_idx[m];
+          atomicOr(xbits + (j >> 5), 1u << (j & 31));
         }
       }
-      const unsigned m = __ballot_sync(0xffffffffu, cand);
-      if (cand) qa[na + __popc(m & lt_mask)] = (short)j;
-      na += __popc(m);
-      __syncwarp();
-      if (na >= 32) drain_a();
     }
-    if (na > 0) drain_a();
-    if (lane < nb) bin_queued(qb[lane]);
-    xn += nb;
-    __syncwarp();
-    if (xl && lane == 0) x_count(a, vv)[chunk] = xn <= kXCap ? xn : -1;
-    flush_counts(s_cnt, a.counts_ipp + vv * a.counts_vstride + (size_t)chunk * T, T, lane);
-    if (kShadow) flush_counts(s_cnt_sh, a.counts_sh + vv * a.counts_vstride + (size_t)chunk * T, T, lane);
+  } else {
+    const int nw = (gridDim.x - cell_blocks) * kWarps;
+    const int na = g.n_always;
+    for (int i = ((blockIdx.x - cell_blocks) * kWarps + warp) * 32 + lane; i < na; i += nw * 32) {
+      const int j = a.always[i];
+      atomicOr(xbits + (j >> 5), 1u << (j & 31));
+    }
   }
+}
+
+// Cell binning, part 2: one warp per (view, chunk after the prefix). The
+// Gaussians whose bits are set are listed in index order and binned exactly
+// (32 lanes at a time), every other Gaussian of the chunk gets empty
+// rectangles, and the chunk's tile counts are written.
+template <bool kShadow>
+__global__ void __launch_bounds__(kBinThreads) bin_finalize_kernel(const BinArgs a) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  constexpr int kWarps = kBinThreads / 32;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int v = blockIdx.y;
+  const int tiles_x = a.views[0].tiles_x, tiles_y = a.views[0].tiles_y, T = tiles_x * tiles_y;
+  const int TW = (T + 1) >> 1;
+  const int cs = a.cov_layout;
+  uint32_t* s_cnt = reinterpret_cast<uint32_t*>(smem_raw) + warp * TW * (kShadow ? 2 : 1);
+  uint32_t* s_cnt_sh = s_cnt + TW;
+  const int k = blockIdx.x * kWarps + warp;
+  if (k >= a.chunks) return;
+  const int chunk = a.chunk_offset + k;
+  const int64_t base = (int64_t)chunk * kChunk;
+  const int gcount = (int)min((int64_t)kChunk, a.n - base);
+  const ViewConst& vg = a.views[v];
+
+  for (int i = lane; i < TW * (kShadow ? 2 : 1); i += 32) s_cnt[i] = 0;
+  const uint32_t word = a.xbits[v * a.xbits_vstride + (size_t)chunk * 32 + lane];
+  const int cnt = __popc(word);
+  const int excl = warp_incl_scan(cnt, lane) - cnt;
+  const int total = __shfl_sync(0xffffffffu, excl + cnt, 31);
+  uint16_t* xl = x_list(a, v, chunk);
+  if (lane == 0) x_count(a, v)[chunk] = total;
+  {
+    uint32_t wbits = word;
+    int pos = excl;
+    while (wbits) {
+      xl[pos++] = (uint16_t)(lane * 32 + __ffs(wbits) - 1);
+      wbits &= wbits - 1;
+    }
+  }
+  __syncwarp();
+
+  uint32_t* rects_ipp = reinterpret_cast<uint32_t*>(a.ipp.base + v * a.ipp.vstride + a.ipp.L.rects) + base;
+  uint32_t* rects_sh =
+      kShadow ? reinterpret_cast<uint32_t*>(a.sh.base + v * a.sh.vstride + a.sh.L.rects) + base : nullptr;
+  const float* means = a.means + base * 3;
+  const float* cov = a.cov + base * cs;
+  for (int i = lane; i < total; i += 32) {
+    const int jl = xl[i];
+    uint32_t rc_ipp = kEmptyRect, rc_sh = kEmptyRect;
+    bin_exact<kShadow>(vg, means, cov, cs, jl, rc_ipp, rc_sh);
+    rects_ipp[jl] = rc_ipp;
+    count_rect(s_cnt, rc_ipp, tiles_x);
+    if (kShadow) {
+      rects_sh[jl] = rc_sh;
+      count_rect(s_cnt_sh, rc_sh, tiles_x);
+    }
+  }
+  // every other Gaussian of the chunk: empty rectangles (coalesced)
+  for (int kk = 0; kk < 32; ++kk) {
+    const uint32_t wk = __shfl_sync(0xffffffffu, word, kk);
+    const int jl = kk * 32 + lane;
+    if (jl < gcount && !((wk >> lane) & 1u)) {
+      rects_ipp[jl] = kEmptyRect;
+      if (kShadow) rects_sh[jl] = kEmptyRect;
+    }
+  }
+  __syncwarp();
+  flush_counts(s_cnt, a.counts_ipp + v * a.counts_vstride + (size_t)chunk * T, T, lane);
+  if (kShadow) flush_counts(s_cnt_sh, a.counts_sh + v * a.counts_vstride + (size_t)chunk * T, T, lane);
 }
 
 // Open-tile summed-area table of one list of one view (grid: views x lists).
@@ -796,15 +832,6 @@ __global__ void __launch_bounds__(kBinThreads, 3) bin_cell_kernel(const BinArgs 
 // ty < y and tx < x. Built in shared memory with warp scans when it fits
 // (kOpenSmemInts), in global memory otherwise.
 constexpr int kOpenSmemInts = 8192;
-
-__device__ __forceinline__ int warp_incl_scan(int x, int lane) {
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const int y = __shfl_up_sync(0xffffffffu, x, o);
-    if (lane >= o) x += y;
-  }
-  return x;
-}
 
 __global__ void __launch_bounds__(256) open_table_kernel(const OpenArgs a) {
   __shared__ int s_tab[kOpenSmemInts];
@@ -1645,34 +1672,29 @@ cudaError_t launch_bin(const BinArgs& a, const Dims& d, int chunks, bool shadow,
   return cudaGetLastError();
 }
 
-// bin_cell_kernel: per-warp cell bitmaps, the chunk's cell ids, per-warp
-// tile counters (both lists counted when the shadow list is built).
-static size_t bin_cell_smem_bytes(const Dims& d, bool shadow) {
-  return (size_t)(kBinThreads / 32) * kCellWords * 4 + (size_t)kChunk * 4 +
-         warp_count_bytes(d, shadow);
-}
-
 bool bin_cell_supported(const Dims& d) { return warp_count_bytes(d, true) <= kWarpCountBytes; }
 
 template <bool kShadow>
-static void launch_bin_cell_t(const BinArgs& a, dim3 grid, size_t smem, cudaStream_t s) {
+static void launch_bin_cell_t(const BinArgs& a, int nviews, size_t smem, cudaStream_t s) {
+  const dim3 cand_grid(kMaxCells / kBinThreads + kAlwaysBlocks, nviews);
+  bin_cand_kernel<kShadow><<<cand_grid, kBinThreads, 0, s>>>(a);
+  const int warps = kBinThreads / 32;
+  const dim3 fin_grid((a.chunks + warps - 1) / warps, nviews);
   if (needs_smem_attr(smem))
-    cudaFuncSetAttribute(bin_cell_kernel<kShadow>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaFuncSetAttribute(bin_finalize_kernel<kShadow>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)smem);
-  bin_cell_kernel<kShadow><<<grid, kBinThreads, smem, s>>>(a);
+  bin_finalize_kernel<kShadow><<<fin_grid, kBinThreads, smem, s>>>(a);
 }
 
 cudaError_t launch_bin_cell(const BinArgs& a, const Dims& d, bool shadow, cudaStream_t s) {
-  const int vgroups = (a.nviews + kBinThreads / 32 - 1) / (kBinThreads / 32);
-  const dim3 grid((a.chunks + a.chunks_per_cta - 1) / a.chunks_per_cta, vgroups);
-  const size_t smem = bin_cell_smem_bytes(d, shadow);
-  if (shadow) launch_bin_cell_t<true>(a, grid, smem, s);
-  else launch_bin_cell_t<false>(a, grid, smem, s);
+  const size_t smem = warp_count_bytes(d, shadow);
+  if (shadow) launch_bin_cell_t<true>(a, a.nviews, smem, s);
+  else launch_bin_cell_t<false>(a, a.nviews, smem, s);
   return cudaGetLastError();
 }
 
 cudaError_t launch_cell_prep(const CellPrepArgs& a, cudaStream_t s) {
-  cell_init_kernel<<<(kMaxCells + 255) / 256, 256, 0, s>>>(a.grid, a.cell_hb);
+  cell_init_kernel<<<(kMaxCells + 255) / 256, 256, 0, s>>>(a.grid, a.cell_hb, a.cell_count);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   const int64_t blocks = min((int64_t)148 * 8, (a.n + 255) / 256);
@@ -1683,6 +1705,12 @@ cudaError_t launch_cell_prep(const CellPrepArgs& a, cudaStream_t s) {
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   cell_assign_kernel<<<(unsigned)((a.n + 255) / 256), 256, 0, s>>>(a);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  cell_scan_kernel<<<1, 1024, 0, s>>>(a);
+  e = cudaGetLastError();
+  if (e != cudaSuccess || a.n <= a.pstart) return e;
+  cell_fill_kernel<<<(unsigned)((a.n - a.pstart + 255) / 256), 256, 0, s>>>(a);
   return cudaGetLastError();
 }
 
