@@ -117,14 +117,15 @@ int cuda_status(cudaError_t e) { return e == cudaSuccess ? SARR_OK : SARR_ERR_CU
 // ---------------------------------------------------------------------------
 enum KernelKind {
   kKindSetup = 0, kKindBin, kKindSelect, kKindSelectShadow, kKindRender, kKindOmegaTile,
-  kKindOmegaScatter, kKindBwdTile, kKindBwdScatter, kKindAux, kKindScan, kKindBinSkip, kKindCount
+  kKindOmegaScatter, kKindBwdTile, kKindBwdScatter, kKindAux, kKindScan, kKindBinSkip,
+  kKindBinFinalize, kKindCount
 };
 static_assert(kKindCount == SARR_KERNEL_KINDS, "kernel kinds");
 
 const char* const kKindNames[kKindCount] = {
     "view_setup", "bin_kernel", "select_kernel", "select_kernel_shadow", "render_kernel",
     "omega_tile_kernel", "omega_scatter_kernel", "bwd_tile_kernel", "bwd_scatter_kernel", "aux",
-    "scan_kernel", "bin_skip_kernel"};
+    "scan_kernel", "bin_skip_kernel", "bin_finalize_kernel"};
 
 struct ProfRecord {
   int kind, device;
@@ -253,6 +254,7 @@ cudaError_t run_cell_prep(const Dims& d, const Ws& w, const float* means, const 
   cp.pstart = (int64_t)kPrefixChunks * kChunk;
   cp.cell_count = reinterpret_cast<int*>(w.base + w.L.cell_count);
   cp.cell_start = reinterpret_cast<int*>(w.base + w.L.cell_start);
+  cp.cell_center = reinterpret_cast<float4*>(w.base + w.L.cell_center);
   cp.mem_pos = reinterpret_cast<float4*>(w.base + w.L.mem_pos);
   cp.mem_idx = reinterpret_cast<int*>(w.base + w.L.mem_idx);
   cp.always = reinterpret_cast<int*>(w.base + w.L.always);
@@ -330,6 +332,7 @@ cudaError_t run_selection(const Dims& d, const Ws& w, int gv, const float* means
       ct.views = w.views;
       ct.grid = reinterpret_cast<const SceneGrid*>(w.base + w.L.scene);
       ct.cell_hb = reinterpret_cast<const int*>(w.base + w.L.cell_hb);
+      ct.cell_center = reinterpret_cast<const float4*>(w.base + w.L.cell_center);
       ct.open_ipp = ba.open_ipp;
       ct.open_sh = ba.open_sh;
       ct.open_vstride = ba.open_vstride;
@@ -351,7 +354,9 @@ cudaError_t run_selection(const Dims& d, const Ws& w, int gv, const float* means
       ba.bits_vstride = ct.bits_vstride;
       ba.xbits = ct.xbits;
       ba.xbits_vstride = ct.xbits_vstride;
-      e = run_kernel(kKindBinSkip, s, [&] { return launch_bin_cell(ba, d, shr != nullptr, s); });
+      e = run_kernel(kKindBinSkip, s, [&] { return launch_bin_cand(ba, shr != nullptr, s); });
+      if (e != cudaSuccess) return e;
+      e = run_kernel(kKindBinFinalize, s, [&] { return launch_bin_finalize(ba, d, shr != nullptr, s); });
       if (e != cudaSuccess) return e;
     } else {
       ba.views_per_cta = views_per_cta(d.C - prefix);

@@ -40,8 +40,15 @@ constexpr uint32_t kEmptyRect = 0x000000FFu;     // tc0 = 255 > tc1 = 0
 // Cell culling of multi-view launches: a view-independent grid of cells over
 // the Gaussian centres; per view, one bit per cell says whether any member
 // can reach a tile that is still open after the saturation prefix.
-constexpr int kMaxCells = 32768;
+constexpr int kMaxCells = 65536;
 constexpr int kCellWords = kMaxCells / 32;
+// Cells split the Gaussians of a spatial cell by their bbox bound, so that a
+// cell's largest bound stays close to its members' bounds.
+constexpr int kHbBuckets = 4;
+constexpr int kMaxSpatialCells = kMaxCells / kHbBuckets;
+__host__ __device__ __forceinline__ int hb_bucket(float hb) {
+  return (int)(hb > 6.0f) + (int)(hb > 8.0f) + (int)(hb > 11.0f);
+}
 constexpr int kCellMinViews = 8;                 // calls with fewer views bin without cells
 constexpr uint32_t kCellAlways = 0xFFFFFFFFu;    // no cell: always tested individually
 constexpr uint32_t kCellNever = 0xFFFFFFFEu;     // transmittance < 0.01: never in a list
@@ -55,6 +62,7 @@ struct SceneGrid {
   int ncells;
   float half_diag;           // bound on |member centre - cell centre| [m], with margins
   int valid;                 // 0: no finite centre (no Gaussian is in a cell)
+  int nspatial;              // spatial cells (ncells = nspatial * kHbBuckets)
   int n_always;              // Gaussians after the prefix that are in no cell
 };
 

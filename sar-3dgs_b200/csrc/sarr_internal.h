@@ -65,7 +65,8 @@ __host__ __device__ inline StateLayout state_layout(int64_t n, int T) {
 // area its cell bitmap bits [kCellWords] u32 and its exactly-binned bitmap
 // xbits [C][32] u32.
 struct WsLayout {
-  size_t viewconst, err, scene, hb, cid, cell_hb, cell_count, cell_start, mem_pos, mem_idx, always, head;
+  size_t viewconst, err, scene, hb, cid, cell_hb, cell_count, cell_start, cell_center, mem_pos, mem_idx,
+      always, head;
   size_t counts_ipp, counts_sh, need_ipp, need_sh, need_n_ipp, need_n_sh, open_ipp, open_sh;
   size_t bits, xbits, xcount, xlist, segmask_ipp, segmask_sh, state_ipp, state_sh, partial_om,
       partial_bwd, per_view;
@@ -85,7 +86,7 @@ __host__ inline WsLayout ws_layout(const Dims& d, bool cells) {
   L.viewconst = 0;
   L.err = align256(sizeof(ViewConst) * kMaxViewsPerLaunch);
   size_t h = L.err + 256;
-  L.scene = L.hb = L.cid = L.cell_hb = L.cell_count = L.cell_start = 0;
+  L.scene = L.hb = L.cid = L.cell_hb = L.cell_count = L.cell_start = L.cell_center = 0;
   L.mem_pos = L.mem_idx = L.always = 0;
   if (cells) {
     L.scene = h;
@@ -100,6 +101,8 @@ __host__ inline WsLayout ws_layout(const Dims& d, bool cells) {
     h += align256((size_t)kMaxCells * 4);
     L.cell_start = h;
     h += align256((size_t)(kMaxCells + 1) * 4);
+    L.cell_center = h;
+    h += align256((size_t)kMaxSpatialCells * 16);
     L.mem_pos = h;
     h += align256((size_t)d.n * 16);
     L.mem_idx = h;
@@ -219,6 +222,7 @@ struct CellPrepArgs {
   int* cell_hb;
   int* cell_count;
   int* cell_start;
+  float4* cell_center;  // [kMaxSpatialCells] centre of each spatial cell
   float4* mem_pos;
   int* mem_idx;
   int* always;
@@ -227,6 +231,7 @@ struct CellPrepArgs {
 struct CellTestArgs {
   const ViewConst* views;
   const SceneGrid* grid;
+  const float4* cell_center;
   const int* cell_hb;
   const int* open_ipp;
   const int* open_sh;
@@ -354,8 +359,9 @@ cudaError_t launch_open_table(const OpenArgs& a, int nviews, int nlists, cudaStr
 cudaError_t launch_cell_prep(const CellPrepArgs& a, cudaStream_t s);
 cudaError_t launch_cell_test(const CellTestArgs& a, int nviews, cudaStream_t s);
 // cell binning of the a.chunks chunks from a.chunk_offset: bin_cand_kernel
-// (candidate cells' members) then bin_finalize_kernel (per chunk)
-cudaError_t launch_bin_cell(const BinArgs& a, const Dims& d, bool shadow, cudaStream_t s);
+// (candidate cells' members), then bin_finalize_kernel (per chunk)
+cudaError_t launch_bin_cand(const BinArgs& a, bool shadow, cudaStream_t s);
+cudaError_t launch_bin_finalize(const BinArgs& a, const Dims& d, bool shadow, cudaStream_t s);
 bool bin_cell_supported(const Dims& d);
 // true when the skipping binner keeps per-warp counters (and records the
 // exact lists); false selects its CTA-wide variant

@@ -561,7 +561,7 @@ __global__ void scene_grid_kernel(SceneGrid* g, int64_t n) {
   const float emax = fmaxf(ext[0], fmaxf(ext[1], ext[2]));
   const float pad = 1e-3f * emax + 1e-6f;
   const float vol = (ext[0] + pad) * (ext[1] + pad) * (ext[2] + pad);
-  const int64_t target = max((int64_t)1, min((int64_t)kMaxCells, n / 32));
+  const int64_t target = max((int64_t)1, min((int64_t)kMaxSpatialCells, n / 64));
   float a = cbrtf(vol / (float)target);
   if (!(a > 0.0f) || !isfinite(a)) a = fmaxf(emax, 1e-6f);
   int dims[3];
@@ -573,11 +573,11 @@ __global__ void scene_grid_kernel(SceneGrid* g, int64_t n) {
       while ((float)dims[k] * a < ext[k]) ++dims[k];
       prod *= dims[k];
     }
-    if (prod <= kMaxCells) break;
+    if (prod <= kMaxSpatialCells) break;
     a *= 1.05f;
   }
   int64_t prod = (int64_t)dims[0] * dims[1] * dims[2];
-  if (prod > kMaxCells) return;  // not reached for finite boxes; no cells then
+  if (prod > kMaxSpatialCells) return;  // not reached for finite boxes; no cells then
   float scale = emax + a;
   for (int k = 0; k < 3; ++k) {
     g->lo[k] = lo[k];
@@ -586,9 +586,20 @@ __global__ void scene_grid_kernel(SceneGrid* g, int64_t n) {
   }
   g->a = a;
   g->inv_a = 1.0f / a;
-  g->ncells = (int)prod;
+  g->nspatial = (int)prod;
+  g->ncells = (int)prod * kHbBuckets;
   g->half_diag = a * 0.8660254f * 1.0001f + 4e-6f * scale;
   g->valid = 1;
+}
+
+// Centres of the spatial cells.
+__global__ void __launch_bounds__(256) cell_center_kernel(const SceneGrid* g, float4* center) {
+  const int c = blockIdx.x * 256 + threadIdx.x;
+  if (!g->valid || c >= g->nspatial) return;
+  const int d0 = g->dims[0], d1 = g->dims[1];
+  const int ix = c % d0, iy = (c / d0) % d1, iz = c / (d0 * d1);
+  center[c] = make_float4(g->lo[0] + ((float)ix + 0.5f) * g->a, g->lo[1] + ((float)iy + 0.5f) * g->a,
+                          g->lo[2] + ((float)iz + 0.5f) * g->a, 0.0f);
 }
 
 // Per Gaussian: its view-independent bbox bound and cell id, and the largest
@@ -610,7 +621,7 @@ __global__ void __launch_bounds__(256) cell_assign_kernel(const CellPrepArgs a) 
       const int ix = min(max((int)floorf((x - g.lo[0]) * g.inv_a), 0), g.dims[0] - 1);
       const int iy = min(max((int)floorf((y - g.lo[1]) * g.inv_a), 0), g.dims[1] - 1);
       const int iz = min(max((int)floorf((z - g.lo[2]) * g.inv_a), 0), g.dims[2] - 1);
-      id = (uint32_t)((iz * g.dims[1] + iy) * g.dims[0] + ix);
+      id = (uint32_t)(((iz * g.dims[1] + iy) * g.dims[0] + ix) * kHbBuckets + hb_bucket(hb));
       atomicMax(a.cell_hb + id, ordered_key(hb));
       if (j >= a.pstart) atomicAdd(a.cell_count + id, 1);
     }
@@ -626,13 +637,9 @@ __global__ void __launch_bounds__(1024) cell_scan_kernel(const CellPrepArgs a) {
   __shared__ int s_warp[32];
   constexpr int kPer = kMaxCells / 1024;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  int v[kPer];
+  const int* cnt = a.cell_count + tid * kPer;
   int sum = 0;
-#pragma unroll
-  for (int k = 0; k < kPer; ++k) {
-    v[k] = a.cell_count[tid * kPer + k];
-    sum += v[k];
-  }
+  for (int k = 0; k < kPer; ++k) sum += cnt[k];
   const int incl = warp_incl_scan(sum, lane);
   if (lane == 31) s_warp[warp] = incl;
   __syncthreads();
@@ -642,11 +649,12 @@ __global__ void __launch_bounds__(1024) cell_scan_kernel(const CellPrepArgs a) {
   }
   __syncthreads();
   int run = s_warp[warp] + incl - sum;
-#pragma unroll
   for (int k = 0; k < kPer; ++k) {
-    a.cell_start[tid * kPer + k] = run;
-    a.cell_count[tid * kPer + k] = run;
-    run += v[k];
+    const int c = tid * kPer + k;
+    const int x = a.cell_count[c];
+    a.cell_start[c] = run;
+    a.cell_count[c] = run;
+    run += x;
   }
   if (tid == 1023) a.cell_start[kMaxCells] = run;
 }
@@ -679,13 +687,9 @@ __global__ void __launch_bounds__(256) cell_test_kernel(const CellTestArgs a) {
     if (hbm >= 0.0f) {
       const ViewConst& vc = a.views[v];
       const int Nr = vc.h.Nr, Na = vc.h.Na, pitch = vc.tiles_x + 1;
-      const int d0 = g.dims[0], d1 = g.dims[1];
-      const int ix = c % d0, iy = (c / d0) % d1, iz = c / (d0 * d1);
-      const float qx = g.lo[0] + ((float)ix + 0.5f) * g.a;
-      const float qy = g.lo[1] + ((float)iy + 0.5f) * g.a;
-      const float qz = g.lo[2] + ((float)iz + 0.5f) * g.a;
+      const float4 q = a.cell_center[c / kHbBuckets];
       float r, cc, xr, yr;
-      approx_center(vc, qx, qy, qz, r, cc, xr, yr);
+      approx_center(vc, q.x, q.y, q.z, r, cc, xr, yr);
       const float base = hbm + 2.0f * vc.center_margin + 0.02f;
       const float hr = base + g.half_diag * fabsf(vc.inv_rho_r) * 1.0001f;
       const float hc = base + g.half_diag * fabsf(vc.inv_rho_a) * 1.0001f;
@@ -724,21 +728,38 @@ __global__ void __launch_bounds__(kBinThreads) bin_cand_kernel(const BinArgs a) 
     if (!g.valid) return;
     const int word = blockIdx.x * kWarps + warp;
     if (word * 32 >= g.ncells) return;
-    uint32_t cand = a.bits[v * a.bits_vstride + word];
+    const uint32_t cand = a.bits[v * a.bits_vstride + word];
     if (!cand) return;
     const ViewConst vc = a.views[v];
     const int Nr = vc.h.Nr, Na = vc.h.Na, pitch = vc.tiles_x + 1;
     const int* open_ipp = a.open_ipp + v * a.open_vstride;
     const int* open_sh = a.open_sh + v * a.open_vstride;
-    while (cand) {
-      const int c = word * 32 + __ffs(cand) - 1;
-      cand &= cand - 1;
-      const int m_end = a.cell_start[c + 1];
-      for (int m = a.cell_start[c] + lane; m < m_end; m += 32) {
-        const float4 p = a.mem_pos[m];
+    // the members of the word's candidate cells, concatenated, 32 per round:
+    // member p of the concatenation belongs to the first lane (cell) whose
+    // inclusive member prefix exceeds p
+    const int c_l = word * 32 + lane;
+    const bool set = (cand >> lane) & 1u;
+    const int start_l = set ? a.cell_start[c_l] : 0;
+    const int cnt_l = set ? a.cell_start[c_l + 1] - start_l : 0;
+    const int incl_l = warp_incl_scan(cnt_l, lane);
+    const int total = __shfl_sync(0xffffffffu, incl_l, 31);
+    for (int p0 = 0; p0 < total; p0 += 32) {
+      const int p = p0 + lane;
+      int lo = 0, hi = 31;  // first lane with incl > p
+#pragma unroll
+      for (int it = 0; it < 5; ++it) {
+        const int mid = (lo + hi) >> 1;
+        const int im = __shfl_sync(0xffffffffu, incl_l, mid);
+        if (im > p) hi = mid; else lo = mid + 1;
+      }
+      const int owner_start = __shfl_sync(0xffffffffu, start_l, lo);
+      const int owner_excl = __shfl_sync(0xffffffffu, incl_l - cnt_l, lo);
+      if (p < total) {
+        const int m = owner_start + (p - owner_excl);
+        const float4 p4 = a.mem_pos[m];
         float r, cc, xr, yr;
-        approx_center(vc, p.x, p.y, p.z, r, cc, xr, yr);
-        const float h = p.w + vc.center_margin;
+        approx_center(vc, p4.x, p4.y, p4.z, r, cc, xr, yr);
+        const float h = p4.w + vc.center_margin;
         bool exact = open_in_rect(bound_rect(r, cc, h, Nr, Na), open_ipp, pitch) != 0;
         if (kShadow && !exact) exact = open_in_rect(bound_rect(yr, xr, h, Nr, Na), open_sh, pitch) != 0;
         if (exact) {
@@ -1674,22 +1695,27 @@ cudaError_t launch_bin(const BinArgs& a, const Dims& d, int chunks, bool shadow,
 
 bool bin_cell_supported(const Dims& d) { return warp_count_bytes(d, true) <= kWarpCountBytes; }
 
+cudaError_t launch_bin_cand(const BinArgs& a, bool shadow, cudaStream_t s) {
+  const dim3 grid(kMaxCells / kBinThreads + kAlwaysBlocks, a.nviews);
+  if (shadow) bin_cand_kernel<true><<<grid, kBinThreads, 0, s>>>(a);
+  else bin_cand_kernel<false><<<grid, kBinThreads, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
 template <bool kShadow>
-static void launch_bin_cell_t(const BinArgs& a, int nviews, size_t smem, cudaStream_t s) {
-  const dim3 cand_grid(kMaxCells / kBinThreads + kAlwaysBlocks, nviews);
-  bin_cand_kernel<kShadow><<<cand_grid, kBinThreads, 0, s>>>(a);
-  const int warps = kBinThreads / 32;
-  const dim3 fin_grid((a.chunks + warps - 1) / warps, nviews);
+static void launch_bin_finalize_t(const BinArgs& a, dim3 grid, size_t smem, cudaStream_t s) {
   if (needs_smem_attr(smem))
     cudaFuncSetAttribute(bin_finalize_kernel<kShadow>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)smem);
-  bin_finalize_kernel<kShadow><<<fin_grid, kBinThreads, smem, s>>>(a);
+  bin_finalize_kernel<kShadow><<<grid, kBinThreads, smem, s>>>(a);
 }
 
-cudaError_t launch_bin_cell(const BinArgs& a, const Dims& d, bool shadow, cudaStream_t s) {
+cudaError_t launch_bin_finalize(const BinArgs& a, const Dims& d, bool shadow, cudaStream_t s) {
+  const int warps = kBinThreads / 32;
+  const dim3 grid((a.chunks + warps - 1) / warps, a.nviews);
   const size_t smem = warp_count_bytes(d, shadow);
-  if (shadow) launch_bin_cell_t<true>(a, a.nviews, smem, s);
-  else launch_bin_cell_t<false>(a, a.nviews, smem, s);
+  if (shadow) launch_bin_finalize_t<true>(a, grid, smem, s);
+  else launch_bin_finalize_t<false>(a, grid, smem, s);
   return cudaGetLastError();
 }
 
@@ -1702,6 +1728,9 @@ cudaError_t launch_cell_prep(const CellPrepArgs& a, cudaStream_t s) {
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   scene_grid_kernel<<<1, 32, 0, s>>>(a.grid, a.n);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  cell_center_kernel<<<kMaxSpatialCells / 256, 256, 0, s>>>(a.grid, a.cell_center);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   cell_assign_kernel<<<(unsigned)((a.n + 255) / 256), 256, 0, s>>>(a);

@@ -286,7 +286,7 @@ def launch_count():
     return int(lib().sarr_launch_count())
 
 
-KERNEL_KINDS = 12
+KERNEL_KINDS = 13
 
 
 def profile_enable(on=True):
