@@ -26,7 +26,7 @@ constexpr int kSh = 16;                         // SH_COEFFS_SIZE
 constexpr int kBinThreads = 256;                 // threads of a binning CTA
 constexpr int kBinPerThread = 4;                 // Gaussians per binning thread
 constexpr int kChunk = kBinThreads * kBinPerThread;  // Gaussians per count row
-constexpr int kSelectThreads = 256;
+constexpr int kSelectThreads = 128;
 constexpr int kScanThreads = 512;
 constexpr int kPrefixChunks = 32;                // chunks binned exactly before saturation skipping
 constexpr int kXCap = kChunk;                    // exactly binned Gaussians listed per skipped chunk

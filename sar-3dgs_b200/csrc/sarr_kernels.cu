@@ -991,11 +991,34 @@ __global__ void __launch_bounds__(kSelectThreads) select_kernel(const SelectArgs
                                      reinterpret_cast<const unsigned char*>(a.xcount) + v * a.x_vstride)
                                : nullptr;
   const unsigned lt_mask = (1u << lane) - 1u;
+  // the need entries and their per-chunk data, prefetched: lane l holds
+  // entries l and l + 32 (exact-list length, or segment mask)
+  int4 nd_l[2];
+  int aux_l[2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int q = lane + 32 * h;
+    nd_l[h] = make_int4(0, 0, 0, 0);
+    aux_l[h] = -1;
+    if (q < nneed) {
+      nd_l[h] = need[q];
+      const int c = nd_l[h].x;
+      if (xcount && c >= a.xlist_from)
+        aux_l[h] = xcount[c];
+      else if (a.segmask && c < a.segmask_to)
+        aux_l[h] = (int)a.segmask[v * a.segmask_vstride + (size_t)c * T + t];
+    }
+  }
   for (int q = 0; q < nneed; ++q) {
-    const int4 nd = need[q];
+    const int hq = q >> 5, src = q & 31;
+    int4 nd;
+    nd.x = __shfl_sync(0xffffffffu, hq ? nd_l[1].x : nd_l[0].x, src);
+    nd.y = __shfl_sync(0xffffffffu, hq ? nd_l[1].y : nd_l[0].y, src);
+    nd.z = __shfl_sync(0xffffffffu, hq ? nd_l[1].z : nd_l[0].z, src);
+    const int aux = __shfl_sync(0xffffffffu, hq ? aux_l[1] : aux_l[0], src);
     const int want = min(nd.z, kCap - nd.y);
     const int64_t b0 = (int64_t)nd.x * kChunk;
-    const int xc = (xcount && nd.x >= a.xlist_from) ? xcount[nd.x] : -1;
+    const int xc = (xcount && nd.x >= a.xlist_from) ? aux : -1;
     if (xc >= 0) {
       // only the chunk's exactly binned Gaussians can hit the tile
       const uint16_t* xl = reinterpret_cast<const uint16_t*>(
@@ -1020,7 +1043,7 @@ __global__ void __launch_bounds__(kSelectThreads) select_kernel(const SelectArgs
     const int valid = (int)min((int64_t)kChunk, a.n - b0);
     if (a.segmask && nd.x < a.segmask_to) {
       // only the 32-Gaussian segments that hold hits of the tile, four at a time
-      uint32_t segs = a.segmask[v * a.segmask_vstride + (size_t)nd.x * T + t];
+      uint32_t segs = (uint32_t)aux;
       int found = 0;
       while (segs && found < want) {
         int sj[4];
