@@ -183,6 +183,7 @@ def rank_views(args, d):
 CHUNK = 1024          # Gaussians per count row of the binning kernels
 PREFIX_CHUNKS = 32    # chunks binned exactly before saturation skipping
 CAP = 64              # tile list capacity
+GROUP_VIEWS = 256     # views per internal launch group of sarr_forward (kMaxViewsPerLaunch)
 
 
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one launch of
@@ -325,8 +326,8 @@ def bench_e2e(args, d, sc, views):
     dm = {k: torch.empty_like(v, device=dev) for k, v in h.items()}
     h_img = torch.empty((V, s, s), dtype=torch.float32).pin_memory()
     d_img = torch.empty((V, s, s), dtype=torch.float32, device=dev)
-    group = 128
-    ws = torch.empty(_native.workspace_bytes(n, s, s, 32), dtype=torch.uint8, device=dev)
+    group = GROUP_VIEWS
+    ws = torch.empty(_native.workspace_bytes(n, s, s, group), dtype=torch.uint8, device=dev)
     comp = torch.cuda.current_stream(dev)
     copy = torch.cuda.Stream(dev)
     flush = torch.empty((512 << 20) // 4, dtype=torch.float32, device=dev)
@@ -505,14 +506,11 @@ def config(args):
             "outputs": "images only (the SARRasterizer forward contract)"}
 
 
-GROUP_VIEWS = 32  # views per internal launch group of sarr_forward
-
-
 def path_roofline(args, r, world):
     """Whole-forward HBM rooflines per GPU. Per view: the 104 B of fp32
     parameters per Gaussian (means 12, cov6 24, transmittance 4, SH 64) read
     and the image written once per view. Batched: the parameters read once
-    per launch group of 32 views, the image once per view."""
+    per launch group of 256 views, the image once per view."""
     peak, peak_kind = peaks()
     n, npix = args.n, args.samples * args.samples
     vps = r["value"] / world

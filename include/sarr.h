@@ -77,7 +77,7 @@ const char *sarr_version(void);
 
 /*
  * Bytes of workspace needed to process up to `n_views` views of `n` Gaussians
- * per call (views are processed in groups of at most 32 per kernel launch; a
+ * per call (views are processed in groups of at most 256 per kernel launch; a
  * smaller workspace than the full request is fine as long as it holds one
  * view: the library then loops over smaller groups). Replaces the ~30
  * per-call cudaMalloc calls of CUDASARRenderer::render

@@ -33,7 +33,7 @@ constexpr int kXCap = kChunk;                    // exactly binned Gaussians lis
 constexpr int kSegMaskMaxTiles = 2048;           // prefix-chunk segment masks up to this many tiles
 constexpr int kWarpsPerTile = 8;                 // 8 warps x 32 pixels = one 16x16 tile
 constexpr int kMaxTilesAxis = 128;               // images up to 2048 x 2048
-constexpr int kMaxViewsPerLaunch = 32;
+constexpr int kMaxViewsPerLaunch = 256;
 constexpr uint32_t kEmptyRect = 0x000000FFu;     // tc0 = 255 > tc1 = 0
 
 // Device error bits (workspace error word).

@@ -139,7 +139,7 @@ def _views_from(views):
 def render_sar_batched(means_world, cov_world, transmittance, sh_coeffs, views, want_omega=False,
                        out=None, states=None):
     """Renders many views of one scene in a few launches (views are processed
-    up to 32 per kernel launch). `views`: SarrView, SARRasterizationSettings,
+    up to 256 per kernel launch). `views`: SarrView, SARRasterizationSettings,
     dicts or 10-tuples sharing range/azimuth samples. Returns images
     [V, range_samples, azimuth_samples] (each in the reference layout) and,
     with want_omega, omega [V, N]."""
