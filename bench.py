@@ -181,7 +181,7 @@ def rank_views(args, d):
 
 
 CHUNK = 1024          # Gaussians per count row of the binning kernels
-PREFIX_CHUNKS = 32    # chunks binned exactly before saturation skipping
+PREFIX_CHUNKS = 48    # chunks binned exactly before saturation skipping
 CAP = 64              # tile list capacity
 GROUP_VIEWS = 256     # views per internal launch group of sarr_forward (kMaxViewsPerLaunch)
 

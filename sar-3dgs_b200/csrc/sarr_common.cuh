@@ -28,7 +28,7 @@ constexpr int kBinPerThread = 4;                 // Gaussians per binning thread
 constexpr int kChunk = kBinThreads * kBinPerThread;  // Gaussians per count row
 constexpr int kSelectThreads = 128;
 constexpr int kScanThreads = 512;
-constexpr int kPrefixChunks = 32;                // chunks binned exactly before saturation skipping
+constexpr int kPrefixChunks = 48;                // chunks binned exactly before saturation skipping
 constexpr int kXCap = kChunk;                    // exactly binned Gaussians listed per skipped chunk
 constexpr int kSegMaskMaxTiles = 2048;           // prefix-chunk segment masks up to this many tiles
 constexpr int kWarpsPerTile = 8;                 // 8 warps x 32 pixels = one 16x16 tile

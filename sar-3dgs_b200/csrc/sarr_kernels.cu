@@ -24,8 +24,9 @@
 //                    again (SH only for them), ranked by (Z_r, index) and
 //                    stored as 48-byte records.
 //   render_kernel    one CTA per tile: TMA bulk copy of its sorted records,
-//                    front-to-back compositing by 8 x 4 pixel warp blocks that
-//                    skip records whose density is 0 on the whole block.
+//                    front-to-back compositing by 8 x 8 pixel warp blocks (two
+//                    pixels per lane) that skip records whose density is 0 on
+//                    the whole block.
 //   omega_tile_kernel / omega_scatter_kernel
 //                    per-pixel Omega walk with per-slot warp reductions, then
 //                    a per-Gaussian gather of those partial sums.
@@ -1247,11 +1248,27 @@ __device__ __forceinline__ float2 density_extent(const Rec& g) {
 }
 
 // One CTA per tile: the tile's sorted records arrive with one TMA bulk copy;
-// warp w composites an 8 (range) x 4 (azimuth) pixel block, lanes along range
-// (contiguous in the image). A record whose density box misses the whole
-// block is skipped by the warp: every pixel of the block would evaluate its
-// density to 0 (< 1e-8) and skip it too.
-__global__ void __launch_bounds__(kWarpsPerTile * 32) render_kernel(const TileArgs a) {
+// warp w composites an 8 x 8 pixel block, each lane two pixels of one range
+// row (azimuth columns c and c + 4; lanes along range, contiguous in the
+// image). A record whose density box misses the whole block is skipped by the
+// warp: every pixel of the block would evaluate its density to 0 (< 1e-8) and
+// skip it too. Each pixel's arithmetic is the reference's, record by record.
+constexpr int kRenderWarps = 4;
+
+__device__ __forceinline__ void composite_one(const Rec& g, float fx, float fy, float& value,
+                                              float& trans, bool& done) {
+  const float gamma_ipp = rec_density(g, fx, fy);
+  if (gamma_ipp < 1e-8f) return;
+  const float alpha_i = mul_(g.sigma, gamma_ipp);
+  value = fma_(mul_(trans, alpha_i), g.s_pos, value);
+  trans = mul_(trans, fma_(-g.sigma, gamma_ipp, 1.0f));
+  if (trans < 1e-8f) {
+    trans = 0.0f;
+    done = true;
+  }
+}
+
+__global__ void __launch_bounds__(kRenderWarps * 32) render_kernel(const TileArgs a) {
   __shared__ __align__(16) Rec s_rec[kCap];
   __shared__ float2 s_ext[kCap];
   __shared__ uint64_t bar;
@@ -1260,40 +1277,38 @@ __global__ void __launch_bounds__(kWarpsPerTile * 32) render_kernel(const TileAr
   const ViewConst& vc = a.views[v];
   const int Nr = vc.h.Nr, Na = vc.h.Na, tiles_x = vc.tiles_x;
   const int tx = t % tiles_x, ty = t / tiles_x;
-  const int r0 = ty * kTile + (warp & 1) * 8, c0 = tx * kTile + (warp >> 1) * 4;
-  const int pr = r0 + (lane & 7), pc = c0 + (lane >> 3);
-  const bool in = pc < Na && pr < Nr;
+  const int r0 = ty * kTile + (warp & 1) * 8, c0 = tx * kTile + (warp >> 1) * 8;
+  const int pr = r0 + (lane & 7), pc0 = c0 + (lane >> 3), pc1 = pc0 + 4;
   const unsigned char* st = a.st.base + v * a.st.vstride;
   const int count = reinterpret_cast<const int*>(st + a.st.L.count)[t];
 
-  float pixel_value = 0.0f;
+  float value0 = 0.0f, value1 = 0.0f;
   if (count > 0) {
     const bool ok = load_tile_recs(s_rec, &bar, st, a.st.L, t, count, a.err, true);
     if (ok)
-      for (int k = tid; k < count; k += kWarpsPerTile * 32) s_ext[k] = density_extent(s_rec[k]);
+      for (int k = tid; k < count; k += kRenderWarps * 32) s_ext[k] = density_extent(s_rec[k]);
     if (__syncthreads_and(ok)) {
-      float transmittance_acc = 1.0f;
-      const float fx = (float)pc, fy = (float)pr;
-      const float bx0 = (float)c0, bx1 = (float)(c0 + 3), by0 = (float)r0, by1 = (float)(r0 + 7);
+      float trans0 = 1.0f, trans1 = 1.0f;
+      bool done0 = false, done1 = false;
+      const float fy = (float)pr, fx0 = (float)pc0, fx1 = (float)pc1;
+      const float bx0 = (float)c0, bx1 = (float)(c0 + 7), by0 = (float)r0, by1 = (float)(r0 + 7);
       for (int k = 0; k < count; ++k) {
         const Rec& g = s_rec[k];
         const float2 e = s_ext[k];
         const float mdx = fmaxf(0.0f, fmaxf(bx0 - g.mx, g.mx - bx1));
         const float mdy = fmaxf(0.0f, fmaxf(by0 - g.my, g.my - by1));
         if (mdx > e.x || mdy > e.y) continue;  // the same for every lane
-        const float gamma_ipp = rec_density(g, fx, fy);
-        if (gamma_ipp < 1e-8f) continue;
-        const float alpha_i = mul_(g.sigma, gamma_ipp);
-        pixel_value = fma_(mul_(transmittance_acc, alpha_i), g.s_pos, pixel_value);
-        transmittance_acc = mul_(transmittance_acc, fma_(-g.sigma, gamma_ipp, 1.0f));
-        if (transmittance_acc < 1e-8f) {
-          transmittance_acc = 0.0f;
-          break;
-        }
+        if (!done0) composite_one(g, fx0, fy, value0, trans0, done0);
+        if (!done1) composite_one(g, fx1, fy, value1, trans1, done1);
+        if (done0 && done1) break;
       }
     }
   }
-  if (in) a.images[v * a.img_vstride + (size_t)pc * Nr + pr] = pixel_value;
+  float* img = a.images + v * a.img_vstride;
+  if (pr < Nr) {
+    if (pc0 < Na) img[(size_t)pc0 * Nr + pr] = value0;
+    if (pc1 < Na) img[(size_t)pc1 * Nr + pr] = value1;
+  }
 }
 
 // Omega per pixel (compute_omega_kernel :696-718): Omega_before of every
@@ -1792,7 +1807,7 @@ cudaError_t launch_select(const SelectArgs& a, const Dims& d, int nviews, bool s
 }
 
 cudaError_t launch_render(const TileArgs& a, const Dims& d, int nviews, cudaStream_t s) {
-  render_kernel<<<dim3(d.T, nviews), kWarpsPerTile * 32, 0, s>>>(a);
+  render_kernel<<<dim3(d.T, nviews), kRenderWarps * 32, 0, s>>>(a);
   return cudaGetLastError();
 }
 
