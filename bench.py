@@ -187,14 +187,12 @@ GROUP_VIEWS = 256     # views per internal launch group of sarr_forward (kMaxVie
 
 
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one launch of
-# 32 views, N = 1M, 256 x 256, from an ncu capture of that launch; they belong
-# to this workload and the current kernels only.
+# 256 views, N = 1M, 256 x 256, from an ncu capture of that launch; they
+# belong to this workload and the current kernels only.
 NCU_DRAM_BYTES_PER_LAUNCH = {
-    "bin_skip_kernel": 132_873_472,
-    "select_kernel": 43_704_832,
-    "render_kernel": 15_006_464,
-    "bin_kernel": 1_356_544,
+    "render_kernel": 118_437_376 + 37_822_000,
 }
+NCU_LAUNCH_VIEWS = 256
 
 
 def kernel_bytes_per_launch(kind, n, views, T, cov_floats, sh_floats, npix):
@@ -202,22 +200,21 @@ def kernel_bytes_per_launch(kind, n, views, T, cov_floats, sh_floats, npix):
     its compulsory reads and writes, each once.
       bin_kernel       the prefix chunks: means/cov/transmittance of their
                        Gaussians once; per view a 4 B tile rectangle per
-                       Gaussian and the u8 per-chunk tile counts.
-      bin_skip_kernel  the same over the remaining chunks.
+                       Gaussian, the u8 per-chunk tile counts and the 4 B
+                       per-chunk tile segment masks.
       select_kernel    per view and tile, the 64 selected Gaussians'
                        parameters (means, cov, transmittance, SH) gathered and
                        their 48 B records, list ids and (Y_r, Z_r) written.
       render_kernel    per view the 64 records of every tile read and the
-                       image written."""
+                       image written.
+    The cell binning kernels touch a view-dependent subset (the members of
+    candidate cells) and have no fixed model."""
     g_bytes = 4 * (3 + cov_floats + 1)
     C = -(-n // CHUNK)
     P = min(C, PREFIX_CHUNKS)
     n_p = min(n, P * CHUNK)
     if kind == "bin_kernel":
-        return g_bytes * n_p + views * (4 * n_p + P * T)
-    if kind == "bin_skip_kernel":
-        n_s = n - n_p
-        return g_bytes * n_s + views * (4 * n_s + (C - P) * T)
+        return g_bytes * n_p + views * (4 * n_p + P * T + 4 * P * T)
     if kind == "select_kernel":
         return views * T * CAP * (g_bytes + 4 * sh_floats + 48 + 4 + 8)
     if kind == "render_kernel":
@@ -297,8 +294,8 @@ def bench_ours(args, d):
                             "peak": peak, "peak_source": peak_kind, "unit": "GB/s",
                             "frac": round(achieved / peak, 4),
                             "traffic": (NCU_DRAM_BYTES_PER_LAUNCH.get(kname)
-                                        if n == 1_000_000 and s == 256 and per_launch_views == 32
-                                        else None),
+                                        if n == 1_000_000 and s == 256
+                                        and per_launch_views == NCU_LAUNCH_VIEWS else None),
                             "bytes_per_launch": int(b), "avg_launch_us": round(kms / klaunch * 1e3, 2)}
     dominant = max(prof.items(), key=lambda kv: kv[1][0])[0]
     roof = rooflines.get(dominant)

@@ -119,7 +119,7 @@ int sarr_forward(const sarr_view *views, int n_views, int64_t n, const float *me
 
 /*
  * sarr_forward for one view, image only, without a workspace argument: the
- * scratch is a 4.5 MiB array inside this library, one per device. No
+ * scratch is a 6 MiB array inside this library, one per device. No
  * counterpart in the reference. It is for callers that cannot allocate
  * device memory: a host whose device memory is all owned by another
  * allocator (a pool reserved at start-up) or a C/C++ caller with no device

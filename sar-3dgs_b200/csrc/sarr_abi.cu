@@ -309,6 +309,8 @@ cudaError_t run_selection(const Dims& d, const Ws& w, int gv, const float* means
   const int prefix = d.C > kPrefixChunks ? kPrefixChunks : d.C;
   ba.chunk_offset = 0;
   ba.views_per_cta = views_per_cta(prefix);
+  // one view per warp in the prefix binner once a CTA holds 8 views or more
+  if (ba.views_per_cta >= 8) ba.views_per_cta = (ba.views_per_cta + 7) / 8 * 8;
   cudaError_t e = run_kernel(kKindBin, s, [&] {
     return launch_bin(ba, d, prefix, shr != nullptr, false, s);
   });
@@ -339,9 +341,9 @@ cudaError_t run_selection(const Dims& d, const Ws& w, int gv, const float* means
       ct.shadow = shr != nullptr;
       ct.bits = reinterpret_cast<uint32_t*>(w.view_area() + w.L.bits);
       ct.bits_vstride = w.L.per_view / sizeof(uint32_t);
-      ct.xbits = reinterpret_cast<uint32_t*>(w.view_area() + w.L.xbits);
-      ct.xbits_vstride = w.L.per_view / sizeof(uint32_t);
-      ct.xbits_words = d.C * 32;
+      ct.ipp = ipp;
+      ct.sparse_from = (int64_t)prefix * kChunk;
+      ct.n = d.n;
       e = run_kernel(kKindAux, s, [&] { return launch_cell_test(ct, gv, s); });
       if (e != cudaSuccess) return e;
       ba.chunks = d.C - prefix;
@@ -352,8 +354,7 @@ cudaError_t run_selection(const Dims& d, const Ws& w, int gv, const float* means
       ba.always = reinterpret_cast<const int*>(w.base + w.L.always);
       ba.bits = ct.bits;
       ba.bits_vstride = ct.bits_vstride;
-      ba.xbits = ct.xbits;
-      ba.xbits_vstride = ct.xbits_vstride;
+
       e = run_kernel(kKindBinSkip, s, [&] { return launch_bin_cand(ba, shr != nullptr, s); });
       if (e != cudaSuccess) return e;
       e = run_kernel(kKindBinFinalize, s, [&] { return launch_bin_finalize(ba, d, shr != nullptr, s); });
@@ -548,6 +549,7 @@ int sarr_forward(const sarr_view* views, int n_views, int64_t n, const float* me
       os.views = w.views;
       os.n = d.n;
       os.sh = shr;
+      os.ipp = ipp;
       os.partial = to.partial;
       os.partial_vstride = to.partial_vstride;
       os.omega = omega + (size_t)g0 * d.n;

@@ -28,8 +28,11 @@ struct Dims {
 //   list   [T][64]   Gaussian ids in index order (the reference's tile list)
 //   yz     [T][64]   (Y_r, Z_r) of list slot s (backward chain)
 //   recs   [T][64]   Rec in compositing (Z_r, index) order
+//   xbits  [n/32] u32 bit i: Gaussian i was binned exactly (cell binning)
+//   meta   int64     first Gaussian whose rectangle is valid only when its
+//                    xbits bit is set (INT64_MAX: every rectangle is valid)
 struct StateLayout {
-  size_t rects, count, list, yz, recs, bytes;
+  size_t rects, count, list, yz, recs, xbits, meta, bytes;
 };
 
 __host__ __device__ inline StateLayout state_layout(int64_t n, int T) {
@@ -45,8 +48,24 @@ __host__ __device__ inline StateLayout state_layout(int64_t n, int T) {
   o += align256((size_t)T * kCap * 8);
   L.recs = o;
   o += align256((size_t)T * kCap * sizeof(Rec));
+  L.xbits = o;
+  o += align256((size_t)(n + 31) / 32 * 4);
+  L.meta = o;
+  o += 256;
   L.bytes = o;
   return L;
+}
+
+// Tile rectangle of Gaussian i in a state whose exactness bits are those of
+// `xs` (the image-plane state of the same view).
+__device__ __forceinline__ uint32_t state_rect(const unsigned char* st, const StateLayout& L,
+                                               const unsigned char* xs, const StateLayout& XL,
+                                               int64_t i) {
+  const int64_t sparse_from = *reinterpret_cast<const int64_t*>(xs + XL.meta);
+  if (i >= sparse_from &&
+      !((reinterpret_cast<const uint32_t*>(xs + XL.xbits)[i >> 5] >> (i & 31)) & 1u))
+    return kEmptyRect;
+  return reinterpret_cast<const uint32_t*>(st + L.rects)[i];
 }
 
 // Workspace: [ViewConst x 32][error word][per-view areas x group]
@@ -62,14 +81,13 @@ __host__ __device__ inline StateLayout state_layout(int64_t n, int T) {
 // member lists (Gaussians after the prefix, cell by cell: cell_start
 // [kMaxCells + 1], mem_pos [n] float4 = centre and bound, mem_idx [n]), the
 // Gaussians after the prefix that are in no cell (always [n]), and each view
-// area its cell bitmap bits [kCellWords] u32 and its exactly-binned bitmap
-// xbits [C][32] u32.
+// area its cell bitmap bits [kCellWords] u32.
 struct WsLayout {
   size_t viewconst, err, scene, hb, cid, cell_hb, cell_count, cell_start, cell_center, mem_pos, mem_idx,
       always, head;
   size_t counts_ipp, counts_sh, need_ipp, need_sh, need_n_ipp, need_n_sh, open_ipp, open_sh;
-  size_t bits, xbits, xcount, xlist, segmask_ipp, segmask_sh, state_ipp, state_sh, partial_om,
-      partial_bwd, per_view;
+  size_t bits, xcount, xlist, segmask_ipp, segmask_sh, state_ipp, state_sh, partial_om, partial_bwd,
+      per_view;
   bool cells;
   StateLayout st;
 };
@@ -143,12 +161,9 @@ __host__ inline WsLayout ws_layout(const Dims& d, bool cells) {
   L.xlist = o;
   o += align256((size_t)d.C * kXCap * 2);
   L.bits = 0;
-  L.xbits = 0;
   if (cells) {
     L.bits = o;
     o += align256((size_t)kCellWords * 4);
-    L.xbits = o;
-    o += align256((size_t)d.C * 32 * 4);
   }
   L.state_ipp = o;
   o += L.st.bytes;
@@ -192,8 +207,7 @@ struct BinArgs {
   const int* always;
   const uint32_t* bits;  // cell bitmaps, bits_vstride words per view
   size_t bits_vstride;
-  uint32_t* xbits;       // exactly-binned bitmaps [C][32] per view
-  size_t xbits_vstride;  // words
+  // exactly-binned bitmaps: the xbits of the image-plane states (ipp)
   int64_t n;
   int C;
   const float* means;
@@ -239,9 +253,9 @@ struct CellTestArgs {
   int shadow;
   uint32_t* bits;
   size_t bits_vstride;
-  uint32_t* xbits;       // exactly-binned bitmaps to clear, xbits_words per view
-  size_t xbits_vstride;  // words
-  int xbits_words;
+  StateRef ipp;          // its xbits are cleared and its meta set (sparse rectangles)
+  int64_t sparse_from;   // first Gaussian after the prefix
+  int64_t n;
 };
 
 struct SelectArgs {
@@ -304,6 +318,7 @@ struct OmegaScatterArgs {
   const ViewConst* views;
   int64_t n;
   StateRef sh;
+  StateRef ipp;  // exactness bits of the rectangles
   const float* partial;
   size_t partial_vstride;
   float* omega;

@@ -213,6 +213,10 @@ __global__ void __launch_bounds__(kBinThreads) bin_kernel(const BinArgs a) {
     uint32_t* rects_ipp = reinterpret_cast<uint32_t*>(a.ipp.base + v * a.ipp.vstride + a.ipp.L.rects);
     uint32_t* rects_sh =
         kShadow ? reinterpret_cast<uint32_t*>(a.sh.base + v * a.sh.vstride + a.sh.L.rects) : nullptr;
+    // every rectangle of the view is written (cell binning marks its state
+    // sparse afterwards)
+    if (!kSkip && chunk == 0 && tid == 0)
+      *reinterpret_cast<int64_t*>(a.ipp.base + v * a.ipp.vstride + a.ipp.L.meta) = INT64_MAX;
 
     if (kSkip) {
       // stage 1: cheap conservative test for every Gaussian
@@ -355,6 +359,19 @@ __device__ __forceinline__ void count_rect(uint32_t* cnt, uint32_t rc, int tiles
     }
 }
 
+// ORs `bit` into a warp's tile masks over a rectangle. Only one warp writes
+// these masks and its lanes OR the same bit between two __syncwarp, so plain
+// read-modify-writes give the same result in any interleaving.
+__device__ __forceinline__ void or_rect(uint32_t* mask, uint32_t rc, int tiles_x, uint32_t bit) {
+  if (rc == kEmptyRect) return;
+  const int tc0 = rc & 0xFF, tc1 = (rc >> 8) & 0xFF, tr0 = (rc >> 16) & 0xFF, tr1 = rc >> 24;
+  for (int ty = tr0; ty <= tr1; ++ty)
+    for (int tx = tc0; tx <= tc1; ++tx) {
+      volatile uint32_t* m = mask + ty * tiles_x + tx;
+      *m = *m | bit;
+    }
+}
+
 // Writes a warp's tile counters of one view and chunk as saturating u8 counts
 // and clears them for the next view.
 __device__ __forceinline__ void flush_counts(uint32_t* cnt, uint8_t* out, int T, int lane) {
@@ -372,6 +389,116 @@ __device__ __forceinline__ void flush_counts(uint32_t* cnt, uint8_t* out, int T,
   __syncwarp();
   for (int i = lane; i < ((T + 1) >> 1); i += 32) cnt[i] = 0;
   __syncwarp();
+}
+
+// Prefix chunks, one view per warp: every Gaussian of the staged chunk is
+// binned exactly by the warp of its view (32 per round), its hits counted in
+// per-warp 16-bit tile counters and, for the segment masks, the round's bit
+// ORed into per-warp tile masks (all lanes of a round OR the same bit, so the
+// plain read-modify-write is exact). No CTA barrier inside the view loop.
+// Means and transmittances are staged; covariances are read through L1.
+template <bool kShadow>
+__global__ void __launch_bounds__(kBinThreads, 3) bin_prefix_kernel(const BinArgs a) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  __shared__ uint64_t bar;
+  constexpr int kWarps = kBinThreads / 32;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int chunk = blockIdx.x + a.chunk_offset;
+  const int tiles_x = a.views[0].tiles_x, tiles_y = a.views[0].tiles_y, T = tiles_x * tiles_y;
+  const int TW = (T + 1) >> 1;
+  const int cs = a.cov_layout;
+  const int lists = kShadow ? 2 : 1;
+  const bool masks = a.segmask != nullptr;
+
+  float* s_means = reinterpret_cast<float*>(smem_raw);
+  float* s_sigma = s_means + 3 * kChunk;
+  uint32_t* s_cnt = reinterpret_cast<uint32_t*>(s_sigma + kChunk) + warp * (TW + T) * lists;
+  uint32_t* s_cnt_sh = s_cnt + TW;
+  uint32_t* s_mask = s_cnt + TW * lists;
+  uint32_t* s_mask_sh = s_mask + T;
+
+  const int64_t base = (int64_t)chunk * kChunk;
+  const int gcount = (int)min((int64_t)kChunk, a.n - base);
+  {
+    const bool tma = a.use_tma && gcount == kChunk;
+    if (tid == 0 && tma) mbar_init(&bar, 1);
+    __syncthreads();
+    bool ok = true;
+    if (tma) {
+      if (tid == 0) {
+        mbar_arrive_expect_tx(&bar, 4u * kChunk * 4u);
+        tma_load_1d(s_means, a.means + base * 3, 3u * kChunk * 4u, &bar);
+        tma_load_1d(s_sigma, a.sigma + base, kChunk * 4u, &bar);
+      }
+      ok = mbar_wait_bounded(&bar, 0, a.err);
+    } else {
+      for (int i = tid; i < 3 * gcount; i += kBinThreads) s_means[i] = a.means[base * 3 + i];
+      for (int i = tid; i < gcount; i += kBinThreads) s_sigma[i] = a.sigma[base + i];
+    }
+    if (!__syncthreads_and(ok)) return;
+  }
+  for (int i = lane; i < (TW + T) * lists; i += 32) s_cnt[i] = 0;
+  __syncwarp();
+  const float* cov = a.cov + base * cs;
+
+  const int v_end = min(a.nviews, (int)(blockIdx.y + 1) * a.views_per_cta);
+  for (int v = blockIdx.y * a.views_per_cta + warp; v < v_end; v += kWarps) {
+    const ViewConst& vg = a.views[v];
+    unsigned char* stv = a.ipp.base + v * a.ipp.vstride;
+    uint32_t* rects_ipp = reinterpret_cast<uint32_t*>(stv + a.ipp.L.rects) + base;
+    uint32_t* rects_sh =
+        kShadow ? reinterpret_cast<uint32_t*>(a.sh.base + v * a.sh.vstride + a.sh.L.rects) + base : nullptr;
+    // every rectangle of the view is written (cell binning marks its state
+    // sparse afterwards)
+    if (chunk == 0 && lane == 0) *reinterpret_cast<int64_t*>(stv + a.ipp.L.meta) = INT64_MAX;
+    for (int r = 0; r < kChunk / 32; ++r) {
+      const int j = r * 32 + lane;
+      if (j < gcount) {
+        uint32_t rc_ipp = kEmptyRect, rc_sh = kEmptyRect;
+        if (!(s_sigma[j] < 0.01f)) {  // preprocess_kernel: transmittance < 0.01 -> invalid (:351)
+          Proj o;
+          const float Rmin = project_center(vg, s_means[3 * j], s_means[3 * j + 1], s_means[3 * j + 2], o);
+          if (proj_valid(o, vg.h.Nr, vg.h.Na)) {
+            float cw[6], X6[6];
+            load_cov6(cov + j * cs, cs, cw);
+            radar_cov(vg, cw, X6);
+            image_cov(vg, X6, Rmin, o);
+            int r0, r1, c0, c1;
+            ipp_ranges(o, vg.h.Nr, vg.h.Na, r0, r1, c0, c1);
+            rc_ipp = make_rect(r0, r1, c0, c1, vg.h.Nr, vg.h.Na);
+            if (kShadow && shadow_ranges(o, vg.h.Nr, vg.h.Na, r0, r1, c0, c1))
+              rc_sh = make_rect(r0, r1, c0, c1, vg.h.Nr, vg.h.Na);
+          }
+        }
+        rects_ipp[j] = rc_ipp;
+        count_rect(s_cnt, rc_ipp, tiles_x);
+        if (masks) or_rect(s_mask, rc_ipp, tiles_x, 1u << r);
+        if (kShadow) {
+          rects_sh[j] = rc_sh;
+          count_rect(s_cnt_sh, rc_sh, tiles_x);
+          if (masks) or_rect(s_mask_sh, rc_sh, tiles_x, 1u << r);
+        }
+      }
+      __syncwarp();  // the next round ORs another bit into the same masks
+    }
+    flush_counts(s_cnt, a.counts_ipp + v * a.counts_vstride + (size_t)chunk * T, T, lane);
+    if (kShadow) flush_counts(s_cnt_sh, a.counts_sh + v * a.counts_vstride + (size_t)chunk * T, T, lane);
+    if (masks) {
+      uint32_t* m = a.segmask + v * a.segmask_vstride + (size_t)chunk * T;
+      for (int t = lane; t < T; t += 32) {
+        m[t] = s_mask[t];
+        s_mask[t] = 0;
+      }
+      if (kShadow) {
+        uint32_t* msh = a.segmask_sh + v * a.segmask_vstride + (size_t)chunk * T;
+        for (int t = lane; t < T; t += 32) {
+          msh[t] = s_mask_sh[t];
+          s_mask_sh[t] = 0;
+        }
+      }
+    }
+    __syncwarp();
+  }
 }
 
 // Saturation-skipping binning of the chunks after the prefix, one view per
@@ -705,8 +832,12 @@ __global__ void __launch_bounds__(256) cell_test_kernel(const CellTestArgs a) {
   }
   const unsigned m = __ballot_sync(0xffffffffu, open);
   if ((threadIdx.x & 31) == 0) a.bits[v * a.bits_vstride + (c >> 5)] = m;
-  for (int i = blockIdx.x * 256 + threadIdx.x; i < a.xbits_words; i += gridDim.x * 256)
-    a.xbits[v * a.xbits_vstride + i] = 0;
+  unsigned char* xs = a.ipp.base + v * a.ipp.vstride;
+  uint32_t* xbits = reinterpret_cast<uint32_t*>(xs + a.ipp.L.xbits);
+  const int64_t words = (a.n + 31) / 32;
+  for (int64_t i = blockIdx.x * 256 + threadIdx.x; i < words; i += (int64_t)gridDim.x * 256) xbits[i] = 0;
+  if (blockIdx.x == 0 && threadIdx.x == 0)
+    *reinterpret_cast<int64_t*>(xs + a.ipp.L.meta) = a.sparse_from;
 }
 
 // Cell binning, part 1 (per view): the members of the view's candidate cells
@@ -723,7 +854,7 @@ __global__ void __launch_bounds__(kBinThreads) bin_cand_kernel(const BinArgs a) 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int v = blockIdx.y;
   const SceneGrid& g = *a.grid;
-  uint32_t* xbits = a.xbits + v * a.xbits_vstride;
+  uint32_t* xbits = reinterpret_cast<uint32_t*>(a.ipp.base + v * a.ipp.vstride + a.ipp.L.xbits);
   const int cell_blocks = kMaxCells / (kWarps * 32);
   if ((int)blockIdx.x < cell_blocks) {
     if (!g.valid) return;
@@ -781,8 +912,7 @@ __global__ void __launch_bounds__(kBinThreads) bin_cand_kernel(const BinArgs a) 
 
 // Cell binning, part 2: one warp per (view, chunk after the prefix). The
 // Gaussians whose bits are set are listed in index order and binned exactly
-// (32 lanes at a time), every other Gaussian of the chunk gets empty
-// rectangles, and the chunk's tile counts are written.
+// (32 lanes at a time), and the chunk's tile counts are written.
 template <bool kShadow>
 __global__ void __launch_bounds__(kBinThreads) bin_finalize_kernel(const BinArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -802,7 +932,8 @@ __global__ void __launch_bounds__(kBinThreads) bin_finalize_kernel(const BinArgs
   const ViewConst& vg = a.views[v];
 
   for (int i = lane; i < TW * (kShadow ? 2 : 1); i += 32) s_cnt[i] = 0;
-  const uint32_t word = a.xbits[v * a.xbits_vstride + (size_t)chunk * 32 + lane];
+  const uint32_t* xbits = reinterpret_cast<const uint32_t*>(a.ipp.base + v * a.ipp.vstride + a.ipp.L.xbits);
+  const uint32_t word = base + lane * 32 < a.n ? xbits[(size_t)chunk * 32 + lane] : 0u;
   const int cnt = __popc(word);
   const int excl = warp_incl_scan(cnt, lane) - cnt;
   const int total = __shfl_sync(0xffffffffu, excl + cnt, 31);
@@ -834,15 +965,8 @@ __global__ void __launch_bounds__(kBinThreads) bin_finalize_kernel(const BinArgs
       count_rect(s_cnt_sh, rc_sh, tiles_x);
     }
   }
-  // every other Gaussian of the chunk: empty rectangles (coalesced)
-  for (int kk = 0; kk < 32; ++kk) {
-    const uint32_t wk = __shfl_sync(0xffffffffu, word, kk);
-    const int jl = kk * 32 + lane;
-    if (jl < gcount && !((wk >> lane) & 1u)) {
-      rects_ipp[jl] = kEmptyRect;
-      if (kShadow) rects_sh[jl] = kEmptyRect;
-    }
-  }
+  // the other Gaussians' rectangles are left unwritten: the state's meta and
+  // exactness bits mark them empty
   __syncwarp();
   flush_counts(s_cnt, a.counts_ipp + v * a.counts_vstride + (size_t)chunk * T, T, lane);
   if (kShadow) flush_counts(s_cnt_sh, a.counts_sh + v * a.counts_vstride + (size_t)chunk * T, T, lane);
@@ -1390,7 +1514,7 @@ __global__ void __launch_bounds__(256) omega_scatter_kernel(const OmegaScatterAr
   const ViewConst& vc = a.views[v];
   const int tiles_x = vc.tiles_x;
   const unsigned char* st = a.sh.base + v * a.sh.vstride;
-  const uint32_t rc = reinterpret_cast<const uint32_t*>(st + a.sh.L.rects)[i];
+  const uint32_t rc = state_rect(st, a.sh.L, a.ipp.base + v * a.ipp.vstride, a.ipp.L, i);
   float s = 0.0f, c = 0.0f;
   const int tc0 = rc & 0xFF, tc1 = (rc >> 8) & 0xFF, tr0 = (rc >> 16) & 0xFF, tr1 = rc >> 24;
   if (tc0 <= tc1) {
@@ -1521,7 +1645,7 @@ __global__ void __launch_bounds__(256) bwd_scatter_kernel(const BwdScatterArgs a
     const ViewConst& vc = a.views[v];
     const int tiles_x = vc.tiles_x;
     const unsigned char* st = a.ipp.base + v * a.ipp.vstride;
-    const uint32_t rc = reinterpret_cast<const uint32_t*>(st + a.ipp.L.rects)[i];
+    const uint32_t rc = state_rect(st, a.ipp.L, st, a.ipp.L, i);
     const int tc0 = rc & 0xFF, tc1 = (rc >> 8) & 0xFF, tr0 = (rc >> 16) & 0xFF, tr1 = rc >> 24;
     if (tc0 > tc1) continue;
     const int* cnts = reinterpret_cast<const int*>(st + a.ipp.L.count);
@@ -1711,9 +1835,31 @@ static void launch_bin_t(const BinArgs& a, dim3 grid, size_t smem, cudaStream_t 
   bin_kernel<kShadow, kSkip><<<grid, kBinThreads, smem, s>>>(a);
 }
 
+// bin_prefix_kernel: staged means + transmittances, per-warp counters and
+// segment masks; larger tile grids use the CTA-wide bin_kernel.
+constexpr size_t kPrefixWarpBytes = 48 * 1024;
+static size_t prefix_warp_bytes(const Dims& d, bool shadow) {
+  return (size_t)(kBinThreads / 32) * ((d.T + 1) / 2 + d.T) * 4 * (shadow ? 2 : 1);
+}
+
+template <bool kShadow>
+static void launch_bin_prefix_t(const BinArgs& a, dim3 grid, size_t smem, cudaStream_t s) {
+  if (needs_smem_attr(smem))
+    cudaFuncSetAttribute(bin_prefix_kernel<kShadow>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)smem);
+  bin_prefix_kernel<kShadow><<<grid, kBinThreads, smem, s>>>(a);
+}
+
 cudaError_t launch_bin(const BinArgs& a, const Dims& d, int chunks, bool shadow, bool skip,
                        cudaStream_t s) {
   const dim3 grid(chunks, (a.nviews + a.views_per_cta - 1) / a.views_per_cta);
+  // one view per warp needs views to fill the CTA's warps
+  if (!skip && a.views_per_cta >= kBinThreads / 32 && prefix_warp_bytes(d, shadow) <= kPrefixWarpBytes) {
+    const size_t smem = (size_t)4 * kChunk * 4 + prefix_warp_bytes(d, shadow);
+    if (shadow) launch_bin_prefix_t<true>(a, grid, smem, s);
+    else launch_bin_prefix_t<false>(a, grid, smem, s);
+    return cudaGetLastError();
+  }
   if (skip && skip_bin_per_warp(d, shadow)) {
     const size_t smem = bin_skip_smem_bytes(d, a.cov_layout, shadow);
     if (shadow) launch_bin_skip_t<true>(a, grid, smem, s);

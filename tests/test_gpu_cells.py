@@ -102,3 +102,13 @@ def test_cell_culling_backward_equals_sum_of_single_views():
     for i in range(4):
         total = sum(s[i] for s in single)
         assert rel_linf(grads[i].cpu().numpy(), total.cpu().numpy()) <= 1e-5
+    # the backward reusing the forward's states (sparse rectangles) agrees
+    n = sc["means"].shape[0]
+    sbytes = _native.state_bytes(n, views[0][8], views[0][9])
+    states = torch.empty(len(views) * sbytes, dtype=torch.uint8, device="cuda")
+    batch2 = M.render_sar_batched(sc["means"], sc["cov6"], sc["sigma"], sc["sh"], views, states=states)
+    assert torch.equal(batch2, batch)
+    grads3 = M.render_sar_backward_batched(sc["means"], sc["cov6"], sc["sigma"], sc["sh"], gimg, views,
+                                           states=states)
+    for i in range(4):
+        assert torch.equal(grads3[i], grads[i])
