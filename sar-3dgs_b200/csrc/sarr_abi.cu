@@ -227,14 +227,9 @@ cudaError_t setup_views(const sarr_view* views, int g0, int gv, const Ws& w, boo
   memset(&pack, 0, sizeof(pack));
   pack.n = gv;
   for (int v = 0; v < gv; ++v) view_host(views[g0 + v], pack.v[v]);
-  if (clear_err) {
-    const cudaError_t e = run_kernel(kKindSetup, s, [&] {
-      clear_err_kernel<<<1, 1, 0, s>>>(w.err);
-      return cudaGetLastError();
-    });
-    if (e != cudaSuccess) return e;
-  }
-  return run_kernel(kKindSetup, s, [&] { return launch_view_setup(pack, w.views, s); });
+  return run_kernel(kKindSetup, s, [&] {
+    return launch_view_setup(pack, w.views, clear_err ? w.err : nullptr, s);
+  });
 }
 
 // The view-independent cell grid of a call (cell culling), before its groups.
@@ -287,6 +282,12 @@ cudaError_t run_selection(const Dims& d, const Ws& w, int gv, const float* means
   ba.segmask = masks ? reinterpret_cast<uint32_t*>(w.view_area() + w.L.segmask_ipp) : nullptr;
   ba.segmask_sh = masks ? reinterpret_cast<uint32_t*>(w.view_area() + w.L.segmask_sh) : nullptr;
   ba.segmask_vstride = w.L.per_view / sizeof(uint32_t);
+  // the per-view skipping binner also writes the masks of its chunks when
+  // every chunk has room for them (few views: select_kernel then batches the
+  // hit segments of all need entries); cell binning lists the exactly binned
+  // Gaussians per chunk instead, which costs the many-view forward less
+  const bool masks_all = masks && segmask_all_chunks(d) && !w.L.cells && skip_bin_per_warp(d, shr != nullptr);
+  ba.skip_masks = masks_all ? 1 : 0;
   ba.xcount = reinterpret_cast<int*>(w.view_area() + w.L.xcount);
   ba.xlist = reinterpret_cast<uint16_t*>(w.view_area() + w.L.xlist);
   ba.x_vstride = w.L.per_view;
@@ -401,9 +402,10 @@ cudaError_t run_selection(const Dims& d, const Ws& w, int gv, const float* means
   // the skipping binners record each chunk's exactly binned Gaussians, except
   // the CTA-wide variant for very large tile grids
   const bool xlists = prefix < d.C && (w.L.cells || skip_bin_per_warp(d, shr != nullptr));
+  sa.xs = ipp;
   sa.segmask = ba.segmask;
   sa.segmask_vstride = ba.segmask_vstride;
-  sa.segmask_to = prefix;
+  sa.segmask_to = masks_all ? d.C : prefix;
   sa.xlist_from = xlists ? prefix : INT32_MAX;
   sa.xcount = xlists ? ba.xcount : nullptr;
   sa.xlist = xlists ? ba.xlist : nullptr;

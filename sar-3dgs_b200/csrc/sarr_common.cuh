@@ -31,6 +31,7 @@ constexpr int kScanThreads = 512;
 constexpr int kPrefixChunks = 48;                // chunks binned exactly before saturation skipping
 constexpr int kXCap = kChunk;                    // exactly binned Gaussians listed per skipped chunk
 constexpr int kSegMaskMaxTiles = 2048;           // prefix-chunk segment masks up to this many tiles
+constexpr int kSegMaskAllMaxTiles = 512;         // segment masks of every chunk up to this many tiles
 constexpr int kWarpsPerTile = 8;                 // 8 warps x 32 pixels = one 16x16 tile
 constexpr int kMaxTilesAxis = 128;               // images up to 2048 x 2048
 constexpr int kMaxViewsPerLaunch = 256;

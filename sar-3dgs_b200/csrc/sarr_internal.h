@@ -150,12 +150,14 @@ __host__ inline WsLayout ws_layout(const Dims& d, bool cells) {
   // Per chunk after the prefix: how many of its Gaussians the skipping binner
   // binned exactly (-1: more than kXCap, or not recorded) and their chunk
   // offsets in index order; select_kernel scans only those.
-  // Per prefix chunk and tile: which 32-Gaussian segments of the chunk hold
-  // hits of the tile (select_kernel reads only those).
+  // Per chunk and tile: which 32-Gaussian segments of the chunk hold hits of
+  // the tile (select_kernel reads only those); for every chunk up to
+  // kSegMaskAllMaxTiles tiles, for the prefix chunks otherwise.
+  const size_t mchunks = d.T <= kSegMaskAllMaxTiles ? (size_t)d.C : (size_t)kPrefixChunks;
   L.segmask_ipp = o;
-  o += align256((size_t)kPrefixChunks * d.T * 4);
+  o += align256(mchunks * d.T * 4);
   L.segmask_sh = o;
-  o += align256((size_t)kPrefixChunks * d.T * 4);
+  o += align256(mchunks * d.T * 4);
   L.xcount = o;
   o += align256((size_t)d.C * 4);
   L.xlist = o;
@@ -192,7 +194,8 @@ struct BinArgs {
   const int* open_ipp;  // open-tile summed-area tables (skip variant), open_vstride ints per view
   const int* open_sh;
   size_t open_vstride;
-  uint32_t* segmask;     // prefix variant: segment masks [chunk][T] (null: none)
+  uint32_t* segmask;     // segment masks [chunk][T] (null: none)
+  int skip_masks;        // the skipping binners write the masks of their chunks too
   uint32_t* segmask_sh;
   size_t segmask_vstride;  // words per view
   int* xcount;         // exactly binned Gaussians per chunk (skip variants)
@@ -277,6 +280,7 @@ struct SelectArgs {
   const uint32_t* segmask;    // segment masks of chunks < segmask_to (null: none)
   size_t segmask_vstride;     // words
   int segmask_to;
+  StateRef xs;                // image-plane states: exactness bits and meta of the rectangles
   int xlist_from;             // first chunk with an exact list (INT32_MAX: none)
   const int* xcount;
   const uint16_t* xlist;
@@ -365,7 +369,9 @@ struct DebugListArgs {
 };
 
 // Launch wrappers; each returns the cudaError_t of the launch.
-cudaError_t launch_view_setup(const ViewHostPack& pack, ViewConst* out, cudaStream_t s);
+// view constants of a group (and, when err_to_clear is set, the error word cleared)
+cudaError_t launch_view_setup(const ViewHostPack& pack, ViewConst* out, int* err_to_clear,
+                              cudaStream_t s);
 // bin_kernel over chunks [a.chunk_offset, a.chunk_offset + chunks)
 cudaError_t launch_bin(const BinArgs& a, const Dims& d, int chunks, bool shadow, bool skip,
                        cudaStream_t s);
@@ -382,6 +388,7 @@ bool bin_cell_supported(const Dims& d);
 // exact lists); false selects its CTA-wide variant
 bool skip_bin_per_warp(const Dims& d, bool shadow);
 bool segmask_supported(const Dims& d);
+bool segmask_all_chunks(const Dims& d);
 cudaError_t launch_scan(const ScanArgs& a, int nviews, cudaStream_t s);
 cudaError_t launch_select(const SelectArgs& a, const Dims& d, int nviews, bool shadow_list,
                           cudaStream_t s);

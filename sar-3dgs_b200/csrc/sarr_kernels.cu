@@ -43,15 +43,14 @@ namespace sarr {
 // ---------------------------------------------------------------------------
 // view setup
 // ---------------------------------------------------------------------------
-__global__ void view_setup_kernel(const ViewHostPack pack, ViewConst* __restrict__ out) {
-  const int v = threadIdx.x;
+// The pack is a __grid_constant__ parameter: indexed in place, not copied.
+__global__ void view_setup_kernel(const __grid_constant__ ViewHostPack pack,
+                                  ViewConst* __restrict__ out, int* err) {
+  const int v = blockIdx.x * blockDim.x + threadIdx.x;
+  if (err && v == 0) *err = 0;
   if (v >= pack.n) return;
   ViewConst c;
-  // static indices into the parameter block (a dynamic one would copy the
-  // whole block to local memory in every thread)
-#pragma unroll
-  for (int i = 0; i < kMaxViewsPerLaunch; ++i)
-    if (i == v) c.h = pack.v[i];
+  c.h = pack.v[v];
   c.cos_a = cosf(c.h.alpha);
   c.sin_a = sinf(c.h.alpha);
   c.cos_b = cosf(c.h.beta);
@@ -501,10 +500,25 @@ __global__ void __launch_bounds__(kBinThreads, 3) bin_prefix_kernel(const BinArg
   }
 }
 
-// Saturation-skipping binning of the chunks after the prefix, one view per
-// warp at a time. The chunk is staged once per CTA (with the view-independent
-// bbox bounds); each warp then bins its views alone, with no CTA barrier:
-// a conservative test of every Gaussian (approximate centre, bbox bound,
+// Writes a warp's tile segment masks of one view and chunk and clears them.
+// Only nonzero masks are written: select_kernel reads the mask of a (chunk,
+// tile) only when the chunk holds hits of the tile.
+__device__ __forceinline__ void flush_masks(uint32_t* mask, uint32_t* out, int T, int lane) {
+  for (int t = lane; t < T; t += 32) {
+    const uint32_t m = mask[t];
+    if (m) {
+      out[t] = m;
+      mask[t] = 0;
+    }
+  }
+  __syncwarp();
+}
+
+// Saturation-skipping binning of the chunks after the prefix. The chunk is
+// staged once per CTA (with the view-independent bbox bounds); with more than
+// four views per CTA each warp then bins whole views alone, with no CTA
+// barrier, and with fewer the warps of a view split the chunk into slices.
+// A conservative test of every Gaussian (approximate centre, bbox bound,
 // open-tile table) writes empty rectangles for those that can only reach
 // saturated tiles, the others go to a warp queue that is drained 32 at a time
 // by exact binning, and the hits land in per-warp tile counters.
@@ -527,12 +541,20 @@ __global__ void __launch_bounds__(kBinThreads, 3) bin_skip_kernel(const BinArgs 
   float* s_hb = s_sigma + kChunk;
   uint32_t* s_cnt = reinterpret_cast<uint32_t*>(s_hb + kChunk) + warp * TW * (kShadow ? 2 : 1);
   uint32_t* s_cnt_sh = s_cnt + TW;
+  // segment masks (when a.skip_masks): bit s of tile t is set when Gaussians
+  // [32 s, 32 s + 32) of the chunk hold a hit of t
+  const bool masks = a.skip_masks != 0;
+  uint32_t* s_mask = reinterpret_cast<uint32_t*>(s_hb + kChunk) + kWarps * TW * (kShadow ? 2 : 1) +
+                     warp * T * (kShadow ? 2 : 1);
+  uint32_t* s_mask_sh = s_mask + T;
 
   const int64_t base = (int64_t)chunk * kChunk;
   const int gcount = (int)min((int64_t)kChunk, a.n - base);
   if (!stage_chunk(a, base, gcount, s_means, s_cov, s_sigma, &bar)) return;
 
   for (int i = lane; i < TW * (kShadow ? 2 : 1); i += 32) s_cnt[i] = 0;
+  if (masks)
+    for (int i = lane; i < T * (kShadow ? 2 : 1); i += 32) s_mask[i] = 0;
   for (int j = tid; j < gcount; j += kBinThreads) {
     float cw[6];
     load_cov6(s_cov + j * cs, cs, cw);
@@ -543,8 +565,11 @@ __global__ void __launch_bounds__(kBinThreads, 3) bin_skip_kernel(const BinArgs 
   const int pitch = tiles_x + 1;
   const unsigned lt_mask = (1u << lane) - 1u;
   short* queue = s_queue[warp];
-  const int v_end = min(a.nviews, (int)(blockIdx.y + 1) * a.views_per_cta);
-  for (int v = blockIdx.y * a.views_per_cta + warp; v < v_end; v += kWarps) {
+
+  // Bins Gaussians [j_lo, j_hi) of the chunk for view v into this warp's
+  // counters; the exactly binned ones are listed (index order) in xl[0..).
+  // Returns how many were listed.
+  auto bin_range = [&](int v, int j_lo, int j_hi, uint16_t* xl) {
     const ViewConst& vg = a.views[v];  // exact binning reads its constants from here (L1)
     const ViewConst vc = vg;            // the stage-1 constants, held in registers
     const int Nr = vc.h.Nr, Na = vc.h.Na;
@@ -553,27 +578,26 @@ __global__ void __launch_bounds__(kBinThreads, 3) bin_skip_kernel(const BinArgs 
         kShadow ? reinterpret_cast<uint32_t*>(a.sh.base + v * a.sh.vstride + a.sh.L.rects) + base : nullptr;
     const int* open_ipp = a.open_ipp + v * a.open_vstride;
     const int* open_sh = a.open_sh + v * a.open_vstride;
-
-    uint16_t* xl = x_list(a, v, chunk);
-    int xn = 0;  // Gaussians of this chunk binned exactly so far (index order)
+    int xn = 0;
     // exact binning of queue[lane] (every lane with a queued Gaussian)
     auto bin_queued = [&](int j) {
       uint32_t rc_ipp = kEmptyRect, rc_sh = kEmptyRect;
       bin_exact<kShadow>(vg, s_means, s_cov, cs, j, rc_ipp, rc_sh);
       rects_ipp[j] = rc_ipp;
       count_rect(s_cnt, rc_ipp, tiles_x);
+      if (masks) mark_rect(s_mask, rc_ipp, tiles_x, 1u << (j >> 5));
       if (kShadow) {
         rects_sh[j] = rc_sh;
         count_rect(s_cnt_sh, rc_sh, tiles_x);
+        if (masks) mark_rect(s_mask_sh, rc_sh, tiles_x, 1u << (j >> 5));
       }
-      if (xl && xn + lane < kXCap) xl[xn + lane] = (uint16_t)j;
+      if (xl) xl[xn + lane] = (uint16_t)j;
     };
-
     int qn = 0;
-    for (int j0 = 0; j0 < gcount; j0 += 32) {
+    for (int j0 = j_lo; j0 < j_hi; j0 += 32) {
       const int j = j0 + lane;
       bool exact = false;
-      if (j < gcount) {
+      if (j < j_hi) {
         bool skip = s_sigma[j] < 0.01f;  // invalid: empty rectangles either way
         const float hb = s_hb[j];
         if (!skip && hb <= 64.0f) {
@@ -605,10 +629,73 @@ __global__ void __launch_bounds__(kBinThreads, 3) bin_skip_kernel(const BinArgs 
     if (lane < qn) bin_queued(queue[lane]);
     xn += qn;
     __syncwarp();
-    if (xl && lane == 0) x_count(a, v)[chunk] = xn <= kXCap ? xn : -1;
+    return xn;
+  };
 
+  const int vbase = blockIdx.y * a.views_per_cta;
+  const int nv_cta = min(a.nviews - vbase, a.views_per_cta);
+  if (nv_cta > kWarps / 2) {
+    // one view per warp at a time
+    for (int v = vbase + warp; v < vbase + nv_cta; v += kWarps) {
+      const int xn = bin_range(v, 0, gcount, x_list(a, v, chunk));
+      if (a.xlist && lane == 0) x_count(a, v)[chunk] = xn;
+      flush_counts(s_cnt, a.counts_ipp + v * a.counts_vstride + (size_t)chunk * T, T, lane);
+      if (kShadow) flush_counts(s_cnt_sh, a.counts_sh + v * a.counts_vstride + (size_t)chunk * T, T, lane);
+      if (masks) {
+        flush_masks(s_mask, a.segmask + v * a.segmask_vstride + (size_t)chunk * T, T, lane);
+        if (kShadow) flush_masks(s_mask_sh, a.segmask_sh + v * a.segmask_vstride + (size_t)chunk * T, T, lane);
+      }
+    }
+    return;
+  }
+  // few views: wpv warps share a view, each binning one contiguous slice of
+  // the chunk; the slices' counters and exact lists are merged in order
+  __shared__ uint16_t s_x[kWarps / 2][kChunk];
+  __shared__ int s_xn[kWarps];
+  const int wpv = kWarps / nv_cta;
+  const int vl = warp / wpv, sl = warp % wpv;
+  const bool active = vl < nv_cta;
+  const int per = (gcount + wpv * 32 - 1) / (wpv * 32) * 32;
+  const int j_lo = min(gcount, sl * per), j_hi = min(gcount, j_lo + per);
+  if (active) {
+    const int xn = bin_range(vbase + vl, j_lo, j_hi, a.xlist ? s_x[vl] + j_lo : nullptr);
+    if (lane == 0) s_xn[warp] = xn;
+  }
+  __syncthreads();
+  if (active && sl == 0) {
+    const int v = vbase + vl;
+    for (int o = 1; o < wpv; ++o) {
+      uint32_t* other = reinterpret_cast<uint32_t*>(s_hb + kChunk) + (warp + o) * TW * (kShadow ? 2 : 1);
+      for (int i = lane; i < TW * (kShadow ? 2 : 1); i += 32) {
+        s_cnt[i] += other[i];
+        other[i] = 0;
+      }
+      if (masks) {
+        uint32_t* om = s_mask + o * T * (kShadow ? 2 : 1);
+        for (int i = lane; i < T * (kShadow ? 2 : 1); i += 32) {
+          s_mask[i] |= om[i];
+          om[i] = 0;
+        }
+      }
+    }
+    __syncwarp();
+    if (a.xlist) {
+      uint16_t* xl = x_list(a, v, chunk);
+      int off = 0;
+      for (int o = 0; o < wpv; ++o) {
+        const int n_o = s_xn[warp + o];
+        const int lo = min(gcount, o * per);
+        for (int i = lane; i < n_o; i += 32) xl[off + i] = s_x[vl][lo + i];
+        off += n_o;
+      }
+      if (lane == 0) x_count(a, v)[chunk] = off;
+    }
     flush_counts(s_cnt, a.counts_ipp + v * a.counts_vstride + (size_t)chunk * T, T, lane);
     if (kShadow) flush_counts(s_cnt_sh, a.counts_sh + v * a.counts_vstride + (size_t)chunk * T, T, lane);
+    if (masks) {
+      flush_masks(s_mask, a.segmask + v * a.segmask_vstride + (size_t)chunk * T, T, lane);
+      if (kShadow) flush_masks(s_mask_sh, a.segmask_sh + v * a.segmask_vstride + (size_t)chunk * T, T, lane);
+    }
   }
 }
 
@@ -924,6 +1011,10 @@ __global__ void __launch_bounds__(kBinThreads) bin_finalize_kernel(const BinArgs
   const int cs = a.cov_layout;
   uint32_t* s_cnt = reinterpret_cast<uint32_t*>(smem_raw) + warp * TW * (kShadow ? 2 : 1);
   uint32_t* s_cnt_sh = s_cnt + TW;
+  const bool masks = a.skip_masks != 0;
+  uint32_t* s_mask = reinterpret_cast<uint32_t*>(smem_raw) + kWarps * TW * (kShadow ? 2 : 1) +
+                     warp * T * (kShadow ? 2 : 1);
+  uint32_t* s_mask_sh = s_mask + T;
   const int k = blockIdx.x * kWarps + warp;
   if (k >= a.chunks) return;
   const int chunk = a.chunk_offset + k;
@@ -932,6 +1023,8 @@ __global__ void __launch_bounds__(kBinThreads) bin_finalize_kernel(const BinArgs
   const ViewConst& vg = a.views[v];
 
   for (int i = lane; i < TW * (kShadow ? 2 : 1); i += 32) s_cnt[i] = 0;
+  if (masks)
+    for (int i = lane; i < T * (kShadow ? 2 : 1); i += 32) s_mask[i] = 0;
   const uint32_t* xbits = reinterpret_cast<const uint32_t*>(a.ipp.base + v * a.ipp.vstride + a.ipp.L.xbits);
   const uint32_t word = base + lane * 32 < a.n ? xbits[(size_t)chunk * 32 + lane] : 0u;
   const int cnt = __popc(word);
@@ -960,9 +1053,11 @@ __global__ void __launch_bounds__(kBinThreads) bin_finalize_kernel(const BinArgs
     bin_exact<kShadow>(vg, means, cov, cs, jl, rc_ipp, rc_sh);
     rects_ipp[jl] = rc_ipp;
     count_rect(s_cnt, rc_ipp, tiles_x);
+    if (masks) mark_rect(s_mask, rc_ipp, tiles_x, 1u << (jl >> 5));
     if (kShadow) {
       rects_sh[jl] = rc_sh;
       count_rect(s_cnt_sh, rc_sh, tiles_x);
+      if (masks) mark_rect(s_mask_sh, rc_sh, tiles_x, 1u << (jl >> 5));
     }
   }
   // the other Gaussians' rectangles are left unwritten: the state's meta and
@@ -970,6 +1065,10 @@ __global__ void __launch_bounds__(kBinThreads) bin_finalize_kernel(const BinArgs
   __syncwarp();
   flush_counts(s_cnt, a.counts_ipp + v * a.counts_vstride + (size_t)chunk * T, T, lane);
   if (kShadow) flush_counts(s_cnt_sh, a.counts_sh + v * a.counts_vstride + (size_t)chunk * T, T, lane);
+  if (masks) {
+    flush_masks(s_mask, a.segmask + v * a.segmask_vstride + (size_t)chunk * T, T, lane);
+    if (kShadow) flush_masks(s_mask_sh, a.segmask_sh + v * a.segmask_vstride + (size_t)chunk * T, T, lane);
+  }
 }
 
 // Open-tile summed-area table of one list of one view (grid: views x lists).
@@ -1118,6 +1217,7 @@ __global__ void __launch_bounds__(kSelectThreads) select_kernel(const SelectArgs
   const unsigned lt_mask = (1u << lane) - 1u;
   // the need entries and their per-chunk data, prefetched: lane l holds
   // entries l and l + 32 (exact-list length, or segment mask)
+  const bool all_masks = a.segmask && a.segmask_to >= a.C;
   int4 nd_l[2];
   int aux_l[2];
 #pragma unroll
@@ -1128,13 +1228,72 @@ __global__ void __launch_bounds__(kSelectThreads) select_kernel(const SelectArgs
     if (q < nneed) {
       nd_l[h] = need[q];
       const int c = nd_l[h].x;
-      if (xcount && c >= a.xlist_from)
+      if (!all_masks && xcount && c >= a.xlist_from)
         aux_l[h] = xcount[c];
       else if (a.segmask && c < a.segmask_to)
         aux_l[h] = (int)a.segmask[v * a.segmask_vstride + (size_t)c * T + t];
     }
   }
-  for (int q = 0; q < nneed; ++q) {
+  if (all_masks) {
+    // Every chunk has segment masks: the (need entry, hit segment) pairs of
+    // all entries, in order, kSelBatch per round with their rectangle loads
+    // in flight together.
+    constexpr int kSelBatch = 8;
+    const unsigned full = 0xffffffffu;
+    // rectangles of Gaussians from sparse_from on are valid only with their
+    // exactness bit (cell binning leaves the others unwritten)
+    const unsigned char* xsv = a.xs.base + v * a.xs.vstride;
+    const int64_t sparse_from = *reinterpret_cast<const int64_t*>(xsv + a.xs.L.meta);
+    const uint32_t* xbits = reinterpret_cast<const uint32_t*>(xsv + a.xs.L.xbits);
+    auto entry_mask = [&](int q) {
+      return (uint32_t)__shfl_sync(full, q >= 32 ? aux_l[1] : aux_l[0], q & 31);
+    };
+    int eq = 0;                        // entry being enumerated
+    uint32_t rem = entry_mask(0);      // its segments not yet enumerated
+    int cur = -1, found = 0, want = 0, ny = 0;
+    bool more = true;
+    while (more) {
+      uint32_t rc[kSelBatch];
+      int jj[kSelBatch], qq[kSelBatch];
+#pragma unroll
+      for (int b = 0; b < kSelBatch; ++b) {
+        while (rem == 0 && eq + 1 < nneed) rem = entry_mask(++eq);
+        qq[b] = -1;
+        jj[b] = 0;
+        rc[b] = kEmptyRect;
+        if (rem != 0) {
+          const int seg = __ffs(rem) - 1;
+          rem &= rem - 1;
+          const int cq = __shfl_sync(full, eq >= 32 ? nd_l[1].x : nd_l[0].x, eq & 31);
+          const int64_t jg = (int64_t)cq * kChunk + seg * 32 + lane;
+          qq[b] = eq;
+          jj[b] = (int)jg;
+          if (jg < a.n && (jg < sparse_from || ((xbits[jg >> 5] >> lane) & 1u))) rc[b] = rects[jg];
+        }
+      }
+      more = rem != 0 || eq + 1 < nneed;
+#pragma unroll
+      for (int b = 0; b < kSelBatch; ++b) {
+        const int q = qq[b];
+        if (q < 0) break;
+        if (q != cur) {
+          cur = q;
+          found = 0;
+          const bool h1 = q >= 32;
+          ny = __shfl_sync(full, h1 ? nd_l[1].y : nd_l[0].y, q & 31);
+          const int z = __shfl_sync(full, h1 ? nd_l[1].z : nd_l[0].z, q & 31);
+          want = min(z, kCap - ny);
+        }
+        if (found >= want) continue;
+        const bool hit = rect_has(rc[b], tx, ty);
+        const unsigned m = __ballot_sync(full, hit);
+        const int rk = found + __popc(m & lt_mask);
+        if (hit && rk < want) list[ny + rk] = jj[b];
+        found += __popc(m);
+      }
+    }
+  }
+  for (int q = 0; q < (all_masks ? 0 : nneed); ++q) {
     const int hq = q >> 5, src = q & 31;
     int4 nd;
     nd.x = __shfl_sync(0xffffffffu, hq ? nd_l[1].x : nd_l[0].x, src);
@@ -1785,9 +1944,9 @@ __global__ void debug_view_kernel(const ViewHost vh, float* __restrict__ out) {
 // launch wrappers
 // ---------------------------------------------------------------------------
 // Dynamic shared memory above the default opt-in limit needs the function
-// attribute; the kernels' static shared memory (< 4 KB) counts against the
+// attribute; the kernels' static shared memory (< 16 KB) counts against the
 // same 48 KB.
-static bool needs_smem_attr(size_t dynamic_smem) { return dynamic_smem + 4096 > 48 * 1024; }
+static bool needs_smem_attr(size_t dynamic_smem) { return dynamic_smem + 16384 > 48 * 1024; }
 
 // Segment masks of the prefix chunks are kept for tile grids up to
 // kSegMaskMaxTiles tiles.
@@ -1806,8 +1965,16 @@ constexpr size_t kWarpCountBytes = 32 * 1024;
 static size_t warp_count_bytes(const Dims& d, bool shadow) {
   return (size_t)(kBinThreads / 32) * ((d.T + 1) / 2) * 4 * (shadow ? 2 : 1);
 }
-static size_t bin_skip_smem_bytes(const Dims& d, int cov_layout, bool shadow) {
-  return (size_t)(3 + cov_layout + 2) * kChunk * sizeof(float) + warp_count_bytes(d, shadow);
+bool segmask_all_chunks(const Dims& d) { return d.T <= kSegMaskAllMaxTiles; }
+
+// per-warp segment masks of the skipping binners
+static size_t warp_mask_bytes(const Dims& d, bool shadow, bool masks) {
+  return masks ? (size_t)(kBinThreads / 32) * d.T * 4 * (shadow ? 2 : 1) : 0;
+}
+
+static size_t bin_skip_smem_bytes(const Dims& d, int cov_layout, bool shadow, bool masks) {
+  return (size_t)(3 + cov_layout + 2) * kChunk * sizeof(float) + warp_count_bytes(d, shadow) +
+         warp_mask_bytes(d, shadow, masks);
 }
 
 bool skip_bin_per_warp(const Dims& d, bool shadow) {
@@ -1822,8 +1989,9 @@ static void launch_bin_skip_t(const BinArgs& a, dim3 grid, size_t smem, cudaStre
   bin_skip_kernel<kShadow><<<grid, kBinThreads, smem, s>>>(a);
 }
 
-cudaError_t launch_view_setup(const ViewHostPack& pack, ViewConst* out, cudaStream_t s) {
-  view_setup_kernel<<<1, kMaxViewsPerLaunch, 0, s>>>(pack, out);
+cudaError_t launch_view_setup(const ViewHostPack& pack, ViewConst* out, int* err_to_clear,
+                              cudaStream_t s) {
+  view_setup_kernel<<<(pack.n + 31) / 32, 32, 0, s>>>(pack, out, err_to_clear);
   return cudaGetLastError();
 }
 
@@ -1861,7 +2029,7 @@ cudaError_t launch_bin(const BinArgs& a, const Dims& d, int chunks, bool shadow,
     return cudaGetLastError();
   }
   if (skip && skip_bin_per_warp(d, shadow)) {
-    const size_t smem = bin_skip_smem_bytes(d, a.cov_layout, shadow);
+    const size_t smem = bin_skip_smem_bytes(d, a.cov_layout, shadow, a.skip_masks != 0);
     if (shadow) launch_bin_skip_t<true>(a, grid, smem, s);
     else launch_bin_skip_t<false>(a, grid, smem, s);
     return cudaGetLastError();
@@ -1897,7 +2065,7 @@ static void launch_bin_finalize_t(const BinArgs& a, dim3 grid, size_t smem, cuda
 cudaError_t launch_bin_finalize(const BinArgs& a, const Dims& d, bool shadow, cudaStream_t s) {
   const int warps = kBinThreads / 32;
   const dim3 grid((a.chunks + warps - 1) / warps, a.nviews);
-  const size_t smem = warp_count_bytes(d, shadow);
+  const size_t smem = warp_count_bytes(d, shadow) + warp_mask_bytes(d, shadow, a.skip_masks != 0);
   if (shadow) launch_bin_finalize_t<true>(a, grid, smem, s);
   else launch_bin_finalize_t<false>(a, grid, smem, s);
   return cudaGetLastError();

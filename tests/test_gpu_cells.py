@@ -112,3 +112,40 @@ def test_cell_culling_backward_equals_sum_of_single_views():
                                            states=states)
     for i in range(4):
         assert torch.equal(grads3[i], grads[i])
+
+
+@pytest.mark.parametrize("nviews", [1, 10])
+def test_results_do_not_depend_on_workspace_contents(nviews):
+    """The workspace and the state buffers are caller memory of any content:
+    zero-filled, 0xFF-filled and random-filled buffers give identical images,
+    Omega and lists (the cell path for 10 views, the per-view path for 1)."""
+    n = 100000
+    sc = {k: v.cuda() for k, v in S.make_scene(n, (40.0, 40.0, 10.0), (0.05, 0.5), seed=55).items()}
+    views = S.sweep_views(80)[::8][:nviews]
+    inputs = _native.prepare_inputs(sc["means"], sc["cov6"], sc["sigma"], sc["sh"])
+    vs = [_native.make_view(*v) for v in views]
+    wsb = _native.workspace_bytes(n, 256, 256, nviews, _native.SARR_FLAG_OMEGA)
+    sbytes = _native.state_bytes(n, 256, 256)
+    out = {}
+    for fill in ("zero", "ff", "random"):
+        ws = torch.zeros(wsb, dtype=torch.uint8, device="cuda")
+        st = torch.zeros(nviews * sbytes, dtype=torch.uint8, device="cuda")
+        if fill == "ff":
+            ws.fill_(255)
+            st.fill_(255)
+        elif fill == "random":
+            g = torch.Generator(device="cuda").manual_seed(9)
+            ws.random_(0, 256, generator=g)
+            st.random_(0, 256, generator=g)
+        imgs = torch.empty((nviews, 256, 256), device="cuda")
+        om = torch.empty((nviews, n), device="cuda")
+        _native.forward(vs, *inputs, imgs, omega=om, states=st, ws=ws, check_device=True)
+        lists = [_state_lists(st, k, n, 256, sbytes) for k in range(nviews)]
+        out[fill] = (imgs, om, lists)
+    for fill in ("ff", "random"):
+        assert torch.equal(out[fill][0], out["zero"][0])
+        assert torch.equal(out[fill][1], out["zero"][1])
+        for (c0, l0), (c1, l1) in zip(out["zero"][2], out[fill][2]):
+            np.testing.assert_array_equal(c1, c0)
+            used = np.arange(64)[None, :] < c0[:, None]
+            np.testing.assert_array_equal(l1[used], l0[used])
