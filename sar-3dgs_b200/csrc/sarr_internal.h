@@ -29,10 +29,14 @@ struct Dims {
 //   yz     [T][64]   (Y_r, Z_r) of list slot s (backward chain)
 //   recs   [T][64]   Rec in compositing (Z_r, index) order
 //   xbits  [n/32] u32 bit i: Gaussian i was binned exactly (cell binning)
-//   meta   int64     first Gaussian whose rectangle is valid only when its
-//                    xbits bit is set (INT64_MAX: every rectangle is valid)
+//   xoff   [n/32] u16 per 32-Gaussian word: exactly binned Gaussians of the
+//                    chunk in its earlier words
+//   meta   int64     first Gaussian from which the chunks are sparse: only
+//                    their exactly binned Gaussians have rectangles, stored
+//                    compactly from the chunk's first slot in index order
+//                    (INT64_MAX: every rectangle is at its Gaussian's slot)
 struct StateLayout {
-  size_t rects, count, list, yz, recs, xbits, meta, bytes;
+  size_t rects, count, list, yz, recs, xbits, xoff, meta, bytes;
 };
 
 __host__ __device__ inline StateLayout state_layout(int64_t n, int T) {
@@ -50,6 +54,8 @@ __host__ __device__ inline StateLayout state_layout(int64_t n, int T) {
   o += align256((size_t)T * kCap * sizeof(Rec));
   L.xbits = o;
   o += align256((size_t)(n + 31) / 32 * 4);
+  L.xoff = o;
+  o += align256((size_t)(n + 31) / 32 * 2);
   L.meta = o;
   o += 256;
   L.bytes = o;
@@ -61,11 +67,14 @@ __host__ __device__ inline StateLayout state_layout(int64_t n, int T) {
 __device__ __forceinline__ uint32_t state_rect(const unsigned char* st, const StateLayout& L,
                                                const unsigned char* xs, const StateLayout& XL,
                                                int64_t i) {
+  const uint32_t* rects = reinterpret_cast<const uint32_t*>(st + L.rects);
   const int64_t sparse_from = *reinterpret_cast<const int64_t*>(xs + XL.meta);
-  if (i >= sparse_from &&
-      !((reinterpret_cast<const uint32_t*>(xs + XL.xbits)[i >> 5] >> (i & 31)) & 1u))
-    return kEmptyRect;
-  return reinterpret_cast<const uint32_t*>(st + L.rects)[i];
+  if (i < sparse_from) return rects[i];
+  const uint32_t word = reinterpret_cast<const uint32_t*>(xs + XL.xbits)[i >> 5];
+  if (!((word >> (i & 31)) & 1u)) return kEmptyRect;
+  const int k = reinterpret_cast<const uint16_t*>(xs + XL.xoff)[i >> 5] +
+                __popc(word & ((1u << (i & 31)) - 1u));
+  return rects[(i / kChunk) * kChunk + k];
 }
 
 // Workspace: [ViewConst x 32][error word][per-view areas x group]

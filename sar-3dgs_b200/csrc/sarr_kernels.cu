@@ -1032,6 +1032,8 @@ __global__ void __launch_bounds__(kBinThreads) bin_finalize_kernel(const BinArgs
   const int total = __shfl_sync(0xffffffffu, excl + cnt, 31);
   uint16_t* xl = x_list(a, v, chunk);
   if (lane == 0) x_count(a, v)[chunk] = total;
+  reinterpret_cast<uint16_t*>(a.ipp.base + v * a.ipp.vstride + a.ipp.L.xoff)[(size_t)chunk * 32 + lane] =
+      (uint16_t)excl;
   {
     uint32_t wbits = word;
     int pos = excl;
@@ -1047,15 +1049,17 @@ __global__ void __launch_bounds__(kBinThreads) bin_finalize_kernel(const BinArgs
       kShadow ? reinterpret_cast<uint32_t*>(a.sh.base + v * a.sh.vstride + a.sh.L.rects) + base : nullptr;
   const float* means = a.means + base * 3;
   const float* cov = a.cov + base * cs;
+  // the chunk is sparse: the listed Gaussians' rectangles are stored
+  // compactly from its first slot, in list order
   for (int i = lane; i < total; i += 32) {
     const int jl = xl[i];
     uint32_t rc_ipp = kEmptyRect, rc_sh = kEmptyRect;
     bin_exact<kShadow>(vg, means, cov, cs, jl, rc_ipp, rc_sh);
-    rects_ipp[jl] = rc_ipp;
+    rects_ipp[i] = rc_ipp;
     count_rect(s_cnt, rc_ipp, tiles_x);
     if (masks) mark_rect(s_mask, rc_ipp, tiles_x, 1u << (jl >> 5));
     if (kShadow) {
-      rects_sh[jl] = rc_sh;
+      rects_sh[i] = rc_sh;
       count_rect(s_cnt_sh, rc_sh, tiles_x);
       if (masks) mark_rect(s_mask_sh, rc_sh, tiles_x, 1u << (jl >> 5));
     }
@@ -1185,7 +1189,7 @@ __global__ void __launch_bounds__(kScanThreads) scan_kernel(const ScanArgs a) {
 //  2. the listed Gaussians (two slots per lane) are projected again in full
 //     (SH only for them) into 48-byte records;
 //  3. each slot's rank by (Z_r, slot) places its record.
-template <bool kShadowList>
+template <bool kShadowList, bool kAllMasks>
 __global__ void __launch_bounds__(kSelectThreads) select_kernel(const SelectArgs a) {
   constexpr int kWarps = kSelectThreads / 32;
   __shared__ int s_list[kWarps][kCap];
@@ -1215,9 +1219,14 @@ __global__ void __launch_bounds__(kSelectThreads) select_kernel(const SelectArgs
                                      reinterpret_cast<const unsigned char*>(a.xcount) + v * a.x_vstride)
                                : nullptr;
   const unsigned lt_mask = (1u << lane) - 1u;
+  // chunks from sparse_from on keep only their exactly binned Gaussians'
+  // rectangles, compactly in list order (cell binning)
+  const unsigned char* xsv = a.xs.base + v * a.xs.vstride;
+  const int64_t sparse_from = *reinterpret_cast<const int64_t*>(xsv + a.xs.L.meta);
   // the need entries and their per-chunk data, prefetched: lane l holds
   // entries l and l + 32 (exact-list length, or segment mask)
-  const bool all_masks = a.segmask && a.segmask_to >= a.C;
+  // kAllMasks: every chunk has segment masks (the per-view path)
+  constexpr bool all_masks = kAllMasks;
   int4 nd_l[2];
   int aux_l[2];
 #pragma unroll
@@ -1234,17 +1243,13 @@ __global__ void __launch_bounds__(kSelectThreads) select_kernel(const SelectArgs
         aux_l[h] = (int)a.segmask[v * a.segmask_vstride + (size_t)c * T + t];
     }
   }
-  if (all_masks) {
+  if constexpr (kAllMasks) {
     // Every chunk has segment masks: the (need entry, hit segment) pairs of
     // all entries, in order, kSelBatch per round with their rectangle loads
     // in flight together.
     constexpr int kSelBatch = 8;
     const unsigned full = 0xffffffffu;
-    // rectangles of Gaussians from sparse_from on are valid only with their
-    // exactness bit (cell binning leaves the others unwritten)
-    const unsigned char* xsv = a.xs.base + v * a.xs.vstride;
-    const int64_t sparse_from = *reinterpret_cast<const int64_t*>(xsv + a.xs.L.meta);
-    const uint32_t* xbits = reinterpret_cast<const uint32_t*>(xsv + a.xs.L.xbits);
+    // (the per-view path keeps every rectangle at its Gaussian's slot)
     auto entry_mask = [&](int q) {
       return (uint32_t)__shfl_sync(full, q >= 32 ? aux_l[1] : aux_l[0], q & 31);
     };
@@ -1268,7 +1273,7 @@ __global__ void __launch_bounds__(kSelectThreads) select_kernel(const SelectArgs
           const int64_t jg = (int64_t)cq * kChunk + seg * 32 + lane;
           qq[b] = eq;
           jj[b] = (int)jg;
-          if (jg < a.n && (jg < sparse_from || ((xbits[jg >> 5] >> lane) & 1u))) rc[b] = rects[jg];
+          if (jg < a.n) rc[b] = rects[jg];
         }
       }
       more = rem != 0 || eq + 1 < nneed;
@@ -1308,6 +1313,7 @@ __global__ void __launch_bounds__(kSelectThreads) select_kernel(const SelectArgs
       const uint16_t* xl = reinterpret_cast<const uint16_t*>(
                                reinterpret_cast<const unsigned char*>(a.xlist) + v * a.x_vstride) +
                            (size_t)nd.x * kXCap;
+      const bool compact = b0 >= sparse_from;
       int found = 0;
       for (int i0 = 0; i0 < xc && found < want; i0 += 32) {
         const int i = i0 + lane;
@@ -1315,7 +1321,7 @@ __global__ void __launch_bounds__(kSelectThreads) select_kernel(const SelectArgs
         int j = 0;
         if (i < xc) {
           j = (int)b0 + xl[i];
-          hit = rect_has(rects[j], tx, ty);
+          hit = rect_has(rects[compact ? b0 + i : j], tx, ty);
         }
         const unsigned m = __ballot_sync(0xffffffffu, hit);
         const int rk = found + __popc(m & lt_mask);
@@ -1536,8 +1542,6 @@ __device__ __forceinline__ float2 density_extent(const Rec& g) {
 // image). A record whose density box misses the whole block is skipped by the
 // warp: every pixel of the block would evaluate its density to 0 (< 1e-8) and
 // skip it too. Each pixel's arithmetic is the reference's, record by record.
-constexpr int kRenderWarps = 4;
-
 __device__ __forceinline__ void composite_one(const Rec& g, float fx, float fy, float& value,
                                               float& trans, bool& done) {
   const float gamma_ipp = rec_density(g, fx, fy);
@@ -1551,7 +1555,12 @@ __device__ __forceinline__ void composite_one(const Rec& g, float fx, float fy, 
   }
 }
 
-__global__ void __launch_bounds__(kRenderWarps * 32) render_kernel(const TileArgs a) {
+// kPix pixels per lane: 2 for launches of many views (4 warps per tile, fewer
+// per-record overheads), 1 for a few views (8 warps per tile, more warps in
+// flight when the grid is small).
+template <int kPix>
+__global__ void __launch_bounds__(kPix == 2 ? 128 : 256) render_kernel(const TileArgs a) {
+  constexpr int kWarps = kPix == 2 ? 4 : 8;
   __shared__ __align__(16) Rec s_rec[kCap];
   __shared__ float2 s_ext[kCap];
   __shared__ uint64_t bar;
@@ -1560,37 +1569,49 @@ __global__ void __launch_bounds__(kRenderWarps * 32) render_kernel(const TileArg
   const ViewConst& vc = a.views[v];
   const int Nr = vc.h.Nr, Na = vc.h.Na, tiles_x = vc.tiles_x;
   const int tx = t % tiles_x, ty = t / tiles_x;
-  const int r0 = ty * kTile + (warp & 1) * 8, c0 = tx * kTile + (warp >> 1) * 8;
-  const int pr = r0 + (lane & 7), pc0 = c0 + (lane >> 3), pc1 = pc0 + 4;
+  // warp block: 8 range rows x (4 * kPix) azimuth columns
+  const int r0 = ty * kTile + (warp & 1) * 8, c0 = tx * kTile + (warp >> 1) * 4 * kPix;
+  const int pr = r0 + (lane & 7), pc0 = c0 + (lane >> 3);
   const unsigned char* st = a.st.base + v * a.st.vstride;
   const int count = reinterpret_cast<const int*>(st + a.st.L.count)[t];
 
-  float value0 = 0.0f, value1 = 0.0f;
+  float value[kPix], trans[kPix];
+  bool done[kPix];
+#pragma unroll
+  for (int i = 0; i < kPix; ++i) {
+    value[i] = 0.0f;
+    trans[i] = 1.0f;
+    done[i] = false;
+  }
   if (count > 0) {
     const bool ok = load_tile_recs(s_rec, &bar, st, a.st.L, t, count, a.err, true);
     if (ok)
-      for (int k = tid; k < count; k += kRenderWarps * 32) s_ext[k] = density_extent(s_rec[k]);
+      for (int k = tid; k < count; k += kWarps * 32) s_ext[k] = density_extent(s_rec[k]);
     if (__syncthreads_and(ok)) {
-      float trans0 = 1.0f, trans1 = 1.0f;
-      bool done0 = false, done1 = false;
-      const float fy = (float)pr, fx0 = (float)pc0, fx1 = (float)pc1;
-      const float bx0 = (float)c0, bx1 = (float)(c0 + 7), by0 = (float)r0, by1 = (float)(r0 + 7);
+      const float fy = (float)pr;
+      const float bx0 = (float)c0, bx1 = (float)(c0 + 4 * kPix - 1), by0 = (float)r0,
+                  by1 = (float)(r0 + 7);
       for (int k = 0; k < count; ++k) {
         const Rec& g = s_rec[k];
         const float2 e = s_ext[k];
         const float mdx = fmaxf(0.0f, fmaxf(bx0 - g.mx, g.mx - bx1));
         const float mdy = fmaxf(0.0f, fmaxf(by0 - g.my, g.my - by1));
         if (mdx > e.x || mdy > e.y) continue;  // the same for every lane
-        if (!done0) composite_one(g, fx0, fy, value0, trans0, done0);
-        if (!done1) composite_one(g, fx1, fy, value1, trans1, done1);
-        if (done0 && done1) break;
+        bool all_done = true;
+#pragma unroll
+        for (int i = 0; i < kPix; ++i) {
+          if (!done[i]) composite_one(g, (float)(pc0 + 4 * i), fy, value[i], trans[i], done[i]);
+          all_done = all_done && done[i];
+        }
+        if (all_done) break;
       }
     }
   }
   float* img = a.images + v * a.img_vstride;
   if (pr < Nr) {
-    if (pc0 < Na) img[(size_t)pc0 * Nr + pr] = value0;
-    if (pc1 < Na) img[(size_t)pc1 * Nr + pr] = value1;
+#pragma unroll
+    for (int i = 0; i < kPix; ++i)
+      if (pc0 + 4 * i < Na) img[(size_t)(pc0 + 4 * i) * Nr + pr] = value[i];
   }
 }
 
@@ -2113,15 +2134,22 @@ cudaError_t launch_scan(const ScanArgs& a, int nviews, cudaStream_t s) {
 cudaError_t launch_select(const SelectArgs& a, const Dims& d, int nviews, bool shadow_list,
                           cudaStream_t s) {
   const dim3 grid((d.T + kSelectThreads / 32 - 1) / (kSelectThreads / 32), nviews);
-  if (shadow_list)
-    select_kernel<true><<<grid, kSelectThreads, 0, s>>>(a);
-  else
-    select_kernel<false><<<grid, kSelectThreads, 0, s>>>(a);
+  const bool all = a.segmask && a.segmask_to >= a.C;
+  if (shadow_list) {
+    if (all) select_kernel<true, true><<<grid, kSelectThreads, 0, s>>>(a);
+    else select_kernel<true, false><<<grid, kSelectThreads, 0, s>>>(a);
+  } else {
+    if (all) select_kernel<false, true><<<grid, kSelectThreads, 0, s>>>(a);
+    else select_kernel<false, false><<<grid, kSelectThreads, 0, s>>>(a);
+  }
   return cudaGetLastError();
 }
 
 cudaError_t launch_render(const TileArgs& a, const Dims& d, int nviews, cudaStream_t s) {
-  render_kernel<<<dim3(d.T, nviews), kRenderWarps * 32, 0, s>>>(a);
+  if (nviews >= 16)
+    render_kernel<2><<<dim3(d.T, nviews), 128, 0, s>>>(a);
+  else
+    render_kernel<1><<<dim3(d.T, nviews), 256, 0, s>>>(a);
   return cudaGetLastError();
 }
 
