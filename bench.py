@@ -414,6 +414,45 @@ def bench_fwd_bwd(args, d, means, cov, layout, sigma, sh, sh_stride, sh_k, views
             "l2": "flushed every 64 steps"}
 
 
+def bench_train_ops(args, d):
+    """The training-step kernels next to the rasterizer: the Gaussian
+    parameter producer over the N Gaussians (72 B per Gaussian: log-scales,
+    quaternion and logit read, 3x3 covariance and transmittance written) and
+    the combined L1 + D-SSIM loss with its gradient over 64 images of the
+    sweep size (12 B per pixel: both images read, the gradient written)."""
+    from cuda_rasterizer import gaussian_params as GP  # noqa: F401
+    dev = d.device
+    n, s = args.n, args.samples
+    g = torch.Generator(device=dev).manual_seed(3)
+    scales = torch.rand((n, 3), device=dev, generator=g) * 3 - 4
+    rot = torch.randn((n, 4), device=dev, generator=g)
+    logits = torch.randn((n,), device=dev, generator=g)
+    pred = torch.rand((64, s, s), device=dev, generator=g)
+    target = torch.rand((64, s, s), device=dev, generator=g)
+    peak, peak_kind = peaks()
+
+    def timed(fn, reps=20):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            fn()
+        b.record()
+        b.synchronize()
+        return a.elapsed_time(b) / reps / 1e3
+
+    t_p = timed(lambda: _native.gaussian_params(scales, rot, logits))
+    t_l = timed(lambda: _native.combined_loss(pred, target, 0.9, 0.1, 5, "plain"))
+    bp, bl = 72 * n, 12 * 64 * s * s
+    return {"producer": {"gaussians_per_s": n / t_p, "achieved_gbs": round(bp / t_p / 1e9, 1),
+                         "frac": round(bp / t_p / 1e9 / peak, 4), "peak_source": peak_kind,
+                         "us": round(t_p * 1e6, 2)},
+            "loss": {"images_per_s": 64 / t_l, "achieved_gbs": round(bl / t_l / 1e9, 1),
+                     "frac": round(bl / t_l / 1e9 / peak, 4), "us_per_64": round(t_l * 1e6, 2)}}
+
+
 def cpu_baseline(args):
     """CPU restatement of the reference algorithm on a bounded sample of the
     same workload (image-only forward), all host threads."""
@@ -545,6 +584,8 @@ def main():
         line["e2e"] = r["e2e"]
     if "fwd_bwd" in r:
         line["fwd_bwd"] = r["fwd_bwd"]
+    if not args.no_fwdbwd:
+        line["train_ops"] = bench_train_ops(args, d)
     if d.rank == 0 and d.world == 1 and not args.no_cpu:
         line["cpu_baseline"] = cpu_baseline(args)
     if d.rank == 0:

@@ -118,6 +118,54 @@ int sarr_forward(const sarr_view *views, int n_views, int64_t n, const float *me
                  void *ws, size_t ws_bytes, sarr_stream_t stream);
 
 /*
+ * Gaussian parameters of a training step: replaces
+ * GaussianModel.compute_covariance_full / compute_covariance and get_opacity
+ * (gaussian_model.py:261-330). For each of the n Gaussians:
+ *   cov_out      Sigma = R diag(exp(s))^2 R^T, R from the quaternion
+ *                (w, x, y, z) exactly as Quaternion.to_rotation_matrix
+ *                builds it (gaussian_model.py:33-55, no normalisation), in
+ *                cov_layout (SARR_COV33 [n,3,3] or SARR_COV6 [n,6] in the
+ *                rasterizer's xx yy zz xy xz yz order); NULL skips it. The
+ *                reference detaches this covariance (no gradient flows back
+ *                to scales or rotations); so does this entry point.
+ *   opacity_out  sigmoid(opacity_logits); NULL skips it.
+ * Inputs scales_log [n,3], rotations [n,4], opacity_logits [n], fp32,
+ * contiguous device arrays.
+ */
+int sarr_gaussian_params(int64_t n, const float *scales_log, const float *rotations,
+                         float *cov_out, int cov_layout, const float *opacity_logits,
+                         float *opacity_out, sarr_stream_t stream);
+
+/* Weighted-L1 modes of losses.py:28-62 (SARR_L1_PLAIN: the plain mean |p - t|). */
+#define SARR_L1_PLAIN 0
+#define SARR_L1_LINEAR 1
+#define SARR_L1_SQUARE 2
+#define SARR_L1_SQRT 3
+
+/* Workspace bytes of sarr_combined_loss for n_images images of height x width. */
+int sarr_loss_workspace_size(int n_images, int height, int width, size_t *bytes);
+
+/*
+ * CombinedLoss.forward (losses.py:160-219) and its gradient with respect to
+ * pred, for n_images images [n_images, height, width] (contiguous fp32):
+ *   losses_out [3] (device)  total = l1_weight * L1 + ssim_weight * D-SSIM,
+ *                            L1, D-SSIM, each a mean over all pixels of all
+ *                            images as the reference computes them for a
+ *                            [B, H, W] batch;
+ *   grad_pred (nullable)     d total / d pred, the same layout as pred.
+ * window_size: odd, <= 11 (the reference's default is 5; Gaussian window of
+ * sigma 1.5, zero padding). The loss and its gradient are symmetric under
+ * transposing both images, so images in the rasterizer's azimuth-major
+ * memory order can be passed as they are. Deterministic (fixed reduction
+ * order). No reference counterpart for the fused gradient (the reference
+ * differentiates the torch graph).
+ */
+int sarr_combined_loss(int n_images, int height, int width, const float *pred,
+                       const float *target, float l1_weight, float ssim_weight, int window_size,
+                       int l1_mode, float *losses_out, float *grad_pred, void *ws, size_t ws_bytes,
+                       sarr_stream_t stream);
+
+/*
  * sarr_forward for one view, image only, without a workspace argument: the
  * scratch is a 6 MiB array inside this library, one per device. No
  * counterpart in the reference. It is for callers that cannot allocate

@@ -64,6 +64,7 @@ struct SceneGrid {
   float half_diag;           // bound on |member centre - cell centre| [m], with margins
   int valid;                 // 0: no finite centre (no Gaussian is in a cell)
   int nspatial;              // spatial cells (ncells = nspatial * kHbBuckets)
+  int block_sums[kMaxCells / 1024];  // member counts per 1024 cells (scan scratch)
   int n_always;              // Gaussians after the prefix that are in no cell
 };
 

@@ -846,16 +846,12 @@ __global__ void __launch_bounds__(256) cell_assign_kernel(const CellPrepArgs a) 
   if (id == kCellAlways && j >= a.pstart) a.always[atomicAdd(&a.grid->n_always, 1)] = (int)j;
 }
 
-// Exclusive scan of the cells' member counts into cell_start (one CTA); the
-// counts become the fill cursors.
-__global__ void __launch_bounds__(1024) cell_scan_kernel(const CellPrepArgs a) {
-  __shared__ int s_warp[32];
-  constexpr int kPer = kMaxCells / 1024;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int* cnt = a.cell_count + tid * kPer;
-  int sum = 0;
-  for (int k = 0; k < kPer; ++k) sum += cnt[k];
-  const int incl = warp_incl_scan(sum, lane);
+// Exclusive scan of the cells' member counts into cell_start, in two passes of
+// 1024-cell blocks (block scans, then block offsets); the counts become the
+// fill cursors.
+__device__ __forceinline__ int block_excl_scan_1024(int x, int* s_warp) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int incl = warp_incl_scan(x, lane);
   if (lane == 31) s_warp[warp] = incl;
   __syncthreads();
   if (warp == 0) {
@@ -863,15 +859,32 @@ __global__ void __launch_bounds__(1024) cell_scan_kernel(const CellPrepArgs a) {
     s_warp[lane] = warp_incl_scan(w, lane) - w;
   }
   __syncthreads();
-  int run = s_warp[warp] + incl - sum;
-  for (int k = 0; k < kPer; ++k) {
-    const int c = tid * kPer + k;
-    const int x = a.cell_count[c];
-    a.cell_start[c] = run;
-    a.cell_count[c] = run;
-    run += x;
+  return s_warp[warp] + incl - x;
+}
+
+__global__ void __launch_bounds__(1024) cell_scan_blocks_kernel(const CellPrepArgs a) {
+  __shared__ int s_warp[32];
+  const int c = blockIdx.x * 1024 + threadIdx.x;
+  const int x = a.cell_count[c];
+  const int excl = block_excl_scan_1024(x, s_warp);
+  a.cell_start[c] = excl;
+  if (threadIdx.x == 1023) a.grid->block_sums[blockIdx.x] = excl + x;
+}
+
+__global__ void __launch_bounds__(1024) cell_scan_offsets_kernel(const CellPrepArgs a) {
+  __shared__ int s_off;
+  const int c = blockIdx.x * 1024 + threadIdx.x;
+  if (threadIdx.x < 32) {
+    int sum = 0;
+    for (int b = threadIdx.x; b < (int)blockIdx.x; b += 32) sum += a.grid->block_sums[b];
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if (threadIdx.x == 0) s_off = sum;
   }
-  if (tid == 1023) a.cell_start[kMaxCells] = run;
+  __syncthreads();
+  const int start = a.cell_start[c] + s_off;
+  a.cell_start[c] = start;
+  a.cell_count[c] = start;
+  if (c == kMaxCells - 1) a.cell_start[kMaxCells] = s_off + a.grid->block_sums[gridDim.x - 1];
 }
 
 // Member lists: centre and bbox bound of every Gaussian after the prefix,
@@ -2109,7 +2122,10 @@ cudaError_t launch_cell_prep(const CellPrepArgs& a, cudaStream_t s) {
   cell_assign_kernel<<<(unsigned)((a.n + 255) / 256), 256, 0, s>>>(a);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  cell_scan_kernel<<<1, 1024, 0, s>>>(a);
+  cell_scan_blocks_kernel<<<kMaxCells / 1024, 1024, 0, s>>>(a);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  cell_scan_offsets_kernel<<<kMaxCells / 1024, 1024, 0, s>>>(a);
   e = cudaGetLastError();
   if (e != cudaSuccess || a.n <= a.pstart) return e;
   cell_fill_kernel<<<(unsigned)((a.n - a.pstart + 255) / 256), 256, 0, s>>>(a);

@@ -19,6 +19,7 @@ SARR_COV6 = 6
 SARR_COV33 = 9
 SARR_FLAG_OMEGA = 1
 SARR_FLAG_ACCUMULATE = 2
+SARR_L1_MODES = {"plain": 0, "linear": 1, "square": 2, "sqrt": 3}
 MAX_SH = 16
 
 
@@ -74,9 +75,14 @@ def _declare(L):
     L.sarr_profile_read.restype = I
     L.sarr_kernel_name.argtypes = [I]
     L.sarr_kernel_name.restype = ctypes.c_char_p
+    L.sarr_gaussian_params.argtypes = [I64, P, P, P, I, P, P, P]
+    L.sarr_loss_workspace_size.argtypes = [I, I, I, ctypes.POINTER(SZ)]
+    F = ctypes.c_float
+    L.sarr_combined_loss.argtypes = [I, I, I, P, P, F, F, I, I, P, P, P, SZ, P]
     for name in ("sarr_workspace_size", "sarr_state_size", "sarr_forward", "sarr_backward",
                  "sarr_debug_preprocess", "sarr_debug_tile_lists", "sarr_check_device_errors",
-                 "sarr_debug_tile_rect"):
+                 "sarr_debug_tile_rect", "sarr_gaussian_params", "sarr_loss_workspace_size",
+                 "sarr_combined_loss"):
         getattr(L, name).restype = I
     return L
 
@@ -299,3 +305,54 @@ def profile_read():
     cnt = (ctypes.c_int64 * KERNEL_KINDS)()
     _check(lib().sarr_profile_read(ms, cnt, KERNEL_KINDS), "sarr_profile_read")
     return {lib().sarr_kernel_name(k).decode(): (ms[k], cnt[k]) for k in range(KERNEL_KINDS)}
+
+
+def gaussian_params(scales_log, rotations, opacity_logits=None, layout=SARR_COV33):
+    """sarr_gaussian_params: (cov [n,3,3] or [n,6] or None, sigmoid(opacity_logits)
+    or None); scales_log/rotations may be None to compute the transmittance only."""
+    cov = sigma = None
+    if scales_log is not None:
+        scales_log = _as_cuda_f32(scales_log, "scales").contiguous()
+        rotations = _as_cuda_f32(rotations, "rotations").contiguous()
+        n = scales_log.shape[0]
+        if scales_log.shape != (n, 3) or rotations.shape != (n, 4):
+            raise RuntimeError("scales must be [N,3] and rotations [N,4]")
+        dev = scales_log.device
+        cov = torch.empty((n, 3, 3) if layout == SARR_COV33 else (n, 6), dtype=torch.float32, device=dev)
+    if opacity_logits is not None:
+        opacity_logits = _as_cuda_f32(opacity_logits, "opacity").contiguous().reshape(-1)
+        if cov is not None and opacity_logits.numel() != n:
+            raise RuntimeError("opacity must have N elements")
+        n = opacity_logits.numel()
+        dev = opacity_logits.device
+        sigma = torch.empty_like(opacity_logits)
+    if cov is None and sigma is None:
+        return None, None
+    with torch.cuda.device(dev):
+        _check(lib().sarr_gaussian_params(n, _ptr(scales_log), _ptr(rotations), _ptr(cov), layout,
+                                          _ptr(opacity_logits), _ptr(sigma), _stream(dev)),
+               "sarr_gaussian_params")
+    return cov, sigma
+
+
+def combined_loss(pred, target, l1_weight, ssim_weight, window_size=5, l1_mode="plain",
+                  want_grad=True):
+    """sarr_combined_loss on [V,H,W] images: (losses [3] device tensor = total,
+    L1, D-SSIM; d total / d pred or None)."""
+    pred = _as_cuda_f32(pred, "pred").contiguous()
+    target = _as_cuda_f32(target, "target").contiguous()
+    if pred.shape != target.shape or pred.dim() != 3:
+        raise RuntimeError("pred and target must both be [V,H,W]")
+    v, h, w = pred.shape
+    dev = pred.device
+    sz = ctypes.c_size_t()
+    _check(lib().sarr_loss_workspace_size(v, h, w, ctypes.byref(sz)), "sarr_loss_workspace_size")
+    ws = torch.empty(sz.value, dtype=torch.uint8, device=dev)
+    losses = torch.empty(3, dtype=torch.float32, device=dev)
+    grad = torch.empty_like(pred) if want_grad else None
+    with torch.cuda.device(dev):
+        _check(lib().sarr_combined_loss(v, h, w, _ptr(pred), _ptr(target), float(l1_weight),
+                                        float(ssim_weight), int(window_size), SARR_L1_MODES[l1_mode],
+                                        _ptr(losses), _ptr(grad), _ptr(ws), ws.numel(), _stream(dev)),
+               "sarr_combined_loss")
+    return losses, grad
