@@ -166,6 +166,40 @@ int sarr_combined_loss(int n_images, int height, int width, const float *pred,
                        sarr_stream_t stream);
 
 /*
+ * Densification and pruning (GaussianModel.densify_and_prune,
+ * gaussian_model.py:433-566) in two calls, with a host decision between them
+ * (the reference's max_gaussians tests, which need the counts):
+ *   sarr_densify_flags   per Gaussian: clone = |exp(s)| < size_threshold and
+ *                        |grad_mean| > grad_threshold; split = |exp(s)| >
+ *                        large_scale_threshold and |grad_mean| >
+ *                        grad_threshold; prune = sigmoid(logit) <
+ *                        opacity_threshold or |exp(s)| > large_scale_threshold.
+ *                        counts_out (device int64 [3]) = kept, clones, splits.
+ *   sarr_densify_apply   writes the new set: the kept Gaussians in order,
+ *                        then (do_clones) one clone per clone flag with mean
+ *                        + 0.01 grad, then (do_splits) two Gaussians per
+ *                        split flag with scale log(0.8 exp(s)) and mean
+ *                        offsets (0.4 exp(s_x) cos a, 0.4 exp(s_y) sin a, 0)
+ *                        for a = 0 and pi (:523-548); output arrays hold kept +
+ *                        do_clones * clones + 2 * do_splits * splits rows.
+ * Inputs: means [n,3], scales_log [n,3], rotations [n,4], opacity_logits
+ * [n], sh [n, sh_cols], grad_means [n,3]; the workspace (from
+ * sarr_densify_workspace_size) carries the flags from the first call to the
+ * second. Deterministic; no reference counterpart for the split into two calls.
+ */
+int sarr_densify_workspace_size(int64_t n, size_t *bytes);
+int sarr_densify_flags(int64_t n, const float *scales_log, const float *opacity_logits,
+                       const float *grad_means, float grad_threshold, float size_threshold,
+                       float large_scale_threshold, float opacity_threshold, int64_t *counts_out,
+                       void *ws, size_t ws_bytes, sarr_stream_t stream);
+int sarr_densify_apply(int64_t n, const float *means, const float *scales_log,
+                       const float *rotations, const float *opacity_logits, const float *sh,
+                       int sh_cols, const float *grad_means, const int64_t *counts, int do_clones,
+                       int do_splits, float *out_means, float *out_scales, float *out_rotations,
+                       float *out_opacity_logits, float *out_sh, void *ws, size_t ws_bytes,
+                       sarr_stream_t stream);
+
+/*
  * sarr_forward for one view, image only, without a workspace argument: the
  * scratch is a 6 MiB array inside this library, one per device. No
  * counterpart in the reference. It is for callers that cannot allocate

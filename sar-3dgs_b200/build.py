@@ -19,7 +19,7 @@ REPO = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 INCLUDE = os.path.join(REPO, "include")
 LIB = os.path.join(HERE, "libsarr.so")
-SOURCES = ["sarr_kernels.cu", "sarr_abi.cu", "sarr_static.cu", "sarr_train.cu"]
+SOURCES = ["sarr_kernels.cu", "sarr_abi.cu", "sarr_static.cu", "sarr_train.cu", "sarr_densify.cu"]
 HEADERS = ["sarr_common.cuh", "sarr_internal.h"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

@@ -79,10 +79,14 @@ def _declare(L):
     L.sarr_loss_workspace_size.argtypes = [I, I, I, ctypes.POINTER(SZ)]
     F = ctypes.c_float
     L.sarr_combined_loss.argtypes = [I, I, I, P, P, F, F, I, I, P, P, P, SZ, P]
+    L.sarr_densify_workspace_size.argtypes = [I64, ctypes.POINTER(SZ)]
+    L.sarr_densify_flags.argtypes = [I64, P, P, P, F, F, F, F, P, P, SZ, P]
+    L.sarr_densify_apply.argtypes = [I64, P, P, P, P, P, I, P, P, I, I, P, P, P, P, P, P, SZ, P]
     for name in ("sarr_workspace_size", "sarr_state_size", "sarr_forward", "sarr_backward",
                  "sarr_debug_preprocess", "sarr_debug_tile_lists", "sarr_check_device_errors",
                  "sarr_debug_tile_rect", "sarr_gaussian_params", "sarr_loss_workspace_size",
-                 "sarr_combined_loss"):
+                 "sarr_combined_loss", "sarr_densify_workspace_size", "sarr_densify_flags",
+                 "sarr_densify_apply"):
         getattr(L, name).restype = I
     return L
 
@@ -356,3 +360,45 @@ def combined_loss(pred, target, l1_weight, ssim_weight, window_size=5, l1_mode="
                                         _ptr(losses), _ptr(grad), _ptr(ws), ws.numel(), _stream(dev)),
                "sarr_combined_loss")
     return losses, grad
+
+
+def densify_and_prune(means, scales, rotations, opacities, sh, grad_means, grad_threshold,
+                      size_threshold, large_scale_threshold, opacity_threshold, max_gaussians):
+    """sarr_densify_flags + sarr_densify_apply with the reference's
+    max_gaussians decisions in between: (new means, scales, rotations,
+    opacities (same trailing shape as the input), sh, (clones, splits, prunes,
+    new))."""
+    dev = means.device
+    n = means.shape[0]
+    t = [_as_cuda_f32(x, nm).contiguous() for x, nm in
+         ((means, "means"), (scales, "scales"), (rotations, "rotations"), (opacities, "opacities"),
+          (sh, "sh"), (grad_means, "grad_means"))]
+    means, scales, rotations, op, sh, grad_means = t
+    sh_cols = sh.shape[1] if sh.dim() == 2 else 0
+    sz = ctypes.c_size_t()
+    _check(lib().sarr_densify_workspace_size(n, ctypes.byref(sz)), "sarr_densify_workspace_size")
+    ws = torch.empty(max(sz.value, 256), dtype=torch.uint8, device=dev)
+    counts = torch.zeros(3, dtype=torch.int64, device=dev)
+    with torch.cuda.device(dev):
+        st = _stream(dev)
+        _check(lib().sarr_densify_flags(n, _ptr(scales), _ptr(op), _ptr(grad_means), float(grad_threshold),
+                                        float(size_threshold), float(large_scale_threshold),
+                                        float(opacity_threshold), _ptr(counts), _ptr(ws), ws.numel(), st),
+               "sarr_densify_flags")
+        kept, clones, splits = (int(x) for x in counts.tolist())
+        prunes = n - kept
+        # gaussian_model.py:504 and :523: the tests against max_gaussians use
+        # the count after pruning
+        do_c = clones > 0 and kept + clones < max_gaussians
+        added = clones if do_c else 0
+        do_s = splits > 0 and kept + added + splits < max_gaussians
+        m = kept + added + (2 * splits if do_s else 0)
+        out = (torch.empty((m, 3), device=dev), torch.empty((m, 3), device=dev),
+               torch.empty((m, 4), device=dev), torch.empty((m,) + tuple(opacities.shape[1:]), device=dev),
+               torch.empty((m, sh_cols), device=dev))
+        _check(lib().sarr_densify_apply(n, _ptr(means), _ptr(scales), _ptr(rotations), _ptr(op), _ptr(sh),
+                                        sh_cols, _ptr(grad_means), _ptr(counts), int(do_c), int(do_s),
+                                        _ptr(out[0]), _ptr(out[1]), _ptr(out[2]), _ptr(out[3]),
+                                        _ptr(out[4]), _ptr(ws), ws.numel(), st), "sarr_densify_apply")
+    new = (clones if do_c else 0) + (2 * splits if do_s else 0)
+    return out, (clones, splits, prunes, new)
