@@ -1550,11 +1550,13 @@ __device__ __forceinline__ float2 density_extent(const Rec& g) {
 }
 
 // One CTA per tile: the tile's sorted records arrive with one TMA bulk copy;
-// warp w composites an 8 x 8 pixel block, each lane two pixels of one range
-// row (azimuth columns c and c + 4; lanes along range, contiguous in the
-// image). A record whose density box misses the whole block is skipped by the
-// warp: every pixel of the block would evaluate its density to 0 (< 1e-8) and
-// skip it too. Each pixel's arithmetic is the reference's, record by record.
+// warp w composites an 8 x (4 kPix) pixel block, each lane kPix pixels of one
+// range row (azimuth columns c, c + 4; lanes along range, contiguous in the
+// image). Before compositing, each warp marks, per 8 x 4 half of its block,
+// the records whose density box meets that half (one bit per record, two
+// ballots): every pixel outside a record's box evaluates its density to 0
+// (< 1e-8) and skips it, so visiting only the marked records, in list order,
+// leaves each pixel's arithmetic the reference's, record by record.
 __device__ __forceinline__ void composite_one(const Rec& g, float fx, float fy, float& value,
                                               float& trans, bool& done) {
   const float gamma_ipp = rec_density(g, fx, fy);
@@ -1573,9 +1575,7 @@ __device__ __forceinline__ void composite_one(const Rec& g, float fx, float fy, 
 // flight when the grid is small).
 template <int kPix>
 __global__ void __launch_bounds__(kPix == 2 ? 128 : 256) render_kernel(const TileArgs a) {
-  constexpr int kWarps = kPix == 2 ? 4 : 8;
   __shared__ __align__(16) Rec s_rec[kCap];
-  __shared__ float2 s_ext[kCap];
   __shared__ uint64_t bar;
   const int v = blockIdx.y, t = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -1598,22 +1598,48 @@ __global__ void __launch_bounds__(kPix == 2 ? 128 : 256) render_kernel(const Til
   }
   if (count > 0) {
     const bool ok = load_tile_recs(s_rec, &bar, st, a.st.L, t, count, a.err, true);
-    if (ok)
-      for (int k = tid; k < count; k += kWarps * 32) s_ext[k] = density_extent(s_rec[k]);
     if (__syncthreads_and(ok)) {
+      // hit[i] bit k: record k's density box meets columns [c0 + 4i, c0 + 4i + 3]
+      // of rows [r0, r0 + 7]
+      uint64_t hit[kPix];
+#pragma unroll
+      for (int i = 0; i < kPix; ++i) hit[i] = 0;
+      const float by0 = (float)r0, by1 = (float)(r0 + 7);
+      for (int h = 0; h < (count > 32 ? 2 : 1); ++h) {
+        const int k = lane + 32 * h;
+        bool in[kPix];
+#pragma unroll
+        for (int i = 0; i < kPix; ++i) in[i] = false;
+        if (k < count) {
+          const Rec& g = s_rec[k];
+          const float2 e = density_extent(g);
+          const float mdy = fmaxf(0.0f, fmaxf(by0 - g.my, g.my - by1));
+          if (!(mdy > e.y)) {
+#pragma unroll
+            for (int i = 0; i < kPix; ++i) {
+              const float hx0 = (float)(c0 + 4 * i), hx1 = hx0 + 3.0f;
+              const float mdx = fmaxf(0.0f, fmaxf(hx0 - g.mx, g.mx - hx1));
+              in[i] = !(mdx > e.x);
+            }
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < kPix; ++i)
+          hit[i] |= (uint64_t)__ballot_sync(0xffffffffu, in[i]) << (32 * h);
+      }
+      uint64_t todo = hit[0];
+#pragma unroll
+      for (int i = 1; i < kPix; ++i) todo |= hit[i];
       const float fy = (float)pr;
-      const float bx0 = (float)c0, bx1 = (float)(c0 + 4 * kPix - 1), by0 = (float)r0,
-                  by1 = (float)(r0 + 7);
-      for (int k = 0; k < count; ++k) {
+      while (todo) {
+        const int k = __ffsll((long long)todo) - 1;
+        todo &= todo - 1;
         const Rec& g = s_rec[k];
-        const float2 e = s_ext[k];
-        const float mdx = fmaxf(0.0f, fmaxf(bx0 - g.mx, g.mx - bx1));
-        const float mdy = fmaxf(0.0f, fmaxf(by0 - g.my, g.my - by1));
-        if (mdx > e.x || mdy > e.y) continue;  // the same for every lane
         bool all_done = true;
 #pragma unroll
         for (int i = 0; i < kPix; ++i) {
-          if (!done[i]) composite_one(g, (float)(pc0 + 4 * i), fy, value[i], trans[i], done[i]);
+          if (!done[i] && ((hit[i] >> k) & 1))
+            composite_one(g, (float)(pc0 + 4 * i), fy, value[i], trans[i], done[i]);
           all_done = all_done && done[i];
         }
         if (all_done) break;
