@@ -397,7 +397,7 @@ __device__ __forceinline__ void flush_counts(uint32_t* cnt, uint8_t* out, int T,
 // plain read-modify-write is exact). No CTA barrier inside the view loop.
 // Means and transmittances are staged; covariances are read through L1.
 template <bool kShadow>
-__global__ void __launch_bounds__(kBinThreads, 3) bin_prefix_kernel(const BinArgs a) {
+__global__ void __launch_bounds__(kBinThreads, 4) bin_prefix_kernel(const BinArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   __shared__ uint64_t bar;
   constexpr int kWarps = kBinThreads / 32;
@@ -1203,7 +1203,7 @@ __global__ void __launch_bounds__(kScanThreads) scan_kernel(const ScanArgs a) {
 //     (SH only for them) into 48-byte records;
 //  3. each slot's rank by (Z_r, slot) places its record.
 template <bool kShadowList, bool kAllMasks>
-__global__ void __launch_bounds__(kSelectThreads) select_kernel(const SelectArgs a) {
+__global__ void __launch_bounds__(kSelectThreads, 8) select_kernel(const SelectArgs a) {
   constexpr int kWarps = kSelectThreads / 32;
   __shared__ int s_list[kWarps][kCap];
   __shared__ float s_z[kWarps][kCap];
