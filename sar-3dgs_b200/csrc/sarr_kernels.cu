@@ -1532,34 +1532,62 @@ __device__ __forceinline__ bool load_tile_recs(Rec* s_rec, uint64_t* bar, const 
   return mbar_wait_bounded(bar, 0, err);
 }
 
-// Half-widths (columns, rows) of the box outside which rec_density's exponent
-// is below -20 for this record, so that it returns 0 there. The exponent is
-// -q / (2 det) with q = cxx dy^2 + cyy dx^2 - 2 cxy dx dy, and q <= 40 det
-// implies |dx| <= sqrt(40 cxx), |dy| <= sqrt(40 cyy). The box is taken for
-// 40.8 det (2 % on q) plus 0.01 px: for correlations |cxy| / sqrt(cxx cyy)
-// <= 0.999 the float evaluation of q and det is within 0.04 % of exact, so
-// the computed exponent stays below -20.39 outside it. Other records: no box
-// (density 0 everywhere when |det| < EPSILON; unbounded otherwise).
-__device__ __forceinline__ float2 density_extent(const Rec& g) {
+// Exponent cutoff of one record for compositing: a pixel whose exponent
+// (rec_density's -q / (2 det)) is below it gets a density below 1e-8 and is
+// skipped by the compositing, so the pixel may skip it without evaluating
+// expf and the division. The cutoff is max(-20, ln(1e-8 norm) - 1e-3):
+// below -20 rec_density returns 0; below ln(1e-8 norm) - 1e-3 the exact
+// exp is below 0.999e-8 norm, and expf (at most 2 ulp from exp, the CUDA
+// math library's documented bound), the correctly rounded division by norm
+// and the error of logf and of the product 1e-8f * norm (both below 1e-6
+// relative) keep the computed density below 1e-8. A NaN from logf leaves the
+// cutoff at -20; an infinite norm gives +inf (density 0 or NaN -> 0 there).
+__device__ __forceinline__ float density_cutoff(const Rec& g) {
+  return fmaxf(-20.0f, logf(mul_(1e-8f, g.norm)) - 1e-3f);
+}
+
+// Half-widths (columns, rows) of the box outside which a record's exponent is
+// below `cutoff` (< 0). The exponent is -q / (2 det) with
+// q = cxx dy^2 + cyy dx^2 - 2 cxy dx dy, and q <= K det implies
+// |dx| <= sqrt(K cxx), |dy| <= sqrt(K cyy). The box is taken for
+// K = -2.04 cutoff (2 % on q) plus 0.01 px: for correlations
+// |cxy| / sqrt(cxx cyy) <= 0.999 the float evaluation of q and det is within
+// 0.04 % of exact, so the computed exponent stays below 1.019 cutoff < cutoff
+// outside it. Other records: no box (density 0 everywhere when
+// |det| < EPSILON; unbounded otherwise, or when cutoff >= -0.01).
+__device__ __forceinline__ float2 density_extent(const Rec& g, float cutoff) {
   if (g.norm < 0.0f) return make_float2(-1.0f, -1.0f);
   const float cxx = g.cxx, cyy = g.cyy, cxy = g.cxy;
   const bool bounded = cxx > 0.0f && cyy > 0.0f && cxx < 1e30f && cyy < 1e30f && g.inv_det > 0.0f &&
-                       cxy * cxy <= 0.998f * (cxx * cyy);
+                       cxy * cxy <= 0.998f * (cxx * cyy) && cutoff < -0.01f;
   if (!bounded) return make_float2(INFINITY, INFINITY);
-  return make_float2(sqrtf(40.8f * cxx) + 0.01f, sqrtf(40.8f * cyy) + 0.01f);
+  const float k = -2.04f * cutoff;
+  return make_float2(sqrtf(k * cxx) + 0.01f, sqrtf(k * cyy) + 0.01f);
 }
 
 // One CTA per tile: the tile's sorted records arrive with one TMA bulk copy;
 // warp w composites an 8 x (4 kPix) pixel block, each lane kPix pixels of one
 // range row (azimuth columns c, c + 4; lanes along range, contiguous in the
 // image). Before compositing, each warp marks, per 8 x 4 half of its block,
-// the records whose density box meets that half (one bit per record, two
-// ballots): every pixel outside a record's box evaluates its density to 0
-// (< 1e-8) and skips it, so visiting only the marked records, in list order,
-// leaves each pixel's arithmetic the reference's, record by record.
-__device__ __forceinline__ void composite_one(const Rec& g, float fx, float fy, float& value,
-                                              float& trans, bool& done) {
-  const float gamma_ipp = rec_density(g, fx, fy);
+// the records whose cutoff box (density_extent) meets that half (one bit per
+// record, two ballots): every pixel outside a record's box is skipped by the
+// compositing, so visiting only the marked records, in list order, leaves
+// each pixel's arithmetic the reference's, record by record.
+//
+// composite_one: rec_density (compute_gaussian_density_2d) and the
+// compositing step for one pixel and one record whose norm is >= 0 (records
+// with norm < 0 have an empty box and are never visited); a pixel whose
+// exponent is below the record's cutoff returns before expf, as the
+// reference's density would be below 1e-8 there.
+__device__ __forceinline__ void composite_one(const Rec& g, float cutoff, float fx, float fy,
+                                              float& value, float& trans, bool& done) {
+  const float dx = sub_(fx, g.mx);
+  const float dy = sub_(fy, g.my);
+  const float q = fma_(mul_(g.cxx, dy), dy,
+                       fma_(mul_(g.cyy, dx), dx, -mul_(mul_(mul_(2.0f, g.cxy), dx), dy)));
+  const float exponent = mul_(mul_(-0.5f, q), g.inv_det);
+  if (exponent < cutoff) return;
+  const float gamma_ipp = fmaxf(div_(expf(exponent), g.norm), 0.0f);
   if (gamma_ipp < 1e-8f) return;
   const float alpha_i = mul_(g.sigma, gamma_ipp);
   value = fma_(mul_(trans, alpha_i), g.s_pos, value);
@@ -1575,7 +1603,9 @@ __device__ __forceinline__ void composite_one(const Rec& g, float fx, float fy, 
 // flight when the grid is small).
 template <int kPix>
 __global__ void __launch_bounds__(kPix == 2 ? 128 : 256) render_kernel(const TileArgs a) {
+  constexpr int kWarps = kPix == 2 ? 4 : 8;
   __shared__ __align__(16) Rec s_rec[kCap];
+  __shared__ float s_cut[kWarps][kCap];
   __shared__ uint64_t bar;
   const int v = blockIdx.y, t = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -1599,11 +1629,12 @@ __global__ void __launch_bounds__(kPix == 2 ? 128 : 256) render_kernel(const Til
   if (count > 0) {
     const bool ok = load_tile_recs(s_rec, &bar, st, a.st.L, t, count, a.err, true);
     if (__syncthreads_and(ok)) {
-      // hit[i] bit k: record k's density box meets columns [c0 + 4i, c0 + 4i + 3]
+      // hit[i] bit k: record k's cutoff box meets columns [c0 + 4i, c0 + 4i + 3]
       // of rows [r0, r0 + 7]
       uint64_t hit[kPix];
 #pragma unroll
       for (int i = 0; i < kPix; ++i) hit[i] = 0;
+      float* cut = s_cut[warp];
       const float by0 = (float)r0, by1 = (float)(r0 + 7);
       for (int h = 0; h < (count > 32 ? 2 : 1); ++h) {
         const int k = lane + 32 * h;
@@ -1612,7 +1643,9 @@ __global__ void __launch_bounds__(kPix == 2 ? 128 : 256) render_kernel(const Til
         for (int i = 0; i < kPix; ++i) in[i] = false;
         if (k < count) {
           const Rec& g = s_rec[k];
-          const float2 e = density_extent(g);
+          const float cutoff = density_cutoff(g);
+          cut[k] = cutoff;
+          const float2 e = density_extent(g, cutoff);
           const float mdy = fmaxf(0.0f, fmaxf(by0 - g.my, g.my - by1));
           if (!(mdy > e.y)) {
 #pragma unroll
@@ -1627,6 +1660,7 @@ __global__ void __launch_bounds__(kPix == 2 ? 128 : 256) render_kernel(const Til
         for (int i = 0; i < kPix; ++i)
           hit[i] |= (uint64_t)__ballot_sync(0xffffffffu, in[i]) << (32 * h);
       }
+      __syncwarp();
       uint64_t todo = hit[0];
 #pragma unroll
       for (int i = 1; i < kPix; ++i) todo |= hit[i];
@@ -1635,11 +1669,12 @@ __global__ void __launch_bounds__(kPix == 2 ? 128 : 256) render_kernel(const Til
         const int k = __ffsll((long long)todo) - 1;
         todo &= todo - 1;
         const Rec& g = s_rec[k];
+        const float cutoff = cut[k];
         bool all_done = true;
 #pragma unroll
         for (int i = 0; i < kPix; ++i) {
           if (!done[i] && ((hit[i] >> k) & 1))
-            composite_one(g, (float)(pc0 + 4 * i), fy, value[i], trans[i], done[i]);
+            composite_one(g, cutoff, (float)(pc0 + 4 * i), fy, value[i], trans[i], done[i]);
           all_done = all_done && done[i];
         }
         if (all_done) break;
