@@ -23,6 +23,7 @@ reference ships no CPU implementation) on the host cores, and times the
 reference's own CUDA kernels on a few views as `gpu_reference`.
 """
 import argparse
+import hashlib
 import json
 import os
 import statistics
@@ -222,6 +223,14 @@ def kernel_bytes_per_launch(kind, n, views, T, cov_floats, sh_floats, npix):
     return None
 
 
+def image_digest(images):
+    """(float64 sum, SHA-1 prefix of the bytes) of a step's images; the hash
+    is bit-exact, the sum is for reading (its reduction order may vary)."""
+    host = images.cpu()
+    return (float(host.double().sum().item()),
+            hashlib.sha1(host.numpy().tobytes()).hexdigest()[:16])
+
+
 def bench_ours(args, d):
     dev = d.device
     torch.cuda.set_device(dev)
@@ -242,7 +251,7 @@ def bench_ours(args, d):
         flush_l2(flush, k)
         step()
     torch.cuda.synchronize()
-    checksum0 = float(images.double().sum().item())
+    checksum0 = image_digest(images)
     d.barrier()
 
     clocks = Clocks(dev)
@@ -267,7 +276,7 @@ def bench_ours(args, d):
     value = total_views / (t_ms_max / 1e3)
 
     # checksum of the last step's images (guards against a step doing no work)
-    checksum = float(images.double().sum().item())
+    checksum = image_digest(images)
 
     # roofline: per-kernel device time from the library's event hooks
     _native.profile_enable(True)
@@ -578,8 +587,8 @@ def main():
             "data": "synthetic (seeded; BASELINE sweep distributions)", "config": config(args),
             "roofline": r["roofline"], "gpu_launches": r["launches"], "clocks": r["clocks"],
             "kernel_rooflines": r["kernel_rooflines"], "path_roofline": path_roofline(args, r, d.world),
-            "kernels": r["kernels"], "image_checksum": r["checksum"],
-            "image_checksum_stable": r["checksum_stable"]}
+            "kernels": r["kernels"], "image_checksum": r["checksum"][0],
+            "image_sha1": r["checksum"][1], "image_checksum_stable": r["checksum_stable"]}
     if "e2e" in r:
         line["e2e"] = r["e2e"]
     if "fwd_bwd" in r:

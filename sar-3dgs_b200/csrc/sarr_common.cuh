@@ -110,10 +110,13 @@ struct ViewConst {
   float center_margin;                   // its error bound [px], with room to spare
 };
 
-struct ViewHostPack {
+template <int kViews>
+struct ViewHostPackN {
   int n;
-  ViewHost v[kMaxViewsPerLaunch];
+  ViewHost v[kViews];
 };
+using ViewHostPack = ViewHostPackN<kMaxViewsPerLaunch>;
+constexpr int kSmallViewPack = 8;  // parameter block of launches of at most 8 views
 
 // One Gaussian of a tile list, as the compositing kernels read it.
 // For the image-plane list (mx, my) = (ipp_c, ipp_r) and (cxx, cxy, cyy) =

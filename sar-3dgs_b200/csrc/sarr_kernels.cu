@@ -44,7 +44,10 @@ namespace sarr {
 // view setup
 // ---------------------------------------------------------------------------
 // The pack is a __grid_constant__ parameter: indexed in place, not copied.
-__global__ void view_setup_kernel(const __grid_constant__ ViewHostPack pack,
+// kViews: capacity of the parameter block (the kernel parameters are copied
+// per launch, so calls of a few views use a small block).
+template <int kViews>
+__global__ void view_setup_kernel(const __grid_constant__ ViewHostPackN<kViews> pack,
                                   ViewConst* __restrict__ out, int* err) {
   const int v = blockIdx.x * blockDim.x + threadIdx.x;
   if (err && v == 0) *err = 0;
@@ -1565,6 +1568,45 @@ __device__ __forceinline__ float2 density_extent(const Rec& g, float cutoff) {
   return make_float2(sqrtf(k * cxx) + 0.01f, sqrtf(k * cyy) + 0.01f);
 }
 
+// rec_density (compute_gaussian_density_2d :215-234) of a record whose norm is
+// >= 0 at pixel (px, py), or 0 where the exponent is below the record's
+// cutoff (there the reference's density is below 1e-8, and every caller
+// treats such a density as no contribution). Records with norm < 0 have an
+// empty cutoff box and reach no caller.
+__device__ __forceinline__ float density_above_cutoff(const Rec& g, float cutoff, float px,
+                                                      float py) {
+  const float dx = sub_(px, g.mx);
+  const float dy = sub_(py, g.my);
+  const float q = fma_(mul_(g.cxx, dy), dy,
+                       fma_(mul_(g.cyy, dx), dx, -mul_(mul_(mul_(2.0f, g.cxy), dx), dy)));
+  const float exponent = mul_(mul_(-0.5f, q), g.inv_det);
+  if (exponent < cutoff) return 0.0f;
+  return fmaxf(div_(expf(exponent), g.norm), 0.0f);
+}
+
+// Marks, for the records of one tile (lanes hold records lane and lane + 32),
+// those whose cutoff box meets the pixel block [bx0, bx1] x [by0, by1]
+// (columns x rows), and stores every record's cutoff in cut[]. Warp-wide.
+__device__ __forceinline__ uint64_t block_hits(const Rec* recs, int count, float* cut, float bx0,
+                                               float bx1, float by0, float by1, int lane) {
+  uint64_t hit = 0;
+  for (int h = 0; h < (count > 32 ? 2 : 1); ++h) {
+    const int k = lane + 32 * h;
+    bool in = false;
+    if (k < count) {
+      const Rec& g = recs[k];
+      const float cutoff = density_cutoff(g);
+      cut[k] = cutoff;
+      const float2 e = density_extent(g, cutoff);
+      const float mdx = fmaxf(0.0f, fmaxf(bx0 - g.mx, g.mx - bx1));
+      const float mdy = fmaxf(0.0f, fmaxf(by0 - g.my, g.my - by1));
+      in = !(mdx > e.x) && !(mdy > e.y);
+    }
+    hit |= (uint64_t)__ballot_sync(0xffffffffu, in) << (32 * h);
+  }
+  return hit;
+}
+
 // One CTA per tile: the tile's sorted records arrive with one TMA bulk copy;
 // warp w composites an 8 x (4 kPix) pixel block, each lane kPix pixels of one
 // range row (azimuth columns c, c + 4; lanes along range, contiguous in the
@@ -1574,20 +1616,9 @@ __device__ __forceinline__ float2 density_extent(const Rec& g, float cutoff) {
 // compositing, so visiting only the marked records, in list order, leaves
 // each pixel's arithmetic the reference's, record by record.
 //
-// composite_one: rec_density (compute_gaussian_density_2d) and the
-// compositing step for one pixel and one record whose norm is >= 0 (records
-// with norm < 0 have an empty box and are never visited); a pixel whose
-// exponent is below the record's cutoff returns before expf, as the
-// reference's density would be below 1e-8 there.
 __device__ __forceinline__ void composite_one(const Rec& g, float cutoff, float fx, float fy,
                                               float& value, float& trans, bool& done) {
-  const float dx = sub_(fx, g.mx);
-  const float dy = sub_(fy, g.my);
-  const float q = fma_(mul_(g.cxx, dy), dy,
-                       fma_(mul_(g.cyy, dx), dx, -mul_(mul_(mul_(2.0f, g.cxy), dx), dy)));
-  const float exponent = mul_(mul_(-0.5f, q), g.inv_det);
-  if (exponent < cutoff) return;
-  const float gamma_ipp = fmaxf(div_(expf(exponent), g.norm), 0.0f);
+  const float gamma_ipp = density_above_cutoff(g, cutoff, fx, fy);
   if (gamma_ipp < 1e-8f) return;
   const float alpha_i = mul_(g.sigma, gamma_ipp);
   value = fma_(mul_(trans, alpha_i), g.s_pos, value);
@@ -1798,6 +1829,7 @@ __global__ void __launch_bounds__(256) omega_scatter_kernel(const OmegaScatterAr
 __global__ void __launch_bounds__(kWarpsPerTile * 32) bwd_tile_kernel(const TileArgs a) {
   __shared__ __align__(16) Rec s_rec[kCap];
   __shared__ float s_red[kWarpsPerTile][kCap][8];
+  __shared__ float s_cut[kWarpsPerTile][kCap];
   __shared__ uint64_t bar;
   const int v = blockIdx.y, t = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -1816,13 +1848,21 @@ __global__ void __launch_bounds__(kWarpsPerTile * 32) bwd_tile_kernel(const Tile
   const float dL_d_pixel = in ? a.images[v * a.img_vstride + (size_t)pc * Nr + pr] : 0.0f;
   const float fx = (float)pc, fy = (float)pr;
   float prev_transmittance = 1.0f;
+  // Records whose cutoff box misses the warp's 2 x 16 pixel block have no
+  // contributing pixel there: their sums stay 0.
+  for (int e = lane; e < count * 8; e += 32) (&s_red[warp][0][0])[e] = 0.0f;
+  const float bx0 = (float)(tx * kTile + warp * 2), by0 = (float)(ty * kTile);
+  uint64_t todo = block_hits(s_rec, count, s_cut[warp], bx0, bx0 + 1.0f, by0, by0 + 15.0f, lane);
+  __syncwarp();
 
-  for (int k = 0; k < count; ++k) {
+  while (todo) {
+    const int k = __ffsll((long long)todo) - 1;
+    todo &= todo - 1;
     const Rec& g = s_rec[k];
     float A[7] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     bool contrib = false;
     if (in) {
-      const float gamma_ipp = rec_density(g, fx, fy);
+      const float gamma_ipp = density_above_cutoff(g, s_cut[warp][k], fx, fy);
       if (gamma_ipp >= 1e-8f) {
         contrib = true;
         const float sigma_i = g.sigma;
@@ -1868,10 +1908,10 @@ __global__ void __launch_bounds__(kWarpsPerTile * 32) bwd_tile_kernel(const Tile
     if (__any_sync(0xffffffffu, contrib)) {
 #pragma unroll
       for (int c = 0; c < 7; ++c) A[c] = warp_sum(A[c]);
-    }
-    if (lane == 0) {
+      if (lane == 0) {
 #pragma unroll
-      for (int c = 0; c < 7; ++c) s_red[warp][k][c] = A[c];
+        for (int c = 0; c < 7; ++c) s_red[warp][k][c] = A[c];
+      }
     }
   }
   __syncthreads();
@@ -2086,7 +2126,14 @@ static void launch_bin_skip_t(const BinArgs& a, dim3 grid, size_t smem, cudaStre
 
 cudaError_t launch_view_setup(const ViewHostPack& pack, ViewConst* out, int* err_to_clear,
                               cudaStream_t s) {
-  view_setup_kernel<<<(pack.n + 31) / 32, 32, 0, s>>>(pack, out, err_to_clear);
+  if (pack.n <= kSmallViewPack) {
+    ViewHostPackN<kSmallViewPack> small;
+    small.n = pack.n;
+    for (int v = 0; v < kSmallViewPack; ++v) small.v[v] = pack.v[v];
+    view_setup_kernel<kSmallViewPack><<<1, 32, 0, s>>>(small, out, err_to_clear);
+  } else {
+    view_setup_kernel<kMaxViewsPerLaunch><<<(pack.n + 31) / 32, 32, 0, s>>>(pack, out, err_to_clear);
+  }
   return cudaGetLastError();
 }
 
