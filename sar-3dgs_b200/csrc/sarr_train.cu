@@ -29,41 +29,72 @@ constexpr int kMaxWindow = 11;
 // Sigma = R diag(exp(s))^2 R^T with R from the quaternion (w, x, y, z) as
 // Quaternion.to_rotation_matrix writes it (gaussian_model.py:40-51, not
 // normalised); transmittance = sigmoid(logit).
-__global__ void gaussian_params_kernel(int64_t n, const float* __restrict__ scales,
-                                       const float* __restrict__ rot, int cov_layout,
-                                       float* __restrict__ cov, const float* __restrict__ logits,
-                                       float* __restrict__ sigma) {
-  const int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (j >= n) return;
+__device__ __forceinline__ void gaussian_cov(float l0, float l1, float l2, float w, float x, float y,
+                                             float z, float S[3][3]) {
+  const float s0 = expf(l0), s1 = expf(l1), s2 = expf(l2);
+  const float R[3][3] = {{1.0f - 2.0f * (y * y + z * z), 2.0f * (x * y - w * z), 2.0f * (x * z + w * y)},
+                         {2.0f * (x * y + w * z), 1.0f - 2.0f * (x * x + z * z), 2.0f * (y * z - w * x)},
+                         {2.0f * (x * z - w * y), 2.0f * (y * z + w * x), 1.0f - 2.0f * (x * x + y * y)}};
+  const float d[3] = {s0 * s0, s1 * s1, s2 * s2};
+#pragma unroll
+  for (int a = 0; a < 3; ++a)
+#pragma unroll
+    for (int b = 0; b < 3; ++b) S[a][b] = R[a][0] * d[0] * R[b][0] + R[a][1] * d[1] * R[b][1] + R[a][2] * d[2] * R[b][2];
+}
+
+// One thread per Gaussian, kParamThreads Gaussians per CTA. `staged`: the
+// rows of a full CTA move through shared memory with 16-byte loads and stores
+// (all rows of the CTA are contiguous: 3, 4 and 6 or 9 floats per Gaussian),
+// so every warp access is coalesced; a partial last CTA, or unaligned
+// pointers, read and write per Gaussian.
+constexpr int kParamThreads = 256;
+
+__global__ void __launch_bounds__(kParamThreads) gaussian_params_kernel(
+    int64_t n, const float* __restrict__ scales, const float* __restrict__ rot, int cov_layout,
+    float* __restrict__ cov, const float* __restrict__ logits, float* __restrict__ sigma, bool staged) {
+  __shared__ __align__(16) float s_sc[kParamThreads * 3];
+  __shared__ __align__(16) float s_cov[kParamThreads * 9];
+  const int tid = threadIdx.x;
+  const int64_t j0 = (int64_t)blockIdx.x * kParamThreads, j = j0 + tid;
+  const bool full = staged && j0 + kParamThreads <= n;  // the same for the whole CTA
+  const int cw = cov_layout == SARR_COV33 ? 9 : 6;
   if (cov) {
-    const float s0 = expf(scales[3 * j]), s1 = expf(scales[3 * j + 1]), s2 = expf(scales[3 * j + 2]);
-    const float w = rot[4 * j], x = rot[4 * j + 1], y = rot[4 * j + 2], z = rot[4 * j + 3];
-    const float R[3][3] = {{1.0f - 2.0f * (y * y + z * z), 2.0f * (x * y - w * z), 2.0f * (x * z + w * y)},
-                           {2.0f * (x * y + w * z), 1.0f - 2.0f * (x * x + z * z), 2.0f * (y * z - w * x)},
-                           {2.0f * (x * z - w * y), 2.0f * (y * z + w * x), 1.0f - 2.0f * (x * x + y * y)}};
-    const float d[3] = {s0 * s0, s1 * s1, s2 * s2};
     float S[3][3];
+    if (full) {
+      const float4* src = reinterpret_cast<const float4*>(scales + 3 * j0);
+      for (int i = tid; i < kParamThreads * 3 / 4; i += kParamThreads)
+        reinterpret_cast<float4*>(s_sc)[i] = src[i];
+      const float4 q = reinterpret_cast<const float4*>(rot)[j];
+      __syncthreads();
+      gaussian_cov(s_sc[3 * tid], s_sc[3 * tid + 1], s_sc[3 * tid + 2], q.x, q.y, q.z, q.w, S);
+    } else if (j < n) {
+      gaussian_cov(scales[3 * j], scales[3 * j + 1], scales[3 * j + 2], rot[4 * j], rot[4 * j + 1],
+                   rot[4 * j + 2], rot[4 * j + 3], S);
+    }
+    float* o = full ? s_cov + cw * tid : cov + cw * j;
+    if (full || j < n) {
+      if (cw == 9) {
 #pragma unroll
-    for (int a = 0; a < 3; ++a)
+        for (int a = 0; a < 3; ++a)
 #pragma unroll
-      for (int b = 0; b < 3; ++b) S[a][b] = R[a][0] * d[0] * R[b][0] + R[a][1] * d[1] * R[b][1] + R[a][2] * d[2] * R[b][2];
-    if (cov_layout == SARR_COV33) {
-      float* o = cov + 9 * j;
-#pragma unroll
-      for (int a = 0; a < 3; ++a)
-#pragma unroll
-        for (int b = 0; b < 3; ++b) o[3 * a + b] = S[a][b];
-    } else {
-      float* o = cov + 6 * j;  // xx yy zz xy xz yz
-      o[0] = S[0][0];
-      o[1] = S[1][1];
-      o[2] = S[2][2];
-      o[3] = S[0][1];
-      o[4] = S[0][2];
-      o[5] = S[1][2];
+          for (int b = 0; b < 3; ++b) o[3 * a + b] = S[a][b];
+      } else {  // xx yy zz xy xz yz
+        o[0] = S[0][0];
+        o[1] = S[1][1];
+        o[2] = S[2][2];
+        o[3] = S[0][1];
+        o[4] = S[0][2];
+        o[5] = S[1][2];
+      }
+    }
+    if (full) {
+      __syncthreads();
+      float4* dst = reinterpret_cast<float4*>(cov + cw * j0);
+      for (int i = tid; i < kParamThreads * cw / 4; i += kParamThreads)
+        dst[i] = reinterpret_cast<const float4*>(s_cov)[i];
     }
   }
-  if (sigma) sigma[j] = 1.0f / (1.0f + expf(-logits[j]));
+  if (sigma && j < n) sigma[j] = 1.0f / (1.0f + expf(-logits[j]));
 }
 
 // ---------------------------------------------------------------------------
@@ -78,20 +109,40 @@ struct LossParams {
   float inv_count;      // 1 / (V H W)
 };
 
-constexpr int kTileX = 32, kTileY = 16;  // output pixels per CTA
-constexpr int kLossThreads = 256;
-constexpr int kHaloMax = kMaxWindow / 2;
+// Loss tiling: a CTA covers kTileX = 32 columns (one per lane) and
+// kLossWarps strips of kStrip rows (one strip per warp); each lane walks down
+// its column, applying the separable window along the row (from the shared
+// memory tile) and then along the column (from the last kWin row sums, kept
+// in registers).
+constexpr int kTileX = 32;
+constexpr int kLossThreads = 128, kLossWarps = kLossThreads / 32;
+constexpr int kStrip = 16;                      // rows per warp
+constexpr int kTileRows = kLossWarps * kStrip;  // output rows per CTA
 
-// Loads rows [y0 - half, y0 + kTileY + half) x columns [x0 - half, x0 + kTileX
-// + half) of image `img` (zero outside) into `tile`.
-__device__ __forceinline__ void load_halo(const float* __restrict__ img, int H, int W, int y0, int x0,
-                                          int half, float* tile, int pitch) {
-  const int rows = kTileY + 2 * half, cols = kTileX + 2 * half;
-  for (int i = threadIdx.x; i < rows * cols; i += kLossThreads) {
-    const int r = i / cols, c = i - r * cols;
-    const int y = y0 - half + r, x = x0 - half + c;
-    tile[r * pitch + c] = (y >= 0 && y < H && x >= 0 && x < W) ? img[(size_t)y * W + x] : 0.0f;
+// Copies rows [y0 - half, y0 + rows - half) x columns [x0 - half, x0 + kTileX
+// + half) of image `img` into `tile` with 4-byte cp.async copies (zero-filled
+// outside the image); the caller waits with cp_async_wait_all. Warp w takes
+// rows w, w + kLossWarps, ..., its lanes consecutive columns.
+__device__ __forceinline__ void load_halo_async(const float* __restrict__ img, int H, int W, int y0,
+                                                int x0, int half, int rows, float* tile, int pitch) {
+  const int cols = kTileX + 2 * half;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int r = warp; r < rows; r += kLossWarps) {
+    const int y = y0 - half + r;
+    const bool yin = y >= 0 && y < H;
+    for (int c = lane; c < cols; c += 32) {
+      const int x = x0 - half + c;
+      const bool in = yin && x >= 0 && x < W;
+      const float* src = in ? img + (size_t)y * W + x : img;  // not read when !in
+      const uint32_t dst = (uint32_t)__cvta_generic_to_shared(tile + r * pitch + c);
+      asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(in ? 4 : 0)
+                   : "memory");
+    }
   }
+}
+
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.wait_all;" ::: "memory");
 }
 
 // Weighted L1 factor of losses.py:28-62 (1 for the plain L1).
@@ -130,89 +181,99 @@ __global__ void loss_tmax_final_kernel(const float* partial, int n, float* tmax)
 // as F.conv2d with padding window/2), the SSIM map value, the L1 term, and
 // dm, de2, dept = d ssim / d (mean p, windowed mean of p^2, windowed mean of
 // p t), scaled by -ssim_weight / count for the gradient. Per-CTA sums of the
-// SSIM map and of the L1 term go to `partial` [2][blocks].
+// SSIM map and of the L1 term go to `partial` [2][blocks]. kWin: the (odd)
+// window size, so that every window loop unrolls.
+template <int kWin>
 __global__ void __launch_bounds__(kLossThreads) loss_moments_kernel(const LossParams P,
                                                                     const float* __restrict__ pred,
                                                                     const float* __restrict__ target,
                                                                     const float* __restrict__ tmax_p,
                                                                     float* __restrict__ dgrad,
                                                                     float* __restrict__ partial) {
-  constexpr int kRowsMax = kTileY + 2 * kHaloMax, kColsMax = kTileX + 2 * kHaloMax;
-  __shared__ float s_p[kRowsMax * kColsMax], s_t[kRowsMax * kColsMax];
-  __shared__ float s_h[5][kRowsMax * kTileX];  // horizontal pass of the 5 quantities
-  __shared__ float s_red[2][kLossThreads / 32];
-  const int v = blockIdx.z, y0 = blockIdx.y * kTileY, x0 = blockIdx.x * kTileX;
-  const int H = P.H, W = P.W, half = P.half, win = P.window;
-  const size_t img = (size_t)v * H * W;
-  const int pitch = kTileX + 2 * half;
-  load_halo(pred + img, H, W, y0, x0, half, s_p, pitch);
-  load_halo(target + img, H, W, y0, x0, half, s_t, pitch);
-  __syncthreads();
-  const int rows = kTileY + 2 * half;
-  for (int i = threadIdx.x; i < rows * kTileX; i += kLossThreads) {
-    const int r = i / kTileX, c = i - r * kTileX;
-    float a = 0.f, b = 0.f, aa = 0.f, bb = 0.f, ab = 0.f;
-    for (int k = 0; k < win; ++k) {
-      const float p = s_p[r * pitch + c + k], t = s_t[r * pitch + c + k], g = P.g[k];
-      a += g * p;
-      b += g * t;
-      aa += g * (p * p);
-      bb += g * (t * t);
-      ab += g * (p * t);
-    }
-    s_h[0][i] = a;
-    s_h[1][i] = b;
-    s_h[2][i] = aa;
-    s_h[3][i] = bb;
-    s_h[4][i] = ab;
-  }
+  constexpr int kHalf = kWin / 2, kIn = kStrip + 2 * kHalf;
+  constexpr int kRows = kTileRows + 2 * kHalf, kPitch = kTileX + 2 * kHalf;
+  __shared__ float s_p[kRows * kPitch], s_t[kRows * kPitch];
+  __shared__ float s_red[2][kLossWarps];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int v = blockIdx.z, y0 = blockIdx.y * kTileRows, x0 = blockIdx.x * kTileX;
+  const int H = P.H, W = P.W;
+  const size_t img = (size_t)v * H * W, plane = (size_t)P.V * H * W;
+  load_halo_async(pred + img, H, W, y0, x0, kHalf, kRows, s_p, kPitch);
+  load_halo_async(target + img, H, W, y0, x0, kHalf, kRows, s_t, kPitch);
+  float g[kWin];
+#pragma unroll
+  for (int k = 0; k < kWin; ++k) g[k] = P.g[k];
+  cp_async_wait_all();
   __syncthreads();
   const float C1 = 0.01f * 0.01f, C2 = 0.03f * 0.03f;
   const float tmax = tmax_p ? *tmax_p : 0.0f;
   const float gs = -P.ssim_weight * P.inv_count;
+  const int x = x0 + lane, rw = warp * kStrip;  // rw: the strip's first row in the tile
   float ssim_sum = 0.f, l1_sum = 0.f;
-  for (int i = threadIdx.x; i < kTileY * kTileX; i += kLossThreads) {
-    const int r = i / kTileX, c = i - r * kTileX;
-    const int y = y0 + r, x = x0 + c;
+  float hs[kWin][5];  // row sums of the last kWin input rows (ring)
+#pragma unroll
+  for (int q = 0; q < kIn; ++q) {
+    const float* rp = s_p + (rw + q) * kPitch + lane;
+    const float* rt = s_t + (rw + q) * kPitch + lane;
+    float a = 0.f, b = 0.f, aa = 0.f, bb = 0.f, ab = 0.f;
+#pragma unroll
+    for (int k = 0; k < kWin; ++k) {
+      const float p = rp[k], t = rt[k];
+      a += g[k] * p;
+      b += g[k] * t;
+      aa += g[k] * (p * p);
+      bb += g[k] * (t * t);
+      ab += g[k] * (p * t);
+    }
+    float* h = hs[q % kWin];
+    h[0] = a;
+    h[1] = b;
+    h[2] = aa;
+    h[3] = bb;
+    h[4] = ab;
+    if (q < kWin - 1) continue;
+    const int o = q - (kWin - 1);  // output row of the strip
+    const int y = y0 + rw + o;
     if (y >= H || x >= W) continue;
     float m[5] = {0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int k = 0; k < win; ++k) {
-      const float g = P.g[k];
 #pragma unroll
-      for (int q = 0; q < 5; ++q) m[q] += g * s_h[q][(r + k) * kTileX + c];
-    }
+    for (int k = 0; k < kWin; ++k)
+#pragma unroll
+      for (int u = 0; u < 5; ++u) m[u] += g[k] * hs[(o + k) % kWin][u];
     const float mp = m[0], mt = m[1];
     const float mp2 = mp * mp, mt2 = mt * mt, mpt = mp * mt;
     const float sp = m[2] - mp2, st = m[3] - mt2, spt = m[4] - mpt;
     const float A1 = 2.0f * mpt + C1, A2 = 2.0f * spt + C2;
     const float B1 = mp2 + mt2 + C1, B2 = sp + st + C2;
-    const float ssim = (A1 * A2) / (B1 * B2);
+    const float inv = 1.0f / (B1 * B2);
+    const float ssim = (A1 * A2) * inv;
     ssim_sum += ssim;
-    const float p = s_p[(r + half) * pitch + c + half], t = s_t[(r + half) * pitch + c + half];
+    const float p = s_p[(rw + o + kHalf) * kPitch + lane + kHalf];
+    const float t = s_t[(rw + o + kHalf) * kPitch + lane + kHalf];
     l1_sum += fabsf(p - t) * l1_factor(P.l1_mode, t, tmax);
     if (dgrad) {
-      const float inv = 1.0f / (B1 * B2);
-      const float d_mp = 2.0f * mt * A2 * inv - ssim * 2.0f * mp / B1;
-      const float d_sp = -ssim / B2;
+      // 1 / B1 = B2 inv and 1 / B2 = B1 inv
+      const float d_mp = 2.0f * mt * A2 * inv - ssim * 2.0f * mp * (B2 * inv);
+      const float d_sp = -ssim * (B1 * inv);
       const float d_spt = 2.0f * A1 * inv;
-      const size_t o = img + (size_t)y * W + x, plane = (size_t)P.V * H * W;
-      dgrad[o] = gs * (d_mp - 2.0f * mp * d_sp - mt * d_spt);
-      dgrad[plane + o] = gs * d_sp;
-      dgrad[2 * plane + o] = gs * d_spt;
+      const size_t oi = img + (size_t)y * W + x;
+      dgrad[oi] = gs * (d_mp - 2.0f * mp * d_sp - mt * d_spt);
+      dgrad[plane + oi] = gs * d_sp;
+      dgrad[2 * plane + oi] = gs * d_spt;
     }
   }
   for (int o = 16; o > 0; o >>= 1) {
     ssim_sum += __shfl_xor_sync(0xffffffffu, ssim_sum, o);
     l1_sum += __shfl_xor_sync(0xffffffffu, l1_sum, o);
   }
-  if ((threadIdx.x & 31) == 0) {
-    s_red[0][threadIdx.x >> 5] = ssim_sum;
-    s_red[1][threadIdx.x >> 5] = l1_sum;
+  if (lane == 0) {
+    s_red[0][warp] = ssim_sum;
+    s_red[1][warp] = l1_sum;
   }
   __syncthreads();
   if (threadIdx.x == 0) {
     float a = 0.f, b = 0.f;
-    for (int w = 0; w < kLossThreads / 32; ++w) {
+    for (int w = 0; w < kLossWarps; ++w) {
       a += s_red[0][w];
       b += s_red[1][w];
     }
@@ -225,67 +286,84 @@ __global__ void __launch_bounds__(kLossThreads) loss_moments_kernel(const LossPa
 
 // grad_j = l1_weight * factor * sign(p - t) / count
 //        + (K * dm)_j + 2 p_j (K * de2)_j + t_j (K * dept)_j
+template <int kWin>
 __global__ void __launch_bounds__(kLossThreads) loss_grad_kernel(const LossParams P,
                                                                  const float* __restrict__ pred,
                                                                  const float* __restrict__ target,
                                                                  const float* __restrict__ tmax_p,
                                                                  const float* __restrict__ dgrad,
                                                                  float* __restrict__ grad) {
-  constexpr int kRowsMax = kTileY + 2 * kHaloMax, kColsMax = kTileX + 2 * kHaloMax;
-  __shared__ float s_d[3][kRowsMax * kColsMax];
-  __shared__ float s_h[3][kRowsMax * kTileX];
-  const int v = blockIdx.z, y0 = blockIdx.y * kTileY, x0 = blockIdx.x * kTileX;
-  const int H = P.H, W = P.W, half = P.half, win = P.window;
+  constexpr int kHalf = kWin / 2, kIn = kStrip + 2 * kHalf;
+  constexpr int kRows = kTileRows + 2 * kHalf, kPitch = kTileX + 2 * kHalf;
+  __shared__ float s_d[3][kRows * kPitch];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int v = blockIdx.z, y0 = blockIdx.y * kTileRows, x0 = blockIdx.x * kTileX;
+  const int H = P.H, W = P.W;
   const size_t img = (size_t)v * H * W, plane = (size_t)P.V * H * W;
-  const int pitch = kTileX + 2 * half;
-  for (int q = 0; q < 3; ++q) load_halo(dgrad + q * plane + img, H, W, y0, x0, half, s_d[q], pitch);
-  __syncthreads();
-  const int rows = kTileY + 2 * half;
-  for (int i = threadIdx.x; i < rows * kTileX; i += kLossThreads) {
-    const int r = i / kTileX, c = i - r * kTileX;
-    float a[3] = {0.f, 0.f, 0.f};
-    for (int k = 0; k < win; ++k) {
-      const float g = P.g[k];
 #pragma unroll
-      for (int q = 0; q < 3; ++q) a[q] += g * s_d[q][r * pitch + c + k];
-    }
+  for (int u = 0; u < 3; ++u)
+    load_halo_async(dgrad + u * plane + img, H, W, y0, x0, kHalf, kRows, s_d[u], kPitch);
+  float g[kWin];
 #pragma unroll
-    for (int q = 0; q < 3; ++q) s_h[q][i] = a[q];
-  }
+  for (int k = 0; k < kWin; ++k) g[k] = P.g[k];
+  cp_async_wait_all();
   __syncthreads();
   const float tmax = tmax_p ? *tmax_p : 0.0f;
-  for (int i = threadIdx.x; i < kTileY * kTileX; i += kLossThreads) {
-    const int r = i / kTileX, c = i - r * kTileX;
-    const int y = y0 + r, x = x0 + c;
-    if (y >= H || x >= W) continue;
-    float a[3] = {0.f, 0.f, 0.f};
-    for (int k = 0; k < win; ++k) {
-      const float g = P.g[k];
+  const float l1s = P.l1_weight * P.inv_count;
+  const int x = x0 + lane, rw = warp * kStrip;
+  float hs[kWin][3];
 #pragma unroll
-      for (int q = 0; q < 3; ++q) a[q] += g * s_h[q][(r + k) * kTileX + c];
-    }
-    const size_t o = img + (size_t)y * W + x;
-    const float p = pred[o], t = target[o];
+  for (int q = 0; q < kIn; ++q) {
+    float a[3] = {0.f, 0.f, 0.f};
+#pragma unroll
+    for (int k = 0; k < kWin; ++k)
+#pragma unroll
+      for (int u = 0; u < 3; ++u) a[u] += g[k] * s_d[u][(rw + q) * kPitch + lane + k];
+#pragma unroll
+    for (int u = 0; u < 3; ++u) hs[q % kWin][u] = a[u];
+    if (q < kWin - 1) continue;
+    const int o = q - (kWin - 1);
+    const int y = y0 + rw + o;
+    if (y >= H || x >= W) continue;
+    float m[3] = {0.f, 0.f, 0.f};
+#pragma unroll
+    for (int k = 0; k < kWin; ++k)
+#pragma unroll
+      for (int u = 0; u < 3; ++u) m[u] += g[k] * hs[(o + k) % kWin][u];
+    const size_t oi = img + (size_t)y * W + x;
+    const float p = pred[oi], t = target[oi];
     const float diff = p - t;
     const float sgn = diff > 0.0f ? 1.0f : (diff < 0.0f ? -1.0f : 0.0f);
-    grad[o] = P.l1_weight * l1_factor(P.l1_mode, t, tmax) * sgn * P.inv_count + a[0] +
-              2.0f * p * a[1] + t * a[2];
+    grad[oi] = l1s * l1_factor(P.l1_mode, t, tmax) * sgn + m[0] + 2.0f * p * m[1] + t * m[2];
   }
 }
 
-// losses [3] = total, l1, dssim from the per-CTA sums (fixed order).
-__global__ void loss_reduce_kernel(const LossParams P, const float* partial, int nblk, float* losses) {
+// losses [3] = total, l1, dssim from the per-CTA sums: thread i adds blocks
+// i, i + kReduceThreads, ... in double, then a fixed pairwise tree (the same
+// order on every call).
+constexpr int kReduceThreads = 1024;
+
+__global__ void __launch_bounds__(kReduceThreads) loss_reduce_kernel(const LossParams P,
+                                                                     const float* partial, int nblk,
+                                                                     float* losses) {
+  __shared__ double s_ssim[kReduceThreads], s_l1[kReduceThreads];
   double ssim = 0.0, l1 = 0.0;
-  for (int i = threadIdx.x; i < nblk; i += 32) {
+  for (int i = threadIdx.x; i < nblk; i += kReduceThreads) {
     ssim += partial[i];
     l1 += partial[nblk + i];
   }
-  for (int o = 16; o > 0; o >>= 1) {
-    ssim += __shfl_xor_sync(0xffffffffu, ssim, o);
-    l1 += __shfl_xor_sync(0xffffffffu, l1, o);
+  s_ssim[threadIdx.x] = ssim;
+  s_l1[threadIdx.x] = l1;
+  __syncthreads();
+  for (int h = kReduceThreads / 2; h > 0; h >>= 1) {
+    if ((int)threadIdx.x < h) {
+      s_ssim[threadIdx.x] += s_ssim[threadIdx.x + h];
+      s_l1[threadIdx.x] += s_l1[threadIdx.x + h];
+    }
+    __syncthreads();
   }
   if (threadIdx.x == 0) {
-    const float l1m = (float)(l1 * P.inv_count), dssim = (float)(1.0 - ssim * P.inv_count);
+    const float l1m = (float)(s_l1[0] * P.inv_count), dssim = (float)(1.0 - s_ssim[0] * P.inv_count);
     losses[0] = P.l1_weight * l1m + P.ssim_weight * dssim;
     losses[1] = l1m;
     losses[2] = dssim;
@@ -301,7 +379,7 @@ constexpr int kTmaxBlocks = 256;
 LossWs loss_ws(int V, int H, int W) {
   LossWs L;
   const size_t plane = (size_t)V * H * W;
-  const size_t blocks = (size_t)((W + kTileX - 1) / kTileX) * ((H + kTileY - 1) / kTileY) * V;
+  const size_t blocks = (size_t)((W + kTileX - 1) / kTileX) * ((H + kTileRows - 1) / kTileRows) * V;
   size_t o = 0;
   L.dgrad = o;
   o += (3 * plane * 4 + 255) & ~(size_t)255;
@@ -317,6 +395,13 @@ LossWs loss_ws(int V, int H, int W) {
 
 int cuda_status(cudaError_t e) { return e == cudaSuccess ? SARR_OK : SARR_ERR_CUDA; }
 
+template <int kWin>
+void launch_loss(dim3 grid, cudaStream_t s, const LossParams& P, const float* pred, const float* target,
+                 const float* tmax, float* dgrad, float* partial, float* grad_pred) {
+  loss_moments_kernel<kWin><<<grid, kLossThreads, 0, s>>>(P, pred, target, tmax, dgrad, partial);
+  if (grad_pred) loss_grad_kernel<kWin><<<grid, kLossThreads, 0, s>>>(P, pred, target, tmax, dgrad, grad_pred);
+}
+
 }  // namespace
 
 extern "C" int sarr_gaussian_params(int64_t n, const float* scales_log, const float* rotations,
@@ -328,8 +413,10 @@ extern "C" int sarr_gaussian_params(int64_t n, const float* scales_log, const fl
   if (opacity_out && !opacity_logits) return SARR_ERR_ARG;
   if (n == 0 || (!cov_out && !opacity_out)) return SARR_OK;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  gaussian_params_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(n, scales_log, rotations, cov_layout,
-                                                                     cov_out, opacity_logits, opacity_out);
+  auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  const bool staged = !cov_out || (a16(scales_log) && a16(rotations) && a16(cov_out));
+  gaussian_params_kernel<<<(unsigned)((n + kParamThreads - 1) / kParamThreads), kParamThreads, 0, s>>>(
+      n, scales_log, rotations, cov_layout, cov_out, opacity_logits, opacity_out, staged);
   return cuda_status(cudaGetLastError());
 }
 
@@ -379,12 +466,18 @@ extern "C" int sarr_combined_loss(int n_images, int height, int width, const flo
     loss_tmax_final_kernel<<<1, 32, 0, s>>>(tp, kTmaxBlocks, reinterpret_cast<float*>(w + L.tmax));
     tmax = reinterpret_cast<const float*>(w + L.tmax);
   }
-  const dim3 grid((width + kTileX - 1) / kTileX, (height + kTileY - 1) / kTileY, n_images);
+  const dim3 grid((width + kTileX - 1) / kTileX, (height + kTileRows - 1) / kTileRows, n_images);
   const int nblk = grid.x * grid.y * grid.z;
   float* dgrad = grad_pred ? reinterpret_cast<float*>(w + L.dgrad) : nullptr;
   float* partial = reinterpret_cast<float*>(w + L.partial);
-  loss_moments_kernel<<<grid, kLossThreads, 0, s>>>(P, pred, target, tmax, dgrad, partial);
-  if (grad_pred) loss_grad_kernel<<<grid, kLossThreads, 0, s>>>(P, pred, target, tmax, dgrad, grad_pred);
-  loss_reduce_kernel<<<1, 32, 0, s>>>(P, partial, nblk, losses_out);
+  switch (window_size) {
+    case 1: launch_loss<1>(grid, s, P, pred, target, tmax, dgrad, partial, grad_pred); break;
+    case 3: launch_loss<3>(grid, s, P, pred, target, tmax, dgrad, partial, grad_pred); break;
+    case 5: launch_loss<5>(grid, s, P, pred, target, tmax, dgrad, partial, grad_pred); break;
+    case 7: launch_loss<7>(grid, s, P, pred, target, tmax, dgrad, partial, grad_pred); break;
+    case 9: launch_loss<9>(grid, s, P, pred, target, tmax, dgrad, partial, grad_pred); break;
+    default: launch_loss<11>(grid, s, P, pred, target, tmax, dgrad, partial, grad_pred); break;
+  }
+  loss_reduce_kernel<<<1, kReduceThreads, 0, s>>>(P, partial, nblk, losses_out);
   return cuda_status(cudaGetLastError());
 }
