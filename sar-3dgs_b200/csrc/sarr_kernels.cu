@@ -909,32 +909,41 @@ __global__ void __launch_bounds__(256) cell_fill_kernel(const CellPrepArgs a) {
 // world position, so its exact image centre lies within half_diag / rho
 // (pixels) of q's, and approximate-centre errors add center_margin at p and q.
 __global__ void __launch_bounds__(256) cell_test_kernel(const CellTestArgs a) {
-  const int c = blockIdx.x * 256 + threadIdx.x;
+  // one thread per spatial cell: its centre is projected once and tested
+  // with the bound of each of its kHbBuckets cells c = spatial * 4 + bucket
+  static_assert(kHbBuckets == 4, "a lane assembles one 4-bit nibble of the cell bitmap");
+  const int sc = blockIdx.x * 256 + threadIdx.x, lane = threadIdx.x & 31;
   const int v = blockIdx.y;
   const SceneGrid& g = *a.grid;
-  bool open = false;
-  if (g.valid && c < g.ncells) {
-    const float hbm = key_float(a.cell_hb[c]);
-    if (hbm >= 0.0f) {
-      const ViewConst& vc = a.views[v];
-      const int Nr = vc.h.Nr, Na = vc.h.Na, pitch = vc.tiles_x + 1;
-      const float4 q = a.cell_center[c / kHbBuckets];
-      float r, cc, xr, yr;
-      approx_center(vc, q.x, q.y, q.z, r, cc, xr, yr);
+  uint32_t nib = 0;
+  if (g.valid && sc * kHbBuckets < g.ncells) {
+    const ViewConst& vc = a.views[v];
+    const int Nr = vc.h.Nr, Na = vc.h.Na, pitch = vc.tiles_x + 1;
+    const float4 q = a.cell_center[sc];
+    float r, cc, xr, yr;
+    approx_center(vc, q.x, q.y, q.z, r, cc, xr, yr);
+    const float dr = g.half_diag * fabsf(vc.inv_rho_r) * 1.0001f;
+    const float dc = g.half_diag * fabsf(vc.inv_rho_a) * 1.0001f;
+    const float ds = g.half_diag * 1.0001f;
+    const int* open_ipp = a.open_ipp + v * a.open_vstride;
+    const int* open_sh = a.open_sh + v * a.open_vstride;
+#pragma unroll
+    for (int b = 0; b < kHbBuckets; ++b) {
+      const int c = sc * kHbBuckets + b;
+      const float hbm = key_float(a.cell_hb[c]);
+      if (!(hbm >= 0.0f)) continue;
       const float base = hbm + 2.0f * vc.center_margin + 0.02f;
-      const float hr = base + g.half_diag * fabsf(vc.inv_rho_r) * 1.0001f;
-      const float hc = base + g.half_diag * fabsf(vc.inv_rho_a) * 1.0001f;
-      open = open_in_rect(bound_rect2(r, cc, hr, hc, Nr, Na), a.open_ipp + v * a.open_vstride,
-                          pitch) > 0;
-      if (a.shadow && !open) {
-        const float hs = base + g.half_diag * 1.0001f;
-        open = open_in_rect(bound_rect2(yr, xr, hs, hs, Nr, Na), a.open_sh + v * a.open_vstride,
-                            pitch) > 0;
-      }
+      bool open = open_in_rect(bound_rect2(r, cc, base + dr, base + dc, Nr, Na), open_ipp, pitch) > 0;
+      if (a.shadow && !open)
+        open = open_in_rect(bound_rect2(yr, xr, base + ds, base + ds, Nr, Na), open_sh, pitch) > 0;
+      if (open) nib |= 1u << b;
     }
   }
-  const unsigned m = __ballot_sync(0xffffffffu, open);
-  if ((threadIdx.x & 31) == 0) a.bits[v * a.bits_vstride + (c >> 5)] = m;
+  // word k of the warp's 4 bitmap words holds the nibbles of lanes 8k .. 8k+7
+  uint32_t word = nib << (4 * (lane & 7));
+#pragma unroll
+  for (int o = 1; o < 8; o <<= 1) word |= __shfl_xor_sync(0xffffffffu, word, o);
+  if ((lane & 7) == 0) a.bits[v * a.bits_vstride + (sc * kHbBuckets >> 5)] = word;
   unsigned char* xs = a.ipp.base + v * a.ipp.vstride;
   uint32_t* xbits = reinterpret_cast<uint32_t*>(xs + a.ipp.L.xbits);
   const int64_t words = (a.n + 31) / 32;
@@ -1192,6 +1201,83 @@ __global__ void __launch_bounds__(kScanThreads) scan_kernel(const ScanArgs a) {
   if (warp == 0 && live) {
     reinterpret_cast<int*>(st + a.st.L.count)[t] = min(total, kCap);
     a.need_n[v * a.need_n_vstride + t] = s_nneed[lane];
+  }
+}
+
+// scan_kernel for tile counts that are a multiple of 4: each lane takes 4
+// adjacent tiles (one 32-bit load of their u8 counts per chunk), a CTA 128
+// tiles of one view, each warp a slice of the chunks.
+constexpr int kScanTilesPerLane = 4;
+constexpr int kScanTilesPerCta = 32 * kScanTilesPerLane;
+
+__global__ void __launch_bounds__(kScanThreads) scan4_kernel(const ScanArgs a) {
+  constexpr int kW = kScanThreads / 32;
+  __shared__ __align__(16) int s_part[kW][kScanTilesPerCta];
+  __shared__ int s_nneed[kScanTilesPerCta];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int v = blockIdx.y;
+  const int T = a.T, C = a.C;
+  const int tb = blockIdx.x * kScanTilesPerCta + kScanTilesPerLane * lane;  // the lane's first tile
+  const bool live = tb < T;
+  const uint8_t* counts = a.counts + v * a.counts_vstride;
+  const int per = (C + kW - 1) / kW;
+  const int c0 = min(warp * per, C), c1 = min(c0 + per, C);
+  int sum[4] = {0, 0, 0, 0};
+  if (live)
+#pragma unroll 8
+    for (int c = c0; c < c1; ++c) {
+      const uint32_t w = *reinterpret_cast<const uint32_t*>(counts + (size_t)c * T + tb);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) sum[i] += (w >> (8 * i)) & 0xFFu;
+    }
+  *reinterpret_cast<int4*>(&s_part[warp][kScanTilesPerLane * lane]) = make_int4(sum[0], sum[1], sum[2], sum[3]);
+  if (tid < kScanTilesPerCta) s_nneed[tid] = 0;
+  __syncthreads();
+  int pre[4] = {0, 0, 0, 0}, total[4] = {0, 0, 0, 0};
+  for (int w = 0; w < kW; ++w) {
+    const int4 x = *reinterpret_cast<const int4*>(&s_part[w][kScanTilesPerLane * lane]);
+    const int xs[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      pre[i] += (w < warp) ? xs[i] : 0;
+      total[i] += xs[i];
+    }
+  }
+  unsigned char* st = a.st.base + v * a.st.vstride;
+  int4* need = reinterpret_cast<int4*>(a.need + v * a.need_vstride);
+  auto open = [&]() {
+    bool o = false;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) o = o || pre[i] < kCap;
+    return o;
+  };
+  if (live && open()) {
+    // four chunks' words in flight per step
+    for (int cb = c0; cb < c1 && open(); cb += 4) {
+      uint32_t wv[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        wv[u] = cb + u < c1 ? *reinterpret_cast<const uint32_t*>(counts + (size_t)(cb + u) * T + tb) : 0u;
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int cnt = (int)((wv[u] >> (8 * i)) & 0xFFu);
+          if (cnt > 0 && pre[i] < kCap) {
+            const int q = atomicAdd(&s_nneed[kScanTilesPerLane * lane + i], 1);
+            need[(size_t)(tb + i) * kCap + q] = make_int4(cb + u, pre[i], cnt, 0);
+          }
+          pre[i] += cnt;
+        }
+    }
+  }
+  __syncthreads();
+  if (warp == 0 && live) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      reinterpret_cast<int*>(st + a.st.L.count)[tb + i] = min(total[i], kCap);
+      a.need_n[v * a.need_n_vstride + tb + i] = s_nneed[kScanTilesPerLane * lane + i];
+    }
   }
 }
 
@@ -2241,7 +2327,7 @@ cudaError_t launch_cell_prep(const CellPrepArgs& a, cudaStream_t s) {
 }
 
 cudaError_t launch_cell_test(const CellTestArgs& a, int nviews, cudaStream_t s) {
-  cell_test_kernel<<<dim3(kMaxCells / 256, nviews), 256, 0, s>>>(a);
+  cell_test_kernel<<<dim3(kMaxSpatialCells / 256, nviews), 256, 0, s>>>(a);
   return cudaGetLastError();
 }
 
@@ -2251,7 +2337,12 @@ cudaError_t launch_open_table(const OpenArgs& a, int nviews, int nlists, cudaStr
 }
 
 cudaError_t launch_scan(const ScanArgs& a, int nviews, cudaStream_t s) {
-  scan_kernel<<<dim3((a.T + 31) / 32, nviews), kScanThreads, 0, s>>>(a);
+  const bool aligned4 = (a.T % kScanTilesPerLane) == 0 && (reinterpret_cast<uintptr_t>(a.counts) & 3) == 0 &&
+                        (a.counts_vstride & 3) == 0;
+  if (aligned4)
+    scan4_kernel<<<dim3((a.T + kScanTilesPerCta - 1) / kScanTilesPerCta, nviews), kScanThreads, 0, s>>>(a);
+  else
+    scan_kernel<<<dim3((a.T + 31) / 32, nviews), kScanThreads, 0, s>>>(a);
   return cudaGetLastError();
 }
 
