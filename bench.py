@@ -617,7 +617,7 @@ def main():
     line = {"metric": METRIC, "value": r["value"], "unit": "views/s", "n_gpus": d.world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": r["ms_per_step"],
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic (seeded; BASELINE sweep distributions)", "config": config(args),
+            "data": "synthetic (seeded; the sweep's scene and view distributions)", "config": config(args),
             "roofline": r["roofline"], "gpu_launches": r["launches"], "clocks": r["clocks"],
             "kernel_rooflines": r["kernel_rooflines"], "path_roofline": path_roofline(args, r, d.world),
             "kernels": r["kernels"], "image_checksum": r["checksum"][0],

@@ -1,6 +1,6 @@
 """CPU restatement (numpy) of GaussianModel.densify_and_prune
 (gaussian_model.py:433-566 of SAR-3DGS), vectorised. Test infrastructure: the
-checker of sarr_densify_flags / sarr_densify_apply.
+oracle of sarr_densify_flags / sarr_densify_apply in the tests.
 
 Flags (:464-475): clone = |exp(s)| < size and |grad| > g; split = |exp(s)| >
 large and |grad| > g; prune = sigmoid(o) < opacity or |exp(s)| > large. New

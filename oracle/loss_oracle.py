@@ -1,6 +1,6 @@
 """CPU restatement (numpy, float64) of the reference's training loss,
 CombinedLoss of losses.py (SAR-3DGS), and of its gradient with respect to the
-predicted image. Test infrastructure: the checker of sarr_combined_loss.
+predicted image. Test infrastructure: the oracle of sarr_combined_loss in the tests.
 
 Forward (losses.py:160-219): L1 = mean |p - t| (weighted by
 1 + f(t / max t) for the weighted modes, losses.py:29-62); SSIM map from the

@@ -1,7 +1,7 @@
 """Test infrastructure: ctypes wrapper of the CPU oracle (oracle/sarr_oracle.c).
 
 Only tests/, __graft_entry__.smoke() and the CPU-baseline leg of bench.py use
-this module, as the checker of the CUDA library. The product never imports it.
+this module, as the oracle of the CUDA library. The product never imports it.
 
 Arrays are numpy float32 / int32. Images use the reference's azimuth-major
 memory layout: a flat array indexed c * Nr + r.
