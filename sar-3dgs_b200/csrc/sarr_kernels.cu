@@ -652,7 +652,8 @@ __global__ void __launch_bounds__(kBinThreads, 3) bin_skip_kernel(const BinArgs 
     return;
   }
   // few views: wpv warps share a view, each binning one contiguous slice of
-  // the chunk; the slices' counters and exact lists are merged in order
+  // the chunk; then all warps merge the slices' counters, masks and exact
+  // lists (in slice order) and write them out
   __shared__ uint16_t s_x[kWarps / 2][kChunk];
   __shared__ int s_xn[kWarps];
   const int wpv = kWarps / nv_cta;
@@ -665,39 +666,51 @@ __global__ void __launch_bounds__(kBinThreads, 3) bin_skip_kernel(const BinArgs 
     if (lane == 0) s_xn[warp] = xn;
   }
   __syncthreads();
-  if (active && sl == 0) {
+  if (active && a.xlist) {  // each warp places its own slice
     const int v = vbase + vl;
-    for (int o = 1; o < wpv; ++o) {
-      uint32_t* other = reinterpret_cast<uint32_t*>(s_hb + kChunk) + (warp + o) * TW * (kShadow ? 2 : 1);
-      for (int i = lane; i < TW * (kShadow ? 2 : 1); i += 32) {
-        s_cnt[i] += other[i];
-        other[i] = 0;
+    int off = 0;
+    for (int o = 0; o < sl; ++o) off += s_xn[vl * wpv + o];
+    const int n_s = s_xn[warp];
+    uint16_t* xl = x_list(a, v, chunk);
+    for (int i = lane; i < n_s; i += 32) xl[off + i] = s_x[vl][j_lo + i];
+    if (sl == wpv - 1 && lane == 0) x_count(a, v)[chunk] = off + n_s;
+  }
+  constexpr int kLists = kShadow ? 2 : 1;
+  const uint32_t* cnt0 = reinterpret_cast<const uint32_t*>(s_hb + kChunk);  // warp w: + w * TW * kLists
+  const uint32_t* mask0 = cnt0 + kWarps * TW * kLists;                     // warp w: + w * T * kLists
+  // counters: the 16-bit tile counts of the copies add without carry (a
+  // chunk holds 1024 Gaussians), then saturate to u8
+  const bool quad = (T & 3) == 0;
+  const int per_list = quad ? T / 4 : T;
+  for (int it = tid; it < nv_cta * kLists * per_list; it += kBinThreads) {
+    const int q = it % per_list, li = (it / per_list) % kLists, v_l = it / (per_list * kLists);
+    const int v = vbase + v_l;
+    uint8_t* out = (li ? a.counts_sh : a.counts_ipp) + v * a.counts_vstride + (size_t)chunk * T;
+    const uint32_t* c = cnt0 + (v_l * wpv) * TW * kLists + li * TW;
+    if (quad) {
+      uint32_t w0 = 0, w1 = 0;
+      for (int o = 0; o < wpv; ++o, c += TW * kLists) {
+        w0 += c[2 * q];
+        w1 += c[2 * q + 1];
       }
-      if (masks) {
-        uint32_t* om = s_mask + o * T * (kShadow ? 2 : 1);
-        for (int i = lane; i < T * (kShadow ? 2 : 1); i += 32) {
-          s_mask[i] |= om[i];
-          om[i] = 0;
-        }
-      }
+      const uint32_t c0 = min(w0 & 0xFFFFu, 255u), c1 = min(w0 >> 16, 255u);
+      const uint32_t c2 = min(w1 & 0xFFFFu, 255u), c3 = min(w1 >> 16, 255u);
+      reinterpret_cast<uint32_t*>(out)[q] = c0 | (c1 << 8) | (c2 << 16) | (c3 << 24);
+    } else {
+      uint32_t w = 0;
+      for (int o = 0; o < wpv; ++o, c += TW * kLists) w += c[q >> 1];
+      out[q] = (uint8_t)min((w >> ((q & 1) << 4)) & 0xFFFFu, 255u);
     }
-    __syncwarp();
-    if (a.xlist) {
-      uint16_t* xl = x_list(a, v, chunk);
-      int off = 0;
-      for (int o = 0; o < wpv; ++o) {
-        const int n_o = s_xn[warp + o];
-        const int lo = min(gcount, o * per);
-        for (int i = lane; i < n_o; i += 32) xl[off + i] = s_x[vl][lo + i];
-        off += n_o;
-      }
-      if (lane == 0) x_count(a, v)[chunk] = off;
-    }
-    flush_counts(s_cnt, a.counts_ipp + v * a.counts_vstride + (size_t)chunk * T, T, lane);
-    if (kShadow) flush_counts(s_cnt_sh, a.counts_sh + v * a.counts_vstride + (size_t)chunk * T, T, lane);
-    if (masks) {
-      flush_masks(s_mask, a.segmask + v * a.segmask_vstride + (size_t)chunk * T, T, lane);
-      if (kShadow) flush_masks(s_mask_sh, a.segmask_sh + v * a.segmask_vstride + (size_t)chunk * T, T, lane);
+  }
+  if (masks) {
+    for (int it = tid; it < nv_cta * kLists * T; it += kBinThreads) {
+      const int t = it % T, li = (it / T) % kLists, v_l = it / (T * kLists);
+      const uint32_t* m = mask0 + (v_l * wpv) * T * kLists + li * T + t;
+      uint32_t acc = 0;
+      for (int o = 0; o < wpv; ++o, m += T * kLists) acc |= *m;
+      // only nonzero masks are read (select_kernel reads the mask of a
+      // (chunk, tile) only when the chunk holds hits of the tile)
+      if (acc) (li ? a.segmask_sh : a.segmask)[(vbase + v_l) * a.segmask_vstride + (size_t)chunk * T + t] = acc;
     }
   }
 }
@@ -1174,6 +1187,7 @@ __global__ void __launch_bounds__(kScanThreads) scan_kernel(const ScanArgs a) {
   const int c0 = min(warp * per, C), c1 = min(c0 + per, C);
   int sum = 0;
   if (live)
+#pragma unroll 8
     for (int c = c0; c < c1; ++c) sum += counts[(size_t)c * T + t];
   s_part[warp][lane] = sum;
   if (warp == 0) s_nneed[lane] = 0;
@@ -2337,8 +2351,10 @@ cudaError_t launch_open_table(const OpenArgs& a, int nviews, int nlists, cudaStr
 }
 
 cudaError_t launch_scan(const ScanArgs& a, int nviews, cudaStream_t s) {
-  const bool aligned4 = (a.T % kScanTilesPerLane) == 0 && (reinterpret_cast<uintptr_t>(a.counts) & 3) == 0 &&
-                        (a.counts_vstride & 3) == 0;
+  // four tiles per lane for launches of many views (a few views would leave
+  // the GPU with too few CTAs)
+  const bool aligned4 = nviews >= 16 && (a.T % kScanTilesPerLane) == 0 &&
+                        (reinterpret_cast<uintptr_t>(a.counts) & 3) == 0 && (a.counts_vstride & 3) == 0;
   if (aligned4)
     scan4_kernel<<<dim3((a.T + kScanTilesPerCta - 1) / kScanTilesPerCta, nviews), kScanThreads, 0, s>>>(a);
   else
