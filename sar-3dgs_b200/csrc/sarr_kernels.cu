@@ -1202,13 +1202,19 @@ __global__ void __launch_bounds__(kScanThreads) scan_kernel(const ScanArgs a) {
   unsigned char* st = a.st.base + v * a.st.vstride;
   int4* need = reinterpret_cast<int4*>(a.need + v * a.need_vstride);
   if (live && pre < kCap) {
-    for (int c = c0; c < c1 && pre < kCap; ++c) {
-      const int cnt = counts[(size_t)c * T + t];
-      if (cnt > 0) {
-        const int q = atomicAdd(&s_nneed[lane], 1);
-        need[(size_t)t * kCap + q] = make_int4(c, pre, cnt, 0);
+    // eight chunks' counts in flight per step
+    for (int cb = c0; cb < c1 && pre < kCap; cb += 8) {
+      int cv[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) cv[u] = cb + u < c1 ? counts[(size_t)(cb + u) * T + t] : 0;
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        if (cv[u] > 0 && pre < kCap) {
+          const int q = atomicAdd(&s_nneed[lane], 1);
+          need[(size_t)t * kCap + q] = make_int4(cb + u, pre, cv[u], 0);
+        }
+        pre += cv[u];
       }
-      pre += cnt;
     }
   }
   __syncthreads();
