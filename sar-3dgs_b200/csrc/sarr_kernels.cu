@@ -1932,9 +1932,17 @@ __global__ void __launch_bounds__(256) omega_scatter_kernel(const OmegaScatterAr
 // Per (pixel, Gaussian) terms of backward_kernel (:910-1018), summed over the
 // tile: 0 grad_sigma, 1 dL/dpixel * dpixel/dS (times the SH basis later),
 // 2..4 grad_cov rr, cc, rc, 5..6 grad_ipp_r, grad_ipp_c.
+// The tile's records are split into kBwdParts consecutive parts, one CTA
+// each (grid.z): the CTA of part q replays the transmittance of every pixel
+// through the records before its part (the same operations in the same order
+// as the full traversal) and computes the gradient terms of its own records,
+// so the per-record sums are those of one front-to-back pass.
+constexpr int kBwdParts = 4;
+constexpr int kBwdPartRecs = kCap / kBwdParts;
+
 __global__ void __launch_bounds__(kWarpsPerTile * 32) bwd_tile_kernel(const TileArgs a) {
   __shared__ __align__(16) Rec s_rec[kCap];
-  __shared__ float s_red[kWarpsPerTile][kCap][8];
+  __shared__ float s_red[kWarpsPerTile][kBwdPartRecs][8];
   __shared__ float s_cut[kWarpsPerTile][kCap];
   __shared__ uint64_t bar;
   const int v = blockIdx.y, t = blockIdx.x;
@@ -1943,8 +1951,10 @@ __global__ void __launch_bounds__(kWarpsPerTile * 32) bwd_tile_kernel(const Tile
   const int Nr = vc.h.Nr, Na = vc.h.Na, tiles_x = vc.tiles_x;
   const int tx = t % tiles_x, ty = t / tiles_x;
   const unsigned char* st = a.st.base + v * a.st.vstride;
-  const int count = reinterpret_cast<const int*>(st + a.st.L.count)[t];
-  if (count == 0) return;
+  const int count_all = reinterpret_cast<const int*>(st + a.st.L.count)[t];
+  const int k_lo = blockIdx.z * kBwdPartRecs;
+  if (k_lo >= count_all) return;
+  const int count = min(count_all, k_lo + kBwdPartRecs);  // records [0, count) are read
   const bool ok = load_tile_recs(s_rec, &bar, st, a.st.L, t, count, a.err, true);
   if (!__syncthreads_and(ok)) return;
 
@@ -1956,10 +1966,26 @@ __global__ void __launch_bounds__(kWarpsPerTile * 32) bwd_tile_kernel(const Tile
   float prev_transmittance = 1.0f;
   // Records whose cutoff box misses the warp's 2 x 16 pixel block have no
   // contributing pixel there: their sums stay 0.
-  for (int e = lane; e < count * 8; e += 32) (&s_red[warp][0][0])[e] = 0.0f;
+  for (int e = lane; e < kBwdPartRecs * 8; e += 32) (&s_red[warp][0][0])[e] = 0.0f;
   const float bx0 = (float)(tx * kTile + warp * 2), by0 = (float)(ty * kTile);
   uint64_t todo = block_hits(s_rec, count, s_cut[warp], bx0, bx0 + 1.0f, by0, by0 + 15.0f, lane);
   __syncwarp();
+
+  // transmittance through the records before this part
+  uint64_t before = k_lo ? todo & ((1ull << k_lo) - 1ull) : 0ull;
+  todo &= ~before;
+  while (before) {
+    const int k = __ffsll((long long)before) - 1;
+    before &= before - 1;
+    const Rec& g = s_rec[k];
+    if (in) {
+      const float gamma_ipp = density_above_cutoff(g, s_cut[warp][k], fx, fy);
+      if (gamma_ipp >= 1e-8f) {
+        prev_transmittance = mul_(prev_transmittance, fma_(-g.sigma, gamma_ipp, 1.0f));
+        if (prev_transmittance < 1e-8f) prev_transmittance = 0.0f;
+      }
+    }
+  }
 
   while (todo) {
     const int k = __ffsll((long long)todo) - 1;
@@ -2016,18 +2042,18 @@ __global__ void __launch_bounds__(kWarpsPerTile * 32) bwd_tile_kernel(const Tile
       for (int c = 0; c < 7; ++c) A[c] = warp_sum(A[c]);
       if (lane == 0) {
 #pragma unroll
-        for (int c = 0; c < 7; ++c) s_red[warp][k][c] = A[c];
+        for (int c = 0; c < 7; ++c) s_red[warp][k - k_lo][c] = A[c];
       }
     }
   }
   __syncthreads();
   float* partial = a.partial + v * a.partial_vstride;
-  for (int e = tid; e < count * 7; e += kWarpsPerTile * 32) {
-    const int k = e / 7, c = e - k * 7;
+  for (int e = tid; e < (count - k_lo) * 7; e += kWarpsPerTile * 32) {
+    const int kp = e / 7, c = e - kp * 7;
     float acc = 0.0f;
 #pragma unroll
-    for (int w = 0; w < kWarpsPerTile; ++w) acc += s_red[w][k][c];
-    partial[((size_t)t * kCap + s_rec[k].pos) * 8 + c] = acc;
+    for (int w = 0; w < kWarpsPerTile; ++w) acc += s_red[w][kp][c];
+    partial[((size_t)t * kCap + s_rec[k_lo + kp].pos) * 8 + c] = acc;
   }
 }
 
@@ -2403,7 +2429,7 @@ cudaError_t launch_omega_scatter(const OmegaScatterArgs& a, const Dims& d, int n
 }
 
 cudaError_t launch_bwd_tile(const TileArgs& a, const Dims& d, int nviews, cudaStream_t s) {
-  bwd_tile_kernel<<<dim3(d.T, nviews), kWarpsPerTile * 32, 0, s>>>(a);
+  bwd_tile_kernel<<<dim3(d.T, nviews, kBwdParts), kWarpsPerTile * 32, 0, s>>>(a);
   return cudaGetLastError();
 }
 

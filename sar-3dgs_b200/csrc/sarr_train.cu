@@ -107,6 +107,7 @@ struct LossParams {
   float l1_weight, ssim_weight;
   int l1_mode;
   float inv_count;      // 1 / (V H W)
+  bool vec;             // W % 4 == 0 and 16-byte aligned images and workspace (16-byte halo copies)
 };
 
 // Loss tiling: a CTA covers kTileX = 32 columns (one per lane) and
@@ -119,24 +120,58 @@ constexpr int kLossThreads = 128, kLossWarps = kLossThreads / 32;
 constexpr int kStrip = 16;                      // rows per warp
 constexpr int kTileRows = kLossWarps * kStrip;  // output rows per CTA
 
-// Copies rows [y0 - half, y0 + rows - half) x columns [x0 - half, x0 + kTileX
-// + half) of image `img` into `tile` with 4-byte cp.async copies (zero-filled
-// outside the image); the caller waits with cp_async_wait_all. Warp w takes
-// rows w, w + kLossWarps, ..., its lanes consecutive columns.
+// Shared-memory tile of one image: rows [y0 - kHalf, y0 + rows - kHalf),
+// columns x0 - kPad + j for j in [0, kTileX + 2 kPad) (kPad = kHalf rounded up
+// to 4, so that the interior columns x0 .. x0 + 31 start on a 16-byte
+// boundary); only j in [kPad - kHalf, kPad + kTileX + kHalf) is filled.
+template <int kHalf>
+struct HaloTile {
+  static constexpr int kPad = (kHalf + 3) / 4 * 4;
+  static constexpr int kPitch = kTileX + 2 * kPad;
+};
+
+__device__ __forceinline__ void cp_async4(float* dst, const float* src, bool in) {
+  const uint32_t d = (uint32_t)__cvta_generic_to_shared(dst);
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(d), "l"(src), "r"(in ? 4 : 0) : "memory");
+}
+
+__device__ __forceinline__ void cp_async16(float* dst, const float* src, bool in) {
+  const uint32_t d = (uint32_t)__cvta_generic_to_shared(dst);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(src), "r"(in ? 16 : 0) : "memory");
+}
+
+// Fills the tile with cp.async copies (zero-filled outside the image); the
+// caller waits with cp_async_wait_all. `vec` (the 32 interior columns lie in
+// the image, W % 4 == 0 and `img` is 16-byte aligned): each row's interior
+// moves as eight 16-byte copies and only the 2 kHalf halo columns one by one.
+template <int kHalf>
 __device__ __forceinline__ void load_halo_async(const float* __restrict__ img, int H, int W, int y0,
-                                                int x0, int half, int rows, float* tile, int pitch) {
-  const int cols = kTileX + 2 * half;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  for (int r = warp; r < rows; r += kLossWarps) {
-    const int y = y0 - half + r;
-    const bool yin = y >= 0 && y < H;
-    for (int c = lane; c < cols; c += 32) {
-      const int x = x0 - half + c;
-      const bool in = yin && x >= 0 && x < W;
-      const float* src = in ? img + (size_t)y * W + x : img;  // not read when !in
-      const uint32_t dst = (uint32_t)__cvta_generic_to_shared(tile + r * pitch + c);
-      asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(in ? 4 : 0)
-                   : "memory");
+                                                int x0, int rows, float* tile, bool vec) {
+  using HT = HaloTile<kHalf>;
+  if (vec) {
+    constexpr int kPer = kTileX / 4 + 2 * kHalf;
+    for (int it = threadIdx.x; it < rows * kPer; it += kLossThreads) {
+      const int r = it / kPer, e = it - r * kPer;
+      const int y = y0 - kHalf + r;
+      const bool yin = y >= 0 && y < H;
+      float* row = tile + r * HT::kPitch;
+      if (e < kTileX / 4) {
+        cp_async16(row + HT::kPad + 4 * e, yin ? img + (size_t)y * W + x0 + 4 * e : img, yin);
+      } else {
+        const int h = e - kTileX / 4;
+        const int j = h < kHalf ? HT::kPad - kHalf + h : HT::kPad + kTileX + (h - kHalf);
+        const int x = x0 - HT::kPad + j;
+        const bool in = yin && x >= 0 && x < W;
+        cp_async4(row + j, in ? img + (size_t)y * W + x : img, in);
+      }
+    }
+  } else {
+    constexpr int kCols = kTileX + 2 * kHalf;
+    for (int it = threadIdx.x; it < rows * kCols; it += kLossThreads) {
+      const int r = it / kCols, c = it - r * kCols;
+      const int y = y0 - kHalf + r, x = x0 - kHalf + c;
+      const bool in = y >= 0 && y < H && x >= 0 && x < W;
+      cp_async4(tile + r * HT::kPitch + HT::kPad - kHalf + c, in ? img + (size_t)y * W + x : img, in);
     }
   }
 }
@@ -191,15 +226,17 @@ __global__ void __launch_bounds__(kLossThreads) loss_moments_kernel(const LossPa
                                                                     float* __restrict__ dgrad,
                                                                     float* __restrict__ partial) {
   constexpr int kHalf = kWin / 2, kIn = kStrip + 2 * kHalf;
-  constexpr int kRows = kTileRows + 2 * kHalf, kPitch = kTileX + 2 * kHalf;
-  __shared__ float s_p[kRows * kPitch], s_t[kRows * kPitch];
+  constexpr int kRows = kTileRows + 2 * kHalf, kPitch = HaloTile<kHalf>::kPitch;
+  constexpr int kOff = HaloTile<kHalf>::kPad - kHalf;  // tile column of x0 - kHalf
+  __shared__ __align__(16) float s_p[kRows * kPitch];
+  __shared__ __align__(16) float s_t[kRows * kPitch];
   __shared__ float s_red[2][kLossWarps];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int v = blockIdx.z, y0 = blockIdx.y * kTileRows, x0 = blockIdx.x * kTileX;
   const int H = P.H, W = P.W;
   const size_t img = (size_t)v * H * W, plane = (size_t)P.V * H * W;
-  load_halo_async(pred + img, H, W, y0, x0, kHalf, kRows, s_p, kPitch);
-  load_halo_async(target + img, H, W, y0, x0, kHalf, kRows, s_t, kPitch);
+  load_halo_async<kHalf>(pred + img, H, W, y0, x0, kRows, s_p, P.vec && x0 + kTileX <= W);
+  load_halo_async<kHalf>(target + img, H, W, y0, x0, kRows, s_t, P.vec && x0 + kTileX <= W);
   float g[kWin];
 #pragma unroll
   for (int k = 0; k < kWin; ++k) g[k] = P.g[k];
@@ -213,8 +250,8 @@ __global__ void __launch_bounds__(kLossThreads) loss_moments_kernel(const LossPa
   float hs[kWin][5];  // row sums of the last kWin input rows (ring)
 #pragma unroll
   for (int q = 0; q < kIn; ++q) {
-    const float* rp = s_p + (rw + q) * kPitch + lane;
-    const float* rt = s_t + (rw + q) * kPitch + lane;
+    const float* rp = s_p + (rw + q) * kPitch + kOff + lane;
+    const float* rt = s_t + (rw + q) * kPitch + kOff + lane;
     float a = 0.f, b = 0.f, aa = 0.f, bb = 0.f, ab = 0.f;
 #pragma unroll
     for (int k = 0; k < kWin; ++k) {
@@ -248,8 +285,8 @@ __global__ void __launch_bounds__(kLossThreads) loss_moments_kernel(const LossPa
     const float inv = 1.0f / (B1 * B2);
     const float ssim = (A1 * A2) * inv;
     ssim_sum += ssim;
-    const float p = s_p[(rw + o + kHalf) * kPitch + lane + kHalf];
-    const float t = s_t[(rw + o + kHalf) * kPitch + lane + kHalf];
+    const float p = s_p[(rw + o + kHalf) * kPitch + kOff + lane + kHalf];
+    const float t = s_t[(rw + o + kHalf) * kPitch + kOff + lane + kHalf];
     l1_sum += fabsf(p - t) * l1_factor(P.l1_mode, t, tmax);
     if (dgrad) {
       // 1 / B1 = B2 inv and 1 / B2 = B1 inv
@@ -294,15 +331,16 @@ __global__ void __launch_bounds__(kLossThreads) loss_grad_kernel(const LossParam
                                                                  const float* __restrict__ dgrad,
                                                                  float* __restrict__ grad) {
   constexpr int kHalf = kWin / 2, kIn = kStrip + 2 * kHalf;
-  constexpr int kRows = kTileRows + 2 * kHalf, kPitch = kTileX + 2 * kHalf;
-  __shared__ float s_d[3][kRows * kPitch];
+  constexpr int kRows = kTileRows + 2 * kHalf, kPitch = HaloTile<kHalf>::kPitch;
+  constexpr int kOff = HaloTile<kHalf>::kPad - kHalf;
+  __shared__ __align__(16) float s_d[3][kRows * kPitch];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int v = blockIdx.z, y0 = blockIdx.y * kTileRows, x0 = blockIdx.x * kTileX;
   const int H = P.H, W = P.W;
   const size_t img = (size_t)v * H * W, plane = (size_t)P.V * H * W;
 #pragma unroll
   for (int u = 0; u < 3; ++u)
-    load_halo_async(dgrad + u * plane + img, H, W, y0, x0, kHalf, kRows, s_d[u], kPitch);
+    load_halo_async<kHalf>(dgrad + u * plane + img, H, W, y0, x0, kRows, s_d[u], P.vec && x0 + kTileX <= W);
   float g[kWin];
 #pragma unroll
   for (int k = 0; k < kWin; ++k) g[k] = P.g[k];
@@ -318,7 +356,7 @@ __global__ void __launch_bounds__(kLossThreads) loss_grad_kernel(const LossParam
 #pragma unroll
     for (int k = 0; k < kWin; ++k)
 #pragma unroll
-      for (int u = 0; u < 3; ++u) a[u] += g[k] * s_d[u][(rw + q) * kPitch + lane + k];
+      for (int u = 0; u < 3; ++u) a[u] += g[k] * s_d[u][(rw + q) * kPitch + kOff + lane + k];
 #pragma unroll
     for (int u = 0; u < 3; ++u) hs[q % kWin][u] = a[u];
     if (q < kWin - 1) continue;
@@ -458,6 +496,8 @@ extern "C" int sarr_combined_loss(int n_images, int height, int width, const flo
   P.ssim_weight = ssim_weight;
   P.l1_mode = l1_mode;
   P.inv_count = (float)(1.0 / ((double)n_images * height * width));
+  auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  P.vec = (width & 3) == 0 && a16(pred) && a16(target) && a16(ws);
 
   const float* tmax = nullptr;
   if (l1_mode != SARR_L1_PLAIN) {

@@ -149,3 +149,39 @@ def test_results_do_not_depend_on_workspace_contents(nviews):
             np.testing.assert_array_equal(c1, c0)
             used = np.arange(64)[None, :] < c0[:, None]
             np.testing.assert_array_equal(l1[used], l0[used])
+
+
+@pytest.mark.parametrize("nviews,with_states", [(1, False), (1, True), (10, False), (10, True)])
+def test_backward_does_not_depend_on_workspace_contents(nviews, with_states):
+    """The backward reads nothing of the caller's workspace (and, without the
+    forward's states, of its own selection scratch) that it did not write:
+    zero-filled, 0xFF-filled and random-filled workspaces give bitwise equal
+    gradients, single view (per-view path) and 10 views (cell path)."""
+    n = 100000
+    sc = {k: v.cuda() for k, v in S.make_scene(n, (40.0, 40.0, 10.0), (0.05, 0.5), seed=56).items()}
+    views = S.sweep_views(80)[::8][:nviews]
+    inputs = _native.prepare_inputs(sc["means"], sc["cov6"], sc["sigma"], sc["sh"])
+    vs = [_native.make_view(*v) for v in views]
+    wsb = _native.workspace_bytes(n, 256, 256, nviews, 0)
+    sbytes = _native.state_bytes(n, 256, 256)
+    g = torch.Generator(device="cuda").manual_seed(11)
+    gimg = torch.randn((nviews, 256, 256), device="cuda", generator=g)
+    states = None
+    if with_states:
+        states = torch.empty(nviews * sbytes, dtype=torch.uint8, device="cuda")
+        imgs = torch.empty((nviews, 256, 256), device="cuda")
+        _native.forward(vs, *inputs, imgs, states=states, check_device=True)
+    out = {}
+    for fill in ("zero", "ff", "random"):
+        ws = torch.zeros(wsb, dtype=torch.uint8, device="cuda")
+        if fill == "ff":
+            ws.fill_(255)
+        elif fill == "random":
+            ws.random_(0, 256, generator=torch.Generator(device="cuda").manual_seed(12))
+        grads = [torch.full((n, c), float("nan"), device="cuda") for c in (3, 6, 1, 16, 1)]
+        _native.backward(vs, *inputs, gimg, grads[0], grads[1], _native.SARR_COV6, grads[2].view(n),
+                         grads[3], grad_norm=grads[4].view(n), states=states, ws=ws, check_device=True)
+        out[fill] = grads
+    for fill in ("ff", "random"):
+        for a, b in zip(out[fill], out["zero"]):
+            assert torch.equal(a, b)
