@@ -459,9 +459,10 @@ def bench_fwd_bwd(args, d, means, cov, layout, sigma, sh, sh_stride, sh_k, views
 def bench_train_ops(args, d):
     """The training-step kernels next to the rasterizer: the Gaussian
     parameter producer over the N Gaussians (72 B per Gaussian: log-scales,
-    quaternion and logit read, 3x3 covariance and transmittance written) and
-    the combined L1 + D-SSIM loss with its gradient over 64 images of the
-    sweep size (12 B per pixel: both images read, the gradient written)."""
+    quaternion and logit read, 3x3 covariance and transmittance written), the
+    combined L1 + D-SSIM loss with its gradient over 64 images of the sweep
+    size (12 B per pixel: both images read, the gradient written), and one
+    densify/prune pass over the N Gaussians."""
     from cuda_rasterizer import gaussian_params as GP  # noqa: F401
     dev = d.device
     n, s = args.n, args.samples
@@ -488,11 +489,30 @@ def bench_train_ops(args, d):
     t_p = timed(lambda: _native.gaussian_params(scales, rot, logits))
     t_l = timed(lambda: _native.combined_loss(pred, target, 0.9, 0.1, 5, "plain"))
     bp, bl = 72 * n, 12 * 64 * s * s
+    # densify/prune over the N Gaussians (flags, order-preserving offsets, the
+    # host's max_gaussians decision on the counts, the new set written)
+    from cuda_rasterizer import densify as DZ
+    dm = (torch.rand((n, 3), device=dev, generator=g) - 0.5) * 40
+    ds = torch.rand((n, 3), device=dev, generator=g) * 8.0 - 6.5
+    dq = torch.randn((n, 4), device=dev, generator=g)
+    do = torch.randn((n, 1), device=dev, generator=g) * 2.5
+    dsh = torch.randn((n, 16), device=dev, generator=g) * 0.1
+    dgr = torch.randn((n, 3), device=dev, generator=g) * 1e-4
+    dargs = (1e-4, 0.01, 2.0, 0.05, 10_000_000)
+    out, counts = DZ.densify_and_prune_tensors(dm, ds, dq, do, dsh, dgr, *dargs)
+    t_d = timed(lambda: DZ.densify_and_prune_tensors(dm, ds, dq, do, dsh, dgr, *dargs), reps=10)
+    n_out = int(out[0].shape[0])
+    bd = n * (12 + 12 + 16 + 4 + 64 + 12) + n_out * (12 + 12 + 16 + 4 + 64)
     return {"producer": {"gaussians_per_s": n / t_p, "achieved_gbs": round(bp / t_p / 1e9, 1),
                          "frac": round(bp / t_p / 1e9 / peak, 4), "peak_source": peak_kind,
                          "us": round(t_p * 1e6, 2)},
             "loss": {"images_per_s": 64 / t_l, "achieved_gbs": round(bl / t_l / 1e9, 1),
-                     "frac": round(bl / t_l / 1e9 / peak, 4), "us_per_64": round(t_l * 1e6, 2)}}
+                     "frac": round(bl / t_l / 1e9 / peak, 4), "us_per_64": round(t_l * 1e6, 2)},
+            "densify": {"gaussians_per_s": n / t_d, "us": round(t_d * 1e6, 2), "n_out": n_out,
+                        "counts": [int(c) for c in counts],
+                        "achieved_gbs": round(bd / t_d / 1e9, 1), "frac": round(bd / t_d / 1e9 / peak, 4),
+                        "bytes": "120 B read per Gaussian, 108 B written per output Gaussian; "
+                                 "includes the host reading the three counts"}}
 
 
 def cpu_baseline(args):
