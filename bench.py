@@ -395,7 +395,7 @@ def bench_e2e(args, d, sc, views):
         end.record(comp)
         return start, end
 
-    steps = max(3, min(args.steps, 10))
+    steps = max(3, min(args.steps, 30))  # the pipeline fills once per timed region
     a, b = run(2)
     b.synchronize()
     d.barrier()

@@ -65,6 +65,15 @@ def test_cell_culling_lists_images_omega(want_omega):
     _check_batch_vs_single(sc, views, want_omega)
 
 
+def test_many_view_launch_matches_single_views():
+    """20 views in one launch group: the four-tile scan, the two-pixel render
+    layout and the cell path give each view the lists, image and Omega of a
+    single-view call."""
+    sc = {k: v.cuda() for k, v in S.make_scene(150000, (40.0, 40.0, 10.0), (0.05, 0.5), seed=57).items()}
+    views = S.sweep_views(160)[::8]  # 20 views
+    _check_batch_vs_single(sc, views, want_omega=True)
+
+
 def test_cell_culling_edge_cases():
     """Non-finite centres, near-singular and very elongated covariances (no
     cell), transmittances below 0.01, and a flat scene (zero z extent)."""
