@@ -110,13 +110,22 @@ struct ApplyArgs {
   const int64_t* counts;
   int do_clones, do_splits;
   float *o_means, *o_scales, *o_rot, *o_logits, *o_sh;
+  bool vec;  // rotation rows and 16-column SH rows 16-byte aligned: copied as float4
 };
 
 __device__ __forceinline__ void copy_row(const ApplyArgs& a, int64_t src, int64_t dst) {
   for (int k = 0; k < 3; ++k) a.o_means[3 * dst + k] = a.means[3 * src + k];
   for (int k = 0; k < 3; ++k) a.o_scales[3 * dst + k] = a.scales[3 * src + k];
-  for (int k = 0; k < 4; ++k) a.o_rot[4 * dst + k] = a.rot[4 * src + k];
   a.o_logits[dst] = a.logits[src];
+  if (a.vec) {
+    reinterpret_cast<float4*>(a.o_rot)[dst] = reinterpret_cast<const float4*>(a.rot)[src];
+    const float4* hs = reinterpret_cast<const float4*>(a.sh) + 4 * src;
+    float4* hd = reinterpret_cast<float4*>(a.o_sh) + 4 * dst;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) hd[q] = hs[q];
+    return;
+  }
+  for (int k = 0; k < 4; ++k) a.o_rot[4 * dst + k] = a.rot[4 * src + k];
   for (int k = 0; k < a.sh_cols; ++k) a.o_sh[(size_t)dst * a.sh_cols + k] = a.sh[(size_t)src * a.sh_cols + k];
 }
 
@@ -233,6 +242,8 @@ extern "C" int sarr_densify_apply(int64_t n, const float* means, const float* sc
   a.o_rot = out_rotations;
   a.o_logits = out_opacity_logits;
   a.o_sh = out_sh;
+  auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  a.vec = sh_cols == 16 && a16(rotations) && a16(out_rotations) && a16(sh) && a16(out_sh);
   densify_apply_kernel<<<blocks, kDensifyThreads, 0, s>>>(a);
   return cuda_status(cudaGetLastError());
 }
