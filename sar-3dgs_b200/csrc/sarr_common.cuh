@@ -27,7 +27,8 @@ constexpr int kBinThreads = 256;                 // threads of a binning CTA
 constexpr int kBinPerThread = 4;                 // Gaussians per binning thread
 constexpr int kChunk = kBinThreads * kBinPerThread;  // Gaussians per count row
 constexpr int kSelectThreads = 128;
-constexpr int kScanThreads = 512;
+constexpr int kScanThreads = 512;                // scan4_kernel (4 tiles per lane)
+constexpr int kScan1Threads = 1024;              // scan_kernel (1 tile per lane, few views: more warps per tile column)
 constexpr int kPrefixChunks = 48;                // chunks binned exactly before saturation skipping
 constexpr int kXCap = kChunk;                    // exactly binned Gaussians listed per skipped chunk
 constexpr int kSegMaskMaxTiles = 2048;           // prefix-chunk segment masks up to this many tiles

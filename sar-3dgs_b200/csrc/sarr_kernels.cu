@@ -1133,7 +1133,15 @@ __global__ void __launch_bounds__(256) open_table_kernel(const OpenArgs a) {
   for (int y = tid; y < tiles_y; y += 256) tab[(y + 1) * pitch] = 0;
   for (int t = tid; t < T; t += 256) {
     int sum = 0;
-    for (int c = 0; c < a.prefix_chunks && sum < kCap; ++c) sum += counts[(size_t)c * T + t];
+    // sixteen chunks' counts in flight per step (only sum < kCap matters, and
+    // the sum only grows)
+    for (int c0 = 0; c0 < a.prefix_chunks && sum < kCap; c0 += 16) {
+      int cv[16];
+#pragma unroll
+      for (int u = 0; u < 16; ++u) cv[u] = c0 + u < a.prefix_chunks ? counts[(size_t)(c0 + u) * T + t] : 0;
+#pragma unroll
+      for (int u = 0; u < 16; ++u) sum += cv[u];
+    }
     const int y = t / tiles_x, x = t - y * tiles_x;
     tab[(y + 1) * pitch + x + 1] = sum < kCap ? 1 : 0;
   }
@@ -1173,8 +1181,8 @@ __global__ void __launch_bounds__(256) open_table_kernel(const OpenArgs a) {
 // tiles (lane = tile), each warp summing a contiguous range of chunk rows.
 // Emits, per tile, the chunks that hold its first 64 hits in index order as
 // (chunk, hits before the chunk, hits in the chunk) and the list length.
-__global__ void __launch_bounds__(kScanThreads) scan_kernel(const ScanArgs a) {
-  __shared__ int s_part[kScanThreads / 32][32];
+__global__ void __launch_bounds__(kScan1Threads) scan_kernel(const ScanArgs a) {
+  __shared__ int s_part[kScan1Threads / 32][32];
   __shared__ int s_nneed[32];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int v = blockIdx.y;
@@ -1183,7 +1191,7 @@ __global__ void __launch_bounds__(kScanThreads) scan_kernel(const ScanArgs a) {
   const bool live = t < T;
   const uint8_t* counts = a.counts + v * a.counts_vstride;
   const int C = a.C;
-  const int per = (C + kScanThreads / 32 - 1) / (kScanThreads / 32);
+  const int per = (C + kScan1Threads / 32 - 1) / (kScan1Threads / 32);
   const int c0 = min(warp * per, C), c1 = min(c0 + per, C);
   int sum = 0;
   if (live)
@@ -1194,7 +1202,7 @@ __global__ void __launch_bounds__(kScanThreads) scan_kernel(const ScanArgs a) {
   __syncthreads();
   int pre = 0, total = 0;
 #pragma unroll
-  for (int w = 0; w < kScanThreads / 32; ++w) {
+  for (int w = 0; w < kScan1Threads / 32; ++w) {
     const int x = s_part[w][lane];
     pre += (w < warp) ? x : 0;
     total += x;
@@ -2390,7 +2398,7 @@ cudaError_t launch_scan(const ScanArgs& a, int nviews, cudaStream_t s) {
   if (aligned4)
     scan4_kernel<<<dim3((a.T + kScanTilesPerCta - 1) / kScanTilesPerCta, nviews), kScanThreads, 0, s>>>(a);
   else
-    scan_kernel<<<dim3((a.T + 31) / 32, nviews), kScanThreads, 0, s>>>(a);
+    scan_kernel<<<dim3((a.T + 31) / 32, nviews), kScan1Threads, 0, s>>>(a);
   return cudaGetLastError();
 }
 
