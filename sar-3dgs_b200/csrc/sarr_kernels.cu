@@ -1312,6 +1312,78 @@ __global__ void __launch_bounds__(kScanThreads) scan4_kernel(const ScanArgs a) {
 // ---------------------------------------------------------------------------
 // capped tile selection + tile records
 // ---------------------------------------------------------------------------
+// The 48-byte record of list slot `slot` of tile t: the listed Gaussian
+// projected again in full (SH scattering only for the image list), its
+// density constants, transmittance, Z_r, Y_r and slot; the image list also
+// stores (Y_r, Z_r) for the backward. Returns Z_r. A list id outside [0, n)
+// (only a corrupted workspace can produce one) is reported and replaced by 0.
+template <bool kShadowList>
+__device__ __forceinline__ float select_record(const SelectArgs& a, const ViewConst& vc,
+                                               unsigned char* st, int t, int slot, int* list,
+                                               Rec& g) {
+  int id = list[slot];
+  if (id < 0 || (int64_t)id >= a.n) {
+    atomicOr(a.err, kDevErrListSlot);
+    id = 0;
+    list[slot] = 0;
+  }
+  float cw[6];
+  load_cov6(a.cov + (size_t)id * a.cov_layout, a.cov_layout, cw);
+  const float* m = a.means + (size_t)id * 3;
+  Proj o;
+  project_gaussian(vc, m[0], m[1], m[2], cw, o);
+  if (!kShadowList) {
+    g.mx = o.c;
+    g.my = o.r;
+    g.cxx = o.cov_cc;
+    g.cxy = o.cov_rc;
+    g.cyy = o.cov_rr;
+    g.s_pos = fmaxf(0.0f, sh_scattering(vc, a.sh + (size_t)id * a.sh_stride, a.sh_k));
+  } else {
+    g.mx = o.xr;
+    g.my = o.yr;
+    g.cxx = o.XX;
+    g.cxy = o.XY;
+    g.cyy = o.YY;
+    g.s_pos = 0.0f;
+  }
+  rec_density_consts(g);
+  g.sigma = a.sigma[id];
+  g.z = o.zr;
+  g.yr = o.yr;
+  g.pos = slot;
+  if (!kShadowList) {
+    float2* yz = reinterpret_cast<float2*>(st + a.st.L.yz);
+    yz[(size_t)t * kCap + slot] = make_float2(o.yr, o.zr);
+  }
+  return o.zr;
+}
+
+// Ranks of `count` slots by (Z_r, slot) into rank_out[slot] when some Z_r is
+// NaN: the reference's stable insertion sort on Z_r with strict '>'
+// (:795-807) replayed by one thread.
+__device__ __forceinline__ void insertion_ranks(const float* z, int count, int* rank_out) {
+  int idx[kCap];
+  float zv[kCap];
+  for (int i = 0; i < count; ++i) {
+    idx[i] = i;
+    zv[i] = z[i];
+  }
+  for (int i = 1; i < count; ++i) {
+    const int ti = idx[i];
+    const float tz = zv[i];
+    int j = i - 1;
+    while (j >= 0 && zv[j] > tz) {
+      idx[j + 1] = idx[j];
+      zv[j + 1] = zv[j];
+      j--;
+    }
+    idx[j + 1] = ti;
+    zv[j + 1] = tz;
+  }
+  for (int k = 0; k < count; ++k) rank_out[idx[k]] = k;
+}
+
 // One warp per tile (kSelectThreads / 32 tiles per CTA), no CTA barrier.
 //  1. emit: every needed chunk's 1024 rectangles are loaded at once (eight
 //     16-byte loads per lane) and its hits are ranked in index order with a
@@ -1533,47 +1605,9 @@ __global__ void __launch_bounds__(kSelectThreads, 8) select_kernel(const SelectA
   for (int h = 0; h < 2; ++h) {
     const int slot = lane + 32 * h;
     if (slot < count) {
-      int id = list[slot];
-      if (id < 0 || (int64_t)id >= a.n) {
-        // Every slot below `count` is filled (counts and rectangles come from
-        // the same bin pass); this guard only keeps a corrupted workspace from
-        // turning into an out-of-range gather.
-        atomicOr(a.err, kDevErrListSlot);
-        id = 0;
-        list[slot] = 0;
-      }
-      float cw[6];
-      load_cov6(a.cov + (size_t)id * a.cov_layout, a.cov_layout, cw);
-      const float* m = a.means + (size_t)id * 3;
-      Proj o;
-      project_gaussian(vc, m[0], m[1], m[2], cw, o);
-      Rec& g = rec[h];
-      if (!kShadowList) {
-        g.mx = o.c;
-        g.my = o.r;
-        g.cxx = o.cov_cc;
-        g.cxy = o.cov_rc;
-        g.cyy = o.cov_rr;
-        g.s_pos = fmaxf(0.0f, sh_scattering(vc, a.sh + (size_t)id * a.sh_stride, a.sh_k));
-      } else {
-        g.mx = o.xr;
-        g.my = o.yr;
-        g.cxx = o.XX;
-        g.cxy = o.XY;
-        g.cyy = o.YY;
-        g.s_pos = 0.0f;
-      }
-      rec_density_consts(g);
-      g.sigma = a.sigma[id];
-      g.z = o.zr;
-      g.yr = o.yr;
-      g.pos = slot;
-      s_z[warp][slot] = o.zr;
-      nan_z = nan_z || (o.zr != o.zr);
-      if (!kShadowList) {
-        float2* yz = reinterpret_cast<float2*>(st + a.st.L.yz);
-        yz[(size_t)t * kCap + slot] = make_float2(o.yr, o.zr);
-      }
+      const float zr = select_record<kShadowList>(a, vc, st, t, slot, list, rec[h]);
+      s_z[warp][slot] = zr;
+      nan_z = nan_z || (zr != zr);
     }
   }
   __syncwarp();
@@ -1584,27 +1618,7 @@ __global__ void __launch_bounds__(kSelectThreads, 8) select_kernel(const SelectA
   int rank[2] = {0, 0};
   const float* z = s_z[warp];
   if (__any_sync(0xffffffffu, nan_z)) {
-    if (lane == 0) {
-      int idx[kCap];
-      float zv[kCap];
-      for (int i = 0; i < count; ++i) {
-        idx[i] = i;
-        zv[i] = z[i];
-      }
-      for (int i = 1; i < count; ++i) {
-        const int ti = idx[i];
-        const float tz = zv[i];
-        int j = i - 1;
-        while (j >= 0 && zv[j] > tz) {
-          idx[j + 1] = idx[j];
-          zv[j + 1] = zv[j];
-          j--;
-        }
-        idx[j + 1] = ti;
-        zv[j + 1] = tz;
-      }
-      for (int k = 0; k < count; ++k) s_rank[warp][idx[k]] = k;
-    }
+    if (lane == 0) insertion_ranks(z, count, s_rank[warp]);
     __syncwarp();
     rank[0] = s_rank[warp][lane];
     rank[1] = s_rank[warp][lane + 32];
@@ -1628,6 +1642,110 @@ __global__ void __launch_bounds__(kSelectThreads, 8) select_kernel(const SelectA
       st_list[slot] = list[slot];
       st_recs[rank[h]] = rec[h];
     }
+  }
+}
+
+// Few-view variant of select_kernel, for launches of fewer than
+// kSelectCtaMaxViews views whose chunks all have segment masks and keep every
+// rectangle at its Gaussian's slot (the per-view path): such a launch has
+// only T tiles of work, so one 128-thread CTA takes each tile. Its four warps
+// take the need entries in turn (each entry fills its own list slots), one
+// thread per slot builds the records and two per slot count the ranks. The
+// lists and records are select_kernel's.
+constexpr int kSelectCtaMaxViews = 16;
+
+template <bool kShadowList>
+__global__ void __launch_bounds__(kSelectThreads) select_cta_kernel(const SelectArgs a) {
+  constexpr int kWarps = kSelectThreads / 32;
+  static_assert(kSelectThreads == 2 * kCap, "two threads per list slot for the ranks");
+  __shared__ int s_list[kCap];
+  __shared__ float s_z[kCap];
+  __shared__ int s_rank[2][kCap];
+  __shared__ int s_nan;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int v = blockIdx.y, t = blockIdx.x;
+  const ViewConst& vc = a.views[v];
+  const int tiles_x = vc.tiles_x, T = tiles_x * vc.tiles_y;
+  const int tx = t % tiles_x, ty = t / tiles_x;
+  unsigned char* st = a.st.base + v * a.st.vstride;
+  const int count = reinterpret_cast<const int*>(st + a.st.L.count)[t];
+  if (count == 0) return;  // the same for the whole CTA
+  const int nneed = a.need_n[v * a.need_n_vstride + t];
+  const int4* need = reinterpret_cast<const int4*>(a.need + v * a.need_vstride) + (size_t)t * kCap;
+  if (tid < kCap) s_list[tid] = -1;
+  if (tid == 0) s_nan = 0;
+  __syncthreads();
+
+  // 1. emit: warp w takes need entries w, w + 4, ...; the hit segments of an
+  // entry's chunk four at a time
+  const uint32_t* rects = reinterpret_cast<const uint32_t*>(st + a.st.L.rects);
+  const uint32_t* masks = a.segmask + v * a.segmask_vstride;
+  const unsigned lt_mask = (1u << lane) - 1u;
+  for (int q = warp; q < nneed; q += kWarps) {
+    const int4 nd = need[q];
+    uint32_t segs = masks[(size_t)nd.x * T + t];
+    const int want = min(nd.z, kCap - nd.y);
+    const int64_t b0 = (int64_t)nd.x * kChunk;
+    int found = 0;
+    while (segs && found < want) {
+      int64_t sj[4];
+      uint32_t rc[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        sj[u] = -1;
+        if (segs) {
+          sj[u] = b0 + (__ffs(segs) - 1) * 32 + lane;
+          segs &= segs - 1;
+        }
+        rc[u] = (sj[u] >= 0 && sj[u] < a.n) ? rects[sj[u]] : kEmptyRect;
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if (found >= want) break;
+        const bool hit = rect_has(rc[u], tx, ty);
+        const unsigned m = __ballot_sync(0xffffffffu, hit);
+        const int rk = found + __popc(m & lt_mask);
+        if (hit && rk < want) s_list[nd.y + rk] = (int)sj[u];
+        found += __popc(m);
+      }
+    }
+  }
+  __syncthreads();
+
+  // 2. records: thread s builds slot s
+  Rec g;
+  if (tid < count) {
+    const float zr = select_record<kShadowList>(a, vc, st, t, tid, s_list, g);
+    s_z[tid] = zr;
+    if (zr != zr) s_nan = 1;
+  }
+  __syncthreads();
+
+  // 3. rank by (Z_r, slot) (see select_kernel): threads s and s + 64 count
+  // the smaller keys among slots [0, 32) and [32, 64)
+  const bool nan_z = s_nan != 0;
+  if (nan_z) {
+    if (tid == 0) insertion_ranks(s_z, count, s_rank[0]);
+  } else {
+    const int slot = tid & (kCap - 1), half = tid >> 6;
+    if (slot < count) {
+      const float zs = s_z[slot];
+      int r = 0;
+      const int j1 = min(count, 32 * half + 32);
+      for (int j = 32 * half; j < j1; ++j) {
+        const float zj = s_z[j];
+        r += (zj < zs) || (zj == zs && j < slot);
+      }
+      s_rank[half][slot] = r;
+    }
+  }
+  __syncthreads();
+
+  // 4. state (the list length was written by scan_kernel)
+  if (tid < count) {
+    const int rank = nan_z ? s_rank[0][tid] : s_rank[0][tid] + s_rank[1][tid];
+    reinterpret_cast<int*>(st + a.st.L.list)[(size_t)t * kCap + tid] = s_list[tid];
+    (reinterpret_cast<Rec*>(st + a.st.L.recs) + (size_t)t * kCap)[rank] = g;
   }
 }
 
@@ -2406,6 +2524,13 @@ cudaError_t launch_select(const SelectArgs& a, const Dims& d, int nviews, bool s
                           cudaStream_t s) {
   const dim3 grid((d.T + kSelectThreads / 32 - 1) / (kSelectThreads / 32), nviews);
   const bool all = a.segmask && a.segmask_to >= a.C;
+  if (all && nviews < kSelectCtaMaxViews) {
+    // (every chunk with segment masks: the per-view path, rectangles at their
+    // Gaussians' slots)
+    if (shadow_list) select_cta_kernel<true><<<dim3(d.T, nviews), kSelectThreads, 0, s>>>(a);
+    else select_cta_kernel<false><<<dim3(d.T, nviews), kSelectThreads, 0, s>>>(a);
+    return cudaGetLastError();
+  }
   if (shadow_list) {
     if (all) select_kernel<true, true><<<grid, kSelectThreads, 0, s>>>(a);
     else select_kernel<true, false><<<grid, kSelectThreads, 0, s>>>(a);
