@@ -160,8 +160,9 @@ __device__ __forceinline__ bool stage_chunk(const BinArgs& a, int64_t base, int 
 // that for every Gaussian from a fast approximate centre and a view-independent
 // bbox bound (both with margins); only the rest are queued, compacted, and
 // binned exactly in stage 2, which keeps the warps of both stages coherent.
-template <bool kShadow, bool kSkip>
-__global__ void __launch_bounds__(kBinThreads) bin_kernel(const BinArgs a) {
+template <bool kShadow, bool kSkip, int kThreads>
+__global__ void __launch_bounds__(kThreads) bin_kernel(const BinArgs a) {
+  constexpr int kPer = kChunk / kThreads;  // Gaussians per thread
   extern __shared__ __align__(16) unsigned char smem_raw[];
   __shared__ uint64_t bar;
   __shared__ int s_qn;
@@ -189,10 +190,10 @@ __global__ void __launch_bounds__(kBinThreads) bin_kernel(const BinArgs a) {
   const int gcount = (int)min((int64_t)kChunk, a.n - base);
   if (!stage_chunk(a, base, gcount, s_means, s_cov, s_sigma, &bar)) return;
 
-  float hb[kBinPerThread];  // view-independent bbox half-width bounds (kSkip)
+  float hb[kPer];  // view-independent bbox half-width bounds (kSkip)
 #pragma unroll
-  for (int k = 0; k < kBinPerThread; ++k) {
-    const int j = tid + k * kBinThreads;
+  for (int k = 0; k < kPer; ++k) {
+    const int j = tid + k * kThreads;
     hb[k] = INFINITY;
     if (kSkip && j < gcount) {
       float cw[6];
@@ -206,9 +207,9 @@ __global__ void __launch_bounds__(kBinThreads) bin_kernel(const BinArgs a) {
   for (int v = v_begin; v < v_end; ++v) {
     const ViewConst& vc = a.views[v];
     const int Nr = vc.h.Nr, Na = vc.h.Na;
-    for (int i = tid; i < T1 * (kShadow ? 2 : 1); i += kBinThreads) s_diff_ipp[i] = 0;
+    for (int i = tid; i < T1 * (kShadow ? 2 : 1); i += kThreads) s_diff_ipp[i] = 0;
     if (masks)
-      for (int i = tid; i < T * (kShadow ? 2 : 1); i += kBinThreads) s_mask_ipp[i] = 0;
+      for (int i = tid; i < T * (kShadow ? 2 : 1); i += kThreads) s_mask_ipp[i] = 0;
     if (kSkip && tid == 0) s_qn = 0;
     __syncthreads();
 
@@ -226,8 +227,8 @@ __global__ void __launch_bounds__(kBinThreads) bin_kernel(const BinArgs a) {
       const int* open_ipp = a.open_ipp + v * a.open_vstride;
       const int* open_sh = a.open_sh + v * a.open_vstride;
 #pragma unroll
-      for (int k = 0; k < kBinPerThread; ++k) {
-        const int j = tid + k * kBinThreads;
+      for (int k = 0; k < kPer; ++k) {
+        const int j = tid + k * kThreads;
         bool exact = false;
         if (j < gcount) {
           bool skip = s_sigma[j] < 0.01f;  // invalid: empty rectangles either way
@@ -255,7 +256,7 @@ __global__ void __launch_bounds__(kBinThreads) bin_kernel(const BinArgs a) {
       __syncthreads();
       // stage 2: the queued Gaussians, exactly
       const int qn = s_qn;
-      for (int q = tid; q < qn; q += kBinThreads) {
+      for (int q = tid; q < qn; q += kThreads) {
         const int j = s_queue[q];
         uint32_t rc_ipp = kEmptyRect, rc_sh = kEmptyRect;
         bin_exact<kShadow>(vcl, s_means, s_cov, cs, j, rc_ipp, rc_sh);
@@ -269,8 +270,8 @@ __global__ void __launch_bounds__(kBinThreads) bin_kernel(const BinArgs a) {
     } else {
       const ViewConst vcl = vc;  // local copy: loaded once for all of this thread's Gaussians
 #pragma unroll
-      for (int k = 0; k < kBinPerThread; ++k) {
-        const int j = tid + k * kBinThreads;
+      for (int k = 0; k < kPer; ++k) {
+        const int j = tid + k * kThreads;
         if (j < gcount) {
           uint32_t rc_ipp = kEmptyRect, rc_sh = kEmptyRect;
           if (!(s_sigma[j] < 0.01f))  // preprocess_kernel: transmittance < 0.01 -> invalid (:351)
@@ -292,7 +293,7 @@ __global__ void __launch_bounds__(kBinThreads) bin_kernel(const BinArgs a) {
     // Threads [0,128) handle the image-plane list, [128,256) the shadow list.
     {
       const int half = tid >> 7, i = tid & 127;
-      if (half == 0 || kShadow) {
+      if (half == 0 || (kShadow && half == 1)) {
         int* d = half ? s_diff_sh : s_diff_ipp;
         if (i < tiles_y) {
           int run = 0;
@@ -306,7 +307,7 @@ __global__ void __launch_bounds__(kBinThreads) bin_kernel(const BinArgs a) {
     __syncthreads();
     {
       const int half = tid >> 7, i = tid & 127;
-      if (half == 0 || kShadow) {
+      if (half == 0 || (kShadow && half == 1)) {
         int* d = half ? s_diff_sh : s_diff_ipp;
         if (i < tiles_x) {
           int run = 0;
@@ -321,17 +322,17 @@ __global__ void __launch_bounds__(kBinThreads) bin_kernel(const BinArgs a) {
 
     uint8_t* cnt_ipp = a.counts_ipp + v * a.counts_vstride + (size_t)chunk * T;
     uint8_t* cnt_sh = kShadow ? a.counts_sh + v * a.counts_vstride + (size_t)chunk * T : nullptr;
-    for (int t = tid; t < T; t += kBinThreads) {
+    for (int t = tid; t < T; t += kThreads) {
       const int y = t / tiles_x, x = t - y * tiles_x;
       cnt_ipp[t] = (uint8_t)min(s_diff_ipp[y * pitch + x], 255);
       if (kShadow) cnt_sh[t] = (uint8_t)min(s_diff_sh[y * pitch + x], 255);
     }
     if (masks) {
       uint32_t* m = a.segmask + v * a.segmask_vstride + (size_t)chunk * T;
-      for (int t = tid; t < T; t += kBinThreads) m[t] = s_mask_ipp[t];
+      for (int t = tid; t < T; t += kThreads) m[t] = s_mask_ipp[t];
       if (kShadow) {
         uint32_t* msh = a.segmask_sh + v * a.segmask_vstride + (size_t)chunk * T;
-        for (int t = tid; t < T; t += kBinThreads) msh[t] = s_mask_sh[t];
+        for (int t = tid; t < T; t += kThreads) msh[t] = s_mask_sh[t];
       }
     }
     __syncthreads();  // the difference arrays and the queue are reused by the next view
@@ -2397,10 +2398,19 @@ cudaError_t launch_view_setup(const ViewHostPack& pack, ViewConst* out, int* err
 
 template <bool kShadow, bool kSkip>
 static void launch_bin_t(const BinArgs& a, dim3 grid, size_t smem, cudaStream_t s) {
+  // a launch of few CTAs (exact binning of one view's prefix chunks) uses 512
+  // threads, two Gaussians each, for a shorter chain per thread
+  if (!kSkip && grid.x * grid.y < 148) {
+    if (needs_smem_attr(smem))
+      cudaFuncSetAttribute(bin_kernel<kShadow, kSkip, 512>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)smem);
+    bin_kernel<kShadow, kSkip, 512><<<grid, 512, smem, s>>>(a);
+    return;
+  }
   if (needs_smem_attr(smem))
-    cudaFuncSetAttribute(bin_kernel<kShadow, kSkip>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaFuncSetAttribute(bin_kernel<kShadow, kSkip, kBinThreads>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)smem);
-  bin_kernel<kShadow, kSkip><<<grid, kBinThreads, smem, s>>>(a);
+  bin_kernel<kShadow, kSkip, kBinThreads><<<grid, kBinThreads, smem, s>>>(a);
 }
 
 // bin_prefix_kernel: staged means + transmittances, per-warp counters and
