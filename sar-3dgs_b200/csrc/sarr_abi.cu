@@ -307,7 +307,23 @@ cudaError_t run_selection(const Dims& d, const Ws& w, int gv, const float* means
   // The first kPrefixChunks chunks are binned exactly; tiles that they fill
   // with 64 hits are marked saturated, and the remaining chunks skip the
   // covariance projection of Gaussians that can only reach saturated tiles.
-  const int prefix = d.C > kPrefixChunks ? kPrefixChunks : d.C;
+  int prefix = d.C > kPrefixChunks ? kPrefixChunks : d.C;
+  // One view on the per-view path (the training step): the skipping binner
+  // runs one CTA per chunk after the prefix, so its last wave can be nearly
+  // empty. The prefix is then widened, up to one CTA per SM of exact binning
+  // (which costs about the same as 48), until the remaining chunks fill whole
+  // waves. The lists do not depend on the prefix length.
+  if (gv == 1 && !w.L.cells && masks_all && d.C > kPrefixChunks) {
+    const int wave = skip_bin_wave(d, cov_layout, shr != nullptr, true);
+    int sms = 0, dev = 0;
+    if (wave > 0 && cudaGetDevice(&dev) == cudaSuccess &&
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess) {
+      const int rest = d.C - kPrefixChunks;
+      const int waves = (rest + wave - 1) / wave;
+      const int p = d.C - (waves - 1) * wave;  // leaves exactly waves - 1 full waves
+      if (waves > 1 && p <= sms) prefix = p;
+    }
+  }
   ba.chunk_offset = 0;
   ba.views_per_cta = views_per_cta(prefix);
   // one view per warp in the prefix binner once a CTA holds 8 views or more

@@ -396,6 +396,7 @@ bool bin_cell_supported(const Dims& d);
 // true when the skipping binner keeps per-warp counters (and records the
 // exact lists); false selects its CTA-wide variant
 bool skip_bin_per_warp(const Dims& d, bool shadow);
+int skip_bin_wave(const Dims& d, int cov_layout, bool shadow, bool masks);
 bool segmask_supported(const Dims& d);
 bool segmask_all_chunks(const Dims& d);
 cudaError_t launch_scan(const ScanArgs& a, int nviews, cudaStream_t s);

@@ -2371,6 +2371,19 @@ static size_t bin_skip_smem_bytes(const Dims& d, int cov_layout, bool shadow, bo
          warp_mask_bytes(d, shadow, masks);
 }
 
+// CTAs of bin_skip_kernel that the whole GPU holds at once (0 if unknown).
+int skip_bin_wave(const Dims& d, int cov_layout, bool shadow, bool masks) {
+  int dev = 0, sms = 0, per_sm = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+  const size_t smem = bin_skip_smem_bytes(d, cov_layout, shadow, masks);
+  const cudaError_t e =
+      shadow ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, bin_skip_kernel<true>, kBinThreads, smem)
+             : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, bin_skip_kernel<false>, kBinThreads, smem);
+  if (e != cudaSuccess) return 0;
+  return sms * per_sm;
+}
+
 bool skip_bin_per_warp(const Dims& d, bool shadow) {
   return warp_count_bytes(d, shadow) <= kWarpCountBytes;
 }
