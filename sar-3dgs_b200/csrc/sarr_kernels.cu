@@ -1662,6 +1662,8 @@ __global__ void __launch_bounds__(kSelectThreads) select_cta_kernel(const Select
   __shared__ int s_list[kCap];
   __shared__ float s_z[kCap];
   __shared__ int s_rank[2][kCap];
+  __shared__ int4 s_need[kCap];
+  __shared__ uint32_t s_segs[kCap];
   __shared__ int s_nan;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int v = blockIdx.y, t = blockIdx.x;
@@ -1673,18 +1675,26 @@ __global__ void __launch_bounds__(kSelectThreads) select_cta_kernel(const Select
   if (count == 0) return;  // the same for the whole CTA
   const int nneed = a.need_n[v * a.need_n_vstride + t];
   const int4* need = reinterpret_cast<const int4*>(a.need + v * a.need_vstride) + (size_t)t * kCap;
-  if (tid < kCap) s_list[tid] = -1;
+  // the need entries and their chunks' segment masks, one thread each
+  const uint32_t* masks = a.segmask + v * a.segmask_vstride;
+  if (tid < kCap) {
+    s_list[tid] = -1;
+    if (tid < nneed) {
+      const int4 nd = need[tid];
+      s_need[tid] = nd;
+      s_segs[tid] = masks[(size_t)nd.x * T + t];
+    }
+  }
   if (tid == 0) s_nan = 0;
   __syncthreads();
 
   // 1. emit: warp w takes need entries w, w + 4, ...; the hit segments of an
   // entry's chunk four at a time
   const uint32_t* rects = reinterpret_cast<const uint32_t*>(st + a.st.L.rects);
-  const uint32_t* masks = a.segmask + v * a.segmask_vstride;
   const unsigned lt_mask = (1u << lane) - 1u;
   for (int q = warp; q < nneed; q += kWarps) {
-    const int4 nd = need[q];
-    uint32_t segs = masks[(size_t)nd.x * T + t];
+    const int4 nd = s_need[q];
+    uint32_t segs = s_segs[q];
     const int want = min(nd.z, kCap - nd.y);
     const int64_t b0 = (int64_t)nd.x * kChunk;
     int found = 0;
