@@ -531,4 +531,25 @@ __device__ __forceinline__ float warp_sum(float x) {
   return x;
 }
 
+// Warp sums of eight values at once (reduce-scatter butterfly, 9 shuffles
+// instead of 40): every lane returns the total of value
+// k = 4 * bit4 + 2 * bit3 + bit2 of its lane index. The order of the
+// additions is fixed, so the sums are reproducible.
+__device__ __forceinline__ float warp_sum8_scatter(const float v[8], int lane) {
+  const unsigned full = 0xffffffffu;
+  const bool h16 = (lane & 16) != 0, h8 = (lane & 8) != 0, h4 = (lane & 4) != 0;
+  float a[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    a[i] = (h16 ? v[4 + i] : v[i]) + __shfl_xor_sync(full, h16 ? v[i] : v[4 + i], 16);
+  float b[2];
+#pragma unroll
+  for (int i = 0; i < 2; ++i)
+    b[i] = (h8 ? a[2 + i] : a[i]) + __shfl_xor_sync(full, h8 ? a[i] : a[2 + i], 8);
+  float c = (h4 ? b[1] : b[0]) + __shfl_xor_sync(full, h4 ? b[0] : b[1], 4);
+  c += __shfl_xor_sync(full, c, 2);
+  c += __shfl_xor_sync(full, c, 1);
+  return c;
+}
+
 }  // namespace sarr

@@ -2175,12 +2175,10 @@ __global__ void __launch_bounds__(kWarpsPerTile * 32) bwd_tile_kernel(const Tile
       }
     }
     if (__any_sync(0xffffffffu, contrib)) {
-#pragma unroll
-      for (int c = 0; c < 7; ++c) A[c] = warp_sum(A[c]);
-      if (lane == 0) {
-#pragma unroll
-        for (int c = 0; c < 7; ++c) s_red[warp][k - k_lo][c] = A[c];
-      }
+      const float A8[8] = {A[0], A[1], A[2], A[3], A[4], A[5], A[6], 0.0f};
+      const float total = warp_sum8_scatter(A8, lane);
+      const int c = 4 * ((lane >> 4) & 1) + 2 * ((lane >> 3) & 1) + ((lane >> 2) & 1);
+      if ((lane & 3) == 0 && c < 7) s_red[warp][k - k_lo][c] = total;
     }
   }
   __syncthreads();
