@@ -2148,14 +2148,16 @@ __global__ void __launch_bounds__(kWarpsPerTile * 32) bwd_tile_kernel(const Tile
         const float cov_rr = g.cyy, cov_cc = g.cxx, cov_rc = g.cxy;
         const float det = fma_(cov_rr, cov_cc, -mul_(cov_rc, cov_rc));
         if (det > kEps) {
-          const float inv_det = div_(1.0f, det);
+          // det equals the record's (fma is symmetric in its factors), so its
+          // reciprocal and 2 pi sqrt(det) are the record's inv_det and norm
+          const float inv_det = g.inv_det;
           // the backward's own exponent pairs cov_cc with dx^2 and cov_rr with dy^2 (:950)
           const float q = fma_(mul_(cov_rr, dy), dy,
                                fma_(mul_(cov_cc, dx), dx, -mul_(mul_(mul_(2.0f, cov_rc), dx), dy)));
           const float exponent = mul_(mul_(-0.5f, q), inv_det);
           if (exponent > -20.0f) {
             const float exp_val = expf(exponent);
-            const float base_val = div_(exp_val, mul_(kTwoPi, sqrt_(det)));
+            const float base_val = div_(exp_val, g.norm);
             const float h = mul_(mul_(0.5f, base_val), inv_det);
             const float d_gamma_d_cov_rr = mul_(h, fma_(dy, dy, -mul_(mul_(cov_cc, inv_det), 0.5f)));
             const float d_gamma_d_cov_cc = mul_(h, fma_(dx, dx, -mul_(mul_(cov_rr, inv_det), 0.5f)));
