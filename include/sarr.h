@@ -166,6 +166,26 @@ int sarr_combined_loss(int n_images, int height, int width, const float *pred,
                        sarr_stream_t stream);
 
 /*
+ * One Adam step over `count` consecutive fp32 parameters: replaces the
+ * optimizer.step() of the reference's training step
+ * (training/training_pipeline.py:205; torch.optim.Adam built at
+ * train.py:429-435 with one learning rate per parameter group, betas and eps
+ * at their defaults, no weight decay). Per element, torch.optim.Adam's update:
+ *   m = lerp(m, g, 1 - beta1);  v = beta2 v + (1 - beta2) g^2;
+ *   p -= lr / (1 - beta1^step) * m / (sqrt(v) / sqrt(1 - beta2^step) + eps),
+ * with the bias corrections in double precision as torch evaluates them.
+ * Learning rates by segment: element i uses segment_lr[k] for the first k with
+ * i < segment_end[k] (host arrays of n_segments <= 8 entries, ends ascending,
+ * the last >= count). `step` is the 1-based step count after this update.
+ * The arrays are device memory and may be a bucket (sub-range) of flat
+ * parameter/gradient/moment buffers.
+ */
+int sarr_adam_step(int64_t count, float *param, const float *grad, float *exp_avg,
+                   float *exp_avg_sq, int n_segments, const int64_t *segment_end,
+                   const float *segment_lr, float beta1, float beta2, float eps, int64_t step,
+                   sarr_stream_t stream);
+
+/*
  * Densification and pruning (GaussianModel.densify_and_prune,
  * gaussian_model.py:433-566) in two calls, with a host decision between them
  * (the reference's max_gaussians tests, which need the counts):
@@ -209,19 +229,32 @@ int sarr_densify_apply(int64_t n, const float *means, const float *scales_log,
  * synchronises the device and can fail under memory pressure).
  *   Limits: n <= 131072 Gaussians, range_samples and azimuth_samples <= 256;
  *           larger requests return SARR_ERR_CAPACITY.
- *   Setup:  the first call on a device (that device current) looks up the
- *           scratch's device address once (cudaGetSymbolAddress); make that
- *           first call before any stream capture begins.
+ *   Setup:  the first call in a CUDA context (that context current: the
+ *           device's primary context for runtime-API callers) looks up the
+ *           scratch's device address once (cudaGetSymbolAddress) and caches it
+ *           under the context handle; make that first call before any stream
+ *           capture begins. Do not reset the device (cudaDeviceReset) between
+ *           calls: the cache does not notice a re-created context.
  *   Zero:   nothing has to start at zero; each call writes every scratch byte
  *           it reads.
  *   Races:  all calls on a device share the scratch; calls on one device
  *           must not overlap (one stream, or ordered by the caller).
+ *   Errors: device-side errors of these calls (a bounded wait that expired)
+ *           are read with sarr_check_static_errors().
  * Arguments as sarr_forward with n_views = 1, omega = states = NULL. Never
  * allocates device or pinned memory.
  */
 int sarr_forward_static(const sarr_view *view, int64_t n, const float *means, const float *cov,
                         int cov_layout, const float *sigma, const float *sh, int sh_stride,
                         int sh_k, float *image, sarr_stream_t stream);
+
+/*
+ * Reads and clears the device error word of sarr_forward_static's scratch in
+ * the current context (synchronises the stream), as sarr_check_device_errors
+ * does for a caller workspace. Returns SARR_OK or SARR_ERR_DEVICE. No
+ * counterpart in the reference.
+ */
+int sarr_check_static_errors(sarr_stream_t stream);
 
 /*
  * Backward of n_views views; the parameter gradients are the SUM over the

@@ -25,6 +25,16 @@ namespace {
 
 std::atomic<int64_t> g_launches{0};
 
+}  // namespace
+
+namespace sarr {
+// Launches of the training-step kernels (sarr_train.cu, sarr_densify.cu),
+// which are launched without the per-kind profiling hooks.
+void count_launches(int k) { g_launches += k; }
+}  // namespace sarr
+
+namespace {
+
 // compute_sh_basis_host (rasterizer_impl_v2.cu:284-320): the reference's own
 // 16-term basis (terms 9-15 are not the standard real SH); constants :15-24.
 void sh_basis_host(float theta, float phi, float* b) {

@@ -8,6 +8,10 @@
 
 #include "sarr.h"
 
+namespace sarr {
+void count_launches(int k);  // the library's launch counter (sarr_abi.cu)
+}
+
 namespace {
 
 constexpr int kDensifyThreads = 1024;
@@ -203,6 +207,7 @@ extern "C" int sarr_densify_flags(int64_t n, const float* scales_log, const floa
                                                           large_scale_threshold, opacity_threshold,
                                                           flags, bc);
   densify_offsets_kernel<<<1, kDensifyThreads, 0, s>>>(blocks, bc, counts_out);
+  sarr::count_launches(2);
   return cuda_status(cudaGetLastError());
 }
 
@@ -245,5 +250,6 @@ extern "C" int sarr_densify_apply(int64_t n, const float* means, const float* sc
   auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
   a.vec = sh_cols == 16 && a16(rotations) && a16(out_rotations) && a16(sh) && a16(out_sh);
   densify_apply_kernel<<<blocks, kDensifyThreads, 0, s>>>(a);
+  sarr::count_launches(1);
   return cuda_status(cudaGetLastError());
 }

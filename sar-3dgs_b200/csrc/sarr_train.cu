@@ -12,12 +12,22 @@
 //                            of the SSIM map with respect to the moments;
 //   loss_grad_kernel         the image gradient: L1 term plus the window
 //                            correlation of those partial derivatives;
-//   loss_reduce_kernel       deterministic reduction of the per-block sums.
+//   loss_reduce_kernel       deterministic reduction of the per-block sums;
+//   adam_kernel              the Adam update of torch.optim.Adam (the
+//                            reference's optimiser, train.py:429-435) over a
+//                            flat range of parameters with per-segment
+//                            learning rates, so that a bucket of a flat
+//                            gradient buffer is updated as soon as its
+//                            all-reduce has landed.
 #include <math.h>
 #include <stdint.h>
 #include <string.h>
 
 #include "sarr.h"
+
+namespace sarr {
+void count_launches(int k);  // the library's launch counter (sarr_abi.cu)
+}
 
 namespace {
 
@@ -440,6 +450,78 @@ void launch_loss(dim3 grid, cudaStream_t s, const LossParams& P, const float* pr
   if (grad_pred) loss_grad_kernel<kWin><<<grid, kLossThreads, 0, s>>>(P, pred, target, tmax, dgrad, grad_pred);
 }
 
+// ---------------------------------------------------------------------------
+// Adam
+// ---------------------------------------------------------------------------
+constexpr int kAdamMaxSegments = 8;
+constexpr int kAdamThreads = 256;
+
+struct AdamParams {
+  int64_t count;
+  int nseg;
+  int64_t seg_end[kAdamMaxSegments];
+  float seg_step[kAdamMaxSegments];  // lr / (1 - beta1^step)
+  float beta1, beta2, one_m_beta1, one_m_beta2;
+  float bc2_sqrt;                    // sqrt(1 - beta2^step)
+  float eps;
+};
+
+// One element of torch.optim.Adam's single-tensor update (weight_decay 0, no
+// amsgrad): exp_avg.lerp_(grad, 1 - beta1); exp_avg_sq.mul_(beta2)
+// .addcmul_(grad, grad, 1 - beta2); denom = sqrt(exp_avg_sq) / bc2_sqrt + eps;
+// param.addcdiv_(exp_avg, denom, -step_size).
+__device__ __forceinline__ float adam_elem(float p, float g, float& m, float& v, float step_size,
+                                           const AdamParams& A) {
+  m = __fmaf_rn(A.one_m_beta1, __fsub_rn(g, m), m);
+  v = __fadd_rn(__fmul_rn(v, A.beta2), __fmul_rn(__fmul_rn(A.one_m_beta2, g), g));
+  const float denom = __fadd_rn(__fdiv_rn(__fsqrt_rn(v), A.bc2_sqrt), A.eps);
+  return __fadd_rn(p, __fmul_rn(-step_size, __fdiv_rn(m, denom)));
+}
+
+__device__ __forceinline__ float adam_step_size(const AdamParams& A, int64_t i) {
+  float s = A.seg_step[A.nseg - 1];
+  for (int k = A.nseg - 2; k >= 0; --k)
+    if (i < A.seg_end[k]) s = A.seg_step[k];
+  return s;
+}
+
+// Four elements per thread with 16-byte accesses when every array is 16-byte
+// aligned; the tail (and unaligned calls) one element per thread.
+__global__ void __launch_bounds__(kAdamThreads) adam_kernel(AdamParams A, float* __restrict__ param,
+                                                            const float* __restrict__ grad,
+                                                            float* __restrict__ m,
+                                                            float* __restrict__ v, bool vec) {
+  const int64_t t = (int64_t)blockIdx.x * kAdamThreads + threadIdx.x;
+  if (vec) {
+    const int64_t i = 4 * t;
+    if (i + 3 < A.count) {
+      float4 p4 = reinterpret_cast<const float4*>(param)[t];
+      const float4 g4 = reinterpret_cast<const float4*>(grad)[t];
+      float4 m4 = reinterpret_cast<const float4*>(m)[t];
+      float4 v4 = reinterpret_cast<const float4*>(v)[t];
+      p4.x = adam_elem(p4.x, g4.x, m4.x, v4.x, adam_step_size(A, i), A);
+      p4.y = adam_elem(p4.y, g4.y, m4.y, v4.y, adam_step_size(A, i + 1), A);
+      p4.z = adam_elem(p4.z, g4.z, m4.z, v4.z, adam_step_size(A, i + 2), A);
+      p4.w = adam_elem(p4.w, g4.w, m4.w, v4.w, adam_step_size(A, i + 3), A);
+      reinterpret_cast<float4*>(param)[t] = p4;
+      reinterpret_cast<float4*>(m)[t] = m4;
+      reinterpret_cast<float4*>(v)[t] = v4;
+    } else {
+      for (int64_t j = i; j < A.count; ++j) {
+        float mj = m[j], vj = v[j];
+        param[j] = adam_elem(param[j], grad[j], mj, vj, adam_step_size(A, j), A);
+        m[j] = mj;
+        v[j] = vj;
+      }
+    }
+  } else if (t < A.count) {
+    float mj = m[t], vj = v[t];
+    param[t] = adam_elem(param[t], grad[t], mj, vj, adam_step_size(A, t), A);
+    m[t] = mj;
+    v[t] = vj;
+  }
+}
+
 }  // namespace
 
 extern "C" int sarr_gaussian_params(int64_t n, const float* scales_log, const float* rotations,
@@ -455,6 +537,7 @@ extern "C" int sarr_gaussian_params(int64_t n, const float* scales_log, const fl
   const bool staged = !cov_out || (a16(scales_log) && a16(rotations) && a16(cov_out));
   gaussian_params_kernel<<<(unsigned)((n + kParamThreads - 1) / kParamThreads), kParamThreads, 0, s>>>(
       n, scales_log, rotations, cov_layout, cov_out, opacity_logits, opacity_out, staged);
+  sarr::count_launches(1);
   return cuda_status(cudaGetLastError());
 }
 
@@ -519,5 +602,44 @@ extern "C" int sarr_combined_loss(int n_images, int height, int width, const flo
     default: launch_loss<11>(grid, s, P, pred, target, tmax, dgrad, partial, grad_pred); break;
   }
   loss_reduce_kernel<<<1, kReduceThreads, 0, s>>>(P, partial, nblk, losses_out);
+  sarr::count_launches((l1_mode != SARR_L1_PLAIN ? 2 : 0) + (grad_pred ? 3 : 2));
+  return cuda_status(cudaGetLastError());
+}
+
+extern "C" int sarr_adam_step(int64_t count, float* param, const float* grad, float* exp_avg,
+                              float* exp_avg_sq, int n_segments, const int64_t* segment_end,
+                              const float* segment_lr, float beta1, float beta2, float eps,
+                              int64_t step, sarr_stream_t stream) {
+  if (count < 0 || step < 1 || n_segments < 1 || n_segments > kAdamMaxSegments) return SARR_ERR_ARG;
+  if (!segment_end || !segment_lr) return SARR_ERR_ARG;
+  if (!(beta1 >= 0.0f && beta1 < 1.0f && beta2 >= 0.0f && beta2 < 1.0f)) return SARR_ERR_ARG;
+  if (count == 0) return SARR_OK;
+  if (!param || !grad || !exp_avg || !exp_avg_sq) return SARR_ERR_ARG;
+  AdamParams A;
+  memset(&A, 0, sizeof(A));
+  A.count = count;
+  A.nseg = n_segments;
+  // torch.optim.Adam evaluates the bias corrections in double precision
+  const double bc1 = 1.0 - pow((double)beta1, (double)step);
+  const double bc2 = 1.0 - pow((double)beta2, (double)step);
+  for (int k = 0; k < n_segments; ++k) {
+    if (k > 0 && segment_end[k] < segment_end[k - 1]) return SARR_ERR_ARG;
+    A.seg_end[k] = segment_end[k];
+    A.seg_step[k] = (float)((double)segment_lr[k] / bc1);
+  }
+  if (segment_end[n_segments - 1] < count) return SARR_ERR_ARG;
+  A.beta1 = beta1;
+  A.beta2 = beta2;
+  A.one_m_beta1 = (float)(1.0 - (double)beta1);
+  A.one_m_beta2 = (float)(1.0 - (double)beta2);
+  A.bc2_sqrt = (float)sqrt(bc2);
+  A.eps = eps;
+  auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  const bool vec = a16(param) && a16(grad) && a16(exp_avg) && a16(exp_avg_sq);
+  const int64_t threads = vec ? (count + 3) / 4 : count;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  adam_kernel<<<(unsigned)((threads + kAdamThreads - 1) / kAdamThreads), kAdamThreads, 0, s>>>(
+      A, param, grad, exp_avg, exp_avg_sq, vec);
+  sarr::count_launches(1);
   return cuda_status(cudaGetLastError());
 }

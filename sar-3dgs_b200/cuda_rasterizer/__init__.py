@@ -24,7 +24,6 @@ from . import _native
 from . import cuda_rasterizer_sar
 from .cuda_rasterizer_sar import SARRasterizationSettings
 
-CUDA_AVAILABLE = _native.available()
 CUDASARRasterizer = None
 render_sar_func = cuda_rasterizer_sar.render_sar
 render_sar_backward = cuda_rasterizer_sar.render_sar_backward
@@ -66,7 +65,7 @@ def render_sar(gaussian_data: GaussianDataGPU, output_height: int = 512,
     """(cuda_rasterizer/__init__.py:147-186): renders with the bundle's own
     sample counts (output_height / output_width are unused, as in the
     reference) and returns ([image, omega], {})."""
-    if not CUDA_AVAILABLE:
+    if not _native.available():
         raise RuntimeError("CUDA SAR rasterizer unavailable (no CUDA device or libsarr.so missing)")
     d = gaussian_data
     out = render_sar_func(d.means, d.covs, d.transmittance, d.scattering, d.radar_position[0],
@@ -74,6 +73,15 @@ def render_sar(gaussian_data: GaussianDataGPU, output_height: int = 512,
                           d.incidence_angle, d.azimuth_angle, d.range_resolution,
                           d.azimuth_resolution, d.range_samples, d.azimuth_samples)
     return out, {}
+
+
+def __getattr__(name):
+    """CUDA_AVAILABLE (cuda_rasterizer/__init__.py:20-64 of the reference) is
+    evaluated on first access rather than at import, so that importing the
+    package (for its synthetic scenes, say) never loads libsarr.so."""
+    if name == "CUDA_AVAILABLE":
+        return _native.available()
+    raise AttributeError(f"module {__name__!r} has no attribute {name!r}")
 
 
 __all__ = ["CUDA_AVAILABLE", "CUDASARRasterizer", "render_sar", "GaussianDataCPU",

@@ -79,13 +79,15 @@ def _declare(L):
     L.sarr_loss_workspace_size.argtypes = [I, I, I, ctypes.POINTER(SZ)]
     F = ctypes.c_float
     L.sarr_combined_loss.argtypes = [I, I, I, P, P, F, F, I, I, P, P, P, SZ, P]
+    L.sarr_adam_step.argtypes = [I64, P, P, P, P, I, ctypes.POINTER(I64), ctypes.POINTER(F), F, F,
+                                 F, I64, P]
     L.sarr_densify_workspace_size.argtypes = [I64, ctypes.POINTER(SZ)]
     L.sarr_densify_flags.argtypes = [I64, P, P, P, F, F, F, F, P, P, SZ, P]
     L.sarr_densify_apply.argtypes = [I64, P, P, P, P, P, I, P, P, I, I, P, P, P, P, P, P, SZ, P]
     for name in ("sarr_workspace_size", "sarr_state_size", "sarr_forward", "sarr_backward",
                  "sarr_debug_preprocess", "sarr_debug_tile_lists", "sarr_check_device_errors",
                  "sarr_debug_tile_rect", "sarr_gaussian_params", "sarr_loss_workspace_size",
-                 "sarr_combined_loss", "sarr_densify_workspace_size", "sarr_densify_flags",
+                 "sarr_combined_loss", "sarr_adam_step", "sarr_densify_workspace_size", "sarr_densify_flags",
                  "sarr_densify_apply"):
         getattr(L, name).restype = I
     return L
@@ -360,6 +362,25 @@ def combined_loss(pred, target, l1_weight, ssim_weight, window_size=5, l1_mode="
                                         _ptr(losses), _ptr(grad), _ptr(ws), ws.numel(), _stream(dev)),
                "sarr_combined_loss")
     return losses, grad
+
+
+def adam_step(param, grad, exp_avg, exp_avg_sq, segments, step, beta1=0.9, beta2=0.999, eps=1e-8):
+    """sarr_adam_step over flat (1-D view) fp32 device tensors of equal length;
+    `segments` = [(end, lr), ...] with ascending ends covering the tensors."""
+    t = [_as_cuda_f32(x, nm) for x, nm in ((param, "param"), (grad, "grad"), (exp_avg, "exp_avg"),
+                                           (exp_avg_sq, "exp_avg_sq"))]
+    count = t[0].numel()
+    for x in t:
+        if x.numel() != count or not x.is_contiguous():
+            raise RuntimeError("Adam buffers must be contiguous and of equal length")
+    k = len(segments)
+    ends = (ctypes.c_int64 * k)(*[int(e) for e, _ in segments])
+    lrs = (ctypes.c_float * k)(*[float(lr) for _, lr in segments])
+    dev = t[0].device
+    with torch.cuda.device(dev):
+        _check(lib().sarr_adam_step(count, *[_ptr(x) for x in t], k, ends, lrs, float(beta1),
+                                    float(beta2), float(eps), int(step), _stream(dev)),
+               "sarr_adam_step")
 
 
 def densify_and_prune(means, scales, rotations, opacities, sh, grad_means, grad_threshold,

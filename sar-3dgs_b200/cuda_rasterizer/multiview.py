@@ -80,3 +80,159 @@ def backward_views(means, cov, transmittance, sh, grad_images, views, group=None
     if dist.is_available() and dist.is_initialized() and dist.get_world_size(group) > 1:
         gn = gm.norm(dim=1)
     return gm, gc, gs, gsh, gn
+
+
+class ViewParallelTrainer:
+    """Data-parallel training step over radar views, one process per GPU.
+
+    The step of the reference's TrainingPipeline.train_step
+    (training/training_pipeline.py:148-212: render -> CombinedLoss ->
+    backward -> optimizer.step()) widened to a batch of views per step and
+    sharded by view over the ranks of `group`:
+
+      1. Gaussian parameters: covariance from log-scales and quaternions
+         (detached, as GaussianModel.compute_covariance_full caches it) and
+         the sigmoid transmittance (sarr_gaussian_params);
+      2. forward of this rank's views keeping their tile states (sarr_forward);
+      3. CombinedLoss (L1 + D-SSIM) against the targets and its image gradient
+         (sarr_combined_loss), weighted by 1 / world so that the summed
+         gradients are those of the mean loss over all ranks' views;
+      4. backward of the views reusing the states, written straight into a
+         flat gradient buffer (sarr_backward); the transmittance gradient
+         is chained through the sigmoid;
+      5. the flat gradient buffer summed over the ranks in `buckets` NCCL
+         all-reduces issued back to back (async), each bucket's Adam update
+         (sarr_adam_step) queued behind its own all-reduce, so that the
+         update of bucket b overlaps the all-reduce of bucket b + 1.
+
+    Trainable parameters (the ones that receive gradients in SAR-3DGS: means,
+    opacity logits, SH) live in one flat fp32 buffer laid out as
+    means [n,3] | logits [n] | SH [n,K], with gradients and Adam moments in
+    the same layout; log-scales and quaternions are held but get no gradient
+    (the covariance is detached, gaussian_model.py:306-315), so Adam leaves
+    them alone as torch.optim.Adam does for parameters without gradients.
+    Learning rates per group follow train.py:429-435 (lr for means and
+    opacity, lr / 100 for SH).
+    """
+
+    def __init__(self, means, scales_log, rotations, opacity_logits, sh, lr=1e-3, group=None,
+                 buckets=4, l1_weight=1.0, ssim_weight=0.2, window_size=5, betas=(0.9, 0.999),
+                 eps=1e-8):
+        from . import _native
+        self._N = _native
+        dev = means.device
+        n, k = means.shape[0], sh.shape[1]
+        self.n, self.k, self.device = n, k, dev
+        self.group = group
+        self.world = (dist.get_world_size(group)
+                      if dist.is_available() and dist.is_initialized() else 1)
+        total = n * (4 + k)
+        self.param = torch.empty(total, dtype=torch.float32, device=dev)
+        self.means = self.param[:3 * n].view(n, 3)
+        self.logits = self.param[3 * n:4 * n]
+        self.sh = self.param[4 * n:].view(n, k)
+        self.means.copy_(means)
+        self.logits.copy_(opacity_logits.reshape(n))
+        self.sh.copy_(sh)
+        self.scales = scales_log.detach().contiguous().clone()
+        self.rotations = rotations.detach().contiguous().clone()
+        self.grad = torch.zeros_like(self.param)
+        self.g_means = self.grad[:3 * n].view(n, 3)
+        self.g_logits = self.grad[3 * n:4 * n]
+        self.g_sh = self.grad[4 * n:].view(n, k)
+        self.exp_avg = torch.zeros_like(self.param)
+        self.exp_avg_sq = torch.zeros_like(self.param)
+        self.g_cov = torch.empty((n, 6), dtype=torch.float32, device=dev)  # reaches no parameter
+        self.cov6 = torch.empty((n, 6), dtype=torch.float32, device=dev)
+        self.sigma = torch.empty((n,), dtype=torch.float32, device=dev)
+        self.segments = [(3 * n, lr), (4 * n, lr), (total, lr * 0.01)]
+        # bucket boundaries on 64-element (256-byte) multiples
+        step = -(-total // max(1, buckets) // 64) * 64
+        self.bounds = [(a, min(total, a + step)) for a in range(0, total, step)]
+        self.loss_w = (l1_weight / self.world, ssim_weight / self.world, window_size)
+        self.betas, self.eps = betas, eps
+        self.steps_done = 0
+        self._buf_key = None
+
+    def _buffers(self, views):
+        N = self._N
+        nr, na, V = views[0].range_samples, views[0].azimuth_samples, len(views)
+        key = (nr, na, V)
+        if key != self._buf_key:
+            dev = self.device
+            self.ws = torch.empty(N.workspace_bytes(self.n, nr, na, V), dtype=torch.uint8, device=dev)
+            self.sbytes = N.state_bytes(self.n, nr, na)
+            self.states = torch.empty(V * self.sbytes, dtype=torch.uint8, device=dev)
+            self.images = torch.empty((V, nr, na), dtype=torch.float32, device=dev)
+            self.grad_images = torch.empty_like(self.images)
+            self.losses = torch.empty(3, dtype=torch.float32, device=dev)
+            import ctypes
+            sz = ctypes.c_size_t()
+            N._check(N.lib().sarr_loss_workspace_size(V, nr, na, ctypes.byref(sz)),
+                     "sarr_loss_workspace_size")
+            self.loss_ws = torch.empty(max(sz.value, 256), dtype=torch.uint8, device=dev)
+            self._buf_key = key
+        return nr, na, V
+
+    def step(self, views, targets):
+        """One training step over this rank's `views` (SarrView list) against
+        `targets` [V, Nr, Na] (the rasterizer's memory layout). Returns this
+        rank's losses [3] (total, L1, D-SSIM; device tensor) of the weighted
+        loss (the mean over all ranks' views is their sum)."""
+        import ctypes
+        N = self._N
+        nr, na, V = self._buffers(views)
+        n, k = self.n, self.k
+        dev = self.device
+        st = N._stream(dev)
+        P = N._ptr
+        with torch.cuda.device(dev):
+            N._check(N.lib().sarr_gaussian_params(n, P(self.scales), P(self.rotations), P(self.cov6),
+                                                  N.SARR_COV6, P(self.logits), P(self.sigma), st),
+                     "sarr_gaussian_params")
+            vs = N._views_array(views)
+            N._check(N.lib().sarr_forward(vs, V, n, P(self.means), P(self.cov6), N.SARR_COV6,
+                                          P(self.sigma), P(self.sh), k, k, P(self.images), None,
+                                          P(self.states), P(self.ws), self.ws.numel(), st),
+                     "sarr_forward")
+            l1w, ssw, win = self.loss_w
+            N._check(N.lib().sarr_combined_loss(V, nr, na, P(self.images), P(targets), float(l1w),
+                                                float(ssw), int(win), 0, P(self.losses),
+                                                P(self.grad_images), P(self.loss_ws),
+                                                self.loss_ws.numel(), st), "sarr_combined_loss")
+            N._check(N.lib().sarr_backward(vs, V, n, P(self.means), P(self.cov6), N.SARR_COV6,
+                                           P(self.sigma), P(self.sh), k, k, P(self.grad_images),
+                                           P(self.states), P(self.g_means), P(self.g_cov),
+                                           N.SARR_COV6, P(self.g_logits), P(self.g_sh), k, None, 0,
+                                           P(self.ws), self.ws.numel(), st), "sarr_backward")
+        # d sigmoid(logit) / d logit = sigma (1 - sigma); the same on every rank,
+        # so it may be applied before the sum over ranks
+        self.g_logits.mul_(self.sigma * (1.0 - self.sigma))
+        self.steps_done += 1
+        self._reduce_and_update()
+        return self.losses
+
+    def _reduce_and_update(self):
+        """Bucketed all-reduce of the flat gradients with each bucket's Adam
+        update queued behind its all-reduce."""
+        N = self._N
+        works = []
+        if self.world > 1:
+            for a, b in self.bounds:
+                works.append(dist.all_reduce(self.grad[a:b], group=self.group, async_op=True))
+        b1, b2 = self.betas
+        for i, (a, b) in enumerate(self.bounds):
+            if works:
+                works[i].wait()  # the current stream waits for this bucket's all-reduce
+            segs = [(max(0, min(e, b) - a), lr) for e, lr in self.segments if e > a]
+            N.adam_step(self.param[a:b], self.grad[a:b], self.exp_avg[a:b], self.exp_avg_sq[a:b],
+                        segs, self.steps_done, b1, b2, self.eps)
+
+    def allreduce_only(self):
+        """The step's collective alone (the same buckets, back to back), for
+        measuring its cost; a no-op on one rank."""
+        if self.world > 1:
+            works = [dist.all_reduce(self.grad[a:b], group=self.group, async_op=True)
+                     for a, b in self.bounds]
+            for w in works:
+                w.wait()

@@ -269,22 +269,32 @@ def test_full_size_sweep_view(view_idx):
     assert rel_linf(image_flat(img), fw["image"]) <= IMAGE_RTOL
 
 
-def test_full_size_backward_is_linear_in_grad_output():
-    sc = scene("sweep_1m", seed=0)
-    view = S.sweep_views(1024)[11]
-    gen = torch.Generator().manual_seed(3)
-    g1 = torch.randn(256, 256, generator=gen).cuda()
-    g2 = torch.randn(256, 256, generator=gen).cuda()
-    a = M.render_sar_backward(sc["means"], sc["cov6"], sc["sigma"], sc["sh"], g1, *view)
-    b = M.render_sar_backward(sc["means"], sc["cov6"], sc["sigma"], sc["sh"], g2, *view)
-    c = M.render_sar_backward(sc["means"], sc["cov6"], sc["sigma"], sc["sh"], 2.0 * g1 - 0.5 * g2, *view)
-    for x, y, z in zip(a, b, c):
-        assert rel_linf(z.cpu().numpy(), (2.0 * x - 0.5 * y).cpu().numpy()) <= 1e-5
-    touched = (a[2] != 0).sum().item()
-    assert 0 < touched <= 64 * 256
-
-
 def test_device_error_word_clear():
     sc = scene("cpu_1k", seed=10)
     img, om = M.render_sar(sc["means"], sc["cov6"], sc["sigma"], sc["sh"], *VIEWS["cpu"], False, True)
     assert img.shape == (128, 128)
+
+
+def test_package_render_sar_and_settings_surface():
+    """cuda_rasterizer.render_sar(GaussianDataGPU, H, W) (the reference's
+    cuda_rasterizer/__init__.py:147-186) and render_sar_with_settings
+    (rasterizer_impl_v2.cu:1664-1699) against the oracle."""
+    import cuda_rasterizer as CR
+    sc = scene("cpu_1k", seed=11)
+    view = VIEWS["odd"]
+    assert CR.CUDA_AVAILABLE is True
+    host = CR.GaussianDataCPU(sc["means"].cpu(), sc["cov6"].cpu(), sc["sigma"].cpu(), sc["sh"].cpu(),
+                              (view[0], view[1], view[2]), view[3], view[4], view[5], view[6],
+                              view[7], view[8], view[9])
+    data = host.to_device(torch.device("cuda"))
+    (img, om), aux = CR.render_sar(data, 512, 512)
+    assert aux == {} and img.shape == (view[8], view[9]) and om.shape == (1000,)
+    fw = oracle_forward(sc, view)
+    assert rel_linf(image_flat(img), fw["image"]) <= IMAGE_RTOL
+    assert rel_linf(om.cpu().numpy(), fw["omega"]) <= IMAGE_RTOL
+    settings = M.SARRasterizationSettings(
+        n_gaussians=1000, radar_x=view[0], radar_y=view[1], radar_z=view[2], track_angle=view[3],
+        incidence_angle=view[4], azimuth_angle=view[5], range_resolution=view[6],
+        azimuth_resolution=view[7], range_samples=view[8], azimuth_samples=view[9])
+    img2, om2 = M.render_sar_with_settings(sc["means"], sc["cov6"], sc["sigma"], sc["sh"], settings)
+    assert torch.equal(img2, img) and torch.equal(om2, om)
