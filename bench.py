@@ -1,27 +1,44 @@
 #!/usr/bin/env python
 """Benchmark of the B200 SAR rasterizer.
 
-Workload (the multi-view inference sweep): N = 1,000,000 Gaussians in a
-40 x 40 x 10 m box, 1,024 radar views per step (track angle stepped by
+Headline workload (the multi-view inference sweep): N = 1,000,000 Gaussians
+in a 40 x 40 x 10 m box, 1,024 radar views per step (track angle stepped by
 0.35 deg, incidence uniform 15-45 deg), 256 x 256 images at 0.2 m, forward
 only. Seeded synthetic data (no dataset). With --gpus N (torchrun), every
 rank renders its own 1,024-view sweep (offset track angles): per-GPU work is
-fixed, views are independent, no collective on the data path.
+fixed, views are independent, no collective on the forward data path.
 
-value     forward views/s over all ranks, inputs resident in HBM, L2 flushed
-          (512 MiB write) before every timed step, device time from CUDA events,
-          max over ranks.
-e2e       the same sweep through the public C ABI with host buffers: pinned
-          host -> device copy of the scene, the render, and device -> host copy
-          of all images every step, pipelined (the next step's upload and the
-          image copies overlap the render) and timed as one region.
-fwd_bwd   forward + backward steps/s of one view at 1M Gaussians, 256 x 256
-          (the autograd path: forward state reused by the backward, dense
-          gradients for all N Gaussians).
+value       forward views/s over all ranks, inputs resident in HBM, L2 flushed
+            (512 MiB write) before every timed step, device time from CUDA
+            events, max over ranks.
+roofline    the dominant kernel against HBM bandwidth with the algorithmic
+            bytes of the forward: 104 B per Gaussian per launch group of 256
+            views (means, cov6, transmittance, SH read once per launch) plus
+            4 B per pixel per view (the image written); path_roofline gives
+            the same model for the whole step. render_issue gives the
+            compositing kernel against its instruction-issue bound.
+e2e         the same sweep through the public C ABI with host buffers: pinned
+            host -> device copy of the scene, the render, and device -> host
+            copy of all images every step, pipelined (the next step's upload
+            and the image copies overlap the render) and timed as one region;
+            host_ceiling is the same copies alone.
+omega       the forward with the Omega output of render_sar (256 views per step).
+fwd_bwd     forward + backward steps/s of one view at 1M Gaussians, 256 x 256
+            (forward state reused by the backward, dense gradients for all N
+            Gaussians), L2 flushed before every step, against its HBM bytes
+            312 B per Gaussian + 8 B per pixel.
+train_step  the data-parallel training step on the full-training shape (1M
+            Gaussians, 256 x 256 at 0.2 m, 64 views per rank per step):
+            parameter producer, forward, L1 + 0.2 D-SSIM loss and gradient,
+            backward, NCCL all-reduce of the trainable gradients (N > 1) and
+            Adam; steps/s (max over ranks) and the all-reduce's own cost.
+train_configs  (1 GPU) the training step on the 50k-Gaussian 64-view 128 px
+            scene and on the 500k-Gaussian 16-view 512 px scene.
 
 --impl reference runs the CPU restatement of the reference algorithm (the
-reference ships no CPU implementation) on the host cores, and times the
-reference's own CUDA kernels on a few views as `gpu_reference`.
+reference ships no CPU implementation) on the host cores, forward and
+forward + backward, and times the reference's own CUDA kernels on a few views
+as `gpu_reference`.
 """
 import argparse
 import hashlib
@@ -47,6 +64,19 @@ from cuda_rasterizer import synthetic as S  # noqa: E402
 
 METRIC = "fwd views/s & fwd+bwd steps/s, 1M Gaussians 256², 1/8 B200; % HBM roofline"
 HBM_FALLBACK_GBS = 6650.0
+GROUP_VIEWS = 256          # views per internal launch group of sarr_forward
+TRAIN_VIEWS_PER_RANK = 64  # views per rank per training step
+# Issue model of the compositing kernel: B200 issues at most one warp
+# instruction per cycle in each of the 4 schedulers of its 148 SMs; the
+# reference's per-(pixel, listed record) work (offsets, quadratic form,
+# exponent and cut-off test, exponential, alpha, the two compositing updates)
+# needs at least 12 thread instructions even with the fastest exponential.
+SMS, SCHEDULERS = 148, 4
+MIN_INSTR_PER_PAIR = 12
+# ncu figures of the current render_kernel on one 256-view launch of this
+# workload (dram__bytes_read.sum + dram__bytes_write.sum, smsp__inst_executed
+# .sum); they belong to this workload and these kernels only.
+NCU_RENDER = {"dram_bytes": 118_454_016 + 37_902_848, "warp_instructions": 588_000_000}
 
 
 def parse():
@@ -59,7 +89,7 @@ def parse():
     ap.add_argument("--views", type=int, default=1024)
     ap.add_argument("--samples", type=int, default=256)
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--no-fwdbwd", action="store_true")
+    ap.add_argument("--no-train", action="store_true", help="skip fwd_bwd, train_step, train_configs")
     ap.add_argument("--no-cpu", action="store_true")
     return ap.parse_args()
 
@@ -70,6 +100,16 @@ def peaks():
             return float(json.load(fh)["hbm_gbs"]), "measured"
     except (OSError, KeyError, ValueError):
         return HBM_FALLBACK_GBS, "fallback"
+
+
+def roof(bytes_, seconds, extra=None):
+    peak, kind = peaks()
+    gbs = bytes_ / seconds / 1e9
+    out = {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+           "frac": round(gbs / peak, 4), "peak_source": kind + " (copy bandwidth)"}
+    if extra:
+        out.update(extra)
+    return out
 
 
 class Dist:
@@ -169,60 +209,14 @@ def flush_l2(buf, k):
     buf.fill_(float(k % 7))
 
 
-def scene_name(n):
-    return "sweep_1m" if n == 1_000_000 else None
-
-
 def make_scene(args, device):
-    if scene_name(args.n):
+    if args.n == 1_000_000:
         return S.named_scene("sweep_1m", seed=0, device=device)
     return S.make_scene(args.n, (40.0, 40.0, 10.0), (0.05, 0.5), seed=0, device=device)
 
 
 def rank_views(args, d):
     return S.sweep_views(args.views, samples=args.samples, offset_deg=0.35 * d.rank / max(d.world, 1))
-
-
-CHUNK = 1024          # Gaussians per count row of the binning kernels
-PREFIX_CHUNKS = 48    # chunks binned exactly before saturation skipping
-CAP = 64              # tile list capacity
-GROUP_VIEWS = 256     # views per internal launch group of sarr_forward (kMaxViewsPerLaunch)
-
-
-# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one launch of
-# 256 views, N = 1M, 256 x 256, from an ncu capture of that launch; they
-# belong to this workload and the current kernels only.
-NCU_DRAM_BYTES_PER_LAUNCH = {
-    "render_kernel": 118_454_016 + 37_902_848,
-}
-NCU_LAUNCH_VIEWS = 256
-
-
-def kernel_bytes_per_launch(kind, n, views, T, cov_floats, sh_floats, npix):
-    """Algorithmic bytes of one launch of a forward kernel over `views` views:
-    its compulsory reads and writes, each once.
-      bin_kernel       the prefix chunks: means/cov/transmittance of their
-                       Gaussians once; per view a 4 B tile rectangle per
-                       Gaussian, the u8 per-chunk tile counts and the 4 B
-                       per-chunk tile segment masks.
-      select_kernel    per view and tile, the 64 selected Gaussians'
-                       parameters (means, cov, transmittance, SH) gathered and
-                       their 48 B records, list ids and (Y_r, Z_r) written.
-      render_kernel    per view the 64 records of every tile read and the
-                       image written.
-    The cell binning kernels touch a view-dependent subset (the members of
-    candidate cells) and have no fixed model."""
-    g_bytes = 4 * (3 + cov_floats + 1)
-    C = -(-n // CHUNK)
-    P = min(C, PREFIX_CHUNKS)
-    n_p = min(n, P * CHUNK)
-    if kind == "bin_kernel":
-        return g_bytes * n_p + views * (4 * n_p + P * T + 4 * P * T)
-    if kind == "select_kernel":
-        return views * T * CAP * (g_bytes + 4 * sh_floats + 48 + 4 + 8)
-    if kind == "render_kernel":
-        return views * (T * CAP * 48 + 4 * npix)
-    return None
 
 
 def image_digest(images):
@@ -233,22 +227,42 @@ def image_digest(images):
             hashlib.sha1(host.numpy().tobytes()).hexdigest()[:16])
 
 
-def bench_ours(args, d):
-    from cuda_rasterizer import _native
+def _a256(x):
+    return (x + 255) // 256 * 256
+
+
+def listed_pairs(N, inputs, views, n, s, dev):
+    """(pixel, listed record) pairs of the compositing of these views: the
+    sum over views and tiles of the list length times the tile's pixels,
+    read from the per-view forward states (256 x 256 images: every tile is
+    16 x 16)."""
+    T = (s // 16) ** 2
+    sb = N.state_bytes(n, s, s)
+    states = torch.empty(len(views) * sb, dtype=torch.uint8, device=dev)
+    img = torch.empty((len(views), s, s), dtype=torch.float32, device=dev)
+    N.forward(views, *inputs, img, states=states)
+    o = _a256(4 * n)
+    counts = states.view(len(views), sb)[:, o:o + 4 * T].contiguous().view(torch.int32)
+    total = int(counts.to(torch.int64).sum().item()) * 256
+    del states
+    return total
+
+
+def bench_forward(args, d):
+    from cuda_rasterizer import _native as N
     dev = d.device
     torch.cuda.set_device(dev)
     sc = make_scene(args, dev)
-    means, cov, layout, sigma, sh, sh_stride, sh_k = _native.prepare_inputs(
-        sc["means"], sc["cov6"], sc["sigma"], sc["sh"])
+    inputs = N.prepare_inputs(sc["means"], sc["cov6"], sc["sigma"], sc["sh"])
     n, s = args.n, args.samples
-    views = [_native.make_view(*t) for t in rank_views(args, d)]
+    views = [N.make_view(*t) for t in rank_views(args, d)]
     V = len(views)
     images = torch.empty((V, s, s), dtype=torch.float32, device=dev)
-    ws = torch.empty(_native.workspace_bytes(n, s, s, V), dtype=torch.uint8, device=dev)
+    ws = torch.empty(N.workspace_bytes(n, s, s, V), dtype=torch.uint8, device=dev)
     flush = torch.empty((512 << 20) // 4, dtype=torch.float32, device=dev)
 
     def step():
-        _native.forward(views, means, cov, layout, sigma, sh, sh_stride, sh_k, images, ws=ws)
+        N.forward(views, *inputs, images, ws=ws)
 
     for k in range(args.warmup):
         flush_l2(flush, k)
@@ -263,66 +277,72 @@ def bench_ours(args, d):
           for _ in range(args.steps)]
     torch.cuda.synchronize()
     d.barrier()
-    l0 = _native.launch_count()
+    l0 = N.launch_count()
     for k in range(args.steps):
         flush_l2(flush, k)
         ev[k][0].record()
         step()
         ev[k][1].record()
     torch.cuda.synchronize()
-    launches = _native.launch_count() - l0
+    launches = N.launch_count() - l0
     d.barrier()
     clk = clocks.stop()
     t_ms = sum(a.elapsed_time(b) for a, b in ev)
     t_ms_max = d.max(t_ms)
-    total_views = d.sum(float(V * args.steps))
-    value = total_views / (t_ms_max / 1e3)
+    value = d.sum(float(V * args.steps)) / (t_ms_max / 1e3)
+    checksum = image_digest(images)  # guards against a step doing no work
 
-    # checksum of the last step's images (guards against a step doing no work)
-    checksum = image_digest(images)
-
-    # roofline: per-kernel device time from the library's event hooks
-    _native.profile_enable(True)
+    # per-kernel device time from the library's event hooks (launch stream)
+    N.profile_enable(True)
     rsteps = min(args.steps, 5)
     for k in range(rsteps):
         flush_l2(flush, k)
         step()
     torch.cuda.synchronize()
-    prof = _native.profile_read()
-    _native.profile_enable(False)
-    T = ((s + 15) // 16) ** 2
-    peak, peak_kind = peaks()
-    cov_floats = 9 if layout == 9 else 6
-    rooflines = {}
-    for kname, (kms, klaunch) in prof.items():
-        if not klaunch:
-            continue
-        per_launch_views = V / (klaunch / rsteps)
-        b = kernel_bytes_per_launch(kname, n, per_launch_views, T, cov_floats, sh_k, s * s)
-        if b is None:
-            continue
-        achieved = b / (kms / klaunch / 1e3) / 1e9
-        rooflines[kname] = {"kernel": kname, "bound": "hbm", "achieved": round(achieved, 1),
-                            "peak": peak, "peak_source": peak_kind, "unit": "GB/s",
-                            "frac": round(achieved / peak, 4),
-                            "traffic": (NCU_DRAM_BYTES_PER_LAUNCH.get(kname)
-                                        if n == 1_000_000 and s == 256
-                                        and per_launch_views == NCU_LAUNCH_VIEWS else None),
-                            "bytes_per_launch": int(b), "avg_launch_us": round(kms / klaunch * 1e3, 2)}
-    dominant = max(prof.items(), key=lambda kv: kv[1][0])[0]
-    roof = rooflines.get(dominant)
-    kernels = {k: {"ms_per_step": round(v[0] / rsteps, 4), "launches_per_step": v[1] / rsteps}
+    prof = N.profile_read()
+    N.profile_enable(False)
+    kernels = {k: {"ms_per_step": round(v[0] / rsteps, 4), "launches_per_step": v[1] / rsteps,
+                   "avg_launch_us": round(v[0] / v[1] * 1e3, 2)}
                for k, v in prof.items() if v[1]}
+    dominant = max(prof.items(), key=lambda kv: kv[1][0])[0]
+    dom_ms, dom_launches = prof[dominant]
+    launch_views = V / (dom_launches / rsteps)
+    npix = s * s
+    fwd_bytes = 104 * n + 4 * npix * launch_views  # one launch group (SURVEY model, batched)
+    dom_s = dom_ms / dom_launches / 1e3
+    full = n == 1_000_000 and s == 256 and launch_views == GROUP_VIEWS
+    roofline = roof(fwd_bytes, dom_s, {
+        "kernel": dominant, "traffic": (NCU_RENDER["dram_bytes"] if full and dominant == "render_kernel"
+                                        else None),
+        "bytes_per_launch": int(fwd_bytes), "views_per_launch": launch_views,
+        "avg_launch_us": round(dom_s * 1e6, 2),
+        "model": "104 B/Gaussian per launch group + 4 B/pixel per view"})
+    groups = -(-V // GROUP_VIEWS)
+    step_bytes = 104 * n * groups + 4 * npix * V
+    path = roof(step_bytes, t_ms_max / args.steps / 1e3,
+                {"bytes_per_step": int(step_bytes), "model": roofline["model"]})
+    path["achieved_total_gbs"] = round(path["achieved"] * d.world, 1)
+
+    # the compositing kernel against its instruction-issue bound
+    render_issue = None
+    if "render_kernel" in prof and prof["render_kernel"][1]:
+        pairs = listed_pairs(N, inputs, views[:GROUP_VIEWS], n, s, dev) * (V / min(V, GROUP_VIEWS))
+        r_ms, r_l = prof["render_kernel"]
+        per_launch_pairs = pairs / (r_l / rsteps)
+        f_hz = (clk["sm_mhz"] if clk else 1965.0) * 1e6
+        bound_s = per_launch_pairs * MIN_INSTR_PER_PAIR / 32 / (SMS * SCHEDULERS * f_hz)
+        r_s = r_ms / r_l / 1e3
+        render_issue = {"bound": "issue", "pairs_per_launch": int(per_launch_pairs),
+                        "min_thread_instr_per_pair": MIN_INSTR_PER_PAIR,
+                        "bound_us": round(bound_s * 1e6, 2), "achieved_us": round(r_s * 1e6, 2),
+                        "frac": round(bound_s / r_s, 4),
+                        "ncu_thread_instr_per_pair": (round(NCU_RENDER["warp_instructions"] * 32 /
+                                                            per_launch_pairs, 2) if full else None)}
 
     out = {"value": value, "ms_per_step": t_ms_max / args.steps, "launches": launches,
-           "clocks": clk, "roofline": roof, "kernel_rooflines": rooflines, "kernels": kernels,
-           "checksum": checksum, "checksum_stable": checksum == checksum0,
-           "views_per_rank": V}
-    if not args.no_e2e:
-        out["e2e"] = bench_e2e(args, d, sc, views)
-    if not args.no_fwdbwd:
-        out["fwd_bwd"] = bench_fwd_bwd(args, d, means, cov, layout, sigma, sh, sh_stride, sh_k,
-                                       views, flush)
+           "clocks": clk, "roofline": roofline, "path_roofline": path, "render_issue": render_issue,
+           "kernels": kernels, "checksum": checksum, "checksum_stable": checksum == checksum0,
+           "views_per_rank": V, "sc": sc, "inputs": inputs, "views": views, "flush": flush}
     return out
 
 
@@ -334,8 +354,9 @@ def bench_e2e(args, d, sc, views):
     memory (download stream) while the next group renders; step k+1's upload
     overlaps step k's render. The timed region runs from the first upload to
     the last image copy, so every step's copies lie inside it; L2 is flushed
-    (512 MiB write) at the start of every step's render."""
-    from cuda_rasterizer import _native
+    (512 MiB write) at the start of every step's render. The host ceiling is
+    the same uploads and downloads with no render."""
+    from cuda_rasterizer import _native as N
     dev = d.device
     n, s, V = args.n, args.samples, len(views)
     keys = ("means", "cov6", "sigma", "sh")
@@ -344,7 +365,7 @@ def bench_e2e(args, d, sc, views):
     h_img = torch.empty((V, s, s), dtype=torch.float32).pin_memory()
     d_img = [torch.empty((V, s, s), dtype=torch.float32, device=dev) for _ in range(2)]
     group = GROUP_VIEWS
-    ws = torch.empty(_native.workspace_bytes(n, s, s, group), dtype=torch.uint8, device=dev)
+    ws = torch.empty(N.workspace_bytes(n, s, s, group), dtype=torch.uint8, device=dev)
     comp = torch.cuda.current_stream(dev)
     up = torch.cuda.Stream(dev)
     down = torch.cuda.Stream(dev)
@@ -352,7 +373,7 @@ def bench_e2e(args, d, sc, views):
     h2d = sum(v.numel() * 4 for v in h.values())
     d2h = V * s * s * 4
 
-    def run(steps):
+    def run(steps, render=True):
         """Enqueues `steps` pipelined steps; returns (start, end) events."""
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         start.record(comp)
@@ -375,13 +396,15 @@ def bench_e2e(args, d, sc, views):
             comp.wait_event(uploaded[j])
             if j >= 2:
                 comp.wait_event(copied[j - 2])  # images of step j - 2 are on the host
-            flush_l2(flush, j)
-            means, cov, layout, sigma, sh, st, kk = _native.prepare_inputs(
-                dm[j % 2]["means"], dm[j % 2]["cov6"], dm[j % 2]["sigma"], dm[j % 2]["sh"])
+            if render:
+                flush_l2(flush, j)
+                inputs = N.prepare_inputs(dm[j % 2]["means"], dm[j % 2]["cov6"], dm[j % 2]["sigma"],
+                                          dm[j % 2]["sh"])
             img = d_img[j % 2]
             for g0 in range(0, V, group):
                 g1 = min(V, g0 + group)
-                _native.forward(views[g0:g1], means, cov, layout, sigma, sh, st, kk, img[g0:g1], ws=ws)
+                if render:
+                    N.forward(views[g0:g1], *inputs, img[g0:g1], ws=ws)
                 e = torch.cuda.Event()
                 e.record(comp)
                 down.wait_event(e)
@@ -399,65 +422,225 @@ def bench_e2e(args, d, sc, views):
         return start, end
 
     steps = max(3, min(args.steps, 30))  # the pipeline fills once per timed region
-    a, b = run(2)
-    b.synchronize()
-    d.barrier()
-    a, b = run(steps)
-    b.synchronize()
-    t = a.elapsed_time(b)
-    ok = bool(torch.equal(h_img[V - 1].to(dev), d_img[(steps - 1) % 2][V - 1]))
-    d.barrier()
-    t_max = d.max(t)
-    value = d.sum(float(V * steps)) / (t_max / 1e3)
+    out = {}
+    ok = False
+    for render in (True, False):
+        a, b = run(2, render)
+        b.synchronize()
+        d.barrier()
+        a, b = run(steps, render)
+        b.synchronize()
+        t = a.elapsed_time(b)
+        if render:
+            ok = bool(torch.equal(h_img[V - 1].to(dev), d_img[(steps - 1) % 2][V - 1]))
+        d.barrier()
+        t_max = d.max(t)
+        out[render] = (d.sum(float(V * steps)) / (t_max / 1e3), t_max / steps)
+    value, ms = out[True]
+    ceil_v, ceil_ms = out[False]
     return {"value": value, "unit": "views/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-            "ms_per_step": t_max / steps, "steps": steps, "host_copy_verified": ok,
+            "ms_per_step": ms, "steps": steps, "host_copy_verified": ok,
+            "host_ceiling": {"value": ceil_v, "unit": "views/s", "ms_per_step": ceil_ms,
+                             "what": "the same pinned uploads and image downloads on all ranks, "
+                                     "no render", "frac": round(value / ceil_v, 4)},
             "pipeline": "step k+1 upload overlaps step k render; group images copied back "
                         "while the next group renders; one timed region over all steps"}
 
 
-def bench_fwd_bwd(args, d, means, cov, layout, sigma, sh, sh_stride, sh_k, views, flush):
+def bench_omega(args, d, inputs, views, flush):
+    """render_sar's full contract (image and Omega) on one 256-view launch
+    group per step: views/s, L2 flushed before every step."""
+    from cuda_rasterizer import _native as N
+    dev = d.device
+    n, s = args.n, args.samples
+    vs = views[:GROUP_VIEWS]
+    V = len(vs)
+    images = torch.empty((V, s, s), dtype=torch.float32, device=dev)
+    omega = torch.empty((V, n), dtype=torch.float32, device=dev)
+    ws = torch.empty(N.workspace_bytes(n, s, s, V, N.SARR_FLAG_OMEGA), dtype=torch.uint8, device=dev)
+    steps = max(3, min(args.steps, 10))
+    t = 0.0
+    for k in range(steps + 2):
+        flush_l2(flush, k)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        N.forward(vs, *inputs, images, omega=omega, ws=ws)
+        b.record()
+        b.synchronize()
+        if k >= 2:
+            t += a.elapsed_time(b)
+    t_max = d.max(t)
+    return {"value": d.sum(float(V * steps)) / (t_max / 1e3), "unit": "views/s",
+            "ms_per_step": t_max / steps, "views_per_step": V,
+            "outputs": "image [Nr, Na] and omega [N] per view (render_sar)"}
+
+
+def bench_fwd_bwd(args, d, inputs, views, flush):
     """One view per step: forward keeping its state, backward reusing it,
-    dense gradients for all N Gaussians (the SARRasterizer training path)."""
-    from cuda_rasterizer import _native
+    dense gradients for all N Gaussians (the SARRasterizer training path);
+    L2 flushed before every step, each step timed by its own events."""
+    from cuda_rasterizer import _native as N
     dev = d.device
     n, s = args.n, args.samples
     img = torch.empty((s, s), dtype=torch.float32, device=dev)
     g = torch.randn((s, s), generator=torch.Generator().manual_seed(1)).to(dev)
-    state = torch.empty(_native.state_bytes(n, s, s), dtype=torch.uint8, device=dev)
-    ws = torch.empty(_native.workspace_bytes(n, s, s, 1), dtype=torch.uint8, device=dev)
+    state = torch.empty(N.state_bytes(n, s, s), dtype=torch.uint8, device=dev)
+    ws = torch.empty(N.workspace_bytes(n, s, s, 1), dtype=torch.uint8, device=dev)
     gm = torch.empty((n, 3), device=dev)
     gc = torch.empty((n, 6), device=dev)
     gs = torch.empty((n,), device=dev)
     gsh = torch.empty((n, 16), device=dev)
     gn = torch.empty((n,), device=dev)
-    per_block = 64
 
-    def block(k0):
-        for j in range(per_block):
-            v = [views[(k0 + j) % len(views)]]
-            _native.forward(v, means, cov, layout, sigma, sh, sh_stride, sh_k, img, states=state, ws=ws)
-            _native.backward(v, means, cov, layout, sigma, sh, sh_stride, sh_k, g, gm, gc,
-                             _native.SARR_COV6, gs, gsh, grad_norm=gn, states=state, ws=ws)
+    def one(k):
+        v = [views[k % len(views)]]
+        N.forward(v, *inputs, img, states=state, ws=ws)
+        N.backward(v, *inputs, g, gm, gc, N.SARR_COV6, gs, gsh, grad_norm=gn, states=state, ws=ws)
 
-    block(0)
+    for k in range(8):
+        one(k)
     torch.cuda.synchronize()
     d.barrier()
-    blocks = 5
-    t = 0.0
-    for b in range(blocks):
-        flush_l2(flush, b)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        block(b * per_block)
-        e1.record()
-        e1.synchronize()
-        t += e0.elapsed_time(e1)
+    steps = 200
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(steps)]
+    for k in range(steps):
+        flush_l2(flush, k)
+        ev[k][0].record()
+        one(k)
+        ev[k][1].record()
+    torch.cuda.synchronize()
+    t = sum(a.elapsed_time(b) for a, b in ev)
     t_max = d.max(t)
-    steps = blocks * per_block
-    value = d.sum(float(steps)) / (t_max / 1e3)
-    return {"value": value, "unit": "steps/s", "ms_per_step": t_max / steps,
+    step_s = t_max / steps / 1e3
+    b_fb = 312 * n + 8 * s * s
+    return {"value": d.sum(float(steps)) / (t_max / 1e3), "unit": "steps/s", "ms_per_step": step_s * 1e3,
             "step": "1 view fwd+bwd, dense grads for 1M Gaussians, 256x256",
-            "l2": "flushed every 64 steps"}
+            "l2": "flushed before every step (512 MiB device write)",
+            "roofline": roof(b_fb, step_s, {"bytes_per_step": b_fb,
+                                             "model": "312 B/Gaussian + 8 B/pixel per view"})}
+
+
+def _targets(N, views_t, n_target, box, scales, dev):
+    """Target images of a separate seeded scene (seed 1) for these views."""
+    tgt = S.make_scene(n_target, box, scales, seed=1, device=dev)
+    vs = [N.make_view(*v) for v in views_t]
+    nr, na = views_t[0][8], views_t[0][9]
+    out = torch.empty((len(vs), nr, na), dtype=torch.float32, device=dev)
+    N.forward(vs, *N.prepare_inputs(tgt["means"], tgt["cov6"], tgt["sigma"], tgt["sh"]), out)
+    return out
+
+
+def _time_trainer(tr, views, targets, steps, warmup, flush, d):
+    from cuda_rasterizer import _native as N
+    for k in range(warmup):
+        tr.step(views, targets)
+    torch.cuda.synchronize()
+    d.barrier()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(steps)]
+    l0 = N.launch_count()
+    for k in range(steps):
+        flush_l2(flush, k)
+        ev[k][0].record()
+        tr.step(views, targets)
+        ev[k][1].record()
+    torch.cuda.synchronize()
+    launches = N.launch_count() - l0
+    return sum(a.elapsed_time(b) for a, b in ev), launches
+
+
+def bench_train_step(args, d, flush):
+    """The full-training shape, data-parallel: 1M Gaussians, 64 views per
+    rank per step (256 x 256 at 0.2 m, azimuth uniform 0-360 deg, incidence
+    15 or 17 deg), loss L1 + 0.2 D-SSIM against a seeded 200k-Gaussian target
+    scene, Adam (lr 1e-3; SH lr 1e-5); the trainable gradients (80 B per
+    Gaussian) summed over the ranks by 4 bucketed NCCL all-reduces, each
+    followed by its bucket's Adam update."""
+    from cuda_rasterizer import _native as N
+    from cuda_rasterizer import multiview
+    dev = d.device
+    n, s = args.n, args.samples
+    box, scales = (40.0, 40.0, 10.0), (0.05, 0.5)
+    p = S.make_param_scene(n, box, scales, seed=0, device=dev)
+    allv = S.training_views(TRAIN_VIEWS_PER_RANK * d.world, rho=0.2, samples=s)
+    mine = allv[d.rank * TRAIN_VIEWS_PER_RANK:(d.rank + 1) * TRAIN_VIEWS_PER_RANK]
+    targets = _targets(N, mine, 200_000, box, scales, dev)
+    views = [N.make_view(*v) for v in mine]
+    tr = multiview.ViewParallelTrainer(p["means"], p["scales"], p["rotations"], p["logits"], p["sh"],
+                                       lr=1e-3, buckets=4)
+    steps = max(3, min(args.steps, 20))
+    t, launches = _time_trainer(tr, views, targets, steps, max(3, args.warmup), flush, d)
+    t_max = d.max(t)
+    step_ms = t_max / steps
+    # the collective alone: the same four buckets, back to back
+    ar_ms = 0.0
+    if d.world > 1:
+        for _ in range(3):
+            tr.allreduce_only()
+        torch.cuda.synchronize()
+        d.barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(steps):
+            tr.allreduce_only()
+        b.record()
+        b.synchronize()
+        ar_ms = d.max(a.elapsed_time(b)) / steps
+    loss = float(tr.losses[0].item())
+    npix = s * s
+    b_fb = 312 * n + 8 * npix * TRAIN_VIEWS_PER_RANK  # batched: parameters once per step
+    return {"value": 1e3 / step_ms, "unit": "steps/s", "ms_per_step": step_ms,
+            "views_per_s": d.world * TRAIN_VIEWS_PER_RANK * 1e3 / step_ms,
+            "views_per_rank_per_step": TRAIN_VIEWS_PER_RANK,
+            "global_views_per_step": TRAIN_VIEWS_PER_RANK * d.world, "scaling": "weak",
+            "n_gaussians": n,
+            "allreduce": {"bytes": int(tr.grad.numel() * 4), "buckets": len(tr.bounds),
+                          "ms_alone": round(ar_ms, 4),
+                          "share_of_step_alone": round(ar_ms / step_ms, 4) if d.world > 1 else 0.0},
+            "loss_last_step": loss, "gpu_launches_per_step": launches / steps,
+            "roofline": roof(b_fb, step_ms / 1e3,
+                             {"model": "312 B/Gaussian per step + 8 B/pixel per view",
+                              "bytes_per_step": b_fb}),
+            "l2": "flushed before every step (512 MiB device write)",
+            "step": "producer, forward (states kept), CombinedLoss(1.0, 0.2) + image gradient, "
+                    "backward, sigmoid chain, bucketed NCCL all-reduce (N > 1), Adam"}
+
+
+def bench_train_configs(args, d, flush):
+    """The training step on one GPU on the two smaller training scenes:
+    50k Gaussians in 20 x 20 x 6 m, 64 views of 128 x 128 at 0.3 m (targets
+    from a separate 20k scene); 500k Gaussians in 60 x 60 x 15 m with scales
+    0.02-0.3 m, 16 views of 512 x 512 at 0.1 m, incidence 15-45 deg (targets
+    from a separate 100k scene)."""
+    from cuda_rasterizer import _native as N
+    from cuda_rasterizer import multiview
+    dev = d.device
+    out = {}
+    cfgs = (("train_n50000_128px_64views", 50_000, (20.0, 20.0, 6.0), (0.05, 0.5), 20_000,
+             S.training_views(64)),
+            ("hires_n500000_512px_16views", 500_000, (60.0, 60.0, 15.0), (0.02, 0.3), 100_000,
+             S.hires_views(16)))
+    for name, n, box, scales, n_tgt, views_t in cfgs:
+        p = S.make_param_scene(n, box, scales, seed=0, device=dev)
+        targets = _targets(N, views_t, n_tgt, box, scales, dev)
+        views = [N.make_view(*v) for v in views_t]
+        tr = multiview.ViewParallelTrainer(p["means"], p["scales"], p["rotations"], p["logits"],
+                                           p["sh"], lr=1e-3, buckets=4, distributed=False)
+        steps = max(5, min(args.steps, 20))
+        t, launches = _time_trainer(tr, views, targets, steps, max(3, args.warmup), flush, d)
+        step_ms = t / steps
+        npix = views_t[0][8] * views_t[0][9]
+        b_fb = 312 * n + 8 * npix * len(views)  # batched: parameters once per step
+        out[name] = {"value": 1e3 / step_ms, "unit": "steps/s", "ms_per_step": step_ms,
+                     "views_per_step": len(views), "views_per_s": len(views) * 1e3 / step_ms,
+                     "gpu_launches_per_step": launches / steps,
+                     "roofline": roof(b_fb, step_ms / 1e3, {
+                         "bytes_per_step": b_fb,
+                         "model": "312 B/Gaussian per step + 8 B/pixel per view"}),
+                     "loss_last_step": float(tr.losses[0].item())}
+        del tr, p, targets
+    return out
 
 
 def bench_train_ops(args, d):
@@ -465,10 +648,10 @@ def bench_train_ops(args, d):
     parameter producer over the N Gaussians (72 B per Gaussian: log-scales,
     quaternion and logit read, 3x3 covariance and transmittance written), the
     combined L1 + D-SSIM loss with its gradient over 64 images of the sweep
-    size (12 B per pixel: both images read, the gradient written), and one
-    densify/prune pass over the N Gaussians."""
-    from cuda_rasterizer import _native
-    from cuda_rasterizer import gaussian_params as GP  # noqa: F401
+    size (12 B per pixel: both images read, the gradient written), one
+    densify/prune pass over the N Gaussians, and Adam over the 20 trainable
+    floats per Gaussian."""
+    from cuda_rasterizer import _native as N
     dev = d.device
     n, s = args.n, args.samples
     g = torch.Generator(device=dev).manual_seed(3)
@@ -491,11 +674,9 @@ def bench_train_ops(args, d):
         b.synchronize()
         return a.elapsed_time(b) / reps / 1e3
 
-    t_p = timed(lambda: _native.gaussian_params(scales, rot, logits))
-    t_l = timed(lambda: _native.combined_loss(pred, target, 0.9, 0.1, 5, "plain"))
+    t_p = timed(lambda: N.gaussian_params(scales, rot, logits))
+    t_l = timed(lambda: N.combined_loss(pred, target, 0.9, 0.1, 5, "plain"))
     bp, bl = 72 * n, 12 * 64 * s * s
-    # densify/prune over the N Gaussians (flags, order-preserving offsets, the
-    # host's max_gaussians decision on the counts, the new set written)
     from cuda_rasterizer import densify as DZ
     dm = (torch.rand((n, 3), device=dev, generator=g) - 0.5) * 40
     ds = torch.rand((n, 3), device=dev, generator=g) * 8.0 - 6.5
@@ -508,6 +689,11 @@ def bench_train_ops(args, d):
     t_d = timed(lambda: DZ.densify_and_prune_tensors(dm, ds, dq, do, dsh, dgr, *dargs), reps=10)
     n_out = int(out[0].shape[0])
     bd = n * (12 + 12 + 16 + 4 + 64 + 12) + n_out * (12 + 12 + 16 + 4 + 64)
+    flat = torch.randn(20 * n, device=dev, generator=g)
+    grad = torch.randn(20 * n, device=dev, generator=g)
+    m, v = torch.zeros_like(flat), torch.zeros_like(flat)
+    t_a = timed(lambda: N.adam_step(flat, grad, m, v, [(20 * n, 1e-3)], 1))
+    ba = 20 * n * (16 + 12)
     return {"producer": {"gaussians_per_s": n / t_p, "achieved_gbs": round(bp / t_p / 1e9, 1),
                          "frac": round(bp / t_p / 1e9 / peak, 4), "peak_source": peak_kind,
                          "us": round(t_p * 1e6, 2)},
@@ -517,16 +703,38 @@ def bench_train_ops(args, d):
                         "counts": [int(c) for c in counts],
                         "achieved_gbs": round(bd / t_d / 1e9, 1), "frac": round(bd / t_d / 1e9 / peak, 4),
                         "bytes": "120 B read per Gaussian, 108 B written per output Gaussian; "
-                                 "includes the host reading the three counts"}}
+                                 "includes the host reading the three counts"},
+            "adam": {"us": round(t_a * 1e6, 2), "achieved_gbs": round(ba / t_a / 1e9, 1),
+                     "frac": round(ba / t_a / 1e9 / peak, 4),
+                     "bytes": "20 floats per Gaussian: param, grad, m, v read; param, m, v written"}}
+
+
+def _cpu_scene(args):
+    sc = make_scene(args, "cpu")
+    return {k: v.numpy() for k, v in sc.items()}
+
+
+def cpu_fwd_bwd_sample(O, s, views, budget_s):
+    """Oracle forward + backward of single views (the reference's
+    render_sar_backward recomputes the forward, .cu:1495-1559) until the
+    budget is used: (steps, seconds)."""
+    g = np.random.default_rng(1).standard_normal(views[0][8] * views[0][9]).astype(np.float32)
+    done, t0 = 0, time.perf_counter()
+    while done < 16:
+        O.backward_full(O.make_view(*views[done]), s["means"], s["cov6"], s["sigma"], s["sh"], g)
+        done += 1
+        if time.perf_counter() - t0 > budget_s:
+            break
+    return done, time.perf_counter() - t0
 
 
 def cpu_baseline(args):
     """CPU restatement of the reference algorithm on a bounded sample of the
-    same workload (image-only forward), all host threads."""
+    same workloads, all host threads: image-only forward views/s (the
+    headline) and forward + backward steps/s (one view per step)."""
     from oracle import oracle as O
     cores = O.set_threads()
-    sc = make_scene(args, "cpu")
-    s = {k: v.numpy() for k, v in sc.items()}
+    s = _cpu_scene(args)
     views = S.sweep_views(args.views, samples=args.samples)
     done, t0 = 0, time.perf_counter()
     while done < 64:
@@ -536,21 +744,24 @@ def cpu_baseline(args):
         if time.perf_counter() - t0 > 12.0:
             break
     dt = time.perf_counter() - t0
+    nb, tb = cpu_fwd_bwd_sample(O, s, views, 8.0)
     return {"value": done / dt, "unit": "views/s", "cores": cores, "kind": "port",
             "sample": f"{done} views of the sweep (N={args.n}, {args.samples}x{args.samples}), "
-                      "image-only forward, C restatement with OpenMP"}
+                      "image-only forward, C restatement with OpenMP",
+            "fwd_bwd": {"value": nb / tb, "unit": "steps/s", "cores": cores, "kind": "port",
+                        "sample": f"{nb} single-view forward + backward steps at N={args.n}"}}
 
 
 def bench_reference(args, d):
     """Reference arm: the CPU restatement on the host cores (rank 0 only), K
-    steps of a bounded 2-view sample; plus the reference's own CUDA kernels on
-    two views when its harness and a GPU are available."""
+    steps of a bounded 2-view sample; forward + backward steps/s of a bounded
+    sample; plus the reference's own CUDA kernels on two views when its
+    harness and a GPU are available."""
     if d.rank != 0:
         return None
     from oracle import oracle as O
     cores = O.set_threads()
-    sc = make_scene(args, "cpu")
-    s = {k: v.numpy() for k, v in sc.items()}
+    s = _cpu_scene(args)
     views = S.sweep_views(args.views, samples=args.samples)
     per_step = 2
     for k in range(args.warmup):
@@ -563,6 +774,7 @@ def bench_reference(args, d):
                       s["sigma"], s["sh"], want_omega=False)
     dt = time.perf_counter() - t0
     value = args.steps * per_step / dt
+    nb, tb = cpu_fwd_bwd_sample(O, s, views, 8.0)
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "views/s",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": dt * 1e3 / args.steps, "higher_is_better": True, "scaling": "weak",
@@ -572,19 +784,21 @@ def bench_reference(args, d):
                              "kind": "port",
                              "sample": f"{per_step} views per step of the sweep, image-only forward"},
             "e2e": {"value": value, "unit": "views/s", "h2d_bytes_per_step": 0,
-                    "d2h_bytes_per_step": 0}}
+                    "d2h_bytes_per_step": 0},
+            "fwd_bwd": {"value": nb / tb, "unit": "steps/s", "cores": cores, "kind": "port",
+                        "sample": f"{nb} single-view forward + backward steps at N={args.n}"}}
     try:
-        line["gpu_reference"] = gpu_reference(args, sc, views)
+        line["gpu_reference"] = gpu_reference(args, s, views)
     except Exception as e:  # reported, not fatal: the CPU arm above is the reference arm
         line["gpu_reference"] = {"unavailable": f"{type(e).__name__}: {e}"}
     return line
 
 
-def gpu_reference(args, sc, views):
+def gpu_reference(args, s, views):
     from oracle.ref import build_ref
     R = build_ref.load_module()
     dev = torch.device("cuda", 0)
-    t = {k: sc[k].to(dev).contiguous() for k in ("means", "cov6", "sigma", "sh")}
+    t = {k: torch.from_numpy(s[k]).to(dev).contiguous() for k in ("means", "cov6", "sigma", "sh")}
     R.render_sar(t["means"], t["cov6"], t["sigma"], t["sh"], *views[0], False, False)
     torch.cuda.synchronize()
     nv = 2
@@ -595,9 +809,21 @@ def gpu_reference(args, sc, views):
     b.record()
     b.synchronize()
     ms = a.elapsed_time(b)
+    g = torch.randn((views[0][8], views[0][9]), generator=torch.Generator().manual_seed(1)).to(dev)
+    R.render_sar_backward(t["means"], t["cov6"], t["sigma"], t["sh"], g, *views[0])
+    torch.cuda.synchronize()
+    a.record()
+    for j in range(nv):
+        R.render_sar(t["means"], t["cov6"], t["sigma"], t["sh"], *views[1 + j], False, False)
+        R.render_sar_backward(t["means"], t["cov6"], t["sigma"], t["sh"], g, *views[1 + j])
+    b.record()
+    b.synchronize()
+    ms_fb = a.elapsed_time(b)
     return {"value": nv / (ms / 1e3), "unit": "views/s", "kind": "reference",
+            "fwd_bwd": {"value": nv / (ms_fb / 1e3), "unit": "steps/s"},
             "sample": f"{nv} views, reference rasterizer_impl_v2.cu kernels (slot-indexing fix), "
-                      "render_sar incl. its per-call allocations and Omega host round trip"}
+                      "render_sar incl. its per-call allocations and Omega host round trip; "
+                      "fwd_bwd: render_sar then render_sar_backward per view"}
 
 
 def config(args):
@@ -605,25 +831,8 @@ def config(args):
             "n_gaussians": args.n, "image": [args.samples, args.samples], "rho_m": 0.2,
             "views_per_step_per_gpu": args.views, "scene_box_m": [40, 40, 10],
             "l2": "flushed before every timed step (512 MiB device write)",
-            "parallelism": f"view-sharded x{args.gpus}, no data-path collective",
-            "outputs": "images only (the SARRasterizer forward contract)"}
-
-
-def path_roofline(args, r, world):
-    """Whole-forward HBM rooflines per GPU. Per view: the 104 B of fp32
-    parameters per Gaussian (means 12, cov6 24, transmittance 4, SH 64) read
-    and the image written once per view. Batched: the parameters read once
-    per launch group of 256 views, the image once per view."""
-    peak, peak_kind = peaks()
-    n, npix = args.n, args.samples * args.samples
-    vps = r["value"] / world
-    per_view = 104 * n + 4 * npix
-    batched = 104 * n / GROUP_VIEWS + 4 * npix
-    return {"peak": peak, "peak_source": peak_kind, "unit": "GB/s",
-            "per_view": {"bytes_per_view": per_view, "achieved": round(per_view * vps / 1e9, 1),
-                         "frac": round(per_view * vps / 1e9 / peak, 4)},
-            "batched": {"bytes_per_view": round(batched), "achieved": round(batched * vps / 1e9, 1),
-                        "frac": round(batched * vps / 1e9 / peak, 4)}}
+            "parallelism": f"view-sharded x{args.gpus}, no data-path collective in the forward",
+            "outputs": "images only (the SARRasterizer forward contract); omega: with Omega"}
 
 
 def main():
@@ -638,21 +847,26 @@ def main():
             d.close()
         return
     d = Dist()
-    r = bench_ours(args, d)
+    r = bench_forward(args, d)
     line = {"metric": METRIC, "value": r["value"], "unit": "views/s", "n_gpus": d.world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": r["ms_per_step"],
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded; the sweep's scene and view distributions)", "config": config(args),
             "roofline": r["roofline"], "gpu_launches": r["launches"], "clocks": r["clocks"],
-            "kernel_rooflines": r["kernel_rooflines"], "path_roofline": path_roofline(args, r, d.world),
+            "path_roofline": r["path_roofline"], "render_issue": r["render_issue"],
             "kernels": r["kernels"], "image_checksum": r["checksum"][0],
             "image_sha1": r["checksum"][1], "image_checksum_stable": r["checksum_stable"]}
-    if "e2e" in r:
-        line["e2e"] = r["e2e"]
-    if "fwd_bwd" in r:
-        line["fwd_bwd"] = r["fwd_bwd"]
-    if not args.no_fwdbwd:
-        line["train_ops"] = bench_train_ops(args, d)
+    if not args.no_e2e:
+        line["e2e"] = bench_e2e(args, d, r["sc"], r["views"])
+    line["omega"] = bench_omega(args, d, r["inputs"], r["views"], r["flush"])
+    if not args.no_train:
+        line["fwd_bwd"] = bench_fwd_bwd(args, d, r["inputs"], r["views"], r["flush"])
+        flush = r["flush"]
+        del r
+        line["train_step"] = bench_train_step(args, d, flush)
+        if d.world == 1:
+            line["train_configs"] = bench_train_configs(args, d, flush)
+            line["train_ops"] = bench_train_ops(args, d)
     if d.rank == 0 and d.world == 1 and not args.no_cpu:
         line["cpu_baseline"] = cpu_baseline(args)
     if d.rank == 0:

@@ -29,7 +29,10 @@ constexpr int kChunk = kBinThreads * kBinPerThread;  // Gaussians per count row
 constexpr int kSelectThreads = 128;
 constexpr int kScanThreads = 512;                // scan4_kernel (4 tiles per lane)
 constexpr int kScan1Threads = 1024;              // scan_kernel (1 tile per lane, few views: more warps per tile column)
-constexpr int kPrefixChunks = 48;                // chunks binned exactly before saturation skipping
+#ifndef SARR_PREFIX_CHUNKS
+#define SARR_PREFIX_CHUNKS 48
+#endif
+constexpr int kPrefixChunks = SARR_PREFIX_CHUNKS;  // chunks binned exactly before saturation skipping
 constexpr int kXCap = kChunk;                    // exactly binned Gaussians listed per skipped chunk
 constexpr int kSegMaskMaxTiles = 2048;           // prefix-chunk segment masks up to this many tiles
 constexpr int kSegMaskAllMaxTiles = 512;         // segment masks of every chunk up to this many tiles
@@ -293,10 +296,8 @@ __device__ __forceinline__ void project_cov(const ViewConst& v, const float cw[6
 // covariance's condition number kappa, so std^2 <= (kappa+1)^2 / (4 kappa); a
 // 1% relative and 1.5 px absolute margin cover the float rounding of the
 // reference's own evaluation, which stays far below 1% for kappa <= 2.5e4.
-// The eigenvalues come from the
-// closed-form trigonometric solution of the symmetric 3x3 eigenproblem; a slack
-// closed-form trigonometric solution of the symmetric 3x3 eigenproblem; a slack
-// of 1e-5 * lambda_max on both extreme eigenvalues covers its float error.
+// The eigenvalues come from the closed-form trigonometric solution of the
+// symmetric 3x3 eigenproblem; a slack of 1e-5 * lambda_max on both extreme eigenvalues covers its float error.
 // +inf for covariances that are not clearly positive definite or have
 // kappa > 2.5e4.
 __device__ __forceinline__ float view_free_half_bound(const float cw[6]) {

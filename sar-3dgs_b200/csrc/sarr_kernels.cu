@@ -1385,6 +1385,52 @@ __device__ __forceinline__ void insertion_ranks(const float* z, int count, int* 
   for (int k = 0; k < count; ++k) rank_out[idx[k]] = k;
 }
 
+// Orderable 64-bit key of (Z_r, slot) for a Z_r that is not NaN: the
+// float's bits mapped to an unsigned order (-0 taken as +0: the reference's
+// comparisons treat them as equal), the slot in the low word; unused slots
+// get the largest key.
+__device__ __forceinline__ uint64_t zslot_key(float z, int slot, bool used) {
+  if (!used) return ~0ull;
+  const uint32_t u = __float_as_uint(z + 0.0f);
+  const uint32_t k = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  return ((uint64_t)k << 32) | (uint32_t)slot;
+}
+
+// Sorted positions of the keys of slots lane and lane + 32 (kN = 64) or of
+// slot lane (kN = 32), by a bitonic sorting network across the warp: the
+// element at position e = lane + 32 h is key[h]; e's partner in a
+// compare-exchange stage (k, j) is e ^ j, in lane ^ j for j < 32 and in the
+// same lane for j = 32. Each sorted position then writes its position into
+// s_rank[slot]. Keys are distinct (the slot is part of the key).
+template <int kN>
+__device__ __forceinline__ void warp_sort_ranks(uint64_t key0, uint64_t key1, int lane, int* s_rank) {
+  uint64_t key[2] = {key0, key1};
+#pragma unroll
+  for (int k = 2; k <= kN; k <<= 1) {
+#pragma unroll
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      if (j == 32) {
+        const uint64_t lo = key[0] < key[1] ? key[0] : key[1];
+        const uint64_t hi = key[0] < key[1] ? key[1] : key[0];
+        key[0] = lo;
+        key[1] = hi;
+      } else {
+#pragma unroll
+        for (int h = 0; h < kN / 32; ++h) {
+          const int e = lane + 32 * h;
+          const uint64_t other = __shfl_xor_sync(0xffffffffu, key[h], j);
+          const bool take_min = ((e & k) == 0) == ((lane & j) == 0);
+          const bool smaller = other < key[h];
+          key[h] = (take_min == smaller) ? other : key[h];
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int h = 0; h < kN / 32; ++h)
+    if (key[h] != ~0ull) s_rank[(uint32_t)key[h]] = lane + 32 * h;
+}
+
 // One warp per tile (kSelectThreads / 32 tiles per CTA), no CTA barrier.
 //  1. emit: every needed chunk's 1024 rectangles are loaded at once (eight
 //     16-byte loads per lane) and its hits are ranked in index order with a
@@ -1624,13 +1670,17 @@ __global__ void __launch_bounds__(kSelectThreads, 8) select_kernel(const SelectA
     rank[0] = s_rank[warp][lane];
     rank[1] = s_rank[warp][lane + 32];
   } else {
-    const float z0 = lane < count ? z[lane] : 0.0f;
-    const float z1 = lane + 32 < count ? z[lane + 32] : 0.0f;
-    for (int j = 0; j < count; ++j) {
-      const float zj = z[j];
-      rank[0] += (zj < z0) || (zj == z0 && j < lane);
-      rank[1] += (zj < z1) || (zj == z1 && j < lane + 32);
+    // no NaN: the position of each slot's (Z_r, slot) key in sorted order
+    int* sr = s_rank[warp];
+    const uint64_t k0 = zslot_key(rec[0].z, lane, lane < count);
+    if (count <= 32) {
+      warp_sort_ranks<32>(k0, ~0ull, lane, sr);
+    } else {
+      warp_sort_ranks<64>(k0, zslot_key(rec[1].z, lane + 32, lane + 32 < count), lane, sr);
     }
+    __syncwarp();
+    rank[0] = sr[lane];
+    rank[1] = sr[lane + 32];
   }
 
   // 4. state (the list length was written by scan_kernel)
@@ -1779,15 +1829,17 @@ __device__ __forceinline__ bool load_tile_recs(Rec* s_rec, uint64_t* bar, const 
 }
 
 // Exponent cutoff of one record for compositing: a pixel whose exponent
-// (rec_density's -q / (2 det)) is below it gets a density below 1e-8 and is
-// skipped by the compositing, so the pixel may skip it without evaluating
-// expf and the division. The cutoff is max(-20, ln(1e-8 norm) - 1e-3):
-// below -20 rec_density returns 0; below ln(1e-8 norm) - 1e-3 the exact
-// exp is below 0.999e-8 norm, and expf (at most 2 ulp from exp, the CUDA
-// math library's documented bound), the correctly rounded division by norm
-// and the error of logf and of the product 1e-8f * norm (both below 1e-6
-// relative) keep the computed density below 1e-8. A NaN from logf leaves the
-// cutoff at -20; an infinite norm gives +inf (density 0 or NaN -> 0 there).
+// (compute_gaussian_density_2d's -q / (2 det)) is below it has a density
+// below 1e-8, in the reference (expf within 2 ulp of exp, the CUDA math
+// library's documented bound, and a correctly rounded division by norm) and
+// in density_above_cutoff (within 2e-6 relative), and is skipped by the
+// compositing, so the pixel may skip it without evaluating the exponential.
+// The cutoff is max(-20, ln(1e-8 norm) - 1e-3): below -20 the reference's
+// density is 0; below ln(1e-8 norm) - 1e-3 the exact exp is below
+// 0.999e-8 norm, and the evaluation errors above and those of logf and of
+// the product 1e-8f * norm (both below 1e-6 relative) keep the computed
+// density below 1e-8. A NaN from logf leaves the cutoff at -20; an infinite
+// norm gives +inf (density 0 or NaN -> 0 there).
 __device__ __forceinline__ float density_cutoff(const Rec& g) {
   return fmaxf(-20.0f, logf(mul_(1e-8f, g.norm)) - 1e-3f);
 }
@@ -1811,26 +1863,51 @@ __device__ __forceinline__ float2 density_extent(const Rec& g, float cutoff) {
   return make_float2(sqrtf(k * cxx) + 0.01f, sqrtf(k * cyy) + 0.01f);
 }
 
-// rec_density (compute_gaussian_density_2d :215-234) of a record whose norm is
-// >= 0 at pixel (px, py), or 0 where the exponent is below the record's
-// cutoff (there the reference's density is below 1e-8, and every caller
-// treats such a density as no contribution). Records with norm < 0 have an
-// empty cutoff box and reach no caller.
-__device__ __forceinline__ float density_above_cutoff(const Rec& g, float cutoff, float px,
-                                                      float py) {
+// 2^x with PTX's ex2.approx (relative error below 2^-22 over the range used
+// here; subnormal results flushed to zero, which only affects densities far
+// below the 1e-8 cut-off).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// -log2(norm) of a record: compute_gaussian_density_2d's division by norm
+// becomes an addition to the base-2 exponent.
+__device__ __forceinline__ float density_log2_scale(const Rec& g) { return -log2f(g.norm); }
+
+// The exponent of compute_gaussian_density_2d (:215-234) at pixel (px, py),
+// evaluated with the reference's operations (so the cut-off boxes of
+// density_extent, derived for this evaluation, hold).
+__device__ __forceinline__ float density_exponent(const Rec& g, float px, float py) {
   const float dx = sub_(px, g.mx);
   const float dy = sub_(py, g.my);
   const float q = fma_(mul_(g.cxx, dy), dy,
                        fma_(mul_(g.cyy, dx), dx, -mul_(mul_(mul_(2.0f, g.cxy), dx), dy)));
-  const float exponent = mul_(mul_(-0.5f, q), g.inv_det);
+  return mul_(mul_(-0.5f, q), g.inv_det);
+}
+
+// compute_gaussian_density_2d of a record whose norm is >= 0 at pixel
+// (px, py): exp(exponent) / norm evaluated as 2^(exponent log2(e) -
+// log2(norm)) with one ex2.approx (`l2s` = density_log2_scale(g)); relative
+// error below 2e-6 against the correctly rounded value for exponents >= -20
+// (the fma's rounding of a product below 29 in magnitude, and ex2's own
+// error). 0 where the exponent is below the record's cutoff (there the
+// reference's density is below 1e-8, and every caller treats such a density
+// as no contribution) and where it is NaN (the reference's fmaxf(NaN, 0)).
+// Records with norm < 0 have an empty cutoff box and reach no caller.
+__device__ __forceinline__ float density_above_cutoff(const Rec& g, float cutoff, float l2s,
+                                                      float px, float py) {
+  const float exponent = density_exponent(g, px, py);
   if (exponent < cutoff) return 0.0f;
-  return fmaxf(div_(expf(exponent), g.norm), 0.0f);
+  return fmaxf(ex2_approx(__fmaf_rn(exponent, 1.4426950408889634f, l2s)), 0.0f);
 }
 
 // Marks, for the records of one tile (lanes hold records lane and lane + 32),
 // those whose cutoff box meets the pixel block [bx0, bx1] x [by0, by1]
-// (columns x rows), and stores every record's cutoff in cut[]. Warp-wide.
-__device__ __forceinline__ uint64_t block_hits(const Rec* recs, int count, float* cut, float bx0,
+// (columns x rows), and stores every record's cutoff and log2 scale in cut[].
+// Warp-wide.
+__device__ __forceinline__ uint64_t block_hits(const Rec* recs, int count, float2* cut, float bx0,
                                                float bx1, float by0, float by1, int lane) {
   uint64_t hit = 0;
   for (int h = 0; h < (count > 32 ? 2 : 1); ++h) {
@@ -1839,7 +1916,7 @@ __device__ __forceinline__ uint64_t block_hits(const Rec* recs, int count, float
     if (k < count) {
       const Rec& g = recs[k];
       const float cutoff = density_cutoff(g);
-      cut[k] = cutoff;
+      cut[k] = make_float2(cutoff, density_log2_scale(g));
       const float2 e = density_extent(g, cutoff);
       const float mdx = fmaxf(0.0f, fmaxf(bx0 - g.mx, g.mx - bx1));
       const float mdy = fmaxf(0.0f, fmaxf(by0 - g.my, g.my - by1));
@@ -1859,9 +1936,9 @@ __device__ __forceinline__ uint64_t block_hits(const Rec* recs, int count, float
 // compositing, so visiting only the marked records, in list order, leaves
 // each pixel's arithmetic the reference's, record by record.
 //
-__device__ __forceinline__ void composite_one(const Rec& g, float cutoff, float fx, float fy,
+__device__ __forceinline__ void composite_one(const Rec& g, float2 cut, float fx, float fy,
                                               float& value, float& trans, bool& done) {
-  const float gamma_ipp = density_above_cutoff(g, cutoff, fx, fy);
+  const float gamma_ipp = density_above_cutoff(g, cut.x, cut.y, fx, fy);
   if (gamma_ipp < 1e-8f) return;
   const float alpha_i = mul_(g.sigma, gamma_ipp);
   value = fma_(mul_(trans, alpha_i), g.s_pos, value);
@@ -1879,7 +1956,7 @@ template <int kPix>
 __global__ void __launch_bounds__(kPix == 2 ? 128 : 256) render_kernel(const TileArgs a) {
   constexpr int kWarps = kPix == 2 ? 4 : 8;
   __shared__ __align__(16) Rec s_rec[kCap];
-  __shared__ float s_cut[kWarps][kCap];
+  __shared__ float2 s_cut[kWarps][kCap];
   __shared__ uint64_t bar;
   const int v = blockIdx.y, t = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -1908,7 +1985,7 @@ __global__ void __launch_bounds__(kPix == 2 ? 128 : 256) render_kernel(const Til
       uint64_t hit[kPix];
 #pragma unroll
       for (int i = 0; i < kPix; ++i) hit[i] = 0;
-      float* cut = s_cut[warp];
+      float2* cut = s_cut[warp];
       const float by0 = (float)r0, by1 = (float)(r0 + 7);
       for (int h = 0; h < (count > 32 ? 2 : 1); ++h) {
         const int k = lane + 32 * h;
@@ -1918,7 +1995,7 @@ __global__ void __launch_bounds__(kPix == 2 ? 128 : 256) render_kernel(const Til
         if (k < count) {
           const Rec& g = s_rec[k];
           const float cutoff = density_cutoff(g);
-          cut[k] = cutoff;
+          cut[k] = make_float2(cutoff, density_log2_scale(g));
           const float2 e = density_extent(g, cutoff);
           const float mdy = fmaxf(0.0f, fmaxf(by0 - g.my, g.my - by1));
           if (!(mdy > e.y)) {
@@ -1943,7 +2020,7 @@ __global__ void __launch_bounds__(kPix == 2 ? 128 : 256) render_kernel(const Til
         const int k = __ffsll((long long)todo) - 1;
         todo &= todo - 1;
         const Rec& g = s_rec[k];
-        const float cutoff = cut[k];
+        const float2 cutoff = cut[k];
         bool all_done = true;
 #pragma unroll
         for (int i = 0; i < kPix; ++i) {
@@ -2080,7 +2157,7 @@ constexpr int kBwdPartRecs = kCap / kBwdParts;
 __global__ void __launch_bounds__(kWarpsPerTile * 32) bwd_tile_kernel(const TileArgs a) {
   __shared__ __align__(16) Rec s_rec[kCap];
   __shared__ float s_red[kWarpsPerTile][kBwdPartRecs][8];
-  __shared__ float s_cut[kWarpsPerTile][kCap];
+  __shared__ float2 s_cut[kWarpsPerTile][kCap];
   __shared__ uint64_t bar;
   const int v = blockIdx.y, t = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -2116,7 +2193,8 @@ __global__ void __launch_bounds__(kWarpsPerTile * 32) bwd_tile_kernel(const Tile
     before &= before - 1;
     const Rec& g = s_rec[k];
     if (in) {
-      const float gamma_ipp = density_above_cutoff(g, s_cut[warp][k], fx, fy);
+      const float2 cut = s_cut[warp][k];
+      const float gamma_ipp = density_above_cutoff(g, cut.x, cut.y, fx, fy);
       if (gamma_ipp >= 1e-8f) {
         prev_transmittance = mul_(prev_transmittance, fma_(-g.sigma, gamma_ipp, 1.0f));
         if (prev_transmittance < 1e-8f) prev_transmittance = 0.0f;
@@ -2131,7 +2209,8 @@ __global__ void __launch_bounds__(kWarpsPerTile * 32) bwd_tile_kernel(const Tile
     float A[7] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     bool contrib = false;
     if (in) {
-      const float gamma_ipp = density_above_cutoff(g, s_cut[warp][k], fx, fy);
+      const float2 cut = s_cut[warp][k];
+      const float gamma_ipp = density_above_cutoff(g, cut.x, cut.y, fx, fy);
       if (gamma_ipp >= 1e-8f) {
         contrib = true;
         const float sigma_i = g.sigma;
@@ -2156,8 +2235,8 @@ __global__ void __launch_bounds__(kWarpsPerTile * 32) bwd_tile_kernel(const Tile
                                fma_(mul_(cov_cc, dx), dx, -mul_(mul_(mul_(2.0f, cov_rc), dx), dy)));
           const float exponent = mul_(mul_(-0.5f, q), inv_det);
           if (exponent > -20.0f) {
-            const float exp_val = expf(exponent);
-            const float base_val = div_(exp_val, g.norm);
+            // exp(exponent) / norm, as in the density (one ex2.approx)
+            const float base_val = ex2_approx(__fmaf_rn(exponent, 1.4426950408889634f, cut.y));
             const float h = mul_(mul_(0.5f, base_val), inv_det);
             const float d_gamma_d_cov_rr = mul_(h, fma_(dy, dy, -mul_(mul_(cov_cc, inv_det), 0.5f)));
             const float d_gamma_d_cov_cc = mul_(h, fma_(dx, dx, -mul_(mul_(cov_rr, inv_det), 0.5f)));

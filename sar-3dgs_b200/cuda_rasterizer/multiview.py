@@ -82,6 +82,21 @@ def backward_views(means, cov, transmittance, sh, grad_images, views, group=None
     return gm, gc, gs, gsh, gn
 
 
+def bucket_bounds(total: int, buckets: int, align: int = 64):
+    """[a, b) ranges splitting `total` elements into at most `buckets`
+    consecutive buckets whose starts are multiples of `align` elements."""
+    if total <= 0:
+        return []
+    step = -(-total // max(1, buckets) // align) * align
+    return [(a, min(total, a + step)) for a in range(0, total, step)]
+
+
+def bucket_segments(segments, a: int, b: int):
+    """The per-segment learning rates [(end, lr), ...] of a flat buffer,
+    restricted to its bucket [a, b) with ends relative to a."""
+    return [(max(0, min(e, b) - a), lr) for e, lr in segments if e > a]
+
+
 class ViewParallelTrainer:
     """Data-parallel training step over radar views, one process per GPU.
 
@@ -112,20 +127,22 @@ class ViewParallelTrainer:
     (the covariance is detached, gaussian_model.py:306-315), so Adam leaves
     them alone as torch.optim.Adam does for parameters without gradients.
     Learning rates per group follow train.py:429-435 (lr for means and
-    opacity, lr / 100 for SH).
+    opacity, lr / 100 for SH). Every rank must call step() the same number of
+    times with the same number of views (the all-reduces are collective).
     """
 
     def __init__(self, means, scales_log, rotations, opacity_logits, sh, lr=1e-3, group=None,
                  buckets=4, l1_weight=1.0, ssim_weight=0.2, window_size=5, betas=(0.9, 0.999),
-                 eps=1e-8):
+                 eps=1e-8, distributed=True):
         from . import _native
         self._N = _native
         dev = means.device
         n, k = means.shape[0], sh.shape[1]
         self.n, self.k, self.device = n, k, dev
         self.group = group
-        self.world = (dist.get_world_size(group)
-                      if dist.is_available() and dist.is_initialized() else 1)
+        # distributed=False: a single-process trainer even inside a process group
+        self.world = (dist.get_world_size(group) if distributed and dist.is_available()
+                      and dist.is_initialized() else 1)
         total = n * (4 + k)
         self.param = torch.empty(total, dtype=torch.float32, device=dev)
         self.means = self.param[:3 * n].view(n, 3)
@@ -146,9 +163,7 @@ class ViewParallelTrainer:
         self.cov6 = torch.empty((n, 6), dtype=torch.float32, device=dev)
         self.sigma = torch.empty((n,), dtype=torch.float32, device=dev)
         self.segments = [(3 * n, lr), (4 * n, lr), (total, lr * 0.01)]
-        # bucket boundaries on 64-element (256-byte) multiples
-        step = -(-total // max(1, buckets) // 64) * 64
-        self.bounds = [(a, min(total, a + step)) for a in range(0, total, step)]
+        self.bounds = bucket_bounds(total, buckets)  # 256-byte aligned bucket starts
         self.loss_w = (l1_weight / self.world, ssim_weight / self.world, window_size)
         self.betas, self.eps = betas, eps
         self.steps_done = 0
@@ -224,7 +239,7 @@ class ViewParallelTrainer:
         for i, (a, b) in enumerate(self.bounds):
             if works:
                 works[i].wait()  # the current stream waits for this bucket's all-reduce
-            segs = [(max(0, min(e, b) - a), lr) for e, lr in self.segments if e > a]
+            segs = bucket_segments(self.segments, a, b)
             N.adam_step(self.param[a:b], self.grad[a:b], self.exp_avg[a:b], self.exp_avg_sq[a:b],
                         segs, self.steps_done, b1, b2, self.eps)
 

@@ -102,3 +102,23 @@ def hires_views(n_views=16, incidence=(15.0, 45.0), rho=0.1, samples=512, seed=2
     az = torch.rand(n_views, generator=g, dtype=torch.float64) * 360.0
     inc = torch.rand(n_views, generator=g, dtype=torch.float64) * (incidence[1] - incidence[0]) + incidence[0]
     return [view_tuple(float(az[k]), float(inc[k]), rho, samples) for k in range(n_views)]
+
+
+def make_param_scene(n, box=(40.0, 40.0, 10.0), scale_range=(0.05, 0.5), seed=0, device="cpu"):
+    """The same distributions as make_scene, in the trainable form of
+    GaussianModel (gaussian_model.py:112-132): means [n,3], log-scales [n,3],
+    unit quaternions (w, x, y, z) [n,4], opacity logits [n] (sigmoid gives
+    the transmittance) and SH [n,16]."""
+    g = torch.Generator().manual_seed(int(seed))
+    W, L, H = box
+    u = torch.rand(n, 3, generator=g, dtype=torch.float64)
+    means = torch.stack([(u[:, 0] - 0.5) * W, (u[:, 1] - 0.5) * L, u[:, 2] * H], dim=1)
+    lo, hi = math.log(scale_range[0]), math.log(scale_range[1])
+    scales = torch.rand(n, 3, generator=g, dtype=torch.float64) * (hi - lo) + lo
+    q = torch.randn(n, 4, generator=g, dtype=torch.float64)
+    q = q / q.norm(dim=1, keepdim=True)
+    logits = torch.randn(n, generator=g, dtype=torch.float64)
+    sh = torch.randn(n, 16, generator=g, dtype=torch.float64) * 0.1
+    sh[:, 0] += 0.5
+    return {k: v.float().to(device) for k, v in
+            (("means", means), ("scales", scales), ("rotations", q), ("logits", logits), ("sh", sh))}

@@ -12,7 +12,9 @@ import numpy as np
 import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+REF = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("SARR_REFERENCE_DIR")
+if not REF:
+    sys.exit("usage: pass the SAR-3DGS checkout as the first argument (or set SARR_REFERENCE_DIR)")
 sys.path.insert(0, REF)
 from losses import CombinedLoss  # noqa: E402
 

@@ -1,8 +1,10 @@
 """View data-parallel training step on 2 GPUs over NCCL: each rank renders and
 differentiates its shard of the views, the bucketed all-reduce sums the
 trainable gradients, and every rank ends with the gradients of one process's
-backward over all views (equal up to float summation order). Skipped with
-fewer than 2 visible GPUs."""
+backward over all views (equal up to float summation order). The training
+step (ViewParallelTrainer: bucketed all-reduce overlapped with Adam) leaves
+identical parameters on both ranks, equal to one process's training on all
+views. Skipped with fewer than 2 visible GPUs."""
 import datetime
 import os
 import socket
@@ -37,6 +39,7 @@ def _worker(rank, world, port, q):
     dist.init_process_group("nccl", rank=rank, world_size=world,
                             timeout=datetime.timedelta(seconds=60), device_id=dev)
     try:
+        from cuda_rasterizer import _native
         from cuda_rasterizer import cuda_rasterizer_sar as M
         from cuda_rasterizer import multiview
         from cuda_rasterizer import synthetic as S
@@ -55,7 +58,33 @@ def _worker(rank, world, port, q):
                                                             grad_norm=True)
         torch.cuda.synchronize()
         errs = [_rel(gm, fm), _rel(gs, fs), _rel(gsh, fsh), _rel(gn, fn)]
-        q.put((rank, same_images, errs))
+        # the training step: each rank trains on its shard. After one step the
+        # summed gradients equal those of one process training on all views
+        # (up to float summation order), and so do the Adam updates wherever
+        # the gradient is well above the rounding noise; after a second step
+        # the parameters are still identical on both ranks.
+        gp = torch.Generator().manual_seed(73)
+        scales = (torch.rand((60000, 3), generator=gp) * 2.3 - 3.0).to(dev)
+        rot = torch.randn((60000, 4), generator=gp).to(dev)
+        logits = torch.randn((60000,), generator=gp).to(dev)
+        vs = [_native.make_view(*v) for v in views]
+        tr = multiview.ViewParallelTrainer(sc["means"], scales, rot, logits, sc["sh"], buckets=3)
+        one = multiview.ViewParallelTrainer(sc["means"], scales, rot, logits, sc["sh"], buckets=3,
+                                            distributed=False)
+        p0 = one.param.clone()
+        targets = images.flip(0).contiguous()
+        tr.step(vs[a:b], targets[a:b])
+        one.step(vs, targets)
+        torch.cuda.synchronize()
+        errs.append(_rel(tr.grad, one.grad))
+        big = one.grad.abs() > 1e-3 * one.grad.abs().max()
+        errs.append(_rel((tr.param - p0)[big], (one.param - p0)[big]))
+        tr.step(vs[a:b], targets[a:b])
+        torch.cuda.synchronize()
+        other = tr.param.clone()
+        dist.broadcast(other, src=0)
+        same_params = bool(torch.equal(other, tr.param))
+        q.put((rank, same_images and same_params, errs))
     except Exception as e:  # reported to the parent
         q.put((rank, "error", repr(e)))
     finally:
@@ -77,4 +106,5 @@ def test_view_parallel_backward_two_gpus_nccl():
         p.join(timeout=60)
     for rank, same, errs in results:
         assert same is True, (rank, same, errs)
-        assert max(errs) <= 1e-5, (rank, errs)
+        assert max(errs[:5]) <= 1e-5, (rank, errs)
+        assert errs[5] <= 1e-4, (rank, errs)  # the first Adam update

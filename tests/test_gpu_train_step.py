@@ -1,0 +1,105 @@
+"""The native Adam step and the view-parallel training step on one GPU.
+
+sarr_adam_step is compared with torch.optim.Adam (parameter groups with their
+own learning rates, three steps); bucketed calls over sub-ranges must give the
+same bits as one call. ViewParallelTrainer's step is compared with the same
+step composed from the drop-in modules and torch.optim.Adam: producer,
+batched forward, CombinedLoss gradient, batched backward, sigmoid chain, Adam.
+"""
+import pytest
+import torch
+
+from cuda_rasterizer import _native
+from cuda_rasterizer import cuda_rasterizer_sar as M
+from cuda_rasterizer import multiview
+from cuda_rasterizer import synthetic as S
+
+from _helpers import rel_linf
+
+pytestmark = pytest.mark.gpu
+
+
+def test_adam_step_matches_torch_adam():
+    g = torch.Generator(device="cuda").manual_seed(81)
+    sizes = (3000, 1000, 16000)
+    lrs = (1e-3, 5e-3, 1e-5)
+    params = [torch.randn(s, device="cuda", generator=g) for s in sizes]
+    ref = [p.clone().requires_grad_(True) for p in params]
+    opt = torch.optim.Adam([{"params": [r], "lr": lr} for r, lr in zip(ref, lrs)])
+    flat = torch.cat(params)
+    m = torch.zeros_like(flat)
+    v = torch.zeros_like(flat)
+    ends = [sum(sizes[:i + 1]) for i in range(3)]
+    segs = list(zip(ends, lrs))
+    for step in range(1, 4):
+        grads = [torch.randn(s, device="cuda", generator=g) for s in sizes]
+        for r, gr in zip(ref, grads):
+            r.grad = gr.clone()
+        opt.step()
+        _native.adam_step(flat, torch.cat(grads), m, v, segs, step)
+    want = torch.cat([r.detach() for r in ref])
+    assert torch.allclose(flat, want, rtol=1e-6, atol=1e-7)
+    exp_avg = torch.cat([opt.state[r]["exp_avg"] for r in ref])
+    assert torch.allclose(m, exp_avg, rtol=1e-5, atol=1e-7)
+
+
+def test_adam_step_buckets_equal_one_call():
+    g = torch.Generator(device="cuda").manual_seed(82)
+    total = 10_003
+    p0 = torch.randn(total, device="cuda", generator=g)
+    grad = torch.randn(total, device="cuda", generator=g)
+    segs = [(4000, 1e-2), (total, 1e-4)]
+    a, ma, va = p0.clone(), torch.zeros(total, device="cuda"), torch.zeros(total, device="cuda")
+    _native.adam_step(a, grad, ma, va, segs, 1)
+    b, mb, vb = p0.clone(), torch.zeros(total, device="cuda"), torch.zeros(total, device="cuda")
+    for lo, hi in ((0, 2048), (2048, 6144), (6144, total)):
+        sub = [(max(0, min(e, hi) - lo), lr) for e, lr in segs if e > lo]
+        _native.adam_step(b[lo:hi], grad[lo:hi], mb[lo:hi], vb[lo:hi], sub, 1)
+    assert torch.equal(a, b) and torch.equal(ma, mb) and torch.equal(va, vb)
+
+
+def _scene_params(n, seed):
+    g = torch.Generator().manual_seed(seed)
+    means = (torch.rand((n, 3), generator=g) - 0.5) * torch.tensor([20.0, 20.0, 0.0]) \
+        + torch.tensor([0.0, 0.0, 3.0]) * torch.rand((n, 1), generator=g)
+    scales = torch.rand((n, 3), generator=g) * 2.3 - 3.0  # log-scales, 0.05-0.5 m
+    rot = torch.randn((n, 4), generator=g)
+    rot = rot / rot.norm(dim=1, keepdim=True)
+    logits = torch.randn((n,), generator=g)
+    sh = torch.randn((n, 16), generator=g) * 0.1
+    sh[:, 0] += 0.5
+    return [t.cuda() for t in (means, scales, rot, logits, sh)]
+
+
+def test_trainer_step_matches_composed_step():
+    n = 20000
+    means, scales, rot, logits, sh = _scene_params(n, 83)
+    views_t = S.training_views(8)
+    views = [_native.make_view(*v) for v in views_t]
+    tgt = S.named_scene("target_20k", seed=1, device="cuda")
+    targets = M.render_sar_batched(tgt["means"], tgt["cov6"], tgt["sigma"], tgt["sh"], views_t)
+    lr = 1e-3
+    tr = multiview.ViewParallelTrainer(means, scales, rot, logits, sh, lr=lr, buckets=3)
+
+    p_means = means.clone().requires_grad_(True)
+    p_logits = logits.clone().requires_grad_(True)
+    p_sh = sh.clone().requires_grad_(True)
+    opt = torch.optim.Adam([{"params": [p_means], "lr": lr}, {"params": [p_logits], "lr": lr},
+                            {"params": [p_sh], "lr": lr * 0.01}])
+    for _ in range(2):
+        losses = tr.step(views, targets)
+        cov6, sigma = _native.gaussian_params(scales, rot, p_logits.detach(), _native.SARR_COV6)
+        imgs = M.render_sar_batched(p_means.detach(), cov6, sigma, p_sh.detach(), views_t)
+        ref_losses, gimg = _native.combined_loss(imgs, targets, 1.0, 0.2, 5, "plain")
+        gm, _, gs, gsh = M.render_sar_backward_batched(p_means.detach(), cov6, sigma,
+                                                       p_sh.detach(), gimg, views_t)
+        p_means.grad = gm
+        p_logits.grad = gs * sigma * (1.0 - sigma)
+        p_sh.grad = gsh
+        opt.step()
+        assert torch.allclose(losses, ref_losses, rtol=1e-6, atol=0)
+    torch.cuda.synchronize()
+    for got, want in ((tr.means, p_means), (tr.logits, p_logits), (tr.sh, p_sh)):
+        assert rel_linf(got.cpu().numpy(), want.detach().cpu().numpy()) <= 1e-6
+    moved = (tr.means - means).abs().max().item()
+    assert moved > 1e-4  # the step moved the means (lr 1e-3)

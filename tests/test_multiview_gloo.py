@@ -87,3 +87,24 @@ def test_failing_rank_is_reported():
     # the surviving rank's collective ends with an error (peer gone or the
     # 20 s process-group timeout) instead of hanging
     assert res[0][1] == "error"
+
+
+def test_bucket_bounds_and_segments():
+    for total in (1, 63, 64, 65, 1000, 20 * 12345):
+        for buckets in (1, 3, 4, 8):
+            b = multiview.bucket_bounds(total, buckets)
+            assert len(b) <= buckets and b[0][0] == 0 and b[-1][1] == total
+            assert all(x[1] == y[0] for x, y in zip(b, b[1:]))
+            assert all(a % 64 == 0 for a, _ in b)
+    assert multiview.bucket_bounds(0, 4) == []
+    segs = [(300, 1.0), (400, 2.0), (2000, 3.0)]
+    assert multiview.bucket_segments(segs, 0, 256) == [(256, 1.0), (256, 2.0), (256, 3.0)]
+    assert multiview.bucket_segments(segs, 256, 512) == [(44, 1.0), (144, 2.0), (256, 3.0)]
+    assert multiview.bucket_segments(segs, 512, 2000) == [(1488, 3.0)]
+    # every element of every bucket gets the learning rate of its segment
+    total = 2000
+    for a, b in multiview.bucket_bounds(total, 3):
+        sub = multiview.bucket_segments(segs, a, b)
+        for i in range(a, b):
+            lr = next(l for e, l in sub if i - a < e)
+            assert lr == next(l for e, l in segs if i < e)
