@@ -30,7 +30,7 @@ constexpr int kSelectThreads = 128;
 constexpr int kScanThreads = 512;                // scan4_kernel (4 tiles per lane)
 constexpr int kScan1Threads = 1024;              // scan_kernel (1 tile per lane, few views: more warps per tile column)
 #ifndef SARR_PREFIX_CHUNKS
-#define SARR_PREFIX_CHUNKS 48
+#define SARR_PREFIX_CHUNKS 64
 #endif
 constexpr int kPrefixChunks = SARR_PREFIX_CHUNKS;  // chunks binned exactly before saturation skipping
 constexpr int kXCap = kChunk;                    // exactly binned Gaussians listed per skipped chunk

@@ -11,6 +11,10 @@
 
 namespace sarr {
 
+// The library's launch counter (sarr_launch_count), for launch steps that
+// issue more than one kernel.
+void count_launches(int k);
+
 __host__ __device__ inline size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
 // Image / tiling geometry of one call (all views of a call share it).

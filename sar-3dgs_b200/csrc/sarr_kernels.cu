@@ -36,6 +36,8 @@
 // tile with warp shuffles; bwd_scatter_kernel gathers them per Gaussian and
 // writes the dense gradient rows, applying the per-Gaussian chain rule once.
 // No float atomics: results are deterministic.
+#include <algorithm>
+
 #include "sarr_internal.h"
 
 namespace sarr {
@@ -401,7 +403,10 @@ __device__ __forceinline__ void flush_counts(uint32_t* cnt, uint8_t* out, int T,
 // plain read-modify-write is exact). No CTA barrier inside the view loop.
 // Means and transmittances are staged; covariances are read through L1.
 template <bool kShadow>
-__global__ void __launch_bounds__(kBinThreads, 4) bin_prefix_kernel(const BinArgs a) {
+#ifndef SARR_PREFIX_MIN_CTAS
+#define SARR_PREFIX_MIN_CTAS 4
+#endif
+__global__ void __launch_bounds__(kBinThreads, SARR_PREFIX_MIN_CTAS) bin_prefix_kernel(const BinArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   __shared__ uint64_t bar;
   constexpr int kWarps = kBinThreads / 32;
@@ -1936,19 +1941,6 @@ __device__ __forceinline__ uint64_t block_hits(const Rec* recs, int count, float
 // compositing, so visiting only the marked records, in list order, leaves
 // each pixel's arithmetic the reference's, record by record.
 //
-__device__ __forceinline__ void composite_one(const Rec& g, float2 cut, float fx, float fy,
-                                              float& value, float& trans, bool& done) {
-  const float gamma_ipp = density_above_cutoff(g, cut.x, cut.y, fx, fy);
-  if (gamma_ipp < 1e-8f) return;
-  const float alpha_i = mul_(g.sigma, gamma_ipp);
-  value = fma_(mul_(trans, alpha_i), g.s_pos, value);
-  trans = mul_(trans, fma_(-g.sigma, gamma_ipp, 1.0f));
-  if (trans < 1e-8f) {
-    trans = 0.0f;
-    done = true;
-  }
-}
-
 // kPix pixels per lane: 2 for launches of many views (4 warps per tile, fewer
 // per-record overheads), 1 for a few views (8 warps per tile, more warps in
 // flight when the grid is small).
@@ -2012,23 +2004,56 @@ __global__ void __launch_bounds__(kPix == 2 ? 128 : 256) render_kernel(const Til
           hit[i] |= (uint64_t)__ballot_sync(0xffffffffu, in[i]) << (32 * h);
       }
       __syncwarp();
-      uint64_t todo = hit[0];
-#pragma unroll
-      for (int i = 1; i < kPix; ++i) todo |= hit[i];
+      // Records in two passes of 32 (32-bit masks); per pixel, the marked
+      // records it still needs (a pixel whose transmittance ran out drops its
+      // mask). Each pixel visits its records in list order.
       const float fy = (float)pr;
-      while (todo) {
-        const int k = __ffsll((long long)todo) - 1;
-        todo &= todo - 1;
-        const Rec& g = s_rec[k];
-        const float2 cutoff = cut[k];
-        bool all_done = true;
+      const float4* recs4 = reinterpret_cast<const float4*>(s_rec);
+      for (int h = 0; h < (count > 32 ? 2 : 1); ++h) {
+        uint32_t m[kPix];
+        uint32_t todo = 0;
 #pragma unroll
         for (int i = 0; i < kPix; ++i) {
-          if (!done[i] && ((hit[i] >> k) & 1))
-            composite_one(g, cutoff, (float)(pc0 + 4 * i), fy, value[i], trans[i], done[i]);
-          all_done = all_done && done[i];
+          m[i] = done[i] ? 0u : (uint32_t)(hit[i] >> (32 * h));
+          todo |= m[i];
         }
-        if (all_done) break;
+        while (todo) {
+          const int kk = __ffs(todo) - 1;
+          const uint32_t bit = 1u << kk;
+          const int k = 32 * h + kk;
+          // mx my cxx cxy | cyy inv_det norm sigma | s_pos z yr pos
+          const float4 ra = recs4[3 * k], rb = recs4[3 * k + 1], rc = recs4[3 * k + 2];
+          const float2 c = cut[k];
+          // the row's part of compute_gaussian_density_2d's quadratic form,
+          // shared by the lane's pixels (same range row)
+          const float dy = sub_(fy, ra.y);
+          const float qy = mul_(ra.z, dy);     // cxx * dy
+          const float cxy2 = mul_(2.0f, ra.w);
+          todo = 0;
+#pragma unroll
+          for (int i = 0; i < kPix; ++i) {
+            if (m[i] & bit) {
+              const float dx = sub_((float)(pc0 + 4 * i), ra.x);
+              const float q = fma_(qy, dy, fma_(mul_(rb.x, dx), dx, -mul_(mul_(cxy2, dx), dy)));
+              const float exponent = mul_(mul_(-0.5f, q), rb.y);
+              float gamma_ipp = 0.0f;
+              if (!(exponent < c.x))
+                gamma_ipp = fmaxf(ex2_approx(__fmaf_rn(exponent, 1.4426950408889634f, c.y)), 0.0f);
+              if (gamma_ipp >= 1e-8f) {
+                const float sigma = rb.w;
+                const float alpha_i = mul_(sigma, gamma_ipp);
+                value[i] = fma_(mul_(trans[i], alpha_i), rc.x, value[i]);
+                trans[i] = mul_(trans[i], fma_(-sigma, gamma_ipp, 1.0f));
+                if (trans[i] < 1e-8f) {
+                  trans[i] = 0.0f;
+                  done[i] = true;
+                }
+              }
+              m[i] = done[i] ? 0u : (m[i] & ~bit);
+            }
+            todo |= m[i];
+          }
+        }
       }
     }
   }
@@ -2110,34 +2135,53 @@ __device__ __forceinline__ int list_find(const int* __restrict__ list, int cnt, 
   return -1;
 }
 
-// Host-side Omega average (:1239-1252) as a gather over the tiles whose shadow
-// list contains the Gaussian.
-__global__ void __launch_bounds__(256) omega_scatter_kernel(const OmegaScatterArgs a) {
-  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  const int v = blockIdx.y;
-  if (i >= a.n) return;
-  const ViewConst& vc = a.views[v];
-  const int tiles_x = vc.tiles_x;
-  const unsigned char* st = a.sh.base + v * a.sh.vstride;
-  const uint32_t rc = state_rect(st, a.sh.L, a.ipp.base + v * a.ipp.vstride, a.ipp.L, i);
-  float s = 0.0f, c = 0.0f;
-  const int tc0 = rc & 0xFF, tc1 = (rc >> 8) & 0xFF, tr0 = (rc >> 16) & 0xFF, tr1 = rc >> 24;
-  if (tc0 <= tc1) {
-    const int* cnts = reinterpret_cast<const int*>(st + a.sh.L.count);
-    const int* lists = reinterpret_cast<const int*>(st + a.sh.L.list);
-    const float2* partial = reinterpret_cast<const float2*>(a.partial + v * a.partial_vstride);
-    for (int ty = tr0; ty <= tr1; ++ty)
-      for (int tx = tc0; tx <= tc1; ++tx) {
-        const int t = ty * tiles_x + tx;
-        const int p = list_find(lists + (size_t)t * kCap, cnts[t], (int)i);
-        if (p >= 0) {
-          const float2 q = partial[(size_t)t * kCap + p];
-          s += q.x;
-          c += q.y;
-        }
-      }
+// Host-side Omega average (:1239-1252). Every Gaussian of a view starts at
+// 1.0 (the reference's value for a Gaussian no pixel reached); then one
+// thread per (tile, slot) entry of the view's shadow lists: the thread of the
+// Gaussian's first listing tile, in the row-major tile order of its shadow
+// rectangle, sums the (Omega, pixel count) partials of every tile that lists
+// it, in that order, and writes their quotient. Only listed Gaussians (at most
+// 64 per tile) do any work beyond the fill.
+__global__ void __launch_bounds__(256) omega_fill_kernel(float* __restrict__ omega, int64_t n,
+                                                         int nviews, size_t vstride) {
+  const int64_t total = n * nviews;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t v = e / n, i = e - v * n;
+    omega[v * vstride + i] = 1.0f;
   }
-  a.omega[v * a.omega_vstride + i] = c > 0.0f ? s / c : 1.0f;
+}
+
+__global__ void __launch_bounds__(256) omega_listed_kernel(const OmegaScatterArgs a) {
+  const int v = blockIdx.y;
+  const ViewConst& vc = a.views[v];
+  const int tiles_x = vc.tiles_x, T = tiles_x * vc.tiles_y;
+  const int e = blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= T * kCap) return;
+  const int t = e / kCap, slot = e - t * kCap;
+  const unsigned char* st = a.sh.base + v * a.sh.vstride;
+  const int* cnts = reinterpret_cast<const int*>(st + a.sh.L.count);
+  if (slot >= cnts[t]) return;
+  const int* lists = reinterpret_cast<const int*>(st + a.sh.L.list);
+  const int i = lists[(size_t)t * kCap + slot];
+  if (i < 0 || (int64_t)i >= a.n) return;
+  const uint32_t rc = state_rect(st, a.sh.L, a.ipp.base + v * a.ipp.vstride, a.ipp.L, i);
+  const int tc0 = rc & 0xFF, tc1 = (rc >> 8) & 0xFF, tr0 = (rc >> 16) & 0xFF, tr1 = rc >> 24;
+  const float2* partial = reinterpret_cast<const float2*>(a.partial + v * a.partial_vstride);
+  float sum = 0.0f, c = 0.0f;
+  bool first = true;
+  for (int ty = tr0; ty <= tr1; ++ty)
+    for (int tx = tc0; tx <= tc1; ++tx) {
+      const int u = ty * tiles_x + tx;
+      const int p = u == t ? slot : list_find(lists + (size_t)u * kCap, cnts[u], i);
+      if (p < 0) continue;
+      if (first && u != t) return;  // an earlier tile's thread writes this Gaussian
+      first = false;
+      const float2 q = partial[(size_t)u * kCap + p];
+      sum += q.x;
+      c += q.y;
+    }
+  a.omega[v * a.omega_vstride + i] = c > 0.0f ? sum / c : 1.0f;
 }
 
 // ---------------------------------------------------------------------------
@@ -2668,8 +2712,13 @@ cudaError_t launch_omega_tile(const TileArgs& a, const Dims& d, int nviews, cuda
 
 cudaError_t launch_omega_scatter(const OmegaScatterArgs& a, const Dims& d, int nviews,
                                  cudaStream_t s) {
-  const unsigned blocks = (unsigned)((d.n + 255) / 256);
-  omega_scatter_kernel<<<dim3(blocks, nviews), 256, 0, s>>>(a);
+  const int64_t total = d.n * nviews;
+  const unsigned fill_blocks = (unsigned)std::min<int64_t>((total + 255) / 256, 148 * 16);
+  omega_fill_kernel<<<fill_blocks, 256, 0, s>>>(a.omega, d.n, nviews, a.omega_vstride);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  count_launches(1);  // the second kernel of this launch step
+  omega_listed_kernel<<<dim3((d.T * kCap + 255) / 256, nviews), 256, 0, s>>>(a);
   return cudaGetLastError();
 }
 

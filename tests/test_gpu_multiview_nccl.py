@@ -44,7 +44,7 @@ def _worker(rank, world, port, q):
         from cuda_rasterizer import multiview
         from cuda_rasterizer import synthetic as S
         sc = {k: v.to(dev) for k, v in
-              S.make_scene(60000, (30.0, 30.0, 8.0), (0.05, 0.5), seed=71).items()}
+              S.make_scene(90000, (30.0, 30.0, 8.0), (0.05, 0.5), seed=71).items()}
         views = S.sweep_views(96)[::8]  # 12 views
         args = (sc["means"], sc["cov6"], sc["sigma"], sc["sh"])
         images = M.render_sar_batched(*args, views)
@@ -64,9 +64,10 @@ def _worker(rank, world, port, q):
         # the gradient is well above the rounding noise; after a second step
         # the parameters are still identical on both ranks.
         gp = torch.Generator().manual_seed(73)
-        scales = (torch.rand((60000, 3), generator=gp) * 2.3 - 3.0).to(dev)
-        rot = torch.randn((60000, 4), generator=gp).to(dev)
-        logits = torch.randn((60000,), generator=gp).to(dev)
+        n = sc["means"].shape[0]
+        scales = (torch.rand((n, 3), generator=gp) * 2.3 - 3.0).to(dev)
+        rot = torch.randn((n, 4), generator=gp).to(dev)
+        logits = torch.randn((n,), generator=gp).to(dev)
         vs = [_native.make_view(*v) for v in views]
         tr = multiview.ViewParallelTrainer(sc["means"], scales, rot, logits, sc["sh"], buckets=3)
         one = multiview.ViewParallelTrainer(sc["means"], scales, rot, logits, sc["sh"], buckets=3,

@@ -28,7 +28,7 @@ VIEWS = {
     "sweep": S.sweep_views(8)[5],
     "odd": S.view_tuple(47.0, 25.0, 0.25, 100)[:8] + (100, 72),
 }
-CASES = [("cpu_1k", "cpu"), ("cpu_1k", "odd"), (20000, "train"), (50000, "sweep")]
+CASES = [("cpu_1k", "cpu"), ("cpu_1k", "odd"), (20000, "train"), (50000, "sweep"), (90000, "sweep")]
 
 
 def _check_lists(sc, view):
@@ -208,7 +208,7 @@ def test_saturation_skip_is_exact():
     spread-out, strongly anisotropic and near-singular Gaussians around the
     saturation boundary must still give the oracle's lists bit for bit."""
     g = torch.Generator().manual_seed(21)
-    n1, n2 = 20000, 30000
+    n1, n2 = 30000, 60000  # past the exactly binned prefix (64 chunks of 1024)
     core = S.make_scene(n1, (6.0, 6.0, 2.0), (0.05, 0.3), seed=22)
     rest = S.make_scene(n2, (30.0, 30.0, 8.0), (0.05, 0.5), seed=23)
     # anisotropic tail: per-axis scales from 1e-3 to 2 m (condition numbers up to 4e6)
@@ -239,7 +239,7 @@ def test_saturation_skip_on_large_tile_grids(npx, rho):
     image-only forward (one list) takes the per-warp path and the debug lists
     (image and shadow list) the CTA-wide one; 1024 px (4096 tiles): CTA-wide
     for both. Lists bit-exact, images within tolerance."""
-    sc = {k: v.cuda() for k, v in S.make_scene(60000, (40.0, 40.0, 6.0), (0.05, 0.4), seed=31).items()}
+    sc = {k: v.cuda() for k, v in S.make_scene(90000, (40.0, 40.0, 6.0), (0.05, 0.4), seed=31).items()}
     view = S.view_tuple(33.0, 21.0, rho, npx)
     f, q, (cnt, lst, srt) = _check_lists(sc, view)
     assert cnt.max() == 64
