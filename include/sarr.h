@@ -50,6 +50,7 @@ typedef struct CUstream_st *sarr_stream_t;
 /* Forward/backward flags. */
 #define SARR_FLAG_OMEGA 1       /* workspace sizing: forward will compute Omega */
 #define SARR_FLAG_ACCUMULATE 2  /* backward: add into the gradient buffers instead of overwriting */
+#define SARR_FLAG_TILES_ONLY 4  /* backward: per-tile pass only; rows come from sarr_backward_scatter */
 
 /*
  * One radar view. Field meaning and units follow SARRenderParams /
@@ -276,6 +277,9 @@ int sarr_check_static_errors(sarr_stream_t stream);
  *   grad_norm    nullable; [n] = ||grad_means[i]||_2, the densification
  *                statistic of GaussianModel.densify_and_prune
  *                (gaussian_model.py:461-466).
+ *   flags        SARR_FLAG_ACCUMULATE; SARR_FLAG_TILES_ONLY (n_views <= 256):
+ *                only the per-tile pass runs, into ws, and the gradient
+ *                arrays are not touched (see sarr_backward_scatter).
  */
 int sarr_backward(const sarr_view *views, int n_views, int64_t n, const float *means,
                   const float *cov, int cov_layout, const float *sigma, const float *sh,
@@ -283,6 +287,26 @@ int sarr_backward(const sarr_view *views, int n_views, int64_t n, const float *m
                   float *grad_means, float *grad_cov, int grad_cov_layout, float *grad_sigma,
                   float *grad_sh, int grad_sh_cols, float *grad_norm, int flags, void *ws,
                   size_t ws_bytes, sarr_stream_t stream);
+
+/*
+ * The second half of a backward split in two (no reference counterpart; the
+ * reference's backward, rasterizer_impl_v2.cu:1380-1616, is one call): after
+ * sarr_backward(..., flags | SARR_FLAG_TILES_ONLY, ws) has run the per-tile
+ * pass of n_views <= 256 views into `ws` (which must then hold all of them in
+ * one launch group), this writes the dense gradient rows of the Gaussians
+ * [begin, end) only, with the same values (and bits) as the single call.
+ * Several calls over disjoint ranges produce the whole gradient, so a caller
+ * can start reducing one range over GPUs while the next one is written.
+ * Arguments: the views, n and states of the SARR_FLAG_TILES_ONLY call; the
+ * gradient arrays are the full [n, ...] arrays of sarr_backward (row i at row
+ * i); flags: SARR_FLAG_ACCUMULATE. The workspace must not be used by another
+ * call in between.
+ */
+int sarr_backward_scatter(const sarr_view *views, int n_views, int64_t n, const void *states,
+                          int64_t begin, int64_t end, float *grad_means, float *grad_cov,
+                          int grad_cov_layout, float *grad_sigma, float *grad_sh, int grad_sh_cols,
+                          float *grad_norm, int flags, void *ws, size_t ws_bytes,
+                          sarr_stream_t stream);
 
 /*
  * Test hook: the per-Gaussian intermediate arrays of preprocess_kernel and

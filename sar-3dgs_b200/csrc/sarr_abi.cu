@@ -606,10 +606,12 @@ int sarr_backward(const sarr_view* views, int n_views, int64_t n, const float* m
   if (npix > 0 && !grad_images) return SARR_ERR_ARG;
   if (states && !aligned(states, 256)) return SARR_ERR_WORKSPACE;
   const bool acc = (flags & SARR_FLAG_ACCUMULATE) != 0;
+  const bool tiles_only = (flags & SARR_FLAG_TILES_ONLY) != 0;
+  if (tiles_only && n_views > kMaxViewsPerLaunch) return SARR_ERR_ARG;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (n == 0) return SARR_OK;
   if (d.T == 0) {
-    if (acc) return SARR_OK;
+    if (acc || tiles_only) return SARR_OK;
     cudaError_t e = cudaMemsetAsync(grad_means, 0, (size_t)n * 3 * 4, s);
     if (e == cudaSuccess) e = cudaMemsetAsync(grad_cov, 0, (size_t)n * grad_cov_layout * 4, s);
     if (e == cudaSuccess) e = cudaMemsetAsync(grad_sigma, 0, (size_t)n * 4, s);
@@ -621,6 +623,7 @@ int sarr_backward(const sarr_view* views, int n_views, int64_t n, const float* m
   Ws w;
   st = carve_ws(d, ws, ws_bytes, n_views, w);
   if (st) return st;
+  if (tiles_only && w.group < n_views) return SARR_ERR_WORKSPACE;  // one launch group
   const size_t state_bytes = w.L.st.bytes;
   if (!states && run_cell_prep(d, w, means, cov, cov_layout, sigma, s) != cudaSuccess)
     return SARR_ERR_CUDA;
@@ -651,8 +654,12 @@ int sarr_backward(const sarr_view* views, int n_views, int64_t n, const float* m
     tb.partial = reinterpret_cast<float*>(w.view_area() + w.L.partial_bwd);
     tb.partial_vstride = w.L.per_view / sizeof(float);
     tb.err = w.err;
+    tb.listed = reinterpret_cast<uint32_t*>(w.view_area() + w.L.listed);
+    tb.listed_vstride = w.L.per_view / sizeof(uint32_t);
+    tb.n = d.n;
     e = run_kernel(kKindBwdTile, s, [&] { return launch_bwd_tile(tb, d, gv, s); });
     if (e != cudaSuccess) return SARR_ERR_CUDA;
+    if (tiles_only) break;  // sarr_backward_scatter writes the rows
 
     BwdScatterArgs bs;
     bs.views = w.views;
@@ -669,10 +676,78 @@ int sarr_backward(const sarr_view* views, int n_views, int64_t n, const float* m
     bs.grad_sh_cols = grad_sh_cols;
     bs.grad_norm = grad_norm;
     bs.accumulate = (acc || g0 > 0) ? 1 : 0;
+    bs.listed = tb.listed;
+    bs.listed_vstride = tb.listed_vstride;
+    bs.begin = 0;
+    bs.end = d.n;
     e = run_kernel(kKindBwdScatter, s, [&] { return launch_bwd_scatter(bs, d, s); });
     if (e != cudaSuccess) return SARR_ERR_CUDA;
   }
   return SARR_OK;
+}
+
+int sarr_backward_scatter(const sarr_view* views, int n_views, int64_t n, const void* states,
+                          int64_t begin, int64_t end, float* grad_means, float* grad_cov,
+                          int grad_cov_layout, float* grad_sigma, float* grad_sh, int grad_sh_cols,
+                          float* grad_norm, int flags, void* ws, size_t ws_bytes,
+                          sarr_stream_t stream) {
+  Dims d;
+  int st = make_dims(views, n_views, n, d);
+  if (st) return st;
+  if (n_views > kMaxViewsPerLaunch) return SARR_ERR_ARG;
+  if (begin < 0 || end < begin || end > n) return SARR_ERR_ARG;
+  if (grad_cov_layout != SARR_COV6 && grad_cov_layout != SARR_COV33) return SARR_ERR_ARG;
+  if (grad_sh_cols < 1 || grad_sh_cols > kSh) return SARR_ERR_ARG;
+  if (end > begin && (!grad_means || !grad_cov || !grad_sigma || !grad_sh)) return SARR_ERR_ARG;
+  if (states && !aligned(states, 256)) return SARR_ERR_WORKSPACE;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (end == begin) return SARR_OK;
+  const bool acc = (flags & SARR_FLAG_ACCUMULATE) != 0;
+  if (d.T == 0) {
+    if (acc) return SARR_OK;
+    const int64_t m = end - begin;
+    cudaError_t e = cudaMemsetAsync(grad_means + 3 * begin, 0, (size_t)m * 3 * 4, s);
+    if (e == cudaSuccess)
+      e = cudaMemsetAsync(grad_cov + grad_cov_layout * begin, 0, (size_t)m * grad_cov_layout * 4, s);
+    if (e == cudaSuccess) e = cudaMemsetAsync(grad_sigma + begin, 0, (size_t)m * 4, s);
+    if (e == cudaSuccess)
+      e = cudaMemsetAsync(grad_sh + (size_t)grad_sh_cols * begin, 0, (size_t)m * grad_sh_cols * 4, s);
+    if (e == cudaSuccess && grad_norm) e = cudaMemsetAsync(grad_norm + begin, 0, (size_t)m * 4, s);
+    return cuda_status(e);
+  }
+  Ws w;
+  st = carve_ws(d, ws, ws_bytes, n_views, w);
+  if (st) return st;
+  if (w.group < n_views) return SARR_ERR_WORKSPACE;
+  StateRef ipp;
+  if (states) {
+    ipp.base = const_cast<unsigned char*>(static_cast<const unsigned char*>(states));
+    ipp.vstride = w.L.st.bytes;
+  } else {
+    ipp.base = w.view_area() + w.L.state_ipp;
+    ipp.vstride = w.L.per_view;
+  }
+  ipp.L = w.L.st;
+  BwdScatterArgs bs;
+  bs.views = w.views;
+  bs.nviews = n_views;
+  bs.n = d.n;
+  bs.ipp = ipp;
+  bs.partial = reinterpret_cast<float*>(w.view_area() + w.L.partial_bwd);
+  bs.partial_vstride = w.L.per_view / sizeof(float);
+  bs.grad_means = grad_means;
+  bs.grad_cov = grad_cov;
+  bs.grad_cov_layout = grad_cov_layout;
+  bs.grad_sigma = grad_sigma;
+  bs.grad_sh = grad_sh;
+  bs.grad_sh_cols = grad_sh_cols;
+  bs.grad_norm = grad_norm;
+  bs.accumulate = acc ? 1 : 0;
+  bs.listed = reinterpret_cast<const uint32_t*>(w.view_area() + w.L.listed);
+  bs.listed_vstride = w.L.per_view / sizeof(uint32_t);
+  bs.begin = begin;
+  bs.end = end;
+  return cuda_status(run_kernel(kKindBwdScatter, s, [&] { return launch_bwd_scatter(bs, d, s); }));
 }
 
 int sarr_debug_preprocess(const sarr_view* view, int64_t n, const float* means, const float* cov,

@@ -87,7 +87,9 @@ __device__ __forceinline__ uint32_t state_rect(const unsigned char* st, const St
 //   tile's list, from scan_kernel), open_ipp / open_sh [tiles_y+1][tiles_x+1]
 //   i32 (summed-area tables of the tiles still open after the saturation
 //   prefix, from open_table_kernel), state_ipp (used when the caller gives no
-//   state), state_sh, partial_om [T][64] float2, partial_bwd [T][64][8] float.
+//   state), state_sh, partial_om [T][64] float2, partial_bwd [T][64][8] float,
+//   listed [ceil(n/32)] u32 (Gaussians in one of the view's tile lists, for
+//   the backward's per-Gaussian gather).
 // With cells (multi-view calls, see kCellMinViews) the head also holds the
 // SceneGrid, per-Gaussian bbox bounds hb [n] f32 and cell ids cid [n] u32, the
 // per-cell largest bound cell_hb [kMaxCells] (ordered-int keys), the cells'
@@ -100,7 +102,7 @@ struct WsLayout {
       always, head;
   size_t counts_ipp, counts_sh, need_ipp, need_sh, need_n_ipp, need_n_sh, open_ipp, open_sh;
   size_t bits, xcount, xlist, segmask_ipp, segmask_sh, state_ipp, state_sh, partial_om, partial_bwd,
-      per_view;
+      listed, per_view;
   bool cells;
   StateLayout st;
 };
@@ -188,6 +190,8 @@ __host__ inline WsLayout ws_layout(const Dims& d, bool cells) {
   o += align256((size_t)d.T * kCap * 8);
   L.partial_bwd = o;
   o += align256((size_t)d.T * kCap * 8 * 4);
+  L.listed = o;
+  o += align256((size_t)(d.n + 31) / 32 * 4);
   L.per_view = o;
   return L;
 }
@@ -329,6 +333,11 @@ struct TileArgs {
   float* partial;  // omega: float2 [T][64]; backward: float [T][64][8]
   size_t partial_vstride;
   int* err;
+  // backward: bit i of view v's words is set when Gaussian i is in one of the
+  // view's tile lists (null: not recorded)
+  uint32_t* listed;
+  size_t listed_vstride;  // words per view
+  int64_t n;
 };
 
 struct OmegaScatterArgs {
@@ -357,6 +366,9 @@ struct BwdScatterArgs {
   int grad_sh_cols;
   float* grad_norm;
   int accumulate;
+  const uint32_t* listed;  // per-view listed-Gaussian bitmaps of bwd_tile_kernel
+  size_t listed_vstride;   // words per view
+  int64_t begin, end;      // the gradient rows written: Gaussians [begin, end)
 };
 
 struct DebugPreArgs {

@@ -2212,6 +2212,12 @@ __global__ void __launch_bounds__(kWarpsPerTile * 32) bwd_tile_kernel(const Tile
   const int count_all = reinterpret_cast<const int*>(st + a.st.L.count)[t];
   const int k_lo = blockIdx.z * kBwdPartRecs;
   if (k_lo >= count_all) return;
+  if (blockIdx.z == 0 && a.listed && tid < count_all) {
+    // the tile's listed Gaussians, for bwd_scatter_kernel's gather
+    const int id = reinterpret_cast<const int*>(st + a.st.L.list)[(size_t)t * kCap + tid];
+    if (id >= 0 && (int64_t)id < a.n)
+      atomicOr(a.listed + v * a.listed_vstride + (id >> 5), 1u << (id & 31));
+  }
   const int count = min(count_all, k_lo + kBwdPartRecs);  // records [0, count) are read
   const bool ok = load_tile_recs(s_rec, &bar, st, a.st.L, t, count, a.err, true);
   if (!__syncthreads_and(ok)) return;
@@ -2319,15 +2325,44 @@ __global__ void __launch_bounds__(kWarpsPerTile * 32) bwd_tile_kernel(const Tile
 
 // Dense gradient rows. The per-Gaussian chain of backward_kernel (:979-1013)
 // is linear in (grad_ipp_r, grad_ipp_c), so it is applied once to the tile sums.
+// 32 x 32 bit-matrix transpose across a warp: on return, bit j of lane l's
+// word is bit l of lane j's word on entry (five butterfly exchange stages).
+__device__ __forceinline__ uint32_t warp_transpose32(uint32_t x, int lane) {
+  const uint32_t masks[5] = {0x0000FFFFu, 0x00FF00FFu, 0x0F0F0F0Fu, 0x33333333u, 0x55555555u};
+#pragma unroll
+  for (int s = 0; s < 5; ++s) {
+    const int j = 16 >> s;
+    const uint32_t y = __shfl_xor_sync(0xffffffffu, x, j);
+    x = (lane & j) ? ((x & ~masks[s]) | ((y >> j) & masks[s])) : ((x & masks[s]) | ((y << j) & ~masks[s]));
+  }
+  return x;
+}
+
+// Dense gradient rows of the Gaussians [begin, end). A warp holds 32
+// consecutive Gaussians (one 32-bit word of the listed bitmaps); per block of
+// 32 views its lanes load the views' words and transpose them, so that each
+// lane visits, in view order, only the views whose tile lists hold its
+// Gaussian (about 16k of 1M Gaussians per 256 x 256 view) instead of
+// testing every view.
 __global__ void __launch_bounds__(256) bwd_scatter_kernel(const BwdScatterArgs a) {
-  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= a.n) return;
+  const int64_t i = (a.begin & ~(int64_t)31) + (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int lane = threadIdx.x & 31;
+  const bool active = i >= a.begin && i < a.end && i < a.n;
+  const int64_t w = i >> 5;  // the same for the whole warp
+  const int64_t words = (a.n + 31) >> 5;
   float g_sigma = 0.f, g_rr = 0.f, g_cc = 0.f, g_rc = 0.f, gx = 0.f, gy = 0.f, gz = 0.f;
   float g_sh[kSh];
 #pragma unroll
   for (int k = 0; k < kSh; ++k) g_sh[k] = 0.f;
 
-  for (int v = 0; v < a.nviews; ++v) {
+  for (int vb = 0; vb < a.nviews; vb += 32) {
+    const int vl = vb + lane;
+    uint32_t word = (vl < a.nviews && w < words) ? a.listed[vl * a.listed_vstride + w] : 0u;
+    uint32_t vmask = warp_transpose32(word, lane);
+    if (!active) vmask = 0u;
+  while (vmask) {
+    const int v = vb + __ffs(vmask) - 1;
+    vmask &= vmask - 1;
     const ViewConst& vc = a.views[v];
     const int tiles_x = vc.tiles_x;
     const unsigned char* st = a.ipp.base + v * a.ipp.vstride;
@@ -2378,6 +2413,8 @@ __global__ void __launch_bounds__(256) bwd_scatter_kernel(const BwdScatterArgs a
     gy += grad_xr * d_xr_d_yw + grad_yr * d_yr_d_yw + grad_zr * d_zr_d_yw;
     gz += grad_xr * d_xr_d_zw + grad_yr * d_yr_d_zw + grad_zr * d_zr_d_zw;
   }
+  }
+  if (!active) return;
 
   float* gm = a.grad_means + i * 3;
   if (a.accumulate) {
@@ -2722,13 +2759,32 @@ cudaError_t launch_omega_scatter(const OmegaScatterArgs& a, const Dims& d, int n
   return cudaGetLastError();
 }
 
+__global__ void __launch_bounds__(256) zero_words_kernel(uint32_t* __restrict__ base, size_t vstride,
+                                                         int64_t words) {
+  uint32_t* p = base + blockIdx.y * vstride;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < words;
+       e += (int64_t)gridDim.x * blockDim.x)
+    p[e] = 0u;
+}
+
 cudaError_t launch_bwd_tile(const TileArgs& a, const Dims& d, int nviews, cudaStream_t s) {
+  if (a.listed) {
+    const int64_t words = (d.n + 31) / 32;
+    const unsigned blocks = (unsigned)std::min<int64_t>((words + 255) / 256, 64);
+    zero_words_kernel<<<dim3(blocks, nviews), 256, 0, s>>>(a.listed, a.listed_vstride, words);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    count_launches(1);  // the second kernel of this launch step
+  }
   bwd_tile_kernel<<<dim3(d.T, nviews, kBwdParts), kWarpsPerTile * 32, 0, s>>>(a);
   return cudaGetLastError();
 }
 
 cudaError_t launch_bwd_scatter(const BwdScatterArgs& a, const Dims& d, cudaStream_t s) {
-  const unsigned blocks = (unsigned)((d.n + 255) / 256);
+  (void)d;
+  if (a.end <= a.begin) return cudaSuccess;
+  const int64_t span = a.end - (a.begin & ~(int64_t)31);
+  const unsigned blocks = (unsigned)((span + 255) / 256);
   bwd_scatter_kernel<<<blocks, 256, 0, s>>>(a);
   return cudaGetLastError();
 }

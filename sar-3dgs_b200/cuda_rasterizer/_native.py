@@ -19,6 +19,7 @@ SARR_COV6 = 6
 SARR_COV33 = 9
 SARR_FLAG_OMEGA = 1
 SARR_FLAG_ACCUMULATE = 2
+SARR_FLAG_TILES_ONLY = 4
 SARR_L1_MODES = {"plain": 0, "linear": 1, "square": 2, "sqrt": 3}
 MAX_SH = 16
 
@@ -60,6 +61,7 @@ def _declare(L):
     L.sarr_forward.argtypes = [VP, I, I64, P, P, I, P, P, I, I, P, P, P, P, SZ, P]
     L.sarr_backward.argtypes = [VP, I, I64, P, P, I, P, P, I, I, P, P, P, P, I, P, P, I, P, I, P,
                                 SZ, P]
+    L.sarr_backward_scatter.argtypes = [VP, I, I64, P, I64, I64, P, P, I, P, P, I, P, I, P, SZ, P]
     L.sarr_debug_preprocess.argtypes = [VP, I64, P, P, I, P, P, I, I, P, P, P]
     L.sarr_debug_tile_lists.argtypes = [VP, I64, P, P, I, P, P, P, P, P, P, P, P, SZ, P]
     L.sarr_check_device_errors.argtypes = [P, SZ, P]
@@ -85,6 +87,7 @@ def _declare(L):
     L.sarr_densify_flags.argtypes = [I64, P, P, P, F, F, F, F, P, P, SZ, P]
     L.sarr_densify_apply.argtypes = [I64, P, P, P, P, P, I, P, P, I, I, P, P, P, P, P, P, SZ, P]
     for name in ("sarr_workspace_size", "sarr_state_size", "sarr_forward", "sarr_backward",
+                 "sarr_backward_scatter",
                  "sarr_debug_preprocess", "sarr_debug_tile_lists", "sarr_check_device_errors",
                  "sarr_debug_tile_rect", "sarr_gaussian_params", "sarr_loss_workspace_size",
                  "sarr_combined_loss", "sarr_adam_step", "sarr_densify_workspace_size", "sarr_densify_flags",
@@ -229,8 +232,9 @@ def forward(views, means, cov, layout, sigma, sh, sh_stride, sh_k, images, omega
 
 def backward(views, means, cov, layout, sigma, sh, sh_stride, sh_k, grad_images, grad_means,
              grad_cov, grad_cov_layout, grad_sigma, grad_sh, grad_norm=None, states=None,
-             accumulate=False, ws=None, check_device=False):
-    """sarr_backward on the current stream of the inputs' device."""
+             accumulate=False, ws=None, check_device=False, tiles_only=False):
+    """sarr_backward on the current stream of the inputs' device (tiles_only:
+    the per-tile pass only, rows then written by backward_scatter)."""
     n = means.shape[0]
     nv = len(views)
     nr, na = views[0].range_samples, views[0].azimuth_samples
@@ -243,10 +247,25 @@ def backward(views, means, cov, layout, sigma, sh, sh_stride, sh_k, grad_images,
             _views_array(views), nv, n, _ptr(means), _ptr(cov), layout, _ptr(sigma), _ptr(sh),
             sh_stride, sh_k, _ptr(grad_images), _ptr(states), _ptr(grad_means), _ptr(grad_cov),
             grad_cov_layout, _ptr(grad_sigma), _ptr(grad_sh), grad_sh.shape[1] if grad_sh.dim() == 2 else 16,
-            _ptr(grad_norm), SARR_FLAG_ACCUMULATE if accumulate else 0, _ptr(ws), ws.numel(), st)
+            _ptr(grad_norm), (SARR_FLAG_ACCUMULATE if accumulate else 0) |
+            (SARR_FLAG_TILES_ONLY if tiles_only else 0), _ptr(ws), ws.numel(), st)
         _check(status, "sarr_backward")
         if check_device:
             _check(lib().sarr_check_device_errors(_ptr(ws), ws.numel(), st), "sarr_backward (device)")
+
+
+def backward_scatter(views, n, begin, end, grad_means, grad_cov, grad_cov_layout, grad_sigma,
+                     grad_sh, ws, states=None, grad_norm=None, accumulate=False):
+    """sarr_backward_scatter: gradient rows [begin, end) after a tiles_only
+    backward of the same views on `ws`."""
+    dev = grad_means.device
+    with torch.cuda.device(dev):
+        _check(lib().sarr_backward_scatter(
+            _views_array(views), len(views), n, _ptr(states), int(begin), int(end), _ptr(grad_means),
+            _ptr(grad_cov), grad_cov_layout, _ptr(grad_sigma), _ptr(grad_sh),
+            grad_sh.shape[1] if grad_sh.dim() == 2 else 16, _ptr(grad_norm),
+            SARR_FLAG_ACCUMULATE if accumulate else 0, _ptr(ws), ws.numel(), _stream(dev)),
+            "sarr_backward_scatter")
 
 
 def debug_preprocess(view, means, cov, layout, sigma, sh, sh_stride, sh_k):

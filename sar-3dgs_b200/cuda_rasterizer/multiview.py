@@ -91,10 +91,11 @@ def bucket_bounds(total: int, buckets: int, align: int = 64):
     return [(a, min(total, a + step)) for a in range(0, total, step)]
 
 
-def bucket_segments(segments, a: int, b: int):
-    """The per-segment learning rates [(end, lr), ...] of a flat buffer,
-    restricted to its bucket [a, b) with ends relative to a."""
-    return [(max(0, min(e, b) - a), lr) for e, lr in segments if e > a]
+def flat_segments(n: int, k: int, g0: int, g1: int):
+    """The parts of Gaussians [g0, g1) in a flat buffer laid out as
+    means [n,3] | opacity logits [n] | SH [n,k]: [(start, stop, group)] with
+    group 0 = means, 1 = logits, 2 = SH."""
+    return [(3 * g0, 3 * g1, 0), (3 * n + g0, 3 * n + g1, 1), (4 * n + k * g0, 4 * n + k * g1, 2)]
 
 
 class ViewParallelTrainer:
@@ -112,13 +113,15 @@ class ViewParallelTrainer:
       3. CombinedLoss (L1 + D-SSIM) against the targets and its image gradient
          (sarr_combined_loss), weighted by 1 / world so that the summed
          gradients are those of the mean loss over all ranks' views;
-      4. backward of the views reusing the states, written straight into a
-         flat gradient buffer (sarr_backward); the transmittance gradient
-         is chained through the sigmoid;
-      5. the flat gradient buffer summed over the ranks in `buckets` NCCL
-         all-reduces issued back to back (async), each bucket's Adam update
-         (sarr_adam_step) queued behind its own all-reduce, so that the
-         update of bucket b overlaps the all-reduce of bucket b + 1.
+      4. backward of the views reusing the states: the per-tile pass
+         (sarr_backward with SARR_FLAG_TILES_ONLY), then, bucket by bucket
+         of `buckets` Gaussian ranges, the dense gradient rows of the range
+         written straight into a flat gradient buffer
+         (sarr_backward_scatter), the transmittance gradient chained through
+         the sigmoid, and the range's NCCL all-reduces issued (async), so
+         that the all-reduce of bucket b overlaps the rows of bucket b + 1;
+      5. each bucket's Adam update (sarr_adam_step) queued behind its own
+         all-reduce.
 
     Trainable parameters (the ones that receive gradients in SAR-3DGS: means,
     opacity logits, SH) live in one flat fp32 buffer laid out as
@@ -162,8 +165,9 @@ class ViewParallelTrainer:
         self.g_cov = torch.empty((n, 6), dtype=torch.float32, device=dev)  # reaches no parameter
         self.cov6 = torch.empty((n, 6), dtype=torch.float32, device=dev)
         self.sigma = torch.empty((n,), dtype=torch.float32, device=dev)
-        self.segments = [(3 * n, lr), (4 * n, lr), (total, lr * 0.01)]
-        self.bounds = bucket_bounds(total, buckets)  # 256-byte aligned bucket starts
+        self.group_lr = (lr, lr, lr * 0.01)  # means, opacity, SH (train.py:429-435)
+        # Gaussian ranges of the buckets (starts on 256-Gaussian multiples)
+        self.bounds = bucket_bounds(n, buckets, align=256)
         self.loss_w = (l1_weight / self.world, ssim_weight / self.world, window_size)
         self.betas, self.eps = betas, eps
         self.steps_done = 0
@@ -218,36 +222,43 @@ class ViewParallelTrainer:
             N._check(N.lib().sarr_backward(vs, V, n, P(self.means), P(self.cov6), N.SARR_COV6,
                                            P(self.sigma), P(self.sh), k, k, P(self.grad_images),
                                            P(self.states), P(self.g_means), P(self.g_cov),
-                                           N.SARR_COV6, P(self.g_logits), P(self.g_sh), k, None, 0,
-                                           P(self.ws), self.ws.numel(), st), "sarr_backward")
-        # d sigmoid(logit) / d logit = sigma (1 - sigma); the same on every rank,
-        # so it may be applied before the sum over ranks
-        self.g_logits.mul_(self.sigma * (1.0 - self.sigma))
+                                           N.SARR_COV6, P(self.g_logits), P(self.g_sh), k, None,
+                                           N.SARR_FLAG_TILES_ONLY, P(self.ws), self.ws.numel(), st),
+                     "sarr_backward")
+            # d sigmoid(logit) / d logit = sigma (1 - sigma); the same on every
+            # rank, so it may be applied before the sum over ranks
+            dsig = self.sigma * (1.0 - self.sigma)
+            works = []
+            for g0, g1 in self.bounds:
+                N.backward_scatter(views, n, g0, g1, self.g_means, self.g_cov, N.SARR_COV6,
+                                   self.g_logits, self.g_sh, self.ws, states=self.states)
+                self.g_logits[g0:g1].mul_(dsig[g0:g1])
+                works.append(self._allreduce_bucket(g0, g1))
         self.steps_done += 1
-        self._reduce_and_update()
+        self._update(works)
         return self.losses
 
-    def _reduce_and_update(self):
-        """Bucketed all-reduce of the flat gradients with each bucket's Adam
-        update queued behind its all-reduce."""
+    def _allreduce_bucket(self, g0, g1):
+        if self.world == 1:
+            return []
+        return [dist.all_reduce(self.grad[a:b], group=self.group, async_op=True)
+                for a, b, _ in flat_segments(self.n, self.k, g0, g1)]
+
+    def _update(self, works):
+        """Each bucket's Adam update, queued behind its all-reduces."""
         N = self._N
-        works = []
-        if self.world > 1:
-            for a, b in self.bounds:
-                works.append(dist.all_reduce(self.grad[a:b], group=self.group, async_op=True))
         b1, b2 = self.betas
-        for i, (a, b) in enumerate(self.bounds):
-            if works:
-                works[i].wait()  # the current stream waits for this bucket's all-reduce
-            segs = bucket_segments(self.segments, a, b)
-            N.adam_step(self.param[a:b], self.grad[a:b], self.exp_avg[a:b], self.exp_avg_sq[a:b],
-                        segs, self.steps_done, b1, b2, self.eps)
+        for i, (g0, g1) in enumerate(self.bounds):
+            for w in works[i] if works else []:
+                w.wait()  # the current stream waits for this bucket's all-reduce
+            for a, b, grp in flat_segments(self.n, self.k, g0, g1):
+                N.adam_step(self.param[a:b], self.grad[a:b], self.exp_avg[a:b], self.exp_avg_sq[a:b],
+                            [(b - a, self.group_lr[grp])], self.steps_done, b1, b2, self.eps)
 
     def allreduce_only(self):
-        """The step's collective alone (the same buckets, back to back), for
-        measuring its cost; a no-op on one rank."""
+        """The step's collectives alone (the same buckets, back to back), for
+        measuring their cost; a no-op on one rank."""
         if self.world > 1:
-            works = [dist.all_reduce(self.grad[a:b], group=self.group, async_op=True)
-                     for a, b in self.bounds]
+            works = [w for g0, g1 in self.bounds for w in self._allreduce_bucket(g0, g1)]
             for w in works:
                 w.wait()

@@ -103,3 +103,35 @@ def test_trainer_step_matches_composed_step():
         assert rel_linf(got.cpu().numpy(), want.detach().cpu().numpy()) <= 1e-6
     moved = (tr.means - means).abs().max().item()
     assert moved > 1e-4  # the step moved the means (lr 1e-3)
+
+
+@pytest.mark.parametrize("nviews", [1, 10])
+def test_split_backward_equals_single_call(nviews):
+    """sarr_backward with SARR_FLAG_TILES_ONLY followed by sarr_backward_scatter
+    over disjoint Gaussian ranges (boundaries not on warp multiples) writes the
+    same gradient bits as one sarr_backward call."""
+    n = 150_000
+    sc = {k: v.cuda() for k, v in S.make_scene(n, (40.0, 40.0, 10.0), (0.05, 0.5), seed=84).items()}
+    views_t = S.sweep_views(80)[::8][:nviews]
+    views = [_native.make_view(*v) for v in views_t]
+    inputs = _native.prepare_inputs(sc["means"], sc["cov6"], sc["sigma"], sc["sh"])
+    g = torch.randn((nviews, 256, 256), generator=torch.Generator().manual_seed(85)).cuda()
+    ws = torch.empty(_native.workspace_bytes(n, 256, 256, nviews), dtype=torch.uint8, device="cuda")
+
+    def grads():
+        return [torch.full((n, 3), float("nan"), device="cuda"), torch.full((n, 6), float("nan"), device="cuda"),
+                torch.full((n,), float("nan"), device="cuda"), torch.full((n, 16), float("nan"), device="cuda"),
+                torch.full((n,), float("nan"), device="cuda")]
+
+    a = grads()
+    _native.backward(views, *inputs, g, a[0], a[1], _native.SARR_COV6, a[2], a[3], grad_norm=a[4], ws=ws)
+    b = grads()
+    _native.backward(views, *inputs, g, b[0], b[1], _native.SARR_COV6, b[2], b[3], ws=ws,
+                     tiles_only=True)
+    assert torch.isnan(b[0]).all()  # the per-tile pass writes no rows
+    for lo, hi in ((0, 1000), (1000, 77_777), (77_777, n)):
+        _native.backward_scatter(views, n, lo, hi, b[0], b[1], _native.SARR_COV6, b[2], b[3], ws,
+                                 grad_norm=b[4])
+    torch.cuda.synchronize()
+    for x, y in zip(a, b):
+        assert torch.equal(x, y)

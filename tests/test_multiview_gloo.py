@@ -97,14 +97,13 @@ def test_bucket_bounds_and_segments():
             assert all(x[1] == y[0] for x, y in zip(b, b[1:]))
             assert all(a % 64 == 0 for a, _ in b)
     assert multiview.bucket_bounds(0, 4) == []
-    segs = [(300, 1.0), (400, 2.0), (2000, 3.0)]
-    assert multiview.bucket_segments(segs, 0, 256) == [(256, 1.0), (256, 2.0), (256, 3.0)]
-    assert multiview.bucket_segments(segs, 256, 512) == [(44, 1.0), (144, 2.0), (256, 3.0)]
-    assert multiview.bucket_segments(segs, 512, 2000) == [(1488, 3.0)]
-    # every element of every bucket gets the learning rate of its segment
-    total = 2000
-    for a, b in multiview.bucket_bounds(total, 3):
-        sub = multiview.bucket_segments(segs, a, b)
-        for i in range(a, b):
-            lr = next(l for e, l in sub if i - a < e)
-            assert lr == next(l for e, l in segs if i < e)
+    # the parts of each bucket of Gaussians in the flat means | logits | SH
+    # layout cover every element once, each with its group
+    n, k = 1000, 16
+    owner = [None] * (n * (4 + k))
+    for g0, g1 in multiview.bucket_bounds(n, 3, align=256):
+        for a, b, grp in multiview.flat_segments(n, k, g0, g1):
+            for e in range(a, b):
+                assert owner[e] is None
+                owner[e] = grp
+    assert owner == [0] * (3 * n) + [1] * n + [2] * (k * n)
