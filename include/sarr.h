@@ -187,6 +187,19 @@ int sarr_adam_step(int64_t count, float *param, const float *grad, float *exp_av
                    sarr_stream_t stream);
 
 /*
+ * sarr_adam_step over up to 8 disjoint ranges [range_begin[k], range_end[k])
+ * of the same flat arrays in one launch, range k with learning rate
+ * range_lr[k] (host arrays): the same update, element for element. For a
+ * bucket of a flat buffer whose parameter groups are not contiguous (the
+ * means, opacity and SH rows of a range of Gaussians). No reference
+ * counterpart beyond sarr_adam_step's.
+ */
+int sarr_adam_step_ranges(int n_ranges, const int64_t *range_begin, const int64_t *range_end,
+                          const float *range_lr, float *param, const float *grad, float *exp_avg,
+                          float *exp_avg_sq, float beta1, float beta2, float eps, int64_t step,
+                          sarr_stream_t stream);
+
+/*
  * Densification and pruning (GaussianModel.densify_and_prune,
  * gaussian_model.py:433-566) in two calls, with a host decision between them
  * (the reference's max_gaussians tests, which need the counts):
@@ -222,7 +235,7 @@ int sarr_densify_apply(int64_t n, const float *means, const float *scales_log,
 
 /*
  * sarr_forward for one view, image only, without a workspace argument: the
- * scratch is a 6 MiB array inside this library, one per device. No
+ * scratch is an 8 MiB array inside this library, one per device. No
  * counterpart in the reference. It is for callers that cannot allocate
  * device memory: a host whose device memory is all owned by another
  * allocator (a pool reserved at start-up) or a C/C++ caller with no device

@@ -454,6 +454,22 @@ cudaError_t run_selection(const Dims& d, const Ws& w, int gv, const float* means
   return e;
 }
 
+// The backward's inverse index of a group's image-plane lists (workspace
+// head and the views' entry slices).
+BwdIndexArgs bwd_index_args(const Dims& d, const Ws& w, int gv, const StateRef& ipp) {
+  BwdIndexArgs ia;
+  ia.nviews = gv;
+  ia.n = d.n;
+  ia.T = d.T;
+  ia.ipp = ipp;
+  ia.cnt = reinterpret_cast<int*>(w.base + w.L.g_cnt);
+  ia.start = reinterpret_cast<int*>(w.base + w.L.g_start);
+  ia.bsum = reinterpret_cast<int*>(w.base + w.L.g_bsum);
+  ia.entries = reinterpret_cast<uint32_t*>(w.view_area() + w.L.entries);
+  ia.entries_vstride = w.L.per_view / sizeof(uint32_t);
+  return ia;
+}
+
 }  // namespace
 
 extern "C" {
@@ -654,10 +670,10 @@ int sarr_backward(const sarr_view* views, int n_views, int64_t n, const float* m
     tb.partial = reinterpret_cast<float*>(w.view_area() + w.L.partial_bwd);
     tb.partial_vstride = w.L.per_view / sizeof(float);
     tb.err = w.err;
-    tb.listed = reinterpret_cast<uint32_t*>(w.view_area() + w.L.listed);
-    tb.listed_vstride = w.L.per_view / sizeof(uint32_t);
-    tb.n = d.n;
     e = run_kernel(kKindBwdTile, s, [&] { return launch_bwd_tile(tb, d, gv, s); });
+    if (e != cudaSuccess) return SARR_ERR_CUDA;
+    BwdIndexArgs ia = bwd_index_args(d, w, gv, ipp);
+    e = run_kernel(kKindAux, s, [&] { return launch_bwd_index(ia, s); });
     if (e != cudaSuccess) return SARR_ERR_CUDA;
     if (tiles_only) break;  // sarr_backward_scatter writes the rows
 
@@ -676,8 +692,10 @@ int sarr_backward(const sarr_view* views, int n_views, int64_t n, const float* m
     bs.grad_sh_cols = grad_sh_cols;
     bs.grad_norm = grad_norm;
     bs.accumulate = (acc || g0 > 0) ? 1 : 0;
-    bs.listed = tb.listed;
-    bs.listed_vstride = tb.listed_vstride;
+    bs.start = ia.start;
+    bs.entries = ia.entries;
+    bs.entries_vstride = ia.entries_vstride;
+    bs.heavy = reinterpret_cast<int*>(w.base + w.L.g_heavy);
     bs.begin = 0;
     bs.end = d.n;
     e = run_kernel(kKindBwdScatter, s, [&] { return launch_bwd_scatter(bs, d, s); });
@@ -743,8 +761,11 @@ int sarr_backward_scatter(const sarr_view* views, int n_views, int64_t n, const 
   bs.grad_sh_cols = grad_sh_cols;
   bs.grad_norm = grad_norm;
   bs.accumulate = acc ? 1 : 0;
-  bs.listed = reinterpret_cast<const uint32_t*>(w.view_area() + w.L.listed);
-  bs.listed_vstride = w.L.per_view / sizeof(uint32_t);
+  const BwdIndexArgs ia = bwd_index_args(d, w, n_views, ipp);
+  bs.start = ia.start;
+  bs.entries = ia.entries;
+  bs.entries_vstride = ia.entries_vstride;
+  bs.heavy = reinterpret_cast<int*>(w.base + w.L.g_heavy);
   bs.begin = begin;
   bs.end = end;
   return cuda_status(run_kernel(kKindBwdScatter, s, [&] { return launch_bwd_scatter(bs, d, s); }));

@@ -39,6 +39,7 @@ constexpr int kSegMaskAllMaxTiles = 512;         // segment masks of every chunk
 constexpr int kWarpsPerTile = 8;                 // 8 warps x 32 pixels = one 16x16 tile
 constexpr int kMaxTilesAxis = 128;               // images up to 2048 x 2048
 constexpr int kMaxViewsPerLaunch = 256;
+constexpr int kGatherScanBlock = 4096;           // elements per CTA of the backward's index scan
 constexpr uint32_t kEmptyRect = 0x000000FFu;     // tc0 = 255 > tc1 = 0
 
 // Device error bits (workspace error word).
@@ -420,15 +421,28 @@ __host__ __device__ __forceinline__ bool rect_has(uint32_t rc, int tx, int ty) {
   return tx >= tc0 && tx <= tc1 && ty >= tr0 && ty <= tr1;
 }
 
-// compute_sh_scattering_with_basis (:236-244).
+// compute_sh_scattering_with_basis (:236-244). A full 16-coefficient row
+// that is 16-byte aligned is read with four 16-byte loads.
 __device__ __forceinline__ float sh_scattering(const ViewConst& v, const float* __restrict__ row,
                                                int sh_k) {
-  float scattering = mul_(sh_k > 0 ? row[0] : 0.0f, v.h.sh_basis[0]);
+  float c[kSh];
+  if (sh_k == kSh && (reinterpret_cast<uintptr_t>(row) & 15) == 0) {
+    const float4* r4 = reinterpret_cast<const float4*>(row);
 #pragma unroll
-  for (int i = 1; i < kSh; i++) {
-    const float ci = i < sh_k ? row[i] : 0.0f;
-    scattering = fma_(ci, v.h.sh_basis[i], scattering);
+    for (int q = 0; q < kSh / 4; ++q) {
+      const float4 x = __ldg(r4 + q);
+      c[4 * q] = x.x;
+      c[4 * q + 1] = x.y;
+      c[4 * q + 2] = x.z;
+      c[4 * q + 3] = x.w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < kSh; ++i) c[i] = i < sh_k ? row[i] : 0.0f;
   }
+  float scattering = mul_(c[0], v.h.sh_basis[0]);
+#pragma unroll
+  for (int i = 1; i < kSh; i++) scattering = fma_(c[i], v.h.sh_basis[i], scattering);
   const float LEAKY_ALPHA = 0.1f;
   return scattering > 0.0f ? scattering : mul_(LEAKY_ALPHA, scattering);
 }

@@ -88,8 +88,10 @@ __device__ __forceinline__ uint32_t state_rect(const unsigned char* st, const St
 //   i32 (summed-area tables of the tiles still open after the saturation
 //   prefix, from open_table_kernel), state_ipp (used when the caller gives no
 //   state), state_sh, partial_om [T][64] float2, partial_bwd [T][64][8] float,
-//   listed [ceil(n/32)] u32 (Gaussians in one of the view's tile lists, for
-//   the backward's per-Gaussian gather).
+//   entries [T][64] u32 (the backward's list entries grouped by Gaussian:
+//   the group's views' slices form one array indexed by g_start).
+// The head also holds the backward's inverse index of the list entries:
+// g_cnt [n], g_start [n + 1] (exclusive scan) and g_bsum (scan block sums).
 // With cells (multi-view calls, see kCellMinViews) the head also holds the
 // SceneGrid, per-Gaussian bbox bounds hb [n] f32 and cell ids cid [n] u32, the
 // per-cell largest bound cell_hb [kMaxCells] (ordered-int keys), the cells'
@@ -99,10 +101,10 @@ __device__ __forceinline__ uint32_t state_rect(const unsigned char* st, const St
 // area its cell bitmap bits [kCellWords] u32.
 struct WsLayout {
   size_t viewconst, err, scene, hb, cid, cell_hb, cell_count, cell_start, cell_center, mem_pos, mem_idx,
-      always, head;
+      always, g_cnt, g_start, g_bsum, g_heavy, head;
   size_t counts_ipp, counts_sh, need_ipp, need_sh, need_n_ipp, need_n_sh, open_ipp, open_sh;
   size_t bits, xcount, xlist, segmask_ipp, segmask_sh, state_ipp, state_sh, partial_om, partial_bwd,
-      listed, per_view;
+      entries, per_view;
   bool cells;
   StateLayout st;
 };
@@ -143,6 +145,16 @@ __host__ inline WsLayout ws_layout(const Dims& d, bool cells) {
     L.always = h;
     h += align256((size_t)d.n * 4);
   }
+  // the backward's inverse index: list entries per Gaussian, their offsets
+  // (exclusive scan) and the scan's per-block sums
+  L.g_cnt = h;
+  h += align256((size_t)d.n * 4);
+  L.g_start = h;
+  h += align256((size_t)(d.n + 1) * 4);
+  L.g_bsum = h;
+  h += align256((size_t)((d.n + kGatherScanBlock - 1) / kGatherScanBlock + 1) * 4);
+  L.g_heavy = h;  // [0]: count, then the Gaussians with many list entries
+  h += align256((size_t)(d.n + 1) * 4);
   L.head = h;
   L.st = state_layout(d.n, d.T);
   size_t o = 0;
@@ -190,8 +202,8 @@ __host__ inline WsLayout ws_layout(const Dims& d, bool cells) {
   o += align256((size_t)d.T * kCap * 8);
   L.partial_bwd = o;
   o += align256((size_t)d.T * kCap * 8 * 4);
-  L.listed = o;
-  o += align256((size_t)(d.n + 31) / 32 * 4);
+  L.entries = o;
+  o += align256((size_t)d.T * kCap * 4);
   L.per_view = o;
   return L;
 }
@@ -333,11 +345,6 @@ struct TileArgs {
   float* partial;  // omega: float2 [T][64]; backward: float [T][64][8]
   size_t partial_vstride;
   int* err;
-  // backward: bit i of view v's words is set when Gaussian i is in one of the
-  // view's tile lists (null: not recorded)
-  uint32_t* listed;
-  size_t listed_vstride;  // words per view
-  int64_t n;
 };
 
 struct OmegaScatterArgs {
@@ -366,9 +373,27 @@ struct BwdScatterArgs {
   int grad_sh_cols;
   float* grad_norm;
   int accumulate;
-  const uint32_t* listed;  // per-view listed-Gaussian bitmaps of bwd_tile_kernel
-  size_t listed_vstride;   // words per view
+  // the inverse index (launch_bwd_index): Gaussian i's list entries are
+  // entries[start[i] .. start[i+1]), entry e at entries + (e / per) *
+  // entries_vstride + e % per (per = T * 64), packed view << 24 | tile << 6 | slot
+  const int* start;
+  const uint32_t* entries;
+  size_t entries_vstride;  // u32 per view
   int64_t begin, end;      // the gradient rows written: Gaussians [begin, end)
+  int* heavy;              // [0]: count, [1..]: Gaussians left to bwd_heavy_kernel
+};
+
+// The inverse index of a group's image-plane tile lists for the backward.
+struct BwdIndexArgs {
+  int nviews;
+  int64_t n;
+  int T;
+  StateRef ipp;
+  int* cnt;       // [n], zero on entry, zero again on return
+  int* start;     // [n + 1]
+  int* bsum;      // [ceil(n / kGatherScanBlock) + 1]
+  uint32_t* entries;
+  size_t entries_vstride;
 };
 
 struct DebugPreArgs {
@@ -424,6 +449,10 @@ cudaError_t launch_omega_scatter(const OmegaScatterArgs& a, const Dims& d, int n
                                  cudaStream_t s);
 cudaError_t launch_bwd_tile(const TileArgs& a, const Dims& d, int nviews, cudaStream_t s);
 cudaError_t launch_bwd_scatter(const BwdScatterArgs& a, const Dims& d, cudaStream_t s);
+// the inverse index: count entries per Gaussian, scan, fill (five kernels);
+// calls of a few views use none (bwd_uses_index)
+bool bwd_uses_index(int nviews);
+cudaError_t launch_bwd_index(const BwdIndexArgs& a, cudaStream_t s);
 cudaError_t launch_debug_preprocess(const DebugPreArgs& a, cudaStream_t s);
 cudaError_t launch_debug_lists(const DebugListArgs& a, cudaStream_t s);
 cudaError_t launch_debug_view(const ViewHost& vh, float* out, cudaStream_t s);

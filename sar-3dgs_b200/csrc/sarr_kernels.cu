@@ -353,28 +353,36 @@ __device__ __forceinline__ int* x_count(const BinArgs& a, int v) {
 }
 
 // Adds one hit to every tile of a rectangle in a warp's tile counters (two
-// 16-bit counters per word; a chunk holds at most kChunk hits per tile).
-__device__ __forceinline__ void count_rect(uint32_t* cnt, uint32_t rc, int tiles_x) {
+// 16-bit counters per word; a chunk holds at most kChunk hits per tile) and,
+// when `mask` is given, ORs `bit` into the tiles' segment masks, in one
+// flattened pass over the rectangle's tiles. The OR is atomic when
+// kAtomicOr (lanes may OR different bits); otherwise it is a plain
+// read-modify-write, exact when every lane between two __syncwarp ORs the
+// same bit into masks only its warp writes.
+template <bool kAtomicOr>
+__device__ __forceinline__ void count_mark_rect(uint32_t* cnt, uint32_t* mask, uint32_t rc,
+                                                int tiles_x, uint32_t bit) {
   if (rc == kEmptyRect) return;
   const int tc0 = rc & 0xFF, tc1 = (rc >> 8) & 0xFF, tr0 = (rc >> 16) & 0xFF, tr1 = rc >> 24;
-  for (int ty = tr0; ty <= tr1; ++ty)
-    for (int tx = tc0; tx <= tc1; ++tx) {
-      const int t = ty * tiles_x + tx;
-      atomicAdd(cnt + (t >> 1), 1u << ((t & 1) << 4));
+  const int w = tc1 - tc0 + 1, cells = w * (tr1 - tr0 + 1);
+  int t = tr0 * tiles_x + tc0, x = 0;
+  for (int e = 0; e < cells; ++e) {
+    atomicAdd(cnt + (t >> 1), 1u << ((t & 1) << 4));
+    if (mask) {
+      if (kAtomicOr) {
+        atomicOr(mask + t, bit);
+      } else {
+        volatile uint32_t* m = mask + t;
+        *m = *m | bit;
+      }
     }
-}
-
-// ORs `bit` into a warp's tile masks over a rectangle. Only one warp writes
-// these masks and its lanes OR the same bit between two __syncwarp, so plain
-// read-modify-writes give the same result in any interleaving.
-__device__ __forceinline__ void or_rect(uint32_t* mask, uint32_t rc, int tiles_x, uint32_t bit) {
-  if (rc == kEmptyRect) return;
-  const int tc0 = rc & 0xFF, tc1 = (rc >> 8) & 0xFF, tr0 = (rc >> 16) & 0xFF, tr1 = rc >> 24;
-  for (int ty = tr0; ty <= tr1; ++ty)
-    for (int tx = tc0; tx <= tc1; ++tx) {
-      volatile uint32_t* m = mask + ty * tiles_x + tx;
-      *m = *m | bit;
+    if (++x == w) {
+      x = 0;
+      t += tiles_x - w + 1;
+    } else {
+      ++t;
     }
+  }
 }
 
 // Writes a warp's tile counters of one view and chunk as saturating u8 counts
@@ -479,12 +487,10 @@ __global__ void __launch_bounds__(kBinThreads, SARR_PREFIX_MIN_CTAS) bin_prefix_
           }
         }
         rects_ipp[j] = rc_ipp;
-        count_rect(s_cnt, rc_ipp, tiles_x);
-        if (masks) or_rect(s_mask, rc_ipp, tiles_x, 1u << r);
+        count_mark_rect<false>(s_cnt, masks ? s_mask : nullptr, rc_ipp, tiles_x, 1u << r);
         if (kShadow) {
           rects_sh[j] = rc_sh;
-          count_rect(s_cnt_sh, rc_sh, tiles_x);
-          if (masks) or_rect(s_mask_sh, rc_sh, tiles_x, 1u << r);
+          count_mark_rect<false>(s_cnt_sh, masks ? s_mask_sh : nullptr, rc_sh, tiles_x, 1u << r);
         }
       }
       __syncwarp();  // the next round ORs another bit into the same masks
@@ -593,12 +599,10 @@ __global__ void __launch_bounds__(kBinThreads, 3) bin_skip_kernel(const BinArgs 
       uint32_t rc_ipp = kEmptyRect, rc_sh = kEmptyRect;
       bin_exact<kShadow>(vg, s_means, s_cov, cs, j, rc_ipp, rc_sh);
       rects_ipp[j] = rc_ipp;
-      count_rect(s_cnt, rc_ipp, tiles_x);
-      if (masks) mark_rect(s_mask, rc_ipp, tiles_x, 1u << (j >> 5));
+      count_mark_rect<true>(s_cnt, masks ? s_mask : nullptr, rc_ipp, tiles_x, 1u << (j >> 5));
       if (kShadow) {
         rects_sh[j] = rc_sh;
-        count_rect(s_cnt_sh, rc_sh, tiles_x);
-        if (masks) mark_rect(s_mask_sh, rc_sh, tiles_x, 1u << (j >> 5));
+        count_mark_rect<true>(s_cnt_sh, masks ? s_mask_sh : nullptr, rc_sh, tiles_x, 1u << (j >> 5));
       }
       if (xl) xl[xn + lane] = (uint16_t)j;
     };
@@ -1100,12 +1104,10 @@ __global__ void __launch_bounds__(kBinThreads) bin_finalize_kernel(const BinArgs
     uint32_t rc_ipp = kEmptyRect, rc_sh = kEmptyRect;
     bin_exact<kShadow>(vg, means, cov, cs, jl, rc_ipp, rc_sh);
     rects_ipp[i] = rc_ipp;
-    count_rect(s_cnt, rc_ipp, tiles_x);
-    if (masks) mark_rect(s_mask, rc_ipp, tiles_x, 1u << (jl >> 5));
+    count_mark_rect<true>(s_cnt, masks ? s_mask : nullptr, rc_ipp, tiles_x, 1u << (jl >> 5));
     if (kShadow) {
       rects_sh[i] = rc_sh;
-      count_rect(s_cnt_sh, rc_sh, tiles_x);
-      if (masks) mark_rect(s_mask_sh, rc_sh, tiles_x, 1u << (jl >> 5));
+      count_mark_rect<true>(s_cnt_sh, masks ? s_mask_sh : nullptr, rc_sh, tiles_x, 1u << (jl >> 5));
     }
   }
   // the other Gaussians' rectangles are left unwritten: the state's meta and
@@ -2212,12 +2214,6 @@ __global__ void __launch_bounds__(kWarpsPerTile * 32) bwd_tile_kernel(const Tile
   const int count_all = reinterpret_cast<const int*>(st + a.st.L.count)[t];
   const int k_lo = blockIdx.z * kBwdPartRecs;
   if (k_lo >= count_all) return;
-  if (blockIdx.z == 0 && a.listed && tid < count_all) {
-    // the tile's listed Gaussians, for bwd_scatter_kernel's gather
-    const int id = reinterpret_cast<const int*>(st + a.st.L.list)[(size_t)t * kCap + tid];
-    if (id >= 0 && (int64_t)id < a.n)
-      atomicOr(a.listed + v * a.listed_vstride + (id >> 5), 1u << (id & 31));
-  }
   const int count = min(count_all, k_lo + kBwdPartRecs);  // records [0, count) are read
   const bool ok = load_tile_recs(s_rec, &bar, st, a.st.L, t, count, a.err, true);
   if (!__syncthreads_and(ok)) return;
@@ -2296,9 +2292,12 @@ __global__ void __launch_bounds__(kWarpsPerTile * 32) bwd_tile_kernel(const Tile
             A[4] = mul_(g_as, d_gamma_d_cov_rc);
           }
         }
-        const float det_eps = add_(det, kEps);
-        const float d_center_dr = div_(-fma_(cov_rc, dx, -mul_(cov_rr, dy)), det_eps);
-        const float d_center_dc = div_(-fma_(cov_cc, dx, -mul_(cov_rc, dy)), det_eps);
+        // (.cu:973-974) divide by det + EPSILON: one correctly rounded
+        // reciprocal and two products instead of two divisions (within
+        // 1.5 ulp of the quotients)
+        const float inv_det_eps = __frcp_rn(add_(det, kEps));
+        const float d_center_dr = mul_(-fma_(cov_rc, dx, -mul_(cov_rr, dy)), inv_det_eps);
+        const float d_center_dc = mul_(-fma_(cov_cc, dx, -mul_(cov_rc, dy)), inv_det_eps);
         A[5] = mul_(g_as, d_center_dr);
         A[6] = mul_(g_as, d_center_dc);
         prev_transmittance = mul_(prev_transmittance, fma_(-sigma_i, gamma_ipp, 1.0f));
@@ -2325,97 +2324,192 @@ __global__ void __launch_bounds__(kWarpsPerTile * 32) bwd_tile_kernel(const Tile
 
 // Dense gradient rows. The per-Gaussian chain of backward_kernel (:979-1013)
 // is linear in (grad_ipp_r, grad_ipp_c), so it is applied once to the tile sums.
-// 32 x 32 bit-matrix transpose across a warp: on return, bit j of lane l's
-// word is bit l of lane j's word on entry (five butterfly exchange stages).
-__device__ __forceinline__ uint32_t warp_transpose32(uint32_t x, int lane) {
-  const uint32_t masks[5] = {0x0000FFFFu, 0x00FF00FFu, 0x0F0F0F0Fu, 0x33333333u, 0x55555555u};
-#pragma unroll
-  for (int s = 0; s < 5; ++s) {
-    const int j = 16 >> s;
-    const uint32_t y = __shfl_xor_sync(0xffffffffu, x, j);
-    x = (lane & j) ? ((x & ~masks[s]) | ((y >> j) & masks[s])) : ((x & masks[s]) | ((y << j) & ~masks[s]));
-  }
-  return x;
+// The backward's inverse index (launch_bwd_index): the list entries of the
+// group's image-plane tile lists grouped by Gaussian. A count pass (one
+// thread per (view, tile, slot)), an exclusive scan of the counts, and a fill
+// pass that places each entry in its Gaussian's range (in any order there;
+// bwd_scatter_kernel orders each Gaussian's few entries itself).
+__device__ __forceinline__ uint32_t* entry_slot(uint32_t* entries, size_t vstride, int per,
+                                                int64_t e) {
+  return entries + (size_t)(e / per) * vstride + (size_t)(e % per);
 }
 
-// Dense gradient rows of the Gaussians [begin, end). A warp holds 32
-// consecutive Gaussians (one 32-bit word of the listed bitmaps); per block of
-// 32 views its lanes load the views' words and transpose them, so that each
-// lane visits, in view order, only the views whose tile lists hold its
-// Gaussian (about 16k of 1M Gaussians per 256 x 256 view) instead of
-// testing every view.
-__global__ void __launch_bounds__(256) bwd_scatter_kernel(const BwdScatterArgs a) {
-  const int64_t i = (a.begin & ~(int64_t)31) + (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  const int lane = threadIdx.x & 31;
-  const bool active = i >= a.begin && i < a.end && i < a.n;
-  const int64_t w = i >> 5;  // the same for the whole warp
-  const int64_t words = (a.n + 31) >> 5;
-  float g_sigma = 0.f, g_rr = 0.f, g_cc = 0.f, g_rc = 0.f, gx = 0.f, gy = 0.f, gz = 0.f;
-  float g_sh[kSh];
-#pragma unroll
-  for (int k = 0; k < kSh; ++k) g_sh[k] = 0.f;
-
-  for (int vb = 0; vb < a.nviews; vb += 32) {
-    const int vl = vb + lane;
-    uint32_t word = (vl < a.nviews && w < words) ? a.listed[vl * a.listed_vstride + w] : 0u;
-    uint32_t vmask = warp_transpose32(word, lane);
-    if (!active) vmask = 0u;
-  while (vmask) {
-    const int v = vb + __ffs(vmask) - 1;
-    vmask &= vmask - 1;
-    const ViewConst& vc = a.views[v];
-    const int tiles_x = vc.tiles_x;
-    const unsigned char* st = a.ipp.base + v * a.ipp.vstride;
-    const uint32_t rc = state_rect(st, a.ipp.L, st, a.ipp.L, i);
-    const int tc0 = rc & 0xFF, tc1 = (rc >> 8) & 0xFF, tr0 = (rc >> 16) & 0xFF, tr1 = rc >> 24;
-    if (tc0 > tc1) continue;
-    const int* cnts = reinterpret_cast<const int*>(st + a.ipp.L.count);
-    const int* lists = reinterpret_cast<const int*>(st + a.ipp.L.list);
-    const float2* yz = reinterpret_cast<const float2*>(st + a.ipp.L.yz);
-    const float* partial = a.partial + v * a.partial_vstride;
-    float A[7] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    float2 yzr = make_float2(0.f, 0.f);
-    bool hit = false;
-    for (int ty = tr0; ty <= tr1; ++ty)
-      for (int tx = tc0; tx <= tc1; ++tx) {
-        const int t = ty * tiles_x + tx;
-        const int p = list_find(lists + (size_t)t * kCap, cnts[t], (int)i);
-        if (p >= 0) {
-          hit = true;
-          const float* q = partial + ((size_t)t * kCap + p) * 8;
-#pragma unroll
-          for (int c = 0; c < 7; ++c) A[c] += q[c];
-          yzr = yz[(size_t)t * kCap + p];
-        }
-      }
-    if (!hit) continue;
-    g_sigma += A[0];
-#pragma unroll
-    for (int k = 0; k < kSh; ++k) g_sh[k] += A[1] * vc.h.sh_basis[k];
-    g_rr += A[2];
-    g_cc += A[3];
-    g_rc += A[4];
-
-    const float rho_r = vc.h.rho_r, rho_a = vc.h.rho_a;
-    const float yr = yzr.x, zr = yzr.y;
-    const float grad_ipp_r = A[5], grad_ipp_c = A[6];
-    const float Rmin = sqrtf(yr * yr + zr * zr + kEps);
-    const float d_r_d_yr = yr / (rho_r * Rmin);
-    const float d_r_d_zr = zr / (rho_r * Rmin);
-    const float grad_xr = grad_ipp_c / rho_a;
-    const float grad_yr = grad_ipp_r * d_r_d_yr / rho_r;
-    const float grad_zr = grad_ipp_r * d_r_d_zr / rho_r;
-    const float cos_a = vc.cos_a, sin_a = vc.sin_a, cos_b = vc.cos_b, sin_b = vc.sin_b;
-    const float d_xr_d_xw = cos_a, d_xr_d_yw = sin_a, d_xr_d_zw = 0.0f;
-    const float d_yr_d_xw = cos_b * sin_a, d_yr_d_yw = -cos_b * cos_a, d_yr_d_zw = -sin_b;
-    const float d_zr_d_xw = -sin_b * sin_a, d_zr_d_yw = sin_b * cos_a, d_zr_d_zw = -cos_b;
-    gx += grad_xr * d_xr_d_xw + grad_yr * d_yr_d_xw + grad_zr * d_zr_d_xw;
-    gy += grad_xr * d_xr_d_yw + grad_yr * d_yr_d_yw + grad_zr * d_zr_d_yw;
-    gz += grad_xr * d_xr_d_zw + grad_yr * d_yr_d_zw + grad_zr * d_zr_d_zw;
+template <bool kFill>
+__global__ void __launch_bounds__(256) bwd_index_kernel(const BwdIndexArgs a) {
+  const int v = blockIdx.y;
+  const int e = blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= a.T * kCap) return;
+  const int t = e / kCap, slot = e - t * kCap;
+  const unsigned char* st = a.ipp.base + v * a.ipp.vstride;
+  if (slot >= reinterpret_cast<const int*>(st + a.ipp.L.count)[t]) return;
+  const int i = reinterpret_cast<const int*>(st + a.ipp.L.list)[(size_t)t * kCap + slot];
+  if (i < 0 || (int64_t)i >= a.n) return;
+  if (!kFill) {
+    atomicAdd(a.cnt + i, 1);
+  } else {
+    const int64_t pos = (int64_t)a.start[i] + atomicSub(a.cnt + i, 1) - 1;
+    *entry_slot(a.entries, a.entries_vstride, a.T * kCap, pos) =
+        ((uint32_t)v << 24) | ((uint32_t)t << 6) | (uint32_t)slot;
   }
-  }
-  if (!active) return;
+}
 
+// Exclusive scan of cnt[0, n) into start[0, n] in three passes: block sums
+// (kGatherScanBlock elements per CTA, 16 per thread), the scan of the block
+// sums by one CTA, and each block's local scan plus its offset.
+constexpr int kGatherScanThreads = kGatherScanBlock / 16;
+static_assert(kGatherScanThreads == 256, "16 elements per thread, 256 threads");
+
+__device__ __forceinline__ int block_excl_scan256(int x, int* s_warp, int& total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int incl = warp_incl_scan(x, lane);
+  if (lane == 31) s_warp[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    const int w = lane < 8 ? s_warp[lane] : 0;
+    const int wi = warp_incl_scan(w, lane);
+    if (lane < 8) s_warp[8 + lane] = wi - w;
+    if (lane == 7) s_warp[16] = wi;
+  }
+  __syncthreads();
+  total = s_warp[16];
+  return s_warp[8 + warp] + incl - x;
+}
+
+__global__ void __launch_bounds__(kGatherScanThreads) gather_scan_sums_kernel(const int* __restrict__ cnt,
+                                                                              int64_t n, int* bsum) {
+  __shared__ int s_warp[17];
+  const int64_t base = (int64_t)blockIdx.x * kGatherScanBlock + threadIdx.x * 16;
+  int x = 0;
+#pragma unroll
+  for (int k = 0; k < 16; ++k)
+    if (base + k < n) x += cnt[base + k];
+  int total;
+  block_excl_scan256(x, s_warp, total);
+  if (threadIdx.x == 0) bsum[blockIdx.x] = total;
+}
+
+__global__ void __launch_bounds__(kGatherScanThreads) gather_scan_top_kernel(int* bsum, int nb,
+                                                                             int* start, int64_t n) {
+  __shared__ int s_warp[17];
+  int carry = 0;
+  for (int b0 = 0; b0 < nb; b0 += kGatherScanThreads) {
+    const int b = b0 + threadIdx.x;
+    const int x = b < nb ? bsum[b] : 0;
+    int total;
+    const int ex = block_excl_scan256(x, s_warp, total);
+    if (b < nb) bsum[b] = carry + ex;
+    carry += total;
+    __syncthreads();  // s_warp is reused by the next round
+  }
+  if (threadIdx.x == 0) {
+    bsum[nb] = carry;
+    start[n] = carry;
+  }
+}
+
+__global__ void __launch_bounds__(kGatherScanThreads) gather_scan_apply_kernel(const int* __restrict__ cnt,
+                                                                               int64_t n,
+                                                                               const int* __restrict__ bsum,
+                                                                               int* start) {
+  __shared__ int s_warp[17];
+  const int64_t base = (int64_t)blockIdx.x * kGatherScanBlock + threadIdx.x * 16;
+  int c[16];
+  int x = 0;
+#pragma unroll
+  for (int k = 0; k < 16; ++k) {
+    c[k] = base + k < n ? cnt[base + k] : 0;
+    x += c[k];
+  }
+  int total;
+  int run = bsum[blockIdx.x] + block_excl_scan256(x, s_warp, total);
+#pragma unroll
+  for (int k = 0; k < 16; ++k) {
+    if (base + k < n) start[base + k] = run;
+    run += c[k];
+  }
+}
+
+// Dense gradient rows of the Gaussians [begin, end). A Gaussian's list
+// entries (from the inverse index) are taken in (view, tile) order -- views
+// ascending, the tiles of a view in row-major order -- their per-slot partial
+// sums added per view, then the view's chain rule (:979-1013), which is
+// linear in (grad_ipp_r, grad_ipp_c), applied once per view and the views'
+// contributions summed in view order. Deterministic: no float atomics.
+// bwd_scatter_kernel takes the Gaussians with at most kScatterLocalEntries
+// entries, one thread each; the others (the lowest-index Gaussians fill most
+// tile lists, so they have one entry per listing tile of every view) go to
+// bwd_heavy_kernel, one CTA each.
+constexpr int kScatterLocalEntries = 16;
+constexpr int kHeavyThreads = 256;
+
+// One view's contribution: its partial sums A[0..4] and the means chain.
+struct ViewContrib {
+  float a0, a1, a2, a3, a4, cx, cy, cz;
+};
+
+__device__ __forceinline__ ViewContrib bwd_view_contrib(const ViewConst& vc, const float A[7], float2 yzr) {
+  ViewContrib o;
+  o.a0 = A[0];
+  o.a1 = A[1];
+  o.a2 = A[2];
+  o.a3 = A[3];
+  o.a4 = A[4];
+  const float rho_r = vc.h.rho_r, rho_a = vc.h.rho_a;
+  const float yr = yzr.x, zr = yzr.y;
+  const float grad_ipp_r = A[5], grad_ipp_c = A[6];
+  const float Rmin = sqrtf(yr * yr + zr * zr + kEps);
+  const float d_r_d_yr = yr / (rho_r * Rmin);
+  const float d_r_d_zr = zr / (rho_r * Rmin);
+  const float grad_xr = grad_ipp_c / rho_a;
+  const float grad_yr = grad_ipp_r * d_r_d_yr / rho_r;
+  const float grad_zr = grad_ipp_r * d_r_d_zr / rho_r;
+  const float cos_a = vc.cos_a, sin_a = vc.sin_a, cos_b = vc.cos_b, sin_b = vc.sin_b;
+  const float d_xr_d_xw = cos_a, d_xr_d_yw = sin_a, d_xr_d_zw = 0.0f;
+  const float d_yr_d_xw = cos_b * sin_a, d_yr_d_yw = -cos_b * cos_a, d_yr_d_zw = -sin_b;
+  const float d_zr_d_xw = -sin_b * sin_a, d_zr_d_yw = sin_b * cos_a, d_zr_d_zw = -cos_b;
+  o.cx = grad_xr * d_xr_d_xw + grad_yr * d_yr_d_xw + grad_zr * d_zr_d_xw;
+  o.cy = grad_xr * d_xr_d_yw + grad_yr * d_yr_d_yw + grad_zr * d_zr_d_yw;
+  o.cz = grad_xr * d_xr_d_zw + grad_yr * d_yr_d_zw + grad_zr * d_zr_d_zw;
+  return o;
+}
+
+// The 23 gradient sums of a Gaussian, accumulated view by view with the
+// same operations on both paths.
+struct GradSums {
+  float sigma, rr, cc, rc, x, y, z;
+  float sh[kSh];
+};
+
+__device__ __forceinline__ void grad_add_view(GradSums& g, const ViewContrib& c, const ViewConst& vc) {
+  g.sigma = __fadd_rn(g.sigma, c.a0);
+#pragma unroll
+  for (int k = 0; k < kSh; ++k) g.sh[k] = __fmaf_rn(c.a1, vc.h.sh_basis[k], g.sh[k]);
+  g.rr = __fadd_rn(g.rr, c.a2);
+  g.cc = __fadd_rn(g.cc, c.a3);
+  g.rc = __fadd_rn(g.rc, c.a4);
+  g.x = __fadd_rn(g.x, c.cx);
+  g.y = __fadd_rn(g.y, c.cy);
+  g.z = __fadd_rn(g.z, c.cz);
+}
+
+__device__ __forceinline__ void entry_partial(const BwdScatterArgs& a, uint32_t key, float A[7], float2& yzr) {
+  const int v = (int)(key >> 24), t = (int)((key >> 6) & 0x3FFFFu), slot = (int)(key & 63u);
+  const float* q8 = a.partial + v * a.partial_vstride + ((size_t)t * kCap + slot) * 8;
+  const float4 p0 = *reinterpret_cast<const float4*>(q8);
+  const float4 p1 = *reinterpret_cast<const float4*>(q8 + 4);
+  A[0] = __fadd_rn(A[0], p0.x);
+  A[1] = __fadd_rn(A[1], p0.y);
+  A[2] = __fadd_rn(A[2], p0.z);
+  A[3] = __fadd_rn(A[3], p0.w);
+  A[4] = __fadd_rn(A[4], p1.x);
+  A[5] = __fadd_rn(A[5], p1.y);
+  A[6] = __fadd_rn(A[6], p1.z);
+  const unsigned char* st = a.ipp.base + v * a.ipp.vstride;
+  yzr = reinterpret_cast<const float2*>(st + a.ipp.L.yz)[(size_t)t * kCap + slot];
+}
+
+__device__ __forceinline__ void write_grad_row(const BwdScatterArgs& a, int64_t i, const GradSums& g) {
+  float gx = g.x, gy = g.y, gz = g.z;
   float* gm = a.grad_means + i * 3;
   if (a.accumulate) {
     gx += gm[0];
@@ -2426,28 +2520,342 @@ __global__ void __launch_bounds__(256) bwd_scatter_kernel(const BwdScatterArgs a
   gm[1] = gy;
   gm[2] = gz;
   if (a.grad_norm) a.grad_norm[i] = sqrtf(gx * gx + gy * gy + gz * gz);
-
   if (a.grad_cov_layout == 6) {
     float* gc = a.grad_cov + i * 6;
-    float c6[6] = {g_rr, g_cc, 0.f, g_rc, 0.f, 0.f};
+    const float c6[6] = {g.rr, g.cc, 0.f, g.rc, 0.f, 0.f};
 #pragma unroll
-    for (int c = 0; c < 6; ++c) gc[c] = a.accumulate ? gc[c] + c6[c] : c6[c];
+    for (int q = 0; q < 6; ++q) gc[q] = a.accumulate ? gc[q] + c6[q] : c6[q];
   } else {
     float* gc = a.grad_cov + i * 9;
-    float c9[9] = {g_rr, g_rc, 0.f, g_rc, g_cc, 0.f, 0.f, 0.f, 0.f};
+    const float c9[9] = {g.rr, g.rc, 0.f, g.rc, g.cc, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-    for (int c = 0; c < 9; ++c) gc[c] = a.accumulate ? gc[c] + c9[c] : c9[c];
+    for (int q = 0; q < 9; ++q) gc[q] = a.accumulate ? gc[q] + c9[q] : c9[q];
   }
-  a.grad_sigma[i] = a.accumulate ? a.grad_sigma[i] + g_sigma : g_sigma;
+  a.grad_sigma[i] = a.accumulate ? a.grad_sigma[i] + g.sigma : g.sigma;
   float* gs = a.grad_sh + i * a.grad_sh_cols;
   if (a.grad_sh_cols == kSh && !a.accumulate && ((uintptr_t)gs & 15) == 0) {
     float4* gs4 = reinterpret_cast<float4*>(gs);
 #pragma unroll
-    for (int q = 0; q < 4; ++q) gs4[q] = make_float4(g_sh[4 * q], g_sh[4 * q + 1], g_sh[4 * q + 2], g_sh[4 * q + 3]);
+    for (int q = 0; q < 4; ++q) gs4[q] = make_float4(g.sh[4 * q], g.sh[4 * q + 1], g.sh[4 * q + 2], g.sh[4 * q + 3]);
   } else {
 #pragma unroll
     for (int k = 0; k < kSh; ++k)
-      if (k < a.grad_sh_cols) gs[k] = a.accumulate ? gs[k] + g_sh[k] : g_sh[k];
+      if (k < a.grad_sh_cols) gs[k] = a.accumulate ? gs[k] + g.sh[k] : g.sh[k];
+  }
+}
+
+__device__ __forceinline__ GradSums grad_zero() {
+  GradSums g;
+  g.sigma = g.rr = g.cc = g.rc = g.x = g.y = g.z = 0.f;
+#pragma unroll
+  for (int k = 0; k < kSh; ++k) g.sh[k] = 0.f;
+  return g;
+}
+
+// The entries of one Gaussian in sorted order (keys[0..c) ascending), summed.
+template <typename KeyAt>
+__device__ __forceinline__ GradSums grad_from_sorted(const BwdScatterArgs& a, int c, KeyAt key_at) {
+  GradSums g = grad_zero();
+  int cur_v = -1;
+  float A[7] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  float2 yzr = make_float2(0.f, 0.f);
+  for (int q = 0; q < c; ++q) {
+    const uint32_t k = key_at(q);
+    const int v = (int)(k >> 24);
+    if (v != cur_v) {
+      if (cur_v >= 0) grad_add_view(g, bwd_view_contrib(a.views[cur_v], A, yzr), a.views[cur_v]);
+      cur_v = v;
+#pragma unroll
+      for (int cc = 0; cc < 7; ++cc) A[cc] = 0.f;
+    }
+    entry_partial(a, k, A, yzr);
+  }
+  if (cur_v >= 0) grad_add_view(g, bwd_view_contrib(a.views[cur_v], A, yzr), a.views[cur_v]);
+  return g;
+}
+
+// Calls of at most kDirectGatherMaxViews views: no inverse index; each
+// Gaussian looks itself up in the lists of the tiles its rectangle covers,
+// view by view (binary searches in the index-ordered lists), in the same
+// (view, tile) order and with the same sums as the indexed path.
+constexpr int kDirectGatherMaxViews = 4;
+
+__global__ void __launch_bounds__(256) bwd_gather_kernel(const BwdScatterArgs a) {
+  const int64_t i = a.begin + (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= a.end) return;
+  GradSums g = grad_zero();
+  for (int v = 0; v < a.nviews; ++v) {
+    const ViewConst& vc = a.views[v];
+    const int tiles_x = vc.tiles_x;
+    const unsigned char* st = a.ipp.base + v * a.ipp.vstride;
+    const uint32_t rc = state_rect(st, a.ipp.L, st, a.ipp.L, i);
+    const int tc0 = rc & 0xFF, tc1 = (rc >> 8) & 0xFF, tr0 = (rc >> 16) & 0xFF, tr1 = rc >> 24;
+    if (tc0 > tc1) continue;
+    const int* cnts = reinterpret_cast<const int*>(st + a.ipp.L.count);
+    const int* lists = reinterpret_cast<const int*>(st + a.ipp.L.list);
+    float A[7] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    float2 yzr = make_float2(0.f, 0.f);
+    bool hit = false;
+    for (int ty = tr0; ty <= tr1; ++ty)
+      for (int tx = tc0; tx <= tc1; ++tx) {
+        const int t = ty * tiles_x + tx;
+        const int p = list_find(lists + (size_t)t * kCap, cnts[t], (int)i);
+        if (p >= 0) {
+          hit = true;
+          entry_partial(a, ((uint32_t)v << 24) | ((uint32_t)t << 6) | (uint32_t)p, A, yzr);
+        }
+      }
+    if (hit) grad_add_view(g, bwd_view_contrib(vc, A, yzr), vc);
+  }
+  write_grad_row(a, i, g);
+}
+
+__global__ void __launch_bounds__(256) bwd_scatter_kernel(const BwdScatterArgs a) {
+  const int64_t i = a.begin + (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= a.end) return;
+  const int e0 = a.start[i], c = a.start[i + 1] - e0;
+  if (c > kScatterLocalEntries) {
+    const int h = atomicAdd(a.heavy, 1);
+    a.heavy[1 + h] = (int)i;
+    return;
+  }
+  const int per_view = a.views[0].tiles_x * a.views[0].tiles_y * kCap;
+  uint32_t key[kScatterLocalEntries];
+  for (int q = 0; q < c; ++q)
+    key[q] = *entry_slot(const_cast<uint32_t*>(a.entries), a.entries_vstride, per_view, (int64_t)e0 + q);
+  for (int q = 1; q < c; ++q) {  // insertion sort (a Gaussian's keys are distinct)
+    const uint32_t x = key[q];
+    int r = q - 1;
+    while (r >= 0 && key[r] > x) {
+      key[r + 1] = key[r];
+      --r;
+    }
+    key[r + 1] = x;
+  }
+  const GradSums g = grad_from_sorted(a, c, [&](int q) { return key[q]; });
+  write_grad_row(a, i, g);
+}
+
+// Groups of at most 32 views: one warp per Gaussian left by
+// bwd_scatter_kernel, lane v for view v, otherwise as bwd_heavy_kernel.
+constexpr int kHeavyWarpViews = 32;
+constexpr int kHeavyViewEntriesW = 32;
+
+__global__ void __launch_bounds__(256) bwd_heavy_warp_kernel(const BwdScatterArgs a) {
+  constexpr int kWarps = 8;
+  __shared__ ViewContrib s_con[kWarps][32];
+  __shared__ int s_has[kWarps][32];
+  __shared__ float s_out[kWarps][23];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int count = a.heavy[0];
+  const int nviews = a.nviews;
+  const int per_view = a.views[0].tiles_x * a.views[0].tiles_y * kCap;
+  for (int h = blockIdx.x * kWarps + warp; h < count; h += gridDim.x * kWarps) {
+    const int64_t i = a.heavy[1 + h];
+    const int e0 = a.start[i], c = a.start[i + 1] - e0;
+    uint32_t key[kHeavyViewEntriesW];
+    int m = 0;
+    {
+      const int per = per_view;
+      int slice = e0 / per, off = e0 % per;
+      for (int q = 0; q < c; ++q) {
+        const uint32_t k = a.entries[(size_t)slice * a.entries_vstride + off];
+        if (++off == per) {
+          off = 0;
+          ++slice;
+        }
+        if ((int)(k >> 24) == lane) {
+          if (m < kHeavyViewEntriesW) key[m] = k;
+          ++m;
+        }
+      }
+    }
+    s_has[warp][lane] = 0;
+    if (lane < nviews && m > 0) {
+      float A[7] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      float2 yzr = make_float2(0.f, 0.f);
+      if (m <= kHeavyViewEntriesW) {
+        for (int q = 1; q < m; ++q) {  // insertion sort by tile
+          const uint32_t x = key[q];
+          int r = q - 1;
+          while (r >= 0 && key[r] > x) {
+            key[r + 1] = key[r];
+            --r;
+          }
+          key[r + 1] = x;
+        }
+        for (int q = 0; q < m; ++q) entry_partial(a, key[q], A, yzr);
+      } else {
+        uint32_t last = 0;
+        for (int q = 0; q < m; ++q) {
+          uint32_t k = 0xFFFFFFFFu;
+          int slice = e0 / per_view, off = e0 % per_view;
+          for (int r = 0; r < c; ++r) {
+            const uint32_t x = a.entries[(size_t)slice * a.entries_vstride + off];
+            if (++off == per_view) {
+              off = 0;
+              ++slice;
+            }
+            if ((int)(x >> 24) == lane && (q == 0 || x > last) && x < k) k = x;
+          }
+          last = k;
+          entry_partial(a, k, A, yzr);
+        }
+      }
+      s_con[warp][lane] = bwd_view_contrib(a.views[lane], A, yzr);
+      s_has[warp][lane] = 1;
+    }
+    __syncwarp();
+    if (lane < 23) {
+      float acc = 0.f;
+      for (int v = 0; v < nviews; ++v) {
+        if (!s_has[warp][v]) continue;
+        const ViewContrib& cv = s_con[warp][v];
+        if (lane == 0) acc = __fadd_rn(acc, cv.a0);
+        else if (lane <= kSh) acc = __fmaf_rn(cv.a1, a.views[v].h.sh_basis[lane - 1], acc);
+        else if (lane == 17) acc = __fadd_rn(acc, cv.a2);
+        else if (lane == 18) acc = __fadd_rn(acc, cv.a3);
+        else if (lane == 19) acc = __fadd_rn(acc, cv.a4);
+        else if (lane == 20) acc = __fadd_rn(acc, cv.cx);
+        else if (lane == 21) acc = __fadd_rn(acc, cv.cy);
+        else acc = __fadd_rn(acc, cv.cz);
+      }
+      s_out[warp][lane] = acc;
+    }
+    __syncwarp();
+    if (lane == 0) {
+      GradSums g;
+      g.sigma = s_out[warp][0];
+#pragma unroll
+      for (int k = 0; k < kSh; ++k) g.sh[k] = s_out[warp][1 + k];
+      g.rr = s_out[warp][17];
+      g.cc = s_out[warp][18];
+      g.rc = s_out[warp][19];
+      g.x = s_out[warp][20];
+      g.y = s_out[warp][21];
+      g.z = s_out[warp][22];
+      write_grad_row(a, i, g);
+    }
+    __syncwarp();
+  }
+}
+
+// One CTA per Gaussian left by bwd_scatter_kernel (persistent over the
+// list), thread v for view v of the group: every thread reads the
+// Gaussian's entries in index order (the same entry at the same time, a
+// broadcast), keeps those of its view, orders them by tile and sums their
+// partials, and applies the view's chain rule; then the views'
+// contributions are accumulated in view order, one thread per output sum.
+// A view with more than kHeavyViewEntries listing tiles of the Gaussian (a
+// bbox wider than ~80 pixels) takes them in order by repeated selection.
+constexpr int kHeavyViewEntries = 32;
+static_assert(kHeavyThreads == kMaxViewsPerLaunch, "one thread per view of a launch group");
+
+// Sequential reader of a Gaussian's entries in the views' entry slices.
+struct EntryCursor {
+  const uint32_t* base;
+  size_t vstride;
+  int per, slice, off;
+  __device__ EntryCursor(const BwdScatterArgs& a, int per_view, int64_t e0)
+      : base(a.entries), vstride(a.entries_vstride), per(per_view),
+        slice((int)(e0 / per_view)), off((int)(e0 % per_view)) {}
+  __device__ __forceinline__ uint32_t next() {
+    const uint32_t k = base[(size_t)slice * vstride + off];
+    if (++off == per) {
+      off = 0;
+      ++slice;
+    }
+    return k;
+  }
+};
+
+__global__ void __launch_bounds__(kHeavyThreads) bwd_heavy_kernel(const BwdScatterArgs a) {
+  __shared__ ViewContrib s_con[kMaxViewsPerLaunch];
+  __shared__ int s_has[kMaxViewsPerLaunch];
+  __shared__ float s_out[23];
+  const int tid = threadIdx.x;
+  const int count = a.heavy[0];
+  const int nviews = a.nviews;
+  const int per_view = a.views[0].tiles_x * a.views[0].tiles_y * kCap;
+  for (int h = blockIdx.x; h < count; h += gridDim.x) {
+    const int64_t i = a.heavy[1 + h];
+    const int e0 = a.start[i], c = a.start[i + 1] - e0;
+    uint32_t key[kHeavyViewEntries];
+    int m = 0;
+    {
+      EntryCursor cur(a, per_view, e0);
+      for (int q = 0; q < c; ++q) {
+        const uint32_t k = cur.next();
+        if ((int)(k >> 24) == tid) {
+          if (m < kHeavyViewEntries) key[m] = k;
+          ++m;
+        }
+      }
+    }
+    s_has[tid] = 0;
+    if (tid < nviews && m > 0) {
+      float A[7] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      float2 yzr = make_float2(0.f, 0.f);
+      if (m <= kHeavyViewEntries) {
+        for (int q = 1; q < m; ++q) {  // insertion sort by tile
+          const uint32_t x = key[q];
+          int r = q - 1;
+          while (r >= 0 && key[r] > x) {
+            key[r + 1] = key[r];
+            --r;
+          }
+          key[r + 1] = x;
+        }
+        for (int q = 0; q < m; ++q) entry_partial(a, key[q], A, yzr);
+      } else {
+        uint32_t last = 0;
+        for (int q = 0; q < m; ++q) {
+          uint32_t k = 0xFFFFFFFFu;
+          EntryCursor cur(a, per_view, e0);
+          for (int r = 0; r < c; ++r) {
+            const uint32_t x = cur.next();
+            if ((int)(x >> 24) == tid && (q == 0 || x > last) && x < k) k = x;
+          }
+          last = k;
+          entry_partial(a, k, A, yzr);
+        }
+      }
+      s_con[tid] = bwd_view_contrib(a.views[tid], A, yzr);
+      s_has[tid] = 1;
+    }
+    __syncthreads();
+    if (tid < 23) {
+      // output sum tid: 0 sigma, 1..16 SH, 17 rr, 18 cc, 19 rc, 20..22 x y z
+      float acc = 0.f;
+      for (int v = 0; v < nviews; ++v) {
+        if (!s_has[v]) continue;
+        const ViewContrib& cv = s_con[v];
+        if (tid == 0) acc = __fadd_rn(acc, cv.a0);
+        else if (tid <= kSh) acc = __fmaf_rn(cv.a1, a.views[v].h.sh_basis[tid - 1], acc);
+        else if (tid == 17) acc = __fadd_rn(acc, cv.a2);
+        else if (tid == 18) acc = __fadd_rn(acc, cv.a3);
+        else if (tid == 19) acc = __fadd_rn(acc, cv.a4);
+        else if (tid == 20) acc = __fadd_rn(acc, cv.cx);
+        else if (tid == 21) acc = __fadd_rn(acc, cv.cy);
+        else acc = __fadd_rn(acc, cv.cz);
+      }
+      s_out[tid] = acc;
+    }
+    __syncthreads();
+    if (tid == 0) {
+      GradSums g;
+      g.sigma = s_out[0];
+#pragma unroll
+      for (int k = 0; k < kSh; ++k) g.sh[k] = s_out[1 + k];
+      g.rr = s_out[17];
+      g.cc = s_out[18];
+      g.rc = s_out[19];
+      g.x = s_out[20];
+      g.y = s_out[21];
+      g.z = s_out[22];
+      write_grad_row(a, i, g);
+    }
+    __syncthreads();
   }
 }
 
@@ -2759,33 +3167,56 @@ cudaError_t launch_omega_scatter(const OmegaScatterArgs& a, const Dims& d, int n
   return cudaGetLastError();
 }
 
-__global__ void __launch_bounds__(256) zero_words_kernel(uint32_t* __restrict__ base, size_t vstride,
-                                                         int64_t words) {
-  uint32_t* p = base + blockIdx.y * vstride;
-  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < words;
-       e += (int64_t)gridDim.x * blockDim.x)
-    p[e] = 0u;
+cudaError_t launch_bwd_tile(const TileArgs& a, const Dims& d, int nviews, cudaStream_t s) {
+  bwd_tile_kernel<<<dim3(d.T, nviews, kBwdParts), kWarpsPerTile * 32, 0, s>>>(a);
+  return cudaGetLastError();
 }
 
-cudaError_t launch_bwd_tile(const TileArgs& a, const Dims& d, int nviews, cudaStream_t s) {
-  if (a.listed) {
-    const int64_t words = (d.n + 31) / 32;
-    const unsigned blocks = (unsigned)std::min<int64_t>((words + 255) / 256, 64);
-    zero_words_kernel<<<dim3(blocks, nviews), 256, 0, s>>>(a.listed, a.listed_vstride, words);
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return e;
-    count_launches(1);  // the second kernel of this launch step
-  }
-  bwd_tile_kernel<<<dim3(d.T, nviews, kBwdParts), kWarpsPerTile * 32, 0, s>>>(a);
+bool bwd_uses_index(int nviews) { return nviews > kDirectGatherMaxViews; }
+
+cudaError_t launch_bwd_index(const BwdIndexArgs& a, cudaStream_t s) {
+  if (!bwd_uses_index(a.nviews)) return cudaSuccess;
+  cudaError_t e = cudaMemsetAsync(a.cnt, 0, (size_t)a.n * sizeof(int), s);
+  if (e != cudaSuccess) return e;
+  const dim3 grid((unsigned)((a.T * kCap + 255) / 256), (unsigned)a.nviews);
+  bwd_index_kernel<false><<<grid, 256, 0, s>>>(a);
+  const int nb = (int)((a.n + kGatherScanBlock - 1) / kGatherScanBlock);
+  gather_scan_sums_kernel<<<nb, kGatherScanThreads, 0, s>>>(a.cnt, a.n, a.bsum);
+  gather_scan_top_kernel<<<1, kGatherScanThreads, 0, s>>>(a.bsum, nb, a.start, a.n);
+  gather_scan_apply_kernel<<<nb, kGatherScanThreads, 0, s>>>(a.cnt, a.n, a.bsum, a.start);
+  bwd_index_kernel<true><<<grid, 256, 0, s>>>(a);
+  count_launches(4);  // five kernels in this launch step
   return cudaGetLastError();
 }
 
 cudaError_t launch_bwd_scatter(const BwdScatterArgs& a, const Dims& d, cudaStream_t s) {
   (void)d;
   if (a.end <= a.begin) return cudaSuccess;
-  const int64_t span = a.end - (a.begin & ~(int64_t)31);
-  const unsigned blocks = (unsigned)((span + 255) / 256);
+  const unsigned blocks = (unsigned)((a.end - a.begin + 255) / 256);
+  if (!bwd_uses_index(a.nviews)) {
+    bwd_gather_kernel<<<blocks, 256, 0, s>>>(a);
+    return cudaGetLastError();
+  }
+  cudaError_t e = cudaMemsetAsync(a.heavy, 0, sizeof(int), s);
+  if (e != cudaSuccess) return e;
   bwd_scatter_kernel<<<blocks, 256, 0, s>>>(a);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  count_launches(1);  // the second kernel of this launch step
+  int sms = 148, per_sm = 0, dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess)
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (a.nviews <= kHeavyWarpViews) {
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, bwd_heavy_warp_kernel, 256, 0) !=
+            cudaSuccess || per_sm < 1)
+      per_sm = 1;
+    bwd_heavy_warp_kernel<<<sms * per_sm, 256, 0, s>>>(a);
+  } else {
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, bwd_heavy_kernel, kHeavyThreads, 0) !=
+            cudaSuccess || per_sm < 1)
+      per_sm = 1;
+    bwd_heavy_kernel<<<sms * per_sm, kHeavyThreads, 0, s>>>(a);
+  }
   return cudaGetLastError();
 }
 

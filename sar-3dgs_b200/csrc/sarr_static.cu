@@ -2,7 +2,7 @@
 // workspace in a file-scope device array of this library, for callers that
 // cannot allocate device memory themselves (see include/sarr.h).
 //
-// Scratch: g_static_scratch, kStaticScratchBytes (6 MiB) per device, which
+// Scratch: g_static_scratch, kStaticScratchBytes (8 MiB) per device, which
 // holds the workspace of one view with n <= kStaticMaxGaussians (131,072)
 // Gaussians and an image of at most 256 x 256 pixels. Nothing in it has to
 // start at zero: every byte the call reads is written earlier in the same
@@ -26,7 +26,7 @@ namespace {
 
 constexpr int64_t kStaticMaxGaussians = 131072;
 constexpr int kStaticMaxSamples = 256;
-constexpr size_t kStaticScratchBytes = (size_t)6 * 1024 * 1024;
+constexpr size_t kStaticScratchBytes = (size_t)8 * 1024 * 1024;
 constexpr int kStaticMaxContexts = 64;
 
 static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];

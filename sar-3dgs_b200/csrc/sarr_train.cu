@@ -522,6 +522,30 @@ __global__ void __launch_bounds__(kAdamThreads) adam_kernel(AdamParams A, float*
   }
 }
 
+// Disjoint ranges [begin_k, end_k) of the same flat arrays in one launch
+// (grid.y = range), each with its own step size.
+struct AdamRanges {
+  int n;
+  int64_t begin[kAdamMaxSegments], end[kAdamMaxSegments];
+};
+
+__global__ void __launch_bounds__(kAdamThreads) adam_ranges_kernel(AdamParams A, AdamRanges R,
+                                                                   float* __restrict__ param,
+                                                                   const float* __restrict__ grad,
+                                                                   float* __restrict__ m,
+                                                                   float* __restrict__ v) {
+  const int k = blockIdx.y;
+  const int64_t b = R.begin[k], e = R.end[k];
+  const float step_size = A.seg_step[k];
+  for (int64_t i = b + (int64_t)blockIdx.x * kAdamThreads + threadIdx.x; i < e;
+       i += (int64_t)gridDim.x * kAdamThreads) {
+    float mi = m[i], vi = v[i];
+    param[i] = adam_elem(param[i], grad[i], mi, vi, step_size, A);
+    m[i] = mi;
+    v[i] = vi;
+  }
+}
+
 }  // namespace
 
 extern "C" int sarr_gaussian_params(int64_t n, const float* scales_log, const float* rotations,
@@ -640,6 +664,46 @@ extern "C" int sarr_adam_step(int64_t count, float* param, const float* grad, fl
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   adam_kernel<<<(unsigned)((threads + kAdamThreads - 1) / kAdamThreads), kAdamThreads, 0, s>>>(
       A, param, grad, exp_avg, exp_avg_sq, vec);
+  sarr::count_launches(1);
+  return cuda_status(cudaGetLastError());
+}
+
+extern "C" int sarr_adam_step_ranges(int n_ranges, const int64_t* range_begin,
+                                     const int64_t* range_end, const float* range_lr,
+                                     float* param, const float* grad, float* exp_avg,
+                                     float* exp_avg_sq, float beta1, float beta2, float eps,
+                                     int64_t step, sarr_stream_t stream) {
+  if (n_ranges < 1 || n_ranges > kAdamMaxSegments || step < 1) return SARR_ERR_ARG;
+  if (!range_begin || !range_end || !range_lr) return SARR_ERR_ARG;
+  if (!(beta1 >= 0.0f && beta1 < 1.0f && beta2 >= 0.0f && beta2 < 1.0f)) return SARR_ERR_ARG;
+  if (!param || !grad || !exp_avg || !exp_avg_sq) return SARR_ERR_ARG;
+  AdamParams A;
+  memset(&A, 0, sizeof(A));
+  AdamRanges R;
+  memset(&R, 0, sizeof(R));
+  const double bc1 = 1.0 - pow((double)beta1, (double)step);
+  const double bc2 = 1.0 - pow((double)beta2, (double)step);
+  int64_t longest = 0;
+  R.n = n_ranges;
+  for (int k = 0; k < n_ranges; ++k) {
+    if (range_begin[k] < 0 || range_end[k] < range_begin[k]) return SARR_ERR_ARG;
+    R.begin[k] = range_begin[k];
+    R.end[k] = range_end[k];
+    A.seg_step[k] = (float)((double)range_lr[k] / bc1);
+    if (range_end[k] - range_begin[k] > longest) longest = range_end[k] - range_begin[k];
+  }
+  if (longest == 0) return SARR_OK;
+  A.nseg = n_ranges;
+  A.beta1 = beta1;
+  A.beta2 = beta2;
+  A.one_m_beta1 = (float)(1.0 - (double)beta1);
+  A.one_m_beta2 = (float)(1.0 - (double)beta2);
+  A.bc2_sqrt = (float)sqrt(bc2);
+  A.eps = eps;
+  const int64_t blocks = (longest + kAdamThreads - 1) / kAdamThreads;
+  const dim3 grid((unsigned)(blocks < 148 * 8 ? blocks : 148 * 8), (unsigned)n_ranges);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  adam_ranges_kernel<<<grid, kAdamThreads, 0, s>>>(A, R, param, grad, exp_avg, exp_avg_sq);
   sarr::count_launches(1);
   return cuda_status(cudaGetLastError());
 }

@@ -83,6 +83,8 @@ def _declare(L):
     L.sarr_combined_loss.argtypes = [I, I, I, P, P, F, F, I, I, P, P, P, SZ, P]
     L.sarr_adam_step.argtypes = [I64, P, P, P, P, I, ctypes.POINTER(I64), ctypes.POINTER(F), F, F,
                                  F, I64, P]
+    L.sarr_adam_step_ranges.argtypes = [I, ctypes.POINTER(I64), ctypes.POINTER(I64),
+                                        ctypes.POINTER(F), P, P, P, P, F, F, F, I64, P]
     L.sarr_densify_workspace_size.argtypes = [I64, ctypes.POINTER(SZ)]
     L.sarr_densify_flags.argtypes = [I64, P, P, P, F, F, F, F, P, P, SZ, P]
     L.sarr_densify_apply.argtypes = [I64, P, P, P, P, P, I, P, P, I, I, P, P, P, P, P, P, SZ, P]
@@ -90,7 +92,7 @@ def _declare(L):
                  "sarr_backward_scatter",
                  "sarr_debug_preprocess", "sarr_debug_tile_lists", "sarr_check_device_errors",
                  "sarr_debug_tile_rect", "sarr_gaussian_params", "sarr_loss_workspace_size",
-                 "sarr_combined_loss", "sarr_adam_step", "sarr_densify_workspace_size", "sarr_densify_flags",
+                 "sarr_combined_loss", "sarr_adam_step", "sarr_adam_step_ranges", "sarr_densify_workspace_size", "sarr_densify_flags",
                  "sarr_densify_apply"):
         getattr(L, name).restype = I
     return L

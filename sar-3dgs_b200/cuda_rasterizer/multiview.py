@@ -166,32 +166,58 @@ class ViewParallelTrainer:
         self.cov6 = torch.empty((n, 6), dtype=torch.float32, device=dev)
         self.sigma = torch.empty((n,), dtype=torch.float32, device=dev)
         self.group_lr = (lr, lr, lr * 0.01)  # means, opacity, SH (train.py:429-435)
-        # Gaussian ranges of the buckets (starts on 256-Gaussian multiples)
-        self.bounds = bucket_bounds(n, buckets, align=256)
+        # Gaussian ranges of the buckets (starts on 256-Gaussian multiples);
+        # one rank has no all-reduce to overlap, so one bucket
+        self.bounds = bucket_bounds(n, buckets if self.world > 1 else 1, align=256)
         self.loss_w = (l1_weight / self.world, ssim_weight / self.world, window_size)
         self.betas, self.eps = betas, eps
         self.steps_done = 0
         self._buf_key = None
+        self._args = None
 
     def _buffers(self, views):
+        """Buffers and C-call arguments for this views list (rebuilt when the
+        list object or its size changes)."""
+        import ctypes
         N = self._N
         nr, na, V = views[0].range_samples, views[0].azimuth_samples, len(views)
-        key = (nr, na, V)
+        key = (id(views), nr, na, V)
         if key != self._buf_key:
             dev = self.device
-            self.ws = torch.empty(N.workspace_bytes(self.n, nr, na, V), dtype=torch.uint8, device=dev)
-            self.sbytes = N.state_bytes(self.n, nr, na)
-            self.states = torch.empty(V * self.sbytes, dtype=torch.uint8, device=dev)
-            self.images = torch.empty((V, nr, na), dtype=torch.float32, device=dev)
-            self.grad_images = torch.empty_like(self.images)
-            self.losses = torch.empty(3, dtype=torch.float32, device=dev)
-            import ctypes
-            sz = ctypes.c_size_t()
-            N._check(N.lib().sarr_loss_workspace_size(V, nr, na, ctypes.byref(sz)),
-                     "sarr_loss_workspace_size")
-            self.loss_ws = torch.empty(max(sz.value, 256), dtype=torch.uint8, device=dev)
+            if self._buf_key is None or self._buf_key[1:] != key[1:]:
+                self.ws = torch.empty(N.workspace_bytes(self.n, nr, na, V), dtype=torch.uint8,
+                                      device=dev)
+                self.sbytes = N.state_bytes(self.n, nr, na)
+                self.states = torch.empty(V * self.sbytes, dtype=torch.uint8, device=dev)
+                self.images = torch.empty((V, nr, na), dtype=torch.float32, device=dev)
+                self.grad_images = torch.empty_like(self.images)
+                self.losses = torch.empty(3, dtype=torch.float32, device=dev)
+                sz = ctypes.c_size_t()
+                N._check(N.lib().sarr_loss_workspace_size(V, nr, na, ctypes.byref(sz)),
+                         "sarr_loss_workspace_size")
+                self.loss_ws = torch.empty(max(sz.value, 256), dtype=torch.uint8, device=dev)
+            self._vs = N._views_array(views)
+            self._views_ref = views  # keeps id(views) from being reused while cached
             self._buf_key = key
         return nr, na, V
+
+    def _call_args(self):
+        """Device pointers and per-bucket Adam ranges (built once)."""
+        import ctypes
+        if getattr(self, "_args", None) is None:
+            P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+            a = {name: P(getattr(self, name)) for name in (
+                "scales", "rotations", "cov6", "logits", "sigma", "means", "sh", "param", "grad",
+                "exp_avg", "exp_avg_sq", "g_means", "g_cov", "g_logits", "g_sh")}
+            ranges = []
+            for g0, g1 in self.bounds:
+                segs = flat_segments(self.n, self.k, g0, g1)
+                ranges.append(((ctypes.c_int64 * 3)(*[x[0] for x in segs]),
+                               (ctypes.c_int64 * 3)(*[x[1] for x in segs]),
+                               (ctypes.c_float * 3)(*[self.group_lr[x[2]] for x in segs])))
+            a["ranges"] = ranges
+            self._args = a
+        return self._args
 
     def step(self, views, targets):
         """One training step over this rank's `views` (SarrView list) against
@@ -200,42 +226,40 @@ class ViewParallelTrainer:
         loss (the mean over all ranks' views is their sum)."""
         import ctypes
         N = self._N
+        L = N.lib()
         nr, na, V = self._buffers(views)
+        A = self._call_args()
         n, k = self.n, self.k
         dev = self.device
-        st = N._stream(dev)
         P = N._ptr
+        vs, ws, wsb, states = self._vs, P(self.ws), self.ws.numel(), P(self.states)
         with torch.cuda.device(dev):
-            N._check(N.lib().sarr_gaussian_params(n, P(self.scales), P(self.rotations), P(self.cov6),
-                                                  N.SARR_COV6, P(self.logits), P(self.sigma), st),
-                     "sarr_gaussian_params")
-            vs = N._views_array(views)
-            N._check(N.lib().sarr_forward(vs, V, n, P(self.means), P(self.cov6), N.SARR_COV6,
-                                          P(self.sigma), P(self.sh), k, k, P(self.images), None,
-                                          P(self.states), P(self.ws), self.ws.numel(), st),
-                     "sarr_forward")
+            st = N._stream(dev)
+            N._check(L.sarr_gaussian_params(n, A["scales"], A["rotations"], A["cov6"], N.SARR_COV6,
+                                            A["logits"], A["sigma"], st), "sarr_gaussian_params")
+            N._check(L.sarr_forward(vs, V, n, A["means"], A["cov6"], N.SARR_COV6, A["sigma"], A["sh"],
+                                    k, k, P(self.images), None, states, ws, wsb, st), "sarr_forward")
             l1w, ssw, win = self.loss_w
-            N._check(N.lib().sarr_combined_loss(V, nr, na, P(self.images), P(targets), float(l1w),
-                                                float(ssw), int(win), 0, P(self.losses),
-                                                P(self.grad_images), P(self.loss_ws),
-                                                self.loss_ws.numel(), st), "sarr_combined_loss")
-            N._check(N.lib().sarr_backward(vs, V, n, P(self.means), P(self.cov6), N.SARR_COV6,
-                                           P(self.sigma), P(self.sh), k, k, P(self.grad_images),
-                                           P(self.states), P(self.g_means), P(self.g_cov),
-                                           N.SARR_COV6, P(self.g_logits), P(self.g_sh), k, None,
-                                           N.SARR_FLAG_TILES_ONLY, P(self.ws), self.ws.numel(), st),
-                     "sarr_backward")
+            N._check(L.sarr_combined_loss(V, nr, na, P(self.images), P(targets), float(l1w),
+                                          float(ssw), int(win), 0, P(self.losses),
+                                          P(self.grad_images), P(self.loss_ws),
+                                          self.loss_ws.numel(), st), "sarr_combined_loss")
+            N._check(L.sarr_backward(vs, V, n, A["means"], A["cov6"], N.SARR_COV6, A["sigma"],
+                                     A["sh"], k, k, P(self.grad_images), states, A["g_means"],
+                                     A["g_cov"], N.SARR_COV6, A["g_logits"], A["g_sh"], k, None,
+                                     N.SARR_FLAG_TILES_ONLY, ws, wsb, st), "sarr_backward")
             # d sigmoid(logit) / d logit = sigma (1 - sigma); the same on every
             # rank, so it may be applied before the sum over ranks
             dsig = self.sigma * (1.0 - self.sigma)
             works = []
             for g0, g1 in self.bounds:
-                N.backward_scatter(views, n, g0, g1, self.g_means, self.g_cov, N.SARR_COV6,
-                                   self.g_logits, self.g_sh, self.ws, states=self.states)
+                N._check(L.sarr_backward_scatter(vs, V, n, states, g0, g1, A["g_means"], A["g_cov"],
+                                                 N.SARR_COV6, A["g_logits"], A["g_sh"], k, None, 0,
+                                                 ws, wsb, st), "sarr_backward_scatter")
                 self.g_logits[g0:g1].mul_(dsig[g0:g1])
                 works.append(self._allreduce_bucket(g0, g1))
-        self.steps_done += 1
-        self._update(works)
+            self.steps_done += 1
+            self._update(works, st)
         return self.losses
 
     def _allreduce_bucket(self, g0, g1):
@@ -244,16 +268,19 @@ class ViewParallelTrainer:
         return [dist.all_reduce(self.grad[a:b], group=self.group, async_op=True)
                 for a, b, _ in flat_segments(self.n, self.k, g0, g1)]
 
-    def _update(self, works):
-        """Each bucket's Adam update, queued behind its all-reduces."""
+    def _update(self, works, st):
+        """Each bucket's Adam update (one launch over its means, opacity and
+        SH ranges), queued behind its all-reduces."""
         N = self._N
+        L = N.lib()
+        A = self._call_args()
         b1, b2 = self.betas
-        for i, (g0, g1) in enumerate(self.bounds):
+        for i, (begin, end, lr) in enumerate(A["ranges"]):
             for w in works[i] if works else []:
                 w.wait()  # the current stream waits for this bucket's all-reduce
-            for a, b, grp in flat_segments(self.n, self.k, g0, g1):
-                N.adam_step(self.param[a:b], self.grad[a:b], self.exp_avg[a:b], self.exp_avg_sq[a:b],
-                            [(b - a, self.group_lr[grp])], self.steps_done, b1, b2, self.eps)
+            N._check(L.sarr_adam_step_ranges(3, begin, end, lr, A["param"], A["grad"], A["exp_avg"],
+                                             A["exp_avg_sq"], float(b1), float(b2), float(self.eps),
+                                             self.steps_done, st), "sarr_adam_step_ranges")
 
     def allreduce_only(self):
         """The step's collectives alone (the same buckets, back to back), for

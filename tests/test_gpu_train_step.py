@@ -135,3 +135,25 @@ def test_split_backward_equals_single_call(nviews):
     torch.cuda.synchronize()
     for x, y in zip(a, b):
         assert torch.equal(x, y)
+
+
+def test_adam_ranges_equal_per_range_calls():
+    g = torch.Generator(device="cuda").manual_seed(86)
+    total = 20_000
+    p0 = torch.randn(total, device="cuda", generator=g)
+    grad = torch.randn(total, device="cuda", generator=g)
+    ranges = [(0, 3000, 1e-3), (12_000, 13_000, 5e-3), (16_000, 19_997, 1e-5)]
+    a, ma, va = p0.clone(), torch.zeros(total, device="cuda"), torch.zeros(total, device="cuda")
+    for lo, hi, lr in ranges:
+        _native.adam_step(a[lo:hi], grad[lo:hi], ma[lo:hi], va[lo:hi], [(hi - lo, lr)], 2)
+    b, mb, vb = p0.clone(), torch.zeros(total, device="cuda"), torch.zeros(total, device="cuda")
+    import ctypes
+    k = len(ranges)
+    st = _native.lib().sarr_adam_step_ranges(
+        k, (ctypes.c_int64 * k)(*[r[0] for r in ranges]), (ctypes.c_int64 * k)(*[r[1] for r in ranges]),
+        (ctypes.c_float * k)(*[r[2] for r in ranges]), ctypes.c_void_p(b.data_ptr()),
+        ctypes.c_void_p(grad.data_ptr()), ctypes.c_void_p(mb.data_ptr()), ctypes.c_void_p(vb.data_ptr()),
+        0.9, 0.999, 1e-8, 2, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert st == 0
+    torch.cuda.synchronize()
+    assert torch.equal(a, b) and torch.equal(ma, mb) and torch.equal(va, vb)
