@@ -51,6 +51,7 @@ typedef struct CUstream_st *sarr_stream_t;
 #define SARR_FLAG_OMEGA 1       /* workspace sizing: forward will compute Omega */
 #define SARR_FLAG_ACCUMULATE 2  /* backward: add into the gradient buffers instead of overwriting */
 #define SARR_FLAG_TILES_ONLY 4  /* backward: per-tile pass only; rows come from sarr_backward_scatter */
+#define SARR_FLAG_RANGE_ROWS 8  /* sarr_backward_scatter: the gradient arrays hold rows [begin, end) only */
 
 /*
  * One radar view. Field meaning and units follow SARRenderParams /
@@ -188,16 +189,17 @@ int sarr_adam_step(int64_t count, float *param, const float *grad, float *exp_av
 
 /*
  * sarr_adam_step over up to 8 disjoint ranges [range_begin[k], range_end[k])
- * of the same flat arrays in one launch, range k with learning rate
- * range_lr[k] (host arrays): the same update, element for element. For a
- * bucket of a flat buffer whose parameter groups are not contiguous (the
- * means, opacity and SH rows of a range of Gaussians). No reference
- * counterpart beyond sarr_adam_step's.
+ * of the flat param / exp_avg / exp_avg_sq arrays in one launch, range k with
+ * learning rate range_lr[k] and its gradient at grad[grad_begin[k] + (i -
+ * range_begin[k])] (host arrays): the same update, element for element. For
+ * a bucket of Gaussians whose parameter groups are not contiguous (their
+ * means, opacity and SH rows) and whose gradients are laid out by bucket. No
+ * reference counterpart beyond sarr_adam_step's.
  */
 int sarr_adam_step_ranges(int n_ranges, const int64_t *range_begin, const int64_t *range_end,
-                          const float *range_lr, float *param, const float *grad, float *exp_avg,
-                          float *exp_avg_sq, float beta1, float beta2, float eps, int64_t step,
-                          sarr_stream_t stream);
+                          const int64_t *grad_begin, const float *range_lr, float *param,
+                          const float *grad, float *exp_avg, float *exp_avg_sq, float beta1,
+                          float beta2, float eps, int64_t step, sarr_stream_t stream);
 
 /*
  * Densification and pruning (GaussianModel.densify_and_prune,
@@ -312,8 +314,9 @@ int sarr_backward(const sarr_view *views, int n_views, int64_t n, const float *m
  * can start reducing one range over GPUs while the next one is written.
  * Arguments: the views, n and states of the SARR_FLAG_TILES_ONLY call; the
  * gradient arrays are the full [n, ...] arrays of sarr_backward (row i at row
- * i); flags: SARR_FLAG_ACCUMULATE. The workspace must not be used by another
- * call in between.
+ * i), or with SARR_FLAG_RANGE_ROWS arrays of end - begin rows (row i at row
+ * i - begin); flags: SARR_FLAG_ACCUMULATE, SARR_FLAG_RANGE_ROWS. The
+ * workspace must not be used by another call in between.
  */
 int sarr_backward_scatter(const sarr_view *views, int n_views, int64_t n, const void *states,
                           int64_t begin, int64_t end, float *grad_means, float *grad_cov,

@@ -696,6 +696,7 @@ int sarr_backward(const sarr_view* views, int n_views, int64_t n, const float* m
     bs.entries = ia.entries;
     bs.entries_vstride = ia.entries_vstride;
     bs.heavy = reinterpret_cast<int*>(w.base + w.L.g_heavy);
+    bs.row0 = 0;
     bs.begin = 0;
     bs.end = d.n;
     e = run_kernel(kKindBwdScatter, s, [&] { return launch_bwd_scatter(bs, d, s); });
@@ -724,13 +725,14 @@ int sarr_backward_scatter(const sarr_view* views, int n_views, int64_t n, const 
   if (d.T == 0) {
     if (acc) return SARR_OK;
     const int64_t m = end - begin;
-    cudaError_t e = cudaMemsetAsync(grad_means + 3 * begin, 0, (size_t)m * 3 * 4, s);
+    const int64_t r0 = (flags & SARR_FLAG_RANGE_ROWS) ? 0 : begin;  // first row written
+    cudaError_t e = cudaMemsetAsync(grad_means + 3 * r0, 0, (size_t)m * 3 * 4, s);
     if (e == cudaSuccess)
-      e = cudaMemsetAsync(grad_cov + grad_cov_layout * begin, 0, (size_t)m * grad_cov_layout * 4, s);
-    if (e == cudaSuccess) e = cudaMemsetAsync(grad_sigma + begin, 0, (size_t)m * 4, s);
+      e = cudaMemsetAsync(grad_cov + grad_cov_layout * r0, 0, (size_t)m * grad_cov_layout * 4, s);
+    if (e == cudaSuccess) e = cudaMemsetAsync(grad_sigma + r0, 0, (size_t)m * 4, s);
     if (e == cudaSuccess)
-      e = cudaMemsetAsync(grad_sh + (size_t)grad_sh_cols * begin, 0, (size_t)m * grad_sh_cols * 4, s);
-    if (e == cudaSuccess && grad_norm) e = cudaMemsetAsync(grad_norm + begin, 0, (size_t)m * 4, s);
+      e = cudaMemsetAsync(grad_sh + (size_t)grad_sh_cols * r0, 0, (size_t)m * grad_sh_cols * 4, s);
+    if (e == cudaSuccess && grad_norm) e = cudaMemsetAsync(grad_norm + r0, 0, (size_t)m * 4, s);
     return cuda_status(e);
   }
   Ws w;
@@ -766,6 +768,7 @@ int sarr_backward_scatter(const sarr_view* views, int n_views, int64_t n, const 
   bs.entries = ia.entries;
   bs.entries_vstride = ia.entries_vstride;
   bs.heavy = reinterpret_cast<int*>(w.base + w.L.g_heavy);
+  bs.row0 = (flags & SARR_FLAG_RANGE_ROWS) ? begin : 0;
   bs.begin = begin;
   bs.end = end;
   return cuda_status(run_kernel(kKindBwdScatter, s, [&] { return launch_bwd_scatter(bs, d, s); }));

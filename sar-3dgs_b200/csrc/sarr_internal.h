@@ -380,6 +380,7 @@ struct BwdScatterArgs {
   const uint32_t* entries;
   size_t entries_vstride;  // u32 per view
   int64_t begin, end;      // the gradient rows written: Gaussians [begin, end)
+  int64_t row0;            // Gaussian i's gradient row is i - row0 (0 or begin)
   int* heavy;              // [0]: count, [1..]: Gaussians left to bwd_heavy_kernel
 };
 

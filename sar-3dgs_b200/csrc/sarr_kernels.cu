@@ -2508,7 +2508,8 @@ __device__ __forceinline__ void entry_partial(const BwdScatterArgs& a, uint32_t 
   yzr = reinterpret_cast<const float2*>(st + a.ipp.L.yz)[(size_t)t * kCap + slot];
 }
 
-__device__ __forceinline__ void write_grad_row(const BwdScatterArgs& a, int64_t i, const GradSums& g) {
+__device__ __forceinline__ void write_grad_row(const BwdScatterArgs& a, int64_t gi, const GradSums& g) {
+  const int64_t i = gi - a.row0;  // the row of Gaussian gi in the gradient arrays
   float gx = g.x, gy = g.y, gz = g.z;
   float* gm = a.grad_means + i * 3;
   if (a.accumulate) {

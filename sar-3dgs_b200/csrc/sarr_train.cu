@@ -526,7 +526,7 @@ __global__ void __launch_bounds__(kAdamThreads) adam_kernel(AdamParams A, float*
 // (grid.y = range), each with its own step size.
 struct AdamRanges {
   int n;
-  int64_t begin[kAdamMaxSegments], end[kAdamMaxSegments];
+  int64_t begin[kAdamMaxSegments], end[kAdamMaxSegments], gbegin[kAdamMaxSegments];
 };
 
 __global__ void __launch_bounds__(kAdamThreads) adam_ranges_kernel(AdamParams A, AdamRanges R,
@@ -535,12 +535,12 @@ __global__ void __launch_bounds__(kAdamThreads) adam_ranges_kernel(AdamParams A,
                                                                    float* __restrict__ m,
                                                                    float* __restrict__ v) {
   const int k = blockIdx.y;
-  const int64_t b = R.begin[k], e = R.end[k];
+  const int64_t b = R.begin[k], e = R.end[k], gshift = R.gbegin[k] - b;
   const float step_size = A.seg_step[k];
   for (int64_t i = b + (int64_t)blockIdx.x * kAdamThreads + threadIdx.x; i < e;
        i += (int64_t)gridDim.x * kAdamThreads) {
     float mi = m[i], vi = v[i];
-    param[i] = adam_elem(param[i], grad[i], mi, vi, step_size, A);
+    param[i] = adam_elem(param[i], grad[i + gshift], mi, vi, step_size, A);
     m[i] = mi;
     v[i] = vi;
   }
@@ -669,12 +669,12 @@ extern "C" int sarr_adam_step(int64_t count, float* param, const float* grad, fl
 }
 
 extern "C" int sarr_adam_step_ranges(int n_ranges, const int64_t* range_begin,
-                                     const int64_t* range_end, const float* range_lr,
-                                     float* param, const float* grad, float* exp_avg,
-                                     float* exp_avg_sq, float beta1, float beta2, float eps,
-                                     int64_t step, sarr_stream_t stream) {
+                                     const int64_t* range_end, const int64_t* grad_begin,
+                                     const float* range_lr, float* param, const float* grad,
+                                     float* exp_avg, float* exp_avg_sq, float beta1, float beta2,
+                                     float eps, int64_t step, sarr_stream_t stream) {
   if (n_ranges < 1 || n_ranges > kAdamMaxSegments || step < 1) return SARR_ERR_ARG;
-  if (!range_begin || !range_end || !range_lr) return SARR_ERR_ARG;
+  if (!range_begin || !range_end || !grad_begin || !range_lr) return SARR_ERR_ARG;
   if (!(beta1 >= 0.0f && beta1 < 1.0f && beta2 >= 0.0f && beta2 < 1.0f)) return SARR_ERR_ARG;
   if (!param || !grad || !exp_avg || !exp_avg_sq) return SARR_ERR_ARG;
   AdamParams A;
@@ -686,9 +686,10 @@ extern "C" int sarr_adam_step_ranges(int n_ranges, const int64_t* range_begin,
   int64_t longest = 0;
   R.n = n_ranges;
   for (int k = 0; k < n_ranges; ++k) {
-    if (range_begin[k] < 0 || range_end[k] < range_begin[k]) return SARR_ERR_ARG;
+    if (range_begin[k] < 0 || range_end[k] < range_begin[k] || grad_begin[k] < 0) return SARR_ERR_ARG;
     R.begin[k] = range_begin[k];
     R.end[k] = range_end[k];
+    R.gbegin[k] = grad_begin[k];
     A.seg_step[k] = (float)((double)range_lr[k] / bc1);
     if (range_end[k] - range_begin[k] > longest) longest = range_end[k] - range_begin[k];
   }

@@ -20,6 +20,7 @@ SARR_COV33 = 9
 SARR_FLAG_OMEGA = 1
 SARR_FLAG_ACCUMULATE = 2
 SARR_FLAG_TILES_ONLY = 4
+SARR_FLAG_RANGE_ROWS = 8
 SARR_L1_MODES = {"plain": 0, "linear": 1, "square": 2, "sqrt": 3}
 MAX_SH = 16
 
@@ -84,7 +85,8 @@ def _declare(L):
     L.sarr_adam_step.argtypes = [I64, P, P, P, P, I, ctypes.POINTER(I64), ctypes.POINTER(F), F, F,
                                  F, I64, P]
     L.sarr_adam_step_ranges.argtypes = [I, ctypes.POINTER(I64), ctypes.POINTER(I64),
-                                        ctypes.POINTER(F), P, P, P, P, F, F, F, I64, P]
+                                        ctypes.POINTER(I64), ctypes.POINTER(F), P, P, P, P, F, F,
+                                        F, I64, P]
     L.sarr_densify_workspace_size.argtypes = [I64, ctypes.POINTER(SZ)]
     L.sarr_densify_flags.argtypes = [I64, P, P, P, F, F, F, F, P, P, SZ, P]
     L.sarr_densify_apply.argtypes = [I64, P, P, P, P, P, I, P, P, I, I, P, P, P, P, P, P, SZ, P]
@@ -257,17 +259,18 @@ def backward(views, means, cov, layout, sigma, sh, sh_stride, sh_k, grad_images,
 
 
 def backward_scatter(views, n, begin, end, grad_means, grad_cov, grad_cov_layout, grad_sigma,
-                     grad_sh, ws, states=None, grad_norm=None, accumulate=False):
+                     grad_sh, ws, states=None, grad_norm=None, accumulate=False, range_rows=False):
     """sarr_backward_scatter: gradient rows [begin, end) after a tiles_only
-    backward of the same views on `ws`."""
+    backward of the same views on `ws` (range_rows: the arrays hold only those
+    rows)."""
     dev = grad_means.device
     with torch.cuda.device(dev):
         _check(lib().sarr_backward_scatter(
             _views_array(views), len(views), n, _ptr(states), int(begin), int(end), _ptr(grad_means),
             _ptr(grad_cov), grad_cov_layout, _ptr(grad_sigma), _ptr(grad_sh),
             grad_sh.shape[1] if grad_sh.dim() == 2 else 16, _ptr(grad_norm),
-            SARR_FLAG_ACCUMULATE if accumulate else 0, _ptr(ws), ws.numel(), _stream(dev)),
-            "sarr_backward_scatter")
+            (SARR_FLAG_ACCUMULATE if accumulate else 0) | (SARR_FLAG_RANGE_ROWS if range_rows else 0),
+            _ptr(ws), ws.numel(), _stream(dev)), "sarr_backward_scatter")
 
 
 def debug_preprocess(view, means, cov, layout, sigma, sh, sh_stride, sh_k):

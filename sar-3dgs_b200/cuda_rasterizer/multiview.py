@@ -116,17 +116,20 @@ class ViewParallelTrainer:
       4. backward of the views reusing the states: the per-tile pass
          (sarr_backward with SARR_FLAG_TILES_ONLY), then, bucket by bucket
          of `buckets` Gaussian ranges, the dense gradient rows of the range
-         written straight into a flat gradient buffer
-         (sarr_backward_scatter), the transmittance gradient chained through
-         the sigmoid, and the range's NCCL all-reduces issued (async), so
-         that the all-reduce of bucket b overlaps the rows of bucket b + 1;
+         written straight into the bucket's part of the gradient buffer
+         (sarr_backward_scatter with SARR_FLAG_RANGE_ROWS), the
+         transmittance gradient chained through the sigmoid, and the
+         bucket's NCCL all-reduce issued (async), so that the all-reduce of
+         bucket b overlaps the rows of bucket b + 1;
       5. each bucket's Adam update (sarr_adam_step) queued behind its own
          all-reduce.
 
     Trainable parameters (the ones that receive gradients in SAR-3DGS: means,
     opacity logits, SH) live in one flat fp32 buffer laid out as
-    means [n,3] | logits [n] | SH [n,K], with gradients and Adam moments in
-    the same layout; log-scales and quaternions are held but get no gradient
+    means [n,3] | logits [n] | SH [n,K], with the Adam moments in the same
+    layout and the gradients bucket by bucket (each bucket's means, logits
+    and SH rows contiguous; `gradients()` gives them in the parameter
+    layout); log-scales and quaternions are held but get no gradient
     (the covariance is detached, gaussian_model.py:306-315), so Adam leaves
     them alone as torch.optim.Adam does for parameters without gradients.
     Learning rates per group follow train.py:429-435 (lr for means and
@@ -156,10 +159,6 @@ class ViewParallelTrainer:
         self.sh.copy_(sh)
         self.scales = scales_log.detach().contiguous().clone()
         self.rotations = rotations.detach().contiguous().clone()
-        self.grad = torch.zeros_like(self.param)
-        self.g_means = self.grad[:3 * n].view(n, 3)
-        self.g_logits = self.grad[3 * n:4 * n]
-        self.g_sh = self.grad[4 * n:].view(n, k)
         self.exp_avg = torch.zeros_like(self.param)
         self.exp_avg_sq = torch.zeros_like(self.param)
         self.g_cov = torch.empty((n, 6), dtype=torch.float32, device=dev)  # reaches no parameter
@@ -169,6 +168,17 @@ class ViewParallelTrainer:
         # Gaussian ranges of the buckets (starts on 256-Gaussian multiples);
         # one rank has no all-reduce to overlap, so one bucket
         self.bounds = bucket_bounds(n, buckets if self.world > 1 else 1, align=256)
+        # gradients laid out by bucket: bucket b = its Gaussians' means rows |
+        # logits | SH rows, contiguous, so that one all-reduce covers it
+        self.grad = torch.zeros_like(self.param)
+        self.gparts = []  # per bucket: (offset, means [nb,3], logits [nb], SH [nb,K], whole)
+        o = 0
+        for g0, g1 in self.bounds:
+            nb = g1 - g0
+            self.gparts.append((o, self.grad[o:o + 3 * nb].view(nb, 3), self.grad[o + 3 * nb:o + 4 * nb],
+                                self.grad[o + 4 * nb:o + (4 + k) * nb].view(nb, k),
+                                self.grad[o:o + (4 + k) * nb]))
+            o += (4 + k) * nb
         self.loss_w = (l1_weight / self.world, ssim_weight / self.world, window_size)
         self.betas, self.eps = betas, eps
         self.steps_done = 0
@@ -208,14 +218,18 @@ class ViewParallelTrainer:
             P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
             a = {name: P(getattr(self, name)) for name in (
                 "scales", "rotations", "cov6", "logits", "sigma", "means", "sh", "param", "grad",
-                "exp_avg", "exp_avg_sq", "g_means", "g_cov", "g_logits", "g_sh")}
-            ranges = []
-            for g0, g1 in self.bounds:
+                "exp_avg", "exp_avg_sq", "g_cov")}
+            ranges, gptr = [], []
+            for (g0, g1), (o, gm, gl, gsh, _) in zip(self.bounds, self.gparts):
+                nb = g1 - g0
                 segs = flat_segments(self.n, self.k, g0, g1)
                 ranges.append(((ctypes.c_int64 * 3)(*[x[0] for x in segs]),
                                (ctypes.c_int64 * 3)(*[x[1] for x in segs]),
+                               (ctypes.c_int64 * 3)(o, o + 3 * nb, o + 4 * nb),
                                (ctypes.c_float * 3)(*[self.group_lr[x[2]] for x in segs])))
+                gptr.append((P(gm), P(gl), P(gsh)))
             a["ranges"] = ranges
+            a["gptr"] = gptr
             self._args = a
         return self._args
 
@@ -244,29 +258,36 @@ class ViewParallelTrainer:
                                           float(ssw), int(win), 0, P(self.losses),
                                           P(self.grad_images), P(self.loss_ws),
                                           self.loss_ws.numel(), st), "sarr_combined_loss")
+            gm0, gl0, gsh0 = A["gptr"][0]
             N._check(L.sarr_backward(vs, V, n, A["means"], A["cov6"], N.SARR_COV6, A["sigma"],
-                                     A["sh"], k, k, P(self.grad_images), states, A["g_means"],
-                                     A["g_cov"], N.SARR_COV6, A["g_logits"], A["g_sh"], k, None,
-                                     N.SARR_FLAG_TILES_ONLY, ws, wsb, st), "sarr_backward")
+                                     A["sh"], k, k, P(self.grad_images), states, gm0, A["g_cov"],
+                                     N.SARR_COV6, gl0, gsh0, k, None, N.SARR_FLAG_TILES_ONLY, ws, wsb,
+                                     st), "sarr_backward")
             # d sigmoid(logit) / d logit = sigma (1 - sigma); the same on every
             # rank, so it may be applied before the sum over ranks
             dsig = self.sigma * (1.0 - self.sigma)
             works = []
-            for g0, g1 in self.bounds:
-                N._check(L.sarr_backward_scatter(vs, V, n, states, g0, g1, A["g_means"], A["g_cov"],
-                                                 N.SARR_COV6, A["g_logits"], A["g_sh"], k, None, 0,
-                                                 ws, wsb, st), "sarr_backward_scatter")
-                self.g_logits[g0:g1].mul_(dsig[g0:g1])
-                works.append(self._allreduce_bucket(g0, g1))
+            for b, (g0, g1) in enumerate(self.bounds):
+                gm, gl, gsh = A["gptr"][b]
+                N._check(L.sarr_backward_scatter(vs, V, n, states, g0, g1, gm, A["g_cov"], N.SARR_COV6,
+                                                 gl, gsh, k, None, N.SARR_FLAG_RANGE_ROWS, ws, wsb,
+                                                 st), "sarr_backward_scatter")
+                self.gparts[b][2].mul_(dsig[g0:g1])
+                works.append(self._allreduce_bucket(b))
             self.steps_done += 1
             self._update(works, st)
         return self.losses
 
-    def _allreduce_bucket(self, g0, g1):
+    def _allreduce_bucket(self, b):
         if self.world == 1:
             return []
-        return [dist.all_reduce(self.grad[a:b], group=self.group, async_op=True)
-                for a, b, _ in flat_segments(self.n, self.k, g0, g1)]
+        return [dist.all_reduce(self.gparts[b][4], group=self.group, async_op=True)]
+
+    def gradients(self):
+        """The last step's gradients (summed over the ranks) in the parameter
+        layout: (means [n,3], opacity logits [n], SH [n,K])."""
+        return (torch.cat([p[1] for p in self.gparts]), torch.cat([p[2] for p in self.gparts]),
+                torch.cat([p[3] for p in self.gparts]))
 
     def _update(self, works, st):
         """Each bucket's Adam update (one launch over its means, opacity and
@@ -275,17 +296,18 @@ class ViewParallelTrainer:
         L = N.lib()
         A = self._call_args()
         b1, b2 = self.betas
-        for i, (begin, end, lr) in enumerate(A["ranges"]):
+        for i, (begin, end, gbegin, lr) in enumerate(A["ranges"]):
             for w in works[i] if works else []:
                 w.wait()  # the current stream waits for this bucket's all-reduce
-            N._check(L.sarr_adam_step_ranges(3, begin, end, lr, A["param"], A["grad"], A["exp_avg"],
-                                             A["exp_avg_sq"], float(b1), float(b2), float(self.eps),
-                                             self.steps_done, st), "sarr_adam_step_ranges")
+            N._check(L.sarr_adam_step_ranges(3, begin, end, gbegin, lr, A["param"], A["grad"],
+                                             A["exp_avg"], A["exp_avg_sq"], float(b1), float(b2),
+                                             float(self.eps), self.steps_done, st),
+                     "sarr_adam_step_ranges")
 
     def allreduce_only(self):
         """The step's collectives alone (the same buckets, back to back), for
         measuring their cost; a no-op on one rank."""
         if self.world > 1:
-            works = [w for g0, g1 in self.bounds for w in self._allreduce_bucket(g0, g1)]
+            works = [w for b in range(len(self.bounds)) for w in self._allreduce_bucket(b)]
             for w in works:
                 w.wait()

@@ -77,8 +77,10 @@ def _worker(rank, world, port, q):
         tr.step(vs[a:b], targets[a:b])
         one.step(vs, targets)
         torch.cuda.synchronize()
-        errs.append(_rel(tr.grad, one.grad))
-        big = one.grad.abs() > 1e-3 * one.grad.abs().max()
+        g_tr = torch.cat([x.reshape(-1) for x in tr.gradients()])
+        g_one = torch.cat([x.reshape(-1) for x in one.gradients()])
+        errs.append(_rel(g_tr, g_one))
+        big = g_one.abs() > 1e-3 * g_one.abs().max()  # the parameter layout, as tr.param
         errs.append(_rel((tr.param - p0)[big], (one.param - p0)[big]))
         tr.step(vs[a:b], targets[a:b])
         torch.cuda.synchronize()

@@ -135,6 +135,14 @@ def test_split_backward_equals_single_call(nviews):
     torch.cuda.synchronize()
     for x, y in zip(a, b):
         assert torch.equal(x, y)
+    # the same rows into arrays that hold only the range (SARR_FLAG_RANGE_ROWS)
+    lo, hi = 1000, 77_777
+    r = [t[:hi - lo].clone().fill_(float("nan")) for t in grads()]
+    _native.backward_scatter(views, n, lo, hi, r[0], r[1], _native.SARR_COV6, r[2], r[3], ws,
+                             grad_norm=r[4], range_rows=True)
+    torch.cuda.synchronize()
+    for x, y in zip(a, r):
+        assert torch.equal(x[lo:hi], y)
 
 
 def test_adam_ranges_equal_per_range_calls():
@@ -149,11 +157,15 @@ def test_adam_ranges_equal_per_range_calls():
     b, mb, vb = p0.clone(), torch.zeros(total, device="cuda"), torch.zeros(total, device="cuda")
     import ctypes
     k = len(ranges)
+    # the gradients of the ranges packed back to back in another array
+    packed = torch.cat([grad[lo:hi] for lo, hi, _ in ranges])
+    gb = [0, 3000, 4000]
     st = _native.lib().sarr_adam_step_ranges(
         k, (ctypes.c_int64 * k)(*[r[0] for r in ranges]), (ctypes.c_int64 * k)(*[r[1] for r in ranges]),
-        (ctypes.c_float * k)(*[r[2] for r in ranges]), ctypes.c_void_p(b.data_ptr()),
-        ctypes.c_void_p(grad.data_ptr()), ctypes.c_void_p(mb.data_ptr()), ctypes.c_void_p(vb.data_ptr()),
-        0.9, 0.999, 1e-8, 2, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+        (ctypes.c_int64 * k)(*gb), (ctypes.c_float * k)(*[r[2] for r in ranges]),
+        ctypes.c_void_p(b.data_ptr()), ctypes.c_void_p(packed.data_ptr()), ctypes.c_void_p(mb.data_ptr()),
+        ctypes.c_void_p(vb.data_ptr()), 0.9, 0.999, 1e-8, 2,
+        ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
     assert st == 0
     torch.cuda.synchronize()
     assert torch.equal(a, b) and torch.equal(ma, mb) and torch.equal(va, vb)
