@@ -91,7 +91,17 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-train", action="store_true", help="skip fwd_bwd, train_step, train_configs")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--sections", default="all",
+                    help="comma-separated subset of forward,e2e,omega,fwd_bwd,train_step,"
+                         "train_configs,train_ops,cpu (default all; without forward the line "
+                         "carries no headline value, for profiling runs)")
     return ap.parse_args()
+
+
+def wanted(args, name):
+    if args.sections == "all":
+        return True
+    return name in args.sections.split(",")
 
 
 def peaks():
@@ -849,6 +859,18 @@ def main():
             d.close()
         return
     d = Dist()
+    if not wanted(args, "forward"):
+        # a profiling run of some sections only (no headline value)
+        flush = torch.empty((512 << 20) // 4, dtype=torch.float32, device=d.device)
+        line = {"metric": METRIC, "sections": args.sections, "n_gpus": d.world}
+        if wanted(args, "train_step"):
+            line["train_step"] = bench_train_step(args, d, flush)
+        if wanted(args, "train_configs") and d.world == 1:
+            line["train_configs"] = bench_train_configs(args, d, flush)
+        if d.rank == 0:
+            print(json.dumps(line))
+        d.close()
+        return
     r = bench_forward(args, d)
     line = {"metric": METRIC, "value": r["value"], "unit": "views/s", "n_gpus": d.world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": r["ms_per_step"],
@@ -858,18 +880,23 @@ def main():
             "path_roofline": r["path_roofline"], "render_issue": r["render_issue"],
             "kernels": r["kernels"], "image_checksum": r["checksum"][0],
             "image_sha1": r["checksum"][1], "image_checksum_stable": r["checksum_stable"]}
-    if not args.no_e2e:
+    if not args.no_e2e and wanted(args, "e2e"):
         line["e2e"] = bench_e2e(args, d, r["sc"], r["views"])
-    line["omega"] = bench_omega(args, d, r["inputs"], r["views"], r["flush"])
+    if wanted(args, "omega"):
+        line["omega"] = bench_omega(args, d, r["inputs"], r["views"], r["flush"])
     if not args.no_train:
-        line["fwd_bwd"] = bench_fwd_bwd(args, d, r["inputs"], r["views"], r["flush"])
+        if wanted(args, "fwd_bwd"):
+            line["fwd_bwd"] = bench_fwd_bwd(args, d, r["inputs"], r["views"], r["flush"])
         flush = r["flush"]
         del r
-        line["train_step"] = bench_train_step(args, d, flush)
+        if wanted(args, "train_step"):
+            line["train_step"] = bench_train_step(args, d, flush)
         if d.world == 1:
-            line["train_configs"] = bench_train_configs(args, d, flush)
-            line["train_ops"] = bench_train_ops(args, d)
-    if d.rank == 0 and d.world == 1 and not args.no_cpu:
+            if wanted(args, "train_configs"):
+                line["train_configs"] = bench_train_configs(args, d, flush)
+            if wanted(args, "train_ops"):
+                line["train_ops"] = bench_train_ops(args, d)
+    if d.rank == 0 and d.world == 1 and not args.no_cpu and wanted(args, "cpu"):
         line["cpu_baseline"] = cpu_baseline(args)
     if d.rank == 0:
         print(json.dumps(line))

@@ -371,7 +371,7 @@ cudaError_t run_selection(const Dims& d, const Ws& w, int gv, const float* means
       ct.ipp = ipp;
       ct.sparse_from = (int64_t)prefix * kChunk;
       ct.n = d.n;
-      e = run_kernel(kKindAux, s, [&] { return launch_cell_test(ct, gv, s); });
+      e = run_kernel(kKindAux, s, [&] { return launch_cell_test(ct, d, gv, s); });
       if (e != cudaSuccess) return e;
       ba.chunks = d.C - prefix;
       ba.grid = ct.grid;
@@ -382,7 +382,7 @@ cudaError_t run_selection(const Dims& d, const Ws& w, int gv, const float* means
       ba.bits = ct.bits;
       ba.bits_vstride = ct.bits_vstride;
 
-      e = run_kernel(kKindBinSkip, s, [&] { return launch_bin_cand(ba, shr != nullptr, s); });
+      e = run_kernel(kKindBinSkip, s, [&] { return launch_bin_cand(ba, d, shr != nullptr, s); });
       if (e != cudaSuccess) return e;
       e = run_kernel(kKindBinFinalize, s, [&] { return launch_bin_finalize(ba, d, shr != nullptr, s); });
       if (e != cudaSuccess) return e;

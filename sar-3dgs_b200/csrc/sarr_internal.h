@@ -429,10 +429,10 @@ cudaError_t launch_bin(const BinArgs& a, const Dims& d, int chunks, bool shadow,
 cudaError_t launch_open_table(const OpenArgs& a, int nviews, int nlists, cudaStream_t s);
 // view-independent cell grid of one call (four kernels)
 cudaError_t launch_cell_prep(const CellPrepArgs& a, cudaStream_t s);
-cudaError_t launch_cell_test(const CellTestArgs& a, int nviews, cudaStream_t s);
+cudaError_t launch_cell_test(const CellTestArgs& a, const Dims& d, int nviews, cudaStream_t s);
 // cell binning of the a.chunks chunks from a.chunk_offset: bin_cand_kernel
 // (candidate cells' members), then bin_finalize_kernel (per chunk)
-cudaError_t launch_bin_cand(const BinArgs& a, bool shadow, cudaStream_t s);
+cudaError_t launch_bin_cand(const BinArgs& a, const Dims& d, bool shadow, cudaStream_t s);
 cudaError_t launch_bin_finalize(const BinArgs& a, const Dims& d, bool shadow, cudaStream_t s);
 bool bin_cell_supported(const Dims& d);
 // true when the skipping binner keeps per-warp counters (and records the

@@ -88,6 +88,32 @@ __device__ __forceinline__ int open_in_rect(uint32_t rc, const int* __restrict__
          __ldg(tab + tr1 * pitch + tc0) + __ldg(tab + tr0 * pitch + tc0);
 }
 
+// open_in_rect on a table staged in shared memory.
+__device__ __forceinline__ int open_in_rect_s(uint32_t rc, const int* tab, int pitch) {
+  if (rc == kEmptyRect) return 0;
+  const int tc0 = rc & 0xFF, tc1 = ((rc >> 8) & 0xFF) + 1, tr0 = (rc >> 16) & 0xFF, tr1 = (rc >> 24) + 1;
+  return tab[tr1 * pitch + tc1] - tab[tr0 * pitch + tc1] - tab[tr1 * pitch + tc0] + tab[tr0 * pitch + tc0];
+}
+
+// The view's open-tile tables (image list, then shadow list when `lists` is
+// 2) copied into shared memory by the whole CTA; ends with a barrier.
+__device__ __forceinline__ void stage_open_tables(int* s_tab, const int* open_ipp, const int* open_sh,
+                                                  int size, int lists) {
+  for (int e = threadIdx.x; e < size; e += blockDim.x) {
+    s_tab[e] = open_ipp[e];
+    if (lists > 1) s_tab[size + e] = open_sh[e];
+  }
+  __syncthreads();
+}
+
+// Shared memory for the staged open tables of one view (0: read them from
+// global memory instead).
+constexpr size_t kOpenStageMaxBytes = 16384;
+static size_t open_stage_bytes(int tiles_x, int tiles_y, int lists) {
+  const size_t b = (size_t)(tiles_x + 1) * (tiles_y + 1) * 4 * lists;
+  return b <= kOpenStageMaxBytes ? b : 0;
+}
+
 // ORs `bit` into the mask of every tile of a rectangle.
 __device__ __forceinline__ void mark_rect(uint32_t* mask, uint32_t rc, int tiles_x, uint32_t bit) {
   if (rc == kEmptyRect) return;
@@ -931,13 +957,19 @@ __global__ void __launch_bounds__(256) cell_fill_kernel(const CellPrepArgs a) {
 // within half_diag of the cell centre q; R_min and X_r are 1-Lipschitz in the
 // world position, so its exact image centre lies within half_diag / rho
 // (pixels) of q's, and approximate-centre errors add center_margin at p and q.
+template <bool kStaged>
 __global__ void __launch_bounds__(256) cell_test_kernel(const CellTestArgs a) {
   // one thread per spatial cell: its centre is projected once and tested
   // with the bound of each of its kHbBuckets cells c = spatial * 4 + bucket
   static_assert(kHbBuckets == 4, "a lane assembles one 4-bit nibble of the cell bitmap");
+  extern __shared__ int s_open[];
   const int sc = blockIdx.x * 256 + threadIdx.x, lane = threadIdx.x & 31;
   const int v = blockIdx.y;
   const SceneGrid& g = *a.grid;
+  const int tsize = (a.views[v].tiles_x + 1) * (a.views[v].tiles_y + 1);
+  if (kStaged)
+    stage_open_tables(s_open, a.open_ipp + v * a.open_vstride, a.open_sh + v * a.open_vstride, tsize,
+                      a.shadow ? 2 : 1);
   uint32_t nib = 0;
   if (g.valid && sc * kHbBuckets < g.ncells) {
     const ViewConst& vc = a.views[v];
@@ -956,9 +988,12 @@ __global__ void __launch_bounds__(256) cell_test_kernel(const CellTestArgs a) {
       const float hbm = key_float(a.cell_hb[c]);
       if (!(hbm >= 0.0f)) continue;
       const float base = hbm + 2.0f * vc.center_margin + 0.02f;
-      bool open = open_in_rect(bound_rect2(r, cc, base + dr, base + dc, Nr, Na), open_ipp, pitch) > 0;
-      if (a.shadow && !open)
-        open = open_in_rect(bound_rect2(yr, xr, base + ds, base + ds, Nr, Na), open_sh, pitch) > 0;
+      const uint32_t ri = bound_rect2(r, cc, base + dr, base + dc, Nr, Na);
+      bool open = (kStaged ? open_in_rect_s(ri, s_open, pitch) : open_in_rect(ri, open_ipp, pitch)) > 0;
+      if (a.shadow && !open) {
+        const uint32_t rs = bound_rect2(yr, xr, base + ds, base + ds, Nr, Na);
+        open = (kStaged ? open_in_rect_s(rs, s_open + tsize, pitch) : open_in_rect(rs, open_sh, pitch)) > 0;
+      }
       if (open) nib |= 1u << b;
     }
   }
@@ -983,12 +1018,17 @@ __global__ void __launch_bounds__(256) cell_test_kernel(const CellTestArgs a) {
 // the 32 cells of one bitmap word, or a stride of the no-cell list.
 constexpr int kAlwaysBlocks = 64;
 
-template <bool kShadow>
+template <bool kShadow, bool kStaged>
 __global__ void __launch_bounds__(kBinThreads) bin_cand_kernel(const BinArgs a) {
   constexpr int kWarps = kBinThreads / 32;
+  extern __shared__ int s_open[];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int v = blockIdx.y;
   const SceneGrid& g = *a.grid;
+  const int tsize = (a.views[v].tiles_x + 1) * (a.views[v].tiles_y + 1);
+  if (kStaged && (int)blockIdx.x < kMaxCells / (kWarps * 32))
+    stage_open_tables(s_open, a.open_ipp + v * a.open_vstride, a.open_sh + v * a.open_vstride, tsize,
+                      kShadow ? 2 : 1);
   uint32_t* xbits = reinterpret_cast<uint32_t*>(a.ipp.base + v * a.ipp.vstride + a.ipp.L.xbits);
   const int cell_blocks = kMaxCells / (kWarps * 32);
   if ((int)blockIdx.x < cell_blocks) {
@@ -1027,8 +1067,12 @@ __global__ void __launch_bounds__(kBinThreads) bin_cand_kernel(const BinArgs a) 
         float r, cc, xr, yr;
         approx_center(vc, p4.x, p4.y, p4.z, r, cc, xr, yr);
         const float h = p4.w + vc.center_margin;
-        bool exact = open_in_rect(bound_rect(r, cc, h, Nr, Na), open_ipp, pitch) != 0;
-        if (kShadow && !exact) exact = open_in_rect(bound_rect(yr, xr, h, Nr, Na), open_sh, pitch) != 0;
+        const uint32_t ri = bound_rect(r, cc, h, Nr, Na);
+        bool exact = (kStaged ? open_in_rect_s(ri, s_open, pitch) : open_in_rect(ri, open_ipp, pitch)) != 0;
+        if (kShadow && !exact) {
+          const uint32_t rs = bound_rect(yr, xr, h, Nr, Na);
+          exact = (kStaged ? open_in_rect_s(rs, s_open + tsize, pitch) : open_in_rect(rs, open_sh, pitch)) != 0;
+        }
         if (exact) {
           const int j = a.mem_idx[m];
           atomicOr(xbits + (j >> 5), 1u << (j & 31));
@@ -1943,12 +1987,13 @@ __device__ __forceinline__ uint64_t block_hits(const Rec* recs, int count, float
 // compositing, so visiting only the marked records, in list order, leaves
 // each pixel's arithmetic the reference's, record by record.
 //
-// kPix pixels per lane: 2 for launches of many views (4 warps per tile, fewer
-// per-record overheads), 1 for a few views (8 warps per tile, more warps in
-// flight when the grid is small).
+// kPix pixels per lane: 4 for launches of many views (2 warps per tile, each
+// an 8 x 16 block: the per-record overheads spread over four pixels; 1.62 ->
+// 1.51 ms per 1024 views against 2 pixels), 1 for a few views (8 warps per
+// tile, more warps in flight when the grid is small).
 template <int kPix>
-__global__ void __launch_bounds__(kPix == 2 ? 128 : 256) render_kernel(const TileArgs a) {
-  constexpr int kWarps = kPix == 2 ? 4 : 8;
+__global__ void __launch_bounds__(kTile * kTile / kPix) render_kernel(const TileArgs a) {
+  constexpr int kWarps = kTile * kTile / kPix / 32;
   __shared__ __align__(16) Rec s_rec[kCap];
   __shared__ float2 s_cut[kWarps][kCap];
   __shared__ uint64_t bar;
@@ -2438,9 +2483,8 @@ __global__ void __launch_bounds__(kGatherScanThreads) gather_scan_apply_kernel(c
 // bwd_scatter_kernel takes the Gaussians with at most kScatterLocalEntries
 // entries, one thread each; the others (the lowest-index Gaussians fill most
 // tile lists, so they have one entry per listing tile of every view) go to
-// bwd_heavy_kernel, one CTA each.
+// bwd_heavy_kernel, one warp each.
 constexpr int kScatterLocalEntries = 16;
-constexpr int kHeavyThreads = 256;
 
 // One view's contribution: its partial sums A[0..4] and the means chain.
 struct ViewContrib {
@@ -2637,92 +2681,101 @@ __global__ void __launch_bounds__(256) bwd_scatter_kernel(const BwdScatterArgs a
   write_grad_row(a, i, g);
 }
 
-// Groups of at most 32 views: one warp per Gaussian left by
-// bwd_scatter_kernel, lane v for view v, otherwise as bwd_heavy_kernel.
-constexpr int kHeavyWarpViews = 32;
-constexpr int kHeavyViewEntriesW = 32;
+// One warp per Gaussian left by bwd_scatter_kernel (8 per CTA, persistent
+// over the list). The group's views are taken in blocks of 32, lane l for
+// view 32 j + l of block j: every lane reads the Gaussian's entries (the same
+// entry at the same time), keeps those of its view, orders them by tile and
+// sums their partials, and applies the view's chain rule; then 23 lanes, one
+// per output sum, add the block's view contributions in view order. A view
+// with more than kHeavyViewEntries listing tiles of the Gaussian (a bbox
+// wider than ~80 pixels) takes them in order by repeated selection.
+constexpr int kHeavyViewEntries = 32;
+constexpr int kHeavyWarps = 8;
 
-__global__ void __launch_bounds__(256) bwd_heavy_warp_kernel(const BwdScatterArgs a) {
-  constexpr int kWarps = 8;
-  __shared__ ViewContrib s_con[kWarps][32];
-  __shared__ int s_has[kWarps][32];
-  __shared__ float s_out[kWarps][23];
+__device__ __forceinline__ uint32_t entry_at(const BwdScatterArgs& a, int per_view, int64_t e) {
+  return a.entries[(size_t)(e / per_view) * a.entries_vstride + (size_t)(e % per_view)];
+}
+
+__global__ void __launch_bounds__(kHeavyWarps * 32) bwd_heavy_kernel(const BwdScatterArgs a) {
+  __shared__ ViewContrib s_con[kHeavyWarps][32];
+  __shared__ int s_has[kHeavyWarps][32];
+  __shared__ float s_out[kHeavyWarps][23];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int count = a.heavy[0];
   const int nviews = a.nviews;
   const int per_view = a.views[0].tiles_x * a.views[0].tiles_y * kCap;
-  for (int h = blockIdx.x * kWarps + warp; h < count; h += gridDim.x * kWarps) {
+  for (int h = blockIdx.x * kHeavyWarps + warp; h < count; h += gridDim.x * kHeavyWarps) {
     const int64_t i = a.heavy[1 + h];
     const int e0 = a.start[i], c = a.start[i + 1] - e0;
-    uint32_t key[kHeavyViewEntriesW];
-    int m = 0;
-    {
-      const int per = per_view;
-      int slice = e0 / per, off = e0 % per;
-      for (int q = 0; q < c; ++q) {
-        const uint32_t k = a.entries[(size_t)slice * a.entries_vstride + off];
-        if (++off == per) {
-          off = 0;
-          ++slice;
-        }
-        if ((int)(k >> 24) == lane) {
-          if (m < kHeavyViewEntriesW) key[m] = k;
-          ++m;
+    float acc = 0.f;  // output sum `lane` (lanes < 23)
+    for (int vb = 0; vb < nviews; vb += 32) {
+      const int v = vb + lane;
+      uint32_t key[kHeavyViewEntries];
+      int m = 0;
+      {
+        int slice = e0 / per_view, off = e0 % per_view;
+        for (int q = 0; q < c; ++q) {
+          const uint32_t k = a.entries[(size_t)slice * a.entries_vstride + off];
+          if (++off == per_view) {
+            off = 0;
+            ++slice;
+          }
+          if ((int)(k >> 24) == v) {
+            if (m < kHeavyViewEntries) key[m] = k;
+            ++m;
+          }
         }
       }
-    }
-    s_has[warp][lane] = 0;
-    if (lane < nviews && m > 0) {
-      float A[7] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      float2 yzr = make_float2(0.f, 0.f);
-      if (m <= kHeavyViewEntriesW) {
-        for (int q = 1; q < m; ++q) {  // insertion sort by tile
-          const uint32_t x = key[q];
-          int r = q - 1;
-          while (r >= 0 && key[r] > x) {
-            key[r + 1] = key[r];
-            --r;
-          }
-          key[r + 1] = x;
-        }
-        for (int q = 0; q < m; ++q) entry_partial(a, key[q], A, yzr);
-      } else {
-        uint32_t last = 0;
-        for (int q = 0; q < m; ++q) {
-          uint32_t k = 0xFFFFFFFFu;
-          int slice = e0 / per_view, off = e0 % per_view;
-          for (int r = 0; r < c; ++r) {
-            const uint32_t x = a.entries[(size_t)slice * a.entries_vstride + off];
-            if (++off == per_view) {
-              off = 0;
-              ++slice;
+      s_has[warp][lane] = 0;
+      if (v < nviews && m > 0) {
+        float A[7] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        float2 yzr = make_float2(0.f, 0.f);
+        if (m <= kHeavyViewEntries) {
+          for (int q = 1; q < m; ++q) {  // insertion sort by tile
+            const uint32_t x = key[q];
+            int r = q - 1;
+            while (r >= 0 && key[r] > x) {
+              key[r + 1] = key[r];
+              --r;
             }
-            if ((int)(x >> 24) == lane && (q == 0 || x > last) && x < k) k = x;
+            key[r + 1] = x;
           }
-          last = k;
-          entry_partial(a, k, A, yzr);
+          for (int q = 0; q < m; ++q) entry_partial(a, key[q], A, yzr);
+        } else {
+          uint32_t last = 0;
+          for (int q = 0; q < m; ++q) {
+            uint32_t k = 0xFFFFFFFFu;
+            for (int r = 0; r < c; ++r) {
+              const uint32_t x = entry_at(a, per_view, (int64_t)e0 + r);
+              if ((int)(x >> 24) == v && (q == 0 || x > last) && x < k) k = x;
+            }
+            last = k;
+            entry_partial(a, k, A, yzr);
+          }
+        }
+        s_con[warp][lane] = bwd_view_contrib(a.views[v], A, yzr);
+        s_has[warp][lane] = 1;
+      }
+      __syncwarp();
+      if (lane < 23) {
+        // output sum lane: 0 sigma, 1..16 SH, 17 rr, 18 cc, 19 rc, 20..22 x y z
+        const int ub = min(32, nviews - vb);
+        for (int u = 0; u < ub; ++u) {
+          if (!s_has[warp][u]) continue;
+          const ViewContrib& cv = s_con[warp][u];
+          if (lane == 0) acc = __fadd_rn(acc, cv.a0);
+          else if (lane <= kSh) acc = __fmaf_rn(cv.a1, a.views[vb + u].h.sh_basis[lane - 1], acc);
+          else if (lane == 17) acc = __fadd_rn(acc, cv.a2);
+          else if (lane == 18) acc = __fadd_rn(acc, cv.a3);
+          else if (lane == 19) acc = __fadd_rn(acc, cv.a4);
+          else if (lane == 20) acc = __fadd_rn(acc, cv.cx);
+          else if (lane == 21) acc = __fadd_rn(acc, cv.cy);
+          else acc = __fadd_rn(acc, cv.cz);
         }
       }
-      s_con[warp][lane] = bwd_view_contrib(a.views[lane], A, yzr);
-      s_has[warp][lane] = 1;
+      __syncwarp();
     }
-    __syncwarp();
-    if (lane < 23) {
-      float acc = 0.f;
-      for (int v = 0; v < nviews; ++v) {
-        if (!s_has[warp][v]) continue;
-        const ViewContrib& cv = s_con[warp][v];
-        if (lane == 0) acc = __fadd_rn(acc, cv.a0);
-        else if (lane <= kSh) acc = __fmaf_rn(cv.a1, a.views[v].h.sh_basis[lane - 1], acc);
-        else if (lane == 17) acc = __fadd_rn(acc, cv.a2);
-        else if (lane == 18) acc = __fadd_rn(acc, cv.a3);
-        else if (lane == 19) acc = __fadd_rn(acc, cv.a4);
-        else if (lane == 20) acc = __fadd_rn(acc, cv.cx);
-        else if (lane == 21) acc = __fadd_rn(acc, cv.cy);
-        else acc = __fadd_rn(acc, cv.cz);
-      }
-      s_out[warp][lane] = acc;
-    }
+    if (lane < 23) s_out[warp][lane] = acc;
     __syncwarp();
     if (lane == 0) {
       GradSums g;
@@ -2738,125 +2791,6 @@ __global__ void __launch_bounds__(256) bwd_heavy_warp_kernel(const BwdScatterArg
       write_grad_row(a, i, g);
     }
     __syncwarp();
-  }
-}
-
-// One CTA per Gaussian left by bwd_scatter_kernel (persistent over the
-// list), thread v for view v of the group: every thread reads the
-// Gaussian's entries in index order (the same entry at the same time, a
-// broadcast), keeps those of its view, orders them by tile and sums their
-// partials, and applies the view's chain rule; then the views'
-// contributions are accumulated in view order, one thread per output sum.
-// A view with more than kHeavyViewEntries listing tiles of the Gaussian (a
-// bbox wider than ~80 pixels) takes them in order by repeated selection.
-constexpr int kHeavyViewEntries = 32;
-static_assert(kHeavyThreads == kMaxViewsPerLaunch, "one thread per view of a launch group");
-
-// Sequential reader of a Gaussian's entries in the views' entry slices.
-struct EntryCursor {
-  const uint32_t* base;
-  size_t vstride;
-  int per, slice, off;
-  __device__ EntryCursor(const BwdScatterArgs& a, int per_view, int64_t e0)
-      : base(a.entries), vstride(a.entries_vstride), per(per_view),
-        slice((int)(e0 / per_view)), off((int)(e0 % per_view)) {}
-  __device__ __forceinline__ uint32_t next() {
-    const uint32_t k = base[(size_t)slice * vstride + off];
-    if (++off == per) {
-      off = 0;
-      ++slice;
-    }
-    return k;
-  }
-};
-
-__global__ void __launch_bounds__(kHeavyThreads) bwd_heavy_kernel(const BwdScatterArgs a) {
-  __shared__ ViewContrib s_con[kMaxViewsPerLaunch];
-  __shared__ int s_has[kMaxViewsPerLaunch];
-  __shared__ float s_out[23];
-  const int tid = threadIdx.x;
-  const int count = a.heavy[0];
-  const int nviews = a.nviews;
-  const int per_view = a.views[0].tiles_x * a.views[0].tiles_y * kCap;
-  for (int h = blockIdx.x; h < count; h += gridDim.x) {
-    const int64_t i = a.heavy[1 + h];
-    const int e0 = a.start[i], c = a.start[i + 1] - e0;
-    uint32_t key[kHeavyViewEntries];
-    int m = 0;
-    {
-      EntryCursor cur(a, per_view, e0);
-      for (int q = 0; q < c; ++q) {
-        const uint32_t k = cur.next();
-        if ((int)(k >> 24) == tid) {
-          if (m < kHeavyViewEntries) key[m] = k;
-          ++m;
-        }
-      }
-    }
-    s_has[tid] = 0;
-    if (tid < nviews && m > 0) {
-      float A[7] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      float2 yzr = make_float2(0.f, 0.f);
-      if (m <= kHeavyViewEntries) {
-        for (int q = 1; q < m; ++q) {  // insertion sort by tile
-          const uint32_t x = key[q];
-          int r = q - 1;
-          while (r >= 0 && key[r] > x) {
-            key[r + 1] = key[r];
-            --r;
-          }
-          key[r + 1] = x;
-        }
-        for (int q = 0; q < m; ++q) entry_partial(a, key[q], A, yzr);
-      } else {
-        uint32_t last = 0;
-        for (int q = 0; q < m; ++q) {
-          uint32_t k = 0xFFFFFFFFu;
-          EntryCursor cur(a, per_view, e0);
-          for (int r = 0; r < c; ++r) {
-            const uint32_t x = cur.next();
-            if ((int)(x >> 24) == tid && (q == 0 || x > last) && x < k) k = x;
-          }
-          last = k;
-          entry_partial(a, k, A, yzr);
-        }
-      }
-      s_con[tid] = bwd_view_contrib(a.views[tid], A, yzr);
-      s_has[tid] = 1;
-    }
-    __syncthreads();
-    if (tid < 23) {
-      // output sum tid: 0 sigma, 1..16 SH, 17 rr, 18 cc, 19 rc, 20..22 x y z
-      float acc = 0.f;
-      for (int v = 0; v < nviews; ++v) {
-        if (!s_has[v]) continue;
-        const ViewContrib& cv = s_con[v];
-        if (tid == 0) acc = __fadd_rn(acc, cv.a0);
-        else if (tid <= kSh) acc = __fmaf_rn(cv.a1, a.views[v].h.sh_basis[tid - 1], acc);
-        else if (tid == 17) acc = __fadd_rn(acc, cv.a2);
-        else if (tid == 18) acc = __fadd_rn(acc, cv.a3);
-        else if (tid == 19) acc = __fadd_rn(acc, cv.a4);
-        else if (tid == 20) acc = __fadd_rn(acc, cv.cx);
-        else if (tid == 21) acc = __fadd_rn(acc, cv.cy);
-        else acc = __fadd_rn(acc, cv.cz);
-      }
-      s_out[tid] = acc;
-    }
-    __syncthreads();
-    if (tid == 0) {
-      GradSums g;
-      g.sigma = s_out[0];
-#pragma unroll
-      for (int k = 0; k < kSh; ++k) g.sh[k] = s_out[1 + k];
-      g.rr = s_out[17];
-      g.cc = s_out[18];
-      g.rc = s_out[19];
-      g.x = s_out[20];
-      g.y = s_out[21];
-      g.z = s_out[22];
-      write_grad_row(a, i, g);
-    }
-    __syncthreads();
   }
 }
 
@@ -3049,10 +2983,16 @@ cudaError_t launch_bin(const BinArgs& a, const Dims& d, int chunks, bool shadow,
 
 bool bin_cell_supported(const Dims& d) { return warp_count_bytes(d, true) <= kWarpCountBytes; }
 
-cudaError_t launch_bin_cand(const BinArgs& a, bool shadow, cudaStream_t s) {
+cudaError_t launch_bin_cand(const BinArgs& a, const Dims& d, bool shadow, cudaStream_t s) {
   const dim3 grid(kMaxCells / kBinThreads + kAlwaysBlocks, a.nviews);
-  if (shadow) bin_cand_kernel<true><<<grid, kBinThreads, 0, s>>>(a);
-  else bin_cand_kernel<false><<<grid, kBinThreads, 0, s>>>(a);
+  const size_t sm = open_stage_bytes(d.tiles_x, d.tiles_y, shadow ? 2 : 1);
+  if (shadow) {
+    if (sm) bin_cand_kernel<true, true><<<grid, kBinThreads, sm, s>>>(a);
+    else bin_cand_kernel<true, false><<<grid, kBinThreads, 0, s>>>(a);
+  } else {
+    if (sm) bin_cand_kernel<false, true><<<grid, kBinThreads, sm, s>>>(a);
+    else bin_cand_kernel<false, false><<<grid, kBinThreads, 0, s>>>(a);
+  }
   return cudaGetLastError();
 }
 
@@ -3100,8 +3040,10 @@ cudaError_t launch_cell_prep(const CellPrepArgs& a, cudaStream_t s) {
   return cudaGetLastError();
 }
 
-cudaError_t launch_cell_test(const CellTestArgs& a, int nviews, cudaStream_t s) {
-  cell_test_kernel<<<dim3(kMaxSpatialCells / 256, nviews), 256, 0, s>>>(a);
+cudaError_t launch_cell_test(const CellTestArgs& a, const Dims& d, int nviews, cudaStream_t s) {
+  const size_t sm = open_stage_bytes(d.tiles_x, d.tiles_y, a.shadow ? 2 : 1);
+  if (sm) cell_test_kernel<true><<<dim3(kMaxSpatialCells / 256, nviews), 256, sm, s>>>(a);
+  else cell_test_kernel<false><<<dim3(kMaxSpatialCells / 256, nviews), 256, 0, s>>>(a);
   return cudaGetLastError();
 }
 
@@ -3143,9 +3085,13 @@ cudaError_t launch_select(const SelectArgs& a, const Dims& d, int nviews, bool s
   return cudaGetLastError();
 }
 
+#ifndef SARR_RENDER_MANY_PIX
+#define SARR_RENDER_MANY_PIX 4
+#endif
 cudaError_t launch_render(const TileArgs& a, const Dims& d, int nviews, cudaStream_t s) {
+  constexpr int kMany = SARR_RENDER_MANY_PIX;
   if (nviews >= 16)
-    render_kernel<2><<<dim3(d.T, nviews), 128, 0, s>>>(a);
+    render_kernel<kMany><<<dim3(d.T, nviews), kTile * kTile / kMany, 0, s>>>(a);
   else
     render_kernel<1><<<dim3(d.T, nviews), 256, 0, s>>>(a);
   return cudaGetLastError();
@@ -3207,17 +3153,10 @@ cudaError_t launch_bwd_scatter(const BwdScatterArgs& a, const Dims& d, cudaStrea
   int sms = 148, per_sm = 0, dev = 0;
   if (cudaGetDevice(&dev) == cudaSuccess)
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  if (a.nviews <= kHeavyWarpViews) {
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, bwd_heavy_warp_kernel, 256, 0) !=
-            cudaSuccess || per_sm < 1)
-      per_sm = 1;
-    bwd_heavy_warp_kernel<<<sms * per_sm, 256, 0, s>>>(a);
-  } else {
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, bwd_heavy_kernel, kHeavyThreads, 0) !=
-            cudaSuccess || per_sm < 1)
-      per_sm = 1;
-    bwd_heavy_kernel<<<sms * per_sm, kHeavyThreads, 0, s>>>(a);
-  }
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, bwd_heavy_kernel, kHeavyWarps * 32, 0) !=
+          cudaSuccess || per_sm < 1)
+    per_sm = 1;
+  bwd_heavy_kernel<<<sms * per_sm, kHeavyWarps * 32, 0, s>>>(a);
   return cudaGetLastError();
 }
 
