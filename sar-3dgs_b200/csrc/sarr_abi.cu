@@ -334,14 +334,47 @@ cudaError_t run_selection(const Dims& d, const Ws& w, int gv, const float* means
       if (waves > 1 && p <= sms) prefix = p;
     }
   }
+  // Cell-culled calls bin the prefix in two stages: the first
+  // kPrefixStage1 chunks exactly, then the rest of the prefix through the
+  // skipping binner against the tiles still open after stage 1 (with
+  // segment masks, as selection expects for prefix chunks); the lists do not
+  // depend on the split.
+  const int stage1 = (w.L.cells && masks && kPrefixStage1 > 0 && kPrefixStage1 < prefix &&
+                      skip_bin_per_warp(d, shr != nullptr))
+                         ? kPrefixStage1
+                         : prefix;
   ba.chunk_offset = 0;
-  ba.views_per_cta = views_per_cta(prefix);
+  ba.views_per_cta = views_per_cta(stage1);
   // one view per warp in the prefix binner once a CTA holds 8 views or more
   if (ba.views_per_cta >= 8) ba.views_per_cta = (ba.views_per_cta + 7) / 8 * 8;
   cudaError_t e = run_kernel(kKindBin, s, [&] {
-    return launch_bin(ba, d, prefix, shr != nullptr, false, s);
+    return launch_bin(ba, d, stage1, shr != nullptr, false, s);
   });
   if (e != cudaSuccess) return e;
+  if (stage1 < prefix) {
+    OpenArgs o1;
+    o1.tiles_x = d.tiles_x;
+    o1.tiles_y = d.tiles_y;
+    o1.prefix_chunks = stage1;
+    o1.counts[0] = ba.counts_ipp;
+    o1.counts[1] = ba.counts_sh;
+    o1.counts_vstride = w.L.per_view;
+    o1.table[0] = const_cast<int*>(ba.open_ipp);
+    o1.table[1] = const_cast<int*>(ba.open_sh);
+    o1.table_vstride = ba.open_vstride;
+    e = run_kernel(kKindAux, s, [&] { return launch_open_table(o1, gv, shr ? 2 : 1, s); });
+    if (e != cudaSuccess) return e;
+    BinArgs b2 = ba;
+    b2.chunk_offset = stage1;
+    b2.views_per_cta = views_per_cta(prefix - stage1);
+    b2.skip_masks = 1;
+    b2.xlist = nullptr;  // prefix chunks are read through their segment masks
+    b2.xcount = nullptr;
+    e = run_kernel(kKindBinSkip, s, [&] {
+      return launch_bin(b2, d, prefix - stage1, shr != nullptr, true, s);
+    });
+    if (e != cudaSuccess) return e;
+  }
   if (prefix < d.C) {
     OpenArgs og;
     og.tiles_x = d.tiles_x;

@@ -33,6 +33,10 @@ constexpr int kScan1Threads = 1024;              // scan_kernel (1 tile per lane
 #define SARR_PREFIX_CHUNKS 64
 #endif
 constexpr int kPrefixChunks = SARR_PREFIX_CHUNKS;  // chunks binned exactly before saturation skipping
+#ifndef SARR_PREFIX_STAGE1
+#define SARR_PREFIX_STAGE1 8
+#endif
+constexpr int kPrefixStage1 = SARR_PREFIX_STAGE1;  // cell-culled calls: chunks of the prefix binned exactly
 constexpr int kXCap = kChunk;                    // exactly binned Gaussians listed per skipped chunk
 constexpr int kSegMaskMaxTiles = 2048;           // prefix-chunk segment masks up to this many tiles
 constexpr int kSegMaskAllMaxTiles = 512;         // segment masks of every chunk up to this many tiles
