@@ -32,6 +32,11 @@ train_step  the data-parallel training step on the full-training shape (1M
             parameter producer, forward, L1 + 0.2 D-SSIM loss and gradient,
             backward, NCCL all-reduce of the trainable gradients (N > 1) and
             Adam; steps/s (max over ranks) and the all-reduce's own cost.
+train_full  full training with densification: 100k Gaussians growing by
+            densify/prune every 100 iterations (cap 2M), SH degree ramp
+            0 -> 3 every 1,000 iterations, 64 views per rank per step,
+            --full-iters iterations (3,000); steps/s over the whole run, the
+            densification record, the final N.
 train_configs  (1 GPU) the training step on the 50k-Gaussian 64-view 128 px
             scene and on the 500k-Gaussian 16-view 512 px scene.
 
@@ -73,10 +78,13 @@ TRAIN_VIEWS_PER_RANK = 64  # views per rank per training step
 # needs at least 12 thread instructions even with the fastest exponential.
 SMS, SCHEDULERS = 148, 4
 MIN_INSTR_PER_PAIR = 12
-# ncu figures of the current render_kernel on one 256-view launch of this
+# ncu figures of the compositing kernels on one 256-view launch of this
 # workload (dram__bytes_read.sum + dram__bytes_write.sum, smsp__inst_executed
-# .sum); they belong to this workload and these kernels only.
-NCU_RENDER = {"dram_bytes": 118_431_744 + 37_014_528, "warp_instructions": 485_642_170}
+# .sum); they belong to this workload and these kernels only. render_kernel
+# runs in calls with states or Omega; image-only calls run
+# select_render_kernel (selection and compositing in one kernel).
+NCU = {"render_kernel": {"dram_bytes": 118_493_696 + 37_277_696, "warp_instructions": 353_205_923},
+       "select_render_kernel": {"dram_bytes": 91_192_320 + 39_073_792, "warp_instructions": 536_528_416}}
 
 
 def parse():
@@ -89,11 +97,14 @@ def parse():
     ap.add_argument("--views", type=int, default=1024)
     ap.add_argument("--samples", type=int, default=256)
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--no-train", action="store_true", help="skip fwd_bwd, train_step, train_configs")
+    ap.add_argument("--no-train", action="store_true",
+                    help="skip fwd_bwd, train_step, train_full, train_configs, train_ops")
+    ap.add_argument("--full-iters", type=int, default=3000,
+                    help="iterations of the full-training run with densification (train_full)")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--sections", default="all",
                     help="comma-separated subset of forward,e2e,omega,fwd_bwd,train_step,"
-                         "train_configs,train_ops,cpu (default all; without forward the line "
+                         "train_full,train_configs,train_ops,cpu (default all; without forward the line "
                          "carries no headline value, for profiling runs)")
     return ap.parse_args()
 
@@ -241,11 +252,12 @@ def _a256(x):
     return (x + 255) // 256 * 256
 
 
-def listed_pairs(N, inputs, views, n, s, dev):
+def listed_pairs(N, inputs, views, n, s, dev, flush):
     """(pixel, listed record) pairs of the compositing of these views: the
     sum over views and tiles of the list length times the tile's pixels,
     read from the per-view forward states (256 x 256 images: every tile is
-    16 x 16)."""
+    16 x 16); and the per-kernel device times of a second such call (after
+    an L2 flush), whose selection and compositing run as separate kernels."""
     T = (s // 16) ** 2
     sb = N.state_bytes(n, s, s)
     states = torch.empty(len(views) * sb, dtype=torch.uint8, device=dev)
@@ -254,8 +266,15 @@ def listed_pairs(N, inputs, views, n, s, dev):
     o = _a256(4 * n)
     counts = states.view(len(views), sb)[:, o:o + 4 * T].contiguous().view(torch.int32)
     total = int(counts.to(torch.int64).sum().item()) * 256
+    flush_l2(flush, 0)
+    torch.cuda.synchronize()
+    N.profile_enable(True)
+    N.forward(views, *inputs, img, states=states)
+    torch.cuda.synchronize()
+    prof = N.profile_read()
+    N.profile_enable(False)
     del states
-    return total
+    return total, prof
 
 
 def bench_forward(args, d):
@@ -324,7 +343,7 @@ def bench_forward(args, d):
     dom_s = dom_ms / dom_launches / 1e3
     full = n == 1_000_000 and s == 256 and launch_views == GROUP_VIEWS
     roofline = roof(fwd_bytes, dom_s, {
-        "kernel": dominant, "traffic": (NCU_RENDER["dram_bytes"] if full and dominant == "render_kernel"
+        "kernel": dominant, "traffic": (NCU[dominant]["dram_bytes"] if full and dominant in NCU
                                         else None),
         "bytes_per_launch": int(fwd_bytes), "views_per_launch": launch_views,
         "avg_launch_us": round(dom_s * 1e6, 2),
@@ -335,21 +354,35 @@ def bench_forward(args, d):
                 {"bytes_per_step": int(step_bytes), "model": roofline["model"]})
     path["achieved_total_gbs"] = round(path["achieved"] * d.world, 1)
 
-    # the compositing kernel against its instruction-issue bound
+    # the compositing against its instruction-issue bound, timed in a call of
+    # one launch group with states, where selection and compositing are
+    # separate kernels; image-only calls (the timed steps above) run both in
+    # select_render_kernel, whose launch time is set beside their sum
     render_issue = None
-    if "render_kernel" in prof and prof["render_kernel"][1]:
-        pairs = listed_pairs(N, inputs, views[:GROUP_VIEWS], n, s, dev) * (V / min(V, GROUP_VIEWS))
-        r_ms, r_l = prof["render_kernel"]
-        per_launch_pairs = pairs / (r_l / rsteps)
+    gv = min(V, GROUP_VIEWS)
+    pairs, sprof = listed_pairs(N, inputs, views[:gv], n, s, dev, flush)
+    if sprof.get("render_kernel", (0.0, 0))[1]:
+        r_ms, r_l = sprof["render_kernel"]
+        per_launch_pairs = pairs / r_l
         f_hz = (clk["sm_mhz"] if clk else 1965.0) * 1e6
         bound_s = per_launch_pairs * MIN_INSTR_PER_PAIR / 32 / (SMS * SCHEDULERS * f_hz)
         r_s = r_ms / r_l / 1e3
-        render_issue = {"bound": "issue", "pairs_per_launch": int(per_launch_pairs),
+        full_group = n == 1_000_000 and s == 256 and gv == GROUP_VIEWS
+        fused = None
+        if prof.get("select_render_kernel", (0.0, 0))[1] and gv == GROUP_VIEWS:
+            f_ms, f_l = prof["select_render_kernel"]
+            sel_ms = sprof.get("select_kernel", (0.0, 0))[0]
+            fused = {"select_render_kernel_us": round(f_ms / f_l * 1e3, 2),
+                     "select_kernel_plus_render_kernel_us": round((sel_ms + r_ms) / r_l * 1e3, 2)}
+        render_issue = {"bound": "issue", "kernel": "render_kernel",
+                        "timed_in": f"one {gv}-view call with states",
+                        "pairs_per_launch": int(per_launch_pairs),
                         "min_thread_instr_per_pair": MIN_INSTR_PER_PAIR,
                         "bound_us": round(bound_s * 1e6, 2), "achieved_us": round(r_s * 1e6, 2),
                         "frac": round(bound_s / r_s, 4),
-                        "ncu_thread_instr_per_pair": (round(NCU_RENDER["warp_instructions"] * 32 /
-                                                            per_launch_pairs, 2) if full else None)}
+                        "ncu_thread_instr_per_pair": (round(NCU["render_kernel"]["warp_instructions"] * 32 /
+                                                            per_launch_pairs, 2) if full_group else None),
+                        "fused": fused}
 
     out = {"value": value, "ms_per_step": t_ms_max / args.steps, "launches": launches,
            "clocks": clk, "roofline": roofline, "path_roofline": path, "render_issue": render_issue,
@@ -619,6 +652,84 @@ def bench_train_step(args, d, flush):
                     "backward, sigmoid chain, bucketed NCCL all-reduce (N > 1), Adam"}
 
 
+def bench_train_full(args, d, flush):
+    """Full training with densification, on the schedule of SAR-3DGS's full
+    training: 100k Gaussians (40 x 40 x 10 m, scales 0.05-0.5 m) trained
+    against a seeded 200k-Gaussian target scene; 64 views per rank per step,
+    in turn from a pool of 1,024 views per rank (256 x 256 at 0.2 m, azimuth
+    uniform 0-360 deg, incidence 15 or 17 deg); L1 + 0.2 D-SSIM, Adam
+    (lr 1e-3; SH lr 1e-5); densify and prune every 100 iterations with the
+    reference's rules (clone: norm(scale) below the clone size and means
+    gradient above 2e-4; split and prune: norm(scale) above 2 m; prune:
+    transmittance below 0.005; cap 2M); SH degree 0 -> 3, one more every
+    1,000 iterations; `--full-iters` iterations. The clone size is 1 m: the
+    reference's default, 0.01 m, clones nothing among scales of 0.05-0.5 m
+    (norms 0.12-0.38 m between the 1st and 50th percentiles), so the set
+    would never grow. Each iteration is timed on the device (densifications
+    included, L2 flushed between iterations), max over ranks; after 3
+    warm-up iterations of a separate trainer."""
+    from cuda_rasterizer import _native as N
+    from cuda_rasterizer import multiview
+    dev = d.device
+    s = args.samples
+    box, scales = (40.0, 40.0, 10.0), (0.05, 0.5)
+    n0, pool, per = 100_000, 1024, TRAIN_VIEWS_PER_RANK
+    p = S.make_param_scene(n0, box, scales, seed=0, device=dev)
+    allv = S.training_views(pool * d.world, rho=0.2, samples=s)
+    mine = allv[d.rank * pool:(d.rank + 1) * pool]
+    targets = _targets(N, mine, 200_000, box, scales, dev)
+    batches = [[N.make_view(*v) for v in mine[b:b + per]] for b in range(0, pool, per)]
+    tbatches = [targets[b:b + per] for b in range(0, pool, per)]
+    kw = dict(lr=1e-3, buckets=4, densify_interval=100, grad_threshold=2e-4, size_threshold=1.0,
+              large_scale_threshold=2.0, opacity_threshold=0.005, max_gaussians=2_000_000,
+              sh_interval=1000, max_sh_degree=3)
+    warm = multiview.DensifyingTrainer(p["means"], p["scales"], p["rotations"], p["logits"], p["sh"],
+                                       **kw)
+    for k in range(3):
+        warm.step(batches[k], tbatches[k])
+    torch.cuda.synchronize()
+    del warm
+    dt = multiview.DensifyingTrainer(p["means"], p["scales"], p["rotations"], p["logits"], p["sh"], **kw)
+    iters = args.full_iters
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(iters)]
+    d.barrier()
+    l0 = N.launch_count()
+    loss_first = None
+    for it in range(iters):
+        k = it % len(batches)
+        flush_l2(flush, it)
+        ev[it][0].record()
+        losses = dt.step(batches[k], tbatches[k])
+        ev[it][1].record()
+        if it == 0:
+            loss_first = losses.clone()
+    torch.cuda.synchronize()
+    launches = N.launch_count() - l0
+    t = [a.elapsed_time(b) for a, b in ev]
+    total_ms = d.max(sum(t))
+    # the loss is each rank's weighted share; the mean over all views is the sum
+    loss_last = float(d.sum(float(losses[0].item())))
+    loss_first = float(d.sum(float(loss_first[0].item())))
+    hist = [list(h) for h in dt.history]
+    return {"value": iters * 1e3 / total_ms, "unit": "steps/s", "iterations": iters,
+            "total_s": round(total_ms / 1e3, 3), "ms_per_step": total_ms / iters,
+            "views_per_rank_per_step": per, "global_views_per_step": per * d.world,
+            "scaling": "weak", "n_start": n0, "n_final": dt.n,
+            "densify": {"interval": 100, "grad_threshold": 2e-4, "clone_size_m": 1.0,
+                        "split_prune_size_m": 2.0, "prune_transmittance": 0.005,
+                        "max_gaussians": 2_000_000},
+            "densifications": hist,
+            "densification_fields": ["iteration", "n_before", "clones", "splits", "prunes", "n_after"],
+            "sh_degree_final": multiview.sh_degree_at(iters - 1, 1000, 3),
+            "loss_first_step": loss_first, "loss_last_step": loss_last,
+            "gpu_launches_per_step": launches / iters,
+            "l2": "flushed between iterations (512 MiB device write, outside the timed region)",
+            "step": "DensifyingTrainer: producer, forward, CombinedLoss, backward, bucketed NCCL "
+                    "all-reduce (N > 1), Adam; densify/prune from the summed gradient every 100 "
+                    "iterations (no update that iteration, Adam state cleared, as the reference)"}
+
+
 def bench_train_configs(args, d, flush):
     """The training step on one GPU on the two smaller training scenes:
     50k Gaussians in 20 x 20 x 6 m, 64 views of 128 x 128 at 0.3 m (targets
@@ -865,6 +976,8 @@ def main():
         line = {"metric": METRIC, "sections": args.sections, "n_gpus": d.world}
         if wanted(args, "train_step"):
             line["train_step"] = bench_train_step(args, d, flush)
+        if wanted(args, "train_full"):
+            line["train_full"] = bench_train_full(args, d, flush)
         if wanted(args, "train_configs") and d.world == 1:
             line["train_configs"] = bench_train_configs(args, d, flush)
         if d.rank == 0:
@@ -891,6 +1004,8 @@ def main():
         del r
         if wanted(args, "train_step"):
             line["train_step"] = bench_train_step(args, d, flush)
+        if wanted(args, "train_full"):
+            line["train_full"] = bench_train_full(args, d, flush)
         if d.world == 1:
             if wanted(args, "train_configs"):
                 line["train_configs"] = bench_train_configs(args, d, flush)

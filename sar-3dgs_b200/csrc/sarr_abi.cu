@@ -128,14 +128,14 @@ int cuda_status(cudaError_t e) { return e == cudaSuccess ? SARR_OK : SARR_ERR_CU
 enum KernelKind {
   kKindSetup = 0, kKindBin, kKindSelect, kKindSelectShadow, kKindRender, kKindOmegaTile,
   kKindOmegaScatter, kKindBwdTile, kKindBwdScatter, kKindAux, kKindScan, kKindBinSkip,
-  kKindBinFinalize, kKindCount
+  kKindBinFinalize, kKindSelectRender, kKindCount
 };
 static_assert(kKindCount == SARR_KERNEL_KINDS, "kernel kinds");
 
 const char* const kKindNames[kKindCount] = {
     "view_setup", "bin_kernel", "select_kernel", "select_kernel_shadow", "render_kernel",
     "omega_tile_kernel", "omega_scatter_kernel", "bwd_tile_kernel", "bwd_scatter_kernel", "aux",
-    "scan_kernel", "bin_skip_kernel", "bin_finalize_kernel"};
+    "scan_kernel", "bin_skip_kernel", "bin_finalize_kernel", "select_render_kernel"};
 
 struct ProfRecord {
   int kind, device;
@@ -267,10 +267,14 @@ cudaError_t run_cell_prep(const Dims& d, const Ws& w, const float* means, const 
 }
 
 // bin + select of the image-plane list (and optionally the shadow list) for a
-// group of views.
+// group of views. With `fuse` given (an image-only call) and a selection that
+// select_render_kernel can take, the image list's selection is not launched:
+// its arguments are left in *fuse for that kernel (fuse->views is set only
+// then).
 cudaError_t run_selection(const Dims& d, const Ws& w, int gv, const float* means, const float* cov,
                           int cov_layout, const float* sigma, const float* sh, int sh_stride,
-                          int sh_k, const StateRef& ipp, const StateRef* shr, cudaStream_t s) {
+                          int sh_k, const StateRef& ipp, const StateRef* shr, cudaStream_t s,
+                          SelectArgs* fuse = nullptr) {
   BinArgs ba;
   memset(&ba, 0, sizeof(ba));
   ba.views = w.views;
@@ -470,6 +474,10 @@ cudaError_t run_selection(const Dims& d, const Ws& w, int gv, const float* means
   sa.xlist = xlists ? ba.xlist : nullptr;
   sa.x_vstride = ba.x_vstride;
   sa.err = w.err;
+  if (fuse && !shr && select_render_fusable(sa, gv)) {
+    *fuse = sa;
+    return cudaSuccess;
+  }
   e = run_kernel(kKindSelect, s, [&] { return launch_select(sa, d, gv, false, s); });
   if (e != cudaSuccess || !shr) return e;
 
@@ -598,8 +606,10 @@ int sarr_forward(const sarr_view* views, int n_views, int64_t n, const float* me
     shr.vstride = w.L.per_view;
     shr.L = w.L.st;
 
+    SelectArgs fused;
+    fused.views = nullptr;
     e = run_selection(d, w, gv, means, cov, cov_layout, sigma, sh, sh_stride, sh_k, ipp,
-                      omega ? &shr : nullptr, s);
+                      omega ? &shr : nullptr, s, (!states && !omega) ? &fused : nullptr);
     if (e != cudaSuccess) return SARR_ERR_CUDA;
 
     TileArgs ta;
@@ -609,7 +619,10 @@ int sarr_forward(const sarr_view* views, int n_views, int64_t n, const float* me
     ta.images = images + (size_t)g0 * npix;
     ta.img_vstride = npix;
     ta.err = w.err;
-    e = run_kernel(kKindRender, s, [&] { return launch_render(ta, d, gv, s); });
+    if (fused.views)
+      e = run_kernel(kKindSelectRender, s, [&] { return launch_select_render(fused, ta, d, gv, s); });
+    else
+      e = run_kernel(kKindRender, s, [&] { return launch_render(ta, d, gv, s); });
     if (e != cudaSuccess) return SARR_ERR_CUDA;
 
     if (omega) {

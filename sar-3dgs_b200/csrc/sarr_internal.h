@@ -445,6 +445,11 @@ cudaError_t launch_scan(const ScanArgs& a, int nviews, cudaStream_t s);
 cudaError_t launch_select(const SelectArgs& a, const Dims& d, int nviews, bool shadow_list,
                           cudaStream_t s);
 cudaError_t launch_render(const TileArgs& a, const Dims& d, int nviews, cudaStream_t s);
+// Whether a launch of the image list's selection and compositing may run as
+// the one select_render_kernel (image-only calls of many views).
+bool select_render_fusable(const SelectArgs& a, int nviews);
+cudaError_t launch_select_render(const SelectArgs& sa, const TileArgs& ta, const Dims& d,
+                                 int nviews, cudaStream_t s);
 cudaError_t launch_omega_tile(const TileArgs& a, const Dims& d, int nviews, cudaStream_t s);
 cudaError_t launch_omega_scatter(const OmegaScatterArgs& a, const Dims& d, int nviews,
                                  cudaStream_t s);

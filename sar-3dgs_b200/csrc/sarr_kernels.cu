@@ -1367,9 +1367,10 @@ __global__ void __launch_bounds__(kScanThreads) scan4_kernel(const ScanArgs a) {
 // The 48-byte record of list slot `slot` of tile t: the listed Gaussian
 // projected again in full (SH scattering only for the image list), its
 // density constants, transmittance, Z_r, Y_r and slot; the image list also
-// stores (Y_r, Z_r) for the backward. Returns Z_r. A list id outside [0, n)
-// (only a corrupted workspace can produce one) is reported and replaced by 0.
-template <bool kShadowList>
+// stores (Y_r, Z_r) for the backward (kStateYz). Returns Z_r. A list id
+// outside [0, n) (only a corrupted workspace can produce one) is reported and
+// replaced by 0.
+template <bool kShadowList, bool kStateYz = true>
 __device__ __forceinline__ float select_record(const SelectArgs& a, const ViewConst& vc,
                                                unsigned char* st, int t, int slot, int* list,
                                                Rec& g) {
@@ -1404,7 +1405,7 @@ __device__ __forceinline__ float select_record(const SelectArgs& a, const ViewCo
   g.z = o.zr;
   g.yr = o.yr;
   g.pos = slot;
-  if (!kShadowList) {
+  if (!kShadowList && kStateYz) {
     float2* yz = reinterpret_cast<float2*>(st + a.st.L.yz);
     yz[(size_t)t * kCap + slot] = make_float2(o.yr, o.zr);
   }
@@ -1482,132 +1483,66 @@ __device__ __forceinline__ void warp_sort_ranks(uint64_t key0, uint64_t key1, in
     if (key[h] != ~0ull) s_rank[(uint32_t)key[h]] = lane + 32 * h;
 }
 
-// One warp per tile (kSelectThreads / 32 tiles per CTA), no CTA barrier.
-//  1. emit: every needed chunk's 1024 rectangles are loaded at once (eight
-//     16-byte loads per lane) and its hits are ranked in index order with a
-//     warp scan, filling list slots [hits before, hits before + needed);
-//  2. the listed Gaussians (two slots per lane) are projected again in full
-//     (SH only for them) into 48-byte records;
-//  3. each slot's rank by (Z_r, slot) places its record.
-template <bool kShadowList, bool kAllMasks>
-__global__ void __launch_bounds__(kSelectThreads, 8) select_kernel(const SelectArgs a) {
-  constexpr int kWarps = kSelectThreads / 32;
-  __shared__ int s_list[kWarps][kCap];
-  __shared__ float s_z[kWarps][kCap];
-  __shared__ int s_rank[kWarps][kCap];
+// Need entries of tile t taken by one warp: q = q0 + qs i, i = 0, 1, ...
+// (qs = 1: every entry; qs = 2: one of two warps' share). Lane l holds
+// entries i = l and i = l + 32, each with its chunk's exact-list length or
+// segment mask in aux (-1: neither). kAllMasks: every chunk has segment
+// masks (the per-view path).
+struct NeedRegs {
+  int4 nd[2];
+  int aux[2];
+};
 
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int v = blockIdx.y;
-  const ViewConst& vc = a.views[v];
-  const int tiles_x = vc.tiles_x, T = tiles_x * vc.tiles_y;
-  const int t = blockIdx.x * kWarps + warp;
-  if (t >= T) return;  // warp-uniform; nothing below synchronises the CTA
-  const int tx = t % tiles_x, ty = t / tiles_x;
-  unsigned char* st = a.st.base + v * a.st.vstride;
-  const int count = reinterpret_cast<const int*>(st + a.st.L.count)[t];
-  if (count == 0) return;
-  const int nneed = a.need_n[v * a.need_n_vstride + t];
+template <bool kAllMasks>
+__device__ __forceinline__ NeedRegs prefetch_need(const SelectArgs& a, int v, int T, int t, int nneed,
+                                                  int lane, int q0, int qs) {
   const int4* need = reinterpret_cast<const int4*>(a.need + v * a.need_vstride) + (size_t)t * kCap;
-  int* list = s_list[warp];
-  list[lane] = -1;
-  list[lane + 32] = -1;
-  __syncwarp();
-
-  // 1. emit
-  const uint32_t* rects = reinterpret_cast<const uint32_t*>(st + a.st.L.rects);
   const int* xcount = a.xcount ? reinterpret_cast<const int*>(
                                      reinterpret_cast<const unsigned char*>(a.xcount) + v * a.x_vstride)
                                : nullptr;
+  NeedRegs r;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int q = q0 + qs * (lane + 32 * h);
+    r.nd[h] = make_int4(0, 0, 0, 0);
+    r.aux[h] = -1;
+    if (q < nneed) {
+      r.nd[h] = need[q];
+      const int c = r.nd[h].x;
+      if (!kAllMasks && xcount && c >= a.xlist_from)
+        r.aux[h] = xcount[c];
+      else if (a.segmask && c < a.segmask_to)
+        r.aux[h] = (int)a.segmask[v * a.segmask_vstride + (size_t)c * T + t];
+    }
+  }
+  return r;
+}
+
+// Emit of the need entries in `nr` (entries q0 + qs i of tile (tx, ty)) when
+// the chunks after the prefix have exact lists or none: each entry's chunk
+// fills list slots [hits before, hits before + needed) with its first
+// Gaussians, in index order, whose rectangle holds the tile, taken from the
+// chunk's exact list, its segment masks, or all of its rectangles. Warp-wide;
+// entries fill disjoint slots, so warps may split them.
+__device__ __forceinline__ void emit_entries(const SelectArgs& a, int v, const unsigned char* st,
+                                             int tx, int ty, int nneed, const NeedRegs& nr, int q0,
+                                             int qs, int* list, int lane) {
+  const uint32_t* rects = reinterpret_cast<const uint32_t*>(st + a.st.L.rects);
   const unsigned lt_mask = (1u << lane) - 1u;
   // chunks from sparse_from on keep only their exactly binned Gaussians'
   // rectangles, compactly in list order (cell binning)
   const unsigned char* xsv = a.xs.base + v * a.xs.vstride;
   const int64_t sparse_from = *reinterpret_cast<const int64_t*>(xsv + a.xs.L.meta);
-  // the need entries and their per-chunk data, prefetched: lane l holds
-  // entries l and l + 32 (exact-list length, or segment mask)
-  // kAllMasks: every chunk has segment masks (the per-view path)
-  constexpr bool all_masks = kAllMasks;
-  int4 nd_l[2];
-  int aux_l[2];
-#pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    const int q = lane + 32 * h;
-    nd_l[h] = make_int4(0, 0, 0, 0);
-    aux_l[h] = -1;
-    if (q < nneed) {
-      nd_l[h] = need[q];
-      const int c = nd_l[h].x;
-      if (!all_masks && xcount && c >= a.xlist_from)
-        aux_l[h] = xcount[c];
-      else if (a.segmask && c < a.segmask_to)
-        aux_l[h] = (int)a.segmask[v * a.segmask_vstride + (size_t)c * T + t];
-    }
-  }
-  if constexpr (kAllMasks) {
-    // Every chunk has segment masks: the (need entry, hit segment) pairs of
-    // all entries, in order, kSelBatch per round with their rectangle loads
-    // in flight together.
-    constexpr int kSelBatch = 8;
-    const unsigned full = 0xffffffffu;
-    // (the per-view path keeps every rectangle at its Gaussian's slot)
-    auto entry_mask = [&](int q) {
-      return (uint32_t)__shfl_sync(full, q >= 32 ? aux_l[1] : aux_l[0], q & 31);
-    };
-    int eq = 0;                        // entry being enumerated
-    uint32_t rem = entry_mask(0);      // its segments not yet enumerated
-    int cur = -1, found = 0, want = 0, ny = 0;
-    bool more = true;
-    while (more) {
-      uint32_t rc[kSelBatch];
-      int jj[kSelBatch], qq[kSelBatch];
-#pragma unroll
-      for (int b = 0; b < kSelBatch; ++b) {
-        while (rem == 0 && eq + 1 < nneed) rem = entry_mask(++eq);
-        qq[b] = -1;
-        jj[b] = 0;
-        rc[b] = kEmptyRect;
-        if (rem != 0) {
-          const int seg = __ffs(rem) - 1;
-          rem &= rem - 1;
-          const int cq = __shfl_sync(full, eq >= 32 ? nd_l[1].x : nd_l[0].x, eq & 31);
-          const int64_t jg = (int64_t)cq * kChunk + seg * 32 + lane;
-          qq[b] = eq;
-          jj[b] = (int)jg;
-          if (jg < a.n) rc[b] = rects[jg];
-        }
-      }
-      more = rem != 0 || eq + 1 < nneed;
-#pragma unroll
-      for (int b = 0; b < kSelBatch; ++b) {
-        const int q = qq[b];
-        if (q < 0) break;
-        if (q != cur) {
-          cur = q;
-          found = 0;
-          const bool h1 = q >= 32;
-          ny = __shfl_sync(full, h1 ? nd_l[1].y : nd_l[0].y, q & 31);
-          const int z = __shfl_sync(full, h1 ? nd_l[1].z : nd_l[0].z, q & 31);
-          want = min(z, kCap - ny);
-        }
-        if (found >= want) continue;
-        const bool hit = rect_has(rc[b], tx, ty);
-        const unsigned m = __ballot_sync(full, hit);
-        const int rk = found + __popc(m & lt_mask);
-        if (hit && rk < want) list[ny + rk] = jj[b];
-        found += __popc(m);
-      }
-    }
-  }
-  for (int q = 0; q < (all_masks ? 0 : nneed); ++q) {
-    const int hq = q >> 5, src = q & 31;
+  for (int i = 0; q0 + qs * i < nneed; ++i) {
+    const int hq = i >> 5, src = i & 31;
     int4 nd;
-    nd.x = __shfl_sync(0xffffffffu, hq ? nd_l[1].x : nd_l[0].x, src);
-    nd.y = __shfl_sync(0xffffffffu, hq ? nd_l[1].y : nd_l[0].y, src);
-    nd.z = __shfl_sync(0xffffffffu, hq ? nd_l[1].z : nd_l[0].z, src);
-    const int aux = __shfl_sync(0xffffffffu, hq ? aux_l[1] : aux_l[0], src);
+    nd.x = __shfl_sync(0xffffffffu, hq ? nr.nd[1].x : nr.nd[0].x, src);
+    nd.y = __shfl_sync(0xffffffffu, hq ? nr.nd[1].y : nr.nd[0].y, src);
+    nd.z = __shfl_sync(0xffffffffu, hq ? nr.nd[1].z : nr.nd[0].z, src);
+    const int aux = __shfl_sync(0xffffffffu, hq ? nr.aux[1] : nr.aux[0], src);
     const int want = min(nd.z, kCap - nd.y);
     const int64_t b0 = (int64_t)nd.x * kChunk;
-    const int xc = (xcount && nd.x >= a.xlist_from) ? aux : -1;
+    const int xc = (a.xcount && nd.x >= a.xlist_from) ? aux : -1;
     if (xc >= 0) {
       // only the chunk's exactly binned Gaussians can hit the tile
       const uint16_t* xl = reinterpret_cast<const uint16_t*>(
@@ -1693,6 +1628,99 @@ __global__ void __launch_bounds__(kSelectThreads, 8) select_kernel(const SelectA
       if (h3) { if (rk < want) list[nd.y + rk] = j + 3; }
       found += __shfl_sync(0xffffffffu, incl, 31);
     }
+  }
+}
+
+// One warp per tile (kSelectThreads / 32 tiles per CTA), no CTA barrier.
+//  1. emit: every needed chunk's 1024 rectangles are loaded at once (eight
+//     16-byte loads per lane) and its hits are ranked in index order with a
+//     warp scan, filling list slots [hits before, hits before + needed);
+//  2. the listed Gaussians (two slots per lane) are projected again in full
+//     (SH only for them) into 48-byte records;
+//  3. each slot's rank by (Z_r, slot) places its record.
+template <bool kShadowList, bool kAllMasks>
+__global__ void __launch_bounds__(kSelectThreads, 8) select_kernel(const SelectArgs a) {
+  constexpr int kWarps = kSelectThreads / 32;
+  __shared__ int s_list[kWarps][kCap];
+  __shared__ float s_z[kWarps][kCap];
+  __shared__ int s_rank[kWarps][kCap];
+
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int v = blockIdx.y;
+  const ViewConst& vc = a.views[v];
+  const int tiles_x = vc.tiles_x, T = tiles_x * vc.tiles_y;
+  const int t = blockIdx.x * kWarps + warp;
+  if (t >= T) return;  // warp-uniform; nothing below synchronises the CTA
+  const int tx = t % tiles_x, ty = t / tiles_x;
+  unsigned char* st = a.st.base + v * a.st.vstride;
+  const int count = reinterpret_cast<const int*>(st + a.st.L.count)[t];
+  if (count == 0) return;
+  const int nneed = a.need_n[v * a.need_n_vstride + t];
+  int* list = s_list[warp];
+  list[lane] = -1;
+  list[lane + 32] = -1;
+  __syncwarp();
+
+  // 1. emit
+  const NeedRegs nr = prefetch_need<kAllMasks>(a, v, T, t, nneed, lane, 0, 1);
+  if constexpr (kAllMasks) {
+    const uint32_t* rects = reinterpret_cast<const uint32_t*>(st + a.st.L.rects);
+    const unsigned lt_mask = (1u << lane) - 1u;
+    // Every chunk has segment masks: the (need entry, hit segment) pairs of
+    // all entries, in order, kSelBatch per round with their rectangle loads
+    // in flight together.
+    constexpr int kSelBatch = 8;
+    const unsigned full = 0xffffffffu;
+    // (the per-view path keeps every rectangle at its Gaussian's slot)
+    auto entry_mask = [&](int q) {
+      return (uint32_t)__shfl_sync(full, q >= 32 ? nr.aux[1] : nr.aux[0], q & 31);
+    };
+    int eq = 0;                        // entry being enumerated
+    uint32_t rem = entry_mask(0);      // its segments not yet enumerated
+    int cur = -1, found = 0, want = 0, ny = 0;
+    bool more = true;
+    while (more) {
+      uint32_t rc[kSelBatch];
+      int jj[kSelBatch], qq[kSelBatch];
+#pragma unroll
+      for (int b = 0; b < kSelBatch; ++b) {
+        while (rem == 0 && eq + 1 < nneed) rem = entry_mask(++eq);
+        qq[b] = -1;
+        jj[b] = 0;
+        rc[b] = kEmptyRect;
+        if (rem != 0) {
+          const int seg = __ffs(rem) - 1;
+          rem &= rem - 1;
+          const int cq = __shfl_sync(full, eq >= 32 ? nr.nd[1].x : nr.nd[0].x, eq & 31);
+          const int64_t jg = (int64_t)cq * kChunk + seg * 32 + lane;
+          qq[b] = eq;
+          jj[b] = (int)jg;
+          if (jg < a.n) rc[b] = rects[jg];
+        }
+      }
+      more = rem != 0 || eq + 1 < nneed;
+#pragma unroll
+      for (int b = 0; b < kSelBatch; ++b) {
+        const int q = qq[b];
+        if (q < 0) break;
+        if (q != cur) {
+          cur = q;
+          found = 0;
+          const bool h1 = q >= 32;
+          ny = __shfl_sync(full, h1 ? nr.nd[1].y : nr.nd[0].y, q & 31);
+          const int z = __shfl_sync(full, h1 ? nr.nd[1].z : nr.nd[0].z, q & 31);
+          want = min(z, kCap - ny);
+        }
+        if (found >= want) continue;
+        const bool hit = rect_has(rc[b], tx, ty);
+        const unsigned m = __ballot_sync(full, hit);
+        const int rk = found + __popc(m & lt_mask);
+        if (hit && rk < want) list[ny + rk] = jj[b];
+        found += __popc(m);
+      }
+    }
+  } else {
+    emit_entries(a, v, st, tx, ty, nneed, nr, 0, 1, list, lane);
   }
   __syncwarp();
 
@@ -1978,6 +2006,108 @@ __device__ __forceinline__ uint64_t block_hits(const Rec* recs, int count, float
   return hit;
 }
 
+// Compositing of one warp's 8 x (4 kPix) pixel block (rows r0 .. r0 + 7,
+// columns c0 .. c0 + 4 kPix - 1; the lane's row pr and first column pc0)
+// from the tile's `count` sorted records in shared memory, into the lane's
+// value / trans / done; `cut` is the warp's scratch for the records' cutoffs.
+// Warp-wide.
+template <int kPix>
+__device__ __forceinline__ void composite_block(const Rec* s_rec, float2* cut, int count, int r0,
+                                                int c0, int pr, int pc0, int lane,
+                                                float (&value)[kPix], float (&trans)[kPix],
+                                                bool (&done)[kPix]) {
+  // hit[i] bit k: record k's cutoff box meets columns [c0 + 4i, c0 + 4i + 3]
+  // of rows [r0, r0 + 7]
+  uint64_t hit[kPix];
+#pragma unroll
+  for (int i = 0; i < kPix; ++i) hit[i] = 0;
+  const float by0 = (float)r0, by1 = (float)(r0 + 7);
+  for (int h = 0; h < (count > 32 ? 2 : 1); ++h) {
+    const int k = lane + 32 * h;
+    bool in[kPix];
+#pragma unroll
+    for (int i = 0; i < kPix; ++i) in[i] = false;
+    if (k < count) {
+      const Rec& g = s_rec[k];
+      const float cutoff = density_cutoff(g);
+      cut[k] = make_float2(cutoff, density_log2_scale(g));
+      const float2 e = density_extent(g, cutoff);
+      const float mdy = fmaxf(0.0f, fmaxf(by0 - g.my, g.my - by1));
+      if (!(mdy > e.y)) {
+#pragma unroll
+        for (int i = 0; i < kPix; ++i) {
+          const float hx0 = (float)(c0 + 4 * i), hx1 = hx0 + 3.0f;
+          const float mdx = fmaxf(0.0f, fmaxf(hx0 - g.mx, g.mx - hx1));
+          in[i] = !(mdx > e.x);
+        }
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < kPix; ++i)
+      hit[i] |= (uint64_t)__ballot_sync(0xffffffffu, in[i]) << (32 * h);
+  }
+  __syncwarp();
+  // Records in two passes of 32 (32-bit masks): the lane visits, in list
+  // order, the records marked for any of its pixels, and each pixel takes
+  // those marked for its quarter. A pixel whose transmittance ran out drops
+  // its mask (and the lane's pending records are narrowed to the others').
+  // A density that is NaN or below 1e-8 (the reference's gamma < 1e-8 skip,
+  // and its fmaxf(NaN, 0)) contributes nothing.
+  const float fy = (float)pr;
+  const float4* recs4 = reinterpret_cast<const float4*>(s_rec);
+  float px[kPix];
+#pragma unroll
+  for (int i = 0; i < kPix; ++i) px[i] = (float)(pc0 + 4 * i);
+  for (int h = 0; h < (count > 32 ? 2 : 1); ++h) {
+    uint32_t m[kPix];
+    uint32_t todo = 0;
+#pragma unroll
+    for (int i = 0; i < kPix; ++i) {
+      m[i] = done[i] ? 0u : (uint32_t)(hit[i] >> (32 * h));
+      todo |= m[i];
+    }
+    while (todo) {
+      const int kk = __ffs(todo) - 1;
+      todo &= todo - 1u;
+      const int k = 32 * h + kk;
+      // mx my cxx cxy | cyy inv_det norm sigma | s_pos z yr pos
+      const float4 ra = recs4[3 * k], rb = recs4[3 * k + 1], rc = recs4[3 * k + 2];
+      const float2 c = cut[k];
+      // the row's part of compute_gaussian_density_2d's quadratic form,
+      // shared by the lane's pixels (same range row)
+      const float dy = sub_(fy, ra.y);
+      const float qy = mul_(ra.z, dy);     // cxx * dy
+      const float cxy2 = mul_(2.0f, ra.w);
+#pragma unroll
+      for (int i = 0; i < kPix; ++i) {
+        if ((m[i] >> kk) & 1u) {
+          const float dx = sub_(px[i], ra.x);
+          const float q = fma_(qy, dy, fma_(mul_(rb.x, dx), dx, -mul_(mul_(cxy2, dx), dy)));
+          const float exponent = mul_(mul_(-0.5f, q), rb.y);
+          if (!(exponent < c.x)) {
+            const float gamma_ipp = ex2_approx(__fmaf_rn(exponent, 1.4426950408889634f, c.y));
+            if (gamma_ipp >= 1e-8f) {
+              const float sigma = rb.w;
+              const float alpha_i = mul_(sigma, gamma_ipp);
+              value[i] = fma_(mul_(trans[i], alpha_i), rc.x, value[i]);
+              trans[i] = mul_(trans[i], fma_(-sigma, gamma_ipp, 1.0f));
+              if (trans[i] < 1e-8f) {
+                trans[i] = 0.0f;
+                done[i] = true;
+                m[i] = 0u;
+                uint32_t keep = 0;
+#pragma unroll
+                for (int j = 0; j < kPix; ++j) keep |= m[j];
+                todo &= keep;
+              }
+            }
+          }
+        }
+      }
+    }
+  }
+}
+
 // One CTA per tile: the tile's sorted records arrive with one TMA bulk copy;
 // warp w composites an 8 x (4 kPix) pixel block, each lane kPix pixels of one
 // range row (azimuth columns c, c + 4; lanes along range, contiguous in the
@@ -2018,93 +2148,94 @@ __global__ void __launch_bounds__(kTile * kTile / kPix) render_kernel(const Tile
   }
   if (count > 0) {
     const bool ok = load_tile_recs(s_rec, &bar, st, a.st.L, t, count, a.err, true);
-    if (__syncthreads_and(ok)) {
-      // hit[i] bit k: record k's cutoff box meets columns [c0 + 4i, c0 + 4i + 3]
-      // of rows [r0, r0 + 7]
-      uint64_t hit[kPix];
-#pragma unroll
-      for (int i = 0; i < kPix; ++i) hit[i] = 0;
-      float2* cut = s_cut[warp];
-      const float by0 = (float)r0, by1 = (float)(r0 + 7);
-      for (int h = 0; h < (count > 32 ? 2 : 1); ++h) {
-        const int k = lane + 32 * h;
-        bool in[kPix];
-#pragma unroll
-        for (int i = 0; i < kPix; ++i) in[i] = false;
-        if (k < count) {
-          const Rec& g = s_rec[k];
-          const float cutoff = density_cutoff(g);
-          cut[k] = make_float2(cutoff, density_log2_scale(g));
-          const float2 e = density_extent(g, cutoff);
-          const float mdy = fmaxf(0.0f, fmaxf(by0 - g.my, g.my - by1));
-          if (!(mdy > e.y)) {
-#pragma unroll
-            for (int i = 0; i < kPix; ++i) {
-              const float hx0 = (float)(c0 + 4 * i), hx1 = hx0 + 3.0f;
-              const float mdx = fmaxf(0.0f, fmaxf(hx0 - g.mx, g.mx - hx1));
-              in[i] = !(mdx > e.x);
-            }
-          }
-        }
-#pragma unroll
-        for (int i = 0; i < kPix; ++i)
-          hit[i] |= (uint64_t)__ballot_sync(0xffffffffu, in[i]) << (32 * h);
-      }
-      __syncwarp();
-      // Records in two passes of 32 (32-bit masks); per pixel, the marked
-      // records it still needs (a pixel whose transmittance ran out drops its
-      // mask). Each pixel visits its records in list order.
-      const float fy = (float)pr;
-      const float4* recs4 = reinterpret_cast<const float4*>(s_rec);
-      for (int h = 0; h < (count > 32 ? 2 : 1); ++h) {
-        uint32_t m[kPix];
-        uint32_t todo = 0;
-#pragma unroll
-        for (int i = 0; i < kPix; ++i) {
-          m[i] = done[i] ? 0u : (uint32_t)(hit[i] >> (32 * h));
-          todo |= m[i];
-        }
-        while (todo) {
-          const int kk = __ffs(todo) - 1;
-          const uint32_t bit = 1u << kk;
-          const int k = 32 * h + kk;
-          // mx my cxx cxy | cyy inv_det norm sigma | s_pos z yr pos
-          const float4 ra = recs4[3 * k], rb = recs4[3 * k + 1], rc = recs4[3 * k + 2];
-          const float2 c = cut[k];
-          // the row's part of compute_gaussian_density_2d's quadratic form,
-          // shared by the lane's pixels (same range row)
-          const float dy = sub_(fy, ra.y);
-          const float qy = mul_(ra.z, dy);     // cxx * dy
-          const float cxy2 = mul_(2.0f, ra.w);
-          todo = 0;
-#pragma unroll
-          for (int i = 0; i < kPix; ++i) {
-            if (m[i] & bit) {
-              const float dx = sub_((float)(pc0 + 4 * i), ra.x);
-              const float q = fma_(qy, dy, fma_(mul_(rb.x, dx), dx, -mul_(mul_(cxy2, dx), dy)));
-              const float exponent = mul_(mul_(-0.5f, q), rb.y);
-              float gamma_ipp = 0.0f;
-              if (!(exponent < c.x))
-                gamma_ipp = fmaxf(ex2_approx(__fmaf_rn(exponent, 1.4426950408889634f, c.y)), 0.0f);
-              if (gamma_ipp >= 1e-8f) {
-                const float sigma = rb.w;
-                const float alpha_i = mul_(sigma, gamma_ipp);
-                value[i] = fma_(mul_(trans[i], alpha_i), rc.x, value[i]);
-                trans[i] = mul_(trans[i], fma_(-sigma, gamma_ipp, 1.0f));
-                if (trans[i] < 1e-8f) {
-                  trans[i] = 0.0f;
-                  done[i] = true;
-                }
-              }
-              m[i] = done[i] ? 0u : (m[i] & ~bit);
-            }
-            todo |= m[i];
-          }
-        }
-      }
-    }
+    if (__syncthreads_and(ok))
+      composite_block<kPix>(s_rec, s_cut[warp], count, r0, c0, pr, pc0, lane, value, trans, done);
   }
   float* img = a.images + v * a.img_vstride;
+  if (pr < Nr) {
+#pragma unroll
+    for (int i = 0; i < kPix; ++i)
+      if (pc0 + 4 * i < Na) img[(size_t)(pc0 + 4 * i) * Nr + pr] = value[i];
+  }
+}
+
+// Image-only launches of many views: select_kernel's selection and
+// render_kernel<4>'s compositing of one tile in one CTA of two warps, the
+// tile's list and records kept in shared memory (neither is written to the
+// state). Warp w emits need entries w, w + 2, ... (entries fill disjoint list
+// slots); thread s builds the record of list slot s; each warp ranks all
+// slots by (Z_r, slot) and places its own slots' records; then each warp
+// composites its 8 x 16 pixel block as render_kernel<4> does. The records
+// and the image equal select_kernel's and render_kernel<4>'s. On one SM the
+// dependent gathers of some CTAs' selection overlap other CTAs' compositing.
+constexpr int kFusedPix = 4;
+constexpr int kFusedThreads = kTile * kTile / kFusedPix;
+
+__global__ void __launch_bounds__(kFusedThreads, 16) select_render_kernel(const SelectArgs sa,
+                                                                         const TileArgs ta) {
+  constexpr int kPix = kFusedPix;
+  static_assert(kFusedThreads == kCap, "one thread per list slot");
+  static_assert(kFusedThreads == 64, "two warps: 8-row halves of the tile");
+  __shared__ __align__(16) Rec s_rec[kCap];
+  __shared__ float2 s_cut[2][kCap];
+  __shared__ int s_list[kCap];
+  __shared__ float s_z[kCap];
+  __shared__ int s_rank[2][kCap];
+  const int v = blockIdx.y, t = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const ViewConst& vc = sa.views[v];
+  const int Nr = vc.h.Nr, Na = vc.h.Na, tiles_x = vc.tiles_x, T = tiles_x * vc.tiles_y;
+  const int tx = t % tiles_x, ty = t / tiles_x;
+  // warp block: 8 range rows x 16 azimuth columns
+  const int r0 = ty * kTile + warp * 8, c0 = tx * kTile;
+  const int pr = r0 + (lane & 7), pc0 = c0 + (lane >> 3);
+  unsigned char* st = sa.st.base + v * sa.st.vstride;
+  const int count = reinterpret_cast<const int*>(st + sa.st.L.count)[t];
+
+  float value[kPix], trans[kPix];
+  bool done[kPix];
+#pragma unroll
+  for (int i = 0; i < kPix; ++i) {
+    value[i] = 0.0f;
+    trans[i] = 1.0f;
+    done[i] = false;
+  }
+  if (count > 0) {  // the same for the whole CTA
+    const int nneed = sa.need_n[v * sa.need_n_vstride + t];
+    s_list[tid] = -1;
+    const NeedRegs nr = prefetch_need<false>(sa, v, T, t, nneed, lane, warp, 2);
+    __syncthreads();
+    emit_entries(sa, v, st, tx, ty, nneed, nr, warp, 2, s_list, lane);
+    __syncthreads();
+
+    Rec rec;
+    bool nan_z = false;
+    if (tid < count) {
+      const float zr = select_record<false, false>(sa, vc, st, t, tid, s_list, rec);
+      s_z[tid] = zr;
+      nan_z = zr != zr;
+    }
+    // rank by (Z_r, slot), as select_kernel
+    int rank = 0;
+    if (__syncthreads_or(nan_z)) {
+      if (tid == 0) insertion_ranks(s_z, count, s_rank[0]);
+      __syncthreads();
+      rank = s_rank[0][tid];
+    } else {
+      int* sr = s_rank[warp];
+      const uint64_t k0 = zslot_key(s_z[lane], lane, lane < count);
+      if (count <= 32)
+        warp_sort_ranks<32>(k0, ~0ull, lane, sr);
+      else
+        warp_sort_ranks<64>(k0, zslot_key(s_z[lane + 32], lane + 32, lane + 32 < count), lane, sr);
+      __syncwarp();
+      rank = sr[tid];
+    }
+    if (tid < count) s_rec[rank] = rec;
+    __syncthreads();
+    composite_block<kPix>(s_rec, s_cut[warp], count, r0, c0, pr, pc0, lane, value, trans, done);
+  }
+  float* img = ta.images + v * ta.img_vstride;
   if (pr < Nr) {
 #pragma unroll
     for (int i = 0; i < kPix; ++i)
@@ -3094,6 +3225,22 @@ cudaError_t launch_render(const TileArgs& a, const Dims& d, int nviews, cudaStre
     render_kernel<kMany><<<dim3(d.T, nviews), kTile * kTile / kMany, 0, s>>>(a);
   else
     render_kernel<1><<<dim3(d.T, nviews), 256, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
+#ifndef SARR_FUSE_SELECT_RENDER
+#define SARR_FUSE_SELECT_RENDER 1
+#endif
+bool select_render_fusable(const SelectArgs& a, int nviews) {
+  // the many-view compositing (render_kernel<4>) and a selection whose chunks
+  // after the prefix have exact lists or none (select_kernel<false, false>)
+  const bool all = a.segmask && a.segmask_to >= a.C;
+  return SARR_FUSE_SELECT_RENDER && nviews >= 16 && SARR_RENDER_MANY_PIX == kFusedPix && !all;
+}
+
+cudaError_t launch_select_render(const SelectArgs& sa, const TileArgs& ta, const Dims& d,
+                                 int nviews, cudaStream_t s) {
+  select_render_kernel<<<dim3(d.T, nviews), kFusedThreads, 0, s>>>(sa, ta);
   return cudaGetLastError();
 }
 

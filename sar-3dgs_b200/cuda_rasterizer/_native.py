@@ -322,7 +322,7 @@ def launch_count():
     return int(lib().sarr_launch_count())
 
 
-KERNEL_KINDS = 13
+KERNEL_KINDS = 14
 
 
 def profile_enable(on=True):

@@ -182,6 +182,10 @@ class ViewParallelTrainer:
         self.loss_w = (l1_weight / self.world, ssim_weight / self.world, window_size)
         self.betas, self.eps = betas, eps
         self.steps_done = 0
+        # SH coefficients in use (the active degree's (d + 1)^2): the others
+        # are neither rendered nor given gradients, as the reference's
+        # get_active_sh_coeffs slice (gaussian_model.py:334-337) leaves them
+        self.sh_active = k
         self._buf_key = None
         self._args = None
 
@@ -233,11 +237,13 @@ class ViewParallelTrainer:
             self._args = a
         return self._args
 
-    def step(self, views, targets):
+    def step(self, views, targets, update=True):
         """One training step over this rank's `views` (SarrView list) against
         `targets` [V, Nr, Na] (the rasterizer's memory layout). Returns this
         rank's losses [3] (total, L1, D-SSIM; device tensor) of the weighted
-        loss (the mean over all ranks' views is their sum)."""
+        loss (the mean over all ranks' views is their sum). update=False
+        stops after the all-reduces: the summed gradients are in place
+        (gradients()) and no parameter changes."""
         import ctypes
         N = self._N
         L = N.lib()
@@ -251,8 +257,9 @@ class ViewParallelTrainer:
             st = N._stream(dev)
             N._check(L.sarr_gaussian_params(n, A["scales"], A["rotations"], A["cov6"], N.SARR_COV6,
                                             A["logits"], A["sigma"], st), "sarr_gaussian_params")
+            ka = self.sh_active
             N._check(L.sarr_forward(vs, V, n, A["means"], A["cov6"], N.SARR_COV6, A["sigma"], A["sh"],
-                                    k, k, P(self.images), None, states, ws, wsb, st), "sarr_forward")
+                                    k, ka, P(self.images), None, states, ws, wsb, st), "sarr_forward")
             l1w, ssw, win = self.loss_w
             N._check(L.sarr_combined_loss(V, nr, na, P(self.images), P(targets), float(l1w),
                                           float(ssw), int(win), 0, P(self.losses),
@@ -260,7 +267,7 @@ class ViewParallelTrainer:
                                           self.loss_ws.numel(), st), "sarr_combined_loss")
             gm0, gl0, gsh0 = A["gptr"][0]
             N._check(L.sarr_backward(vs, V, n, A["means"], A["cov6"], N.SARR_COV6, A["sigma"],
-                                     A["sh"], k, k, P(self.grad_images), states, gm0, A["g_cov"],
+                                     A["sh"], k, ka, P(self.grad_images), states, gm0, A["g_cov"],
                                      N.SARR_COV6, gl0, gsh0, k, None, N.SARR_FLAG_TILES_ONLY, ws, wsb,
                                      st), "sarr_backward")
             # d sigmoid(logit) / d logit = sigma (1 - sigma); the same on every
@@ -273,10 +280,30 @@ class ViewParallelTrainer:
                                                  gl, gsh, k, None, N.SARR_FLAG_RANGE_ROWS, ws, wsb,
                                                  st), "sarr_backward_scatter")
                 self.gparts[b][2].mul_(dsig[g0:g1])
+                if ka < k:
+                    self.gparts[b][3][:, ka:].zero_()
                 works.append(self._allreduce_bucket(b))
+            if not update:
+                for w in (w for ws_ in works for w in ws_):
+                    w.wait()
+                return self.losses
             self.steps_done += 1
             self._update(works, st)
         return self.losses
+
+    def reset_optimizer(self):
+        """Adam from scratch (zero moments, step count 0), as the reference's
+        optimizer.state.clear() after densification."""
+        self.exp_avg.zero_()
+        self.exp_avg_sq.zero_()
+        self.steps_done = 0
+
+    def apply_update(self):
+        """The Adam update of the gradients in place (after step(update=False))."""
+        N = self._N
+        with torch.cuda.device(self.device):
+            self.steps_done += 1
+            self._update([], N._stream(self.device))
 
     def _allreduce_bucket(self, b):
         if self.world == 1:
@@ -311,3 +338,88 @@ class ViewParallelTrainer:
             works = [w for b in range(len(self.bounds)) for w in self._allreduce_bucket(b)]
             for w in works:
                 w.wait()
+
+
+def sh_degree_at(iteration: int, interval: int = 1000, max_degree: int = 3) -> int:
+    """Active SH degree at an iteration: one more every `interval` iterations
+    up to max_degree (the 0 -> 3 ramp of full training; the reference's
+    iteration rule is train_gui.py:951-961, with its own interval)."""
+    return min(iteration // interval, max_degree)
+
+
+def densify_due(iteration: int, n: int, interval: int = 100, start: int = 0,
+                max_gaussians: int = 2_000_000) -> bool:
+    """DensifyPruneManager.should_densify_or_prune (training/densify_prune.py:
+    53-86) without its epoch throttle: past `start`, on a multiple of
+    `interval`, and with the set below max_gaussians."""
+    return iteration > start and iteration % interval == 0 and n < max_gaussians
+
+
+class DensifyingTrainer:
+    """Full training with densification and pruning, data-parallel over views:
+    TrainingPipeline.train_step (training/training_pipeline.py:148-212) with
+    DensifyPruneManager (training/densify_prune.py:53-141) and the SH-degree
+    ramp, on ViewParallelTrainer.
+
+    Each step sets the active SH degree from the iteration (sh_degree_at),
+    computes the step's gradients and all-reduces them. When densification is
+    due (densify_due), the Gaussian set is densified and pruned from the
+    all-reduced means gradient (GaussianModel.densify_and_prune,
+    gaussian_model.py:433-566, through sarr_densify_flags/_apply); every rank
+    holds the same parameters and the same summed gradient, and the kernels
+    are deterministic, so every rank gets the same new set. Then, as the
+    reference's step does (optimizer.state.clear(), then optimizer.step()):
+    if the set changed, this step updates nothing (the new parameters have no
+    gradient) and training continues on a new ViewParallelTrainer over the new
+    set; if it did not, Adam restarts from zero moments with this step's
+    gradients. `history` records each densification as (iteration, n before,
+    clones, splits, prunes, n after).
+    """
+
+    def __init__(self, means, scales_log, rotations, opacity_logits, sh, lr=1e-3, group=None,
+                 buckets=4, densify_interval=100, densify_start=0, grad_threshold=2e-4,
+                 size_threshold=0.01, large_scale_threshold=2.0, opacity_threshold=0.005,
+                 max_gaussians=2_000_000, sh_interval=1000, max_sh_degree=3, **trainer_kw):
+        self.lr, self.group, self.buckets, self.trainer_kw = lr, group, buckets, trainer_kw
+        self.densify_interval, self.densify_start = densify_interval, densify_start
+        self.thresholds = (grad_threshold, size_threshold, large_scale_threshold, opacity_threshold)
+        self.max_gaussians = max_gaussians
+        self.sh_interval, self.max_sh_degree = sh_interval, max_sh_degree
+        self.iteration = 0
+        self.history = []
+        self.tr = self._trainer(means, scales_log, rotations, opacity_logits, sh)
+
+    def _trainer(self, means, scales_log, rotations, logits, sh):
+        return ViewParallelTrainer(means, scales_log, rotations, logits, sh, lr=self.lr,
+                                   group=self.group, buckets=self.buckets, **self.trainer_kw)
+
+    @property
+    def n(self) -> int:
+        return self.tr.n
+
+    def step(self, views, targets):
+        """One iteration over this rank's views; returns its losses [3]."""
+        tr, it = self.tr, self.iteration
+        degree = sh_degree_at(it, self.sh_interval, self.max_sh_degree)
+        tr.sh_active = min((degree + 1) ** 2, tr.k)
+        due = densify_due(it, tr.n, self.densify_interval, self.densify_start, self.max_gaussians)
+        losses = tr.step(views, targets, update=not due)
+        if due:
+            self._densify()
+        self.iteration += 1
+        return losses
+
+    def _densify(self):
+        from . import densify as DZ
+        tr = self.tr
+        grad_means = tr.gradients()[0]
+        out, counts = DZ.densify_and_prune_tensors(tr.means, tr.scales, tr.rotations, tr.logits, tr.sh,
+                                                   grad_means, *self.thresholds, self.max_gaussians)
+        clones, splits, prunes, new = counts
+        n_before = tr.n
+        if prunes == 0 and new == 0:
+            tr.reset_optimizer()
+            tr.apply_update()
+        else:
+            self.tr = self._trainer(*out)
+        self.history.append((self.iteration, n_before, clones, splits, prunes, self.tr.n))

@@ -74,9 +74,9 @@ def test_many_view_launch_matches_single_views():
     _check_batch_vs_single(sc, views, want_omega=True)
 
 
-def test_cell_culling_edge_cases():
+def _edge_scene():
     """Non-finite centres, near-singular and very elongated covariances (no
-    cell), transmittances below 0.01, and a flat scene (zero z extent)."""
+    cell), transmittances below 0.01, in a flat scene (zero z extent)."""
     g = torch.Generator().manual_seed(52)
     sc = S.make_scene(120000, (30.0, 30.0, 0.0), (0.02, 0.6), seed=53)
     n = sc["means"].shape[0]
@@ -92,9 +92,53 @@ def test_cell_culling_edge_cases():
     sc["cov33"][idx[100:100 + k]] = cov
     sc["cov6"][idx[100:100 + k]] = S.cov33_to_cov6(cov)
     sc["sigma"][idx[5000:9000]] = 0.005
-    sc = {key: v.cuda() for key, v in sc.items()}
+    return {key: v.cuda() for key, v in sc.items()}
+
+
+def test_cell_culling_edge_cases():
+    """Non-finite centres, near-singular and very elongated covariances (no
+    cell), transmittances below 0.01, and a flat scene (zero z extent)."""
+    sc = _edge_scene()
     views = S.sweep_views(64, rho=0.15)[::7]  # 10 views
     _check_batch_vs_single(sc, views, want_omega=True)
+
+
+@pytest.mark.parametrize("scene", ["sweep", "edge"])
+def test_fused_select_render_matches_separate_kernels(scene):
+    """Image-only calls of 16 views or more select and composite each tile in
+    one kernel (the tile's list and records stay in shared memory); the same
+    call with per-view states runs the separate selection and compositing
+    kernels. The images agree bit for bit whatever the workspace holds, and
+    equal those of single-view calls."""
+    if scene == "sweep":
+        sc = {k: v.cuda() for k, v in
+              S.make_scene(150000, (40.0, 40.0, 10.0), (0.05, 0.5), seed=58).items()}
+        views = S.sweep_views(160)[::8]  # 20 views
+    else:
+        sc = _edge_scene()
+        views = S.sweep_views(66, rho=0.15)[::3]  # 22 views
+    inputs = _native.prepare_inputs(sc["means"], sc["cov6"], sc["sigma"], sc["sh"])
+    n = inputs[0].shape[0]
+    vs = [_native.make_view(*v) for v in views]
+    V, nr, na = len(vs), views[0][8], views[0][9]
+    sbytes = _native.state_bytes(n, nr, na)
+    states = torch.empty(V * sbytes, dtype=torch.uint8, device="cuda")
+    ref = torch.empty((V, nr, na), dtype=torch.float32, device="cuda")
+    _native.forward(vs, *inputs, ref, states=states, check_device=True)
+    wsb = _native.workspace_bytes(n, nr, na, V)
+    for fill in ("zero", "ff", "random"):
+        ws = torch.zeros(wsb, dtype=torch.uint8, device="cuda")
+        if fill == "ff":
+            ws.fill_(255)
+        elif fill == "random":
+            ws.random_(0, 256, generator=torch.Generator(device="cuda").manual_seed(13))
+        imgs = torch.full((V, nr, na), float("nan"), device="cuda")
+        _native.forward(vs, *inputs, imgs, ws=ws, check_device=True)
+        assert torch.equal(imgs, ref)
+    one = torch.empty((1, nr, na), dtype=torch.float32, device="cuda")
+    for k in (0, V // 2, V - 1):
+        _native.forward([vs[k]], *inputs, one, check_device=True)
+        assert torch.equal(one[0], ref[k])
 
 
 def test_cell_culling_backward_equals_sum_of_single_views():

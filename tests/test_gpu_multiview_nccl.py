@@ -4,7 +4,9 @@ trainable gradients, and every rank ends with the gradients of one process's
 backward over all views (equal up to float summation order). The training
 step (ViewParallelTrainer: bucketed all-reduce overlapped with Adam) leaves
 identical parameters on both ranks, equal to one process's training on all
-views. Skipped with fewer than 2 visible GPUs."""
+views; full training with densification (DensifyingTrainer) leaves the same
+Gaussian set and parameters on both ranks. Skipped with fewer than 2 visible
+GPUs."""
 import datetime
 import os
 import socket
@@ -87,7 +89,24 @@ def _worker(rank, world, port, q):
         other = tr.param.clone()
         dist.broadcast(other, src=0)
         same_params = bool(torch.equal(other, tr.param))
-        q.put((rank, same_images and same_params, errs))
+        # full training with densification (iterations 2 and 4): every rank
+        # densifies from the same summed gradient, so the sets stay identical
+        dt = multiview.DensifyingTrainer(sc["means"], scales, rot, logits, sc["sh"], buckets=3,
+                                         densify_interval=2, grad_threshold=1e-7, size_threshold=1.0,
+                                         sh_interval=2)
+        for _ in range(5):
+            dt.step(vs[a:b], targets[a:b])
+        torch.cuda.synchronize()
+        n_t = torch.tensor([dt.n], device=dev)
+        n_0 = n_t.clone()
+        dist.broadcast(n_0, src=0)
+        same_dense = bool(torch.equal(n_0, n_t)) and len(dt.history) == 2 and dt.n != n
+        if same_dense:
+            for t in (dt.tr.param, dt.tr.scales, dt.tr.rotations):
+                o = t.clone()
+                dist.broadcast(o, src=0)
+                same_dense = same_dense and bool(torch.equal(o, t))
+        q.put((rank, same_images and same_params and same_dense, errs))
     except Exception as e:  # reported to the parent
         q.put((rank, "error", repr(e)))
     finally:

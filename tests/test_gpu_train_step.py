@@ -169,3 +169,59 @@ def test_adam_ranges_equal_per_range_calls():
     assert st == 0
     torch.cuda.synchronize()
     assert torch.equal(a, b) and torch.equal(ma, mb) and torch.equal(va, vb)
+
+
+def test_densifying_trainer_sh_ramp_and_densification():
+    """DensifyingTrainer: (1) at SH degree d only the first (d + 1)^2
+    coefficients are rendered and trained, the others keep their values;
+    (2) densification runs on the due iterations from the step's summed means
+    gradient, the new set is densify_and_prune_tensors' output, and that step
+    updates nothing; (3) a densification that changes nothing restarts Adam:
+    one update from zero moments."""
+    from cuda_rasterizer import densify
+    n = 20000
+    means, scales, rot, logits, sh = _scene_params(n, 84)
+    views_t = S.training_views(8)
+    views = [_native.make_view(*v) for v in views_t]
+    tgt = S.named_scene("target_20k", seed=1, device="cuda")
+    targets = M.render_sar_batched(tgt["means"], tgt["cov6"], tgt["sigma"], tgt["sh"], views_t)
+    # clone every Gaussian of norm(scale) < 1 m with a nonzero gradient
+    dt = multiview.DensifyingTrainer(means, scales, rot, logits, sh, buckets=1, densify_interval=3,
+                                     grad_threshold=0.0, size_threshold=1.0, sh_interval=2)
+    dt.step(views, targets)
+    dt.step(views, targets)  # iterations 0 and 1: degree 0
+    torch.cuda.synchronize()
+    assert torch.equal(dt.tr.sh[:, 1:], sh[:, 1:])
+    assert not torch.equal(dt.tr.sh[:, 0], sh[:, 0])
+    dt.step(views, targets)  # iteration 2: degree 1
+    torch.cuda.synchronize()
+    assert torch.equal(dt.tr.sh[:, 4:], sh[:, 4:])
+    assert not torch.equal(dt.tr.sh[:, 1:4], sh[:, 1:4])
+    assert dt.history == []
+
+    old = dt.tr
+    before = [t.clone() for t in (old.means, old.scales, old.rotations, old.logits, old.sh)]
+    dt.step(views, targets)  # iteration 3: densification
+    torch.cuda.synchronize()
+    out, counts = densify.densify_and_prune_tensors(*before, old.gradients()[0], 0.0, 1.0, 2.0,
+                                                    0.005, 2_000_000)
+    assert counts[3] > 0
+    assert dt.history == [(3, n) + tuple(counts[:3]) + (out[0].shape[0],)]
+    assert dt.n == out[0].shape[0] != n
+    for got, want in zip((dt.tr.means, dt.tr.scales, dt.tr.rotations, dt.tr.logits, dt.tr.sh), out):
+        assert torch.equal(got, want.reshape(got.shape))
+    assert dt.tr.steps_done == 0
+    dt.step(views, targets)  # the new set trains
+    torch.cuda.synchronize()
+    assert dt.tr.steps_done == 1 and not torch.equal(dt.tr.means, out[0])
+
+    dt2 = multiview.DensifyingTrainer(means, scales, rot, logits, sh, buckets=1, densify_interval=1,
+                                      grad_threshold=1e30, large_scale_threshold=1e30,
+                                      opacity_threshold=0.0)
+    dt2.step(views, targets)  # iteration 0: not due
+    dt2.step(views, targets)  # iteration 1: due, nothing changes
+    torch.cuda.synchronize()
+    assert dt2.history == [(1, n, 0, 0, 0, n)]
+    assert dt2.tr.steps_done == 1
+    g = torch.cat([x.reshape(-1) for x in dt2.tr.gradients()])
+    assert torch.allclose(dt2.tr.exp_avg, 0.1 * g, rtol=1e-5, atol=0)

@@ -75,6 +75,18 @@ def _run(world, fail_rank=-1):
     return sorted(results, key=lambda x: x[0])
 
 
+def test_densify_schedule_and_sh_ramp():
+    """The full-training schedule: densification on multiples of the
+    interval past the start while the set is below the cap; the SH degree
+    one higher every interval up to the maximum."""
+    due = [i for i in range(0, 501) if multiview.densify_due(i, 1000, 100, 0, 2_000_000)]
+    assert due == [100, 200, 300, 400, 500]
+    assert not multiview.densify_due(200, 2_000_000, 100, 0, 2_000_000)
+    assert [i for i in range(0, 301) if multiview.densify_due(i, 10, 100, 100, 50)] == [200, 300]
+    degs = [multiview.sh_degree_at(i, 1000, 3) for i in (0, 999, 1000, 2500, 3000, 9000)]
+    assert degs == [0, 0, 1, 2, 3, 3]
+
+
 def test_allreduce_and_sharding_two_ranks():
     res = _run(2)
     assert [r[1] for r in res] == [True, True]
