@@ -395,7 +395,7 @@ int64_t sarr_launch_count(void);
  * then clears the record. Kinds are numbered 0 .. SARR_KERNEL_KINDS-1 and
  * named by sarr_kernel_name(). Intended for one device per process.
  */
-#define SARR_KERNEL_KINDS 14
+#define SARR_KERNEL_KINDS 15
 int sarr_profile_enable(int enable);
 int sarr_profile_read(double *total_ms, int64_t *launches, int n_kinds);
 const char *sarr_kernel_name(int kind);

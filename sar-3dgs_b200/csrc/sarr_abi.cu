@@ -128,14 +128,15 @@ int cuda_status(cudaError_t e) { return e == cudaSuccess ? SARR_OK : SARR_ERR_CU
 enum KernelKind {
   kKindSetup = 0, kKindBin, kKindSelect, kKindSelectShadow, kKindRender, kKindOmegaTile,
   kKindOmegaScatter, kKindBwdTile, kKindBwdScatter, kKindAux, kKindScan, kKindBinSkip,
-  kKindBinFinalize, kKindSelectRender, kKindCount
+  kKindBinFinalize, kKindSelectRender, kKindBinCand, kKindCount
 };
 static_assert(kKindCount == SARR_KERNEL_KINDS, "kernel kinds");
 
 const char* const kKindNames[kKindCount] = {
     "view_setup", "bin_kernel", "select_kernel", "select_kernel_shadow", "render_kernel",
     "omega_tile_kernel", "omega_scatter_kernel", "bwd_tile_kernel", "bwd_scatter_kernel", "aux",
-    "scan_kernel", "bin_skip_kernel", "bin_finalize_kernel", "select_render_kernel"};
+    "scan_kernel", "bin_skip_kernel", "bin_finalize_kernel", "select_render_kernel",
+    "bin_cand_kernel"};
 
 struct ProfRecord {
   int kind, device;
@@ -366,6 +367,7 @@ cudaError_t run_selection(const Dims& d, const Ws& w, int gv, const float* means
     o1.table[0] = const_cast<int*>(ba.open_ipp);
     o1.table[1] = const_cast<int*>(ba.open_sh);
     o1.table_vstride = ba.open_vstride;
+    o1.cand_count = nullptr;
     e = run_kernel(kKindAux, s, [&] { return launch_open_table(o1, gv, shr ? 2 : 1, s); });
     if (e != cudaSuccess) return e;
     BinArgs b2 = ba;
@@ -390,6 +392,7 @@ cudaError_t run_selection(const Dims& d, const Ws& w, int gv, const float* means
     og.table[0] = const_cast<int*>(ba.open_ipp);
     og.table[1] = const_cast<int*>(ba.open_sh);
     og.table_vstride = ba.open_vstride;
+    og.cand_count = w.L.cells ? reinterpret_cast<int*>(w.base + w.L.cand_count) : nullptr;
     e = run_kernel(kKindAux, s, [&] { return launch_open_table(og, gv, shr ? 2 : 1, s); });
     if (e != cudaSuccess) return e;
     ba.chunk_offset = prefix;
@@ -405,6 +408,9 @@ cudaError_t run_selection(const Dims& d, const Ws& w, int gv, const float* means
       ct.shadow = shr != nullptr;
       ct.bits = reinterpret_cast<uint32_t*>(w.view_area() + w.L.bits);
       ct.bits_vstride = w.L.per_view / sizeof(uint32_t);
+      ct.cand_count = og.cand_count;
+      ct.cand_words = reinterpret_cast<uint32_t*>(w.view_area() + w.L.cand_words);
+      ct.cand_vstride = ct.bits_vstride;
       ct.ipp = ipp;
       ct.sparse_from = (int64_t)prefix * kChunk;
       ct.n = d.n;
@@ -418,8 +424,11 @@ cudaError_t run_selection(const Dims& d, const Ws& w, int gv, const float* means
       ba.always = reinterpret_cast<const int*>(w.base + w.L.always);
       ba.bits = ct.bits;
       ba.bits_vstride = ct.bits_vstride;
+      ba.cand_count = ct.cand_count;
+      ba.cand_words = ct.cand_words;
+      ba.cand_vstride = ct.cand_vstride;
 
-      e = run_kernel(kKindBinSkip, s, [&] { return launch_bin_cand(ba, d, shr != nullptr, s); });
+      e = run_kernel(kKindBinCand, s, [&] { return launch_bin_cand(ba, d, shr != nullptr, s); });
       if (e != cudaSuccess) return e;
       e = run_kernel(kKindBinFinalize, s, [&] { return launch_bin_finalize(ba, d, shr != nullptr, s); });
       if (e != cudaSuccess) return e;

@@ -97,13 +97,16 @@ __device__ __forceinline__ uint32_t state_rect(const unsigned char* st, const St
 // per-cell largest bound cell_hb [kMaxCells] (ordered-int keys), the cells'
 // member lists (Gaussians after the prefix, cell by cell: cell_start
 // [kMaxCells + 1], mem_pos [n] float4 = centre and bound, mem_idx [n]), the
-// Gaussians after the prefix that are in no cell (always [n]), and each view
-// area its cell bitmap bits [kCellWords] u32.
+// Gaussians after the prefix that are in no cell (always [n]) and, per view of
+// a launch group, the number of nonzero cell-bitmap words (cand_count
+// [kMaxViewsPerLaunch]); each view area holds its cell bitmap bits
+// [kCellWords] u32 and the indices of its nonzero words (cand_words
+// [kCellWords] u32).
 struct WsLayout {
   size_t viewconst, err, scene, hb, cid, cell_hb, cell_count, cell_start, cell_center, mem_pos, mem_idx,
-      always, g_cnt, g_start, g_bsum, g_heavy, head;
+      always, cand_count, g_cnt, g_start, g_bsum, g_heavy, head;
   size_t counts_ipp, counts_sh, need_ipp, need_sh, need_n_ipp, need_n_sh, open_ipp, open_sh;
-  size_t bits, xcount, xlist, segmask_ipp, segmask_sh, state_ipp, state_sh, partial_om, partial_bwd,
+  size_t bits, cand_words, xcount, xlist, segmask_ipp, segmask_sh, state_ipp, state_sh, partial_om, partial_bwd,
       entries, per_view;
   bool cells;
   StateLayout st;
@@ -122,7 +125,7 @@ __host__ inline WsLayout ws_layout(const Dims& d, bool cells) {
   L.err = align256(sizeof(ViewConst) * kMaxViewsPerLaunch);
   size_t h = L.err + 256;
   L.scene = L.hb = L.cid = L.cell_hb = L.cell_count = L.cell_start = L.cell_center = 0;
-  L.mem_pos = L.mem_idx = L.always = 0;
+  L.mem_pos = L.mem_idx = L.always = L.cand_count = 0;
   if (cells) {
     L.scene = h;
     h += align256(sizeof(SceneGrid));
@@ -144,6 +147,8 @@ __host__ inline WsLayout ws_layout(const Dims& d, bool cells) {
     h += align256((size_t)d.n * 4);
     L.always = h;
     h += align256((size_t)d.n * 4);
+    L.cand_count = h;
+    h += align256((size_t)kMaxViewsPerLaunch * 4);
   }
   // the backward's inverse index: list entries per Gaussian, their offsets
   // (exclusive scan) and the scan's per-block sums
@@ -189,9 +194,11 @@ __host__ inline WsLayout ws_layout(const Dims& d, bool cells) {
   o += align256((size_t)d.C * 4);
   L.xlist = o;
   o += align256((size_t)d.C * kXCap * 2);
-  L.bits = 0;
+  L.bits = L.cand_words = 0;
   if (cells) {
     L.bits = o;
+    o += align256((size_t)kCellWords * 4);
+    L.cand_words = o;
     o += align256((size_t)kCellWords * 4);
   }
   L.state_ipp = o;
@@ -239,6 +246,9 @@ struct BinArgs {
   const int* always;
   const uint32_t* bits;  // cell bitmaps, bits_vstride words per view
   size_t bits_vstride;
+  const int* cand_count;        // per view: bitmap words with a candidate cell
+  const uint32_t* cand_words;   // their indices, cand_vstride words per view
+  size_t cand_vstride;
   // exactly-binned bitmaps: the xbits of the image-plane states (ipp)
   int64_t n;
   int C;
@@ -285,6 +295,9 @@ struct CellTestArgs {
   int shadow;
   uint32_t* bits;
   size_t bits_vstride;
+  int* cand_count;       // per view: nonzero bitmap words (cleared by open_table_kernel)
+  uint32_t* cand_words;  // their indices, in no particular order
+  size_t cand_vstride;
   StateRef ipp;          // its xbits are cleared and its meta set (sparse rectangles)
   int64_t sparse_from;   // first Gaussian after the prefix
   int64_t n;
@@ -324,6 +337,7 @@ struct OpenArgs {
   size_t counts_vstride;
   int* table[2];
   size_t table_vstride;  // ints
+  int* cand_count;       // nullable: per view, cleared here for cell_test_kernel
 };
 
 struct ScanArgs {

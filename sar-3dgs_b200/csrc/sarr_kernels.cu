@@ -1001,7 +1001,11 @@ __global__ void __launch_bounds__(256) cell_test_kernel(const CellTestArgs a) {
   uint32_t word = nib << (4 * (lane & 7));
 #pragma unroll
   for (int o = 1; o < 8; o <<= 1) word |= __shfl_xor_sync(0xffffffffu, word, o);
-  if ((lane & 7) == 0) a.bits[v * a.bits_vstride + (sc * kHbBuckets >> 5)] = word;
+  if ((lane & 7) == 0) {
+    const int wi = sc * kHbBuckets >> 5;
+    a.bits[v * a.bits_vstride + wi] = word;
+    if (word) a.cand_words[v * a.cand_vstride + atomicAdd(a.cand_count + v, 1)] = (uint32_t)wi;
+  }
   unsigned char* xs = a.ipp.base + v * a.ipp.vstride;
   uint32_t* xbits = reinterpret_cast<uint32_t*>(xs + a.ipp.L.xbits);
   const int64_t words = (a.n + 31) / 32;
@@ -1014,9 +1018,12 @@ __global__ void __launch_bounds__(256) cell_test_kernel(const CellTestArgs a) {
 // (bit set by cell_test_kernel) go through bin_skip_kernel's per-Gaussian
 // test; those it cannot skip, and the Gaussians in no cell, get their bit set
 // in the view's exactly-binned bitmap. bin_finalize_kernel bins them.
-// Grid: (kMaxCells / 256 cell blocks + kAlwaysBlocks, views); a warp handles
-// the 32 cells of one bitmap word, or a stride of the no-cell list.
-constexpr int kAlwaysBlocks = 64;
+// Grid: (kCandBlocks + kAlwaysBlocks, views). The first kCandBlocks CTAs'
+// warps take the view's nonzero bitmap words (cell_test_kernel's list) in
+// turn, a warp the 32 cells of one word; the others take strides of the
+// no-cell list. The bits are ORed, so the order of the words does not matter.
+constexpr int kCandBlocks = 32;
+constexpr int kAlwaysBlocks = 16;
 
 template <bool kShadow, bool kStaged>
 __global__ void __launch_bounds__(kBinThreads) bin_cand_kernel(const BinArgs a) {
@@ -1025,64 +1032,66 @@ __global__ void __launch_bounds__(kBinThreads) bin_cand_kernel(const BinArgs a) 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int v = blockIdx.y;
   const SceneGrid& g = *a.grid;
-  const int tsize = (a.views[v].tiles_x + 1) * (a.views[v].tiles_y + 1);
-  if (kStaged && (int)blockIdx.x < kMaxCells / (kWarps * 32))
-    stage_open_tables(s_open, a.open_ipp + v * a.open_vstride, a.open_sh + v * a.open_vstride, tsize,
-                      kShadow ? 2 : 1);
   uint32_t* xbits = reinterpret_cast<uint32_t*>(a.ipp.base + v * a.ipp.vstride + a.ipp.L.xbits);
-  const int cell_blocks = kMaxCells / (kWarps * 32);
-  if ((int)blockIdx.x < cell_blocks) {
-    if (!g.valid) return;
-    const int word = blockIdx.x * kWarps + warp;
-    if (word * 32 >= g.ncells) return;
-    const uint32_t cand = a.bits[v * a.bits_vstride + word];
-    if (!cand) return;
+  if ((int)blockIdx.x < kCandBlocks) {
+    const int nw = a.cand_count[v];
+    // the same for the whole CTA (the staging below synchronises it)
+    if (!g.valid || (int)blockIdx.x * kWarps >= nw) return;
+    const int tsize = (a.views[v].tiles_x + 1) * (a.views[v].tiles_y + 1);
+    if (kStaged)
+      stage_open_tables(s_open, a.open_ipp + v * a.open_vstride, a.open_sh + v * a.open_vstride, tsize,
+                        kShadow ? 2 : 1);
     const ViewConst vc = a.views[v];
     const int Nr = vc.h.Nr, Na = vc.h.Na, pitch = vc.tiles_x + 1;
     const int* open_ipp = a.open_ipp + v * a.open_vstride;
     const int* open_sh = a.open_sh + v * a.open_vstride;
-    // the members of the word's candidate cells, concatenated, 32 per round:
-    // member p of the concatenation belongs to the first lane (cell) whose
-    // inclusive member prefix exceeds p
-    const int c_l = word * 32 + lane;
-    const bool set = (cand >> lane) & 1u;
-    const int start_l = set ? a.cell_start[c_l] : 0;
-    const int cnt_l = set ? a.cell_start[c_l + 1] - start_l : 0;
-    const int incl_l = warp_incl_scan(cnt_l, lane);
-    const int total = __shfl_sync(0xffffffffu, incl_l, 31);
-    for (int p0 = 0; p0 < total; p0 += 32) {
-      const int p = p0 + lane;
-      int lo = 0, hi = 31;  // first lane with incl > p
+    const uint32_t* words = a.cand_words + v * a.cand_vstride;
+    for (int q = blockIdx.x * kWarps + warp; q < nw; q += kCandBlocks * kWarps) {
+      const int word = (int)words[q];
+      const uint32_t cand = a.bits[v * a.bits_vstride + word];
+      // the members of the word's candidate cells, concatenated, 32 per round:
+      // member p of the concatenation belongs to the first lane (cell) whose
+      // inclusive member prefix exceeds p
+      const int c_l = word * 32 + lane;
+      const bool set = (cand >> lane) & 1u;
+      const int start_l = set ? a.cell_start[c_l] : 0;
+      const int cnt_l = set ? a.cell_start[c_l + 1] - start_l : 0;
+      const int incl_l = warp_incl_scan(cnt_l, lane);
+      const int total = __shfl_sync(0xffffffffu, incl_l, 31);
+      for (int p0 = 0; p0 < total; p0 += 32) {
+        const int p = p0 + lane;
+        int lo = 0, hi = 31;  // first lane with incl > p
 #pragma unroll
-      for (int it = 0; it < 5; ++it) {
-        const int mid = (lo + hi) >> 1;
-        const int im = __shfl_sync(0xffffffffu, incl_l, mid);
-        if (im > p) hi = mid; else lo = mid + 1;
-      }
-      const int owner_start = __shfl_sync(0xffffffffu, start_l, lo);
-      const int owner_excl = __shfl_sync(0xffffffffu, incl_l - cnt_l, lo);
-      if (p < total) {
-        const int m = owner_start + (p - owner_excl);
-        const float4 p4 = a.mem_pos[m];
-        float r, cc, xr, yr;
-        approx_center(vc, p4.x, p4.y, p4.z, r, cc, xr, yr);
-        const float h = p4.w + vc.center_margin;
-        const uint32_t ri = bound_rect(r, cc, h, Nr, Na);
-        bool exact = (kStaged ? open_in_rect_s(ri, s_open, pitch) : open_in_rect(ri, open_ipp, pitch)) != 0;
-        if (kShadow && !exact) {
-          const uint32_t rs = bound_rect(yr, xr, h, Nr, Na);
-          exact = (kStaged ? open_in_rect_s(rs, s_open + tsize, pitch) : open_in_rect(rs, open_sh, pitch)) != 0;
+        for (int it = 0; it < 5; ++it) {
+          const int mid = (lo + hi) >> 1;
+          const int im = __shfl_sync(0xffffffffu, incl_l, mid);
+          if (im > p) hi = mid; else lo = mid + 1;
         }
-        if (exact) {
-          const int j = a.mem_idx[m];
-          atomicOr(xbits + (j >> 5), 1u << (j & 31));
+        const int owner_start = __shfl_sync(0xffffffffu, start_l, lo);
+        const int owner_excl = __shfl_sync(0xffffffffu, incl_l - cnt_l, lo);
+        if (p < total) {
+          const int m = owner_start + (p - owner_excl);
+          const float4 p4 = a.mem_pos[m];
+          float r, cc, xr, yr;
+          approx_center(vc, p4.x, p4.y, p4.z, r, cc, xr, yr);
+          const float h = p4.w + vc.center_margin;
+          const uint32_t ri = bound_rect(r, cc, h, Nr, Na);
+          bool exact = (kStaged ? open_in_rect_s(ri, s_open, pitch) : open_in_rect(ri, open_ipp, pitch)) != 0;
+          if (kShadow && !exact) {
+            const uint32_t rs = bound_rect(yr, xr, h, Nr, Na);
+            exact = (kStaged ? open_in_rect_s(rs, s_open + tsize, pitch) : open_in_rect(rs, open_sh, pitch)) != 0;
+          }
+          if (exact) {
+            const int j = a.mem_idx[m];
+            atomicOr(xbits + (j >> 5), 1u << (j & 31));
+          }
         }
       }
     }
   } else {
-    const int nw = (gridDim.x - cell_blocks) * kWarps;
+    const int nwarps = (gridDim.x - kCandBlocks) * kWarps;
     const int na = g.n_always;
-    for (int i = ((blockIdx.x - cell_blocks) * kWarps + warp) * 32 + lane; i < na; i += nw * 32) {
+    for (int i = ((blockIdx.x - kCandBlocks) * kWarps + warp) * 32 + lane; i < na; i += nwarps * 32) {
       const int j = a.always[i];
       atomicOr(xbits + (j >> 5), 1u << (j & 31));
     }
@@ -1177,6 +1186,7 @@ __global__ void __launch_bounds__(256) open_table_kernel(const OpenArgs a) {
   const int v = blockIdx.x, list = blockIdx.y;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int tiles_x = a.tiles_x, tiles_y = a.tiles_y, T = tiles_x * tiles_y, pitch = tiles_x + 1;
+  if (a.cand_count && list == 0 && tid == 0) a.cand_count[v] = 0;
   const int size = (tiles_y + 1) * pitch;
   const uint8_t* counts = (list ? a.counts[1] : a.counts[0]) + v * a.counts_vstride;
   int* out = (list ? a.table[1] : a.table[0]) + v * a.table_vstride;
@@ -3115,7 +3125,7 @@ cudaError_t launch_bin(const BinArgs& a, const Dims& d, int chunks, bool shadow,
 bool bin_cell_supported(const Dims& d) { return warp_count_bytes(d, true) <= kWarpCountBytes; }
 
 cudaError_t launch_bin_cand(const BinArgs& a, const Dims& d, bool shadow, cudaStream_t s) {
-  const dim3 grid(kMaxCells / kBinThreads + kAlwaysBlocks, a.nviews);
+  const dim3 grid(kCandBlocks + kAlwaysBlocks, a.nviews);
   const size_t sm = open_stage_bytes(d.tiles_x, d.tiles_y, shadow ? 2 : 1);
   if (shadow) {
     if (sm) bin_cand_kernel<true, true><<<grid, kBinThreads, sm, s>>>(a);

@@ -322,7 +322,7 @@ def launch_count():
     return int(lib().sarr_launch_count())
 
 
-KERNEL_KINDS = 14
+KERNEL_KINDS = 15
 
 
 def profile_enable(on=True):
