@@ -982,11 +982,10 @@ __global__ void __launch_bounds__(256) cell_test_kernel(const CellTestArgs a) {
     const float ds = g.half_diag * 1.0001f;
     const int* open_ipp = a.open_ipp + v * a.open_vstride;
     const int* open_sh = a.open_sh + v * a.open_vstride;
-#pragma unroll
-    for (int b = 0; b < kHbBuckets; ++b) {
-      const int c = sc * kHbBuckets + b;
-      const float hbm = key_float(a.cell_hb[c]);
-      if (!(hbm >= 0.0f)) continue;
+    // a larger bound gives a rectangle that contains the smaller one's, so
+    // the cell's largest bound is tested first: when it reaches no open tile,
+    // neither does any of its buckets (most cells of a view)
+    auto reaches_open = [&](float hbm) {
       const float base = hbm + 2.0f * vc.center_margin + 0.02f;
       const uint32_t ri = bound_rect2(r, cc, base + dr, base + dc, Nr, Na);
       bool open = (kStaged ? open_in_rect_s(ri, s_open, pitch) : open_in_rect(ri, open_ipp, pitch)) > 0;
@@ -994,7 +993,19 @@ __global__ void __launch_bounds__(256) cell_test_kernel(const CellTestArgs a) {
         const uint32_t rs = bound_rect2(yr, xr, base + ds, base + ds, Nr, Na);
         open = (kStaged ? open_in_rect_s(rs, s_open + tsize, pitch) : open_in_rect(rs, open_sh, pitch)) > 0;
       }
-      if (open) nib |= 1u << b;
+      return open;
+    };
+    float hbv[kHbBuckets];
+    float hmax = -1.0f;
+#pragma unroll
+    for (int b = 0; b < kHbBuckets; ++b) {
+      hbv[b] = key_float(a.cell_hb[sc * kHbBuckets + b]);
+      if (hbv[b] >= 0.0f && hbv[b] > hmax) hmax = hbv[b];
+    }
+    if (hmax >= 0.0f && reaches_open(hmax)) {
+#pragma unroll
+      for (int b = 0; b < kHbBuckets; ++b)
+        if (hbv[b] >= 0.0f && (hbv[b] == hmax || reaches_open(hbv[b]))) nib |= 1u << b;
     }
   }
   // word k of the warp's 4 bitmap words holds the nibbles of lanes 8k .. 8k+7
@@ -1294,24 +1305,28 @@ __global__ void __launch_bounds__(kScan1Threads) scan_kernel(const ScanArgs a) {
   }
 }
 
-// scan_kernel for tile counts that are a multiple of 4: each lane takes 4
-// adjacent tiles (one 32-bit load of their u8 counts per chunk), a CTA 128
-// tiles of one view, each warp a slice of the chunks.
+// scan_kernel for tile counts that are a multiple of 4: a CTA takes 32
+// adjacent tiles of one view, 8 lanes of a warp cover them with 4 tiles each
+// (one 32-bit load of their u8 counts per chunk, a 32-byte sector per 8
+// lanes), and the chunks are split into kScanSlices slices, four per warp
+// (one per 8-lane group). Each slice's sums give every slice the hits before
+// it; the slices that start below 64 hits then emit their need entries.
 constexpr int kScanTilesPerLane = 4;
-constexpr int kScanTilesPerCta = 32 * kScanTilesPerLane;
+constexpr int kScanTilesPerCta = 8 * kScanTilesPerLane;
+constexpr int kScanSlices = kScanThreads / 8;
 
 __global__ void __launch_bounds__(kScanThreads) scan4_kernel(const ScanArgs a) {
-  constexpr int kW = kScanThreads / 32;
-  __shared__ __align__(16) int s_part[kW][kScanTilesPerCta];
+  __shared__ __align__(16) int s_part[kScanSlices][kScanTilesPerCta];
   __shared__ int s_nneed[kScanTilesPerCta];
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  __shared__ __align__(16) int s_total[kScanTilesPerCta];
+  const int tid = threadIdx.x, grp = tid & 7, slice = tid >> 3;
   const int v = blockIdx.y;
   const int T = a.T, C = a.C;
-  const int tb = blockIdx.x * kScanTilesPerCta + kScanTilesPerLane * lane;  // the lane's first tile
+  const int tb = blockIdx.x * kScanTilesPerCta + kScanTilesPerLane * grp;  // the lane's first tile
   const bool live = tb < T;
   const uint8_t* counts = a.counts + v * a.counts_vstride;
-  const int per = (C + kW - 1) / kW;
-  const int c0 = min(warp * per, C), c1 = min(c0 + per, C);
+  const int per = (C + kScanSlices - 1) / kScanSlices;
+  const int c0 = min(slice * per, C), c1 = min(c0 + per, C);
   int sum[4] = {0, 0, 0, 0};
   if (live)
 #pragma unroll 8
@@ -1320,18 +1335,26 @@ __global__ void __launch_bounds__(kScanThreads) scan4_kernel(const ScanArgs a) {
 #pragma unroll
       for (int i = 0; i < 4; ++i) sum[i] += (w >> (8 * i)) & 0xFFu;
     }
-  *reinterpret_cast<int4*>(&s_part[warp][kScanTilesPerLane * lane]) = make_int4(sum[0], sum[1], sum[2], sum[3]);
+  *reinterpret_cast<int4*>(&s_part[slice][kScanTilesPerLane * grp]) = make_int4(sum[0], sum[1], sum[2], sum[3]);
   if (tid < kScanTilesPerCta) s_nneed[tid] = 0;
   __syncthreads();
-  int pre[4] = {0, 0, 0, 0}, total[4] = {0, 0, 0, 0};
-  for (int w = 0; w < kW; ++w) {
-    const int4 x = *reinterpret_cast<const int4*>(&s_part[w][kScanTilesPerLane * lane]);
-    const int xs[4] = {x.x, x.y, x.z, x.w};
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      pre[i] += (w < warp) ? xs[i] : 0;
-      total[i] += xs[i];
+  // the slices' sums become the hits before each slice (one lane per tile)
+  if (tid < kScanTilesPerCta) {
+    int run = 0;
+    for (int q = 0; q < kScanSlices; ++q) {
+      const int x = s_part[q][tid];
+      s_part[q][tid] = run;
+      run += x;
     }
+    s_total[tid] = run;
+  }
+  __syncthreads();
+  int pre[4], total[4];
+  {
+    const int4 x = *reinterpret_cast<const int4*>(&s_part[slice][kScanTilesPerLane * grp]);
+    const int4 y = *reinterpret_cast<const int4*>(&s_total[kScanTilesPerLane * grp]);
+    pre[0] = x.x, pre[1] = x.y, pre[2] = x.z, pre[3] = x.w;
+    total[0] = y.x, total[1] = y.y, total[2] = y.z, total[3] = y.w;
   }
   unsigned char* st = a.st.base + v * a.st.vstride;
   int4* need = reinterpret_cast<int4*>(a.need + v * a.need_vstride);
@@ -1354,7 +1377,7 @@ __global__ void __launch_bounds__(kScanThreads) scan4_kernel(const ScanArgs a) {
         for (int i = 0; i < 4; ++i) {
           const int cnt = (int)((wv[u] >> (8 * i)) & 0xFFu);
           if (cnt > 0 && pre[i] < kCap) {
-            const int q = atomicAdd(&s_nneed[kScanTilesPerLane * lane + i], 1);
+            const int q = atomicAdd(&s_nneed[kScanTilesPerLane * grp + i], 1);
             need[(size_t)(tb + i) * kCap + q] = make_int4(cb + u, pre[i], cnt, 0);
           }
           pre[i] += cnt;
@@ -1362,11 +1385,11 @@ __global__ void __launch_bounds__(kScanThreads) scan4_kernel(const ScanArgs a) {
     }
   }
   __syncthreads();
-  if (warp == 0 && live) {
+  if (slice == 0 && live) {
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       reinterpret_cast<int*>(st + a.st.L.count)[tb + i] = min(total[i], kCap);
-      a.need_n[v * a.need_n_vstride + tb + i] = s_nneed[kScanTilesPerLane * lane + i];
+      a.need_n[v * a.need_n_vstride + tb + i] = s_nneed[kScanTilesPerLane * grp + i];
     }
   }
 }
