@@ -451,11 +451,6 @@ cudaError_t run_selection(const Dims& d, const Ws& w, int gv, const float* means
   sc.need_vstride = w.L.per_view;
   sc.need_n = reinterpret_cast<int*>(w.view_area() + w.L.need_n_ipp);
   sc.need_n_vstride = w.L.per_view / sizeof(int);
-  // the open-tile tables after the prefix exist when chunks follow it
-  sc.open_tab = prefix < d.C ? ba.open_ipp : nullptr;
-  sc.open_vstride = ba.open_vstride;
-  sc.tiles_x = d.tiles_x;
-  sc.prefix = prefix;
   e = run_kernel(kKindScan, s, [&] { return launch_scan(sc, gv, s); });
   if (e != cudaSuccess) return e;
 
@@ -499,7 +494,6 @@ cudaError_t run_selection(const Dims& d, const Ws& w, int gv, const float* means
   sc.st = *shr;
   sc.need = w.view_area() + w.L.need_sh;
   sc.need_n = reinterpret_cast<int*>(w.view_area() + w.L.need_n_sh);
-  sc.open_tab = prefix < d.C ? ba.open_sh : nullptr;
   e = run_kernel(kKindScan, s, [&] { return launch_scan(sc, gv, s); });
   if (e != cudaSuccess) return e;
   sa.st = *shr;

@@ -349,12 +349,6 @@ struct ScanArgs {
   size_t need_vstride;
   int* need_n;
   size_t need_n_vstride;
-  // nullable: the open-tile table of this list after the first `prefix`
-  // chunks (open_table_kernel); chunks from `prefix` on are read only for
-  // tiles still open there
-  const int* open_tab;
-  size_t open_vstride;  // ints
-  int tiles_x, prefix;
 };
 
 struct TileArgs {

@@ -1327,25 +1327,8 @@ __global__ void __launch_bounds__(kScanThreads) scan4_kernel(const ScanArgs a) {
   const uint8_t* counts = a.counts + v * a.counts_vstride;
   const int per = (C + kScanSlices - 1) / kScanSlices;
   const int c0 = min(slice * per, C), c1 = min(c0 + per, C);
-  // A slice after the prefix is read only when one of the lane's tiles is
-  // still open after the prefix: a tile the prefix filled has its list (and
-  // its length, 64) from the prefix alone, and later slices only add to hits
-  // before them that are already >= 64, so their sums may count as 0.
-  bool needed = live;
-  if (live && a.open_tab && c0 >= a.prefix) {
-    const int* tab = a.open_tab + v * a.open_vstride;
-    const int pitch = a.tiles_x + 1;
-    int open_tiles = 0;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int t = tb + i, ty = t / a.tiles_x, tx = t - ty * a.tiles_x;
-      open_tiles += tab[(ty + 1) * pitch + tx + 1] - tab[ty * pitch + tx + 1] - tab[(ty + 1) * pitch + tx] +
-                    tab[ty * pitch + tx];
-    }
-    needed = open_tiles > 0;
-  }
   int sum[4] = {0, 0, 0, 0};
-  if (needed)
+  if (live)
 #pragma unroll 8
     for (int c = c0; c < c1; ++c) {
       const uint32_t w = *reinterpret_cast<const uint32_t*>(counts + (size_t)c * T + tb);
@@ -2222,7 +2205,7 @@ constexpr int kFusedPix = 4;
 constexpr int kFusedThreads = kTile * kTile / kFusedPix;
 
 #ifndef SARR_FUSED_MIN_CTAS
-#define SARR_FUSED_MIN_CTAS 16
+#define SARR_FUSED_MIN_CTAS 18
 #endif
 __global__ void __launch_bounds__(kFusedThreads, SARR_FUSED_MIN_CTAS)
     select_render_kernel(const SelectArgs sa, const TileArgs ta) {
