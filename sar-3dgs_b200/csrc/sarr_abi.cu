@@ -352,6 +352,13 @@ cudaError_t run_selection(const Dims& d, const Ws& w, int gv, const float* means
   ba.views_per_cta = views_per_cta(stage1);
   // one view per warp in the prefix binner once a CTA holds 8 views or more
   if (ba.views_per_cta >= 8) ba.views_per_cta = (ba.views_per_cta + 7) / 8 * 8;
+  // the first stage of a two-stage prefix keeps the hit words of its chunks
+  // (image list), which selection reads instead of re-testing rectangles
+  const bool hit_words = stage1 < prefix && w.L.hbits != 0 && masks &&
+                         prefix_hit_words(d);
+  ba.hbits = hit_words ? reinterpret_cast<uint32_t*>(w.view_area() + w.L.hbits) : nullptr;
+  ba.hbits_vstride = w.L.per_view / sizeof(uint32_t);
+  ba.hbits_to = stage1;
   cudaError_t e = run_kernel(kKindBin, s, [&] {
     return launch_bin(ba, d, stage1, shr != nullptr, false, s);
   });
@@ -371,6 +378,7 @@ cudaError_t run_selection(const Dims& d, const Ws& w, int gv, const float* means
     e = run_kernel(kKindAux, s, [&] { return launch_open_table(o1, gv, shr ? 2 : 1, s); });
     if (e != cudaSuccess) return e;
     BinArgs b2 = ba;
+    b2.hbits = nullptr;
     b2.chunk_offset = stage1;
     b2.views_per_cta = views_per_cta(prefix - stage1);
     b2.skip_masks = 1;
@@ -478,6 +486,9 @@ cudaError_t run_selection(const Dims& d, const Ws& w, int gv, const float* means
   sa.segmask = ba.segmask;
   sa.segmask_vstride = ba.segmask_vstride;
   sa.segmask_to = masks_all ? d.C : prefix;
+  sa.hbits = ba.hbits;
+  sa.hbits_vstride = ba.hbits_vstride;
+  sa.hbits_to = ba.hbits_to;
   sa.xlist_from = xlists ? prefix : INT32_MAX;
   sa.xcount = xlists ? ba.xcount : nullptr;
   sa.xlist = xlists ? ba.xlist : nullptr;
@@ -498,6 +509,7 @@ cudaError_t run_selection(const Dims& d, const Ws& w, int gv, const float* means
   if (e != cudaSuccess) return e;
   sa.st = *shr;
   sa.segmask = ba.segmask_sh;
+  sa.hbits = nullptr;  // hit words are kept for the image list only
   sa.need = sc.need;
   sa.need_n = sc.need_n;
   e = run_kernel(kKindSelectShadow, s, [&] { return launch_select(sa, d, gv, true, s); });

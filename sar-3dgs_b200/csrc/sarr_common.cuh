@@ -33,6 +33,10 @@ constexpr int kScan1Threads = 1024;              // scan_kernel (1 tile per lane
 #define SARR_PREFIX_CHUNKS 64
 #endif
 constexpr int kPrefixChunks = SARR_PREFIX_CHUNKS;  // chunks binned exactly before saturation skipping
+// Images of at most this many tiles keep per-(chunk, tile) hit words for the
+// first-stage prefix chunks (selection reads hits instead of re-testing
+// rectangles).
+constexpr int kHitBitsMaxTiles = 1024;
 #ifndef SARR_PREFIX_STAGE1
 #define SARR_PREFIX_STAGE1 8
 #endif

@@ -100,13 +100,15 @@ __device__ __forceinline__ uint32_t state_rect(const unsigned char* st, const St
 // Gaussians after the prefix that are in no cell (always [n]) and, per view of
 // a launch group, the number of nonzero cell-bitmap words (cand_count
 // [kMaxViewsPerLaunch]); each view area holds its cell bitmap bits
-// [kCellWords] u32 and the indices of its nonzero words (cand_words
-// [kCellWords] u32).
+// [kCellWords] u32, the indices of its nonzero words (cand_words
+// [kCellWords] u32) and, for images of at most kHitBitsMaxTiles tiles, the
+// hit words of the first kPrefixStage1 chunks (hbits [kPrefixStage1][T][32]
+// u32, see BinArgs::hbits).
 struct WsLayout {
   size_t viewconst, err, scene, hb, cid, cell_hb, cell_count, cell_start, cell_center, mem_pos, mem_idx,
       always, cand_count, g_cnt, g_start, g_bsum, g_heavy, head;
   size_t counts_ipp, counts_sh, need_ipp, need_sh, need_n_ipp, need_n_sh, open_ipp, open_sh;
-  size_t bits, cand_words, xcount, xlist, segmask_ipp, segmask_sh, state_ipp, state_sh, partial_om, partial_bwd,
+  size_t bits, cand_words, hbits, xcount, xlist, segmask_ipp, segmask_sh, state_ipp, state_sh, partial_om, partial_bwd,
       entries, per_view;
   bool cells;
   StateLayout st;
@@ -194,12 +196,16 @@ __host__ inline WsLayout ws_layout(const Dims& d, bool cells) {
   o += align256((size_t)d.C * 4);
   L.xlist = o;
   o += align256((size_t)d.C * kXCap * 2);
-  L.bits = L.cand_words = 0;
+  L.bits = L.cand_words = L.hbits = 0;
   if (cells) {
     L.bits = o;
     o += align256((size_t)kCellWords * 4);
     L.cand_words = o;
     o += align256((size_t)kCellWords * 4);
+    if (d.T <= kHitBitsMaxTiles) {
+      L.hbits = o;
+      o += align256((size_t)kPrefixStage1 * d.T * 32 * 4);
+    }
   }
   L.state_ipp = o;
   o += L.st.bytes;
@@ -232,6 +238,12 @@ struct BinArgs {
   size_t open_vstride;
   uint32_t* segmask;     // segment masks [chunk][T] (null: none)
   int skip_masks;        // the skipping binners write the masks of their chunks too
+  // nullable: hit words of the image list [chunk][T][32] (bit l of word r:
+  // Gaussian 32 r + l of the chunk hits the tile), written by
+  // bin_prefix_kernel for chunks < hbits_to where nonzero
+  uint32_t* hbits;
+  size_t hbits_vstride;  // words per view
+  int hbits_to;
   uint32_t* segmask_sh;
   size_t segmask_vstride;  // words per view
   int* xcount;         // exactly binned Gaussians per chunk (skip variants)
@@ -322,6 +334,9 @@ struct SelectArgs {
   const uint32_t* segmask;    // segment masks of chunks < segmask_to (null: none)
   size_t segmask_vstride;     // words
   int segmask_to;
+  const uint32_t* hbits;      // hit words of chunks < hbits_to (null: none); read
+  size_t hbits_vstride;       // only where the segment mask has the word's bit
+  int hbits_to;
   StateRef xs;                // image-plane states: exactness bits and meta of the rectangles
   int xlist_from;             // first chunk with an exact list (INT32_MAX: none)
   const int* xcount;
@@ -449,6 +464,9 @@ cudaError_t launch_cell_test(const CellTestArgs& a, const Dims& d, int nviews, c
 cudaError_t launch_bin_cand(const BinArgs& a, const Dims& d, bool shadow, cudaStream_t s);
 cudaError_t launch_bin_finalize(const BinArgs& a, const Dims& d, bool shadow, cudaStream_t s);
 bool bin_cell_supported(const Dims& d);
+// Whether the exact prefix binners can keep hit words (BinArgs::hbits) for
+// this tile grid (both bin_prefix_kernel and bin_kernel write them).
+bool prefix_hit_words(const Dims& d);
 // true when the skipping binner keeps per-warp counters (and records the
 // exact lists); false selects its CTA-wide variant
 bool skip_bin_per_warp(const Dims& d, bool shadow);

@@ -122,6 +122,25 @@ __device__ __forceinline__ void mark_rect(uint32_t* mask, uint32_t rc, int tiles
     for (int tx = tc0; tx <= tc1; ++tx) atomicOr(mask + ty * tiles_x + tx, bit);
 }
 
+// Writes the round's nonzero hit words of a rectangle's tiles (out[t * 32])
+// and clears them. Lanes whose rectangles share a tile may both write its
+// word: all ORs of the round are done (the caller synchronises the warp
+// before), so every writer writes the same word, and a lane that finds it
+// cleared by another has nothing left to write.
+__device__ __forceinline__ void flush_hit_words(uint32_t* hw, uint32_t rc, int tiles_x, uint32_t* out) {
+  if (rc == kEmptyRect) return;
+  const int tc0 = rc & 0xFF, tc1 = (rc >> 8) & 0xFF, tr0 = (rc >> 16) & 0xFF, tr1 = rc >> 24;
+  for (int tr = tr0; tr <= tr1; ++tr)
+    for (int tc = tc0; tc <= tc1; ++tc) {
+      const int t = tr * tiles_x + tc;
+      const uint32_t w = hw[t];
+      if (w) {
+        out[(size_t)t * 32] = w;
+        hw[t] = 0;
+      }
+    }
+}
+
 // Tile rectangle of the pixel box centred on (cr, cc) with half-width h,
 // clamped like the reference's bboxes.
 __device__ __forceinline__ uint32_t bound_rect(float cr, float cc, float h, int Nr, int Na) {
@@ -213,10 +232,19 @@ __global__ void __launch_bounds__(kThreads) bin_kernel(const BinArgs a) {
   const bool masks = !kSkip && a.segmask != nullptr;
   uint32_t* s_mask_ipp = reinterpret_cast<uint32_t*>(s_diff_ipp + T1 * (kShadow ? 2 : 1));
   uint32_t* s_mask_sh = s_mask_ipp + T;
+  // hit words (BinArgs::hbits) of the image list: iteration k of warp w
+  // bins segment w + k kThreads / 32 of the chunk, one Gaussian per lane, so
+  // each warp ORs one segment's word per tile in its own array
+  const bool hits = masks && a.hbits != nullptr && chunk < a.hbits_to;
+  uint32_t* s_hw = s_mask_ipp + T * (kShadow ? 2 : 1) + (tid >> 5) * T;
 
   const int64_t base = (int64_t)chunk * kChunk;
   const int gcount = (int)min((int64_t)kChunk, a.n - base);
   if (!stage_chunk(a, base, gcount, s_means, s_cov, s_sigma, &bar)) return;
+  if (hits) {
+    for (int i = lane; i < T; i += 32) s_hw[i] = 0;
+    __syncwarp();
+  }
 
   float hb[kPer];  // view-independent bbox half-width bounds (kSkip)
 #pragma unroll
@@ -297,9 +325,11 @@ __global__ void __launch_bounds__(kThreads) bin_kernel(const BinArgs a) {
       }
     } else {
       const ViewConst vcl = vc;  // local copy: loaded once for all of this thread's Gaussians
+      uint32_t* ghw = hits ? a.hbits + v * a.hbits_vstride + (size_t)chunk * T * 32 : nullptr;
 #pragma unroll
       for (int k = 0; k < kPer; ++k) {
         const int j = tid + k * kThreads;
+        uint32_t rc_hit = kEmptyRect;
         if (j < gcount) {
           uint32_t rc_ipp = kEmptyRect, rc_sh = kEmptyRect;
           if (!(s_sigma[j] < 0.01f))  // preprocess_kernel: transmittance < 0.01 -> invalid (:351)
@@ -307,11 +337,18 @@ __global__ void __launch_bounds__(kThreads) bin_kernel(const BinArgs a) {
           rects_ipp[base + j] = rc_ipp;
           diff_add(s_diff_ipp, pitch, rc_ipp);
           if (masks) mark_rect(s_mask_ipp, rc_ipp, tiles_x, 1u << (j >> 5));
+          if (hits) mark_rect(s_hw, rc_ipp, tiles_x, 1u << lane);
+          rc_hit = rc_ipp;
           if (kShadow) {
             rects_sh[base + j] = rc_sh;
             diff_add(s_diff_sh, pitch, rc_sh);
             if (masks) mark_rect(s_mask_sh, rc_sh, tiles_x, 1u << (j >> 5));
           }
+        }
+        if (hits) {
+          __syncwarp();
+          flush_hit_words(s_hw, rc_hit, tiles_x, ghw + ((tid + k * kThreads) >> 5));
+          __syncwarp();  // the words are clear before the next segment's ORs
         }
       }
     }
@@ -387,13 +424,15 @@ __device__ __forceinline__ int* x_count(const BinArgs& a, int v) {
 // same bit into masks only its warp writes.
 template <bool kAtomicOr>
 __device__ __forceinline__ void count_mark_rect(uint32_t* cnt, uint32_t* mask, uint32_t rc,
-                                                int tiles_x, uint32_t bit) {
+                                                int tiles_x, uint32_t bit, uint32_t* hw = nullptr,
+                                                uint32_t hbit = 0) {
   if (rc == kEmptyRect) return;
   const int tc0 = rc & 0xFF, tc1 = (rc >> 8) & 0xFF, tr0 = (rc >> 16) & 0xFF, tr1 = rc >> 24;
   const int w = tc1 - tc0 + 1, cells = w * (tr1 - tr0 + 1);
   int t = tr0 * tiles_x + tc0, x = 0;
   for (int e = 0; e < cells; ++e) {
     atomicAdd(cnt + (t >> 1), 1u << ((t & 1) << 4));
+    if (hw) atomicOr(hw + t, hbit);
     if (mask) {
       if (kAtomicOr) {
         atomicOr(mask + t, bit);
@@ -458,6 +497,9 @@ __global__ void __launch_bounds__(kBinThreads, SARR_PREFIX_MIN_CTAS) bin_prefix_
   uint32_t* s_cnt_sh = s_cnt + TW;
   uint32_t* s_mask = s_cnt + TW * lists;
   uint32_t* s_mask_sh = s_mask + T;
+  // hit words of the current round (image list), after every warp's counters
+  const bool hits = a.hbits != nullptr && masks && chunk < a.hbits_to;
+  uint32_t* s_hw = reinterpret_cast<uint32_t*>(s_sigma + kChunk) + kWarps * (TW + T) * lists + warp * T;
 
   const int64_t base = (int64_t)chunk * kChunk;
   const int gcount = (int)min((int64_t)kChunk, a.n - base);
@@ -480,6 +522,8 @@ __global__ void __launch_bounds__(kBinThreads, SARR_PREFIX_MIN_CTAS) bin_prefix_
     if (!__syncthreads_and(ok)) return;
   }
   for (int i = lane; i < (TW + T) * lists; i += 32) s_cnt[i] = 0;
+  if (hits)
+    for (int i = lane; i < T; i += 32) s_hw[i] = 0;
   __syncwarp();
   const float* cov = a.cov + base * cs;
 
@@ -493,8 +537,10 @@ __global__ void __launch_bounds__(kBinThreads, SARR_PREFIX_MIN_CTAS) bin_prefix_
     // every rectangle of the view is written (cell binning marks its state
     // sparse afterwards)
     if (chunk == 0 && lane == 0) *reinterpret_cast<int64_t*>(stv + a.ipp.L.meta) = INT64_MAX;
+    uint32_t* ghw = hits ? a.hbits + v * a.hbits_vstride + (size_t)chunk * T * 32 : nullptr;
     for (int r = 0; r < kChunk / 32; ++r) {
       const int j = r * 32 + lane;
+      uint32_t rc_hit = kEmptyRect;
       if (j < gcount) {
         uint32_t rc_ipp = kEmptyRect, rc_sh = kEmptyRect;
         if (!(s_sigma[j] < 0.01f)) {  // preprocess_kernel: transmittance < 0.01 -> invalid (:351)
@@ -513,13 +559,19 @@ __global__ void __launch_bounds__(kBinThreads, SARR_PREFIX_MIN_CTAS) bin_prefix_
           }
         }
         rects_ipp[j] = rc_ipp;
-        count_mark_rect<false>(s_cnt, masks ? s_mask : nullptr, rc_ipp, tiles_x, 1u << r);
+        count_mark_rect<false>(s_cnt, masks ? s_mask : nullptr, rc_ipp, tiles_x, 1u << r,
+                               hits ? s_hw : nullptr, 1u << lane);
+        rc_hit = rc_ipp;
         if (kShadow) {
           rects_sh[j] = rc_sh;
           count_mark_rect<false>(s_cnt_sh, masks ? s_mask_sh : nullptr, rc_sh, tiles_x, 1u << r);
         }
       }
       __syncwarp();  // the next round ORs another bit into the same masks
+      if (hits) {
+        flush_hit_words(s_hw, rc_hit, tiles_x, ghw + r);
+        __syncwarp();  // the words are clear before the next round's ORs
+      }
     }
     flush_counts(s_cnt, a.counts_ipp + v * a.counts_vstride + (size_t)chunk * T, T, lane);
     if (kShadow) flush_counts(s_cnt_sh, a.counts_sh + v * a.counts_vstride + (size_t)chunk * T, T, lane);
@@ -1558,8 +1610,8 @@ __device__ __forceinline__ NeedRegs prefetch_need(const SelectArgs& a, int v, in
 // chunk's exact list, its segment masks, or all of its rectangles. Warp-wide;
 // entries fill disjoint slots, so warps may split them.
 __device__ __forceinline__ void emit_entries(const SelectArgs& a, int v, const unsigned char* st,
-                                             int tx, int ty, int nneed, const NeedRegs& nr, int q0,
-                                             int qs, int* list, int lane) {
+                                             int t, int T, int tx, int ty, int nneed,
+                                             const NeedRegs& nr, int q0, int qs, int* list, int lane) {
   const uint32_t* rects = reinterpret_cast<const uint32_t*>(st + a.st.L.rects);
   const unsigned lt_mask = (1u << lane) - 1u;
   // chunks from sparse_from on keep only their exactly binned Gaussians'
@@ -1575,6 +1627,23 @@ __device__ __forceinline__ void emit_entries(const SelectArgs& a, int v, const u
     const int aux = __shfl_sync(0xffffffffu, hq ? nr.aux[1] : nr.aux[0], src);
     const int want = min(nd.z, kCap - nd.y);
     const int64_t b0 = (int64_t)nd.x * kChunk;
+    if (a.hbits && a.segmask && nd.x < a.hbits_to && nd.x < a.segmask_to) {
+      // the chunk's hit words of the tile, lane r taking word r when the
+      // segment mask (aux) marks it; their hits in order are the chunk's
+      // hits in index order
+      const uint32_t* hw = a.hbits + v * a.hbits_vstride + ((size_t)nd.x * T + t) * 32;
+      const uint32_t w = (((uint32_t)aux >> lane) & 1u) ? hw[lane] : 0u;
+      const int cnt = __popc(w);
+      int rk = warp_incl_scan(cnt, lane) - cnt;
+      uint32_t bits = w;
+      const int jb = (int)b0 + 32 * lane;
+      while (bits && rk < want) {
+        list[nd.y + rk] = jb + __ffs(bits) - 1;
+        bits &= bits - 1u;
+        ++rk;
+      }
+      continue;
+    }
     const int xc = (a.xcount && nd.x >= a.xlist_from) ? aux : -1;
     if (xc >= 0) {
       // only the chunk's exactly binned Gaussians can hit the tile
@@ -1753,7 +1822,7 @@ __global__ void __launch_bounds__(kSelectThreads, 8) select_kernel(const SelectA
       }
     }
   } else {
-    emit_entries(a, v, st, tx, ty, nneed, nr, 0, 1, list, lane);
+    emit_entries(a, v, st, t, T, tx, ty, nneed, nr, 0, 1, list, lane);
   }
   __syncwarp();
 
@@ -2241,7 +2310,7 @@ __global__ void __launch_bounds__(kFusedThreads, SARR_FUSED_MIN_CTAS)
     s_list[tid] = -1;
     const NeedRegs nr = prefetch_need<false>(sa, v, T, t, nneed, lane, warp, 2);
     __syncthreads();
-    emit_entries(sa, v, st, tx, ty, nneed, nr, warp, 2, s_list, lane);
+    emit_entries(sa, v, st, t, T, tx, ty, nneed, nr, warp, 2, s_list, lane);
     __syncthreads();
 
     Rec rec;
@@ -3090,28 +3159,34 @@ cudaError_t launch_view_setup(const ViewHostPack& pack, ViewConst* out, int* err
 }
 
 template <bool kShadow, bool kSkip>
-static void launch_bin_t(const BinArgs& a, dim3 grid, size_t smem, cudaStream_t s) {
+static void launch_bin_t(const BinArgs& a, dim3 grid, size_t smem, size_t hit_bytes_per_warp,
+                         cudaStream_t s) {
   // a launch of few CTAs (exact binning of one view's prefix chunks) uses 512
-  // threads, two Gaussians each, for a shorter chain per thread
+  // threads, two Gaussians each, for a shorter chain per thread; the hit
+  // words take one array per warp
   if (!kSkip && grid.x * grid.y < 148) {
-    if (needs_smem_attr(smem))
+    const size_t sm = smem + (512 / 32) * hit_bytes_per_warp;
+    if (needs_smem_attr(sm))
       cudaFuncSetAttribute(bin_kernel<kShadow, kSkip, 512>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           (int)smem);
-    bin_kernel<kShadow, kSkip, 512><<<grid, 512, smem, s>>>(a);
+                           (int)sm);
+    bin_kernel<kShadow, kSkip, 512><<<grid, 512, sm, s>>>(a);
     return;
   }
-  if (needs_smem_attr(smem))
+  const size_t sm = smem + (kBinThreads / 32) * hit_bytes_per_warp;
+  if (needs_smem_attr(sm))
     cudaFuncSetAttribute(bin_kernel<kShadow, kSkip, kBinThreads>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)smem);
-  bin_kernel<kShadow, kSkip, kBinThreads><<<grid, kBinThreads, smem, s>>>(a);
+                         (int)sm);
+  bin_kernel<kShadow, kSkip, kBinThreads><<<grid, kBinThreads, sm, s>>>(a);
 }
 
 // bin_prefix_kernel: staged means + transmittances, per-warp counters and
 // segment masks; larger tile grids use the CTA-wide bin_kernel.
 constexpr size_t kPrefixWarpBytes = 48 * 1024;
-static size_t prefix_warp_bytes(const Dims& d, bool shadow) {
-  return (size_t)(kBinThreads / 32) * ((d.T + 1) / 2 + d.T) * 4 * (shadow ? 2 : 1);
+static size_t prefix_warp_bytes(const Dims& d, bool shadow, bool hits) {
+  return (size_t)(kBinThreads / 32) * (((d.T + 1) / 2 + d.T) * (shadow ? 2 : 1) + (hits ? d.T : 0)) * 4;
 }
+
+bool prefix_hit_words(const Dims& d) { return d.T <= kHitBitsMaxTiles; }
 
 template <bool kShadow>
 static void launch_bin_prefix_t(const BinArgs& a, dim3 grid, size_t smem, cudaStream_t s) {
@@ -3125,8 +3200,9 @@ cudaError_t launch_bin(const BinArgs& a, const Dims& d, int chunks, bool shadow,
                        cudaStream_t s) {
   const dim3 grid(chunks, (a.nviews + a.views_per_cta - 1) / a.views_per_cta);
   // one view per warp needs views to fill the CTA's warps
-  if (!skip && a.views_per_cta >= kBinThreads / 32 && prefix_warp_bytes(d, shadow) <= kPrefixWarpBytes) {
-    const size_t smem = (size_t)4 * kChunk * 4 + prefix_warp_bytes(d, shadow);
+  const bool hits = a.hbits != nullptr;
+  if (!skip && a.views_per_cta >= kBinThreads / 32 && prefix_warp_bytes(d, shadow, hits) <= kPrefixWarpBytes) {
+    const size_t smem = (size_t)4 * kChunk * 4 + prefix_warp_bytes(d, shadow, hits);
     if (shadow) launch_bin_prefix_t<true>(a, grid, smem, s);
     else launch_bin_prefix_t<false>(a, grid, smem, s);
     return cudaGetLastError();
@@ -3137,13 +3213,15 @@ cudaError_t launch_bin(const BinArgs& a, const Dims& d, int chunks, bool shadow,
     else launch_bin_skip_t<false>(a, grid, smem, s);
     return cudaGetLastError();
   }
-  const size_t smem = bin_smem_bytes(d, a.cov_layout, shadow, !skip && a.segmask != nullptr);
+  const bool masks = !skip && a.segmask != nullptr;
+  const size_t smem = bin_smem_bytes(d, a.cov_layout, shadow, masks);
+  const size_t hw = masks && hits ? (size_t)d.T * 4 : 0;
   if (shadow) {
-    if (skip) launch_bin_t<true, true>(a, grid, smem, s);
-    else launch_bin_t<true, false>(a, grid, smem, s);
+    if (skip) launch_bin_t<true, true>(a, grid, smem, 0, s);
+    else launch_bin_t<true, false>(a, grid, smem, hw, s);
   } else {
-    if (skip) launch_bin_t<false, true>(a, grid, smem, s);
-    else launch_bin_t<false, false>(a, grid, smem, s);
+    if (skip) launch_bin_t<false, true>(a, grid, smem, 0, s);
+    else launch_bin_t<false, false>(a, grid, smem, hw, s);
   }
   return cudaGetLastError();
 }
