@@ -207,8 +207,12 @@ __device__ __forceinline__ bool stage_chunk(const BinArgs& a, int64_t base, int 
 // that for every Gaussian from a fast approximate centre and a view-independent
 // bbox bound (both with margins); only the rest are queued, compacted, and
 // binned exactly in stage 2, which keeps the warps of both stages coherent.
+#ifndef SARR_BIN_MIN_CTAS
+#define SARR_BIN_MIN_CTAS 1
+#endif
 template <bool kShadow, bool kSkip, int kThreads>
-__global__ void __launch_bounds__(kThreads) bin_kernel(const BinArgs a) {
+__global__ void __launch_bounds__(kThreads, kThreads == kBinThreads ? SARR_BIN_MIN_CTAS : 1)
+    bin_kernel(const BinArgs a) {
   constexpr int kPer = kChunk / kThreads;  // Gaussians per thread
   extern __shared__ __align__(16) unsigned char smem_raw[];
   __shared__ uint64_t bar;
