@@ -208,7 +208,7 @@ __device__ __forceinline__ bool stage_chunk(const BinArgs& a, int64_t base, int 
 // bbox bound (both with margins); only the rest are queued, compacted, and
 // binned exactly in stage 2, which keeps the warps of both stages coherent.
 #ifndef SARR_BIN_MIN_CTAS
-#define SARR_BIN_MIN_CTAS 1
+#define SARR_BIN_MIN_CTAS 4
 #endif
 template <bool kShadow, bool kSkip, int kThreads>
 __global__ void __launch_bounds__(kThreads, kThreads == kBinThreads ? SARR_BIN_MIN_CTAS : 1)
@@ -1615,7 +1615,8 @@ __device__ __forceinline__ NeedRegs prefetch_need(const SelectArgs& a, int v, in
 // entries fill disjoint slots, so warps may split them.
 __device__ __forceinline__ void emit_entries(const SelectArgs& a, int v, const unsigned char* st,
                                              int t, int T, int tx, int ty, int nneed,
-                                             const NeedRegs& nr, int q0, int qs, int* list, int lane) {
+                                             const NeedRegs& nr, int q0, int qs, int* list, int lane,
+                                             bool skip_hit_words = false) {
   const uint32_t* rects = reinterpret_cast<const uint32_t*>(st + a.st.L.rects);
   const unsigned lt_mask = (1u << lane) - 1u;
   // chunks from sparse_from on keep only their exactly binned Gaussians'
@@ -1632,6 +1633,7 @@ __device__ __forceinline__ void emit_entries(const SelectArgs& a, int v, const u
     const int want = min(nd.z, kCap - nd.y);
     const int64_t b0 = (int64_t)nd.x * kChunk;
     if (a.hbits && a.segmask && nd.x < a.hbits_to && nd.x < a.segmask_to) {
+      if (skip_hit_words) continue;  // taken by emit_hit_words
       // the chunk's hit words of the tile, lane r taking word r when the
       // segment mask (aux) marks it; their hits in order are the chunk's
       // hits in index order
@@ -1737,6 +1739,69 @@ __device__ __forceinline__ void emit_entries(const SelectArgs& a, int v, const u
   }
 }
 
+// The need entries of the chunks that have hit words (chunk < a.hbits_to,
+// at most one entry per chunk), all together in chunk order: the pairs
+// (chunk, marked segment) are taken 32 per round, one lane each, and a warp
+// scan of the words' popcounts numbers the hits in index order. Entries of
+// earlier chunks hold every hit before a later chunk's (scan_kernel emits
+// entries only while fewer than 64 hits precede the chunk), so a hit's list
+// slot is the number of hits before it. Warp-wide; nr holds the entries
+// lane and lane + 32 (prefetch_need with q0 = 0, qs = 1).
+__device__ __forceinline__ void emit_hit_words(const SelectArgs& a, int v, int t, int T, int nneed,
+                                               const NeedRegs& nr, int* list, int lane) {
+  const unsigned full = 0xffffffffu;
+  // lane c: the segment mask of chunk c's entry (0: none)
+  uint32_t mask = 0;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const bool mine = lane + 32 * h < nneed && nr.nd[h].x < a.hbits_to;
+    unsigned m = __ballot_sync(full, mine);
+    while (m) {
+      const int src = __ffs(m) - 1;
+      m &= m - 1u;
+      const int c = __shfl_sync(full, nr.nd[h].x, src);
+      const uint32_t mk = (uint32_t)__shfl_sync(full, nr.aux[h], src);
+      if (lane == c) mask = mk;
+    }
+  }
+  const int nseg = __popc(mask);
+  const int seg_incl = warp_incl_scan(nseg, lane);
+  const int pairs = __shfl_sync(full, seg_incl, 31);
+  const uint32_t* hw0 = a.hbits + v * a.hbits_vstride + (size_t)t * 32;
+  const size_t chunk_stride = (size_t)T * 32;
+  int carry = 0;  // hits numbered so far
+  for (int p0 = 0; p0 < pairs && carry < kCap; p0 += 32) {
+    const int p = p0 + lane;
+    // the pair's chunk: the first lane whose inclusive segment count exceeds p
+    int lo = 0, hi = 31;
+#pragma unroll
+    for (int it = 0; it < 5; ++it) {
+      const int mid = (lo + hi) >> 1;
+      if (__shfl_sync(full, seg_incl, mid) > p) hi = mid; else lo = mid + 1;
+    }
+    const int c = lo;
+    const int k = p - (__shfl_sync(full, seg_incl, c) - __shfl_sync(full, nseg, c));
+    uint32_t mm = __shfl_sync(full, mask, c);
+    uint32_t w = 0;
+    int r = 0;
+    if (p < pairs) {
+      for (int i = 0; i < k; ++i) mm &= mm - 1u;  // drop the chunk's first k marked segments
+      r = __ffs(mm) - 1;
+      w = hw0[c * chunk_stride + r];
+    }
+    const int cnt = __popc(w);
+    const int incl = warp_incl_scan(cnt, lane);
+    int rk = carry + incl - cnt;
+    const int jb = c * kChunk + 32 * r;
+    while (w && rk < kCap) {
+      list[rk] = jb + __ffs(w) - 1;
+      w &= w - 1u;
+      ++rk;
+    }
+    carry += __shfl_sync(full, incl, 31);
+  }
+}
+
 // One warp per tile (kSelectThreads / 32 tiles per CTA), no CTA barrier.
 //  1. emit: every needed chunk's 1024 rectangles are loaded at once (eight
 //     16-byte loads per lane) and its hits are ranked in index order with a
@@ -1826,7 +1891,9 @@ __global__ void __launch_bounds__(kSelectThreads, 8) select_kernel(const SelectA
       }
     }
   } else {
-    emit_entries(a, v, st, t, T, tx, ty, nneed, nr, 0, 1, list, lane);
+    const bool hw = a.hbits != nullptr && a.segmask != nullptr;
+    if (hw) emit_hit_words(a, v, t, T, nneed, nr, list, lane);
+    emit_entries(a, v, st, t, T, tx, ty, nneed, nr, 0, 1, list, lane, hw);
   }
   __syncwarp();
 
@@ -2184,12 +2251,16 @@ __device__ __forceinline__ void composite_block(const Rec* s_rec, float2* cut, i
       const float dy = sub_(fy, ra.y);
       const float qy = mul_(ra.z, dy);     // cxx * dy
       const float cxy2 = mul_(2.0f, ra.w);
+      // (-0.5 q) inv_det and q (-0.5 inv_det) are the same rounding of the
+      // same exact product (-0.5 is a power of two) unless a factor is
+      // subnormal
+      const float nh_inv_det = mul_(-0.5f, rb.y);
 #pragma unroll
       for (int i = 0; i < kPix; ++i) {
         if ((m[i] >> kk) & 1u) {
           const float dx = sub_(px[i], ra.x);
           const float q = fma_(qy, dy, fma_(mul_(rb.x, dx), dx, -mul_(mul_(cxy2, dx), dy)));
-          const float exponent = mul_(mul_(-0.5f, q), rb.y);
+          const float exponent = mul_(q, nh_inv_det);
           if (!(exponent < c.x)) {
             const float gamma_ipp = ex2_approx(__fmaf_rn(exponent, 1.4426950408889634f, c.y));
             if (gamma_ipp >= 1e-8f) {
@@ -2312,6 +2383,8 @@ __global__ void __launch_bounds__(kFusedThreads, SARR_FUSED_MIN_CTAS)
   if (count > 0) {  // the same for the whole CTA
     const int nneed = sa.need_n[v * sa.need_n_vstride + t];
     s_list[tid] = -1;
+    // the warps take alternate entries (entries with hit words one at a
+    // time: emit_hit_words would leave the other warp idle on most tiles)
     const NeedRegs nr = prefetch_need<false>(sa, v, T, t, nneed, lane, warp, 2);
     __syncthreads();
     emit_entries(sa, v, st, t, T, tx, ty, nneed, nr, warp, 2, s_list, lane);
