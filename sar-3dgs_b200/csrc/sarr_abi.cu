@@ -381,6 +381,13 @@ cudaError_t run_selection(const Dims& d, const Ws& w, int gv, const float* means
     b2.hbits = nullptr;
     b2.chunk_offset = stage1;
     b2.views_per_cta = views_per_cta(prefix - stage1);
+    // whole rounds of one view per warp (a CTA of 12 views left half of its
+    // 8 warps idle in the second round)
+#ifndef SARR_STAGE2_ROUND_VIEWS
+#define SARR_STAGE2_ROUND_VIEWS 1
+#endif
+    if (SARR_STAGE2_ROUND_VIEWS && b2.views_per_cta > kBinThreads / 32)
+      b2.views_per_cta = b2.views_per_cta / (kBinThreads / 32) * (kBinThreads / 32);
     b2.skip_masks = 1;
     b2.xlist = nullptr;  // prefix chunks are read through their segment masks
     b2.xcount = nullptr;
