@@ -1383,7 +1383,13 @@ constexpr int kScanTilesPerLane = 4;
 constexpr int kScanTilesPerCta = 8 * kScanTilesPerLane;
 constexpr int kScanSlices = kScanThreads / 8;
 
-__global__ void __launch_bounds__(kScanThreads) scan4_kernel(const ScanArgs a) {
+// 40 registers for 3 CTAs (48 warps) per SM: the chunk-row loads are
+// latency-bound (0.31 -> 0.24 ms per 1024 sweep views against 42 registers)
+#ifndef SARR_SCAN_MIN_CTAS
+#define SARR_SCAN_MIN_CTAS 3
+#endif
+#define SARR_SCAN_BOUNDS __launch_bounds__(kScanThreads, SARR_SCAN_MIN_CTAS)
+__global__ void SARR_SCAN_BOUNDS scan4_kernel(const ScanArgs a) {
   __shared__ __align__(16) int s_part[kScanSlices][kScanTilesPerCta];
   __shared__ int s_nneed[kScanTilesPerCta];
   __shared__ __align__(16) int s_total[kScanTilesPerCta];
@@ -2191,19 +2197,12 @@ __device__ __forceinline__ uint64_t block_hits(const Rec* recs, int count, float
   return hit;
 }
 
-// Compositing of one warp's 8 x (4 kPix) pixel block (rows r0 .. r0 + 7,
-// columns c0 .. c0 + 4 kPix - 1; the lane's row pr and first column pc0)
-// from the tile's `count` sorted records in shared memory, into the lane's
-// value / trans / done; `cut` is the warp's scratch for the records' cutoffs.
-// Warp-wide.
+// hit[i] bit k: record k's cutoff box meets columns [c0 + 4i, c0 + 4i + 3]
+// of rows [r0, r0 + 7]; cut[k] receives record k's cutoff and log2 scale.
+// Warp-wide; ends with __syncwarp.
 template <int kPix>
-__device__ __forceinline__ void composite_block(const Rec* s_rec, float2* cut, int count, int r0,
-                                                int c0, int pr, int pc0, int lane,
-                                                float (&value)[kPix], float (&trans)[kPix],
-                                                bool (&done)[kPix]) {
-  // hit[i] bit k: record k's cutoff box meets columns [c0 + 4i, c0 + 4i + 3]
-  // of rows [r0, r0 + 7]
-  uint64_t hit[kPix];
+__device__ __forceinline__ void quarter_hits(const Rec* s_rec, float2* cut, int count, int r0, int c0,
+                                             int lane, uint64_t (&hit)[kPix]) {
 #pragma unroll
   for (int i = 0; i < kPix; ++i) hit[i] = 0;
   const float by0 = (float)r0, by1 = (float)(r0 + 7);
@@ -2232,6 +2231,20 @@ __device__ __forceinline__ void composite_block(const Rec* s_rec, float2* cut, i
       hit[i] |= (uint64_t)__ballot_sync(0xffffffffu, in[i]) << (32 * h);
   }
   __syncwarp();
+}
+
+// Compositing of one warp's 8 x (4 kPix) pixel block (rows r0 .. r0 + 7,
+// columns c0 .. c0 + 4 kPix - 1; the lane's row pr and first column pc0)
+// from the tile's `count` sorted records in shared memory, into the lane's
+// value / trans / done; `cut` is the warp's scratch for the records' cutoffs.
+// Warp-wide.
+template <int kPix>
+__device__ __forceinline__ void composite_block(const Rec* s_rec, float2* cut, int count, int r0,
+                                                int c0, int pr, int pc0, int lane,
+                                                float (&value)[kPix], float (&trans)[kPix],
+                                                bool (&done)[kPix]) {
+  uint64_t hit[kPix];
+  quarter_hits<kPix>(s_rec, cut, count, r0, c0, lane, hit);
   // Records in two passes of 32 (32-bit masks): the lane visits, in list
   // order, the records marked for any of its pixels, and each pixel takes
   // those marked for its quarter. A pixel whose transmittance ran out drops
@@ -2567,6 +2580,63 @@ __global__ void __launch_bounds__(256) omega_listed_kernel(const OmegaScatterArg
 // through the records before its part (the same operations in the same order
 // as the full traversal) and computes the gradient terms of its own records,
 // so the per-record sums are those of one front-to-back pass.
+// The gradient terms of one pixel for one record (backward_kernel :910-1018,
+// written into A[0..6] where the pixel contributes, A untouched otherwise)
+// and the pixel's transmittance update; returns whether it contributes.
+__device__ __forceinline__ bool bwd_pixel_terms(const Rec& g, float2 cut, float fx, float fy,
+                                                float dL_d_pixel, float& prev_transmittance,
+                                                float (&A)[7]) {
+  bool contrib = false;
+  const float gamma_ipp = density_above_cutoff(g, cut.x, cut.y, fx, fy);
+  if (gamma_ipp >= 1e-8f) {
+    contrib = true;
+    const float sigma_i = g.sigma;
+    const float S_i = g.s_pos;
+    const float alpha_i = mul_(sigma_i, gamma_ipp);
+    const float d_pixel_d_alpha = mul_(prev_transmittance, S_i);
+    const float d_pixel_d_S = mul_(prev_transmittance, alpha_i);
+    const float g_a = mul_(dL_d_pixel, d_pixel_d_alpha);  // dL/dpixel * dpixel/dalpha
+    const float g_as = mul_(g_a, sigma_i);
+    A[0] = mul_(g_a, gamma_ipp);
+    A[1] = mul_(dL_d_pixel, d_pixel_d_S);
+    const float dx = sub_(fx, g.mx);
+    const float dy = sub_(fy, g.my);
+    const float cov_rr = g.cyy, cov_cc = g.cxx, cov_rc = g.cxy;
+    const float det = fma_(cov_rr, cov_cc, -mul_(cov_rc, cov_rc));
+    if (det > kEps) {
+      // det equals the record's (fma is symmetric in its factors), so its
+      // reciprocal and 2 pi sqrt(det) are the record's inv_det and norm
+      const float inv_det = g.inv_det;
+      // the backward's own exponent pairs cov_cc with dx^2 and cov_rr with dy^2 (:950)
+      const float q = fma_(mul_(cov_rr, dy), dy,
+                           fma_(mul_(cov_cc, dx), dx, -mul_(mul_(mul_(2.0f, cov_rc), dx), dy)));
+      const float exponent = mul_(mul_(-0.5f, q), inv_det);
+      if (exponent > -20.0f) {
+        // exp(exponent) / norm, as in the density (one ex2.approx)
+        const float base_val = ex2_approx(__fmaf_rn(exponent, 1.4426950408889634f, cut.y));
+        const float h = mul_(mul_(0.5f, base_val), inv_det);
+        const float d_gamma_d_cov_rr = mul_(h, fma_(dy, dy, -mul_(mul_(cov_cc, inv_det), 0.5f)));
+        const float d_gamma_d_cov_cc = mul_(h, fma_(dx, dx, -mul_(mul_(cov_rr, inv_det), 0.5f)));
+        const float d_gamma_d_cov_rc = mul_(mul_(mul_(-base_val, inv_det), dx), dy);
+        A[2] = mul_(g_as, d_gamma_d_cov_rr);
+        A[3] = mul_(g_as, d_gamma_d_cov_cc);
+        A[4] = mul_(g_as, d_gamma_d_cov_rc);
+      }
+    }
+    // (.cu:973-974) divide by det + EPSILON: one correctly rounded
+    // reciprocal and two products instead of two divisions (within
+    // 1.5 ulp of the quotients)
+    const float inv_det_eps = __frcp_rn(add_(det, kEps));
+    const float d_center_dr = mul_(-fma_(cov_rc, dx, -mul_(cov_rr, dy)), inv_det_eps);
+    const float d_center_dc = mul_(-fma_(cov_cc, dx, -mul_(cov_rc, dy)), inv_det_eps);
+    A[5] = mul_(g_as, d_center_dr);
+    A[6] = mul_(g_as, d_center_dc);
+    prev_transmittance = mul_(prev_transmittance, fma_(-sigma_i, gamma_ipp, 1.0f));
+    if (prev_transmittance < 1e-8f) prev_transmittance = 0.0f;
+  }
+  return contrib;
+}
+
 constexpr int kBwdParts = 4;
 constexpr int kBwdPartRecs = kCap / kBwdParts;
 
@@ -2624,56 +2694,7 @@ __global__ void __launch_bounds__(kWarpsPerTile * 32) bwd_tile_kernel(const Tile
     const Rec& g = s_rec[k];
     float A[7] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     bool contrib = false;
-    if (in) {
-      const float2 cut = s_cut[warp][k];
-      const float gamma_ipp = density_above_cutoff(g, cut.x, cut.y, fx, fy);
-      if (gamma_ipp >= 1e-8f) {
-        contrib = true;
-        const float sigma_i = g.sigma;
-        const float S_i = g.s_pos;
-        const float alpha_i = mul_(sigma_i, gamma_ipp);
-        const float d_pixel_d_alpha = mul_(prev_transmittance, S_i);
-        const float d_pixel_d_S = mul_(prev_transmittance, alpha_i);
-        const float g_a = mul_(dL_d_pixel, d_pixel_d_alpha);  // dL/dpixel * dpixel/dalpha
-        const float g_as = mul_(g_a, sigma_i);
-        A[0] = mul_(g_a, gamma_ipp);
-        A[1] = mul_(dL_d_pixel, d_pixel_d_S);
-        const float dx = sub_(fx, g.mx);
-        const float dy = sub_(fy, g.my);
-        const float cov_rr = g.cyy, cov_cc = g.cxx, cov_rc = g.cxy;
-        const float det = fma_(cov_rr, cov_cc, -mul_(cov_rc, cov_rc));
-        if (det > kEps) {
-          // det equals the record's (fma is symmetric in its factors), so its
-          // reciprocal and 2 pi sqrt(det) are the record's inv_det and norm
-          const float inv_det = g.inv_det;
-          // the backward's own exponent pairs cov_cc with dx^2 and cov_rr with dy^2 (:950)
-          const float q = fma_(mul_(cov_rr, dy), dy,
-                               fma_(mul_(cov_cc, dx), dx, -mul_(mul_(mul_(2.0f, cov_rc), dx), dy)));
-          const float exponent = mul_(mul_(-0.5f, q), inv_det);
-          if (exponent > -20.0f) {
-            // exp(exponent) / norm, as in the density (one ex2.approx)
-            const float base_val = ex2_approx(__fmaf_rn(exponent, 1.4426950408889634f, cut.y));
-            const float h = mul_(mul_(0.5f, base_val), inv_det);
-            const float d_gamma_d_cov_rr = mul_(h, fma_(dy, dy, -mul_(mul_(cov_cc, inv_det), 0.5f)));
-            const float d_gamma_d_cov_cc = mul_(h, fma_(dx, dx, -mul_(mul_(cov_rr, inv_det), 0.5f)));
-            const float d_gamma_d_cov_rc = mul_(mul_(mul_(-base_val, inv_det), dx), dy);
-            A[2] = mul_(g_as, d_gamma_d_cov_rr);
-            A[3] = mul_(g_as, d_gamma_d_cov_cc);
-            A[4] = mul_(g_as, d_gamma_d_cov_rc);
-          }
-        }
-        // (.cu:973-974) divide by det + EPSILON: one correctly rounded
-        // reciprocal and two products instead of two divisions (within
-        // 1.5 ulp of the quotients)
-        const float inv_det_eps = __frcp_rn(add_(det, kEps));
-        const float d_center_dr = mul_(-fma_(cov_rc, dx, -mul_(cov_rr, dy)), inv_det_eps);
-        const float d_center_dc = mul_(-fma_(cov_cc, dx, -mul_(cov_rc, dy)), inv_det_eps);
-        A[5] = mul_(g_as, d_center_dr);
-        A[6] = mul_(g_as, d_center_dc);
-        prev_transmittance = mul_(prev_transmittance, fma_(-sigma_i, gamma_ipp, 1.0f));
-        if (prev_transmittance < 1e-8f) prev_transmittance = 0.0f;
-      }
-    }
+    if (in) contrib = bwd_pixel_terms(g, s_cut[warp][k], fx, fy, dL_d_pixel, prev_transmittance, A);
     if (__any_sync(0xffffffffu, contrib)) {
       const float A8[8] = {A[0], A[1], A[2], A[3], A[4], A[5], A[6], 0.0f};
       const float total = warp_sum8_scatter(A8, lane);
@@ -2689,6 +2710,110 @@ __global__ void __launch_bounds__(kWarpsPerTile * 32) bwd_tile_kernel(const Tile
 #pragma unroll
     for (int w = 0; w < kWarpsPerTile; ++w) acc += s_red[w][kp][c];
     partial[((size_t)t * kCap + s_rec[k_lo + kp].pos) * 8 + c] = acc;
+  }
+}
+
+// bwd_tile_kernel for launches of many views: two warps per (tile, part),
+// each an 8 x 16 pixel block with four pixels per lane (one range row,
+// azimuth columns c, c + 4, c + 8, c + 12, as render_kernel<4>). Per record,
+// each lane adds its pixels' terms first, so one warp reduction covers 128
+// pixels; per pixel, only the records whose cutoff box meets its 8 x 4
+// quarter are visited (the others have density 0 there). The per-record sums
+// are those of bwd_tile_kernel up to the order of the additions.
+constexpr int kBwdPix = 4;
+constexpr int kBwdManyMinViews = 16;
+
+__global__ void __launch_bounds__(kTile * kTile / kBwdPix) bwd_tile4_kernel(const TileArgs a) {
+  constexpr int kWarps = kTile * kTile / kBwdPix / 32;
+  static_assert(kWarps == 2, "two 8-row halves of the tile");
+  __shared__ __align__(16) Rec s_rec[kCap];
+  __shared__ float s_red[kWarps][kBwdPartRecs][8];
+  __shared__ float2 s_cut[kWarps][kCap];
+  __shared__ uint64_t bar;
+  const int v = blockIdx.y, t = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const ViewConst& vc = a.views[v];
+  const int Nr = vc.h.Nr, Na = vc.h.Na, tiles_x = vc.tiles_x;
+  const int tx = t % tiles_x, ty = t / tiles_x;
+  const unsigned char* st = a.st.base + v * a.st.vstride;
+  const int count_all = reinterpret_cast<const int*>(st + a.st.L.count)[t];
+  const int k_lo = blockIdx.z * kBwdPartRecs;
+  if (k_lo >= count_all) return;
+  const int count = min(count_all, k_lo + kBwdPartRecs);  // records [0, count) are read
+  const bool ok = load_tile_recs(s_rec, &bar, st, a.st.L, t, count, a.err, true);
+  if (!__syncthreads_and(ok)) return;
+
+  const int r0 = ty * kTile + warp * 8, c0 = tx * kTile;
+  const int pr = r0 + (lane & 7), pc0 = c0 + (lane >> 3);
+  const float fy = (float)pr;
+  float dL[kBwdPix], trans[kBwdPix], fx[kBwdPix];
+  bool in[kBwdPix];
+  const float* gimg = a.images + v * a.img_vstride;
+#pragma unroll
+  for (int i = 0; i < kBwdPix; ++i) {
+    const int pc = pc0 + 4 * i;
+    in[i] = pc < Na && pr < Nr;
+    dL[i] = in[i] ? gimg[(size_t)pc * Nr + pr] : 0.0f;
+    trans[i] = 1.0f;
+    fx[i] = (float)pc;
+  }
+  for (int e = lane; e < kBwdPartRecs * 8; e += 32) (&s_red[warp][0][0])[e] = 0.0f;
+  uint64_t hit[kBwdPix];
+  quarter_hits<kBwdPix>(s_rec, s_cut[warp], count, r0, c0, lane, hit);
+  uint64_t any = 0;
+#pragma unroll
+  for (int i = 0; i < kBwdPix; ++i) any |= hit[i];
+
+  // transmittance through the records before this part
+  uint64_t before = k_lo ? any & ((1ull << k_lo) - 1ull) : 0ull;
+  uint64_t todo = any & ~before;
+  while (before) {
+    const int k = __ffsll((long long)before) - 1;
+    before &= before - 1;
+    const Rec& g = s_rec[k];
+    const float2 cut = s_cut[warp][k];
+#pragma unroll
+    for (int i = 0; i < kBwdPix; ++i) {
+      if (((hit[i] >> k) & 1ull) && in[i]) {
+        const float gamma_ipp = density_above_cutoff(g, cut.x, cut.y, fx[i], fy);
+        if (gamma_ipp >= 1e-8f) {
+          trans[i] = mul_(trans[i], fma_(-g.sigma, gamma_ipp, 1.0f));
+          if (trans[i] < 1e-8f) trans[i] = 0.0f;
+        }
+      }
+    }
+  }
+
+  while (todo) {
+    const int k = __ffsll((long long)todo) - 1;
+    todo &= todo - 1;
+    const Rec& g = s_rec[k];
+    const float2 cut = s_cut[warp][k];
+    float A[7] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    bool contrib = false;
+#pragma unroll
+    for (int i = 0; i < kBwdPix; ++i) {
+      if (((hit[i] >> k) & 1ull) && in[i]) {
+        float Ai[7] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        if (bwd_pixel_terms(g, cut, fx[i], fy, dL[i], trans[i], Ai)) {
+          contrib = true;
+#pragma unroll
+          for (int j = 0; j < 7; ++j) A[j] = add_(A[j], Ai[j]);
+        }
+      }
+    }
+    if (__any_sync(0xffffffffu, contrib)) {
+      const float A8[8] = {A[0], A[1], A[2], A[3], A[4], A[5], A[6], 0.0f};
+      const float total = warp_sum8_scatter(A8, lane);
+      const int c = 4 * ((lane >> 4) & 1) + 2 * ((lane >> 3) & 1) + ((lane >> 2) & 1);
+      if ((lane & 3) == 0 && c < 7) s_red[warp][k - k_lo][c] = total;
+    }
+  }
+  __syncthreads();
+  float* partial = a.partial + v * a.partial_vstride;
+  for (int e = tid; e < (count - k_lo) * 7; e += kWarps * 32) {
+    const int kp = e / 7, c = e - kp * 7;
+    partial[((size_t)t * kCap + s_rec[k_lo + kp].pos) * 8 + c] = add_(s_red[0][kp][c], s_red[1][kp][c]);
   }
 }
 
@@ -3464,8 +3589,14 @@ cudaError_t launch_omega_scatter(const OmegaScatterArgs& a, const Dims& d, int n
   return cudaGetLastError();
 }
 
+#ifndef SARR_BWD_MANY_PIX
+#define SARR_BWD_MANY_PIX 1
+#endif
 cudaError_t launch_bwd_tile(const TileArgs& a, const Dims& d, int nviews, cudaStream_t s) {
-  bwd_tile_kernel<<<dim3(d.T, nviews, kBwdParts), kWarpsPerTile * 32, 0, s>>>(a);
+  if (SARR_BWD_MANY_PIX && nviews >= kBwdManyMinViews)
+    bwd_tile4_kernel<<<dim3(d.T, nviews, kBwdParts), kTile * kTile / kBwdPix, 0, s>>>(a);
+  else
+    bwd_tile_kernel<<<dim3(d.T, nviews, kBwdParts), kWarpsPerTile * 32, 0, s>>>(a);
   return cudaGetLastError();
 }
 

@@ -141,9 +141,13 @@ def test_fused_select_render_matches_separate_kernels(scene):
         assert torch.equal(one[0], ref[k])
 
 
-def test_cell_culling_backward_equals_sum_of_single_views():
+@pytest.mark.parametrize("nviews", [10, 20])
+def test_cell_culling_backward_equals_sum_of_single_views(nviews):
+    """10 views: the per-tile pass with one pixel per lane; 20 views: four
+    pixels per lane (launches of 16 views or more). Single views use the
+    first."""
     sc = {k: v.cuda() for k, v in S.make_scene(100000, (40.0, 40.0, 10.0), (0.05, 0.5), seed=54).items()}
-    views = S.sweep_views(80)[::8]  # 10 views
+    views = S.sweep_views(8 * nviews)[::8]
     batch = M.render_sar_batched(sc["means"], sc["cov6"], sc["sigma"], sc["sh"], views)
     for k, v in enumerate(views):
         img, _ = M.render_sar(sc["means"], sc["cov6"], sc["sigma"], sc["sh"], *v)
