@@ -2293,18 +2293,31 @@ __device__ __forceinline__ void composite_block(const Rec* s_rec, float2* cut, i
               const float alpha_i = mul_(sigma, gamma_ipp);
               value[i] = fma_(mul_(trans[i], alpha_i), rc.x, value[i]);
               trans[i] = mul_(trans[i], fma_(-sigma, gamma_ipp, 1.0f));
-              if (trans[i] < 1e-8f) {
-                trans[i] = 0.0f;
-                done[i] = true;
-                m[i] = 0u;
-                uint32_t keep = 0;
-#pragma unroll
-                for (int j = 0; j < kPix; ++j) keep |= m[j];
-                todo &= keep;
-              }
             }
           }
         }
+      }
+      // a pixel whose transmittance fell below 1e-8 at this record takes no
+      // later record (the reference's break after the update); each pixel
+      // meets the record once, so one test per record suffices. A finished
+      // pixel's transmittance is set to 1 (it is not read again: its mask is
+      // cleared), which keeps it out of later tests.
+      float tmin = trans[0];
+#pragma unroll
+      for (int i = 1; i < kPix; ++i) tmin = fminf(tmin, trans[i]);
+      if (tmin < 1e-8f) {
+#pragma unroll
+        for (int i = 0; i < kPix; ++i) {
+          if (trans[i] < 1e-8f) {
+            trans[i] = 1.0f;
+            done[i] = true;
+            m[i] = 0u;
+          }
+        }
+        uint32_t keep = 0;
+#pragma unroll
+        for (int j = 0; j < kPix; ++j) keep |= m[j];
+        todo &= keep;
       }
     }
   }

@@ -66,7 +66,7 @@ def test_cell_culling_lists_images_omega(want_omega):
 
 
 def test_many_view_launch_matches_single_views():
-    """20 views in one launch group: the four-tile scan, the two-pixel render
+    """20 views in one launch group: the tile scan, the four-pixel render
     layout and the cell path give each view the lists, image and Omega of a
     single-view call."""
     sc = {k: v.cuda() for k, v in S.make_scene(150000, (40.0, 40.0, 10.0), (0.05, 0.5), seed=57).items()}

@@ -3,7 +3,9 @@
 The sweep (N = 1M Gaussians in 40 x 40 x 10 m, 1024 views of 256 x 256 at
 0.2 m, incidence 15-45 deg) is rendered exactly as the benchmark calls it: one
 sarr_forward call over the 1024 views, processed in launch groups of 256 views
-(cell culling, the four-tile scan, the two-pixel compositing layout). Views
+(cell culling, the tile scan, the fused selection and four-pixel
+compositing for the image-only call, the separate kernels for the call with
+states). Views
 spread over the groups are checked against the CPU oracle: tile lists and
 depth orders bit-exact, images and Omega within 1e-4 relative L-inf. The
 backward is checked against the oracle's gradients at 1M Gaussians (1e-3
