@@ -81,6 +81,23 @@ struct SceneGrid {
   int n_always;              // Gaussians after the prefix that are in no cell
 };
 
+// Spatial cells are numbered in blocks of 4 x 4 x 2 grid cells, the blocks in
+// x-major order, so that a warp of cell_test_kernel (32 cells) and a bitmap
+// word of bin_cand_kernel (8 cells) cover compact pieces of the scene: the
+// candidate cells of a view, which lie along the scene's edges in its image,
+// gather into fewer warps and words (cell test 0.55 -> 0.49 ms, candidate
+// test 0.71 -> 0.68 ms per 1024 sweep views against x-major rows). The grid
+// is padded to whole blocks (padding cells have no members).
+constexpr int kCellBlock = 32;
+__host__ __device__ __forceinline__ int64_t padded_spatial_cells(const int dims[3]) {
+  return (int64_t)((dims[0] + 3) / 4) * ((dims[1] + 3) / 4) * ((dims[2] + 1) / 2) * kCellBlock;
+}
+__host__ __device__ __forceinline__ int spatial_cell(const int dims[3], int ix, int iy, int iz) {
+  const int nbx = (dims[0] + 3) / 4, nby = (dims[1] + 3) / 4;
+  const int blk = ((iz >> 1) * nby + (iy >> 2)) * nbx + (ix >> 2);
+  return blk * kCellBlock + (((iz & 1) * 4 + (iy & 3)) * 4 + (ix & 3));
+}
+
 // Order-preserving map of floats to ints (for atomicMin / atomicMax).
 __device__ __forceinline__ int ordered_key(float f) {
   const int i = __float_as_int(f);

@@ -889,17 +889,15 @@ __global__ void scene_grid_kernel(SceneGrid* g, int64_t n) {
   if (!(a > 0.0f) || !isfinite(a)) a = fmaxf(emax, 1e-6f);
   int dims[3];
   for (int it = 0; it < 200; ++it) {
-    int64_t prod = 1;
     for (int k = 0; k < 3; ++k) {
       float t = ceilf(ext[k] / a);
       dims[k] = t < 1.0f ? 1 : (t > 1e6f ? 1000000 : (int)t);
       while ((float)dims[k] * a < ext[k]) ++dims[k];
-      prod *= dims[k];
     }
-    if (prod <= kMaxSpatialCells) break;
+    if (padded_spatial_cells(dims) <= kMaxSpatialCells) break;
     a *= 1.05f;
   }
-  int64_t prod = (int64_t)dims[0] * dims[1] * dims[2];
+  const int64_t prod = padded_spatial_cells(dims);
   if (prod > kMaxSpatialCells) return;  // not reached for finite boxes; no cells then
   float scale = emax + a;
   for (int k = 0; k < 3; ++k) {
@@ -919,8 +917,11 @@ __global__ void scene_grid_kernel(SceneGrid* g, int64_t n) {
 __global__ void __launch_bounds__(256) cell_center_kernel(const SceneGrid* g, float4* center) {
   const int c = blockIdx.x * 256 + threadIdx.x;
   if (!g->valid || c >= g->nspatial) return;
-  const int d0 = g->dims[0], d1 = g->dims[1];
-  const int ix = c % d0, iy = (c / d0) % d1, iz = c / (d0 * d1);
+  // the inverse of spatial_cell
+  const int nbx = (g->dims[0] + 3) / 4, nby = (g->dims[1] + 3) / 4;
+  const int blk = c / kCellBlock, l = c % kCellBlock;
+  const int ix = (blk % nbx) * 4 + (l & 3), iy = ((blk / nbx) % nby) * 4 + ((l >> 2) & 3);
+  const int iz = (blk / (nbx * nby)) * 2 + (l >> 4);
   center[c] = make_float4(g->lo[0] + ((float)ix + 0.5f) * g->a, g->lo[1] + ((float)iy + 0.5f) * g->a,
                           g->lo[2] + ((float)iz + 0.5f) * g->a, 0.0f);
 }
@@ -944,7 +945,7 @@ __global__ void __launch_bounds__(256) cell_assign_kernel(const CellPrepArgs a) 
       const int ix = min(max((int)floorf((x - g.lo[0]) * g.inv_a), 0), g.dims[0] - 1);
       const int iy = min(max((int)floorf((y - g.lo[1]) * g.inv_a), 0), g.dims[1] - 1);
       const int iz = min(max((int)floorf((z - g.lo[2]) * g.inv_a), 0), g.dims[2] - 1);
-      id = (uint32_t)(((iz * g.dims[1] + iy) * g.dims[0] + ix) * kHbBuckets + hb_bucket(hb));
+      id = (uint32_t)(spatial_cell(g.dims, ix, iy, iz) * kHbBuckets + hb_bucket(hb));
       atomicMax(a.cell_hb + id, ordered_key(hb));
       if (j >= a.pstart) atomicAdd(a.cell_count + id, 1);
     }
@@ -1030,9 +1031,7 @@ __global__ void __launch_bounds__(256) cell_test_kernel(const CellTestArgs a) {
   if (g.valid && sc * kHbBuckets < g.ncells) {
     const ViewConst& vc = a.views[v];
     const int Nr = vc.h.Nr, Na = vc.h.Na, pitch = vc.tiles_x + 1;
-    const float4 q = a.cell_center[sc];
-    float r, cc, xr, yr;
-    approx_center(vc, q.x, q.y, q.z, r, cc, xr, yr);
+    float r = 0.0f, cc = 0.0f, xr = 0.0f, yr = 0.0f;  // the cell centre's image position
     const float dr = g.half_diag * fabsf(vc.inv_rho_r) * 1.0001f;
     const float dc = g.half_diag * fabsf(vc.inv_rho_a) * 1.0001f;
     const float ds = g.half_diag * 1.0001f;
@@ -1057,6 +1056,10 @@ __global__ void __launch_bounds__(256) cell_test_kernel(const CellTestArgs a) {
     for (int b = 0; b < kHbBuckets; ++b) {
       hbv[b] = key_float(a.cell_hb[sc * kHbBuckets + b]);
       if (hbv[b] >= 0.0f && hbv[b] > hmax) hmax = hbv[b];
+    }
+    if (hmax >= 0.0f) {
+      const float4 q = a.cell_center[sc];
+      approx_center(vc, q.x, q.y, q.z, r, cc, xr, yr);
     }
     if (hmax >= 0.0f && reaches_open(hmax)) {
 #pragma unroll
