@@ -84,7 +84,7 @@ MIN_INSTR_PER_PAIR = 12
 # runs in calls with states or Omega; image-only calls run
 # select_render_kernel (selection and compositing in one kernel).
 NCU = {"render_kernel": {"dram_bytes": 118_493_696 + 37_277_696, "warp_instructions": 353_205_923},
-       "select_render_kernel": {"dram_bytes": 103_717_632 + 39_274_496, "warp_instructions": 471_424_277}}
+       "select_render_kernel": {"dram_bytes": 103_740_416 + 41_093_376, "warp_instructions": 439_858_375}}
 
 
 def parse():
