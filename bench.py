@@ -83,7 +83,7 @@ MIN_INSTR_PER_PAIR = 12
 # .sum); they belong to this workload and these kernels only. render_kernel
 # runs in calls with states or Omega; image-only calls run
 # select_render_kernel (selection and compositing in one kernel).
-NCU = {"render_kernel": {"dram_bytes": 118_493_696 + 37_277_696, "warp_instructions": 353_205_923},
+NCU = {"render_kernel": {"dram_bytes": 118_546_432 + 38_688_768, "warp_instructions": 299_738_669},
        "select_render_kernel": {"dram_bytes": 103_740_416 + 41_093_376, "warp_instructions": 439_858_375}}
 
 
