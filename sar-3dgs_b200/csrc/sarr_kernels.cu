@@ -868,11 +868,27 @@ __global__ void __launch_bounds__(256) scene_bounds_kernel(const float* __restri
       hi[k] = fmaxf(hi[k], __shfl_xor_sync(0xffffffffu, hi[k], o));
     }
   }
+  // one set of atomics per CTA (the per-warp ones contended on six words)
+  __shared__ float s_lo[8][3], s_hi[8][3];
+  const int warp = threadIdx.x >> 5;
   if ((threadIdx.x & 31) == 0) {
 #pragma unroll
     for (int k = 0; k < 3; ++k) {
-      atomicMin(&g->lo_key[k], ordered_key(lo[k]));
-      atomicMax(&g->hi_key[k], ordered_key(hi[k]));
+      s_lo[warp][k] = lo[k];
+      s_hi[warp][k] = hi[k];
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+      float l = s_lo[0][k], h = s_hi[0][k];
+      for (int w = 1; w < (int)(blockDim.x >> 5); ++w) {
+        l = fminf(l, s_lo[w][k]);
+        h = fmaxf(h, s_hi[w][k]);
+      }
+      atomicMin(&g->lo_key[k], ordered_key(l));
+      atomicMax(&g->hi_key[k], ordered_key(h));
     }
   }
 }
