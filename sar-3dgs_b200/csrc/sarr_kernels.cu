@@ -2763,15 +2763,23 @@ __global__ void __launch_bounds__(kWarpsPerTile * 32) bwd_tile_kernel(const Tile
 // each lane adds its pixels' terms first, so one warp reduction covers 128
 // pixels; per pixel, only the records whose cutoff box meets its 8 x 4
 // quarter are visited (the others have density 0 there). The per-record sums
-// are those of bwd_tile_kernel up to the order of the additions.
+// are those of bwd_tile_kernel up to the order of the additions. kParts is
+// the number of record parts (grid.z): launches of many views have CTAs
+// enough with one part, which walks each pixel through the tile's records
+// once instead of replaying the records before each part.
 constexpr int kBwdPix = 4;
 constexpr int kBwdManyMinViews = 16;
+#ifndef SARR_BWD_ONE_PART_MIN_VIEWS
+#define SARR_BWD_ONE_PART_MIN_VIEWS 32
+#endif
 
+template <int kParts>
 __global__ void __launch_bounds__(kTile * kTile / kBwdPix) bwd_tile4_kernel(const TileArgs a) {
   constexpr int kWarps = kTile * kTile / kBwdPix / 32;
   static_assert(kWarps == 2, "two 8-row halves of the tile");
+  constexpr int kPartRecs = kCap / kParts;
   __shared__ __align__(16) Rec s_rec[kCap];
-  __shared__ float s_red[kWarps][kBwdPartRecs][8];
+  __shared__ float s_red[kWarps][kPartRecs][8];
   __shared__ float2 s_cut[kWarps][kCap];
   __shared__ uint64_t bar;
   const int v = blockIdx.y, t = blockIdx.x;
@@ -2781,9 +2789,9 @@ __global__ void __launch_bounds__(kTile * kTile / kBwdPix) bwd_tile4_kernel(cons
   const int tx = t % tiles_x, ty = t / tiles_x;
   const unsigned char* st = a.st.base + v * a.st.vstride;
   const int count_all = reinterpret_cast<const int*>(st + a.st.L.count)[t];
-  const int k_lo = blockIdx.z * kBwdPartRecs;
+  const int k_lo = blockIdx.z * kPartRecs;
   if (k_lo >= count_all) return;
-  const int count = min(count_all, k_lo + kBwdPartRecs);  // records [0, count) are read
+  const int count = min(count_all, k_lo + kPartRecs);  // records [0, count) are read
   const bool ok = load_tile_recs(s_rec, &bar, st, a.st.L, t, count, a.err, true);
   if (!__syncthreads_and(ok)) return;
 
@@ -2801,7 +2809,7 @@ __global__ void __launch_bounds__(kTile * kTile / kBwdPix) bwd_tile4_kernel(cons
     trans[i] = 1.0f;
     fx[i] = (float)pc;
   }
-  for (int e = lane; e < kBwdPartRecs * 8; e += 32) (&s_red[warp][0][0])[e] = 0.0f;
+  for (int e = lane; e < kPartRecs * 8; e += 32) (&s_red[warp][0][0])[e] = 0.0f;
   uint64_t hit[kBwdPix];
   quarter_hits<kBwdPix>(s_rec, s_cut[warp], count, r0, c0, lane, hit);
   uint64_t any = 0;
@@ -3177,12 +3185,13 @@ __global__ void __launch_bounds__(256) bwd_scatter_kernel(const BwdScatterArgs a
 
 // One warp per Gaussian left by bwd_scatter_kernel (8 per CTA, persistent
 // over the list). The group's views are taken in blocks of 32, lane l for
-// view 32 j + l of block j: every lane reads the Gaussian's entries (the same
-// entry at the same time), keeps those of its view, orders them by tile and
-// sums their partials, and applies the view's chain rule; then 23 lanes, one
-// per output sum, add the block's view contributions in view order. A view
-// with more than kHeavyViewEntries listing tiles of the Gaussian (a bbox
-// wider than ~80 pixels) takes them in order by repeated selection.
+// view 32 j + l of block j: the lanes read the Gaussian's entries 32 at a
+// time and drop each entry of the block into its view's bucket in shared
+// memory; each lane then orders its view's bucket by tile, sums the
+// partials and applies the view's chain rule; then 23 lanes, one per output
+// sum, add the block's view contributions in view order. A view with more
+// than kHeavyViewEntries listing tiles of the Gaussian (a bbox wider than
+// ~80 pixels) takes them in order by repeated selection.
 constexpr int kHeavyViewEntries = 32;
 constexpr int kHeavyWarps = 8;
 
@@ -3193,48 +3202,60 @@ __device__ __forceinline__ uint32_t entry_at(const BwdScatterArgs& a, int per_vi
 __global__ void __launch_bounds__(kHeavyWarps * 32) bwd_heavy_kernel(const BwdScatterArgs a) {
   __shared__ ViewContrib s_con[kHeavyWarps][32];
   __shared__ int s_has[kHeavyWarps][32];
+  __shared__ int s_cnt[kHeavyWarps][32];
+  // one bucket row per view of the block, padded so that the lanes, each on
+  // its own row at the same position, hit distinct banks
+  __shared__ uint32_t s_keys[kHeavyWarps][32][kHeavyViewEntries + 1];
   __shared__ float s_out[kHeavyWarps][23];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int count = a.heavy[0];
   const int nviews = a.nviews;
-  const int per_view = a.views[0].tiles_x * a.views[0].tiles_y * kCap;
+  const int per_view = a.views[0].tiles_x * a.views[0].tiles_y * kCap;  // >= 64 entries per slice
+  uint32_t* keys = s_keys[warp][lane];
   for (int h = blockIdx.x * kHeavyWarps + warp; h < count; h += gridDim.x * kHeavyWarps) {
     const int64_t i = a.heavy[1 + h];
     const int e0 = a.start[i], c = a.start[i + 1] - e0;
     float acc = 0.f;  // output sum `lane` (lanes < 23)
     for (int vb = 0; vb < nviews; vb += 32) {
       const int v = vb + lane;
-      uint32_t key[kHeavyViewEntries];
-      int m = 0;
+      s_cnt[warp][lane] = 0;
+      __syncwarp();
       {
-        int slice = e0 / per_view, off = e0 % per_view;
-        for (int q = 0; q < c; ++q) {
-          const uint32_t k = a.entries[(size_t)slice * a.entries_vstride + off];
-          if (++off == per_view) {
-            off = 0;
-            ++slice;
+        // entry e0 + q0 + lane lies in slice `slice` at offset `off`
+        int slice = (e0 + lane) / per_view, off = (e0 + lane) % per_view;
+        for (int q0 = 0; q0 < c; q0 += 32) {
+          if (q0 + lane < c) {
+            const uint32_t k = a.entries[(size_t)slice * a.entries_vstride + off];
+            const int vr = (int)(k >> 24) - vb;
+            if (vr >= 0 && vr < 32) {
+              const int p = atomicAdd(&s_cnt[warp][vr], 1);
+              if (p < kHeavyViewEntries) s_keys[warp][vr][p] = k;
+            }
           }
-          if ((int)(k >> 24) == v) {
-            if (m < kHeavyViewEntries) key[m] = k;
-            ++m;
+          off += 32;
+          if (off >= per_view) {
+            off -= per_view;
+            ++slice;
           }
         }
       }
+      __syncwarp();
+      const int m = s_cnt[warp][lane];
       s_has[warp][lane] = 0;
       if (v < nviews && m > 0) {
         float A[7] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
         float2 yzr = make_float2(0.f, 0.f);
         if (m <= kHeavyViewEntries) {
-          for (int q = 1; q < m; ++q) {  // insertion sort by tile
-            const uint32_t x = key[q];
+          for (int q = 1; q < m; ++q) {  // insertion sort by tile (a view's keys are distinct)
+            const uint32_t x = keys[q];
             int r = q - 1;
-            while (r >= 0 && key[r] > x) {
-              key[r + 1] = key[r];
+            while (r >= 0 && keys[r] > x) {
+              keys[r + 1] = keys[r];
               --r;
             }
-            key[r + 1] = x;
+            keys[r + 1] = x;
           }
-          for (int q = 0; q < m; ++q) entry_partial(a, key[q], A, yzr);
+          for (int q = 0; q < m; ++q) entry_partial(a, keys[q], A, yzr);
         } else {
           uint32_t last = 0;
           for (int q = 0; q < m; ++q) {
@@ -3252,19 +3273,17 @@ __global__ void __launch_bounds__(kHeavyWarps * 32) bwd_heavy_kernel(const BwdSc
       }
       __syncwarp();
       if (lane < 23) {
-        // output sum lane: 0 sigma, 1..16 SH, 17 rr, 18 cc, 19 rc, 20..22 x y z
+        // output sum lane: 0 sigma, 1..16 SH, 17 rr, 18 cc, 19 rc, 20..22 x y z.
+        // Every lane takes acc = fma(x, y, acc): y is the view's SH basis value
+        // for the SH sums and 1 for the others (x * 1 is exact, so that is
+        // acc + x rounded once), so the lanes run one path.
+        const int field = lane == 0 ? 0 : (lane <= kSh ? 1 : lane - kSh + 1);  // ViewContrib member
         const int ub = min(32, nviews - vb);
         for (int u = 0; u < ub; ++u) {
           if (!s_has[warp][u]) continue;
-          const ViewContrib& cv = s_con[warp][u];
-          if (lane == 0) acc = __fadd_rn(acc, cv.a0);
-          else if (lane <= kSh) acc = __fmaf_rn(cv.a1, a.views[vb + u].h.sh_basis[lane - 1], acc);
-          else if (lane == 17) acc = __fadd_rn(acc, cv.a2);
-          else if (lane == 18) acc = __fadd_rn(acc, cv.a3);
-          else if (lane == 19) acc = __fadd_rn(acc, cv.a4);
-          else if (lane == 20) acc = __fadd_rn(acc, cv.cx);
-          else if (lane == 21) acc = __fadd_rn(acc, cv.cy);
-          else acc = __fadd_rn(acc, cv.cz);
+          const float x = (&s_con[warp][u].a0)[field];
+          const float y = (lane >= 1 && lane <= kSh) ? a.views[vb + u].h.sh_basis[lane - 1] : 1.0f;
+          acc = __fmaf_rn(x, y, acc);
         }
       }
       __syncwarp();
@@ -3637,8 +3656,10 @@ cudaError_t launch_omega_scatter(const OmegaScatterArgs& a, const Dims& d, int n
 #define SARR_BWD_MANY_PIX 1
 #endif
 cudaError_t launch_bwd_tile(const TileArgs& a, const Dims& d, int nviews, cudaStream_t s) {
-  if (SARR_BWD_MANY_PIX && nviews >= kBwdManyMinViews)
-    bwd_tile4_kernel<<<dim3(d.T, nviews, kBwdParts), kTile * kTile / kBwdPix, 0, s>>>(a);
+  if (SARR_BWD_MANY_PIX && nviews >= SARR_BWD_ONE_PART_MIN_VIEWS)
+    bwd_tile4_kernel<1><<<dim3(d.T, nviews, 1), kTile * kTile / kBwdPix, 0, s>>>(a);
+  else if (SARR_BWD_MANY_PIX && nviews >= kBwdManyMinViews)
+    bwd_tile4_kernel<kBwdParts><<<dim3(d.T, nviews, kBwdParts), kTile * kTile / kBwdPix, 0, s>>>(a);
   else
     bwd_tile_kernel<<<dim3(d.T, nviews, kBwdParts), kWarpsPerTile * 32, 0, s>>>(a);
   return cudaGetLastError();

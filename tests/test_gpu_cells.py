@@ -141,11 +141,12 @@ def test_fused_select_render_matches_separate_kernels(scene):
         assert torch.equal(one[0], ref[k])
 
 
-@pytest.mark.parametrize("nviews", [10, 20])
+@pytest.mark.parametrize("nviews", [10, 20, 40])
 def test_cell_culling_backward_equals_sum_of_single_views(nviews):
     """10 views: the per-tile pass with one pixel per lane; 20 views: four
-    pixels per lane (launches of 16 views or more). Single views use the
-    first."""
+    pixels per lane (launches of 16 views or more), the tile's records in
+    four parts; 40 views: four pixels per lane, one part (launches of 32
+    views or more). Single views use the first."""
     sc = {k: v.cuda() for k, v in S.make_scene(100000, (40.0, 40.0, 10.0), (0.05, 0.5), seed=54).items()}
     views = S.sweep_views(8 * nviews)[::8]
     batch = M.render_sar_batched(sc["means"], sc["cov6"], sc["sigma"], sc["sh"], views)
