@@ -2624,10 +2624,32 @@ __global__ void __launch_bounds__(256) omega_listed_kernel(const OmegaScatterArg
 // through the records before its part (the same operations in the same order
 // as the full traversal) and computes the gradient terms of its own records,
 // so the per-record sums are those of one front-to-back pass.
+// The per-record constants of bwd_pixel_terms, computed once per record with
+// the operations the per-pixel terms would repeat: x = 1 / (det + EPSILON)
+// (.cu:973-974: one correctly rounded reciprocal and two products instead of
+// two divisions, within 1.5 ulp of the quotients), y = -(cov_cc inv_det) / 2,
+// z = -(cov_rr inv_det) / 2, w = 1 where det > EPSILON. det equals the
+// record's (fma is symmetric in its factors), so its reciprocal and
+// 2 pi sqrt(det) are the record's inv_det and norm.
+__device__ __forceinline__ float4 bwd_rec_const(const Rec& g) {
+  const float cov_rr = g.cyy, cov_cc = g.cxx, cov_rc = g.cxy;
+  const float det = fma_(cov_rr, cov_cc, -mul_(cov_rc, cov_rc));
+  const float inv_det = g.inv_det;
+  return make_float4(__frcp_rn(add_(det, kEps)), -mul_(mul_(cov_cc, inv_det), 0.5f),
+                     -mul_(mul_(cov_rr, inv_det), 0.5f), det > kEps ? 1.0f : 0.0f);
+}
+
+// bwd_rec_const of the records [0, count) into rc[] (CTA-wide, then a barrier).
+__device__ __forceinline__ void fill_bwd_rec_consts(const Rec* recs, int count, float4* rc) {
+  for (int k = threadIdx.x; k < count; k += blockDim.x) rc[k] = bwd_rec_const(recs[k]);
+  __syncthreads();
+}
+
 // The gradient terms of one pixel for one record (backward_kernel :910-1018,
 // written into A[0..6] where the pixel contributes, A untouched otherwise)
 // and the pixel's transmittance update; returns whether it contributes.
-__device__ __forceinline__ bool bwd_pixel_terms(const Rec& g, float2 cut, float fx, float fy,
+// `rc`: the record's bwd_rec_const.
+__device__ __forceinline__ bool bwd_pixel_terms(const Rec& g, float2 cut, float4 rc, float fx, float fy,
                                                 float dL_d_pixel, float& prev_transmittance,
                                                 float (&A)[7]) {
   bool contrib = false;
@@ -2646,10 +2668,7 @@ __device__ __forceinline__ bool bwd_pixel_terms(const Rec& g, float2 cut, float 
     const float dx = sub_(fx, g.mx);
     const float dy = sub_(fy, g.my);
     const float cov_rr = g.cyy, cov_cc = g.cxx, cov_rc = g.cxy;
-    const float det = fma_(cov_rr, cov_cc, -mul_(cov_rc, cov_rc));
-    if (det > kEps) {
-      // det equals the record's (fma is symmetric in its factors), so its
-      // reciprocal and 2 pi sqrt(det) are the record's inv_det and norm
+    if (rc.w != 0.0f) {  // det > EPSILON
       const float inv_det = g.inv_det;
       // the backward's own exponent pairs cov_cc with dx^2 and cov_rr with dy^2 (:950)
       const float q = fma_(mul_(cov_rr, dy), dy,
@@ -2659,18 +2678,15 @@ __device__ __forceinline__ bool bwd_pixel_terms(const Rec& g, float2 cut, float 
         // exp(exponent) / norm, as in the density (one ex2.approx)
         const float base_val = ex2_approx(__fmaf_rn(exponent, 1.4426950408889634f, cut.y));
         const float h = mul_(mul_(0.5f, base_val), inv_det);
-        const float d_gamma_d_cov_rr = mul_(h, fma_(dy, dy, -mul_(mul_(cov_cc, inv_det), 0.5f)));
-        const float d_gamma_d_cov_cc = mul_(h, fma_(dx, dx, -mul_(mul_(cov_rr, inv_det), 0.5f)));
+        const float d_gamma_d_cov_rr = mul_(h, fma_(dy, dy, rc.y));
+        const float d_gamma_d_cov_cc = mul_(h, fma_(dx, dx, rc.z));
         const float d_gamma_d_cov_rc = mul_(mul_(mul_(-base_val, inv_det), dx), dy);
         A[2] = mul_(g_as, d_gamma_d_cov_rr);
         A[3] = mul_(g_as, d_gamma_d_cov_cc);
         A[4] = mul_(g_as, d_gamma_d_cov_rc);
       }
     }
-    // (.cu:973-974) divide by det + EPSILON: one correctly rounded
-    // reciprocal and two products instead of two divisions (within
-    // 1.5 ulp of the quotients)
-    const float inv_det_eps = __frcp_rn(add_(det, kEps));
+    const float inv_det_eps = rc.x;  // 1 / (det + EPSILON) (.cu:973-974)
     const float d_center_dr = mul_(-fma_(cov_rc, dx, -mul_(cov_rr, dy)), inv_det_eps);
     const float d_center_dc = mul_(-fma_(cov_cc, dx, -mul_(cov_rc, dy)), inv_det_eps);
     A[5] = mul_(g_as, d_center_dr);
@@ -2688,6 +2704,7 @@ __global__ void __launch_bounds__(kWarpsPerTile * 32) bwd_tile_kernel(const Tile
   __shared__ __align__(16) Rec s_rec[kCap];
   __shared__ float s_red[kWarpsPerTile][kBwdPartRecs][8];
   __shared__ float2 s_cut[kWarpsPerTile][kCap];
+  __shared__ float4 s_rc[kCap];
   __shared__ uint64_t bar;
   const int v = blockIdx.y, t = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -2701,6 +2718,7 @@ __global__ void __launch_bounds__(kWarpsPerTile * 32) bwd_tile_kernel(const Tile
   const int count = min(count_all, k_lo + kBwdPartRecs);  // records [0, count) are read
   const bool ok = load_tile_recs(s_rec, &bar, st, a.st.L, t, count, a.err, true);
   if (!__syncthreads_and(ok)) return;
+  fill_bwd_rec_consts(s_rec, count, s_rc);
 
   const int pc = tx * kTile + warp * 2 + (lane >> 4);
   const int pr = ty * kTile + (lane & 15);
@@ -2738,7 +2756,7 @@ __global__ void __launch_bounds__(kWarpsPerTile * 32) bwd_tile_kernel(const Tile
     const Rec& g = s_rec[k];
     float A[7] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     bool contrib = false;
-    if (in) contrib = bwd_pixel_terms(g, s_cut[warp][k], fx, fy, dL_d_pixel, prev_transmittance, A);
+    if (in) contrib = bwd_pixel_terms(g, s_cut[warp][k], s_rc[k], fx, fy, dL_d_pixel, prev_transmittance, A);
     if (__any_sync(0xffffffffu, contrib)) {
       const float A8[8] = {A[0], A[1], A[2], A[3], A[4], A[5], A[6], 0.0f};
       const float total = warp_sum8_scatter(A8, lane);
@@ -2781,6 +2799,7 @@ __global__ void __launch_bounds__(kTile * kTile / kBwdPix) bwd_tile4_kernel(cons
   __shared__ __align__(16) Rec s_rec[kCap];
   __shared__ float s_red[kWarps][kPartRecs][8];
   __shared__ float2 s_cut[kWarps][kCap];
+  __shared__ float4 s_rc[kCap];
   __shared__ uint64_t bar;
   const int v = blockIdx.y, t = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -2794,6 +2813,7 @@ __global__ void __launch_bounds__(kTile * kTile / kBwdPix) bwd_tile4_kernel(cons
   const int count = min(count_all, k_lo + kPartRecs);  // records [0, count) are read
   const bool ok = load_tile_recs(s_rec, &bar, st, a.st.L, t, count, a.err, true);
   if (!__syncthreads_and(ok)) return;
+  fill_bwd_rec_consts(s_rec, count, s_rc);
 
   const int r0 = ty * kTile + warp * 8, c0 = tx * kTile;
   const int pr = r0 + (lane & 7), pc0 = c0 + (lane >> 3);
@@ -2841,13 +2861,14 @@ __global__ void __launch_bounds__(kTile * kTile / kBwdPix) bwd_tile4_kernel(cons
     todo &= todo - 1;
     const Rec& g = s_rec[k];
     const float2 cut = s_cut[warp][k];
+    const float4 rc = s_rc[k];
     float A[7] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     bool contrib = false;
 #pragma unroll
     for (int i = 0; i < kBwdPix; ++i) {
       if (((hit[i] >> k) & 1ull) && in[i]) {
         float Ai[7] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        if (bwd_pixel_terms(g, cut, fx[i], fy, dL[i], trans[i], Ai)) {
+        if (bwd_pixel_terms(g, cut, rc, fx[i], fy, dL[i], trans[i], Ai)) {
           contrib = true;
 #pragma unroll
           for (int j = 0; j < 7; ++j) A[j] = add_(A[j], Ai[j]);
