@@ -2619,11 +2619,12 @@ __global__ void __launch_bounds__(256) omega_listed_kernel(const OmegaScatterArg
 // Per (pixel, Gaussian) terms of backward_kernel (:910-1018), summed over the
 // tile: 0 grad_sigma, 1 dL/dpixel * dpixel/dS (times the SH basis later),
 // 2..4 grad_cov rr, cc, rc, 5..6 grad_ipp_r, grad_ipp_c.
-// The tile's records are split into kBwdParts consecutive parts, one CTA
-// each (grid.z): the CTA of part q replays the transmittance of every pixel
-// through the records before its part (the same operations in the same order
-// as the full traversal) and computes the gradient terms of its own records,
-// so the per-record sums are those of one front-to-back pass.
+// Launches of fewer than SARR_BWD_ONE_PART_MIN_VIEWS views split the tile's
+// records into kBwdParts consecutive parts, one CTA each (grid.z): the CTA of
+// part q replays the transmittance of every pixel through the records before
+// its part (the same operations in the same order as the full traversal) and
+// computes the gradient terms of its own records, so the per-record sums are
+// those of one front-to-back pass; larger launches take a tile in one CTA.
 // The per-record constants of bwd_pixel_terms, computed once per record with
 // the operations the per-pixel terms would repeat: x = 1 / (det + EPSILON)
 // (.cu:973-974: one correctly rounded reciprocal and two products instead of
